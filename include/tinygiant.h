@@ -1,0 +1,143 @@
+/*
+ * tinygiant.h — C ABI of the B200 TinyGiant MoE expert-FFN library
+ * (tinygiant_b200/libtinygiant.so).
+ *
+ * Plain pointers and sizes only.  Every entry point returns TG_OK (0) or a
+ * negative TG_E* status; tg_last_error() gives the calling thread's last message.
+ *
+ * Two groups:
+ *  - tg_*   the reference's entry points, same argument order and meaning,
+ *           on host pointers; each call copies its inputs to the GPU, runs the
+ *           kernels and copies the result back before returning.
+ *  - tgx_*  device-resident API: a context owns the model in HBM and runs the
+ *           routed MoE decode on caller streams (cudaStream_t passed as void*).
+ *
+ * Weight format: ggml Q4_0 (18-byte blocks: fp16 d, 16 bytes of nibbles) in the
+ * reference's expert-contiguous relayout order gate | up | down
+ * (reference tinygiant/relayout.py:142-157).  Activations are quantised to ggml
+ * Q8_0 (34-byte blocks).  Row lengths (embed, inter, ncols) must be multiples of
+ * 256, as the reference's QK_K-blocked kernels require.
+ */
+#ifndef TINYGIANT_H
+#define TINYGIANT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TG_OK 0
+#define TG_EINVAL (-1)        /* bad argument (null pointer, bad dims, index range) */
+#define TG_ECUDA (-2)         /* a CUDA call failed; see tg_last_error() */
+#define TG_ENOMEM (-3)        /* device or pinned host allocation failed */
+#define TG_EUNSUPPORTED (-4)  /* format or configuration not implemented */
+#define TG_ENODEV (-5)        /* no CUDA device */
+#define TG_ETIMEOUT (-6)      /* a bounded device wait gave up */
+
+/* down_format codes of tg_expert_forward_mixed (reference libtinygiant.c:599-643
+ * uses 0 = Q4_K, 1 = f16, 2 = Q6_K; this library adds 3 = all-Q4_0 expert). */
+#define TG_FMT_Q4_K 0
+#define TG_FMT_F16 1
+#define TG_FMT_Q6_K 2
+#define TG_FMT_Q4_0 3
+
+const char *tg_last_error(void);
+int tg_version(void);
+int tg_device_count(void);
+
+/* ===================== reference-shaped entry points (host pointers) ===================== */
+
+/* Q8_0-quantise x[n] (n a multiple of 32) into n/32 ggml blocks of 34 bytes.
+ * Replaces the quantiser inside the reference library, csrc/libtinygiant.c:61-89. */
+int tg_quantize_q8_0(const float *x, void *out, int n);
+
+/* Q4_0-quantise x[n] into n/32 ggml blocks of 18 bytes (gguf Q4_0.quantize_blocks);
+ * the weight format the reference's relayout stores (tinygiant/relayout.py:111-157). */
+int tg_quantize_q4_0(const float *x, void *out, long long n);
+
+/* Exact int32 dot of every Q4_0 block of W[nrows][ncols] with the matching Q8_0 block
+ * of xq: out[r][b] = sum_j (q4 - 8) * q8.  The integer core of dot_q4k_q8,
+ * csrc/libtinygiant.c:104-169 (vdotq_s32 part, lines 135-158). */
+int tg_block_dots_q4_0(const uint8_t *W, const void *xq, int32_t *out, int nrows, int ncols);
+
+/* out[r] = W[r] . Q8_0(in).  Q4_0 twin of tg_matmul_q4k, csrc/libtinygiant.c:187-190. */
+int tg_matmul_q4_0(const uint8_t *q4_matrix, const float *input, float *output, int nrows, int ncols);
+
+/* out += weight * down(silu(gate . x) * (up . x)), x and h Q8_0-quantised; q4_data is
+ * one expert blob gate | up | down.  Q4_0 twin of tg_expert_forward, csrc/libtinygiant.c:555-595. */
+int tg_expert_forward_q4_0(const uint8_t *q4_data, const float *input, float *output, float weight,
+                           int embed_dim, int inter_dim);
+
+/* csrc/libtinygiant.c:599-643 with separate gate/up/down pointers (the symbol the
+ * reference engine calls, tinygiant/engine.py:249-257).  Supported down_format:
+ * TG_FMT_Q4_0; the others return TG_EUNSUPPORTED. */
+int tg_expert_forward_mixed(const uint8_t *gate_q4, const uint8_t *up_q4, const void *down_data,
+                            int down_format, const float *input, float *output, float weight,
+                            int embed_dim, int inter_dim);
+
+/* output = sum_e weights[e] * expert_e(input), accumulated in e order from zero.
+ * Q4_0 twin of tg_moe_forward, csrc/libtinygiant.c:647-655. */
+int tg_moe_forward_q4_0(const uint8_t **expert_ptrs, const float *weights, int n_experts,
+                        const float *input, float *output, int embed_dim, int inter_dim);
+
+/* mlock the pages of [addr, addr+len); returns mlock's result (0 or -1), as
+ * csrc/libtinygiant.c:761-766 does. */
+int tg_mlock(const void *addr, size_t len);
+
+/* ===================== device-resident API ===================== */
+
+typedef struct tgx_ctx tgx_ctx;
+
+typedef struct {
+    int embed;      /* hidden size H (multiple of 256) */
+    int inter;      /* expert intermediate size I (multiple of 256) */
+    int n_experts;  /* routed experts per layer E (<= 1024) */
+    int top_k;      /* experts per token k (<= 16) */
+    int n_layers;   /* MoE layers L */
+} tgx_shape;
+
+/* Create a context on `device` holding L x E experts and L routers in HBM.
+ * Model shape constants follow tinygiant/_constants.py. */
+int tgx_ctx_create(int device, const tgx_shape *shape, tgx_ctx **out);
+int tgx_ctx_destroy(tgx_ctx *ctx);
+
+/* Bytes of one expert blob (gate | up | down, Q4_0) for this context's shape. */
+size_t tgx_expert_bytes(const tgx_ctx *ctx);
+
+/* Copy n experts (ggml blobs, expert-contiguous as in a layer_NNN.q4.bin file,
+ * tinygiant/relayout.py:142-157) into layer `layer` starting at expert `first`.
+ * src is host memory (pinned or pageable) unless src_on_device. */
+int tgx_load_experts(tgx_ctx *ctx, int layer, int first, int n, const void *src, int src_on_device);
+
+/* Read n experts of a layer back as ggml blobs into host memory. */
+int tgx_read_experts(tgx_ctx *ctx, int layer, int first, int n, void *dst_host);
+
+/* Set layer `layer`'s router, R[E][embed] fp32 row-major (engine.py:231 `self.routers[i]`). */
+int tgx_set_router(tgx_ctx *ctx, int layer, const float *R, int src_on_device);
+
+/* Fill every expert with Q4_0(N(0, w_sigma)) weights and every router with
+ * N(0, r_sigma), generated on the device from `seed` (synthetic benchmark model). */
+int tgx_fill_synthetic(tgx_ctx *ctx, uint64_t seed, float w_sigma, float r_sigma);
+
+/* One routed MoE block on x_dev[embed] in place: x += sum_j w_j * expert_{idx_j}(x)
+ * with idx, w = top-k/softmax of R_layer . x (tinygiant/engine.py:229-258 without norms). */
+int tgx_moe_layer(tgx_ctx *ctx, int layer, float *x_dev, void *stream);
+
+/* One decode step: all L MoE blocks chained on x_dev[embed], x_{l+1} = x_l + moe_l(x_l).
+ * flags: TGX_EAGER launches kernel by kernel; otherwise the step is replayed from a
+ * CUDA graph captured on first use for this x_dev. */
+#define TGX_EAGER 1
+int tgx_decode_step(tgx_ctx *ctx, float *x_dev, void *stream, int flags);
+
+/* Routing chosen by the last tgx_moe_layer / tgx_decode_step for `layer`
+ * (idx[k] in ascending-logit order, w[k], logits[E]); any pointer may be NULL.
+ * Synchronises the context's device. */
+int tgx_last_routing(tgx_ctx *ctx, int layer, int32_t *idx, float *w, float *logits);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TINYGIANT_H */

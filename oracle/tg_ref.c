@@ -1,0 +1,501 @@
+/*
+ * tg_ref.c — CPU oracle for TinyGiant's MoE expert-FFN hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY: a portable C restatement of the reference's scalar
+ * routines, used by tests/, __graft_entry__.smoke() and bench.py's CPU arm as
+ * the checker.  The shipped library never links or calls it.
+ *
+ * What it follows (paths relative to the reference project):
+ *   fp16 -> fp32 ............ csrc/libtinygiant.c:24-33
+ *   Q8 quantiser structure .. csrc/libtinygiant.c:61-89  (block amax, scale = amax/127,
+ *                             per-element round) with ggml Q8_0 semantics
+ *                             (gguf/quants.py Q8_0.quantize_blocks, gguf 0.19.0)
+ *   Q4_0 weights ............ gguf/quants.py Q4_0.quantize_blocks / dequantize_blocks
+ *   block dot ............... csrc/libtinygiant.c:104-169 and csrc/test_libtinygiant.c:22-61
+ *                             (integer block dot, then scale, then fp32 accumulation)
+ *   matvec .................. csrc/libtinygiant.c:173-190 (quantise input once, one dot per row)
+ *   expert forward .......... csrc/libtinygiant.c:555-595 / 599-643 (quantise x, gate rows,
+ *                             up rows, g/(1+exp(-g))*u, requantise h, down rows, out += w*y)
+ *   MoE combine ............. csrc/libtinygiant.c:647-655, tinygiant/engine.py:238-258
+ *   router / top-k / softmax  tinygiant/engine.py:231-236
+ *
+ * Build with -ffp-contract=off: every float operation below is a separately
+ * rounded IEEE operation unless written as fmaf().
+ */
+#include "tg_ref.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------ fp16 */
+
+/* csrc/libtinygiant.c:24-33: IEEE half -> float, subnormals normalised. */
+float ref_f16_to_f32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu, m = h & 0x3FFu;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            int ee = 1;
+            while (!(m & 0x400u)) { m <<= 1; ee--; }
+            m &= 0x3FFu;
+            bits = sign | ((uint32_t)(ee + 112) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7F800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112) << 23) | (m << 13);
+    }
+    float r;
+    memcpy(&r, &bits, 4);
+    return r;
+}
+
+/* float -> IEEE half, round to nearest even (numpy astype(float16), ggml FP32_TO_FP16). */
+uint16_t ref_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) /* inf / nan */
+        return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x200u : 0u));
+    int e = (int)(ax >> 23) - 127;
+    uint32_t m = ax & 0x7FFFFFu;
+    if (e > 15) return (uint16_t)(sign | 0x7C00u);
+    if (e >= -14) {
+        uint32_t r = ((uint32_t)(e + 15) << 10) | (m >> 13);
+        uint32_t rem = m & 0x1FFFu;
+        if (rem > 0x1000u || (rem == 0x1000u && (r & 1u))) r++;
+        return (uint16_t)(sign | r);
+    }
+    /* half subnormal: units of 2^-24 */
+    if (ax < 0x00800000u) return (uint16_t)sign; /* float subnormal/zero -> 0 */
+    uint32_t full = 0x800000u | m;          /* value = full * 2^(e-23) */
+    int s = -(e + 1);                        /* shift to units of 2^-24 */
+    if (s >= 32) return (uint16_t)sign;
+    uint32_t q = full >> s;
+    uint32_t rem = full & ((1u << s) - 1u);
+    uint32_t half = 1u << (s - 1);
+    if (rem > half || (rem == half && (q & 1u))) q++;
+    return (uint16_t)(sign | q);
+}
+
+/* ------------------------------------------------------------------ exp */
+
+/*
+ * tg_expf: exp(x) by Cody-Waite argument reduction (W. J. Cody and W. Waite,
+ * "Software Manual for the Elementary Functions", 1980) and the degree-7 Taylor
+ * polynomial of exp on |r| <= ln2/2 (truncation error < r^8/8! ~ 5.3e-9).
+ *   k = rint(x * log2 e),  r = (x - k*ln2_hi) - k*ln2_lo,  exp(x) = 2^k * P(r)
+ * ln2_hi carries 12 significant bits so k*ln2_hi is exact; the scale by 2^k is
+ * split in two power-of-two multiplies so only a subnormal result rounds.
+ * The device kernels evaluate the identical sequence of IEEE operations.
+ */
+float ref_expf(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const float log2e = 0x1.715476p+0f;
+    const float ln2_hi = 0x1.62ep-1f;
+    const float ln2_lo = 0x1.0bfbe8p-15f;
+    float kf = rintf(x * log2e);
+    float r = fmaf(-kf, ln2_hi, x);
+    r = fmaf(-kf, ln2_lo, r);
+    float p = 0x1.a01a02p-13f;          /* 1/7! */
+    p = fmaf(p, r, 0x1.6c16c2p-10f);    /* 1/6! */
+    p = fmaf(p, r, 0x1.111112p-7f);     /* 1/5! */
+    p = fmaf(p, r, 0x1.555556p-5f);     /* 1/4! */
+    p = fmaf(p, r, 0x1.555556p-3f);     /* 1/3! */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int k = (int)kf;
+    int k1 = k / 2, k2 = k - k1;
+    uint32_t b1 = (uint32_t)(k1 + 127) << 23, b2 = (uint32_t)(k2 + 127) << 23;
+    float s1, s2;
+    memcpy(&s1, &b1, 4);
+    memcpy(&s2, &b2, 4);
+    return (p * s1) * s2;
+}
+
+/* ------------------------------------------------------------------ quantisers */
+
+/* Q8_0 (gguf Q8_0.quantize_blocks; structure of libtinygiant.c:61-89 with
+ * 32-wide blocks, fp16 scale, round half away from zero). */
+void ref_quantize_q8_0(const float *x, uint8_t *out, int64_t n) {
+    int64_t nb = n / REF_QK;
+    for (int64_t b = 0; b < nb; b++) {
+        const float *xb = x + b * REF_QK;
+        uint8_t *ob = out + b * REF_Q8_0_BYTES;
+        float amax = 0.0f;
+        for (int j = 0; j < REF_QK; j++) {
+            float a = fabsf(xb[j]);
+            if (a > amax) amax = a;
+        }
+        float d = amax / 127.0f;
+        float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint16_t dh = ref_f32_to_f16(d);
+        memcpy(ob, &dh, 2);
+        for (int j = 0; j < REF_QK; j++) {
+            float v = xb[j] * id;
+            ob[2 + j] = (uint8_t)(int8_t)roundf(v);
+        }
+    }
+}
+
+/* Q4_0 (gguf Q4_0.quantize_blocks): d = (signed value of max |x|) / -8,
+ * q = min(15, trunc(x/d + 8.5)), low nibbles = elements 0..15. */
+void ref_quantize_q4_0(const float *x, uint8_t *out, int64_t n) {
+    int64_t nb = n / REF_QK;
+    #pragma omp parallel for schedule(static) if (nb > 65536)
+    for (int64_t b = 0; b < nb; b++) {
+        const float *xb = x + b * REF_QK;
+        uint8_t *ob = out + b * REF_Q4_0_BYTES;
+        /* first element of largest magnitude (numpy argmax of |x|) */
+        float amax = fabsf(xb[0]), mx = xb[0];
+        for (int j = 1; j < REF_QK; j++) {
+            float a = fabsf(xb[j]);
+            if (a > amax) { amax = a; mx = xb[j]; }
+        }
+        float d = mx / -8.0f;
+        float id = d != 0.0f ? 1.0f / d : 0.0f;
+        uint16_t dh = ref_f32_to_f16(d);
+        memcpy(ob, &dh, 2);
+        uint8_t q[REF_QK];
+        for (int j = 0; j < REF_QK; j++) {
+            float v = truncf(xb[j] * id + 8.5f);
+            int qi = (int)v;
+            q[j] = (uint8_t)(qi > 15 ? 15 : qi);
+        }
+        for (int j = 0; j < 16; j++) ob[2 + j] = (uint8_t)(q[j] | (q[j + 16] << 4));
+    }
+}
+
+void ref_dequantize_q8_0(const uint8_t *q, float *out, int64_t n) {
+    for (int64_t b = 0; b < n / REF_QK; b++) {
+        const uint8_t *qb = q + b * REF_Q8_0_BYTES;
+        uint16_t dh;
+        memcpy(&dh, qb, 2);
+        float d = ref_f16_to_f32(dh);
+        for (int j = 0; j < REF_QK; j++) out[b * REF_QK + j] = (float)(int8_t)qb[2 + j] * d;
+    }
+}
+
+void ref_dequantize_q4_0(const uint8_t *q, float *out, int64_t n) {
+    for (int64_t b = 0; b < n / REF_QK; b++) {
+        const uint8_t *qb = q + b * REF_Q4_0_BYTES;
+        uint16_t dh;
+        memcpy(&dh, qb, 2);
+        float d = ref_f16_to_f32(dh);
+        for (int j = 0; j < 16; j++) {
+            out[b * REF_QK + j] = (float)((qb[2 + j] & 15) - 8) * d;
+            out[b * REF_QK + j + 16] = (float)((qb[2 + j] >> 4) - 8) * d;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ dots */
+
+/* Integer block dot of one Q4_0 block with one Q8_0 block
+ * (the vdotq_s32 part of libtinygiant.c:135-158, written as in test_libtinygiant.c:41-53). */
+int32_t ref_block_dot_q4_0_q8_0(const uint8_t *wblk, const uint8_t *xblk) {
+    const uint8_t *qs = wblk + 2;
+    const int8_t *xs = (const int8_t *)(xblk + 2);
+    int32_t s = 0;
+    for (int j = 0; j < 16; j++) {
+        s += ((int32_t)(qs[j] & 15) - 8) * (int32_t)xs[j];
+        s += ((int32_t)(qs[j] >> 4) - 8) * (int32_t)xs[j + 16];
+    }
+    return s;
+}
+
+void ref_block_dots(const uint8_t *W, const uint8_t *xq, int32_t *out, int rows, int cols) {
+    int nb = cols / REF_QK;
+    for (int r = 0; r < rows; r++)
+        for (int b = 0; b < nb; b++)
+            out[(size_t)r * nb + b] = ref_block_dot_q4_0_q8_0(
+                W + ((size_t)r * nb + b) * REF_Q4_0_BYTES, xq + (size_t)b * REF_Q8_0_BYTES);
+}
+
+static inline float block_term(const uint8_t *wblk, const uint8_t *xblk) {
+    uint16_t dw, dx;
+    memcpy(&dw, wblk, 2);
+    memcpy(&dx, xblk, 2);
+    int32_t s = ref_block_dot_q4_0_q8_0(wblk, xblk);
+    /* ggml: sumf += sumi * d_w * d_x, evaluated left to right */
+    return ((float)s * ref_f16_to_f32(dw)) * ref_f16_to_f32(dx);
+}
+
+/* 32-lane xor butterfly, the device warp reduction order. */
+static inline float butterfly32(float *p) {
+    for (int off = 16; off >= 1; off >>= 1) {
+        float q[32];
+        for (int l = 0; l < 32; l++) q[l] = p[l] + p[l ^ off];
+        memcpy(p, q, sizeof(q));
+    }
+    return p[0];
+}
+
+float ref_row_dot(const uint8_t *wrow, const uint8_t *xq, int nb, int mode) {
+    if (mode == TG_REF_ORDER) {
+        float total = 0.0f;
+        for (int b = 0; b < nb; b++)
+            total += block_term(wrow + (size_t)b * REF_Q4_0_BYTES, xq + (size_t)b * REF_Q8_0_BYTES);
+        return total;
+    }
+    float p[32];
+    for (int l = 0; l < 32; l++) {
+        float acc = 0.0f;
+        for (int b = l; b < nb; b += 32)
+            acc = acc + block_term(wrow + (size_t)b * REF_Q4_0_BYTES, xq + (size_t)b * REF_Q8_0_BYTES);
+        p[l] = acc;
+    }
+    return butterfly32(p);
+}
+
+void ref_matvec_q4_0(const uint8_t *W, const uint8_t *xq, float *y, int rows, int cols, int mode) {
+    int nb = cols / REF_QK;
+    for (int r = 0; r < rows; r++)
+        y[r] = ref_row_dot(W + (size_t)r * nb * REF_Q4_0_BYTES, xq, nb, mode);
+}
+
+/* ------------------------------------------------------------------ expert */
+
+float ref_silu_mul(float g, float u, int mode) {
+    float e = mode == TG_REF_ORDER ? expf(-g) : ref_expf(-g);
+    float silu = g / (1.0f + e);
+    return silu * u;
+}
+
+void ref_expert_forward_stages(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
+                               const float *x, float *out, float w,
+                               int embed, int inter, int mode,
+                               uint8_t *xq_out, float *g_out, float *u_out,
+                               float *h_out, uint8_t *hq_out, float *y_out) {
+    int nbe = embed / REF_QK, nbi = inter / REF_QK;
+    uint8_t *xq = malloc((size_t)nbe * REF_Q8_0_BYTES);
+    uint8_t *hq = malloc((size_t)nbi * REF_Q8_0_BYTES);
+    float *g = malloc(sizeof(float) * inter), *u = malloc(sizeof(float) * inter);
+    float *h = malloc(sizeof(float) * inter), *y = malloc(sizeof(float) * embed);
+    ref_quantize_q8_0(x, xq, embed);
+    ref_matvec_q4_0(gate, xq, g, inter, embed, mode);
+    ref_matvec_q4_0(up, xq, u, inter, embed, mode);
+    for (int i = 0; i < inter; i++) h[i] = ref_silu_mul(g[i], u[i], mode);
+    ref_quantize_q8_0(h, hq, inter);
+    ref_matvec_q4_0(down, hq, y, embed, inter, mode);
+    if (out)
+        for (int i = 0; i < embed; i++) out[i] = out[i] + w * y[i];
+    if (xq_out) memcpy(xq_out, xq, (size_t)nbe * REF_Q8_0_BYTES);
+    if (hq_out) memcpy(hq_out, hq, (size_t)nbi * REF_Q8_0_BYTES);
+    if (g_out) memcpy(g_out, g, sizeof(float) * inter);
+    if (u_out) memcpy(u_out, u, sizeof(float) * inter);
+    if (h_out) memcpy(h_out, h, sizeof(float) * inter);
+    if (y_out) memcpy(y_out, y, sizeof(float) * embed);
+    free(xq); free(hq); free(g); free(u); free(h); free(y);
+}
+
+void ref_expert_forward(const uint8_t *gate, const uint8_t *up, const uint8_t *down,
+                        const float *x, float *out, float w, int embed, int inter, int mode) {
+    ref_expert_forward_stages(gate, up, down, x, out, w, embed, inter, mode,
+                              NULL, NULL, NULL, NULL, NULL, NULL);
+}
+
+/* ------------------------------------------------------------------ routing */
+
+/*
+ * Router logits (engine.py:231, logits = router @ normed).  Each product
+ * R[e][r]*x[r] is rounded to fp32, clamped to +-2^22, converted to fixed point
+ * with 2^-40 units (round to nearest even) and summed in int64, so the sum is
+ * exact and independent of how the rows are split across threads or blocks:
+ *   logit_e = float(2^-40 * sum_r rint(clamp(fl(R[e][r]*x[r])) * 2^40))
+ */
+static inline int64_t router_fixed(float r, float x) {
+    float p = r * x;
+    p = fminf(fmaxf(p, -0x1p22f), 0x1p22f);
+    return llrintf(p * 0x1p40f);
+}
+
+void ref_router_logits(const float *R, const float *x, int n_experts, int hidden, float *logits) {
+    for (int e = 0; e < n_experts; e++) {
+        int64_t s = 0;
+        for (int r = 0; r < hidden; r++) s += router_fixed(R[(size_t)e * hidden + r], x[r]);
+        logits[e] = (float)((double)s * 0x1p-40);
+    }
+}
+
+/*
+ * Top-k + renormalised softmax (engine.py:232-236): idx = argsort(logits)[-k:]
+ * (ascending, so idx[k-1] is the largest; equal logits order by expert id),
+ * w = exp(l - max) / sum(exp(l - max)).  The sum over k = 8 uses numpy's
+ * pairwise order ((e0+e1)+(e2+e3))+((e4+e5)+(e6+e7)); other k sum sequentially.
+ */
+void ref_topk_softmax(const float *logits, int n_experts, int k, int32_t *idx, float *w, int mode) {
+    for (int i = 0; i < n_experts; i++) {
+        int rank = 0;
+        for (int j = 0; j < n_experts; j++)
+            if (logits[j] > logits[i] || (logits[j] == logits[i] && j > i)) rank++;
+        if (rank < k) idx[k - 1 - rank] = i;
+    }
+    float m = logits[idx[k - 1]];
+    float ex[64];
+    for (int j = 0; j < k; j++) {
+        float a = logits[idx[j]] - m;
+        ex[j] = mode == TG_REF_ORDER ? expf(a) : ref_expf(a);
+    }
+    float s;
+    if (k <= 8) {
+        float t[8];
+        for (int j = 0; j < 8; j++) t[j] = j < k ? ex[j] : 0.0f;
+        s = ((t[0] + t[1]) + (t[2] + t[3])) + ((t[4] + t[5]) + (t[6] + t[7]));
+    } else {
+        s = 0.0f;
+        for (int j = 0; j < k; j++) s = s + ex[j];
+    }
+    for (int j = 0; j < k; j++) w[j] = ex[j] / s;
+}
+
+/* ------------------------------------------------------------------ MoE block */
+
+static void expert_ptrs(const uint8_t *blob, int embed, int inter,
+                        const uint8_t **g, const uint8_t **u, const uint8_t **d) {
+    size_t t = (size_t)inter * (embed / REF_QK) * REF_Q4_0_BYTES;
+    *g = blob;
+    *u = blob + t;
+    *d = blob + 2 * t;
+}
+
+void ref_moe_layer(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
+                   float *x, int n_experts, int k, int embed, int inter, int mode,
+                   int32_t *idx_out, float *w_out, float *logits_out) {
+    float *logits = malloc(sizeof(float) * n_experts);
+    int32_t idx[64];
+    float w[64];
+    ref_router_logits(R, x, n_experts, embed, logits);
+    ref_topk_softmax(logits, n_experts, k, idx, w, mode);
+    float *moe = calloc((size_t)embed, sizeof(float));
+    for (int j = 0; j < k; j++) {
+        const uint8_t *g, *u, *d;
+        expert_ptrs(layer_blob + (size_t)idx[j] * expert_bytes, embed, inter, &g, &u, &d);
+        ref_expert_forward(g, u, d, x, moe, w[j], embed, inter, mode);
+    }
+    for (int i = 0; i < embed; i++) x[i] = x[i] + moe[i];
+    if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * k);
+    if (w_out) memcpy(w_out, w, sizeof(float) * k);
+    if (logits_out) memcpy(logits_out, logits, sizeof(float) * n_experts);
+    free(moe);
+    free(logits);
+}
+
+void ref_decode_step(const uint8_t *const *layer_blobs, const float *const *routers,
+                     int n_layers, float *x, int n_experts, int k, int embed, int inter,
+                     int mode, int32_t *idx_out) {
+    size_t eb = (size_t)3 * inter * (embed / REF_QK) * REF_Q4_0_BYTES;
+    for (int l = 0; l < n_layers; l++)
+        ref_moe_layer(layer_blobs[l], eb, routers[l], x, n_experts, k, embed, inter, mode,
+                      idx_out ? idx_out + (size_t)l * k : NULL, NULL, NULL);
+}
+
+/* ------------------------------------------------------------------ threaded */
+
+/* One MoE block with the per-row work spread over threads; same arithmetic as
+ * ref_moe_layer (each row is still computed by one thread in the same order). */
+static void moe_layer_mt(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
+                         float *x, int n_experts, int k, int embed, int inter, int mode,
+                         uint8_t *xq, float *h, uint8_t *hq, float *logits) {
+    int nbe = embed / REF_QK, nbi = inter / REF_QK;
+    int32_t idx[64];
+    float w[64];
+    #pragma omp parallel for schedule(static)
+    for (int e = 0; e < n_experts; e++) {
+        int64_t s = 0;
+        for (int r = 0; r < embed; r++) s += router_fixed(R[(size_t)e * embed + r], x[r]);
+        logits[e] = (float)((double)s * 0x1p-40);
+    }
+    ref_topk_softmax(logits, n_experts, k, idx, w, mode);
+    ref_quantize_q8_0(x, xq, embed);
+    size_t tb = (size_t)inter * nbe * REF_Q4_0_BYTES;
+    #pragma omp parallel for schedule(static)
+    for (int t = 0; t < k * inter; t++) {
+        int j = t / inter, i = t % inter;
+        const uint8_t *blob = layer_blob + (size_t)idx[j] * expert_bytes;
+        float g = ref_row_dot(blob + (size_t)i * nbe * REF_Q4_0_BYTES, xq, nbe, mode);
+        float u = ref_row_dot(blob + tb + (size_t)i * nbe * REF_Q4_0_BYTES, xq, nbe, mode);
+        h[t] = ref_silu_mul(g, u, mode);
+    }
+    for (int j = 0; j < k; j++)
+        ref_quantize_q8_0(h + (size_t)j * inter, hq + (size_t)j * nbi * REF_Q8_0_BYTES, inter);
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < embed; r++) {
+        float moe = 0.0f;
+        for (int j = 0; j < k; j++) {
+            const uint8_t *down = layer_blob + (size_t)idx[j] * expert_bytes + 2 * tb;
+            float y = ref_row_dot(down + (size_t)r * nbi * REF_Q4_0_BYTES,
+                                  hq + (size_t)j * nbi * REF_Q8_0_BYTES, nbi, mode);
+            moe = moe + w[j] * y;
+        }
+        x[r] = x[r] + moe;
+    }
+}
+
+void ref_decode_step_mt(const uint8_t *const *layer_blobs, const float *const *routers,
+                        int n_layers, float *x, int n_experts, int k, int embed, int inter,
+                        int mode, int n_threads) {
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+#else
+    (void)n_threads;
+#endif
+    size_t eb = (size_t)3 * inter * (embed / REF_QK) * REF_Q4_0_BYTES;
+    uint8_t *xq = malloc((size_t)(embed / REF_QK) * REF_Q8_0_BYTES);
+    float *h = malloc(sizeof(float) * (size_t)k * inter);
+    uint8_t *hq = malloc((size_t)k * (inter / REF_QK) * REF_Q8_0_BYTES);
+    float *logits = malloc(sizeof(float) * n_experts);
+    for (int l = 0; l < n_layers; l++)
+        moe_layer_mt(layer_blobs[l], eb, routers[l], x, n_experts, k, embed, inter, mode,
+                     xq, h, hq, logits);
+    free(xq); free(h); free(hq); free(logits);
+}
+
+void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
+                           float *x, int T, int n_experts, int k, int embed, int inter,
+                           int mode, int n_threads) {
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+    #pragma omp parallel for schedule(dynamic, 1)
+#else
+    (void)n_threads;
+#endif
+    for (int t = 0; t < T; t++)
+        ref_moe_layer(layer_blob, expert_bytes, R, x + (size_t)t * embed, n_experts, k,
+                      embed, inter, mode, NULL, NULL, NULL);
+}
+
+/* ------------------------------------------------------------------ data */
+
+static inline uint64_t splitmix64(uint64_t *s) {
+    uint64_t z = (*s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void ref_fill_normal(float *out, int64_t n, uint64_t seed, float sigma) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t c = 0; c < (n + 4095) / 4096; c++) {
+        uint64_t s = seed ^ (0xD1B54A32D192ED03ull * (uint64_t)(c + 1));
+        int64_t lo = c * 4096, hi = lo + 4096 < n ? lo + 4096 : n;
+        for (int64_t i = lo; i < hi; i += 2) {
+            double u1 = ((splitmix64(&s) >> 11) + 1.0) * 0x1p-53;
+            double u2 = (splitmix64(&s) >> 11) * 0x1p-53;
+            double rr = sqrt(-2.0 * log(u1));
+            out[i] = (float)(sigma * rr * cos(6.283185307179586 * u2));
+            if (i + 1 < hi) out[i + 1] = (float)(sigma * rr * sin(6.283185307179586 * u2));
+        }
+    }
+}

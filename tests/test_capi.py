@@ -1,0 +1,63 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares, and its
+argument checks work without a GPU (no compute calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+
+from tinygiant_b200 import _lib as L
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"\b(tgx?_[a-z0-9_]+)\s*\(", text):
+            names.add(m.group(1))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    for n in ("tg_expert_forward_mixed", "tg_moe_forward_q4_0", "tg_quantize_q8_0", "tgx_decode_step"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(str(L.find_library()))
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_prototypes_cover_header():
+    assert declared_symbols() <= set(L.PROTOTYPES)
+
+
+def test_argument_errors_without_device():
+    lib = L.load_tinygiant_lib()
+    assert lib.tg_quantize_q8_0(None, None, 0) == L.TG_EINVAL
+    assert b"bad arguments" in lib.tg_last_error()
+    x = np.zeros(48, np.float32)
+    out = np.zeros(64, np.uint8)
+    assert lib.tg_quantize_q8_0(x.ctypes.data, out.ctypes.data, 48) == L.TG_EINVAL  # not a multiple of 32
+    assert lib.tg_expert_forward_q4_0(out.ctypes.data, x.ctypes.data, x.ctypes.data, 1.0, 2000, 768) == L.TG_EINVAL
+    assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, L.TG_FMT_Q6_K,
+                                       x.ctypes.data, x.ctypes.data, 1.0, 2048, 768) == L.TG_EUNSUPPORTED
+    shape = L.TgxShape(2048, 768, 128, 8, 48)
+    h = ctypes.c_void_p()
+    bad = L.TgxShape(2048, 768, 128, 200, 48)
+    assert lib.tgx_ctx_create(0, ctypes.byref(bad), ctypes.byref(h)) == L.TG_EINVAL
+    if lib.tg_device_count() == 0:
+        assert lib.tgx_ctx_create(0, ctypes.byref(shape), ctypes.byref(h)) == L.TG_ENODEV
+        xs = np.zeros(64, np.float32)
+        assert lib.tg_quantize_q8_0(xs.ctypes.data, out.ctypes.data, 64) == L.TG_ENODEV
+
+
+def test_mlock_matches_reference_semantics():
+    lib = L.load_tinygiant_lib()
+    buf = np.zeros(1 << 16, np.uint8)
+    rc = lib.tg_mlock(buf.ctypes.data, buf.nbytes)
+    assert rc in (0, -1)  # mlock's own result, as csrc/libtinygiant.c:761-766 returns it

@@ -1,0 +1,120 @@
+"""ctypes bindings of libtinygiant.so (the B200 build), mirroring the reference's
+tinygiant/_lib.py: find_library() looks next to the package and in the repo
+root, load_tinygiant_lib() registers the prototypes and returns the CDLL (or
+None when no library is found, as the reference does).
+
+Differences from the reference (tinygiant/_lib.py:26-76): every entry point
+returns an int status (0 = TG_OK, negative = error) instead of void, and the
+device-resident tgx_* API is registered as well.  check() turns a status into a
+TinyGiantError carrying tg_last_error().
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+VP = ctypes.c_void_p
+CI = ctypes.c_int
+CF = ctypes.c_float
+SZ = ctypes.c_size_t
+LL = ctypes.c_longlong
+U64 = ctypes.c_uint64
+
+TG_OK = 0
+TG_EINVAL = -1
+TG_ECUDA = -2
+TG_ENOMEM = -3
+TG_EUNSUPPORTED = -4
+TG_ENODEV = -5
+TG_ETIMEOUT = -6
+
+TG_FMT_Q4_K = 0
+TG_FMT_F16 = 1
+TG_FMT_Q6_K = 2
+TG_FMT_Q4_0 = 3
+
+TGX_EAGER = 1
+
+LIB_NAME = "libtinygiant.so"
+
+
+class TinyGiantError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"tinygiant error {code}: {msg}")
+        self.code = code
+
+
+class TgxShape(ctypes.Structure):
+    _fields_ = [("embed", CI), ("inter", CI), ("n_experts", CI), ("top_k", CI), ("n_layers", CI)]
+
+
+# name -> (restype, argtypes); the order follows include/tinygiant.h
+PROTOTYPES = {
+    "tg_last_error": (ctypes.c_char_p, []),
+    "tg_version": (CI, []),
+    "tg_device_count": (CI, []),
+    "tg_quantize_q8_0": (CI, [VP, VP, CI]),
+    "tg_quantize_q4_0": (CI, [VP, VP, LL]),
+    "tg_block_dots_q4_0": (CI, [VP, VP, VP, CI, CI]),
+    "tg_matmul_q4_0": (CI, [VP, VP, VP, CI, CI]),
+    "tg_expert_forward_q4_0": (CI, [VP, VP, VP, CF, CI, CI]),
+    "tg_expert_forward_mixed": (CI, [VP, VP, VP, CI, VP, VP, CF, CI, CI]),
+    "tg_moe_forward_q4_0": (CI, [VP, VP, CI, VP, VP, CI, CI]),
+    "tg_mlock": (CI, [VP, SZ]),
+    "tgx_ctx_create": (CI, [CI, ctypes.POINTER(TgxShape), ctypes.POINTER(VP)]),
+    "tgx_ctx_destroy": (CI, [VP]),
+    "tgx_expert_bytes": (SZ, [VP]),
+    "tgx_load_experts": (CI, [VP, CI, CI, CI, VP, CI]),
+    "tgx_read_experts": (CI, [VP, CI, CI, CI, VP]),
+    "tgx_set_router": (CI, [VP, CI, VP, CI]),
+    "tgx_fill_synthetic": (CI, [VP, U64, CF, CF]),
+    "tgx_moe_layer": (CI, [VP, CI, VP, VP]),
+    "tgx_decode_step": (CI, [VP, VP, VP, CI]),
+    "tgx_last_routing": (CI, [VP, CI, VP, VP, VP]),
+}
+
+
+def find_library():
+    """Find libtinygiant.so next to this package or in the repository root."""
+    pkg_dir = Path(__file__).parent
+    repo_dir = pkg_dir.parent
+    for path in (pkg_dir / LIB_NAME, repo_dir / LIB_NAME):
+        if path.exists():
+            return path
+    return None
+
+
+def load_tinygiant_lib(lib_path=None):
+    """Load the B200 library and register its prototypes; None if not found."""
+    if lib_path is None:
+        lib_path = find_library()
+    if lib_path is None:
+        return None
+    lib = ctypes.CDLL(str(lib_path))
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_LIB = None
+
+
+def get_lib():
+    """The loaded library; raises if it has not been built (no silent fallback)."""
+    global _LIB
+    if _LIB is None:
+        _LIB = load_tinygiant_lib()
+        if _LIB is None:
+            raise RuntimeError(
+                "libtinygiant.so not found: build it with `python -m tinygiant_b200.build`")
+    return _LIB
+
+
+def check(rc: int, lib=None) -> int:
+    if rc != TG_OK:
+        lib = lib or get_lib()
+        msg = lib.tg_last_error()
+        raise TinyGiantError(rc, msg.decode() if msg else "")
+    return rc

@@ -1,0 +1,60 @@
+"""Build libtinygiant.so (the C-ABI library) in-tree with nvcc for sm_100a.
+
+    python -m tinygiant_b200.build [-v]
+
+The library lands next to this file (tinygiant_b200/libtinygiant.so), where
+tinygiant_b200/_lib.py finds it, as the reference's _lib.find_library does.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+CSRC = PKG / "csrc"
+OUT = PKG / "libtinygiant.so"
+SOURCES = ["tg_kernels.cu", "tg_decode.cu", "tg_capi.cu"]
+NVCC_FLAGS = [
+    "-O3", "-std=c++17", "-lineinfo",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+    "--expt-relaxed-constexpr",
+]
+
+
+def nvcc() -> str:
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if c and (Path(c).exists() or c == "nvcc"):
+            return c
+    return "nvcc"
+
+
+def sources() -> list[Path]:
+    return [CSRC / s for s in SOURCES if (CSRC / s).exists()]
+
+
+def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
+    srcs = sources()
+    objs = []
+    for src in srcs:
+        obj = CSRC / (src.stem + ".o")
+        deps = [src] + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [PKG.parent / "include" / "tinygiant.h"]
+        if not obj.exists() or any(d.stat().st_mtime > obj.stat().st_mtime for d in deps if d.exists()):
+            cmd = [nvcc(), *NVCC_FLAGS, *(extra or []), "-c", str(src), "-o", str(obj)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+                print(" ".join(cmd), flush=True)
+            subprocess.run(cmd, check=True)
+        objs.append(obj)
+    if not OUT.exists() or any(o.stat().st_mtime > OUT.stat().st_mtime for o in objs):
+        cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(OUT)]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

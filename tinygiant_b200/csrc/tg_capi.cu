@@ -1,0 +1,553 @@
+// tg_capi.cu — the C ABI declared in include/tinygiant.h.
+//
+// tg_*  : the reference library's entry points (csrc/libtinygiant.c) on host
+//         pointers.  They share one device workspace per process (grown on
+//         demand, guarded by a mutex) and are synchronous like the reference's.
+// tgx_* : a context that owns an L x E expert model and L routers in HBM and
+//         runs the routed MoE decode on caller streams.
+#include <cuda_runtime.h>
+#include <sys/mman.h>
+#include <unistd.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tinygiant.h"
+#include "tg_internal.h"
+
+using tg::ActView;
+using tg::Geom;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+#define TG_CUDA(call)                                                                         \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess)                                                                \
+            return fail(e_ == cudaErrorMemoryAllocation ? TG_ENOMEM : TG_ECUDA,               \
+                        std::string(#call) + ": " + cudaGetErrorString(e_));                  \
+    } while (0)
+
+#define TG_CHECK(cond, code, msg) \
+    do {                          \
+        if (!(cond)) return fail((code), (msg)); \
+    } while (0)
+
+int have_device() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t n = 0;
+};
+
+int ensure(DevBuf& b, size_t n) {
+    if (b.n >= n && b.p) return TG_OK;
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.n = 0;
+    size_t want = n < 256 ? 256 : n;
+    if (cudaMalloc(&b.p, want) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(TG_ENOMEM, "cudaMalloc of " + std::to_string(want) + " bytes failed");
+    }
+    b.n = want;
+    return TG_OK;
+}
+
+// Device workspace of the host-pointer entry points.
+struct HostWS {
+    std::mutex mu;
+    int device = -1;
+    cudaStream_t s = nullptr;
+    DevBuf raw, w, x, out, act, hq, ptrs, wts, i32;
+
+    int bind() {
+        int dev = 0;
+        if (!have_device()) return fail(TG_ENODEV, "no CUDA device");
+        if (cudaGetDevice(&dev) != cudaSuccess) return fail(TG_ECUDA, "cudaGetDevice failed");
+        if (dev != device) {
+            release();
+            device = dev;
+        }
+        if (!s && cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess)
+            return fail(TG_ECUDA, "cudaStreamCreate failed");
+        return TG_OK;
+    }
+    void release() {
+        for (DevBuf* b : {&raw, &w, &x, &out, &act, &hq, &ptrs, &wts, &i32}) {
+            if (b->p) cudaFree(b->p);
+            b->p = nullptr;
+            b->n = 0;
+        }
+        if (s) cudaStreamDestroy(s);
+        s = nullptr;
+    }
+};
+
+HostWS& ws() {
+    static HostWS* w = new HostWS();  // never destroyed: safe at process exit
+    return *w;
+}
+
+#define TG_TRY(expr)            \
+    do {                        \
+        int rc_ = (expr);       \
+        if (rc_ != TG_OK) return rc_; \
+    } while (0)
+
+// Copy a ggml expert blob already on the device (raw) into row-split form (dst).
+cudaError_t repack_expert(const uint8_t* raw, uint8_t* dst, const Geom& g, cudaStream_t s) {
+    cudaError_t e = tg::launch_repack_rows(raw, dst, 2LL * g.I, g.nbH, s);
+    if (e != cudaSuccess) return e;
+    return tg::launch_repack_rows(raw + 2 * g.t_gu, dst + 2 * g.t_gu, g.H, g.nbI, s);
+}
+cudaError_t unpack_expert(const uint8_t* src, uint8_t* raw, const Geom& g, cudaStream_t s) {
+    cudaError_t e = tg::launch_unpack_rows(src, raw, 2LL * g.I, g.nbH, s);
+    if (e != cudaSuccess) return e;
+    return tg::launch_unpack_rows(src + 2 * g.t_gu, raw + 2 * g.t_gu, g.H, g.nbI, s);
+}
+
+// Expert forward of n experts already row-split on the device in ws.w
+// (expert e at w + e * expert_bytes), on input ws.x, into ws.out.
+int run_experts(HostWS& W, const Geom& g, int n, const float* weights_host, float w_scalar,
+                int accumulate) {
+    std::vector<const uint8_t*> ptrs(n);
+    for (int e = 0; e < n; e++) ptrs[e] = (const uint8_t*)W.w.p + (size_t)e * g.expert_bytes;
+    TG_TRY(ensure(W.ptrs, sizeof(void*) * n));
+    TG_TRY(ensure(W.hq, tg::act_bytes(g.nbI) * n));
+    TG_CUDA(cudaMemcpyAsync(W.ptrs.p, ptrs.data(), sizeof(void*) * n, cudaMemcpyHostToDevice, W.s));
+    const float* wdev = nullptr;
+    if (weights_host) {
+        TG_TRY(ensure(W.wts, sizeof(float) * n));
+        TG_CUDA(cudaMemcpyAsync(W.wts.p, weights_host, sizeof(float) * n, cudaMemcpyHostToDevice, W.s));
+        wdev = (const float*)W.wts.p;
+    }
+    TG_CUDA(tg::prepare_kernels(g, n));
+    TG_CUDA(tg::launch_gateup((const uint8_t* const*)W.ptrs.p, n, (const float*)W.x.p, g, (uint8_t*)W.hq.p,
+                              nullptr, nullptr, W.s));
+    TG_CUDA(tg::launch_down_combine((const uint8_t* const*)W.ptrs.p, n, (const uint8_t*)W.hq.p, wdev, w_scalar,
+                                    g, nullptr, (float*)W.out.p, accumulate, nullptr, W.s));
+    return TG_OK;
+}
+
+}  // namespace
+
+// ============================================================ reference-shaped
+
+extern "C" const char* tg_last_error(void) { return g_err.c_str(); }
+extern "C" int tg_version(void) { return 1; }
+extern "C" int tg_device_count(void) { return have_device(); }
+
+extern "C" int tg_quantize_q8_0(const float* x, void* out, int n) {
+    TG_CHECK(x && out && n > 0 && n % 32 == 0, TG_EINVAL, "tg_quantize_q8_0: bad arguments");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    int nb = n / 32;
+    TG_TRY(ensure(W.x, sizeof(float) * n));
+    TG_TRY(ensure(W.act, tg::act_bytes(nb)));
+    TG_TRY(ensure(W.raw, (size_t)nb * tg::Q8_0_BYTES));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, x, sizeof(float) * n, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_quantize_act((const float*)W.x.p, n, tg::act_view(W.act.p, nb), (uint8_t*)W.raw.p, W.s));
+    TG_CUDA(cudaMemcpyAsync(out, W.raw.p, (size_t)nb * tg::Q8_0_BYTES, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_quantize_q4_0(const float* x, void* out, long long n) {
+    TG_CHECK(x && out && n > 0 && n % 32 == 0, TG_EINVAL, "tg_quantize_q4_0: bad arguments");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    long long nb = n / 32;
+    TG_TRY(ensure(W.x, sizeof(float) * (size_t)n));
+    TG_TRY(ensure(W.raw, (size_t)nb * tg::Q4_0_BYTES));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, x, sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_quantize_q4_0((const float*)W.x.p, n, (uint8_t*)W.raw.p, W.s));
+    TG_CUDA(cudaMemcpyAsync(out, W.raw.p, (size_t)nb * tg::Q4_0_BYTES, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_block_dots_q4_0(const uint8_t* Wq, const void* xq, int32_t* out, int nrows, int ncols) {
+    TG_CHECK(Wq && xq && out && nrows > 0 && ncols > 0 && ncols % 256 == 0, TG_EINVAL,
+             "tg_block_dots_q4_0: bad arguments (ncols must be a multiple of 256)");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    int nb = ncols / 32;
+    size_t wb = (size_t)nrows * nb * tg::Q4_0_BYTES;
+    TG_TRY(ensure(W.raw, wb));
+    TG_TRY(ensure(W.w, wb));
+    TG_TRY(ensure(W.x, (size_t)nb * tg::Q8_0_BYTES));
+    TG_TRY(ensure(W.act, tg::act_bytes(nb)));
+    TG_TRY(ensure(W.i32, sizeof(int32_t) * (size_t)nrows * nb));
+    TG_CUDA(cudaMemcpyAsync(W.raw.p, Wq, wb, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, xq, (size_t)nb * tg::Q8_0_BYTES, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_repack_rows((const uint8_t*)W.raw.p, (uint8_t*)W.w.p, nrows, nb, W.s));
+    ActView a = tg::act_view(W.act.p, nb);
+    TG_CUDA(tg::launch_q8_0_to_act((const uint8_t*)W.x.p, nb, a, W.s));
+    TG_CUDA(tg::launch_block_dots((const uint8_t*)W.w.p, a, (int32_t*)W.i32.p, nrows, nb, W.s));
+    TG_CUDA(cudaMemcpyAsync(out, W.i32.p, sizeof(int32_t) * (size_t)nrows * nb, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_matmul_q4_0(const uint8_t* Wq, const float* input, float* output, int nrows, int ncols) {
+    TG_CHECK(Wq && input && output && nrows > 0 && ncols > 0 && ncols % 256 == 0, TG_EINVAL,
+             "tg_matmul_q4_0: bad arguments (ncols must be a multiple of 256)");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    int nb = ncols / 32;
+    size_t wb = (size_t)nrows * nb * tg::Q4_0_BYTES;
+    TG_TRY(ensure(W.raw, wb));
+    TG_TRY(ensure(W.w, wb));
+    TG_TRY(ensure(W.x, sizeof(float) * ncols));
+    TG_TRY(ensure(W.act, tg::act_bytes(nb)));
+    TG_TRY(ensure(W.out, sizeof(float) * nrows));
+    TG_CUDA(cudaMemcpyAsync(W.raw.p, Wq, wb, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, input, sizeof(float) * ncols, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_repack_rows((const uint8_t*)W.raw.p, (uint8_t*)W.w.p, nrows, nb, W.s));
+    ActView a = tg::act_view(W.act.p, nb);
+    TG_CUDA(tg::launch_quantize_act((const float*)W.x.p, ncols, a, nullptr, W.s));
+    TG_CUDA(tg::launch_matvec((const uint8_t*)W.w.p, a, (float*)W.out.p, nrows, nb, W.s));
+    TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * nrows, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+static int expert_forward_parts(const uint8_t* gate, const uint8_t* up, const uint8_t* down, const float* input,
+                                float* output, float weight, int embed, int inter) {
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    Geom g = Geom::make(embed, inter);
+    TG_TRY(ensure(W.raw, g.expert_bytes));
+    TG_TRY(ensure(W.w, g.expert_bytes));
+    TG_TRY(ensure(W.x, sizeof(float) * embed));
+    TG_TRY(ensure(W.out, sizeof(float) * embed));
+    uint8_t* raw = (uint8_t*)W.raw.p;
+    TG_CUDA(cudaMemcpyAsync(raw, gate, g.t_gu, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(raw + g.t_gu, up, g.t_gu, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(raw + 2 * g.t_gu, down, g.t_d, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(repack_expert(raw, (uint8_t*)W.w.p, g, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, input, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.out.p, output, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
+    TG_TRY(run_experts(W, g, 1, nullptr, weight, 1));
+    TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * embed, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_expert_forward_q4_0(const uint8_t* q4_data, const float* input, float* output, float weight,
+                                      int embed_dim, int inter_dim) {
+    TG_CHECK(q4_data && input && output, TG_EINVAL, "tg_expert_forward_q4_0: null pointer");
+    TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
+             "tg_expert_forward_q4_0: embed/inter must be positive multiples of 256");
+    Geom g = Geom::make(embed_dim, inter_dim);
+    return expert_forward_parts(q4_data, q4_data + g.t_gu, q4_data + 2 * g.t_gu, input, output, weight,
+                                embed_dim, inter_dim);
+}
+
+extern "C" int tg_expert_forward_mixed(const uint8_t* gate_q4, const uint8_t* up_q4, const void* down_data,
+                                       int down_format, const float* input, float* output, float weight,
+                                       int embed_dim, int inter_dim) {
+    TG_CHECK(gate_q4 && up_q4 && down_data && input && output, TG_EINVAL, "tg_expert_forward_mixed: null pointer");
+    if (down_format != TG_FMT_Q4_0)
+        return fail(TG_EUNSUPPORTED, "tg_expert_forward_mixed: only TG_FMT_Q4_0 experts are implemented");
+    TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
+             "tg_expert_forward_mixed: embed/inter must be positive multiples of 256");
+    return expert_forward_parts(gate_q4, up_q4, (const uint8_t*)down_data, input, output, weight, embed_dim,
+                                inter_dim);
+}
+
+extern "C" int tg_moe_forward_q4_0(const uint8_t** expert_ptrs, const float* weights, int n_experts,
+                                   const float* input, float* output, int embed_dim, int inter_dim) {
+    TG_CHECK(expert_ptrs && weights && input && output && n_experts > 0 && n_experts <= 16, TG_EINVAL,
+             "tg_moe_forward_q4_0: bad arguments (1 <= n_experts <= 16)");
+    for (int e = 0; e < n_experts; e++) TG_CHECK(expert_ptrs[e], TG_EINVAL, "tg_moe_forward_q4_0: null expert");
+    TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
+             "tg_moe_forward_q4_0: embed/inter must be positive multiples of 256");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    Geom g = Geom::make(embed_dim, inter_dim);
+    size_t tot = g.expert_bytes * n_experts;
+    TG_TRY(ensure(W.raw, tot));
+    TG_TRY(ensure(W.w, tot));
+    TG_TRY(ensure(W.x, sizeof(float) * embed_dim));
+    TG_TRY(ensure(W.out, sizeof(float) * embed_dim));
+    for (int e = 0; e < n_experts; e++) {
+        uint8_t* raw = (uint8_t*)W.raw.p + (size_t)e * g.expert_bytes;
+        TG_CUDA(cudaMemcpyAsync(raw, expert_ptrs[e], g.expert_bytes, cudaMemcpyHostToDevice, W.s));
+        TG_CUDA(repack_expert(raw, (uint8_t*)W.w.p + (size_t)e * g.expert_bytes, g, W.s));
+    }
+    TG_CUDA(cudaMemcpyAsync(W.x.p, input, sizeof(float) * embed_dim, cudaMemcpyHostToDevice, W.s));
+    TG_TRY(run_experts(W, g, n_experts, weights, 0.0f, 0));
+    TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * embed_dim, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_mlock(const void* addr, size_t len) {
+    uintptr_t page = (uintptr_t)sysconf(_SC_PAGESIZE);
+    uintptr_t a = (uintptr_t)addr & ~(page - 1);
+    size_t l = len + ((uintptr_t)addr - a);
+    return mlock((const void*)a, l);
+}
+
+// ============================================================ device-resident
+
+struct tgx_ctx {
+    int device = 0;
+    tgx_shape shape{};
+    Geom g;
+    size_t layer_bytes = 0;
+    uint8_t* weights = nullptr;   // [L][E] experts, row-split
+    float* routers = nullptr;     // [L][E][H]
+    long long* acc = nullptr;     // [E] router accumulators (kept zero between uses)
+    unsigned* counter = nullptr;  // router block counter (kept zero)
+    float* logits = nullptr;      // [L][E]
+    int* idx = nullptr;           // [L][k]
+    float* wts = nullptr;         // [L][k]
+    const uint8_t** eptrs = nullptr;  // [L][k]
+    uint8_t* hq = nullptr;        // k activation blocks of I/32
+    uint8_t* staging = nullptr;   // ggml blobs in transit
+    size_t staging_bytes = 0;
+    cudaStream_t s = nullptr;     // loads, synthetic fill, graph capture
+    cudaGraphExec_t gexec = nullptr;
+    float* gx = nullptr;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+void ctx_free(tgx_ctx* c) {
+    if (!c) return;
+    DeviceGuard dg(c->device);
+    if (c->gexec) cudaGraphExecDestroy(c->gexec);
+    for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->acc, (void*)c->counter, (void*)c->logits,
+                    (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging})
+        if (p) cudaFree(p);
+    if (c->s) cudaStreamDestroy(c->s);
+    delete c;
+}
+
+int moe_layer_launch(tgx_ctx* c, int layer, float* x, cudaStream_t s) {
+    const tgx_shape& sh = c->shape;
+    const int E = sh.n_experts, k = sh.top_k, H = sh.embed;
+    const uint8_t* lb = c->weights + (size_t)layer * c->layer_bytes;
+    const uint8_t** ep = c->eptrs + (size_t)layer * k;
+    float* w = c->wts + (size_t)layer * k;
+    TG_CUDA(tg::launch_router_topk(c->routers + (size_t)layer * E * H, x, E, H, k, c->acc, c->counter,
+                                   c->logits + (size_t)layer * E, c->idx + (size_t)layer * k, w, lb,
+                                   c->g.expert_bytes, ep, s));
+    TG_CUDA(tg::launch_gateup(ep, k, x, c->g, c->hq, nullptr, nullptr, s));
+    TG_CUDA(tg::launch_down_combine(ep, k, c->hq, w, 0.0f, c->g, x, x, 0, nullptr, s));
+    return TG_OK;
+}
+
+}  // namespace
+
+extern "C" int tgx_ctx_create(int device, const tgx_shape* shape, tgx_ctx** out) {
+    TG_CHECK(shape && out, TG_EINVAL, "tgx_ctx_create: null argument");
+    *out = nullptr;
+    TG_CHECK(Geom::valid_dims(shape->embed, shape->inter), TG_EINVAL,
+             "tgx_ctx_create: embed/inter must be positive multiples of 256");
+    TG_CHECK(shape->n_experts > 0 && shape->n_experts <= 1024 && shape->top_k > 0 && shape->top_k <= 16 &&
+                 shape->top_k <= shape->n_experts && shape->n_layers > 0,
+             TG_EINVAL, "tgx_ctx_create: bad expert/top_k/layer counts");
+    int ndev = have_device();
+    TG_CHECK(ndev > 0, TG_ENODEV, "no CUDA device");
+    TG_CHECK(device >= 0 && device < ndev, TG_EINVAL, "tgx_ctx_create: bad device index");
+    DeviceGuard dg(device);
+    tgx_ctx* c = new tgx_ctx();
+    c->device = device;
+    c->shape = *shape;
+    c->g = Geom::make(shape->embed, shape->inter);
+    c->layer_bytes = c->g.expert_bytes * shape->n_experts;
+    const int L = shape->n_layers, E = shape->n_experts, k = shape->top_k, H = shape->embed;
+    c->staging_bytes = c->g.expert_bytes * 8;
+    auto A = [&](void** p, size_t n) -> int {
+        if (cudaMalloc(p, n) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(TG_ENOMEM, "tgx_ctx_create: cudaMalloc of " + std::to_string(n) + " bytes failed");
+        }
+        return TG_OK;
+    };
+    int rc = TG_OK;
+    if ((rc = A((void**)&c->weights, c->layer_bytes * L)) || (rc = A((void**)&c->routers, sizeof(float) * L * E * H)) ||
+        (rc = A((void**)&c->acc, sizeof(long long) * E)) || (rc = A((void**)&c->counter, sizeof(unsigned))) ||
+        (rc = A((void**)&c->logits, sizeof(float) * L * E)) || (rc = A((void**)&c->idx, sizeof(int) * L * k)) ||
+        (rc = A((void**)&c->wts, sizeof(float) * L * k)) || (rc = A((void**)&c->eptrs, sizeof(void*) * L * k)) ||
+        (rc = A((void**)&c->hq, tg::act_bytes(c->g.nbI) * k)) || (rc = A((void**)&c->staging, c->staging_bytes))) {
+        ctx_free(c);
+        return rc;
+    }
+    cudaError_t e = cudaMemset(c->acc, 0, sizeof(long long) * E);
+    if (e == cudaSuccess) e = cudaMemset(c->counter, 0, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemset(c->routers, 0, sizeof(float) * L * E * H);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->s, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = tg::prepare_kernels(c->g, k);
+    if (e != cudaSuccess) {
+        ctx_free(c);
+        return fail(TG_ECUDA, std::string("tgx_ctx_create: ") + cudaGetErrorString(e));
+    }
+    *out = c;
+    return TG_OK;
+}
+
+extern "C" int tgx_ctx_destroy(tgx_ctx* ctx) {
+    if (!ctx) return TG_OK;
+    ctx_free(ctx);
+    return TG_OK;
+}
+
+extern "C" size_t tgx_expert_bytes(const tgx_ctx* ctx) { return ctx ? ctx->g.expert_bytes : 0; }
+
+extern "C" int tgx_load_experts(tgx_ctx* ctx, int layer, int first, int n, const void* src, int src_on_device) {
+    TG_CHECK(ctx && src, TG_EINVAL, "tgx_load_experts: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers && first >= 0 && n >= 0 && first + n <= ctx->shape.n_experts,
+             TG_EINVAL, "tgx_load_experts: layer/expert range out of bounds");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    const int chunk = (int)(ctx->staging_bytes / g.expert_bytes);
+    for (int e0 = 0; e0 < n; e0 += chunk) {
+        int m = n - e0 < chunk ? n - e0 : chunk;
+        const uint8_t* s = (const uint8_t*)src + (size_t)e0 * g.expert_bytes;
+        TG_CUDA(cudaMemcpyAsync(ctx->staging, s, (size_t)m * g.expert_bytes,
+                                src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->s));
+        for (int e = 0; e < m; e++) {
+            uint8_t* dst = ctx->weights + (size_t)layer * ctx->layer_bytes + (size_t)(first + e0 + e) * g.expert_bytes;
+            TG_CUDA(repack_expert(ctx->staging + (size_t)e * g.expert_bytes, dst, g, ctx->s));
+        }
+        TG_CUDA(cudaStreamSynchronize(ctx->s));
+    }
+    return TG_OK;
+}
+
+extern "C" int tgx_read_experts(tgx_ctx* ctx, int layer, int first, int n, void* dst_host) {
+    TG_CHECK(ctx && dst_host, TG_EINVAL, "tgx_read_experts: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers && first >= 0 && n >= 0 && first + n <= ctx->shape.n_experts,
+             TG_EINVAL, "tgx_read_experts: layer/expert range out of bounds");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    const int chunk = (int)(ctx->staging_bytes / g.expert_bytes);
+    for (int e0 = 0; e0 < n; e0 += chunk) {
+        int m = n - e0 < chunk ? n - e0 : chunk;
+        for (int e = 0; e < m; e++) {
+            const uint8_t* src = ctx->weights + (size_t)layer * ctx->layer_bytes + (size_t)(first + e0 + e) * g.expert_bytes;
+            TG_CUDA(unpack_expert(src, ctx->staging + (size_t)e * g.expert_bytes, g, ctx->s));
+        }
+        TG_CUDA(cudaMemcpyAsync((uint8_t*)dst_host + (size_t)e0 * g.expert_bytes, ctx->staging,
+                                (size_t)m * g.expert_bytes, cudaMemcpyDeviceToHost, ctx->s));
+        TG_CUDA(cudaStreamSynchronize(ctx->s));
+    }
+    return TG_OK;
+}
+
+extern "C" int tgx_set_router(tgx_ctx* ctx, int layer, const float* R, int src_on_device) {
+    TG_CHECK(ctx && R, TG_EINVAL, "tgx_set_router: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_set_router: layer out of range");
+    DeviceGuard dg(ctx->device);
+    size_t n = (size_t)ctx->shape.n_experts * ctx->shape.embed;
+    TG_CUDA(cudaMemcpyAsync(ctx->routers + (size_t)layer * n, R, n * sizeof(float),
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->s));
+    TG_CUDA(cudaStreamSynchronize(ctx->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_fill_synthetic(tgx_ctx* ctx, uint64_t seed, float w_sigma, float r_sigma) {
+    TG_CHECK(ctx, TG_EINVAL, "tgx_fill_synthetic: null context");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    const tgx_shape& sh = ctx->shape;
+    const unsigned long long per_expert = 3ULL * g.H * g.I;  // weights per expert
+    for (int l = 0; l < sh.n_layers; l++) {
+        unsigned long long base = (unsigned long long)l * sh.n_experts * per_expert;
+        TG_CUDA(tg::launch_fill_experts_q4_0(ctx->weights + (size_t)l * ctx->layer_bytes, sh.n_experts, g, seed,
+                                             base, w_sigma, ctx->s));
+        size_t nr = (size_t)sh.n_experts * sh.embed;
+        TG_CUDA(tg::launch_fill_normal(ctx->routers + (size_t)l * nr, (long long)nr, seed ^ 0x5DEECE66Dull,
+                                       (unsigned long long)l * nr * 2, r_sigma, ctx->s));
+    }
+    TG_CUDA(cudaStreamSynchronize(ctx->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_moe_layer(tgx_ctx* ctx, int layer, float* x_dev, void* stream) {
+    TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_moe_layer: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_moe_layer: layer out of range");
+    DeviceGuard dg(ctx->device);
+    return moe_layer_launch(ctx, layer, x_dev, (cudaStream_t)stream);
+}
+
+extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int flags) {
+    TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_decode_step: null argument");
+    DeviceGuard dg(ctx->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (flags & TGX_EAGER) {
+        for (int l = 0; l < ctx->shape.n_layers; l++) TG_TRY(moe_layer_launch(ctx, l, x_dev, s));
+        return TG_OK;
+    }
+    if (!ctx->gexec || ctx->gx != x_dev) {
+        if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
+        ctx->gexec = nullptr;
+        ctx->gx = nullptr;
+        cudaGraph_t graph = nullptr;
+        TG_CUDA(cudaStreamBeginCapture(ctx->s, cudaStreamCaptureModeThreadLocal));
+        int rc = TG_OK;
+        for (int l = 0; l < ctx->shape.n_layers && rc == TG_OK; l++) rc = moe_layer_launch(ctx, l, x_dev, ctx->s);
+        cudaError_t e = cudaStreamEndCapture(ctx->s, &graph);
+        if (rc != TG_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        TG_CUDA(e);
+        e = cudaGraphInstantiate(&ctx->gexec, graph, 0);
+        cudaGraphDestroy(graph);
+        TG_CUDA(e);
+        ctx->gx = x_dev;
+    }
+    TG_CUDA(cudaGraphLaunch(ctx->gexec, s));
+    return TG_OK;
+}
+
+extern "C" int tgx_last_routing(tgx_ctx* ctx, int layer, int32_t* idx, float* w, float* logits) {
+    TG_CHECK(ctx, TG_EINVAL, "tgx_last_routing: null context");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_last_routing: layer out of range");
+    DeviceGuard dg(ctx->device);
+    TG_CUDA(cudaDeviceSynchronize());
+    const int k = ctx->shape.top_k, E = ctx->shape.n_experts;
+    if (idx) TG_CUDA(cudaMemcpy(idx, ctx->idx + (size_t)layer * k, sizeof(int) * k, cudaMemcpyDeviceToHost));
+    if (w) TG_CUDA(cudaMemcpy(w, ctx->wts + (size_t)layer * k, sizeof(float) * k, cudaMemcpyDeviceToHost));
+    if (logits)
+        TG_CUDA(cudaMemcpy(logits, ctx->logits + (size_t)layer * E, sizeof(float) * E, cudaMemcpyDeviceToHost));
+    return TG_OK;
+}

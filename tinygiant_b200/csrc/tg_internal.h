@@ -1,0 +1,65 @@
+// tg_internal.h — launchers shared between the kernel and C-ABI translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "tg_layout.h"
+
+namespace tg {
+
+// ggml Q4_0 rows -> row-split rows (same bytes, same size); src and dst may not alias.
+cudaError_t launch_repack_rows(const uint8_t* src, uint8_t* dst, long long nrows, int nb,
+                               cudaStream_t s);
+// row-split rows -> ggml Q4_0 rows.
+cudaError_t launch_unpack_rows(const uint8_t* src, uint8_t* dst, long long nrows, int nb,
+                               cudaStream_t s);
+
+// f32[n] -> activation form (and, if ggml != null, ggml Q8_0 blocks).
+cudaError_t launch_quantize_act(const float* x, int n, ActView a, uint8_t* ggml, cudaStream_t s);
+// ggml Q8_0 blocks -> activation form.
+cudaError_t launch_q8_0_to_act(const uint8_t* ggml, int nb, ActView a, cudaStream_t s);
+// f32[n] -> ggml Q4_0 blocks.
+cudaError_t launch_quantize_q4_0(const float* x, long long n, uint8_t* out, cudaStream_t s);
+
+// y[r] = row_r . x  (row-split weights, activation form input)
+cudaError_t launch_matvec(const uint8_t* W, ActView x, float* y, int rows, int nb, cudaStream_t s);
+// exact int32 block dots sumi[r][b]
+cudaError_t launch_block_dots(const uint8_t* W, ActView x, int32_t* out, int rows, int nb,
+                              cudaStream_t s);
+
+// Router: logits, top-k, softmax weights and the chosen experts' base pointers.
+// acc: int64[E] zeroed accumulators, counter: zeroed uint; both are left zeroed.
+cudaError_t launch_router_topk(const float* R, const float* x, int E, int H, int k,
+                               long long* acc, unsigned* counter, float* logits, int* idx,
+                               float* w, const uint8_t* layer_base, size_t expert_bytes,
+                               const uint8_t** expert_ptrs, cudaStream_t s);
+
+// Grouped gate/up + SwiGLU + Q8_0 requant of h for k experts.
+// experts: device array of k expert bases (row-split layout).
+// hq: k activation blocks of I/32 each, laid out expert after expert (act_bytes(nbI) each).
+// h_dbg (optional): f32 [k][I].
+cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, Geom g,
+                          uint8_t* hq, float* h_dbg, float* gu_dbg, cudaStream_t s);
+
+// Down projections of k experts + weighted combine, per output row r:
+//   acc = accumulate ? out[r] : 0;  for j: acc = acc + w[j]*y_j[r]
+//   out[r] = resid ? resid[r] + acc : acc
+// w: device float[k] (or null: use w_host_scalar for k == 1).
+cudaError_t launch_down_combine(const uint8_t* const* experts, int k, const uint8_t* hq,
+                                const float* w, float w_scalar, Geom g, const float* resid,
+                                float* out, int accumulate, float* y_dbg, cudaStream_t s);
+
+// out[i] ~ N(0, sigma); value i depends only on (seed, base + i); base must be even.
+cudaError_t launch_fill_normal(float* out, long long n, unsigned long long seed, unsigned long long base,
+                               float sigma, cudaStream_t s);
+
+// Synthetic Q4_0 experts N(0, sigma) written directly in row-split form (value index =
+// base + position in the f32 expert tensors, so a weight does not depend on the launch split).
+cudaError_t launch_fill_experts_q4_0(uint8_t* dst, int n_experts, Geom g, unsigned long long seed,
+                                     unsigned long long base, float sigma, cudaStream_t s);
+
+// Raise dynamic shared-memory limits for the shapes a context uses (call before capture).
+cudaError_t prepare_kernels(Geom g, int k);
+
+}  // namespace tg
