@@ -96,6 +96,7 @@ typedef struct {
     int n_experts;  /* routed experts per layer E (<= 1024) */
     int top_k;      /* experts per token k (<= 16) */
     int n_layers;   /* MoE layers L */
+    float rms_eps;  /* FFN RMSNorm epsilon; <= 0 selects 1e-6 (tinygiant/_constants.py RMS_EPS) */
 } tgx_shape;
 
 /* Create a context on `device` holding L x E experts and L routers in HBM.
@@ -117,19 +118,40 @@ int tgx_read_experts(tgx_ctx *ctx, int layer, int first, int n, void *dst_host);
 /* Set layer `layer`'s router, R[E][embed] fp32 row-major (engine.py:231 `self.routers[i]`). */
 int tgx_set_router(tgx_ctx *ctx, int layer, const float *R, int src_on_device);
 
+/* Set layer `layer`'s FFN RMSNorm weight w[embed] (engine.py:229 `self.ffn_norms[i]`; default all 1). */
+int tgx_set_ffn_norm(tgx_ctx *ctx, int layer, const float *w, int src_on_device);
+
 /* Fill every expert with Q4_0(N(0, w_sigma)) weights and every router with
  * N(0, r_sigma), generated on the device from `seed` (synthetic benchmark model). */
 int tgx_fill_synthetic(tgx_ctx *ctx, uint64_t seed, float w_sigma, float r_sigma);
 
-/* One routed MoE block on x_dev[embed] in place: x += sum_j w_j * expert_{idx_j}(x)
- * with idx, w = top-k/softmax of R_layer . x (tinygiant/engine.py:229-258 without norms). */
+/* One MoE block on x_dev[embed] in place, as the reference engine runs it
+ * (tinygiant/engine.py:229-258, attention excluded): normed = RMSNorm(x) * ffn_norm,
+ * idx, w = top-k / softmax of R_layer . normed, x += sum_j w_j * expert_{idx_j}(normed). */
 int tgx_moe_layer(tgx_ctx *ctx, int layer, float *x_dev, void *stream);
 
-/* One decode step: all L MoE blocks chained on x_dev[embed], x_{l+1} = x_l + moe_l(x_l).
- * flags: TGX_EAGER launches kernel by kernel; otherwise the step is replayed from a
- * CUDA graph captured on first use for this x_dev. */
+/* One decode step: all L MoE blocks chained on x_dev[embed], x_{l+1} = x_l + moe_l(norm_l(x_l)).
+ * By default one persistent kernel runs all layers (one CTA per SM, weights
+ * staged by bulk copies, no grid-wide barriers).  flags: TGX_EAGER launches
+ * directly; otherwise the step is replayed from a CUDA graph captured on first
+ * use for this x_dev.  TGX_MULTI selects the three-kernels-per-layer path. */
 #define TGX_EAGER 1
+#define TGX_MULTI 2   /* three kernels per layer instead of the single fused kernel per step */
 int tgx_decode_step(tgx_ctx *ctx, float *x_dev, void *stream, int flags);
+
+/* Synchronise the context's device and report whether a bounded wait inside the
+ * fused decode kernel expired since the last call (TG_ETIMEOUT; the kernel's
+ * cross-block state is then reset).  TG_OK otherwise. */
+int tgx_sync_status(tgx_ctx *ctx);
+
+/* Diagnostics of the fused path: its control words (epoch, finished blocks, error
+ * stage, error detail = (layer << 20) | (entry << 8) | observed count) and the first
+ * n_acc words of its routing accumulators.  Synchronises the device. */
+int tgx_fused_debug(tgx_ctx *ctx, uint32_t *ctl4, uint64_t *acc, size_t n_acc);
+
+/* The fused path's launch geometry: CTAs (0 when the shape runs on the
+ * multi-kernel path), dynamic shared memory per CTA, weight staging bytes per CTA. */
+int tgx_fused_info(tgx_ctx *ctx, int *ctas, int *smem_bytes, int *arena_bytes);
 
 /* Routing chosen by the last tgx_moe_layer / tgx_decode_step for `layer`
  * (idx[k] in ascending-logit order, w[k], logits[E]); any pointer may be NULL.

@@ -62,8 +62,10 @@ def lib():
         "ref_router_logits": (None, [VP, VP, CI, CI, VP]),
         "ref_topk_softmax": (None, [VP, CI, CI, VP, VP, CI]),
         "ref_moe_layer": (None, [VP, ctypes.c_size_t, VP, VP, CI, CI, CI, CI, CI, VP, VP, VP]),
-        "ref_decode_step": (None, [VP, VP, CI, VP, CI, CI, CI, CI, CI, VP]),
-        "ref_decode_step_mt": (None, [VP, VP, CI, VP, CI, CI, CI, CI, CI, CI]),
+        "ref_rms_scale": (CF, [VP, CI, CF]),
+        "ref_moe_block": (None, [VP, ctypes.c_size_t, VP, VP, CF, VP, CI, CI, CI, CI, CI, VP, VP, VP]),
+        "ref_decode_step": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, VP]),
+        "ref_decode_step_mt": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, CI]),
         "ref_moe_layer_batched": (None, [VP, ctypes.c_size_t, VP, VP, CI, CI, CI, CI, CI, CI, CI]),
         "ref_fill_normal": (None, [VP, I64, ctypes.c_uint64, CF]),
     }
@@ -194,24 +196,52 @@ def moe_layer(layer_blob: np.ndarray, R: np.ndarray, x: np.ndarray, k: int, embe
     return x, idx, w, logits
 
 
-def decode_step(layer_blobs, routers, x, k, embed, inter, mode=TG_MIRROR):
-    """Chained decode step over len(layer_blobs) layers; returns (x_new, idx[L,k])."""
+RMS_EPS = 1e-6
+
+
+def rms_scale(x: np.ndarray, eps: float = RMS_EPS) -> float:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    return float(lib().ref_rms_scale(_p(x), x.size, eps))
+
+
+def moe_block(layer_blob: np.ndarray, R: np.ndarray, x: np.ndarray, k: int, embed: int, inter: int,
+              normw=None, eps: float = RMS_EPS, mode=TG_MIRROR):
+    """The engine's MoE block with its FFN RMSNorm; returns (x_new, idx, w, logits)."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    E = R.shape[0]
+    idx = np.empty(k, np.int32)
+    w = np.empty(k, np.float32)
+    logits = np.empty(E, np.float32)
+    nw = None if normw is None else np.ascontiguousarray(normw, dtype=np.float32)
+    lib().ref_moe_block(_p(np.ascontiguousarray(layer_blob)), expert_bytes(embed, inter),
+                        _p(np.ascontiguousarray(R, dtype=np.float32)), None if nw is None else _p(nw), eps,
+                        _p(x), E, k, embed, inter, mode, _p(idx), _p(w), _p(logits))
+    return x, idx, w, logits
+
+
+def _ptr_array(arrs):
+    return (ctypes.c_void_p * len(arrs))(*[a.ctypes.data for a in arrs])
+
+
+def decode_step(layer_blobs, routers, x, k, embed, inter, norms=None, eps: float = RMS_EPS, mode=TG_MIRROR):
+    """Chained decode step over len(layer_blobs) MoE blocks; returns (x_new, idx[L,k])."""
     L = len(layer_blobs)
     blobs = [np.ascontiguousarray(b) for b in layer_blobs]
     rs = [np.ascontiguousarray(r, dtype=np.float32) for r in routers]
-    bp = (ctypes.c_void_p * L)(*[b.ctypes.data for b in blobs])
-    rp = (ctypes.c_void_p * L)(*[r.ctypes.data for r in rs])
+    ns = None if norms is None else [np.ascontiguousarray(n, dtype=np.float32) for n in norms]
     x = np.array(x, dtype=np.float32, copy=True)
     idx = np.empty((L, k), np.int32)
-    lib().ref_decode_step(bp, rp, L, _p(x), rs[0].shape[0], k, embed, inter, mode, _p(idx))
+    lib().ref_decode_step(_ptr_array(blobs), _ptr_array(rs), None if ns is None else _ptr_array(ns), eps, L,
+                          _p(x), rs[0].shape[0], k, embed, inter, mode, _p(idx))
     return x, idx
 
 
-def decode_step_mt(layer_blobs, routers, x, k, embed, inter, mode=TG_MIRROR, n_threads=0):
+def decode_step_mt(layer_blobs, routers, x, k, embed, inter, mode=TG_MIRROR, n_threads=0, norms=None,
+                   eps: float = RMS_EPS):
     L = len(layer_blobs)
-    bp = (ctypes.c_void_p * L)(*[b.ctypes.data for b in layer_blobs])
-    rp = (ctypes.c_void_p * L)(*[r.ctypes.data for r in routers])
-    lib().ref_decode_step_mt(bp, rp, L, _p(x), routers[0].shape[0], k, embed, inter, mode, n_threads)
+    lib().ref_decode_step_mt(_ptr_array(layer_blobs), _ptr_array(routers),
+                             None if norms is None else _ptr_array(norms), eps, L, _p(x), routers[0].shape[0],
+                             k, embed, inter, mode, n_threads)
     return x
 
 

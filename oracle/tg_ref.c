@@ -310,22 +310,21 @@ void ref_expert_forward(const uint8_t *gate, const uint8_t *up, const uint8_t *d
 
 /*
  * Router logits (engine.py:231, logits = router @ normed).  Each product
- * R[e][r]*x[r] is rounded to fp32, clamped to +-2^22, converted to fixed point
- * with 2^-40 units (round to nearest even) and summed in int64, so the sum is
+ * R[e][r]*x[r] is rounded to fp32, clamped to +-512, converted to fixed point
+ * with 2^-32 units (round to nearest even) and summed in int64, so the sum is
  * exact and independent of how the rows are split across threads or blocks:
- *   logit_e = float(2^-40 * sum_r rint(clamp(fl(R[e][r]*x[r])) * 2^40))
+ *   logit_e = float(2^-32 * sum_r rint(clamp(fl(R[e][r]*x[r])) * 2^32))
  */
 static inline int64_t router_fixed(float r, float x) {
     float p = r * x;
-    p = fminf(fmaxf(p, -0x1p22f), 0x1p22f);
-    return llrintf(p * 0x1p40f);
+    p = fminf(fmaxf(p, -512.0f), 512.0f);
+    return llrintf(p * 0x1p32f);
 }
-
 void ref_router_logits(const float *R, const float *x, int n_experts, int hidden, float *logits) {
     for (int e = 0; e < n_experts; e++) {
         int64_t s = 0;
         for (int r = 0; r < hidden; r++) s += router_fixed(R[(size_t)e * hidden + r], x[r]);
-        logits[e] = (float)((double)s * 0x1p-40);
+        logits[e] = (float)((double)s * 0x1p-32);
     }
 }
 
@@ -360,6 +359,39 @@ void ref_topk_softmax(const float *logits, int n_experts, int k, int32_t *idx, f
     for (int j = 0; j < k; j++) w[j] = ex[j] / s;
 }
 
+/* ------------------------------------------------------------------ RMS norm */
+
+/*
+ * The FFN RMSNorm in front of each MoE block (engine.py:229-230, tg_rms_norm
+ * csrc/libtinygiant.c:322-340: scale = 1/sqrtf(ss/dim + eps), out = (x*scale)*w).
+ * ss is summed exactly in fixed point: each fl(x*x), clamped to [0, 2^22], in
+ * units of 2^-16, so the sum does not depend on how rows are split.
+ */
+static inline int64_t ss_fixed(float x) {
+    float p = x * x;
+    p = fminf(p, 0x1p22f);
+    return llrintf(p * 0x1p16f);
+}
+
+float ref_rms_scale(const float *x, int dim, float eps) {
+    int64_t s = 0;
+    for (int r = 0; r < dim; r++) s += ss_fixed(x[r]);
+    float ss = (float)((double)s * 0x1p-16);
+    return 1.0f / sqrtf(ss / (float)dim + eps);
+}
+
+/* Router logits of the normed input without forming it first:
+ * logit_e = fl(scale * float(2^-40 * sum_r rint(fl(R[e][r] * fl(x_r * w_r)) * 2^40))),
+ * i.e. R . normed with the scalar RMS scale applied after the exact sum. */
+static void block_logits(const float *R, const float *x, const float *w, float scale,
+                         int n_experts, int hidden, float *logits) {
+    for (int e = 0; e < n_experts; e++) {
+        int64_t s = 0;
+        for (int r = 0; r < hidden; r++) s += router_fixed(R[(size_t)e * hidden + r], w ? x[r] * w[r] : x[r]);
+        logits[e] = scale * (float)((double)s * 0x1p-32);
+    }
+}
+
 /* ------------------------------------------------------------------ MoE block */
 
 static void expert_ptrs(const uint8_t *blob, int embed, int inter,
@@ -392,33 +424,64 @@ void ref_moe_layer(const uint8_t *layer_blob, size_t expert_bytes, const float *
     free(logits);
 }
 
+/* The engine's MoE block (engine.py:229-258 without attention): normed =
+ * RMSNorm(x) * w, route on normed, run the top-k experts on normed, x += moe. */
+void ref_moe_block(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                   float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
+                   int32_t *idx_out, float *w_out, float *logits_out) {
+    float *logits = malloc(sizeof(float) * n_experts);
+    float *normed = malloc(sizeof(float) * embed);
+    int32_t idx[64];
+    float w[64];
+    float scale = ref_rms_scale(x, embed, eps);
+    block_logits(R, x, normw, scale, n_experts, embed, logits);
+    ref_topk_softmax(logits, n_experts, k, idx, w, mode);
+    for (int r = 0; r < embed; r++) normed[r] = normw ? (x[r] * scale) * normw[r] : x[r] * scale;
+    float *moe = calloc((size_t)embed, sizeof(float));
+    for (int j = 0; j < k; j++) {
+        const uint8_t *g, *u, *d;
+        expert_ptrs(layer_blob + (size_t)idx[j] * expert_bytes, embed, inter, &g, &u, &d);
+        ref_expert_forward(g, u, d, normed, moe, w[j], embed, inter, mode);
+    }
+    for (int i = 0; i < embed; i++) x[i] = x[i] + moe[i];
+    if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * k);
+    if (w_out) memcpy(w_out, w, sizeof(float) * k);
+    if (logits_out) memcpy(logits_out, logits, sizeof(float) * n_experts);
+    free(moe);
+    free(normed);
+    free(logits);
+}
+
 void ref_decode_step(const uint8_t *const *layer_blobs, const float *const *routers,
-                     int n_layers, float *x, int n_experts, int k, int embed, int inter,
-                     int mode, int32_t *idx_out) {
+                     const float *const *norms, float eps, int n_layers, float *x, int n_experts, int k,
+                     int embed, int inter, int mode, int32_t *idx_out) {
     size_t eb = (size_t)3 * inter * (embed / REF_QK) * REF_Q4_0_BYTES;
     for (int l = 0; l < n_layers; l++)
-        ref_moe_layer(layer_blobs[l], eb, routers[l], x, n_experts, k, embed, inter, mode,
-                      idx_out ? idx_out + (size_t)l * k : NULL, NULL, NULL);
+        ref_moe_block(layer_blobs[l], eb, routers[l], norms ? norms[l] : NULL, eps, x, n_experts, k, embed,
+                      inter, mode, idx_out ? idx_out + (size_t)l * k : NULL, NULL, NULL);
 }
 
 /* ------------------------------------------------------------------ threaded */
 
 /* One MoE block with the per-row work spread over threads; same arithmetic as
  * ref_moe_layer (each row is still computed by one thread in the same order). */
-static void moe_layer_mt(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
-                         float *x, int n_experts, int k, int embed, int inter, int mode,
-                         uint8_t *xq, float *h, uint8_t *hq, float *logits) {
+static void moe_layer_mt(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                         float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
+                         uint8_t *xq, float *h, uint8_t *hq, float *logits, float *normed) {
     int nbe = embed / REF_QK, nbi = inter / REF_QK;
     int32_t idx[64];
     float w[64];
+    float scale = ref_rms_scale(x, embed, eps);
     #pragma omp parallel for schedule(static)
     for (int e = 0; e < n_experts; e++) {
         int64_t s = 0;
-        for (int r = 0; r < embed; r++) s += router_fixed(R[(size_t)e * embed + r], x[r]);
-        logits[e] = (float)((double)s * 0x1p-40);
+        for (int r = 0; r < embed; r++)
+            s += router_fixed(R[(size_t)e * embed + r], normw ? x[r] * normw[r] : x[r]);
+        logits[e] = scale * (float)((double)s * 0x1p-32);
     }
     ref_topk_softmax(logits, n_experts, k, idx, w, mode);
-    ref_quantize_q8_0(x, xq, embed);
+    for (int r = 0; r < embed; r++) normed[r] = normw ? (x[r] * scale) * normw[r] : x[r] * scale;
+    ref_quantize_q8_0(normed, xq, embed);
     size_t tb = (size_t)inter * nbe * REF_Q4_0_BYTES;
     #pragma omp parallel for schedule(static)
     for (int t = 0; t < k * inter; t++) {
@@ -444,8 +507,8 @@ static void moe_layer_mt(const uint8_t *layer_blob, size_t expert_bytes, const f
 }
 
 void ref_decode_step_mt(const uint8_t *const *layer_blobs, const float *const *routers,
-                        int n_layers, float *x, int n_experts, int k, int embed, int inter,
-                        int mode, int n_threads) {
+                        const float *const *norms, float eps, int n_layers, float *x, int n_experts, int k,
+                        int embed, int inter, int mode, int n_threads) {
 #ifdef _OPENMP
     if (n_threads > 0) omp_set_num_threads(n_threads);
 #else
@@ -456,10 +519,11 @@ void ref_decode_step_mt(const uint8_t *const *layer_blobs, const float *const *r
     float *h = malloc(sizeof(float) * (size_t)k * inter);
     uint8_t *hq = malloc((size_t)k * (inter / REF_QK) * REF_Q8_0_BYTES);
     float *logits = malloc(sizeof(float) * n_experts);
+    float *normed = malloc(sizeof(float) * embed);
     for (int l = 0; l < n_layers; l++)
-        moe_layer_mt(layer_blobs[l], eb, routers[l], x, n_experts, k, embed, inter, mode,
-                     xq, h, hq, logits);
-    free(xq); free(h); free(hq); free(logits);
+        moe_layer_mt(layer_blobs[l], eb, routers[l], norms ? norms[l] : NULL, eps, x, n_experts, k, embed,
+                     inter, mode, xq, h, hq, logits, normed);
+    free(xq); free(h); free(hq); free(logits); free(normed);
 }
 
 void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R,

@@ -75,8 +75,18 @@ void ref_moe_layer(const uint8_t *layer_blob, size_t expert_bytes, const float *
                    float *x, int n_experts, int k, int embed, int inter, int mode,
                    int32_t *idx, float *w, float *logits);
 
-/* Decode step: n_layers chained MoE blocks, x_{l+1} = x_l + moe_l(x_l). */
+/* FFN RMSNorm scale 1/sqrtf(ss/dim + eps) with ss summed exactly in fixed point. */
+float ref_rms_scale(const float *x, int dim, float eps);
+
+/* The engine's MoE block: normed = RMSNorm(x)*normw (normw NULL = ones), route
+ * and run the experts on normed, x += weighted expert sum (engine.py:229-258). */
+void ref_moe_block(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                   float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
+                   int32_t *idx, float *w, float *logits);
+
+/* Decode step: n_layers chained MoE blocks, x_{l+1} = x_l + moe_l(norm_l(x_l)). */
 void ref_decode_step(const uint8_t *const *layer_blobs, const float *const *routers,
+                     const float *const *norms /* [n_layers] or NULL */, float eps,
                      int n_layers, float *x, int n_experts, int k, int embed, int inter,
                      int mode, int32_t *idx_out /* [n_layers*k] or NULL */);
 
@@ -87,8 +97,8 @@ void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const
 
 /* Multi-threaded decode step for the CPU baseline (OpenMP over rows). */
 void ref_decode_step_mt(const uint8_t *const *layer_blobs, const float *const *routers,
-                        int n_layers, float *x, int n_experts, int k, int embed, int inter,
-                        int mode, int n_threads);
+                        const float *const *norms, float eps, int n_layers, float *x, int n_experts, int k,
+                        int embed, int inter, int mode, int n_threads);
 
 /* Seeded synthetic data: splitmix64 stream -> N(0, sigma) floats (Box-Muller). */
 void ref_fill_normal(float *out, int64_t n, uint64_t seed, float sigma);

@@ -46,9 +46,9 @@ def test_argument_errors_without_device():
     assert lib.tg_expert_forward_q4_0(out.ctypes.data, x.ctypes.data, x.ctypes.data, 1.0, 2000, 768) == L.TG_EINVAL
     assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, L.TG_FMT_Q6_K,
                                        x.ctypes.data, x.ctypes.data, 1.0, 2048, 768) == L.TG_EUNSUPPORTED
-    shape = L.TgxShape(2048, 768, 128, 8, 48)
+    shape = L.TgxShape(2048, 768, 128, 8, 48, 1e-6)
     h = ctypes.c_void_p()
-    bad = L.TgxShape(2048, 768, 128, 200, 48)
+    bad = L.TgxShape(2048, 768, 128, 200, 48, 1e-6)
     assert lib.tgx_ctx_create(0, ctypes.byref(bad), ctypes.byref(h)) == L.TG_EINVAL
     if lib.tg_device_count() == 0:
         assert lib.tgx_ctx_create(0, ctypes.byref(shape), ctypes.byref(h)) == L.TG_ENODEV

@@ -119,16 +119,37 @@ def test_moe_layer_and_decode_consistent(oracle):
     blobs = [oracle.quantize_q4_0((rng.standard_normal(E * 3 * H * I) * 0.02).astype(np.float32)) for _ in range(L)]
     assert blobs[0].size == E * eb
     Rs = [(rng.standard_normal((E, H)) * 0.02).astype(np.float32) for _ in range(L)]
+    Ns = [(1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32) for _ in range(L)]
     x = rng.standard_normal(H).astype(np.float32)
     xs = x.copy()
     for l in range(L):
-        xs, idx, w, logits = oracle.moe_layer(blobs[l], Rs[l], xs, k, H, I)
+        xs, idx, w, logits = oracle.moe_block(blobs[l], Rs[l], xs, k, H, I, normw=Ns[l])
         assert len(set(idx.tolist())) == k
-    xd, idx_all = oracle.decode_step(blobs, Rs, x, k, H, I)
+    xd, idx_all = oracle.decode_step(blobs, Rs, x, k, H, I, norms=Ns)
     assert np.array_equal(xd, xs)
     xm = x.copy()
-    oracle.decode_step_mt(blobs, Rs, xm, k, H, I, 1, 4)
+    oracle.decode_step_mt(blobs, Rs, xm, k, H, I, 1, 4, norms=Ns)
     assert np.array_equal(xm, xs)
+
+
+def test_rms_norm_block_matches_engine_order(oracle):
+    """The MoE block's norm follows tg_rms_norm (csrc/libtinygiant.c:322-340):
+    routing and expert input are RMSNorm(x) * w; the residual adds to raw x."""
+    rng = np.random.default_rng(13)
+    H, I, E, k = 256, 256, 8, 2
+    blob = oracle.quantize_q4_0((rng.standard_normal(E * 3 * H * I) * 0.02).astype(np.float32))
+    R = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+    nw = (1.0 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+    x = (3.0 * rng.standard_normal(H)).astype(np.float32)
+    scale = oracle.rms_scale(x)
+    assert abs(scale - 1.0 / np.sqrt(np.mean(x.astype(np.float64) ** 2) + 1e-6)) < 1e-6 * scale
+    normed = (x * np.float32(scale)) * nw
+    xn, idx, w, logits = oracle.moe_block(blob, R, x, k, H, I, normw=nw)
+    l64 = R.astype(np.float64) @ normed.astype(np.float64)
+    assert np.max(np.abs(logits - l64)) < 1e-5
+    xl, idx2, w2, _ = oracle.moe_layer(blob, R, normed, k, H, I)   # same block on the pre-normed input
+    assert np.array_equal(idx, idx2)
+    assert np.array_equal(xn - x, (xl - normed)) or np.max(np.abs((xn - x) - (xl - normed))) < 1e-6
 
 
 def test_engine_order_combine(oracle):

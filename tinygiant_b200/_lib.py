@@ -34,6 +34,7 @@ TG_FMT_Q6_K = 2
 TG_FMT_Q4_0 = 3
 
 TGX_EAGER = 1
+TGX_MULTI = 2
 
 LIB_NAME = "libtinygiant.so"
 
@@ -45,7 +46,8 @@ class TinyGiantError(RuntimeError):
 
 
 class TgxShape(ctypes.Structure):
-    _fields_ = [("embed", CI), ("inter", CI), ("n_experts", CI), ("top_k", CI), ("n_layers", CI)]
+    _fields_ = [("embed", CI), ("inter", CI), ("n_experts", CI), ("top_k", CI), ("n_layers", CI),
+                ("rms_eps", CF)]
 
 
 # name -> (restype, argtypes); the order follows include/tinygiant.h
@@ -67,9 +69,13 @@ PROTOTYPES = {
     "tgx_load_experts": (CI, [VP, CI, CI, CI, VP, CI]),
     "tgx_read_experts": (CI, [VP, CI, CI, CI, VP]),
     "tgx_set_router": (CI, [VP, CI, VP, CI]),
+    "tgx_set_ffn_norm": (CI, [VP, CI, VP, CI]),
     "tgx_fill_synthetic": (CI, [VP, U64, CF, CF]),
     "tgx_moe_layer": (CI, [VP, CI, VP, VP]),
     "tgx_decode_step": (CI, [VP, VP, VP, CI]),
+    "tgx_sync_status": (CI, [VP]),
+    "tgx_fused_info": (CI, [VP, VP, VP, VP]),
+    "tgx_fused_debug": (CI, [VP, VP, VP, SZ]),
     "tgx_last_routing": (CI, [VP, CI, VP, VP, VP]),
 }
 

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../include/tinygiant.h"
+#include "tg_decode.h"
 #include "tg_internal.h"
 
 using tg::ActView;
@@ -138,8 +139,8 @@ int run_experts(HostWS& W, const Geom& g, int n, const float* weights_host, floa
         wdev = (const float*)W.wts.p;
     }
     TG_CUDA(tg::prepare_kernels(g, n));
-    TG_CUDA(tg::launch_gateup((const uint8_t* const*)W.ptrs.p, n, (const float*)W.x.p, g, (uint8_t*)W.hq.p,
-                              nullptr, nullptr, W.s));
+    TG_CUDA(tg::launch_gateup((const uint8_t* const*)W.ptrs.p, n, (const float*)W.x.p, nullptr, nullptr, g,
+                              (uint8_t*)W.hq.p, nullptr, nullptr, W.s));
     TG_CUDA(tg::launch_down_combine((const uint8_t* const*)W.ptrs.p, n, (const uint8_t*)W.hq.p, wdev, w_scalar,
                                     g, nullptr, (float*)W.out.p, accumulate, nullptr, W.s));
     return TG_OK;
@@ -321,7 +322,10 @@ struct tgx_ctx {
     size_t layer_bytes = 0;
     uint8_t* weights = nullptr;   // [L][E] experts, row-split
     float* routers = nullptr;     // [L][E][H]
-    long long* acc = nullptr;     // [E] router accumulators (kept zero between uses)
+    float eps = 1e-6f;            // FFN RMSNorm epsilon
+    float* norms = nullptr;       // [L][H] FFN RMSNorm weights (default 1)
+    float* nscale = nullptr;      // RMSNorm scale of the current layer (multi-kernel path)
+    long long* acc = nullptr;     // [E + 1] router / sum-of-squares accumulators (kept zero)
     unsigned* counter = nullptr;  // router block counter (kept zero)
     float* logits = nullptr;      // [L][E]
     int* idx = nullptr;           // [L][k]
@@ -332,7 +336,19 @@ struct tgx_ctx {
     size_t staging_bytes = 0;
     cudaStream_t s = nullptr;     // loads, synthetic fill, graph capture
     cudaGraphExec_t gexec = nullptr;
-    float* gx = nullptr;
+    const float* gx = nullptr;
+    // fused (one kernel per step) path
+    bool fused_ok = false;
+    int G = 0;                          // CTAs = SMs
+    float* RT = nullptr;                // [L][H][E] transposed routers
+    float* xbuf = nullptr;              // [L + 1][H]
+    unsigned long long* facc = nullptr; // [L][E]
+    unsigned long long* hqt = nullptr;  // [L][k * nbI * 6]
+    unsigned* ctl = nullptr;            // epoch, finish count, error
+    uint16_t* plan = nullptr;
+    tg::FusedParams fp{};
+    cudaGraphExec_t fexec = nullptr;
+    const float* fx = nullptr;
 };
 
 namespace {
@@ -352,8 +368,11 @@ void ctx_free(tgx_ctx* c) {
     if (!c) return;
     DeviceGuard dg(c->device);
     if (c->gexec) cudaGraphExecDestroy(c->gexec);
-    for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->acc, (void*)c->counter, (void*)c->logits,
-                    (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging})
+    if (c->fexec) cudaGraphExecDestroy(c->fexec);
+    for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->nscale, (void*)c->acc,
+                    (void*)c->counter, (void*)c->logits,
+                    (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging, (void*)c->RT,
+                    (void*)c->xbuf, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -365,11 +384,100 @@ int moe_layer_launch(tgx_ctx* c, int layer, float* x, cudaStream_t s) {
     const uint8_t* lb = c->weights + (size_t)layer * c->layer_bytes;
     const uint8_t** ep = c->eptrs + (size_t)layer * k;
     float* w = c->wts + (size_t)layer * k;
-    TG_CUDA(tg::launch_router_topk(c->routers + (size_t)layer * E * H, x, E, H, k, c->acc, c->counter,
-                                   c->logits + (size_t)layer * E, c->idx + (size_t)layer * k, w, lb,
+    const float* nw = c->norms + (size_t)layer * H;
+    TG_CUDA(tg::launch_router_topk(c->routers + (size_t)layer * E * H, x, nw, c->eps, E, H, k, c->acc, c->counter,
+                                   c->logits + (size_t)layer * E, c->idx + (size_t)layer * k, w, c->nscale, lb,
                                    c->g.expert_bytes, ep, s));
-    TG_CUDA(tg::launch_gateup(ep, k, x, c->g, c->hq, nullptr, nullptr, s));
+    TG_CUDA(tg::launch_gateup(ep, k, x, nw, c->nscale, c->g, c->hq, nullptr, nullptr, s));
     TG_CUDA(tg::launch_down_combine(ep, k, c->hq, w, 0.0f, c->g, x, x, 0, nullptr, s));
+    return TG_OK;
+}
+
+// Allocate the fused path's state and plan its work split; the fused path is
+// disabled (fused_ok = false) when the shape does not fit one CTA per SM.
+int fused_setup(tgx_ctx* c) {
+    const tgx_shape& sh = c->shape;
+    const int L = sh.n_layers, E = sh.n_experts, k = sh.top_k, H = sh.embed;
+    int dev = c->device, sms = 0, smem_optin = 0;
+    TG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    TG_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    auto A = [&](void** p, size_t n) -> int {
+        if (cudaMalloc(p, n) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(TG_ENOMEM, "tgx_ctx_create: cudaMalloc of " + std::to_string(n) + " bytes failed");
+        }
+        return TG_OK;
+    };
+    int rc;
+    if ((rc = A((void**)&c->RT, sizeof(float) * (size_t)L * E * H)) ||
+        (rc = A((void**)&c->xbuf, sizeof(float) * (size_t)(L + 1) * H)) ||
+        (rc = A((void**)&c->facc, sizeof(unsigned long long) * (size_t)L * (E + 1))) ||
+        (rc = A((void**)&c->hqt, sizeof(unsigned long long) * (size_t)L * k * c->g.nbI * 6)) ||
+        (rc = A((void**)&c->ctl, sizeof(unsigned) * 4)))
+        return rc;
+    TG_CUDA(cudaMemset(c->RT, 0, sizeof(float) * (size_t)L * E * H));
+    TG_CUDA(cudaMemset(c->facc, 0, sizeof(unsigned long long) * (size_t)L * (E + 1)));
+    TG_CUDA(cudaMemset(c->hqt, 0, sizeof(unsigned long long) * (size_t)L * k * c->g.nbI * 6));
+    TG_CUDA(cudaMemset(c->ctl, 0, sizeof(unsigned) * 4));
+    std::vector<uint16_t> plan;
+    size_t arena = 0;
+    int stride = 0;
+    const int rd = 4;
+    if (sms > 255 || c->g.H > 16384) return TG_OK;  // count tags and fixed-point bounds
+    if (tg::fused_plan(c->g, E, k, sms, rd, plan, arena, stride) != 0) return TG_OK;  // fused path off
+    tg::FusedParams& P = c->fp;
+    P.weights = c->weights;
+    P.layer_bytes = c->layer_bytes;
+    P.g = c->g;
+    P.RT = c->RT;
+    P.normw = c->norms;
+    P.eps = c->eps;
+    P.E = E;
+    P.k = k;
+    P.rd = rd;
+    P.L0 = 0;
+    P.nL = L;
+    P.xbuf = c->xbuf;
+    P.acc = c->facc;
+    P.hqt = c->hqt;
+    P.ctl = c->ctl;
+    P.plan_stride = stride;
+    P.idx_out = c->idx;
+    P.w_out = c->wts;
+    P.logits_out = c->logits;
+    P.h_dbg = nullptr;
+    P.arena_bytes = arena;
+    if (tg::fused_smem_layout(P).total > (uint32_t)smem_optin) return TG_OK;
+    if ((rc = A((void**)&c->plan, plan.size() * sizeof(uint16_t)))) return rc;
+    TG_CUDA(cudaMemcpy(c->plan, plan.data(), plan.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    P.plan = c->plan;
+    TG_CUDA(tg::fused_prepare(P));
+    int per_sm = 0;
+    TG_CUDA(tg::fused_occupancy(P, &per_sm));
+    if (per_sm < 1) return TG_OK;
+    c->G = sms;
+    c->fused_ok = true;
+    return TG_OK;
+}
+
+// Launch the fused kernel for layers [L0, L0 + nL) on x (in place).
+int fused_launch(tgx_ctx* c, int L0, int nL, float* x, cudaStream_t s) {
+    tg::FusedParams P = c->fp;
+    P.L0 = L0;
+    P.nL = nL;
+    P.x_in = x;
+    // in place is safe when nL >= 2 (every read of x_in precedes the last layer's writes)
+    P.x_out = nL >= 2 ? x : c->xbuf + (size_t)nL * c->g.H;
+    TG_CUDA(tg::launch_decode_fused(P, c->G, s));
+    if (nL < 2)
+        TG_CUDA(cudaMemcpyAsync(x, P.x_out, sizeof(float) * c->g.H, cudaMemcpyDeviceToDevice, s));
+    return TG_OK;
+}
+
+int transpose_router(tgx_ctx* c, int layer) {
+    const size_t n = (size_t)c->shape.n_experts * c->shape.embed;
+    TG_CUDA(tg::launch_transpose(c->routers + (size_t)layer * n, c->RT + (size_t)layer * n, c->shape.n_experts,
+                                 c->shape.embed, c->s));
     return TG_OK;
 }
 
@@ -403,14 +511,23 @@ extern "C" int tgx_ctx_create(int device, const tgx_shape* shape, tgx_ctx** out)
     };
     int rc = TG_OK;
     if ((rc = A((void**)&c->weights, c->layer_bytes * L)) || (rc = A((void**)&c->routers, sizeof(float) * L * E * H)) ||
-        (rc = A((void**)&c->acc, sizeof(long long) * E)) || (rc = A((void**)&c->counter, sizeof(unsigned))) ||
+        (rc = A((void**)&c->norms, sizeof(float) * L * H)) || (rc = A((void**)&c->nscale, sizeof(float))) ||
+        (rc = A((void**)&c->acc, sizeof(long long) * (E + 1))) || (rc = A((void**)&c->counter, sizeof(unsigned))) ||
         (rc = A((void**)&c->logits, sizeof(float) * L * E)) || (rc = A((void**)&c->idx, sizeof(int) * L * k)) ||
         (rc = A((void**)&c->wts, sizeof(float) * L * k)) || (rc = A((void**)&c->eptrs, sizeof(void*) * L * k)) ||
         (rc = A((void**)&c->hq, tg::act_bytes(c->g.nbI) * k)) || (rc = A((void**)&c->staging, c->staging_bytes))) {
         ctx_free(c);
         return rc;
     }
-    cudaError_t e = cudaMemset(c->acc, 0, sizeof(long long) * E);
+    if (shape->rms_eps > 0.0f) c->eps = shape->rms_eps;
+    {
+        std::vector<float> ones((size_t)L * H, 1.0f);
+        if (cudaMemcpy(c->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) {
+            ctx_free(c);
+            return fail(TG_ECUDA, "tgx_ctx_create: norm weight init failed");
+        }
+    }
+    cudaError_t e = cudaMemset(c->acc, 0, sizeof(long long) * (E + 1));
     if (e == cudaSuccess) e = cudaMemset(c->counter, 0, sizeof(unsigned));
     if (e == cudaSuccess) e = cudaMemset(c->routers, 0, sizeof(float) * L * E * H);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->s, cudaStreamNonBlocking);
@@ -418,6 +535,10 @@ extern "C" int tgx_ctx_create(int device, const tgx_shape* shape, tgx_ctx** out)
     if (e != cudaSuccess) {
         ctx_free(c);
         return fail(TG_ECUDA, std::string("tgx_ctx_create: ") + cudaGetErrorString(e));
+    }
+    if ((rc = fused_setup(c)) != TG_OK) {
+        ctx_free(c);
+        return rc;
     }
     *out = c;
     return TG_OK;
@@ -479,6 +600,18 @@ extern "C" int tgx_set_router(tgx_ctx* ctx, int layer, const float* R, int src_o
     size_t n = (size_t)ctx->shape.n_experts * ctx->shape.embed;
     TG_CUDA(cudaMemcpyAsync(ctx->routers + (size_t)layer * n, R, n * sizeof(float),
                             src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->s));
+    TG_TRY(transpose_router(ctx, layer));
+    TG_CUDA(cudaStreamSynchronize(ctx->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_set_ffn_norm(tgx_ctx* ctx, int layer, const float* w, int src_on_device) {
+    TG_CHECK(ctx && w, TG_EINVAL, "tgx_set_ffn_norm: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_set_ffn_norm: layer out of range");
+    DeviceGuard dg(ctx->device);
+    size_t n = (size_t)ctx->shape.embed;
+    TG_CUDA(cudaMemcpyAsync(ctx->norms + (size_t)layer * n, w, n * sizeof(float),
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->s));
     TG_CUDA(cudaStreamSynchronize(ctx->s));
     return TG_OK;
 }
@@ -496,6 +629,7 @@ extern "C" int tgx_fill_synthetic(tgx_ctx* ctx, uint64_t seed, float w_sigma, fl
         size_t nr = (size_t)sh.n_experts * sh.embed;
         TG_CUDA(tg::launch_fill_normal(ctx->routers + (size_t)l * nr, (long long)nr, seed ^ 0x5DEECE66Dull,
                                        (unsigned long long)l * nr * 2, r_sigma, ctx->s));
+        TG_TRY(transpose_router(ctx, l));
     }
     TG_CUDA(cudaStreamSynchronize(ctx->s));
     return TG_OK;
@@ -505,6 +639,7 @@ extern "C" int tgx_moe_layer(tgx_ctx* ctx, int layer, float* x_dev, void* stream
     TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_moe_layer: null argument");
     TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_moe_layer: layer out of range");
     DeviceGuard dg(ctx->device);
+    if (ctx->fused_ok) return fused_launch(ctx, layer, 1, x_dev, (cudaStream_t)stream);
     return moe_layer_launch(ctx, layer, x_dev, (cudaStream_t)stream);
 }
 
@@ -512,30 +647,76 @@ extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int fla
     TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_decode_step: null argument");
     DeviceGuard dg(ctx->device);
     cudaStream_t s = (cudaStream_t)stream;
+    const bool fused = ctx->fused_ok && !(flags & TGX_MULTI);
     if (flags & TGX_EAGER) {
+        if (fused) return fused_launch(ctx, 0, ctx->shape.n_layers, x_dev, s);
         for (int l = 0; l < ctx->shape.n_layers; l++) TG_TRY(moe_layer_launch(ctx, l, x_dev, s));
         return TG_OK;
     }
-    if (!ctx->gexec || ctx->gx != x_dev) {
-        if (ctx->gexec) cudaGraphExecDestroy(ctx->gexec);
-        ctx->gexec = nullptr;
-        ctx->gx = nullptr;
+    cudaGraphExec_t& exec = fused ? ctx->fexec : ctx->gexec;
+    const float*& gx = fused ? ctx->fx : ctx->gx;
+    if (!exec || gx != x_dev) {
+        if (exec) cudaGraphExecDestroy(exec);
+        exec = nullptr;
+        gx = nullptr;
         cudaGraph_t graph = nullptr;
         TG_CUDA(cudaStreamBeginCapture(ctx->s, cudaStreamCaptureModeThreadLocal));
         int rc = TG_OK;
-        for (int l = 0; l < ctx->shape.n_layers && rc == TG_OK; l++) rc = moe_layer_launch(ctx, l, x_dev, ctx->s);
+        if (fused) {
+            rc = fused_launch(ctx, 0, ctx->shape.n_layers, x_dev, ctx->s);
+        } else {
+            for (int l = 0; l < ctx->shape.n_layers && rc == TG_OK; l++) rc = moe_layer_launch(ctx, l, x_dev, ctx->s);
+        }
         cudaError_t e = cudaStreamEndCapture(ctx->s, &graph);
         if (rc != TG_OK) {
             if (graph) cudaGraphDestroy(graph);
             return rc;
         }
         TG_CUDA(e);
-        e = cudaGraphInstantiate(&ctx->gexec, graph, 0);
+        e = cudaGraphInstantiate(&exec, graph, 0);
         cudaGraphDestroy(graph);
         TG_CUDA(e);
-        ctx->gx = x_dev;
+        gx = x_dev;
     }
-    TG_CUDA(cudaGraphLaunch(ctx->gexec, s));
+    TG_CUDA(cudaGraphLaunch(exec, s));
+    return TG_OK;
+}
+
+extern "C" int tgx_sync_status(tgx_ctx* ctx) {
+    TG_CHECK(ctx, TG_EINVAL, "tgx_sync_status: null context");
+    DeviceGuard dg(ctx->device);
+    TG_CUDA(cudaDeviceSynchronize());
+    if (!ctx->ctl) return TG_OK;
+    unsigned ctl[4];
+    TG_CUDA(cudaMemcpy(ctl, ctx->ctl, sizeof(ctl), cudaMemcpyDeviceToHost));
+    if (ctl[2] == 0) return TG_OK;
+    // a bounded wait expired inside the fused kernel: reset its cross-CTA state
+    const tgx_shape& sh = ctx->shape;
+    TG_CUDA(cudaMemset(ctx->facc, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * (sh.n_experts + 1)));
+    TG_CUDA(cudaMemset(ctx->hqt, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * sh.top_k * ctx->g.nbI * 6));
+    unsigned fresh[4] = {ctl[0] + 1, 0, 0, 0};
+    TG_CUDA(cudaMemcpy(ctx->ctl, fresh, sizeof(fresh), cudaMemcpyHostToDevice));
+    return fail(TG_ETIMEOUT, "fused decode: a bounded device wait expired (stage " + std::to_string(ctl[2]) +
+                                 ", layer " + std::to_string(ctl[3] >> 20) + ", entry " +
+                                 std::to_string((ctl[3] >> 8) & 0xfff) + ", seen " + std::to_string(ctl[3] & 0xff) +
+                                 ", finished blocks " + std::to_string(ctl[1]) + ")");
+}
+
+extern "C" int tgx_fused_debug(tgx_ctx* ctx, uint32_t* ctl4, uint64_t* acc, size_t n_acc) {
+    TG_CHECK(ctx && ctl4, TG_EINVAL, "tgx_fused_debug: null argument");
+    DeviceGuard dg(ctx->device);
+    TG_CUDA(cudaDeviceSynchronize());
+    TG_CUDA(cudaMemcpy(ctl4, ctx->ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost));
+    size_t have = (size_t)ctx->shape.n_layers * (ctx->shape.n_experts + 1);
+    if (acc && n_acc) TG_CUDA(cudaMemcpy(acc, ctx->facc, (n_acc < have ? n_acc : have) * 8, cudaMemcpyDeviceToHost));
+    return TG_OK;
+}
+
+extern "C" int tgx_fused_info(tgx_ctx* ctx, int* ctas, int* smem_bytes, int* arena_bytes) {
+    TG_CHECK(ctx, TG_EINVAL, "tgx_fused_info: null context");
+    if (ctas) *ctas = ctx->fused_ok ? ctx->G : 0;
+    if (smem_bytes) *smem_bytes = ctx->fused_ok ? (int)tg::fused_smem_layout(ctx->fp).total : 0;
+    if (arena_bytes) *arena_bytes = ctx->fused_ok ? (int)ctx->fp.arena_bytes : 0;
     return TG_OK;
 }
 

@@ -48,6 +48,13 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
     return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
 }
 
+// A lane's share of a block's abs-max: |v|, or 0 for NaN, so the block amax is
+// max(0, max over non-NaN |v|) (the CPU loop `if (|v| > amax) amax = |v|` from 0).
+__device__ __forceinline__ float absmax_lane(float v) {
+    float a = fabsf(v);
+    return a > 0.0f ? a : 0.0f;
+}
+
 // Q8_0 scale of a block from its abs-max (ggml: d = amax/127, id = 1/d or 0).
 struct Q8Scale { float id; uint16_t dh; };
 __device__ __forceinline__ Q8Scale q8_scale(float amax) {
@@ -115,14 +122,28 @@ __device__ __forceinline__ long long warp_sum_i64(long long v) {
     return v;
 }
 
-// Router product in 2^-40 fixed point: rint(clamp(fl(r*x), +-2^22) * 2^40).
+// Router product in fixed point: rint(clamp(fl(r*x), +-512) * 2^32).  The clamp
+// bounds any sum over <= 2^14 rows below 2^55, so sums are exact, independent of
+// how rows are split, and can never reach the count tag kept above bit 56.
 __device__ __forceinline__ long long router_fixed(float r, float x) {
     float p = __fmul_rn(r, x);
-    p = fminf(fmaxf(p, -0x1p22f), 0x1p22f);
-    return __float2ll_rn(__fmul_rn(p, 0x1p40f));
+    p = fminf(fmaxf(p, -512.0f), 512.0f);
+    return __float2ll_rn(__fmul_rn(p, 0x1p32f));
 }
 __device__ __forceinline__ float router_logit(long long s) {
-    return __double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-40));
+    return __double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-32));
+}
+
+// FFN RMSNorm (csrc/libtinygiant.c:322-340): ss = sum x^2 exactly, as fixed-point
+// sums of fl(x*x) clamped to [0, 2^22] in units of 2^-16 (< 2^52 for <= 2^14 rows);
+// scale = 1/sqrtf(ss/dim + eps).
+__device__ __forceinline__ long long ss_fixed(float x) {
+    float p = fminf(__fmul_rn(x, x), 0x1p22f);
+    return __float2ll_rn(__fmul_rn(p, 0x1p16f));
+}
+__device__ __forceinline__ float rms_scale_from(long long s, int dim, float eps) {
+    float ss = __double2float_rn(__dmul_rn(__ll2double_rn(s), 0x1p-16));
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
 }
 
 }  // namespace tg

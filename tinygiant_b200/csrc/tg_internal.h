@@ -30,17 +30,21 @@ cudaError_t launch_block_dots(const uint8_t* W, ActView x, int32_t* out, int row
 
 // Router: logits, top-k, softmax weights and the chosen experts' base pointers.
 // acc: int64[E] zeroed accumulators, counter: zeroed uint; both are left zeroed.
-cudaError_t launch_router_topk(const float* R, const float* x, int E, int H, int k,
-                               long long* acc, unsigned* counter, float* logits, int* idx,
-                               float* w, const uint8_t* layer_base, size_t expert_bytes,
+// Routing of the normed input: x * normw * scale, scale = RMSNorm scale of x (written
+// to scale_out for the gate/up kernel).  acc: int64[E + 1] zeroed; left zeroed.
+cudaError_t launch_router_topk(const float* R, const float* x, const float* normw, float eps, int E, int H,
+                               int k, long long* acc, unsigned* counter, float* logits, int* idx,
+                               float* w, float* scale_out, const uint8_t* layer_base, size_t expert_bytes,
                                const uint8_t** expert_ptrs, cudaStream_t s);
 
 // Grouped gate/up + SwiGLU + Q8_0 requant of h for k experts.
 // experts: device array of k expert bases (row-split layout).
 // hq: k activation blocks of I/32 each, laid out expert after expert (act_bytes(nbI) each).
 // h_dbg (optional): f32 [k][I].
-cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, Geom g,
-                          uint8_t* hq, float* h_dbg, float* gu_dbg, cudaStream_t s);
+// x is quantised as is, or as (x * *scale) * normw when scale is not null.
+cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, const float* normw,
+                          const float* scale, Geom g, uint8_t* hq, float* h_dbg, float* gu_dbg,
+                          cudaStream_t s);
 
 // Down projections of k experts + weighted combine, per output row r:
 //   acc = accumulate ? out[r] : 0;  for j: acc = acc + w[j]*y_j[r]
@@ -58,6 +62,9 @@ cudaError_t launch_fill_normal(float* out, long long n, unsigned long long seed,
 // base + position in the f32 expert tensors, so a weight does not depend on the launch split).
 cudaError_t launch_fill_experts_q4_0(uint8_t* dst, int n_experts, Geom g, unsigned long long seed,
                                      unsigned long long base, float sigma, cudaStream_t s);
+
+// out[c][r] = in[r][c] (fp32, rows x cols -> cols x rows).
+cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cudaStream_t s);
 
 // Raise dynamic shared-memory limits for the shapes a context uses (call before capture).
 cudaError_t prepare_kernels(Geom g, int k);

@@ -47,7 +47,7 @@ __device__ __forceinline__ XBlk load_xblk(const ActView& a, int b) {
 // Returns the code; lane 0 also gets the fp16 scale bits and 8*sum.
 struct Q8Lane { int q; uint16_t dh; int s8; };
 __device__ __forceinline__ Q8Lane quantize_lane(float v) {
-    float am = fabsf(v);
+    float am = absmax_lane(v);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
     Q8Scale sc = q8_scale(am);
@@ -61,11 +61,16 @@ __device__ __forceinline__ Q8Lane quantize_lane(float v) {
     return r;
 }
 
-// Quantise f32 x[0 .. 32*nb) into an activation view, one warp per block.
+// Quantise f32 x[0 .. 32*nb) into an activation view, one warp per block.  With
+// a norm (scale != null) the quantised values are (x * scale) * normw.
 __device__ __forceinline__ void quantize_to_act(const float* __restrict__ x, int nb, ActView a,
-                                                int warp, int nwarps, int lane) {
+                                                int warp, int nwarps, int lane,
+                                                const float* __restrict__ normw = nullptr,
+                                                const float* __restrict__ scale = nullptr) {
+    const float sc = scale ? *scale : 1.0f;
     for (int b = warp; b < nb; b += nwarps) {
         float v = x[(size_t)b * 32 + lane];
+        if (scale) v = __fmul_rn(__fmul_rn(v, sc), normw[(size_t)b * 32 + lane]);
         Q8Lane q = quantize_lane(v);
         a.qs[(size_t)b * 32 + lane] = (int8_t)q.q;
         if (lane == 0) {
@@ -73,6 +78,18 @@ __device__ __forceinline__ void quantize_to_act(const float* __restrict__ x, int
             a.s8[b] = q.s8;
         }
     }
+}
+
+// Store one Q4_0 block held one code per lane (lane = element) as nine aligned
+// 16-bit words: scale, then nibble bytes (element j low, element j+16 high).
+__device__ __forceinline__ void store_q4_0_block(uint8_t* o, uint16_t dh, int q, int lane) {
+    int qh = __shfl_down_sync(0xffffffffu, q, 16);
+    unsigned byte = (unsigned)(q | (qh << 4)) & 0xffu;         // valid in lanes 0..15
+    unsigned b0 = __shfl_sync(0xffffffffu, byte, (2 * lane) & 31);
+    unsigned b1 = __shfl_sync(0xffffffffu, byte, (2 * lane + 1) & 31);
+    uint16_t* o16 = reinterpret_cast<uint16_t*>(o);
+    if (lane == 0) o16[0] = dh;
+    if (lane < 8) o16[1 + lane] = (uint16_t)(b0 | (b1 << 8));
 }
 
 }  // namespace
@@ -184,14 +201,7 @@ __global__ void k_quantize_q4_0(const float* __restrict__ x, long long nblocks, 
     float d = __fdiv_rn(mx, -8.0f);
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q = q4_code(v, id);
-    int qh = __shfl_down_sync(0xffffffffu, q, 16);
-    uint8_t* o = out + blk * Q4_0_BYTES;
-    if (lane < 16) o[2 + lane] = (uint8_t)(q | (qh << 4));
-    if (lane == 0) {
-        uint16_t dh = f32_to_f16_bits(d);
-        o[0] = (uint8_t)(dh & 0xff);
-        o[1] = (uint8_t)(dh >> 8);
-    }
+    store_q4_0_block(out + blk * Q4_0_BYTES, f32_to_f16_bits(d), q, lane);
 }
 
 cudaError_t launch_quantize_act(const float* x, int n, ActView a, uint8_t* ggml, cudaStream_t s) {
@@ -335,25 +345,39 @@ __device__ void topk_softmax_block(const float* sl, int E, int k, int* sidx, flo
     __syncthreads();
 }
 
+// Routing of the normed hidden state (engine.py:229-236): warps 0..E-1 add
+// fixed-point partial sums of R[e] . (x * normw) over a 256-column chunk into
+// acc[e]; warp E adds the chunk's sum of x^2 into acc[E].  The last block to
+// finish turns them into scale = 1/sqrt(ss/H + eps), logits = scale * sum, the
+// top-k and softmax weights, and leaves acc zeroed.
 __global__ void __launch_bounds__(256) k_router_topk(
-    const float* __restrict__ R, const float* __restrict__ x, int E, int H, int k,
-    unsigned long long* acc, unsigned* counter, float* logits, int* idx, float* w,
-    const uint8_t* layer_base, size_t expert_bytes, const uint8_t** expert_ptrs) {
+    const float* __restrict__ R, const float* __restrict__ x, const float* __restrict__ normw, float eps,
+    int E, int H, int k, unsigned long long* acc, unsigned* counter, float* logits, int* idx, float* w,
+    float* scale_out, const uint8_t* layer_base, size_t expert_bytes, const uint8_t** expert_ptrs) {
     int lane = threadIdx.x & 31;
     int warp = threadIdx.x >> 5;
     int e = blockIdx.x * 8 + warp;
+    int c0 = blockIdx.y * ROUTER_HCHUNK;
     if (e < E) {
-        int c0 = blockIdx.y * ROUTER_HCHUNK;
         const float* rr = R + (size_t)e * H;
         long long s = 0;
         for (int c = c0 + 4 * lane; c < c0 + ROUTER_HCHUNK; c += 128) {
             float4 rv = __ldg(reinterpret_cast<const float4*>(rr + c));
             float4 xv = __ldg(reinterpret_cast<const float4*>(x + c));
-            s += router_fixed(rv.x, xv.x) + router_fixed(rv.y, xv.y) +
-                 router_fixed(rv.z, xv.z) + router_fixed(rv.w, xv.w);
+            float4 nv = __ldg(reinterpret_cast<const float4*>(normw + c));
+            s += router_fixed(rv.x, __fmul_rn(xv.x, nv.x)) + router_fixed(rv.y, __fmul_rn(xv.y, nv.y)) +
+                 router_fixed(rv.z, __fmul_rn(xv.z, nv.z)) + router_fixed(rv.w, __fmul_rn(xv.w, nv.w));
         }
         s = warp_sum_i64(s);
         if (lane == 0) atomicAdd(acc + e, (unsigned long long)s);
+    } else if (e == E) {
+        long long s = 0;
+        for (int c = c0 + 4 * lane; c < c0 + ROUTER_HCHUNK; c += 128) {
+            float4 xv = __ldg(reinterpret_cast<const float4*>(x + c));
+            s += ss_fixed(xv.x) + ss_fixed(xv.y) + ss_fixed(xv.z) + ss_fixed(xv.w);
+        }
+        s = warp_sum_i64(s);
+        if (lane == 0) atomicAdd(acc + E, (unsigned long long)s);
     }
     __threadfence();
     __syncthreads();
@@ -365,9 +389,17 @@ __global__ void __launch_bounds__(256) k_router_topk(
     __shared__ float sl[MAX_EXPERTS];
     __shared__ int sidx[MAX_TOPK];
     __shared__ float sw[MAX_TOPK];
+    __shared__ float sscale;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long ss = (long long)atomicExch(acc + E, 0ull);
+        sscale = rms_scale_from(ss, H, eps);
+        if (scale_out) *scale_out = sscale;
+    }
+    __syncthreads();
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
         long long v = (long long)atomicExch(acc + i, 0ull);
-        float l = router_logit(v);
+        float l = __fmul_rn(sscale, router_logit(v));
         sl[i] = l;
         if (logits) logits[i] = l;
     }
@@ -382,15 +414,15 @@ __global__ void __launch_bounds__(256) k_router_topk(
     if (threadIdx.x == 0) *counter = 0u;
 }
 
-cudaError_t launch_router_topk(const float* R, const float* x, int E, int H, int k, long long* acc,
-                               unsigned* counter, float* logits, int* idx, float* w,
-                               const uint8_t* layer_base, size_t expert_bytes,
+cudaError_t launch_router_topk(const float* R, const float* x, const float* normw, float eps, int E, int H, int k,
+                               long long* acc, unsigned* counter, float* logits, int* idx, float* w,
+                               float* scale_out, const uint8_t* layer_base, size_t expert_bytes,
                                const uint8_t** expert_ptrs, cudaStream_t s) {
     if (E <= 0 || E > MAX_EXPERTS || k <= 0 || k > MAX_TOPK || k > E || H % ROUTER_HCHUNK != 0)
         return cudaErrorInvalidValue;
-    dim3 grid((E + 7) / 8, H / ROUTER_HCHUNK);
-    k_router_topk<<<grid, 256, 0, s>>>(R, x, E, H, k, reinterpret_cast<unsigned long long*>(acc), counter,
-                                       logits, idx, w, layer_base, expert_bytes, expert_ptrs);
+    dim3 grid((E + 1 + 7) / 8, H / ROUTER_HCHUNK);
+    k_router_topk<<<grid, 256, 0, s>>>(R, x, normw, eps, E, H, k, reinterpret_cast<unsigned long long*>(acc),
+                                       counter, logits, idx, w, scale_out, layer_base, expert_bytes, expert_ptrs);
     return cudaGetLastError();
 }
 
@@ -399,7 +431,8 @@ cudaError_t launch_router_topk(const float* R, const float* x, int E, int H, int
 // grid (I/32, k), 256 threads.  CTA (c, j) computes gate and up rows
 // 32c .. 32c+31 of expert j, h = silu(g)*u, and quantises that h block.
 __global__ void __launch_bounds__(256) k_gateup(const uint8_t* const* __restrict__ experts,
-                                                const float* __restrict__ x, Geom g,
+                                                const float* __restrict__ x, const float* __restrict__ normw,
+                                                const float* __restrict__ scale, Geom g,
                                                 uint8_t* __restrict__ hq, float* __restrict__ h_dbg,
                                                 float* __restrict__ gu_dbg) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -407,7 +440,7 @@ __global__ void __launch_bounds__(256) k_gateup(const uint8_t* const* __restrict
     int lane = threadIdx.x & 31;
     int warp = threadIdx.x >> 5;
     ActView xs = act_view(smem, g.nbH);
-    quantize_to_act(x, g.nbH, xs, warp, 8, lane);
+    quantize_to_act(x, g.nbH, xs, warp, 8, lane, normw, scale);
     __syncthreads();
 
     const int j = blockIdx.y;
@@ -462,8 +495,8 @@ __global__ void __launch_bounds__(256) k_gateup(const uint8_t* const* __restrict
     }
 }
 
-cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, Geom g, uint8_t* hq,
-                          float* h_dbg, float* gu_dbg, cudaStream_t s) {
+cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, const float* normw,
+                          const float* scale, Geom g, uint8_t* hq, float* h_dbg, float* gu_dbg, cudaStream_t s) {
     if (k <= 0) return cudaSuccess;
     size_t sm = act_bytes(g.nbH);
     if (sm > 48 * 1024) {
@@ -471,7 +504,7 @@ cudaError_t launch_gateup(const uint8_t* const* experts, int k, const float* x, 
         if (e != cudaSuccess) return e;
     }
     dim3 grid(g.I / 32, k);
-    k_gateup<<<grid, 256, sm, s>>>(experts, x, g, hq, h_dbg, gu_dbg);
+    k_gateup<<<grid, 256, sm, s>>>(experts, x, normw, scale, g, hq, h_dbg, gu_dbg);
     return cudaGetLastError();
 }
 
@@ -643,8 +676,11 @@ __global__ void k_fill_experts_q4_0(uint8_t* __restrict__ dst, int n_experts, Ge
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q = q4_code(v, id);
     int qh = __shfl_down_sync(0xffffffffu, q, 16);
+    unsigned byte = (unsigned)(q | (qh << 4)) & 0xffu;        // valid in lanes 0..15
+    unsigned b0 = __shfl_sync(0xffffffffu, byte, (2 * lane) & 31);
+    unsigned b1 = __shfl_sync(0xffffffffu, byte, (2 * lane + 1) & 31);
     uint8_t* rowp = dst + e * g.expert_bytes + tensor_off + row * row_bytes;
-    if (lane < 16) rowp[16 * b + lane] = (uint8_t)(q | (qh << 4));
+    if (lane < 8) reinterpret_cast<uint16_t*>(rowp + 16 * b)[lane] = (uint16_t)(b0 | (b1 << 8));
     if (lane == 0) *reinterpret_cast<uint16_t*>(rowp + 16 * (size_t)nb + 2 * b) = f32_to_f16_bits(d);
 }
 
@@ -653,6 +689,27 @@ cudaError_t launch_fill_experts_q4_0(uint8_t* dst, int n_experts, Geom g, unsign
     long long nblk = 3LL * g.I * g.nbH * n_experts;
     if (nblk <= 0) return cudaSuccess;
     k_fill_experts_q4_0<<<(unsigned)((nblk + 7) / 8), 256, 0, s>>>(dst, n_experts, g, seed, base, sigma);
+    return cudaGetLastError();
+}
+
+// out[c][r] = in[r][c] for a rows x cols fp32 matrix (32x32 tiles through shared memory).
+__global__ void k_transpose(const float* __restrict__ in, float* __restrict__ out, int rows, int cols) {
+    __shared__ float tile[32][33];
+    int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) tile[i][threadIdx.x] = in[(size_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) out[(size_t)c * rows + r] = tile[threadIdx.x][i];
+    }
+}
+
+cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cudaStream_t s) {
+    dim3 grid((cols + 31) / 32, (rows + 31) / 32), block(32, 8);
+    k_transpose<<<grid, block, 0, s>>>(in, out, rows, cols);
     return cudaGetLastError();
 }
 

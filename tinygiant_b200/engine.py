@@ -13,7 +13,7 @@ import ctypes
 import numpy as np
 
 from . import _constants as C
-from ._lib import TGX_EAGER, TgxShape, check, get_lib
+from ._lib import TGX_EAGER, TGX_MULTI, TgxShape, check, get_lib
 
 
 def _stream_handle(stream):
@@ -35,7 +35,7 @@ class MoEModel:
     def __init__(self, embed=C.EMBED_DIM, inter=C.EXPERT_INTERMEDIATE, n_experts=C.N_EXPERTS,
                  top_k=C.N_EXPERTS_USED, n_layers=C.N_LAYERS, device=0):
         self.lib = get_lib()
-        self.shape = TgxShape(embed, inter, n_experts, top_k, n_layers)
+        self.shape = TgxShape(embed, inter, n_experts, top_k, n_layers, C.RMS_EPS)
         self.embed, self.inter, self.n_experts, self.top_k, self.n_layers = embed, inter, n_experts, top_k, n_layers
         self.device = device
         h = ctypes.c_void_p()
@@ -81,18 +81,36 @@ class MoEModel:
         assert R.shape == (self.n_experts, self.embed)
         check(self.lib.tgx_set_router(self._ctx, layer, R.ctypes.data, 0), self.lib)
 
+    def set_ffn_norm(self, layer: int, w: np.ndarray):
+        """FFN RMSNorm weight of `layer` (engine.py:229, default all ones)."""
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        assert w.shape == (self.embed,)
+        check(self.lib.tgx_set_ffn_norm(self._ctx, layer, w.ctypes.data, 0), self.lib)
+
     def fill_synthetic(self, seed: int, w_sigma: float = 0.02, r_sigma: float = 0.02):
         check(self.lib.tgx_fill_synthetic(self._ctx, seed, w_sigma, r_sigma), self.lib)
 
     # ---------------------------------------------------------------- compute
     def moe_layer(self, layer: int, x, stream=None):
-        """x (cuda f32[embed]) += MoE block `layer` of x."""
+        """MoE block `layer` on x (cuda f32[embed]) in place:
+        x += sum_j w_j * expert_j(RMSNorm(x) * ffn_norm)."""
         check(self.lib.tgx_moe_layer(self._ctx, layer, _dev_ptr(x), _stream_handle(stream)), self.lib)
 
-    def decode_step(self, x, stream=None, eager: bool = False):
-        """All layers chained on x in place (CUDA-graph replay unless eager)."""
-        check(self.lib.tgx_decode_step(self._ctx, _dev_ptr(x), _stream_handle(stream),
-                                       TGX_EAGER if eager else 0), self.lib)
+    def decode_step(self, x, stream=None, eager: bool = False, multi: bool = False):
+        """All layers chained on x in place: one fused kernel per step (or three
+        kernels per layer with multi=True), replayed from a CUDA graph unless eager."""
+        flags = (TGX_EAGER if eager else 0) | (TGX_MULTI if multi else 0)
+        check(self.lib.tgx_decode_step(self._ctx, _dev_ptr(x), _stream_handle(stream), flags), self.lib)
+
+    def sync_status(self):
+        """Synchronise; raise if a bounded wait inside the fused kernel expired."""
+        check(self.lib.tgx_sync_status(self._ctx), self.lib)
+
+    def fused_info(self):
+        ctas, smem, arena = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        check(self.lib.tgx_fused_info(self._ctx, ctypes.byref(ctas), ctypes.byref(smem), ctypes.byref(arena)),
+              self.lib)
+        return ctas.value, smem.value, arena.value
 
     def last_routing(self, layer: int):
         idx = np.empty(self.top_k, np.int32)
