@@ -149,6 +149,12 @@ int tgx_sync_status(tgx_ctx *ctx);
  * n_acc words of its routing accumulators.  Synchronises the device. */
 int tgx_fused_debug(tgx_ctx *ctx, uint32_t *ctl4, uint64_t *acc, size_t n_acc);
 
+/* One eager fused decode step on x_dev that also records, per layer and CTA, eight
+ * %globaltimer stamps (ns) of its phases into stamps_host[L][ctas][8]: routing
+ * known, copies issued, input quantised, gate/up published, h gathered, down data
+ * landed, down rows done, next-layer sums sent (0 where a CTA has no such phase). */
+int tgx_fused_trace(tgx_ctx *ctx, float *x_dev, uint64_t *stamps_host, void *stream);
+
 /* The fused path's launch geometry: CTAs (0 when the shape runs on the
  * multi-kernel path), dynamic shared memory per CTA, weight staging bytes per CTA. */
 int tgx_fused_info(tgx_ctx *ctx, int *ctas, int *smem_bytes, int *arena_bytes);

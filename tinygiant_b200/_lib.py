@@ -76,6 +76,7 @@ PROTOTYPES = {
     "tgx_sync_status": (CI, [VP]),
     "tgx_fused_info": (CI, [VP, VP, VP, VP]),
     "tgx_fused_debug": (CI, [VP, VP, VP, SZ]),
+    "tgx_fused_trace": (CI, [VP, VP, VP, VP]),
     "tgx_last_routing": (CI, [VP, CI, VP, VP, VP]),
 }
 

@@ -421,10 +421,9 @@ int fused_setup(tgx_ctx* c) {
     TG_CUDA(cudaMemset(c->ctl, 0, sizeof(unsigned) * 4));
     std::vector<uint16_t> plan;
     size_t arena = 0;
-    int stride = 0;
-    const int rd = 4;
+    int max_rows = 0;
     if (sms > 255 || c->g.H > 16384) return TG_OK;  // count tags and fixed-point bounds
-    if (tg::fused_plan(c->g, E, k, sms, rd, plan, arena, stride) != 0) return TG_OK;  // fused path off
+    if (tg::fused_plan(c->g, E, k, sms, plan, arena, max_rows) != 0) return TG_OK;  // fused path off
     tg::FusedParams& P = c->fp;
     P.weights = c->weights;
     P.layer_bytes = c->layer_bytes;
@@ -434,18 +433,17 @@ int fused_setup(tgx_ctx* c) {
     P.eps = c->eps;
     P.E = E;
     P.k = k;
-    P.rd = rd;
     P.L0 = 0;
     P.nL = L;
+    P.max_rows = max_rows;
     P.xbuf = c->xbuf;
     P.acc = c->facc;
     P.hqt = c->hqt;
     P.ctl = c->ctl;
-    P.plan_stride = stride;
     P.idx_out = c->idx;
     P.w_out = c->wts;
     P.logits_out = c->logits;
-    P.h_dbg = nullptr;
+    P.trace = nullptr;
     P.arena_bytes = arena;
     if (tg::fused_smem_layout(P).total > (uint32_t)smem_optin) return TG_OK;
     if ((rc = A((void**)&c->plan, plan.size() * sizeof(uint16_t)))) return rc;
@@ -710,6 +708,27 @@ extern "C" int tgx_fused_debug(tgx_ctx* ctx, uint32_t* ctl4, uint64_t* acc, size
     size_t have = (size_t)ctx->shape.n_layers * (ctx->shape.n_experts + 1);
     if (acc && n_acc) TG_CUDA(cudaMemcpy(acc, ctx->facc, (n_acc < have ? n_acc : have) * 8, cudaMemcpyDeviceToHost));
     return TG_OK;
+}
+
+extern "C" int tgx_fused_trace(tgx_ctx* ctx, float* x_dev, uint64_t* stamps_host, void* stream) {
+    TG_CHECK(ctx && x_dev && stamps_host, TG_EINVAL, "tgx_fused_trace: null argument");
+    TG_CHECK(ctx->fused_ok, TG_EUNSUPPORTED, "tgx_fused_trace: fused path not available for this shape");
+    DeviceGuard dg(ctx->device);
+    const size_t n = (size_t)ctx->shape.n_layers * ctx->G * tg::FUSED_TRACE;
+    unsigned long long* buf = nullptr;
+    TG_CUDA(cudaMalloc(&buf, n * 8));
+    TG_CUDA(cudaMemset(buf, 0, n * 8));
+    tg::FusedParams saved = ctx->fp;
+    ctx->fp.trace = buf;
+    int rc = fused_launch(ctx, 0, ctx->shape.n_layers, x_dev, (cudaStream_t)stream);
+    ctx->fp = saved;
+    if (rc == TG_OK) {
+        cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+        if (e == cudaSuccess) e = cudaMemcpy(stamps_host, buf, n * 8, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = fail(TG_ECUDA, std::string("tgx_fused_trace: ") + cudaGetErrorString(e));
+    }
+    cudaFree(buf);
+    return rc;
 }
 
 extern "C" int tgx_fused_info(tgx_ctx* ctx, int* ctas, int* smem_bytes, int* arena_bytes) {

@@ -110,13 +110,17 @@ __device__ __forceinline__ float block_term(int sumi, float dw, float dx) {
     return __fmul_rn(__fmul_rn(__int2float_rn(sumi), dw), dx);
 }
 
+// Warp-collective helpers reconverge the warp first: a full-mask shuffle that
+// follows lane-divergent code otherwise waits a long time for the stragglers.
 __device__ __forceinline__ float warp_sum_butterfly(float v) {
+    __syncwarp();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
     return v;
 }
 
 __device__ __forceinline__ long long warp_sum_i64(long long v) {
+    __syncwarp();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
     return v;

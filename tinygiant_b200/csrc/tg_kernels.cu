@@ -47,6 +47,7 @@ __device__ __forceinline__ XBlk load_xblk(const ActView& a, int b) {
 // Returns the code; lane 0 also gets the fp16 scale bits and 8*sum.
 struct Q8Lane { int q; uint16_t dh; int s8; };
 __device__ __forceinline__ Q8Lane quantize_lane(float v) {
+    __syncwarp();
     float am = absmax_lane(v);
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
@@ -83,6 +84,7 @@ __device__ __forceinline__ void quantize_to_act(const float* __restrict__ x, int
 // Store one Q4_0 block held one code per lane (lane = element) as nine aligned
 // 16-bit words: scale, then nibble bytes (element j low, element j+16 high).
 __device__ __forceinline__ void store_q4_0_block(uint8_t* o, uint16_t dh, int q, int lane) {
+    __syncwarp();
     int qh = __shfl_down_sync(0xffffffffu, q, 16);
     unsigned byte = (unsigned)(q | (qh << 4)) & 0xffu;         // valid in lanes 0..15
     unsigned b0 = __shfl_sync(0xffffffffu, byte, (2 * lane) & 31);
@@ -174,6 +176,7 @@ __global__ void k_q8_0_to_act(const uint8_t* __restrict__ ggml, int nb, ActView 
     int q = (int)(int8_t)o[2 + lane];
     a.qs[(size_t)warp * 32 + lane] = (int8_t)q;
     int s = q;
+    __syncwarp();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
     if (lane == 0) {
@@ -191,6 +194,7 @@ __global__ void k_quantize_q4_0(const float* __restrict__ x, long long nblocks, 
     float v = x[blk * 32 + lane];
     float am = fabsf(v);
     int ai = lane;
+    __syncwarp();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
         float oa = __shfl_xor_sync(0xffffffffu, am, off);
@@ -242,6 +246,7 @@ __global__ void __launch_bounds__(256) k_matvec(const uint8_t* __restrict__ W, A
     extern __shared__ __align__(16) uint8_t smem[];
     ActView xs;
     act_to_smem(xa, xs, nb, smem);
+    __syncwarp();
     __syncthreads();
     int lane = threadIdx.x & 31;
     int warp = threadIdx.x >> 5;
@@ -266,6 +271,7 @@ __global__ void __launch_bounds__(256) k_block_dots(const uint8_t* __restrict__ 
     extern __shared__ __align__(16) uint8_t smem[];
     ActView xs;
     act_to_smem(xa, xs, nb, smem);
+    __syncwarp();
     __syncthreads();
     int lane = threadIdx.x & 31;
     int warp = threadIdx.x >> 5;
@@ -325,6 +331,7 @@ __device__ void topk_softmax_block(const float* sl, int E, int k, int* sidx, flo
         }
         if (rank < k) sidx[k - 1 - rank] = i;
     }
+    __syncwarp();
     __syncthreads();
     if (threadIdx.x == 0) {
         float m = sl[sidx[k - 1]];
@@ -342,6 +349,7 @@ __device__ void topk_softmax_block(const float* sl, int E, int k, int* sidx, flo
         }
         for (int j = 0; j < k; j++) sw[j] = __fdiv_rn(ex[j], s);
     }
+    __syncwarp();
     __syncthreads();
 }
 
@@ -380,9 +388,11 @@ __global__ void __launch_bounds__(256) k_router_topk(
         if (lane == 0) atomicAdd(acc + E, (unsigned long long)s);
     }
     __threadfence();
+    __syncwarp();
     __syncthreads();
     __shared__ unsigned ticket;
     if (threadIdx.x == 0) ticket = atomicAdd(counter, 1u);
+    __syncwarp();
     __syncthreads();
     if (ticket != gridDim.x * gridDim.y - 1) return;
     __threadfence();
@@ -390,12 +400,14 @@ __global__ void __launch_bounds__(256) k_router_topk(
     __shared__ int sidx[MAX_TOPK];
     __shared__ float sw[MAX_TOPK];
     __shared__ float sscale;
+    __syncwarp();
     __syncthreads();
     if (threadIdx.x == 0) {
         long long ss = (long long)atomicExch(acc + E, 0ull);
         sscale = rms_scale_from(ss, H, eps);
         if (scale_out) *scale_out = sscale;
     }
+    __syncwarp();
     __syncthreads();
     for (int i = threadIdx.x; i < E; i += blockDim.x) {
         long long v = (long long)atomicExch(acc + i, 0ull);
@@ -403,6 +415,7 @@ __global__ void __launch_bounds__(256) k_router_topk(
         sl[i] = l;
         if (logits) logits[i] = l;
     }
+    __syncwarp();
     __syncthreads();
     topk_softmax_block(sl, E, k, sidx, sw);
     if (threadIdx.x < k) {
@@ -441,6 +454,7 @@ __global__ void __launch_bounds__(256) k_gateup(const uint8_t* const* __restrict
     int warp = threadIdx.x >> 5;
     ActView xs = act_view(smem, g.nbH);
     quantize_to_act(x, g.nbH, xs, warp, 8, lane, normw, scale);
+    __syncwarp();
     __syncthreads();
 
     const int j = blockIdx.y;
@@ -480,6 +494,7 @@ __global__ void __launch_bounds__(256) k_gateup(const uint8_t* const* __restrict
             }
         }
     }
+    __syncwarp();
     __syncthreads();
     if (warp == 0) {
         float hv = sh[lane];
@@ -528,6 +543,7 @@ __global__ void __launch_bounds__(256) k_down_combine(const uint8_t* const* __re
         int n16 = (int)(ab * k / 16);
         for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = src[i];
     }
+    __syncwarp();
     __syncthreads();
     for (int rr = 0; rr < 2; rr++) {
         int r = blockIdx.x * DOWN_ROWS_PER_CTA + warp * 2 + rr;
@@ -665,6 +681,7 @@ __global__ void k_fill_experts_q4_0(uint8_t* __restrict__ dst, int n_experts, Ge
     float v = sqrtf(-2.0f * logf(u1)) * sigma * ((vi & 1) ? sv : cv);
     float am = fabsf(v);
     int ai = lane;
+    __syncwarp();
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
         float oa = __shfl_xor_sync(0xffffffffu, am, off);
@@ -675,6 +692,7 @@ __global__ void k_fill_experts_q4_0(uint8_t* __restrict__ dst, int n_experts, Ge
     float d = __fdiv_rn(mx, -8.0f);
     float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
     int q = q4_code(v, id);
+    __syncwarp();
     int qh = __shfl_down_sync(0xffffffffu, q, 16);
     unsigned byte = (unsigned)(q | (qh << 4)) & 0xffu;        // valid in lanes 0..15
     unsigned b0 = __shfl_sync(0xffffffffu, byte, (2 * lane) & 31);
@@ -700,6 +718,7 @@ __global__ void k_transpose(const float* __restrict__ in, float* __restrict__ ou
         int r = r0 + i, c = c0 + threadIdx.x;
         if (r < rows && c < cols) tile[i][threadIdx.x] = in[(size_t)r * cols + c];
     }
+    __syncwarp();
     __syncthreads();
     for (int i = threadIdx.y; i < 32; i += blockDim.y) {
         int c = c0 + i, r = r0 + threadIdx.x;
