@@ -82,6 +82,22 @@ int tg_expert_forward_mixed(const uint8_t *gate_q4, const uint8_t *up_q4, const 
 int tg_moe_forward_q4_0(const uint8_t **expert_ptrs, const float *weights, int n_experts,
                         const float *input, float *output, int embed_dim, int inter_dim);
 
+/* Bytes of the fixed device scratch of tg_expert_forward_q4_0_noalloc (per device). */
+#define TG_NOALLOC_SCRATCH_BYTES 4194304
+
+/* tg_expert_forward_q4_0 on DEVICE pointers (q4_data 2-byte aligned, input/output
+ * 4-byte aligned), enqueued on `stream` (cudaStream_t; NULL = default stream) and
+ * returning without waiting for it.  No counterpart in the reference: it exists for
+ * callers that cannot let a library allocate (a fully committed HBM budget, or a
+ * latency-bound loop where cudaMalloc/cudaFree may stall).  It allocates nothing,
+ * on the device or the host; its scratch is a fixed TG_NOALLOC_SCRATCH_BYTES array
+ * per device, so an expert needing more (expert bytes rounded up to 256, + 40 * inter/32
+ * + 256) is rejected with TG_EINVAL.  The first call on each device sets that scratch
+ * up (symbol address, one synchronous copy): make it before any stream capture.
+ * Calls overlapping in time on one device share the scratch and race; order them. */
+int tg_expert_forward_q4_0_noalloc(const uint8_t *q4_data, const float *input, float *output, float weight,
+                                   int embed_dim, int inter_dim, void *stream);
+
 /* mlock the pages of [addr, addr+len); returns mlock's result (0 or -1), as
  * csrc/libtinygiant.c:761-766 does. */
 int tg_mlock(const void *addr, size_t len);

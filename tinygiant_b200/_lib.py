@@ -33,6 +33,8 @@ TG_FMT_F16 = 1
 TG_FMT_Q6_K = 2
 TG_FMT_Q4_0 = 3
 
+TG_NOALLOC_SCRATCH_BYTES = 4194304  # include/tinygiant.h
+
 TGX_EAGER = 1
 TGX_MULTI = 2
 
@@ -62,6 +64,7 @@ PROTOTYPES = {
     "tg_expert_forward_q4_0": (CI, [VP, VP, VP, CF, CI, CI]),
     "tg_expert_forward_mixed": (CI, [VP, VP, VP, CI, VP, VP, CF, CI, CI]),
     "tg_moe_forward_q4_0": (CI, [VP, VP, CI, VP, VP, CI, CI]),
+    "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),
     "tg_mlock": (CI, [VP, SZ]),
     "tgx_ctx_create": (CI, [CI, ctypes.POINTER(TgxShape), ctypes.POINTER(VP)]),
     "tgx_ctx_destroy": (CI, [VP]),

@@ -148,6 +148,10 @@ int run_experts(HostWS& W, const Geom& g, int n, const float* weights_host, floa
 
 }  // namespace
 
+namespace tg {
+int set_error(int code, const char* msg) { return fail(code, msg); }
+}  // namespace tg
+
 // ============================================================ reference-shaped
 
 extern "C" const char* tg_last_error(void) { return g_err.c_str(); }

@@ -69,4 +69,7 @@ cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cu
 // Raise dynamic shared-memory limits for the shapes a context uses (call before capture).
 cudaError_t prepare_kernels(Geom g, int k);
 
+// Record msg as the calling thread's tg_last_error() text; returns code.
+int set_error(int code, const char* msg);
+
 }  // namespace tg
