@@ -162,13 +162,17 @@ int tgx_sync_status(tgx_ctx *ctx);
 
 /* Diagnostics of the fused path: its control words (epoch, finished blocks, error
  * stage, error detail = (layer << 20) | (entry << 8) | observed count) and the first
- * n_acc words of its routing accumulators.  Synchronises the device. */
+ * n_acc words of its routing accumulators ([L][8 copies][E + 1] count-tagged words).
+ * Synchronises the device. */
 int tgx_fused_debug(tgx_ctx *ctx, uint32_t *ctl4, uint64_t *acc, size_t n_acc);
 
-/* One eager fused decode step on x_dev that also records, per layer and CTA, eight
- * %globaltimer stamps (ns) of its phases into stamps_host[L][ctas][8]: routing
- * known, copies issued, input quantised, gate/up published, h gathered, down data
- * landed, down rows done, next-layer sums sent (0 where a CTA has no such phase). */
+/* One eager fused decode step on x_dev that also records, per layer and CTA, phase
+ * stamps into stamps_host[L][ctas][32]: slots 0..15 %globaltimer (ns), slots 16..31
+ * the SM's clock64 at the same events.  Slots: 0 routing and x seen, 1 gate/up copies
+ * issued, 2 input quantised, 3 gate/up published, 4 early h gathered, 5 down data
+ * landed, 6 down rows done, 7 next-layer sums sent, 8 first gate/up unit landed,
+ * 9 top-k done, 10 down copies issued, 11 late h gathered (0 where a CTA has no such
+ * event). */
 int tgx_fused_trace(tgx_ctx *ctx, float *x_dev, uint64_t *stamps_host, void *stream);
 
 /* The fused path's launch geometry: CTAs (0 when the shape runs on the

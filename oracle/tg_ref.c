@@ -310,14 +310,15 @@ void ref_expert_forward(const uint8_t *gate, const uint8_t *up, const uint8_t *d
 
 /*
  * Router logits (engine.py:231, logits = router @ normed).  Each product
- * R[e][r]*x[r] is rounded to fp32, clamped to +-512, converted to fixed point
+ * R[e][r]*x[r] is rounded to fp32, clamped to +-256, converted to fixed point
  * with 2^-32 units (round to nearest even) and summed in int64, so the sum is
- * exact and independent of how the rows are split across threads or blocks:
+ * exact and independent of how the rows are split across threads or blocks
+ * (|sum| <= 2^14 * 2^8 * 2^32 = 2^54 for up to 2^14 rows):
  *   logit_e = float(2^-32 * sum_r rint(clamp(fl(R[e][r]*x[r])) * 2^32))
  */
 static inline int64_t router_fixed(float r, float x) {
     float p = r * x;
-    p = fminf(fmaxf(p, -512.0f), 512.0f);
+    p = fminf(fmaxf(p, -256.0f), 256.0f);
     return llrintf(p * 0x1p32f);
 }
 void ref_router_logits(const float *R, const float *x, int n_experts, int hidden, float *logits) {
@@ -381,7 +382,7 @@ float ref_rms_scale(const float *x, int dim, float eps) {
 }
 
 /* Router logits of the normed input without forming it first:
- * logit_e = fl(scale * float(2^-40 * sum_r rint(fl(R[e][r] * fl(x_r * w_r)) * 2^40))),
+ * logit_e = fl(scale * float(2^-32 * sum_r rint(clamp(fl(R[e][r] * fl(x_r * w_r))) * 2^32))),
  * i.e. R . normed with the scalar RMS scale applied after the exact sum. */
 static void block_logits(const float *R, const float *x, const float *w, float scale,
                          int n_experts, int hidden, float *logits) {

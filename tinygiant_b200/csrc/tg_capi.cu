@@ -345,8 +345,9 @@ struct tgx_ctx {
     bool fused_ok = false;
     int G = 0;                          // CTAs = SMs
     float* RT = nullptr;                // [L][H][E] transposed routers
-    float* xbuf = nullptr;              // [L + 1][H]
-    unsigned long long* facc = nullptr; // [L][E]
+    unsigned long long* xw = nullptr;   // [L + 1][H] tagged hidden states between layers
+    float* xbuf = nullptr;              // [H] output of a one-layer launch
+    unsigned long long* facc = nullptr; // [L][FUSED_ACC][E + 1]
     unsigned long long* hqt = nullptr;  // [L][k * nbI * 6]
     unsigned* ctl = nullptr;            // epoch, finish count, error
     uint16_t* plan = nullptr;
@@ -376,7 +377,7 @@ void ctx_free(tgx_ctx* c) {
     for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->nscale, (void*)c->acc,
                     (void*)c->counter, (void*)c->logits,
                     (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging, (void*)c->RT,
-                    (void*)c->xbuf, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
+                    (void*)c->xw, (void*)c->xbuf, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -414,20 +415,27 @@ int fused_setup(tgx_ctx* c) {
     };
     int rc;
     if ((rc = A((void**)&c->RT, sizeof(float) * (size_t)L * E * H)) ||
-        (rc = A((void**)&c->xbuf, sizeof(float) * (size_t)(L + 1) * H)) ||
-        (rc = A((void**)&c->facc, sizeof(unsigned long long) * (size_t)L * (E + 1))) ||
+        (rc = A((void**)&c->xw, sizeof(unsigned long long) * (size_t)(L + 1) * H)) ||
+        (rc = A((void**)&c->xbuf, sizeof(float) * (size_t)H)) ||
+        (rc = A((void**)&c->facc, sizeof(unsigned long long) * (size_t)L * tg::FUSED_ACC * (E + 1))) ||
         (rc = A((void**)&c->hqt, sizeof(unsigned long long) * (size_t)L * k * c->g.nbI * 6)) ||
         (rc = A((void**)&c->ctl, sizeof(unsigned) * 4)))
         return rc;
     TG_CUDA(cudaMemset(c->RT, 0, sizeof(float) * (size_t)L * E * H));
-    TG_CUDA(cudaMemset(c->facc, 0, sizeof(unsigned long long) * (size_t)L * (E + 1)));
+    TG_CUDA(cudaMemset(c->xw, 0, sizeof(unsigned long long) * (size_t)(L + 1) * H));
+    TG_CUDA(cudaMemset(c->facc, 0, sizeof(unsigned long long) * (size_t)L * tg::FUSED_ACC * (E + 1)));
     TG_CUDA(cudaMemset(c->hqt, 0, sizeof(unsigned long long) * (size_t)L * k * c->g.nbI * 6));
     TG_CUDA(cudaMemset(c->ctl, 0, sizeof(unsigned) * 4));
     std::vector<uint16_t> plan;
     size_t arena = 0;
-    int max_rows = 0;
+    int max_rows = 0, k_early = 0;
     if (sms > 255 || c->g.H > 16384) return TG_OK;  // count tags and fixed-point bounds
-    if (tg::fused_plan(c->g, E, k, sms, plan, arena, max_rows) != 0) return TG_OK;  // fused path off
+    if (E % 4 != 0) return TG_OK;                   // router columns are bulk-copied in 16-byte units
+    // each thread of a CTA polls at most 32 words (x and router sums; h records)
+    if ((size_t)H + (size_t)tg::FUSED_ACC * (E + 1) > 32u * tg::FUSED_THREADS ||
+        (size_t)k * c->g.nbI * 6 > 32u * tg::FUSED_THREADS)
+        return TG_OK;
+    if (tg::fused_plan(c->g, E, k, sms, plan, arena, max_rows, k_early) != 0) return TG_OK;  // fused path off
     tg::FusedParams& P = c->fp;
     P.weights = c->weights;
     P.layer_bytes = c->layer_bytes;
@@ -440,9 +448,14 @@ int fused_setup(tgx_ctx* c) {
     P.L0 = 0;
     P.nL = L;
     P.max_rows = max_rows;
-    P.xbuf = c->xbuf;
+    P.k_early = k_early;
+    // The down phase can run in two stages (early slots while late gate/up units
+    // still stream); at the Qwen3 shape one stage measured faster, so it is the default.
+    P.k_early = 0;
+    P.xw = c->xw;
     P.acc = c->facc;
     P.hqt = c->hqt;
+    P.Lmax = L;
     P.ctl = c->ctl;
     P.idx_out = c->idx;
     P.w_out = c->wts;
@@ -469,7 +482,7 @@ int fused_launch(tgx_ctx* c, int L0, int nL, float* x, cudaStream_t s) {
     P.nL = nL;
     P.x_in = x;
     // in place is safe when nL >= 2 (every read of x_in precedes the last layer's writes)
-    P.x_out = nL >= 2 ? x : c->xbuf + (size_t)nL * c->g.H;
+    P.x_out = nL >= 2 ? x : c->xbuf;
     TG_CUDA(tg::launch_decode_fused(P, c->G, s));
     if (nL < 2)
         TG_CUDA(cudaMemcpyAsync(x, P.x_out, sizeof(float) * c->g.H, cudaMemcpyDeviceToDevice, s));
@@ -694,7 +707,9 @@ extern "C" int tgx_sync_status(tgx_ctx* ctx) {
     if (ctl[2] == 0) return TG_OK;
     // a bounded wait expired inside the fused kernel: reset its cross-CTA state
     const tgx_shape& sh = ctx->shape;
-    TG_CUDA(cudaMemset(ctx->facc, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * (sh.n_experts + 1)));
+    TG_CUDA(cudaMemset(ctx->facc, 0,
+                       sizeof(unsigned long long) * (size_t)sh.n_layers * tg::FUSED_ACC * (sh.n_experts + 1)));
+    TG_CUDA(cudaMemset(ctx->xw, 0, sizeof(unsigned long long) * (size_t)(sh.n_layers + 1) * sh.embed));
     TG_CUDA(cudaMemset(ctx->hqt, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * sh.top_k * ctx->g.nbI * 6));
     unsigned fresh[4] = {ctl[0] + 1, 0, 0, 0};
     TG_CUDA(cudaMemcpy(ctx->ctl, fresh, sizeof(fresh), cudaMemcpyHostToDevice));
@@ -709,7 +724,7 @@ extern "C" int tgx_fused_debug(tgx_ctx* ctx, uint32_t* ctl4, uint64_t* acc, size
     DeviceGuard dg(ctx->device);
     TG_CUDA(cudaDeviceSynchronize());
     TG_CUDA(cudaMemcpy(ctl4, ctx->ctl, 4 * sizeof(uint32_t), cudaMemcpyDeviceToHost));
-    size_t have = (size_t)ctx->shape.n_layers * (ctx->shape.n_experts + 1);
+    size_t have = (size_t)ctx->shape.n_layers * tg::FUSED_ACC * (ctx->shape.n_experts + 1);
     if (acc && n_acc) TG_CUDA(cudaMemcpy(acc, ctx->facc, (n_acc < have ? n_acc : have) * 8, cudaMemcpyDeviceToHost));
     return TG_OK;
 }

@@ -2,29 +2,29 @@
 // persistent cooperative kernel (one CTA per SM: 16 compute warps + 1 producer warp).
 //
 // Per layer l (tinygiant/engine.py:229-258, attention excluded):
-//   A  routing: wait until all CTAs' partial sums for layer l have landed in
-//      acc[l] (count-tagged fixed point: R . (x * ffn_norm) per expert and sum x^2),
-//      form the RMSNorm scale and the logits, top-k + softmax (engine.py:229-236);
+//   A  routing: each CTA gathers x_l (tagged words written by the row owners) and
+//      the router sums R . (x * ffn_norm) and sum x^2 of all CTAs (count-tagged
+//      fixed point, spread over FUSED_ACC copies) in one polling sweep, forms the
+//      RMSNorm scale and the logits, and takes top-k + softmax (engine.py:229-236);
 //      every CTA computes the same result.
-//   B  issue: the producer warp bulk-copies (cp.async.bulk, TMA) all of this CTA's
-//      weight bytes for the layer into shared memory: its gate/up units (32 rows
-//      of gate + up of one chosen expert), then its contiguous range of down rows
-//      for all k chosen experts, the next layer's router columns for those rows
-//      and the next layer's norm weights.  Meanwhile the compute warps quantise
-//      RMSNorm(x_l) to Q8_0 (libtinygiant.c:322-340, 61-89).
+//   B  the producer warp bulk-copies (cp.async.bulk) this CTA's gate/up units
+//      (32 rows of gate + up of one chosen expert) into shared memory; the compute
+//      warps quantise RMSNorm(x_l) to Q8_0 (libtinygiant.c:322-340, 61-89).
 //   C  gate/up: per unit, 32 gate and 32 up row dots, h = silu(g)*u, Q8_0 of the
-//      32 h values (libtinygiant.c:566-586); the block is published as six
-//      epoch-tagged 64-bit words (no separate flag round trip).
-//   D  down: wait for all k*I/32 h blocks (polling their tags), then the CTA's
-//      output rows for all k experts, combined in expert-slot order and added to
-//      x (libtinygiant.c:588-594, engine.py:240-258); the rows' products with the
-//      next router and their squares (fixed point, so partition-free and exact)
-//      are added into acc[l+1] together with a count tag.
+//      32 h values (libtinygiant.c:566-586), published as six tagged 64-bit words.
+//      Once the CTA's last unit has landed, its down rows (all k experts), the next
+//      layer's router columns and norm weights are copied in.
+//   D  down: gather the h records (polling their tags) and compute the CTA's output
+//      rows for all k experts, in two stages (early slots, then the late ones),
+//      combine in slot order and add to x (libtinygiant.c:588-594, engine.py:240-258);
+//      publish x_{l+1} as tagged words, and add the rows' products with the next
+//      router and their squares (exact fixed point) into acc[l+1] with a count tag.
 // Arithmetic is identical to the multi-kernel path and to the oracle's mirror
-// order, so results are bit-identical.
+// order, so results are bit-identical.  No grid-wide barrier and no memory fence
+// sits in the layer loop: every cross-CTA word validates itself.
 //
-// Every wait (mbarrier, tag poll) has a wall-clock limit; on expiry the kernel
-// records an error in ctl[2..3], drains its own outstanding copies and returns.
+// Every wait (mbarrier, tag poll) has a cycle limit; on expiry the kernel records
+// an error in ctl[2..3], drains its own outstanding copies and returns.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -105,9 +105,6 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
 }
 __device__ __forceinline__ void red_add_relaxed_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
 // CTA barriers.  __syncthreads is an aligned barrier: every warp must reach it
@@ -206,6 +203,113 @@ __device__ __forceinline__ XBlk load_xblk_s(const ActView& a, int b) {
     return x;
 }
 
+
+// Gather the h records of slots [jlo, jlo + nwords / (6 * nbI)) of one layer (six
+// tagged words each) straight into the activation form: codes, fp32 scale, 8 * sum
+// of codes.  Each thread re-polls only its missing words.  False when the wait limit
+// passed (error recorded) or another CTA reported an error.  Called from one place
+// only (the stage loop), so the layer loop holds one copy of it.
+__device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, int nwords, int jlo, int nbI,
+                                              uint8_t* hq_base, int ab_i, unsigned tag, unsigned* ctl, int* flags,
+                                              int l) {
+    const int tid = threadIdx.x;
+    unsigned mine = 0, done = 0;
+    for (int i = 0; i * NT + tid < nwords; i++) mine |= 1u << i;
+    const long long t0 = clock64();
+    int spins = 0;
+    while (done != mine) {
+#pragma unroll 1
+        for (int i0 = 0; i0 * NT + tid < nwords; i0 += 8) {
+            unsigned long long v[8];
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const int i = i0 + t, w = i * NT + tid;
+                v[t] = (w < nwords && !(done >> i & 1u)) ? ld_relaxed_u64(hw + w) : 0ull;
+            }
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const int i = i0 + t, w = i * NT + tid;
+                if (w >= nwords || (done >> i & 1u)) continue;
+                if ((unsigned)(v[t] >> 48) != tag) continue;
+                done |= 1u << i;
+                const int rec = w / 6, part = w - rec * 6;
+                const int jj = jlo + rec / nbI, c = rec % nbI;
+                uint8_t* base = hq_base + (size_t)jj * ab_i;
+                uint16_t* q16 = reinterpret_cast<uint16_t*>(base + (size_t)c * 32 + 6 * part);
+                const unsigned long long pv = v[t];
+                if (part < 5) {
+                    q16[0] = (uint16_t)pv;
+                    q16[1] = (uint16_t)(pv >> 16);
+                    q16[2] = (uint16_t)(pv >> 32);
+                } else {
+                    q16[0] = (uint16_t)pv;   // codes 30, 31
+                    reinterpret_cast<float*>(base + (size_t)nbI * 32)[c] = f16_bits_to_f32((uint16_t)(pv >> 16));
+                    reinterpret_cast<int*>(base + (size_t)nbI * 36)[c] = 8 * (int)(int16_t)(uint16_t)(pv >> 32);
+                }
+            }
+        }
+        if (done == mine) break;
+        if ((++spins & 63) == 0) {
+            if (clock64() - t0 > WAIT_CYCLES) {
+                const int i = __ffs(mine & ~done) - 1, w = i * NT + tid;
+                flags[1] = (l << 20) | (((jlo * nbI + w / 6) & 0xfff) << 8);
+                record_failure(ctl, flags, 4);
+                return false;
+            }
+            if (ld_relaxed_u32(ctl + 2) != 0) return false;
+        }
+    }
+    return true;
+}
+
+// Down values y_j of this CTA's rows for slots [jlo, jhi) into ys[j][q]: a warp per
+// row (two rows per warp above 16 rows, sharing each h block load), lane partials
+// in block order b = lane, lane + 32, ... for up to 8 slots, then one transposed
+// reduction per row (the mirror order).  Called from one place only.
+__device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* hq_base, float* ys, uint32_t d_chunk,
+                                       int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (warp >= CW) return;
+    const int rpw = d_n <= CW ? 1 : 2;
+    for (int pr = warp; pr * rpw < d_n; pr += CW) {
+        const int q0 = pr * rpw;
+        const bool two = rpw == 2 && q0 + 1 < d_n;
+        for (int j0 = jlo; j0 < jhi; j0 += 8) {
+            float acc0[8], acc1[8];
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) acc0[jj] = acc1[jj] = 0.0f;
+#pragma unroll 1
+            for (int b = lane; b < nbI; b += 32) {
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++) {
+                    const int j = j0 + jj;
+                    if (j < jhi) {
+                        const uint8_t* row = dbase + (size_t)j * d_chunk + (size_t)q0 * row_d;
+                        const XBlk xb = load_xblk_s(act_view(hq_base + (size_t)j * ab_i, nbI), b);
+                        const uint4 w0 = *reinterpret_cast<const uint4*>(row + 16 * b);
+                        const float dw0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * nbI + 2 * b));
+                        acc0[jj] = __fadd_rn(acc0[jj], block_term(block_sumi(w0, xb), dw0, xb.d));
+                        if (two) {
+                            const uint8_t* row1 = row + row_d;
+                            const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 16 * b);
+                            const float dw1 =
+                                f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row1 + 16 * nbI + 2 * b));
+                            acc1[jj] = __fadd_rn(acc1[jj], block_term(block_sumi(w1, xb), dw1, xb.d));
+                        }
+                    }
+                }
+            }
+            const float y0 = warp_sum8_transposed(acc0, lane);   // slot j0+jj in lanes 4jj..4jj+3
+            const float y1 = two ? warp_sum8_transposed(acc1, lane) : 0.0f;
+            const int jj = lane >> 2;
+            if ((lane & 3) == 0 && j0 + jj < jhi) {
+                ys[(size_t)(j0 + jj) * max_rows + q0] = y0;
+                if (two) ys[(size_t)(j0 + jj) * max_rows + q0 + 1] = y1;
+            }
+        }
+    }
+}
+
 }  // namespace
 
 template <bool TRACE>
@@ -216,22 +320,21 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     uint64_t* mbar_d = mbar_gu + FUSED_MAX_GU;                             // down rows + next router / norm
     uint64_t* mbar_rt0 = mbar_gu + FUSED_MAX_GU + 1;                       // first router columns + norm
     uint16_t* plan = reinterpret_cast<uint16_t*>(smem + S.plan);
-    long long* slog_fx = reinterpret_cast<long long*>(smem + S.slogfx);
+    long long* slog_fx = reinterpret_cast<long long*>(smem + S.slogfx);   // [FUSED_ACC][E + 1]
     float* slog = reinterpret_cast<float*>(smem + S.slog);
     int* sidx = reinterpret_cast<int*>(smem + S.sidx);
-    float* sw = reinterpret_cast<float*>(smem + S.sw);
-    int* flags = reinterpret_cast<int*>(smem + S.flags);   // [0] error seen, [1] error detail
-    float* sscale = reinterpret_cast<float*>(flags + 2);   // RMSNorm scale of the current layer
+    int* flags = reinterpret_cast<int*>(smem + S.flags);   // [0] error seen, [1] error detail, [2] last CTA
+    float* sscale = reinterpret_cast<float*>(flags + 4);   // RMSNorm scale of the current layer
     float* xs = reinterpret_cast<float*>(smem + S.xs);
     ActView xq = act_view(smem + S.xq, P.g.nbH);
     uint8_t* hq_base = smem + S.hq;
-    uint8_t* rec = smem + S.rec;
-    float* sh = reinterpret_cast<float*>(smem + S.sh);      // [2][32]
+    float* sh = reinterpret_cast<float*>(smem + S.sh);      // [2][32] h of a unit, then [16] routing weights
     uint8_t* hrec = smem + S.hrec;                           // [2][64]
     float* xnext = reinterpret_cast<float*>(smem + S.xnext);  // x of the next layer, this CTA's rows
     float* xw = reinterpret_cast<float*>(smem + S.xw);        // the same rows times the next norm weight
     float* rt = reinterpret_cast<float*>(smem + S.rt);        // router columns of this CTA's rows [rows][E]
     float* snorm = reinterpret_cast<float*>(smem + S.snorm);  // [2][H]
+    float* ys = reinterpret_cast<float*>(smem + S.ys);        // [k][max_rows] per-slot down values
     uint8_t* arena = smem + S.arena;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -241,27 +344,27 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     const size_t ab_i = act_bytes(nbI);
     const uint32_t gu_unit_bytes = (uint32_t)(32 * g.row_gu);  // one of gate / up
     const uint32_t norm_bytes = (uint32_t)(4 * g.H);           // one layer's FFN norm weights
+    const size_t acc_words = (size_t)FUSED_ACC * (E + 1);      // one layer's router accumulators
 
     if (tid < FUSED_PLAN) plan[tid] = P.plan[(size_t)cta * FUSED_PLAN + tid];
     if (tid == PT) {
         for (int i = 0; i < FUSED_MAX_GU + 2; i++) mbar_init(mbar_gu + i, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (tid == 0) {
-        flags[0] = 0;
-        flags[1] = 0;
-    }
+    if (tid < 4) flags[tid] = 0;
     cta_sync();
-    const int n_gu = plan[0], d_lo = plan[1], d_n = plan[2];
-    const uint16_t* gu_units = plan + 3;
+    const int n_gu = plan[0], d_lo = plan[1], d_n = plan[2], d_place = plan[3];
+    const uint16_t* gu_units = plan + 4;
     const uint32_t d_chunk = (uint32_t)d_n * (uint32_t)g.row_d;   // this CTA's rows of one expert's down
     const uint32_t rt_bytes = (uint32_t)d_n * (uint32_t)E * 4u;  // their router columns
+    // down rows: in unit 0's space once it is computed (placement 1), else after the units
+    uint8_t* dbase = arena + (d_place ? (size_t)0 : (size_t)n_gu * 2 * gu_unit_bytes);
     const unsigned epoch = ld_relaxed_u32(P.ctl);
-    const unsigned long long tag = (unsigned long long)(epoch % 65535u + 1u);
+    const unsigned tag = epoch % 65535u + 1u;   // 1..65535; the tagged buffers are cleared before it repeats
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
 
-    // Producer-thread bookkeeping of armed, not yet waited mbarriers (for the error
+    // Producer-lane bookkeeping of armed, not yet waited mbarriers (for the error
     // path).  Every mbarrier completes at most once per layer, so the parity to
     // wait for in layer l is l & 1 (0 for the one-off first router copy).
     unsigned pending = 0;  // bits 0..3: gate/up units, bit 4: down group, bit 5: first router copy
@@ -269,28 +372,108 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
 
     auto fail = [&](unsigned code) { record_failure(P.ctl, flags, code); };
     auto error_seen = [&]() -> bool { return ld_relaxed_u32(P.ctl + 2) != 0; };
-    // trace stamp: %globaltimer (ns) for cross-SM alignment and clock64 taken after
-    // it, so cycle intervals exclude the timer read; slot 31 keeps the read's cost
+    // trace stamp: %globaltimer (ns) for cross-SM alignment and clock64 for cycles
     auto stamp = [&](int l, int slot) {
         if (TRACE) {
-            const long long c0 = clock64();
             const unsigned long long t = gtime();
             const long long c1 = clock64();
             unsigned long long* row = P.trace + ((size_t)l * G + cta) * FUSED_TRACE;
             row[slot] = t;
-            if (slot < 15) row[16 + slot] = (unsigned long long)c1;
-            if (slot == 3) row[31] = (unsigned long long)(c1 - c0);
+            row[16 + slot] = (unsigned long long)c1;
         }
     };
-    // all threads: bounded wait on an mbarrier phase (records an error on timeout)
-    auto wait_bar = [&](uint64_t* bar, unsigned parity, unsigned code) {
+    // bounded wait on an mbarrier phase by the calling thread; false (and an error
+    // recorded) when the limit passes
+    auto wait_bar = [&](uint64_t* bar, unsigned parity, unsigned code) -> bool {
         const long long t0 = clock64();
         int spins = 0;
         while (!mbar_try_wait(bar, parity)) {
             if ((++spins & 255) == 0 && clock64() - t0 > WAIT_CYCLES) {
-                if (lane == 0) fail(code);
-                return;
+                fail(code);
+                return false;
             }
+        }
+        return true;
+    };
+    // Copies are cut into pieces of at most 16 KB (16-byte multiples), except the
+    // gate / up halves, which go as one copy each (fewer copies issue faster); lane i
+    // of the producer warp issues pieces i, i + 32, ..., so one warp instruction
+    // starts up to 32 copies.
+    auto pieces_of = [](uint32_t bytes) -> int { return (int)((bytes + 16383u) / 16384u); };
+    auto piece_span = [](uint32_t bytes, int np, int p, uint32_t& off, uint32_t& n) {
+        const uint32_t ps = ((bytes + np - 1) / np + 15u) & ~15u;
+        off = (uint32_t)p * ps;
+        n = off >= bytes ? 0u : (bytes - off < ps ? bytes - off : ps);
+    };
+    // producer warp: the gate and up halves of this CTA's units, one mbarrier per unit
+    auto issue_gateup = [&](const uint8_t* lbase) {
+        for (int pi = lane; pi < 2 * n_gu; pi += 32) {
+            const int u = pi >> 1, half = pi & 1;
+            const int unit = gu_units[u];
+            const int j = unit / nbI, c = unit - j * nbI;
+            const uint8_t* src = lbase + (size_t)sidx[j] * g.expert_bytes + (half ? g.t_gu : 0) +
+                                 (size_t)c * gu_unit_bytes;
+            bulk_g2s(arena + ((size_t)u * 2 + half) * gu_unit_bytes, src, gu_unit_bytes, mbar_gu + u, pol_stream);
+        }
+    };
+    // producer warp: this layer's down rows of all k experts, plus the next layer's
+    // router columns and norm weights, all on mbar_d
+    auto issue_down = [&](int l, int layer, const uint8_t* lbase, bool next) {
+        if (!(d_n > 0 || next)) return;
+        const uint32_t total = (uint32_t)k * d_chunk + (next ? rt_bytes + norm_bytes : 0u);
+        if (lane == 0) {
+            mbar_arrive_expect_tx(mbar_d, total);
+            pending |= 1u << 4;
+        }
+        __syncwarp();
+        const int npd = d_n > 0 ? pieces_of(d_chunk) : 0;
+        const int npr = (next && d_n > 0) ? pieces_of(rt_bytes) : 0;
+        const int npn = next ? pieces_of(norm_bytes) : 0;
+        const int nd = k * npd;
+        for (int pi = lane; pi < nd + npr + npn; pi += 32) {
+            uint32_t off, n;
+            const uint8_t* src;
+            uint8_t* dst;
+            uint64_t pol;
+            if (pi < nd) {
+                const int j = pi / npd, p = pi - j * npd;
+                piece_span(d_chunk, npd, p, off, n);
+                src = lbase + (size_t)sidx[j] * g.expert_bytes + 2 * g.t_gu + (size_t)d_lo * g.row_d + off;
+                dst = dbase + (size_t)j * d_chunk + off;
+                pol = pol_stream;
+            } else if (pi < nd + npr) {
+                piece_span(rt_bytes, npr, pi - nd, off, n);
+                src = reinterpret_cast<const uint8_t*>(P.RT + ((size_t)(layer + 1) * g.H + d_lo) * E) + off;
+                dst = reinterpret_cast<uint8_t*>(rt) + off;
+                pol = pol_keep;
+            } else {
+                piece_span(norm_bytes, npn, pi - nd - npr, off, n);
+                src = reinterpret_cast<const uint8_t*>(P.normw + (size_t)(layer + 1) * g.H) + off;
+                dst = reinterpret_cast<uint8_t*>(snorm + (size_t)((l + 1) & 1) * g.H) + off;
+                pol = pol_keep;
+            }
+            if (n) bulk_g2s(dst, src, n, mbar_d, pol);
+        }
+        __syncwarp();
+    };
+    // this CTA's rows' share of the next layer's router sums and sum of x^2, added with
+    // a count tag into copy cta % FUSED_ACC: four threads per entry, exact int64 sums
+    auto router_partials = [&](unsigned long long* accn) {
+        accn += (size_t)(cta % FUSED_ACC) * (E + 1);
+        for (int i0 = 0; i0 < 4 * (E + 1); i0 += NT) {
+            const int i = i0 + tid, e = i >> 2, part = i & 3;
+            long long s = 0;
+            if (e < E) {
+#pragma unroll 1
+                for (int q = part; q < d_n; q += 4) s += router_fixed(rt[(size_t)q * E + e], xw[q]);
+            } else if (e == E) {
+#pragma unroll 1
+                for (int q = part; q < d_n; q += 4) s += ss_fixed(xnext[q]);
+            }
+            __syncwarp();
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            if (e <= E && part == 0) red_add_relaxed_u64(accn + e, CNT_UNIT + (unsigned long long)s);
         }
     };
 
@@ -303,80 +486,117 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     }
     #pragma unroll 1
     for (int q = tid; q < d_n; q += NT) xnext[q] = P.x_in[d_lo + q];
-    wait_bar(mbar_rt0, 0, 1);
-    cta_sync();
-    if (flags[0]) goto drain;
+    if (!cta_sync_and(wait_bar(mbar_rt0, 0, 1))) goto drain;
     if (tid == PT) pending &= ~(1u << 5);
     #pragma unroll 1
     for (int q = tid; q < d_n; q += NT) xw[q] = __fmul_rn(xnext[q], snorm[d_lo + q]);
     cta_sync();
-    for (int e = tid; e <= E; e += NT) {
-        long long s = 0;
-        if (e < E)
-#pragma unroll 1
-            for (int q = 0; q < d_n; q++) s += router_fixed(rt[(size_t)q * E + e], xw[q]);
-        else
-#pragma unroll 1
-            for (int q = 0; q < d_n; q++) s += ss_fixed(xnext[q]);
-        atomicAdd(P.acc + e, CNT_UNIT + (unsigned long long)s);   // x_in is complete before the launch
-    }
+    router_partials(P.acc);   // x_in is complete before the launch
 
     for (int l = 0; l < P.nL; l++) {
         const int layer = P.L0 + l;
         cur_l = l;
-        unsigned long long* accl = P.acc + (size_t)l * (E + 1);
-        // ------------------------------------------------------------ A: routing
+        unsigned long long* accl = P.acc + (size_t)l * acc_words;
+        const bool next = l + 1 < P.nL;
+        const uint8_t* lbase = P.weights + (size_t)layer * P.layer_bytes;
+        // ------------------------------------------------------------ A: routing sums and x_l
+        // Every word is validated on its own: x_l values carry the launch tag (x_in
+        // needs none), router sums carry a count of contributing CTAs, so no fence is
+        // needed.  Each thread re-polls only its missing words until all are in (or the
+        // wait limit passes); one barrier ends the phase.
         {
+            const int nwords = g.H + (int)acc_words;
+            const unsigned long long* xl = P.xw + (size_t)l * g.H;
+            unsigned mine = 0, done = 0;   // words tid + i * NT of this thread, and those taken
+            for (int i = 0; i * NT + tid < nwords; i++) mine |= 1u << i;
             const long long t0 = clock64();
             int spins = 0;
-            while (true) {
-                int ok = 1;
-                for (int e = tid; e <= E; e += NT) {
-                    unsigned long long v = ld_relaxed_u64(accl + e);
-                    unsigned long long cnt = (v + (1ull << 55)) >> 56;
-                    if (cnt != (unsigned long long)G) {
-                        ok = 0;
-                        flags[1] = (l << 20) | ((e & 0xfff) << 8) | (int)(cnt & 0xff);
-                    } else {
-                        slog_fx[e] = (long long)(v - (unsigned long long)G * CNT_UNIT);
+            bool ok = true;
+            while (done != mine) {
+#pragma unroll 1
+                for (int i0 = 0; i0 * NT + tid < nwords; i0 += 8) {
+                    unsigned long long v[8];
+#pragma unroll
+                    for (int t = 0; t < 8; t++) {
+                        const int i = i0 + t, w = i * NT + tid;
+                        v[t] = 0ull;
+                        if (w < nwords && !(done >> i & 1u)) {
+                            if (w >= g.H)
+                                v[t] = ld_relaxed_u64(accl + (w - g.H));
+                            else if (l == 0)
+                                v[t] = ((unsigned long long)tag << 32) | __float_as_uint(__ldcg(P.x_in + w));
+                            else
+                                v[t] = ld_relaxed_u64(xl + w);
+                        }
+                    }
+#pragma unroll
+                    for (int t = 0; t < 8; t++) {
+                        const int i = i0 + t, w = i * NT + tid;
+                        if (w >= nwords || (done >> i & 1u)) continue;
+                        if (w < g.H) {
+                            if ((unsigned)(v[t] >> 32) == tag) {
+                                xs[w] = __uint_as_float((unsigned)v[t]);
+                                done |= 1u << i;
+                            }
+                        } else {
+                            // copy a holds the CTAs c with c % FUSED_ACC == a
+                            const int a = (w - g.H) / (E + 1);
+                            const unsigned long long want = (unsigned long long)((G - a + FUSED_ACC - 1) / FUSED_ACC);
+                            const unsigned long long cnt = (v[t] + (1ull << 55)) >> 56;
+                            if (cnt == want) {
+                                slog_fx[w - g.H] = (long long)(v[t] - want * CNT_UNIT);
+                                done |= 1u << i;
+                            }
+                        }
                     }
                 }
-                if (cta_sync_and(ok)) break;
-                if (tid == 0 && ((++spins & 63) == 0) && (clock64() - t0 > WAIT_CYCLES || error_seen())) fail(2);
-                cta_sync();
-                if (flags[0]) goto drain;
+                if (done == mine) break;
+                if ((++spins & 63) == 0) {
+                    if (clock64() - t0 > WAIT_CYCLES) {
+                        const int i = __ffs(mine & ~done) - 1, w = i * NT + tid;
+                        flags[1] = (l << 20) | (((w < g.H ? w : w - g.H) & 0xfff) << 8) | (w < g.H ? 0xff : 0xfe);
+                        fail(2);
+                        ok = false;
+                        break;
+                    }
+                    if (error_seen()) {
+                        ok = false;
+                        break;
+                    }
+                }
             }
+            if (!cta_sync_and(ok)) goto drain;
         }
-        // thread 0 read acc[l][0] after every CTA's release: its acquire fence orders
-        // this CTA's later reads of x_l (after the next barrier) behind all producers
-        if (tid == 0) {
-            fence_acq_rel_gpu();
-            *sscale = rms_scale_from(slog_fx[E], g.H, P.eps);
-        }
-        cta_sync();
         if (tid == 0) stamp(l, 0);
         // logits of the normed input: scale * (R . (x * w)), scale = 1/sqrt(ss/H + eps);
-        // once every CTA has contributed to acc[l], acc[l-1] is read by no one and is recycled
+        // each sum is the exact int64 total of the accumulator copies
         {
-            const float scale = *sscale;
+            auto total = [&](int e) {
+                long long t = 0;
+#pragma unroll
+                for (int a = 0; a < FUSED_ACC; a++) t += slog_fx[(size_t)a * (E + 1) + e];
+                return t;
+            };
+            const float scale = rms_scale_from(total(E), g.H, P.eps);
 #pragma unroll 1
-            for (int e = tid; e < E; e += NT) slog[e] = __fmul_rn(scale, router_logit(slog_fx[e]));
+            for (int e = tid; e < E; e += NT) slog[e] = __fmul_rn(scale, router_logit(total(e)));
+            if (tid == 0) *sscale = scale;
+            // every CTA has contributed to acc[l], so acc[l-1] is read by no one: recycle it
             if (cta == 0 && l >= 1)
-                for (int e = tid; e <= E; e += NT) accl[e - (E + 1)] = 0ull;
+                for (size_t i = tid; i < acc_words; i += NT) accl[i - acc_words] = 0ull;
         }
         cta_sync();
-        // top-k by rank: 4 threads per expert share the scan; the element beaten by
-        // fewer than k others (larger logit, or equal logit and larger id) is kept
+        // top-k by rank: 4 threads per expert share the scan (interleaved, so the four
+        // read neighbouring banks); the element beaten by fewer than k others (larger
+        // logit, or equal logit and larger id) is kept
         for (int base = 0; base < E; base += NT / 4) {
-            int e = base + (tid >> 2), part = tid & 3;
+            const int e = base + (tid >> 2), part = tid & 3;
             int rank = 0;
             if (e < E) {
-                float le = slog[e];
-                int chunk = (E + 3) / 4;
-                int j0 = part * chunk, j1 = min(E, j0 + chunk);
-#pragma unroll 4
-                for (int j = j0; j < j1; j++) {
-                    float lj = slog[j];
+                const float le = slog[e];
+#pragma unroll 8
+                for (int j = part; j < E; j += 4) {
+                    const float lj = slog[j];
                     rank += (lj > le) || (lj == le && j > e);
                 }
             }
@@ -387,11 +607,32 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         }
         cta_sync();
         if (tid == 0) stamp(l, 9);
-        // softmax over the k chosen logits (engine.py:233-236): lane j holds exp(l_j - max);
-        // the sum for k <= 8 is ((e0+e1)+(e2+e3))+((e4+e5)+(e6+e7)), three xor steps
-        if (warp == 0) {
+
+        // ------------------------------------------------------------ B: copies, softmax, x quantise
+        if (warp == CW) {
+            // producer warp: gate/up units now; the down rows once unit 0 is computed
+            // (placement 1) or this CTA's last unit has landed (placement 0), so gate/up
+            // bytes go first
+            if (lane == 0) {
+                // the regions below were read by this CTA's threads in the previous layer
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                for (int u = 0; u < n_gu; u++) mbar_arrive_expect_tx(mbar_gu + u, 2 * gu_unit_bytes);
+                pending |= (1u << n_gu) - 1u;
+            }
+            __syncwarp();
+            issue_gateup(lbase);
+            __syncwarp();
+            if (lane == 0) stamp(l, 1);
+            if (n_gu == 0) {
+                issue_down(l, layer, lbase, next);
+                if (lane == 0) stamp(l, 10);
+            }
+        } else {
+            // softmax over the k chosen logits (engine.py:233-236), held by lane j of
+            // every compute warp: w_j = exp(l_j - max) / sum, sum for k <= 8 as
+            // ((e0+e1)+(e2+e3))+((e4+e5)+(e6+e7))
             const float m = slog[sidx[k - 1]];
-            float ex = lane < k ? tg_expf(__fsub_rn(slog[sidx[lane]], m)) : 0.0f;
+            const float ex = lane < k ? tg_expf(__fsub_rn(slog[sidx[lane < k ? lane : 0]], m)) : 0.0f;
             __syncwarp();
             float s;
             if (k <= 8) {
@@ -404,77 +645,44 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                 s = 0.0f;
                 for (int j = 0; j < k; j++) s = __fadd_rn(s, __shfl_sync(0xffffffffu, ex, j));
             }
-            if (lane < k) sw[lane] = __fdiv_rn(ex, s);
-        }
-        cta_sync();
-        if (tid == 0) stamp(l, 10);
-        if (cta == 0) {
-            if (tid < k) {
-                P.idx_out[(size_t)layer * k + tid] = sidx[tid];
-                P.w_out[(size_t)layer * k + tid] = sw[tid];
-            }
-            for (int e = tid; e < E; e += NT) P.logits_out[(size_t)layer * E + e] = slog[e];
-        }
-
-        // ------------------------------------------------------------ B: the producer issues all copies
-        const uint8_t* lbase = P.weights + (size_t)layer * P.layer_bytes;
-        const bool next = l + 1 < P.nL;
-        const bool d_armed = d_n > 0 || next;   // mbar_d also carries the next layer's norm weights
-        if (tid == PT) {
-            stamp(l, 11);
-            // the regions below were read by this CTA's threads in the previous layer
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            stamp(l, 12);
-            for (int u = 0; u < n_gu; u++) {
-                int unit = gu_units[u];
-                int j = unit / nbI, c = unit - j * nbI;
-                const uint8_t* eb = lbase + (size_t)sidx[j] * g.expert_bytes;
-                uint8_t* dst = arena + (size_t)u * 2 * gu_unit_bytes;
-                mbar_arrive_expect_tx(mbar_gu + u, 2 * gu_unit_bytes);
-                bulk_g2s(dst, eb + (size_t)c * gu_unit_bytes, gu_unit_bytes, mbar_gu + u, pol_stream);
-                bulk_g2s(dst + gu_unit_bytes, eb + g.t_gu + (size_t)c * gu_unit_bytes, gu_unit_bytes, mbar_gu + u,
-                         pol_stream);
-                pending |= 1u << u;
-            }
-            stamp(l, 13);
-            if (d_armed) {
-                mbar_arrive_expect_tx(mbar_d, (uint32_t)k * d_chunk + (next ? rt_bytes + norm_bytes : 0u));
-                uint8_t* dbase = arena + (size_t)n_gu * 2 * gu_unit_bytes;
-                if (d_n > 0)
-#pragma unroll 1
-                    for (int j = 0; j < k; j++)
-                        bulk_g2s(dbase + (size_t)j * d_chunk,
-                                 lbase + (size_t)sidx[j] * g.expert_bytes + 2 * g.t_gu + (size_t)d_lo * g.row_d,
-                                 d_chunk, mbar_d, pol_stream);
-                if (next) {
-                    if (d_n > 0)
-                        bulk_g2s(rt, P.RT + ((size_t)(layer + 1) * g.H + d_lo) * E, rt_bytes, mbar_d, pol_keep);
-                    bulk_g2s(snorm + (size_t)((l + 1) & 1) * g.H, P.normw + (size_t)(layer + 1) * g.H, norm_bytes,
-                             mbar_d, pol_keep);
+            const float wl = lane < k ? __fdiv_rn(ex, s) : 0.0f;
+            if (cta == 0) {
+                if (warp == 0 && lane < k) {
+                    P.idx_out[(size_t)layer * k + lane] = sidx[lane];
+                    P.w_out[(size_t)layer * k + lane] = wl;
                 }
-                pending |= 1u << 4;
+                for (int e = tid; e < E; e += CT) P.logits_out[(size_t)layer * E + e] = slog[e];
             }
-            stamp(l, 1);
-        }
-        // x_l -> shared (f32) and the Q8_0 activation form of RMSNorm(x_l), while the copies fly
-        if (warp < CW) {
-            const float* xsrc = l == 0 ? P.x_in : P.xbuf + (size_t)l * g.H;
-#pragma unroll 1
-            for (int i = tid; i < g.H; i += CT) xs[i] = __ldcg(xsrc + i);
-        }
-        cta_sync();
-        if (tid == 0) stamp(l, 14);
-        if (warp < CW) {
+            if (warp == 0 && lane < 16) sh[64 + lane] = wl;   // the routing weights, for the combine
+            // Q8_0 of RMSNorm(x_l) * w (libtinygiant.c:336-339, 61-89): four blocks per
+            // warp at a time, eight lanes per block, four values per lane
             const float scale = *sscale;
             const float* nw = snorm + (size_t)(l & 1) * g.H;
-            for (int b = warp; b < nbH; b += CW) {
-                // expert input = RMSNorm(x) * w = (x * scale) * w  (libtinygiant.c:336-339)
-                const float v = __fmul_rn(__fmul_rn(xs[(size_t)b * 32 + lane], scale), nw[(size_t)b * 32 + lane]);
-                const Q8Res r = q8_block_lane(v);
-                xq.qs[(size_t)b * 32 + lane] = (int8_t)r.q;
-                if (lane == 0) {
-                    xq.d[b] = f16_bits_to_f32((uint16_t)r.dh);
-                    xq.s8[b] = r.s8;
+            for (int b0 = warp * 4; b0 < nbH; b0 += CW * 4) {
+                const int b = b0 + (lane >> 3), sub = lane & 7;
+                const float4 xv = reinterpret_cast<const float4*>(xs)[b * 8 + sub];
+                const float4 wv = reinterpret_cast<const float4*>(nw)[b * 8 + sub];
+                const float v0 = __fmul_rn(__fmul_rn(xv.x, scale), wv.x);
+                const float v1 = __fmul_rn(__fmul_rn(xv.y, scale), wv.y);
+                const float v2 = __fmul_rn(__fmul_rn(xv.z, scale), wv.z);
+                const float v3 = __fmul_rn(__fmul_rn(xv.w, scale), wv.w);
+                float am = fmaxf(fmaxf(absmax_lane(v0), absmax_lane(v1)), fmaxf(absmax_lane(v2), absmax_lane(v3)));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+                am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+                const Q8Scale sc = q8_scale(am);
+                const int q0 = q8_round(v0, sc.id), q1 = q8_round(v1, sc.id);
+                const int q2 = q8_round(v2, sc.id), q3 = q8_round(v3, sc.id);
+                reinterpret_cast<uint32_t*>(xq.qs)[b * 8 + sub] =
+                    (uint32_t)(q0 & 0xff) | ((uint32_t)(q1 & 0xff) << 8) | ((uint32_t)(q2 & 0xff) << 16) |
+                    ((uint32_t)(q3 & 0xff) << 24);
+                int qs = q0 + q1 + q2 + q3;
+                qs += __shfl_xor_sync(0xffffffffu, qs, 4);
+                qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+                qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+                if (sub == 0) {
+                    xq.d[b] = f16_bits_to_f32(sc.dh);
+                    xq.s8[b] = 8 * qs;
                 }
             }
         }
@@ -482,36 +690,48 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         if (tid == 0) stamp(l, 2);
 
         // ------------------------------------------------------------ C: gate/up units
+        // x blocks lane and lane + 32 stay in registers for all units when H <= 2048
+        const bool xreg = nbH <= 64;
+        XBlk xr0 = {}, xr1 = {};
+        if (xreg && warp < CW) {
+            if (lane < nbH) xr0 = load_xblk_s(xq, lane);
+            if (lane + 32 < nbH) xr1 = load_xblk_s(xq, lane + 32);
+        }
         for (int u = 0; u < n_gu; u++) {
-            wait_bar(mbar_gu + u, (unsigned)l & 1u, 3);
-            cta_sync();
-            if (flags[0]) goto drain;
+            const bool ok = wait_bar(mbar_gu + u, (unsigned)l & 1u, 3);
             if (u == 0 && tid == 0) stamp(l, 8);
-            if (tid == PT) pending &= ~(1u << u);
             const int unit = gu_units[u];
             const int j = unit / nbI, c = unit - j * nbI;
             float* shu = sh + (u & 1) * 32;
-            uint8_t* hr = hrec + (u & 1) * 64;
-            if (warp < CW) {
+            if (warp == CW) {
+                if (lane == 0) pending &= ~(1u << u);
+                if (__all_sync(0xffffffffu, ok) && u == n_gu - 1 && !d_place) {
+                    issue_down(l, layer, lbase, next);
+                    if (lane == 0) stamp(l, 10);
+                }
+            } else if (ok) {
                 const uint8_t* gate = arena + (size_t)u * 2 * gu_unit_bytes;
                 const uint8_t* up = gate + gu_unit_bytes;
                 const int r0 = warp * 2;   // two h rows per compute warp (CW * 2 == 32)
+                const uint8_t* rg0 = gate + (size_t)r0 * g.row_gu;
+                const uint8_t* rg1 = rg0 + g.row_gu;
+                const uint8_t* ru0 = up + (size_t)r0 * g.row_gu;
+                const uint8_t* ru1 = ru0 + g.row_gu;
                 float ag0 = 0.f, ag1 = 0.f, au0 = 0.f, au1 = 0.f;
+                // lane partials in block order b = lane, lane + 32, ... (the mirror order); x
+                // from registers for the first two blocks of each lane when they are held there
 #pragma unroll 1
-                for (int b = lane; b < nbH; b += 32) {
-                    XBlk xb = load_xblk_s(xq, b);
-                    const uint8_t* rg0 = gate + (size_t)r0 * g.row_gu;
-                    const uint8_t* rg1 = rg0 + g.row_gu;
-                    const uint8_t* ru0 = up + (size_t)r0 * g.row_gu;
-                    const uint8_t* ru1 = ru0 + g.row_gu;
-                    uint4 wg0 = *reinterpret_cast<const uint4*>(rg0 + 16 * b);
-                    uint4 wg1 = *reinterpret_cast<const uint4*>(rg1 + 16 * b);
-                    uint4 wu0 = *reinterpret_cast<const uint4*>(ru0 + 16 * b);
-                    uint4 wu1 = *reinterpret_cast<const uint4*>(ru1 + 16 * b);
-                    float dg0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg0 + 16 * nbH + 2 * b));
-                    float dg1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg1 + 16 * nbH + 2 * b));
-                    float du0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru0 + 16 * nbH + 2 * b));
-                    float du1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru1 + 16 * nbH + 2 * b));
+                for (int it = 0; lane + 32 * it < nbH; it++) {
+                    const int b = lane + 32 * it;
+                    const XBlk xb = (xreg && it < 2) ? (it ? xr1 : xr0) : load_xblk_s(xq, b);
+                    const uint4 wg0 = *reinterpret_cast<const uint4*>(rg0 + 16 * b);
+                    const uint4 wg1 = *reinterpret_cast<const uint4*>(rg1 + 16 * b);
+                    const uint4 wu0 = *reinterpret_cast<const uint4*>(ru0 + 16 * b);
+                    const uint4 wu1 = *reinterpret_cast<const uint4*>(ru1 + 16 * b);
+                    const float dg0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg0 + 16 * nbH + 2 * b));
+                    const float dg1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg1 + 16 * nbH + 2 * b));
+                    const float du0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru0 + 16 * nbH + 2 * b));
+                    const float du1 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru1 + 16 * nbH + 2 * b));
                     ag0 = __fadd_rn(ag0, block_term(block_sumi(wg0, xb), dg0, xb.d));
                     ag1 = __fadd_rn(ag1, block_term(block_sumi(wg1, xb), dg1, xb.d));
                     au0 = __fadd_rn(au0, block_term(block_sumi(wu0, xb), du0, xb.d));
@@ -523,8 +743,17 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                 const float hu = __shfl_sync(0xffffffffu, y, 16 + (lane & 8));  // its up
                 if ((lane & 23) == 0) shu[r0 + (lane >> 3)] = silu_mul_out(hg, hu);   // lanes 0 and 8
             }
-            cta_sync();
-            if (warp == 0) {
+            if (!cta_sync_and(ok)) goto drain;
+            // placement 1: the down rows go into unit 0's space, free from here on
+            if (u == 0 && d_place && warp == CW) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue_down(l, layer, lbase, next);
+                if (lane == 0) stamp(l, 10);
+            }
+            // one warp (rotating) turns the 32 h values into a Q8_0 record and publishes
+            // it as six tagged words; the others go on with the next unit
+            if (warp == u % CW) {
+                uint8_t* hr = hrec + (u & 1) * 64;
                 const Q8Res r = q8_block_lane(shu[lane]);
                 const int s = r.s8 >> 3;   // sum of the codes (|s| <= 32 * 127)
                 hr[lane] = (uint8_t)(int8_t)r.q;
@@ -536,141 +765,94 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                 }
                 __syncwarp();
                 if (lane < 6) {
-                    unsigned long long wv = tag << 48;
+                    unsigned long long wv = (unsigned long long)tag << 48;
 #pragma unroll
                     for (int t = 0; t < 6; t++) wv |= (unsigned long long)hr[lane * 6 + t] << (8 * t);
                     st_relaxed_u64(P.hqt + (((size_t)l * k + j) * nbI + c) * 6 + lane, wv);
                 }
             }
             // the next unit writes the other sh / hrec buffer; the one after it is
-            // ordered behind warp 0's publish by the next unit's barriers
+            // ordered behind this publish by the next unit's barrier
         }
         if (tid == 0) stamp(l, 3);
 
         // ------------------------------------------------------------ D: down rows + combine + next routing
-        if (d_n > 0) {
-            // gather all k * nbI h blocks (tagged words) into shared memory
-            const int nwords = k * nbI * 6;
-            {
-                const long long t0 = clock64();
-                int spins = 0;
-                while (true) {
-                    int ok = 1;
-#pragma unroll 1
-                    for (int w = tid; w < nwords; w += NT) {
-                        unsigned long long v = ld_relaxed_u64(P.hqt + (size_t)l * nwords + w);
-                        if ((v >> 48) != tag) {
-                            ok = 0;
-                            flags[1] = (l << 20) | ((w / 6) & 0xfff) << 8 | (int)((v >> 48) & 0xff);
-                        } else {
-                            uint8_t* r = rec + (size_t)(w / 6) * 36 + (w % 6) * 6;
-#pragma unroll
-                            for (int t = 0; t < 6; t++) r[t] = (uint8_t)(v >> (8 * t));
-                        }
-                    }
-                    if (cta_sync_and(ok)) break;
-                    if (tid == 0 && ((++spins & 63) == 0) && (clock64() - t0 > WAIT_CYCLES || error_seen())) fail(4);
-                    cta_sync();
-                    if (flags[0]) goto drain;
-                }
+        // Two stages: slots [0, ke) were computed as the first gate/up unit of their
+        // CTAs, so their h is complete early and their down values are computed while
+        // the late units still stream; then slots [ke, k).  Per row and slot, y_j is the
+        // mirror-order dot; the combine a = a + w_j * y_j runs in slot order at the end
+        // (engine.py:240-258).
+        const int ke = (P.k_early > 0 && P.k_early < k) ? P.k_early : k;
+        const unsigned long long* hwl = P.hqt + (size_t)l * k * nbI * 6;
+        auto gather_h = [&](int jlo, int jhi) -> bool {
+            return gather_h_records(hwl + (size_t)jlo * nbI * 6, (jhi - jlo) * nbI * 6, jlo, nbI, hq_base, (int)ab_i,
+                                    tag, P.ctl, flags, l);
+        };
+        auto down_partial = [&](int jlo, int jhi) {
+            down_rows(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
+        };
+        // stage 0: slots [0, ke); stage 1: slots [ke, k) (empty when ke == k)
+        for (int stage = 0; stage < 2; stage++) {
+            const int jlo = stage ? ke : 0, jhi = stage ? k : ke;
+            if (jlo >= jhi) continue;
+            if (d_n > 0) {
+                if (!cta_sync_and(gather_h(jlo, jhi))) goto drain;
             }
-            if (tid == 0) stamp(l, 4);
-            // records -> activation form: codes, fp32 scale, 8*sum
-#pragma unroll 1
-            for (int i = tid; i < k * nbI; i += NT) {
-                const uint8_t* r = rec + (size_t)i * 36;
-                int j = i / nbI, b = i - j * nbI;
-                ActView ha = act_view(hq_base + (size_t)j * ab_i, nbI);
-                int4* dq = reinterpret_cast<int4*>(ha.qs + (size_t)b * 32);
-                uint32_t wv[8];
-#pragma unroll
-                for (int t = 0; t < 8; t++)
-                    wv[t] = (uint32_t)r[4 * t] | ((uint32_t)r[4 * t + 1] << 8) | ((uint32_t)r[4 * t + 2] << 16) |
-                            ((uint32_t)r[4 * t + 3] << 24);
-                dq[0] = make_int4((int)wv[0], (int)wv[1], (int)wv[2], (int)wv[3]);
-                dq[1] = make_int4((int)wv[4], (int)wv[5], (int)wv[6], (int)wv[7]);
-                ha.d[b] = f16_bits_to_f32((uint16_t)(r[32] | (r[33] << 8)));
-                ha.s8[b] = 8 * (int)(int16_t)(uint16_t)(r[34] | (r[35] << 8));
+            if (tid == 0) stamp(l, stage ? 11 : 4);
+            if (stage == 0) {
+                if (!cta_sync_and(!(d_n > 0 || next) || wait_bar(mbar_d, (unsigned)l & 1u, 5))) goto drain;
+                if (tid == PT) pending &= ~(1u << 4);
+                if (tid == 0) stamp(l, 5);
             }
-            cta_sync();
-            if (tid == 0) stamp(l, 15);
+            if (d_n > 0) down_partial(jlo, jhi);
         }
-        if (d_armed) wait_bar(mbar_d, (unsigned)l & 1u, 5);
-        cta_sync();
-        if (flags[0]) goto drain;
-        if (tid == PT) pending &= ~(1u << 4);
-        if (tid == 0) stamp(l, 5);
-        if (d_n > 0 && warp < CW) {
-            const uint8_t* dbase = arena + (size_t)n_gu * 2 * gu_unit_bytes;
-            float* xout = next ? P.xbuf + (size_t)(l + 1) * g.H : P.x_out;
+        if (d_n > 0) {
+            cta_sync();
+            // combine in slot order and the residual: x_{l+1} = x_l + sum_j w_j * y_j
             const float* nw1 = snorm + (size_t)((l + 1) & 1) * g.H;
-            for (int q = warp; q < d_n; q += CW) {
-                const int r = d_lo + q;
+            for (int q = tid; q < d_n; q += NT) {
                 float a = 0.0f;
-                for (int j0 = 0; j0 < k; j0 += 8) {
-                    // lane partials of up to 8 experts, then one transposed reduction
-                    float acc[8];
-#pragma unroll
-                    for (int jj = 0; jj < 8; jj++) acc[jj] = 0.0f;
 #pragma unroll 1
-                    for (int b = lane; b < nbI; b += 32) {
-#pragma unroll
-                        for (int jj = 0; jj < 8; jj++) {
-                            const int j = j0 + jj;
-                            if (j < k) {
-                                const uint8_t* row = dbase + (size_t)j * d_chunk + (size_t)q * g.row_d;
-                                const ActView ha = act_view(hq_base + (size_t)j * ab_i, nbI);
-                                const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * b);
-                                const float dw =
-                                    f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * nbI + 2 * b));
-                                const XBlk xb = load_xblk_s(ha, b);
-                                acc[jj] = __fadd_rn(acc[jj], block_term(block_sumi(wv, xb), dw, xb.d));
-                            }
-                        }
-                    }
-                    const float y = warp_sum8_transposed(acc, lane);   // expert j0+jj in lanes 4jj..4jj+3
-                    for (int jj = 0; jj < 8 && j0 + jj < k; jj++)
-                        a = __fadd_rn(a, __fmul_rn(sw[j0 + jj], __shfl_sync(0xffffffffu, y, 4 * jj)));
-                }
-                if (lane == 0) {
-                    float xn = __fadd_rn(xs[r], a);
-                    xout[r] = xn;
+                for (int j = 0; j < k; j++) a = __fadd_rn(a, __fmul_rn(sh[64 + j], ys[(size_t)j * P.max_rows + q]));
+                const int r = d_lo + q;
+                const float xn = __fadd_rn(xs[r], a);
+                if (next) {
+                    st_relaxed_u64(P.xw + (size_t)(l + 1) * g.H + r, ((unsigned long long)tag << 32) | __float_as_uint(xn));
                     xnext[q] = xn;
-                    if (next) xw[q] = __fmul_rn(xn, nw1[r]);
+                    xw[q] = __fmul_rn(xn, nw1[r]);
+                } else {
+                    P.x_out[r] = xn;
                 }
             }
         }
         cta_sync();
         if (tid == 0) stamp(l, 6);
-        if (next) {
-            // release: the barrier orders every thread's x stores before thread 0's
-            // fence, and the next barrier orders the fence before the adds
-            if (tid == 0) fence_acq_rel_gpu();
-            cta_sync();
-            unsigned long long* accn = P.acc + (size_t)(l + 1) * (E + 1);
-            for (int e = tid; e <= E; e += NT) {
-                long long s = 0;
-                if (e < E)
-        #pragma unroll 1
-            for (int q = 0; q < d_n; q++) s += router_fixed(rt[(size_t)q * E + e], xw[q]);
-                else
-        #pragma unroll 1
-            for (int q = 0; q < d_n; q++) s += ss_fixed(xnext[q]);
-                red_add_relaxed_u64(accn + e, CNT_UNIT + (unsigned long long)s);
-            }
-        }
-        cta_sync();
+        if (next) router_partials(P.acc + (size_t)(l + 1) * acc_words);
         if (tid == 0) stamp(l, 7);
     }
 
-    // ---------------------------------------------------------------- finish: last CTA advances the epoch
+    // ---------------------------------------------------------------- finish
+    // The last CTA to finish recycles the last layer's sums, clears the tagged
+    // buffers before their 16-bit tag can repeat, and advances the epoch.
+    cta_sync();
     if (tid == 0) {
         __threadfence();
-        unsigned t = atomicAdd(P.ctl + 1, 1u);
-        if (t == (unsigned)G - 1) {
+        const unsigned t = atomicAdd(P.ctl + 1, 1u);
+        flags[2] = t == (unsigned)G - 1;
+    }
+    cta_sync();
+    if (flags[2]) {
+        __threadfence();
+        unsigned long long* last = P.acc + (size_t)(P.nL - 1) * acc_words;
+        for (size_t i = tid; i < acc_words; i += NT) last[i] = 0ull;
+        if (tag == 65535u) {
+            const size_t nh = (size_t)P.Lmax * k * nbI * 6, nx = (size_t)(P.Lmax + 1) * g.H;
+            for (size_t i = tid; i < nh; i += NT) P.hqt[i] = 0ull;
+            for (size_t i = tid; i < nx; i += NT) P.xw[i] = 0ull;
+        }
+        cta_sync();
+        if (tid == 0) {
             __threadfence();
-            unsigned long long* last = P.acc + (size_t)(P.nL - 1) * (E + 1);
-            for (int e = 0; e <= E; e++) last[e] = 0ull;
             P.ctl[1] = 0u;
             __threadfence();
             atomicAdd(P.ctl, 1u);
@@ -699,58 +881,53 @@ drain:
 // ---------------------------------------------------------------- host side
 
 int fused_plan(const Geom& g, int E, int k, int G, std::vector<uint16_t>& plan, size_t& arena_bytes,
-               int& max_rows) {
+               int& max_rows, int& k_early) {
     if (k > 16 || E > 1024 || G <= 0) return -1;
     const int n_gu_units = k * g.nbI;
     const size_t gu_b = 2 * 32 * g.row_gu;
-    const size_t drow_b = (size_t)k * g.row_d + (size_t)E * 4;   // one down row of all k experts + router column
-    std::vector<double> load(G, 0.0);
+    std::vector<int> n_of(G, 0);
     std::vector<std::vector<int>> gu(G);
     for (int u = 0; u < n_gu_units; u++) {
         int best = 0;
         for (int c = 1; c < G; c++)
-            if (load[c] < load[best]) best = c;
+            if (n_of[c] < n_of[best]) best = c;
         gu[best].push_back(u);
-        load[best] += (double)gu_b;
+        n_of[best]++;
     }
-    double total = (double)g.H * (double)drow_b;
-    for (int c = 0; c < G; c++) total += load[c];
-    const double target = total / G;
-    std::vector<double> quota(G);
-    double qs = 0;
-    for (int c = 0; c < G; c++) {
-        quota[c] = std::max(0.0, (target - load[c]) / (double)drow_b);
-        qs += quota[c];
-    }
-    std::vector<int> rows(G);
-    int assigned = 0;
-    for (int c = 0; c < G; c++) {
-        quota[c] = qs > 0 ? quota[c] * g.H / qs : (double)g.H / G;
-        rows[c] = (int)quota[c];
-        assigned += rows[c];
-    }
-    std::vector<int> order(G);
+    std::vector<int> rows(G, g.H / G), order(G);
     for (int c = 0; c < G; c++) order[c] = c;
-    std::stable_sort(order.begin(), order.end(),
-                     [&](int a, int b) { return quota[a] - rows[a] > quota[b] - rows[b]; });
-    for (int i = 0; assigned < g.H; i = (i + 1) % G, assigned++) rows[order[i]]++;
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return n_of[a] < n_of[b]; });
+    for (int i = 0; i < g.H % G; i++) rows[order[i]]++;
     plan.assign((size_t)G * FUSED_PLAN, 0);
     arena_bytes = 0;
     max_rows = 0;
     int lo = 0;
     for (int c = 0; c < G; c++) {
         if ((int)gu[c].size() > FUSED_MAX_GU || rows[c] > FUSED_MAX_ROWS) return -2;
+        const size_t down_b = (size_t)rows[c] * k * g.row_d;
+        const int place = (!gu[c].empty() && down_b <= gu_b) ? 1 : 0;
         uint16_t* p = plan.data() + (size_t)c * FUSED_PLAN;
         p[0] = (uint16_t)gu[c].size();
         p[1] = (uint16_t)lo;
         p[2] = (uint16_t)rows[c];
-        for (size_t i = 0; i < gu[c].size(); i++) p[3 + i] = (uint16_t)gu[c][i];
+        p[3] = (uint16_t)place;
+        for (size_t i = 0; i < gu[c].size(); i++) p[4 + i] = (uint16_t)gu[c][i];
         lo += rows[c];
-        arena_bytes = std::max(arena_bytes, gu[c].size() * gu_b + (size_t)rows[c] * k * g.row_d);
+        arena_bytes = std::max(arena_bytes, std::max(gu[c].size() * gu_b, (place ? 0 : gu[c].size() * gu_b) + down_b));
         max_rows = std::max(max_rows, rows[c]);
     }
     if (lo != g.H) return -3;
     arena_bytes = (arena_bytes + 15) & ~(size_t)15;
+    std::vector<char> first(n_gu_units, 0);
+    for (int c = 0; c < G; c++)
+        if (!gu[c].empty()) first[gu[c][0]] = 1;
+    k_early = 0;
+    while (k_early < k) {
+        bool all = true;
+        for (int c = 0; c < g.nbI; c++) all = all && first[k_early * g.nbI + c];
+        if (!all) break;
+        k_early++;
+    }
     return 0;
 }
 

@@ -14,13 +14,16 @@ constexpr int FUSED_MAX_GU = 4;          // gate/up units (32 rows of one expert
 constexpr int FUSED_MAX_ROWS = 64;       // contiguous down-projection output rows per CTA
 constexpr int FUSED_COMPUTE_WARPS = 16;  // warps that compute (2 h rows each per gate/up unit)
 constexpr int FUSED_THREADS = (FUSED_COMPUTE_WARPS + 1) * 32;  // + one producer warp issuing copies
-constexpr int FUSED_PLAN = 3 + FUSED_MAX_GU;  // per CTA: n_gu, first down row, down rows, gu units
-// phase stamps: 0 routing seen, 1 copies issued, 2 x quantised, 3 gate/up published,
-// 4 h gathered, 5 down data landed, 6 down rows done, 7 next-layer sums sent,
-// 8 first gate/up unit landed, 9 top-k done, 10 softmax done, 11 producer start,
-// 12 after the proxy fence, 13 gate/up copies issued, 14 x loaded, 15 h records decoded
-// slots 16..31 hold the SM's clock64 at the same events
+constexpr int FUSED_PLAN = 4 + FUSED_MAX_GU;  // per CTA: n_gu, first down row, down rows, down placement, units
+// phase stamps: 0 routing and x seen, 1 gate/up copies issued, 2 x quantised,
+// 3 gate/up published, 4 early h gathered, 5 down data landed, 6 down rows done,
+// 7 next-layer sums sent, 8 first gate/up unit landed, 9 top-k done,
+// 10 down copies issued, 11 late h gathered; slots 16..31 hold the SM's clock64 at
+// the same events
 constexpr int FUSED_TRACE = 32;
+// router sums are spread over this many accumulator copies (CTA c adds into copy
+// c % FUSED_ACC), so each word takes ~G / FUSED_ACC atomic adds instead of G
+constexpr int FUSED_ACC = 8;
 
 struct FusedParams {
     const uint8_t* weights;   // [L][E] row-split experts
@@ -31,25 +34,27 @@ struct FusedParams {
     float eps;                // RMSNorm epsilon
     int E, k, L0, nL;         // layers [L0, L0 + nL) of the model
     int max_rows;             // largest down-row range of any CTA
+    int k_early;              // > 0: down in two stages, slots [0, k_early) (all their gate/up units
+                              // first in their CTAs) before the rest; 0: one stage
     const float* x_in;        // hidden state in
     float* x_out;             // hidden state out (may equal x_in when nL >= 2)
-    float* xbuf;              // [nL + 1][H] intermediate hidden states
-    unsigned long long* acc;  // [nL][E + 1] count-tagged fixed-point router sums, then sum of x^2
-                              // (zero between launches)
-    unsigned long long* hqt;  // [nL][k * nbI * 6] epoch-tagged requantised h words
+    unsigned long long* xw;   // [Lmax + 1][H] hidden states between layers: (tag << 32) | f32 bits
+    unsigned long long* acc;  // [nL][FUSED_ACC][E + 1] count-tagged fixed-point router sums, then
+                              // sum of x^2 (zero between launches)
+    unsigned long long* hqt;  // [Lmax][k * nbI * 6] tagged requantised h words: (tag << 48) | 6 bytes
+    int Lmax;                 // layers the xw / hqt buffers hold (cleared before the tag repeats)
     unsigned* ctl;            // [0] epoch, [1] finished CTAs, [2] error stage, [3] error detail
     const uint16_t* plan;     // [G][FUSED_PLAN]
     int* idx_out;             // [L][k] routing record (absolute layer index)
     float* w_out;             // [L][k]
     float* logits_out;        // [L][E]
-    unsigned long long* trace;  // optional [nL][G][FUSED_TRACE] %globaltimer stamps per CTA and layer
+    unsigned long long* trace;  // optional [nL][G][FUSED_TRACE] stamps per CTA and layer
     size_t arena_bytes;       // weight staging bytes per CTA
 };
 
 // Shared-memory carve-up, identical on host and device.
 struct FusedSmem {
-    uint32_t mbar, plan, slogfx, slog, sidx, sw, flags, xs, xq, hq, rec, sh, hrec, xnext, xw, rt, snorm, arena,
-        total;
+    uint32_t mbar, plan, slogfx, slog, sidx, flags, xs, xq, hq, sh, hrec, xnext, xw, rt, snorm, ys, arena, total;
 };
 
 TG_HD uint32_t fused_take(uint32_t& o, size_t bytes) {
@@ -63,31 +68,34 @@ TG_HD FusedSmem fused_smem_layout(const FusedParams& P) {
     uint32_t o = 0;
     s.mbar = fused_take(o, 8 * (FUSED_MAX_GU + 2));
     s.plan = fused_take(o, 2 * FUSED_PLAN);
-    s.slogfx = fused_take(o, 8 * ((size_t)P.E + 1));
+    s.slogfx = fused_take(o, 8 * (size_t)FUSED_ACC * ((size_t)P.E + 1));   // per-copy router sums
     s.slog = fused_take(o, 4 * (size_t)P.E);
     s.sidx = fused_take(o, 4 * 16);
-    s.sw = fused_take(o, 4 * 16);
     s.flags = fused_take(o, 4 * 8);
     s.xs = fused_take(o, 4 * (size_t)P.g.H);
     s.xq = fused_take(o, act_bytes(P.g.nbH));
     s.hq = fused_take(o, act_bytes(P.g.nbI) * P.k);
-    s.rec = fused_take(o, 36 * (size_t)P.k * P.g.nbI);
-    s.sh = fused_take(o, 2 * 4 * 32);       // h of a gate/up unit, double buffered
-    s.hrec = fused_take(o, 2 * 64);         // its Q8_0 record, double buffered
+    s.sh = fused_take(o, 4 * (2 * 32 + 16));  // h of a gate/up unit, double buffered; routing weights
+    s.hrec = fused_take(o, 2 * 64);           // its Q8_0 record, double buffered
     s.xnext = fused_take(o, 4 * (size_t)P.max_rows);
     s.xw = fused_take(o, 4 * (size_t)P.max_rows);
     s.rt = fused_take(o, 4 * (size_t)P.max_rows * P.E);
     s.snorm = fused_take(o, 2 * 4 * (size_t)P.g.H);   // FFN norm weights, double buffered by layer parity
+    s.ys = fused_take(o, 4 * 16 * (size_t)P.max_rows);  // per-slot down values of this CTA's rows
     s.arena = fused_take(o, P.arena_bytes);
     s.total = o;
     return s;
 }
 
 // Static work split of one layer over G CTAs: gate/up units by longest-processing-
-// time greedy on bytes, then contiguous down-row ranges sized to even out each
-// CTA's total bytes.  Returns 0, or < 0 when the shape does not fit the limits.
+// time greedy, then contiguous down-row ranges of H/G or H/G + 1 rows (the extra
+// rows to CTAs with fewer units).  A CTA's down rows go into the space of its first
+// gate/up unit once that unit is computed when they fit there (placement 1), else
+// after its units (placement 0, fetched once its last unit has landed).  k_early
+// counts the leading slots whose units are all first units of their CTAs (their h
+// is complete early).  Returns 0, or < 0 when the shape does not fit the limits.
 int fused_plan(const Geom& g, int E, int k, int G, std::vector<uint16_t>& plan, size_t& arena_bytes,
-               int& max_rows);
+               int& max_rows, int& k_early);
 cudaError_t fused_prepare(const FusedParams& P);
 cudaError_t fused_occupancy(const FusedParams& P, int* blocks_per_sm);
 cudaError_t launch_decode_fused(const FusedParams& P, int G, cudaStream_t s);

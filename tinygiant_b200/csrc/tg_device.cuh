@@ -126,12 +126,12 @@ __device__ __forceinline__ long long warp_sum_i64(long long v) {
     return v;
 }
 
-// Router product in fixed point: rint(clamp(fl(r*x), +-512) * 2^32).  The clamp
-// bounds any sum over <= 2^14 rows below 2^55, so sums are exact, independent of
-// how rows are split, and can never reach the count tag kept above bit 56.
+// Router product in fixed point: rint(clamp(fl(r*x), +-256) * 2^32).  The clamp
+// bounds any sum over <= 2^14 rows by 2^54, so sums are exact, independent of
+// how rows are split, and stay clear of the count tag kept from bit 56 up.
 __device__ __forceinline__ long long router_fixed(float r, float x) {
     float p = __fmul_rn(r, x);
-    p = fminf(fmaxf(p, -512.0f), 512.0f);
+    p = fminf(fmaxf(p, -256.0f), 256.0f);
     return __float2ll_rn(__fmul_rn(p, 0x1p32f));
 }
 __device__ __forceinline__ float router_logit(long long s) {
