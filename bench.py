@@ -285,9 +285,17 @@ def run_ours(args):
     if pk.exists():
         peaks = json.loads(pk.read_text())
     peak_gbs = peaks.get("hbm_gbs", 6650.0)
+    # DRAM bytes per launch from the committed ncu summary (4-layer capture scaled to 48)
+    traffic = None
+    prof = ROOT / "profiles" / "k_decode_fused_qwen3.txt"
+    if fused and NL == L and prof.exists():
+        for line in prof.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1])
     achieved = q4_bytes / (kernel_ms / 1000.0) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak_gbs, "unit": "GB/s",
-                "frac": achieved / peak_gbs, "traffic": None,
+                "frac": achieved / peak_gbs, "traffic": traffic,
+                "traffic_source": "ncu dram__bytes_read+write, profiles/k_decode_fused_qwen3.txt" if traffic else None,
                 "kernel": ("k_decode_fused: one launch per token, all layers" if fused
                            else f"decode step, {kernels_per_step} launches (CUDA graph)"),
                 "kernel_ms": kernel_ms,
