@@ -266,14 +266,15 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
 // row (two rows per warp above 16 rows, sharing each h block load), lane partials
 // in block order b = lane, lane + 32, ... for up to 8 slots, then one transposed
 // reduction per row (the mirror order).  Called from one place only.
+template <bool TWO>
 __device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* hq_base, float* ys, uint32_t d_chunk,
                                        int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (warp >= CW) return;
-    const int rpw = d_n <= CW ? 1 : 2;
+    const int rpw = TWO ? 2 : 1;
     for (int pr = warp; pr * rpw < d_n; pr += CW) {
         const int q0 = pr * rpw;
-        const bool two = rpw == 2 && q0 + 1 < d_n;
+        const bool two = TWO && q0 + 1 < d_n;
         for (int j0 = jlo; j0 < jhi; j0 += 8) {
             float acc0[8], acc1[8];
 #pragma unroll
@@ -322,6 +323,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     uint16_t* plan = reinterpret_cast<uint16_t*>(smem + S.plan);
     long long* slog_fx = reinterpret_cast<long long*>(smem + S.slogfx);   // [FUSED_ACC][E + 1]
     float* slog = reinterpret_cast<float*>(smem + S.slog);
+    unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + S.skey);   // [E] rank keys
     int* sidx = reinterpret_cast<int*>(smem + S.sidx);
     int* flags = reinterpret_cast<int*>(smem + S.flags);   // [0] error seen, [1] error detail, [2] last CTA
     float* sscale = reinterpret_cast<float*>(flags + 4);   // RMSNorm scale of the current layer
@@ -579,25 +581,35 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             };
             const float scale = rms_scale_from(total(E), g.H, P.eps);
 #pragma unroll 1
-            for (int e = tid; e < E; e += NT) slog[e] = __fmul_rn(scale, router_logit(total(e)));
+            for (int e = tid; e < E; e += NT) {
+                // +0 for a zero logit, so equal logits get equal keys
+                const float lg = __fadd_rn(__fmul_rn(scale, router_logit(total(e))), 0.0f);
+                slog[e] = lg;
+                // rank key: order-preserving bits of the logit, then the expert id, so
+                // key_j > key_e exactly when l_j > l_e or (l_j == l_e and j > e)
+                const unsigned b = __float_as_uint(lg);
+                const unsigned ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+                skey[e] = ((unsigned long long)ord << 32) | (unsigned)e;
+            }
             if (tid == 0) *sscale = scale;
             // every CTA has contributed to acc[l], so acc[l-1] is read by no one: recycle it
             if (cta == 0 && l >= 1)
                 for (size_t i = tid; i < acc_words; i += NT) accl[i - acc_words] = 0ull;
         }
         cta_sync();
-        // top-k by rank: 4 threads per expert share the scan (interleaved, so the four
-        // read neighbouring banks); the element beaten by fewer than k others (larger
-        // logit, or equal logit and larger id) is kept
+        // top-k by rank: 4 threads per expert share the scan, two keys per 16-byte
+        // load (the four parts read neighbouring banks); the element beaten by fewer
+        // than k others (larger logit, or equal logit and larger id) is kept
         for (int base = 0; base < E; base += NT / 4) {
             const int e = base + (tid >> 2), part = tid & 3;
             int rank = 0;
             if (e < E) {
-                const float le = slog[e];
-#pragma unroll 8
-                for (int j = part; j < E; j += 4) {
-                    const float lj = slog[j];
-                    rank += (lj > le) || (lj == le && j > e);
+                const unsigned long long ke = skey[e];
+                const ulonglong2* kp = reinterpret_cast<const ulonglong2*>(skey);
+#pragma unroll 4
+                for (int j2 = part; 2 * j2 < E; j2 += 4) {
+                    const ulonglong2 kk = kp[j2];
+                    rank += (kk.x > ke) + (kk.y > ke);
                 }
             }
             __syncwarp();
@@ -789,7 +801,11 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                                     tag, P.ctl, flags, l);
         };
         auto down_partial = [&](int jlo, int jhi) {
-            down_rows(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
+            // one row per warp up to 16 rows, else two rows per warp sharing each h block load
+            if (d_n <= CW)
+                down_rows<false>(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
+            else
+                down_rows<true>(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
         };
         // stage 0: slots [0, ke); stage 1: slots [ke, k) (empty when ke == k)
         for (int stage = 0; stage < 2; stage++) {

@@ -54,7 +54,8 @@ struct FusedParams {
 
 // Shared-memory carve-up, identical on host and device.
 struct FusedSmem {
-    uint32_t mbar, plan, slogfx, slog, sidx, flags, xs, xq, hq, sh, hrec, xnext, xw, rt, snorm, ys, arena, total;
+    uint32_t mbar, plan, slogfx, slog, skey, sidx, flags, xs, xq, hq, sh, hrec, xnext, xw, rt, snorm, ys, arena,
+        total;
 };
 
 TG_HD uint32_t fused_take(uint32_t& o, size_t bytes) {
@@ -70,6 +71,7 @@ TG_HD FusedSmem fused_smem_layout(const FusedParams& P) {
     s.plan = fused_take(o, 2 * FUSED_PLAN);
     s.slogfx = fused_take(o, 8 * (size_t)FUSED_ACC * ((size_t)P.E + 1));   // per-copy router sums
     s.slog = fused_take(o, 4 * (size_t)P.E);
+    s.skey = fused_take(o, 8 * (size_t)P.E);
     s.sidx = fused_take(o, 4 * 16);
     s.flags = fused_take(o, 4 * 8);
     s.xs = fused_take(o, 4 * (size_t)P.g.H);
