@@ -2,9 +2,11 @@
 """Batch-1 MoE expert-FFN decode benchmark, Qwen3-30B-A3B shape, on B200.
 
 One step = one decode token through all 48 MoE layers, chained
-(x_{l+1} = x_l + moe_l(x_l), tinygiant/engine.py:229-258 without attention and
-norms): per layer the router (128 x 2048 fp32), top-8 + softmax, the 8 chosen
-experts' gate/up (Q4_0) -> SwiGLU -> Q8_0 requant -> down, weighted combine.
+(x_{l+1} = x_l + moe_l(RMSNorm(x_l)), tinygiant/engine.py:229-258 without
+attention): per layer the FFN RMSNorm, the router (128 x 2048 fp32), top-8 +
+softmax, the 8 chosen experts' gate/up (Q4_0) -> SwiGLU -> Q8_0 requant -> down,
+weighted combine.  With --tokens T > 1 a step is T tokens through the batched
+path (each expert's weights read once per layer for all its tokens).
 Weights: 48 x 128 synthetic Q4_0 experts drawn from N(0, 0.02), all resident in
 HBM (16.3 GB); routers N(0, 0.02); a fresh N(0, 1) hidden state per step.
 
@@ -48,6 +50,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--multi", action="store_true", help="three kernels per layer instead of the fused kernel")
     ap.add_argument("--layers", type=int, default=L, help="fewer layers, for small profiling cases only")
+    ap.add_argument("--tokens", type=int, default=1, help="T > 1: T tokens per step through the batched path")
     return ap.parse_args()
 
 
@@ -345,10 +348,87 @@ def run_ours(args):
     return 0
 
 
+def run_batched(args):
+    """T tokens per step through all layers with the batched kernels (tgx_decode_batched)."""
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = init_dist(ws, "nccl") if ws > 1 else None
+    from tinygiant_b200.engine import MoEModel
+
+    T, NL = args.tokens, args.layers
+    model = MoEModel(H, I, E, K_TOP, NL, device=local)
+    model.fill_synthetic(args.seed + 7919 * rank)
+    K, W = args.steps, max(3, args.warmup)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed + rank)
+    pool = [torch.randn(T, H, generator=gen, device="cuda") for _ in range(4)]
+    X = torch.empty(T, H, device="cuda")
+    stream = torch.cuda.current_stream()
+    for i in range(W):
+        X.copy_(pool[i % 4])
+        model.decode_batched(X, stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(K):
+        X.copy_(pool[i % 4])                    # fresh hidden states (device copy, 8 KB per token)
+        model.decode_batched(X, stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    # e2e: host pinned tokens in, results out, every step
+    Xh = pool[0].cpu().pin_memory()
+    Yh = torch.empty_like(Xh).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ke = max(1, K // 4)
+    e0.record(stream)
+    for i in range(ke):
+        X.copy_(Xh, non_blocking=True)
+        model.decode_batched(X, stream)
+        Yh.copy_(X, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms, ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ems = float(t[0]), float(t[1])
+    model.close()
+    if rank == 0:
+        distinct = min(E, T * K_TOP)   # at most this many experts per layer are read
+        out = {
+            "metric": f"batched MoE decode tok/s (Qwen3-30B-A3B shape, {T} tokens per step)",
+            "value": ws * T * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"configs[2]: {T} tokens per step, {NL} layers, batched path",
+                       "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "layers": NL, "tokens": T,
+                       "parallelism": "replicas" if ws > 1 else "single GPU"},
+            "weights_read_upper_bound_gbs": NL * distinct * EXPERT_BYTES / (ms / K / 1000.0) / 1e9,
+            "e2e": {"value": ws * T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4},
+            "gpu_launches": 7 * NL * K,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(out), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.tokens > 1:
+        return run_batched(args)
     return run_ours(args)
 
 

@@ -155,6 +155,16 @@ int tgx_moe_layer(tgx_ctx *ctx, int layer, float *x_dev, void *stream);
 #define TGX_MULTI 2   /* three kernels per layer instead of the single fused kernel per step */
 int tgx_decode_step(tgx_ctx *ctx, float *x_dev, void *stream, int flags);
 
+/* The MoE block for T tokens at once (prefill, or T independent decode streams),
+ * in place on x_dev[T][embed]: each token gets exactly what tgx_moe_layer gives it,
+ * bit for bit (engine.py:229-258 per token).  Each expert's weights are read once per
+ * layer for all the tokens routed to it.  1 <= T <= 65536/top_k.  Grows a scratch
+ * buffer in the context on first use of a larger T (cudaMalloc; not during capture). */
+int tgx_moe_batched(tgx_ctx *ctx, int layer, float *x_dev, int T, void *stream);
+
+/* All L MoE blocks for T tokens, layer after layer (tgx_moe_batched for l = 0 .. L-1). */
+int tgx_decode_batched(tgx_ctx *ctx, float *x_dev, int T, void *stream);
+
 /* Synchronise the context's device and report whether a bounded wait inside the
  * fused decode kernel expired since the last call (TG_ETIMEOUT; the kernel's
  * cross-block state is then reset).  TG_OK otherwise. */

@@ -67,6 +67,7 @@ def lib():
         "ref_decode_step": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, VP]),
         "ref_decode_step_mt": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, CI]),
         "ref_moe_layer_batched": (None, [VP, ctypes.c_size_t, VP, VP, CI, CI, CI, CI, CI, CI, CI]),
+        "ref_moe_block_batched": (None, [VP, ctypes.c_size_t, VP, VP, CF, VP, CI, CI, CI, CI, CI, CI, CI]),
         "ref_fill_normal": (None, [VP, I64, ctypes.c_uint64, CF]),
     }
     for name, (res, args) in sig.items():
@@ -251,6 +252,18 @@ def moe_layer_batched(layer_blob, R, x, k, embed, inter, mode=TG_MIRROR, n_threa
     lib().ref_moe_layer_batched(_p(np.ascontiguousarray(layer_blob)), expert_bytes(embed, inter),
                                 _p(np.ascontiguousarray(R, dtype=np.float32)), _p(x), T, R.shape[0], k,
                                 embed, inter, mode, n_threads)
+    return x
+
+
+def moe_block_batched(layer_blob, R, x, k, embed, inter, normw=None, eps: float = RMS_EPS, mode=TG_MIRROR,
+                      n_threads=0):
+    """moe_block for every row of x[T][embed] (independent tokens); returns the new x."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    T = x.shape[0]
+    nw = None if normw is None else np.ascontiguousarray(normw, dtype=np.float32)
+    lib().ref_moe_block_batched(_p(np.ascontiguousarray(layer_blob)), expert_bytes(embed, inter),
+                                _p(np.ascontiguousarray(R, dtype=np.float32)), None if nw is None else _p(nw), eps,
+                                _p(x), T, R.shape[0], k, embed, inter, mode, n_threads)
     return x
 
 

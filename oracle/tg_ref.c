@@ -541,6 +541,23 @@ void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const
                       embed, inter, mode, NULL, NULL, NULL);
 }
 
+/* The MoE block with its FFN RMSNorm for T independent tokens x[T][embed], in place:
+ * ref_moe_block per token (engine.py:229-258 for each row of a batch); tokens run in
+ * parallel across n_threads (0 = OpenMP default). */
+void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                           float eps, float *x, int T, int n_experts, int k, int embed, int inter, int mode,
+                           int n_threads) {
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+    #pragma omp parallel for schedule(dynamic, 1)
+#else
+    (void)n_threads;
+#endif
+    for (int t = 0; t < T; t++)
+        ref_moe_block(layer_blob, expert_bytes, R, normw, eps, x + (size_t)t * embed, n_experts, k, embed, inter,
+                      mode, NULL, NULL, NULL);
+}
+
 /* ------------------------------------------------------------------ data */
 
 static inline uint64_t splitmix64(uint64_t *s) {

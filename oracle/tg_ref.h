@@ -91,6 +91,9 @@ void ref_decode_step(const uint8_t *const *layer_blobs, const float *const *rout
                      int mode, int32_t *idx_out /* [n_layers*k] or NULL */);
 
 /* Batched tokens: T independent tokens through one MoE block (x is [T][embed]). */
+void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                           float eps, float *x, int T, int n_experts, int k, int embed, int inter, int mode,
+                           int n_threads);
 void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
                            float *x, int T, int n_experts, int k, int embed, int inter,
                            int mode, int n_threads);

@@ -1,0 +1,331 @@
+// tg_batched.cu — the MoE block for T tokens at once (prefill / batched decode).
+//
+// Per layer (tinygiant/engine.py:229-258 applied to every token, attention excluded):
+//   k_router_sums_batched   exact fixed-point router sums S[t][e] = sum_r R[e][r] * fl(x[t][r] * w[r]),
+//                           split over 256-column chunks (int64 atomics: exact, split-independent)
+//   k_topk_quant_batched    per token: sum x^2 -> RMSNorm scale, logits, top-k + softmax
+//                           (engine.py:229-236), Q8_0 of (x * scale) * w (libtinygiant.c:61-89)
+//   k_group_pairs           (token, slot) pairs grouped by expert (counting sort)
+//   k_gateup_batched        per (expert, 32-row unit): the unit's gate and up rows are staged in
+//                           shared memory once, then h = silu(g) * u and its Q8_0 block for every
+//                           token routed to the expert (libtinygiant.c:566-586)
+//   k_down_batched          per (expert, 16 output rows): the rows are staged once, then
+//                           y[pair][r] for every token routed to the expert (:588-594)
+//   k_combine_batched       x[t] += sum_j w[t][j] * y[(t, j)] in slot order (engine.py:240-258)
+// Each token's values use the same reduction order as the single-token kernels (lane-strided
+// block partials, xor butterfly), so a batch gives bit-identical results to T single-token
+// calls and to the CPU oracle's mirror mode.
+#include <cuda_runtime.h>
+
+#include "tg_device.cuh"
+#include "tg_internal.h"
+
+namespace tg {
+
+namespace {
+
+constexpr int RT_TOK = 4;         // tokens per router CTA
+constexpr int DOWN_ROWS = 16;     // output rows per down CTA
+
+// grid (ceil(T / RT_TOK), ceil(E / 8), H / 256), 256 threads: warp w adds expert
+// 8 * blockIdx.y + w's fixed-point partial sums over a 256-column chunk for RT_TOK tokens
+// into S[t][e] (exact int64, so the split does not change the sums; S starts at zero).
+__global__ void __launch_bounds__(256) k_router_sums_batched(const float* __restrict__ X, int T,
+                                                             const float* __restrict__ R,
+                                                             const float* __restrict__ normw, int E, int H,
+                                                             unsigned long long* __restrict__ S) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.y * 8 + warp;
+    const int t0 = blockIdx.x * RT_TOK;
+    const int nt = min(RT_TOK, T - t0);
+    const int c0 = blockIdx.z * 256;
+    if (e >= E) return;
+    long long s[RT_TOK];
+#pragma unroll
+    for (int t = 0; t < RT_TOK; t++) s[t] = 0;
+    const float* rr = R + (size_t)e * H;
+    for (int c = c0 + 4 * lane; c < c0 + 256; c += 128) {
+        const float4 rv = __ldg(reinterpret_cast<const float4*>(rr + c));
+        const float4 nv = __ldg(reinterpret_cast<const float4*>(normw + c));
+#pragma unroll
+        for (int t = 0; t < RT_TOK; t++) {
+            if (t < nt) {
+                const float4 xv = __ldg(reinterpret_cast<const float4*>(X + (size_t)(t0 + t) * H + c));
+                s[t] += router_fixed(rv.x, __fmul_rn(xv.x, nv.x)) + router_fixed(rv.y, __fmul_rn(xv.y, nv.y)) +
+                        router_fixed(rv.z, __fmul_rn(xv.z, nv.z)) + router_fixed(rv.w, __fmul_rn(xv.w, nv.w));
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < RT_TOK; t++) {
+        const long long v = warp_sum_i64(s[t]);
+        if (lane == 0 && t < nt) atomicAdd(S + (size_t)(t0 + t) * E + e, (unsigned long long)v);
+    }
+}
+
+// grid T, 256 threads: token t's RMSNorm scale, logits, top-k and softmax weights, and
+// the Q8_0 activation form of (x * scale) * w.
+__global__ void __launch_bounds__(256) k_topk_quant_batched(const float* __restrict__ X, const float* __restrict__ normw,
+                                                            float eps, int E, int H, int k,
+                                                            const unsigned long long* __restrict__ S, int* __restrict__ idx,
+                                                            float* __restrict__ wts, float* __restrict__ logits,
+                                                            uint8_t* __restrict__ xq) {
+    __shared__ float sl[1024];
+    __shared__ int sidx[MAX_TOPK];
+    __shared__ float sw[MAX_TOPK];
+    __shared__ long long wsum[8];
+    __shared__ float sscale;
+    const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float* x = X + (size_t)t * H;
+    long long ss = 0;
+    for (int r = threadIdx.x; r < H; r += blockDim.x) ss += ss_fixed(x[r]);
+    ss = warp_sum_i64(ss);
+    if (lane == 0) wsum[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long tot = 0;
+        for (int w = 0; w < 8; w++) tot += wsum[w];
+        sscale = rms_scale_from(tot, H, eps);
+    }
+    __syncthreads();
+    const float scale = sscale;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const float l = __fmul_rn(scale, router_logit((long long)S[(size_t)t * E + e]));
+        sl[e] = l;
+        if (logits) logits[(size_t)t * E + e] = l;
+    }
+    __syncthreads();
+    topk_softmax_block(sl, E, k, sidx, sw);
+    if (threadIdx.x < k) {
+        idx[(size_t)t * k + threadIdx.x] = sidx[threadIdx.x];
+        wts[(size_t)t * k + threadIdx.x] = sw[threadIdx.x];
+    }
+    // Q8_0 of the normed input, one warp per block (the single-token quantiser's order)
+    const int nb = H / 32;
+    ActView a = act_view(xq + (size_t)t * act_bytes(nb), nb);
+    for (int b = warp; b < nb; b += 8) {
+        const float v = __fmul_rn(__fmul_rn(x[(size_t)b * 32 + lane], scale), normw[(size_t)b * 32 + lane]);
+        const Q8Lane q = quantize_lane(v);
+        a.qs[(size_t)b * 32 + lane] = (int8_t)q.q;
+        if (lane == 0) {
+            a.d[b] = f16_bits_to_f32(q.dh);
+            a.s8[b] = q.s8;
+        }
+    }
+}
+
+// one CTA of 256 threads: pairs p = t * k + j grouped by expert idx[p]; off[E + 1],
+// list[T * k] (the order inside a group does not affect any result) and the active experts
+__global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int E,
+                                                     int* __restrict__ off, int* __restrict__ list,
+                                                     int* __restrict__ active) {
+    __shared__ int cnt[1024];
+    __shared__ int pos[1024];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) atomicAdd(&cnt[idx[p]], 1);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0, na = 0;
+        for (int e = 0; e < E; e++) {
+            off[e] = acc;
+            pos[e] = acc;
+            acc += cnt[e];
+            if (cnt[e]) active[1 + na++] = e;
+        }
+        off[E] = acc;
+        active[0] = na;   // active[1 .. na]: the experts with tokens, ascending
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) list[atomicAdd(&pos[idx[p]], 1)] = p;
+}
+
+// grid (I / 32, min(E, T * k)), 256 threads.  CTA (c, a) takes the a-th active expert e and
+// stages rows 32c .. 32c+31 of its
+// gate and up in shared memory, then for every pair p routed to e: 4 rows per warp,
+// h = silu(g) * u, and h's Q8_0 block c into hq[p].
+__global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer, Geom g,
+                                                        const int* __restrict__ off, const int* __restrict__ list,
+                                                        const int* __restrict__ active, int k,
+                                                        const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq) {
+    extern __shared__ __align__(16) uint8_t smem[];   // gate rows | up rows
+    __shared__ float sh[32];
+    if ((int)blockIdx.y >= active[0]) return;
+    const int e = active[1 + blockIdx.y], c = blockIdx.x;
+    const int p0 = off[e], n = off[e + 1] - p0;
+    if (n == 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint8_t* eb = layer + (size_t)e * g.expert_bytes;
+    const size_t unit = (size_t)32 * g.row_gu;
+    {
+        const int4* sg = reinterpret_cast<const int4*>(eb + (size_t)c * unit);
+        const int4* su = reinterpret_cast<const int4*>(eb + g.t_gu + (size_t)c * unit);
+        int4* d = reinterpret_cast<int4*>(smem);
+        const int n16 = (int)(unit / 16);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+            d[i] = __ldg(sg + i);
+            d[n16 + i] = __ldg(su + i);
+        }
+    }
+    __syncthreads();
+    const uint8_t* gate = smem;
+    const uint8_t* up = smem + unit;
+    const int nb = g.nbH, i0 = warp * 4;
+    const size_t abx = act_bytes(nb), abh = act_bytes(g.nbI);
+    for (int q = 0; q < n; q++) {
+        const int p = list[p0 + q], t = p / k;
+        const ActView xa = act_view(xq + (size_t)t * abx, nb);
+        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int b = lane; b < nb; b += 32) {
+            const XBlk xb = load_xblk(xa, b);
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const uint8_t* rg = gate + (size_t)(i0 + r) * g.row_gu;
+                const uint8_t* ru = up + (size_t)(i0 + r) * g.row_gu;
+                const uint4 wg = *reinterpret_cast<const uint4*>(rg + 16 * b);
+                const uint4 wu = *reinterpret_cast<const uint4*>(ru + 16 * b);
+                const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 16 * (size_t)nb + 2 * b));
+                const float du = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru + 16 * (size_t)nb + 2 * b));
+                ag[r] = __fadd_rn(ag[r], block_term(block_sumi(wg, xb), dg, xb.d));
+                au[r] = __fadd_rn(au[r], block_term(block_sumi(wu, xb), du, xb.d));
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const float gv = warp_sum_butterfly(ag[r]);
+            const float uv = warp_sum_butterfly(au[r]);
+            if (lane == r) sh[i0 + r] = silu_mul(gv, uv);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const Q8Lane qz = quantize_lane(sh[lane]);
+            ActView ha = act_view(hq + (size_t)p * abh, g.nbI);
+            ha.qs[(size_t)c * 32 + lane] = (int8_t)qz.q;
+            if (lane == 0) {
+                ha.d[c] = f16_bits_to_f32(qz.dh);
+                ha.s8[c] = qz.s8;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// grid (H / 16, min(E, T * k)), 256 threads.  CTA (rb, a) takes the a-th active expert e,
+// stages its down rows 16rb .. 16rb+15, then for every pair p routed to e: 2 rows per
+// warp, y[p][r] = row . hq[p].
+__global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer, Geom g,
+                                                      const int* __restrict__ off, const int* __restrict__ list,
+                                                      const int* __restrict__ active, const uint8_t* __restrict__ hq,
+                                                      float* __restrict__ y) {
+    extern __shared__ __align__(16) uint8_t smem[];   // DOWN_ROWS rows
+    if ((int)blockIdx.y >= active[0]) return;
+    const int e = active[1 + blockIdx.y], rb = blockIdx.x;
+    const int p0 = off[e], n = off[e + 1] - p0;
+    if (n == 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = rb * DOWN_ROWS;
+    const int nrows = min(DOWN_ROWS, g.H - r0);
+    {
+        const int4* src = reinterpret_cast<const int4*>(layer + (size_t)e * g.expert_bytes + 2 * g.t_gu +
+                                                        (size_t)r0 * g.row_d);
+        int4* d = reinterpret_cast<int4*>(smem);
+        const int n16 = (int)((size_t)nrows * g.row_d / 16);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) d[i] = __ldg(src + i);
+    }
+    __syncthreads();
+    const int nb = g.nbI;
+    const size_t abh = act_bytes(nb);
+    for (int q = 0; q < n; q++) {
+        const int p = list[p0 + q];
+        const ActView ha = act_view(hq + (size_t)p * abh, nb);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int lr = warp * 2 + rr;
+            if (lr >= nrows) break;
+            const uint8_t* row = smem + (size_t)lr * g.row_d;
+            float acc = 0.0f;
+            for (int b = lane; b < nb; b += 32) {
+                const XBlk xb = load_xblk(ha, b);
+                const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * b);
+                const float dw = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * (size_t)nb + 2 * b));
+                acc = __fadd_rn(acc, block_term(block_sumi(wv, xb), dw, xb.d));
+            }
+            const float yv = warp_sum_butterfly(acc);
+            if (lane == 0) y[(size_t)p * g.H + r0 + lr] = yv;
+        }
+    }
+}
+
+// grid T, 256 threads: x[t][r] = x[t][r] + (sum over slots j in order of w[t][j] * y[t*k+j][r])
+__global__ void __launch_bounds__(256) k_combine_batched(float* __restrict__ X, int H, int k,
+                                                         const float* __restrict__ wts, const float* __restrict__ y) {
+    const int t = blockIdx.x;
+    for (int r = threadIdx.x; r < H; r += blockDim.x) {
+        float a = 0.0f;
+        for (int j = 0; j < k; j++) a = __fadd_rn(a, __fmul_rn(wts[(size_t)t * k + j], y[((size_t)t * k + j) * H + r]));
+        X[(size_t)t * H + r] = __fadd_rn(X[(size_t)t * H + r], a);
+    }
+}
+
+}  // namespace
+
+size_t batched_smem_bytes(const Geom& g) {
+    size_t m = (size_t)2 * 32 * g.row_gu;
+    m = m > (size_t)DOWN_ROWS * g.row_d ? m : (size_t)DOWN_ROWS * g.row_d;
+    return m + 256;
+}
+
+size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
+    const size_t n_pairs = (size_t)T * k;
+    return (size_t)T * E * 8 + (size_t)(E + 1) * 4 + (size_t)T * act_bytes(g.nbH) + n_pairs * 8 + (E + 1) * 4 + n_pairs * 4 +
+           n_pairs * act_bytes(g.nbI) + n_pairs * g.H * 4 + (size_t)T * E * 4 + 8 * 256;
+}
+
+cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
+                               int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
+                               float* w_out, float* logits_out, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || batched_scratch_bytes(g, E, k, T) > scratch_bytes)
+        return cudaErrorInvalidValue;
+    const size_t n_pairs = (size_t)T * k;
+    uint8_t* p = static_cast<uint8_t*>(scratch);
+    auto take = [&](size_t n) {
+        uint8_t* r = p;
+        p += (n + 255) & ~(size_t)255;
+        return r;
+    };
+    unsigned long long* S = reinterpret_cast<unsigned long long*>(take((size_t)T * E * 8));
+    int* active = reinterpret_cast<int*>(take((E + 1) * 4));
+    uint8_t* xq = take((size_t)T * act_bytes(g.nbH));
+    int* idx = idx_out ? idx_out : reinterpret_cast<int*>(take(n_pairs * 4));
+    float* wts = w_out ? w_out : reinterpret_cast<float*>(take(n_pairs * 4));
+    int* off = reinterpret_cast<int*>(take((E + 1) * 4));
+    int* list = reinterpret_cast<int*>(take(n_pairs * 4));
+    uint8_t* hq = take(n_pairs * act_bytes(g.nbI));
+    float* y = reinterpret_cast<float*>(take(n_pairs * g.H * 4));
+
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
+    k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
+                                                                                                g.H, S);
+    k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, S, idx, wts, logits_out, xq);
+    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, E, off, list, active);
+    const int n_act = (int)(n_pairs < (size_t)E ? n_pairs : (size_t)E);
+    const size_t sm_gu = (size_t)2 * 32 * g.row_gu;
+    if (sm_gu > 48 * 1024 &&
+        (e = cudaFuncSetAttribute(k_gateup_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
+            cudaSuccess)
+        return e;
+    k_gateup_batched<<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, g, off, list, active, k, xq, hq);
+    const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
+    if (sm_d > 48 * 1024 &&
+        (e = cudaFuncSetAttribute(k_down_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_d)) !=
+            cudaSuccess)
+        return e;
+    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, g, off, list, active,
+                                                                                      hq, y);
+    k_combine_batched<<<T, 256, 0, s>>>(X, g.H, k, wts, y);
+    return cudaGetLastError();
+}
+
+}  // namespace tg

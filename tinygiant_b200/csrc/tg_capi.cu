@@ -352,6 +352,8 @@ struct tgx_ctx {
     unsigned* ctl = nullptr;            // epoch, finish count, error
     uint16_t* plan = nullptr;
     tg::FusedParams fp{};
+    void* bscratch = nullptr;           // batched path scratch, grown on demand
+    size_t bscratch_bytes = 0;
     cudaGraphExec_t fexec = nullptr;
     const float* fx = nullptr;
 };
@@ -377,7 +379,7 @@ void ctx_free(tgx_ctx* c) {
     for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->nscale, (void*)c->acc,
                     (void*)c->counter, (void*)c->logits,
                     (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging, (void*)c->RT,
-                    (void*)c->xw, (void*)c->xbuf, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
+                    (void*)c->xw, (void*)c->xbuf, (void*)c->bscratch, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -656,6 +658,49 @@ extern "C" int tgx_moe_layer(tgx_ctx* ctx, int layer, float* x_dev, void* stream
     DeviceGuard dg(ctx->device);
     if (ctx->fused_ok) return fused_launch(ctx, layer, 1, x_dev, (cudaStream_t)stream);
     return moe_layer_launch(ctx, layer, x_dev, (cudaStream_t)stream);
+}
+
+namespace {
+// Run MoE blocks [l0, l1) for T tokens on x_dev[T][embed] with the batched kernels.
+int batched_run(tgx_ctx* ctx, int l0, int l1, float* x_dev, int T, cudaStream_t s, const char* fn) {
+    const tgx_shape& sh = ctx->shape;
+    TG_CHECK(T >= 1 && T <= 65536 / sh.top_k, TG_EINVAL, std::string(fn) + ": T must be in [1, 65536/top_k]");
+    int optin = 0;
+    TG_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device));
+    TG_CHECK(tg::batched_smem_bytes(ctx->g) <= (size_t)optin, TG_EUNSUPPORTED,
+             std::string(fn) + ": shape needs more shared memory per block than the device has");
+    const size_t need = tg::batched_scratch_bytes(ctx->g, sh.n_experts, sh.top_k, T);
+    if (need > ctx->bscratch_bytes) {
+        TG_CUDA(cudaStreamSynchronize(s));
+        if (ctx->bscratch) cudaFree(ctx->bscratch);
+        ctx->bscratch = nullptr;
+        ctx->bscratch_bytes = 0;
+        if (cudaMalloc(&ctx->bscratch, need) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(TG_ENOMEM, std::string(fn) + ": cudaMalloc of " + std::to_string(need) + " bytes failed");
+        }
+        ctx->bscratch_bytes = need;
+    }
+    const size_t n = (size_t)sh.n_experts * sh.embed;
+    for (int l = l0; l < l1; l++)
+        TG_CUDA(tg::launch_moe_batched(ctx->weights + (size_t)l * ctx->layer_bytes, ctx->g, ctx->routers + (size_t)l * n,
+                                       ctx->norms + (size_t)l * sh.embed, ctx->eps, sh.n_experts, sh.top_k, x_dev, T,
+                                       ctx->bscratch, ctx->bscratch_bytes, nullptr, nullptr, nullptr, s));
+    return TG_OK;
+}
+}  // namespace
+
+extern "C" int tgx_moe_batched(tgx_ctx* ctx, int layer, float* x_dev, int T, void* stream) {
+    TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_moe_batched: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_moe_batched: layer out of range");
+    DeviceGuard dg(ctx->device);
+    return batched_run(ctx, layer, layer + 1, x_dev, T, (cudaStream_t)stream, "tgx_moe_batched");
+}
+
+extern "C" int tgx_decode_batched(tgx_ctx* ctx, float* x_dev, int T, void* stream) {
+    TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_decode_batched: null argument");
+    DeviceGuard dg(ctx->device);
+    return batched_run(ctx, 0, ctx->shape.n_layers, x_dev, T, (cudaStream_t)stream, "tgx_decode_batched");
 }
 
 extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int flags) {

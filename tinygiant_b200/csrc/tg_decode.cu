@@ -193,15 +193,6 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
     return y;
 }
 
-__device__ __forceinline__ XBlk load_xblk_s(const ActView& a, int b) {
-    XBlk x;
-    const int4* q = reinterpret_cast<const int4*>(a.qs + (size_t)b * 32);
-    x.lo = q[0];
-    x.hi = q[1];
-    x.d = a.d[b];
-    x.s8 = a.s8[b];
-    return x;
-}
 
 
 // Gather the h records of slots [jlo, jlo + nwords / (6 * nbI)) of one layer (six
@@ -286,7 +277,7 @@ __device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* h
                     const int j = j0 + jj;
                     if (j < jhi) {
                         const uint8_t* row = dbase + (size_t)j * d_chunk + (size_t)q0 * row_d;
-                        const XBlk xb = load_xblk_s(act_view(hq_base + (size_t)j * ab_i, nbI), b);
+                        const XBlk xb = load_xblk(act_view(hq_base + (size_t)j * ab_i, nbI), b);
                         const uint4 w0 = *reinterpret_cast<const uint4*>(row + 16 * b);
                         const float dw0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * nbI + 2 * b));
                         acc0[jj] = __fadd_rn(acc0[jj], block_term(block_sumi(w0, xb), dw0, xb.d));
@@ -706,8 +697,8 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         const bool xreg = nbH <= 64;
         XBlk xr0 = {}, xr1 = {};
         if (xreg && warp < CW) {
-            if (lane < nbH) xr0 = load_xblk_s(xq, lane);
-            if (lane + 32 < nbH) xr1 = load_xblk_s(xq, lane + 32);
+            if (lane < nbH) xr0 = load_xblk(xq, lane);
+            if (lane + 32 < nbH) xr1 = load_xblk(xq, lane + 32);
         }
         for (int u = 0; u < n_gu; u++) {
             const bool ok = wait_bar(mbar_gu + u, (unsigned)l & 1u, 3);
@@ -735,7 +726,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
 #pragma unroll 1
                 for (int it = 0; lane + 32 * it < nbH; it++) {
                     const int b = lane + 32 * it;
-                    const XBlk xb = (xreg && it < 2) ? (it ? xr1 : xr0) : load_xblk_s(xq, b);
+                    const XBlk xb = (xreg && it < 2) ? (it ? xr1 : xr0) : load_xblk(xq, b);
                     const uint4 wg0 = *reinterpret_cast<const uint4*>(rg0 + 16 * b);
                     const uint4 wg1 = *reinterpret_cast<const uint4*>(rg1 + 16 * b);
                     const uint4 wu0 = *reinterpret_cast<const uint4*>(ru0 + 16 * b);

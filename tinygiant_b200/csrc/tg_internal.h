@@ -69,6 +69,17 @@ cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cu
 // Raise dynamic shared-memory limits for the shapes a context uses (call before capture).
 cudaError_t prepare_kernels(Geom g, int k);
 
+// The MoE block for T tokens at once, in place on X[T][H] (tg_batched.cu).  layer:
+// the layer's row-split experts; R: its router [E][H]; scratch of at
+// least batched_scratch_bytes(g, E, k, T); idx_out / w_out / logits_out optional
+// ([T][k], [T][k], [T][E]).  batched_smem_bytes: the largest dynamic shared memory
+// a CTA of the path needs.
+size_t batched_scratch_bytes(const Geom& g, int E, int k, int T);
+size_t batched_smem_bytes(const Geom& g);
+cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
+                               int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
+                               float* w_out, float* logits_out, cudaStream_t s);
+
 // Record msg as the calling thread's tg_last_error() text; returns code.
 int set_error(int code, const char* msg);
 

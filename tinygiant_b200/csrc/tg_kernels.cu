@@ -33,35 +33,6 @@ __device__ __forceinline__ uint16_t ldg_nc_u16(const void* p) {
     return v;
 }
 
-__device__ __forceinline__ XBlk load_xblk(const ActView& a, int b) {
-    XBlk x;
-    const int4* q = reinterpret_cast<const int4*>(a.qs + (size_t)b * 32);
-    x.lo = q[0];
-    x.hi = q[1];
-    x.d = a.d[b];
-    x.s8 = a.s8[b];
-    return x;
-}
-
-// Quantise one 32-value block held one value per lane (lane = position).
-// Returns the code; lane 0 also gets the fp16 scale bits and 8*sum.
-struct Q8Lane { int q; uint16_t dh; int s8; };
-__device__ __forceinline__ Q8Lane quantize_lane(float v) {
-    __syncwarp();
-    float am = absmax_lane(v);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-    Q8Scale sc = q8_scale(am);
-    Q8Lane r;
-    r.q = q8_round(v, sc.id);
-    int s = r.q;
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-    r.dh = sc.dh;
-    r.s8 = 8 * s;
-    return r;
-}
-
 // Quantise f32 x[0 .. 32*nb) into an activation view, one warp per block.  With
 // a norm (scale != null) the quantised values are (x * scale) * normw.
 __device__ __forceinline__ void quantize_to_act(const float* __restrict__ x, int nb, ActView a,
@@ -317,41 +288,6 @@ cudaError_t launch_block_dots(const uint8_t* W, ActView x, int32_t* out, int row
 
 constexpr int ROUTER_HCHUNK = 256;
 constexpr int MAX_EXPERTS = 1024;
-constexpr int MAX_TOPK = 16;
-
-// Top-k by rank: element i is selected when fewer than k elements beat it
-// (larger logit, or equal logit and larger id); its ascending position is k-1-rank.
-__device__ void topk_softmax_block(const float* sl, int E, int k, int* sidx, float* sw) {
-    for (int i = threadIdx.x; i < E; i += blockDim.x) {
-        float li = sl[i];
-        int rank = 0;
-        for (int j = 0; j < E; j++) {
-            float lj = sl[j];
-            rank += (lj > li) || (lj == li && j > i);
-        }
-        if (rank < k) sidx[k - 1 - rank] = i;
-    }
-    __syncwarp();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float m = sl[sidx[k - 1]];
-        float ex[MAX_TOPK];
-        for (int j = 0; j < k; j++) ex[j] = tg_expf(__fsub_rn(sl[sidx[j]], m));
-        float s;
-        if (k <= 8) {
-            float t[8];
-            for (int j = 0; j < 8; j++) t[j] = j < k ? ex[j] : 0.0f;
-            s = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[1]), __fadd_rn(t[2], t[3])),
-                          __fadd_rn(__fadd_rn(t[4], t[5]), __fadd_rn(t[6], t[7])));
-        } else {
-            s = 0.0f;
-            for (int j = 0; j < k; j++) s = __fadd_rn(s, ex[j]);
-        }
-        for (int j = 0; j < k; j++) sw[j] = __fdiv_rn(ex[j], s);
-    }
-    __syncwarp();
-    __syncthreads();
-}
 
 // Routing of the normed hidden state (engine.py:229-236): warps 0..E-1 add
 // fixed-point partial sums of R[e] . (x * normw) over a 256-column chunk into

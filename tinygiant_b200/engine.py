@@ -102,6 +102,17 @@ class MoEModel:
         flags = (TGX_EAGER if eager else 0) | (TGX_MULTI if multi else 0)
         check(self.lib.tgx_decode_step(self._ctx, _dev_ptr(x), _stream_handle(stream), flags), self.lib)
 
+    def moe_batched(self, layer: int, X, stream=None):
+        """MoE block `layer` for T tokens at once on X (cuda f32[T][embed]) in place;
+        each row gets exactly what moe_layer gives it."""
+        assert X.dim() == 2 and X.shape[1] == self.embed
+        check(self.lib.tgx_moe_batched(self._ctx, layer, _dev_ptr(X), X.shape[0], _stream_handle(stream)), self.lib)
+
+    def decode_batched(self, X, stream=None):
+        """All layers chained for T tokens on X (cuda f32[T][embed]) in place."""
+        assert X.dim() == 2 and X.shape[1] == self.embed
+        check(self.lib.tgx_decode_batched(self._ctx, _dev_ptr(X), X.shape[0], _stream_handle(stream)), self.lib)
+
     def sync_status(self):
         """Synchronise; raise if a bounded wait inside the fused kernel expired."""
         check(self.lib.tgx_sync_status(self._ctx), self.lib)
