@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--multi", action="store_true", help="three kernels per layer instead of the fused kernel")
     ap.add_argument("--layers", type=int, default=L, help="fewer layers, for small profiling cases only")
     ap.add_argument("--tokens", type=int, default=1, help="T > 1: T tokens per step through the batched path")
+    ap.add_argument("--tier", type=int, default=-1,
+                    help="P >= 0: host tier with P experts per layer pinned in HBM, Zipf(1.1) routing (configs[3])")
+    ap.add_argument("--cache-slots", type=int, default=24, help="HBM cache slots of the host tier")
     return ap.parse_args()
 
 
@@ -423,10 +426,92 @@ def run_batched(args):
     return 0
 
 
+def zipf_routes(n_steps, n_layers, E, k, s, seed):
+    """Per layer a seeded permutation of the experts ranked by Zipf(s); per step and
+    layer k distinct experts drawn with probability ~ rank^-s.  Returns ids[step][layer][k]
+    and the permutations (most popular first)."""
+    rng = np.random.default_rng(seed)
+    perms = [rng.permutation(E) for _ in range(n_layers)]
+    p = 1.0 / np.arange(1, E + 1) ** s
+    p /= p.sum()
+    ids = np.empty((n_steps, n_layers, k), np.int64)
+    for t in range(n_steps):
+        for l in range(n_layers):
+            ids[t, l] = perms[l][rng.choice(E, size=k, replace=False, p=p)]
+    return ids, perms
+
+
+def run_tier(args):
+    """P experts per layer pinned in HBM, the rest copied on demand from a
+    pinned host copy of the relayout bytes into HBM cache slots on a side stream, the
+    next layer's misses prefetched while the current layer computes."""
+    import ctypes
+    import torch
+    from tinygiant_b200.cache import HostTierCache
+    from tinygiant_b200.engine import MoEModel
+    torch.cuda.set_device(0)
+    NL, P = args.layers, args.tier
+    model = MoEModel(H, I, E, K_TOP, NL)
+    model.fill_synthetic(args.seed)
+    host = []
+    for l in range(NL):   # the relayout bytes of each layer in pinned host memory
+        t = torch.empty(E * EXPERT_BYTES, dtype=torch.uint8, pin_memory=True)
+        r = model.lib.tgx_read_experts(model.handle, l, 0, E, ctypes.c_void_p(t.data_ptr()))
+        assert r == 0
+        host.append(t)
+    K, W = args.steps, max(3, args.warmup)
+    ids, perms = zipf_routes(K + W, NL, E, K_TOP, 1.1, args.seed + 1)
+    cache = HostTierCache(model, host, cache_slots=args.cache_slots)
+    for l in range(NL):
+        cache.pin(l, perms[l][:P])
+    w = np.full(K_TOP, 1.0 / K_TOP, np.float32)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    X = torch.randn(K + W, H, generator=gen, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def token(i):
+        x = X[i]
+        for l in range(NL):
+            nl, ni = (l + 1, i) if l + 1 < NL else (0, i + 1)
+            if ni < K + W:
+                cache.prefetch(nl, ids[ni, nl])
+            cache.forward(l, ids[i, l], w, x, stream)
+
+    for i in range(W):
+        token(i)
+    torch.cuda.synchronize()
+    h0, m0, b0 = cache.hits, cache.misses, cache.bytes_h2d
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    t0 = time.perf_counter()
+    for i in range(W, W + K):
+        token(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = ev0.elapsed_time(ev1)
+    hits, misses, nbytes = cache.hits - h0, cache.misses - m0, cache.bytes_h2d - b0
+    model.close()
+    print(json.dumps({
+        "metric": f"host-tier expert decode tok/s (Qwen3-30B-A3B shape, {P} experts per layer pinned in HBM)",
+        "value": K / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"configs[3]: {NL} layers, top-{K_TOP} by Zipf(1.1) routing, {P} pinned per layer, "
+                               f"{args.cache_slots} HBM cache slots, relayout bytes in pinned host memory",
+                   "layers": NL, "pinned_per_layer": P, "cache_slots": args.cache_slots},
+        "hit_rate": hits / max(1, hits + misses), "misses_per_token": misses / K,
+        "h2d_gbs": nbytes / (ms / 1000.0) / 1e9, "wall_tok_s": K / wall,
+    }), flush=True)
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.tier >= 0:
+        return run_tier(args)
     if args.tokens > 1:
         return run_batched(args)
     return run_ours(args)

@@ -165,6 +165,18 @@ int tgx_moe_batched(tgx_ctx *ctx, int layer, float *x_dev, int T, void *stream);
 /* All L MoE blocks for T tokens, layer after layer (tgx_moe_batched for l = 0 .. L-1). */
 int tgx_decode_batched(tgx_ctx *ctx, float *x_dev, int T, void *stream);
 
+/* The MoE block of layer `layer` over a given list of experts (routing decided by the
+ * caller, e.g. a host-tier cache): x += sum_j weights[j] * expert_j((x * scale) * ffn_norm),
+ * scale the layer's RMSNorm scale of x.  experts: host array of n DEVICE pointers to
+ * expert blobs in the library's row-split layout (tgx_repack_experts); weights: host
+ * array of n floats; 1 <= n <= 16.  The expert-forward order of engine.py:238-258. */
+int tgx_experts_forward(tgx_ctx *ctx, int layer, const void *const *experts, const float *weights, int n,
+                        float *x_dev, void *stream);
+
+/* Convert n ggml expert blobs (relayout order, device memory) into the row-split
+ * layout the kernels read; raw_dev and dst_dev must not overlap. */
+int tgx_repack_experts(tgx_ctx *ctx, const void *raw_dev, void *dst_dev, int n, void *stream);
+
 /* Synchronise the context's device and report whether a bounded wait inside the
  * fused decode kernel expired since the last call (TG_ETIMEOUT; the kernel's
  * cross-block state is then reset).  TG_OK otherwise. */

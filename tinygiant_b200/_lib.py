@@ -78,6 +78,8 @@ PROTOTYPES = {
     "tgx_decode_step": (CI, [VP, VP, VP, CI]),
     "tgx_moe_batched": (CI, [VP, CI, VP, CI, VP]),
     "tgx_decode_batched": (CI, [VP, VP, CI, VP]),
+    "tgx_experts_forward": (CI, [VP, CI, VP, VP, CI, VP, VP]),
+    "tgx_repack_experts": (CI, [VP, VP, VP, CI, VP]),
     "tgx_sync_status": (CI, [VP]),
     "tgx_fused_info": (CI, [VP, VP, VP, VP]),
     "tgx_fused_debug": (CI, [VP, VP, VP, SZ]),

@@ -354,6 +354,11 @@ struct tgx_ctx {
     tg::FusedParams fp{};
     void* bscratch = nullptr;           // batched path scratch, grown on demand
     size_t bscratch_bytes = 0;
+    // tgx_experts_forward: up to 16 expert pointers and weights, their h blocks, the norm scale
+    const uint8_t** lptrs = nullptr;
+    float* lwts = nullptr;
+    uint8_t* lhq = nullptr;
+    float* lscale = nullptr;
     cudaGraphExec_t fexec = nullptr;
     const float* fx = nullptr;
 };
@@ -379,7 +384,8 @@ void ctx_free(tgx_ctx* c) {
     for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->nscale, (void*)c->acc,
                     (void*)c->counter, (void*)c->logits,
                     (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging, (void*)c->RT,
-                    (void*)c->xw, (void*)c->xbuf, (void*)c->bscratch, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
+                    (void*)c->xw, (void*)c->xbuf, (void*)c->bscratch, (void*)c->lptrs, (void*)c->lwts,
+                    (void*)c->lhq, (void*)c->lscale, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -701,6 +707,46 @@ extern "C" int tgx_decode_batched(tgx_ctx* ctx, float* x_dev, int T, void* strea
     TG_CHECK(ctx && x_dev, TG_EINVAL, "tgx_decode_batched: null argument");
     DeviceGuard dg(ctx->device);
     return batched_run(ctx, 0, ctx->shape.n_layers, x_dev, T, (cudaStream_t)stream, "tgx_decode_batched");
+}
+
+extern "C" int tgx_experts_forward(tgx_ctx* ctx, int layer, const void* const* experts, const float* weights, int n,
+                                   float* x_dev, void* stream) {
+    TG_CHECK(ctx && experts && weights && x_dev, TG_EINVAL, "tgx_experts_forward: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers, TG_EINVAL, "tgx_experts_forward: layer out of range");
+    TG_CHECK(n >= 1 && n <= 16, TG_EINVAL, "tgx_experts_forward: n must be in [1, 16]");
+    for (int j = 0; j < n; j++) TG_CHECK(experts[j], TG_EINVAL, "tgx_experts_forward: null expert pointer");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    if (!ctx->lptrs) {
+        if (cudaMalloc((void**)&ctx->lptrs, 16 * sizeof(void*)) != cudaSuccess ||
+            cudaMalloc((void**)&ctx->lwts, 16 * sizeof(float)) != cudaSuccess ||
+            cudaMalloc((void**)&ctx->lhq, 16 * tg::act_bytes(g.nbI)) != cudaSuccess ||
+            cudaMalloc((void**)&ctx->lscale, sizeof(float)) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(TG_ENOMEM, "tgx_experts_forward: cudaMalloc of its small buffers failed");
+        }
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    // pageable sources: the copies are staged before the calls return, so the
+    // caller's arrays may be reused at once
+    TG_CUDA(cudaMemcpyAsync(ctx->lptrs, experts, n * sizeof(void*), cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(ctx->lwts, weights, n * sizeof(float), cudaMemcpyHostToDevice, s));
+    const float* nw = ctx->norms + (size_t)layer * g.H;
+    TG_CUDA(tg::prepare_kernels(g, n));
+    TG_CUDA(tg::launch_rms_scale(x_dev, g.H, ctx->eps, ctx->lscale, s));
+    TG_CUDA(tg::launch_gateup(ctx->lptrs, n, x_dev, nw, ctx->lscale, g, ctx->lhq, nullptr, nullptr, s));
+    TG_CUDA(tg::launch_down_combine(ctx->lptrs, n, ctx->lhq, ctx->lwts, 0.0f, g, x_dev, x_dev, 0, nullptr, s));
+    return TG_OK;
+}
+
+extern "C" int tgx_repack_experts(tgx_ctx* ctx, const void* raw_dev, void* dst_dev, int n, void* stream) {
+    TG_CHECK(ctx && raw_dev && dst_dev && n >= 0, TG_EINVAL, "tgx_repack_experts: bad arguments");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    for (int e = 0; e < n; e++)
+        TG_CUDA(repack_expert((const uint8_t*)raw_dev + (size_t)e * g.expert_bytes, (uint8_t*)dst_dev + (size_t)e * g.expert_bytes,
+                              g, (cudaStream_t)stream));
+    return TG_OK;
 }
 
 extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int flags) {

@@ -66,6 +66,9 @@ cudaError_t launch_fill_experts_q4_0(uint8_t* dst, int n_experts, Geom g, unsign
 // out[c][r] = in[r][c] (fp32, rows x cols -> cols x rows).
 cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cudaStream_t s);
 
+// *scale = RMSNorm scale of x[H] (exact fixed-point sum of squares), one CTA.
+cudaError_t launch_rms_scale(const float* x, int H, float eps, float* scale, cudaStream_t s);
+
 // Raise dynamic shared-memory limits for the shapes a context uses (call before capture).
 cudaError_t prepare_kernels(Geom g, int k);
 

@@ -545,6 +545,30 @@ cudaError_t launch_down_combine(const uint8_t* const* experts, int k, const uint
     return cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ RMSNorm scale
+
+// one CTA of 256 threads: *scale = 1/sqrt(sum x^2 / H + eps) with the exact
+// fixed-point sum of the routing kernel (csrc/libtinygiant.c:322-340)
+__global__ void __launch_bounds__(256) k_rms_scale(const float* __restrict__ x, int H, float eps,
+                                                   float* __restrict__ scale) {
+    __shared__ long long ws[8];
+    long long s = 0;
+    for (int r = threadIdx.x; r < H; r += blockDim.x) s += ss_fixed(x[r]);
+    s = warp_sum_i64(s);
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        long long t = 0;
+        for (int w = 0; w < 8; w++) t += ws[w];
+        *scale = rms_scale_from(t, H, eps);
+    }
+}
+
+cudaError_t launch_rms_scale(const float* x, int H, float eps, float* scale, cudaStream_t s) {
+    k_rms_scale<<<1, 256, 0, s>>>(x, H, eps, scale);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ synthetic data
 
 __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
