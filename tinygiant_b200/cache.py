@@ -48,6 +48,7 @@ class HostTierCache:
         self.pinned = {}                        # (layer, expert) -> device tensor (row-split)
         self.hits = self.misses = self.pinned_hits = 0
         self.bytes_h2d = 0
+        self.prefetched = set()   # loaded by prefetch, not yet requested: a miss when requested
 
     # ------------------------------------------------------------ pinning
     def pin(self, layer: int, ids):
@@ -77,6 +78,7 @@ class HostTierCache:
             if victim is None:
                 raise RuntimeError("HostTierCache: every slot is needed by the current request; add cache_slots")
             slot = self.lru.pop(victim)
+            self.prefetched.discard(victim)
         layer, e = key
         cs = self.copy_stream
         cs.wait_event(self.used[slot])          # no kernel still reads the old contents
@@ -99,6 +101,7 @@ class HostTierCache:
         for key in keys:
             if key not in self.pinned and key not in self.lru:
                 self._load(key, protect)
+                self.prefetched.add(key)
 
     def resident(self, layer: int, ids, count: bool = True):
         """Device pointers of experts `ids` (loading misses); hits/misses are counted."""
@@ -112,7 +115,11 @@ class HostTierCache:
                 ptrs.append(self.pinned[key].data_ptr())
                 continue
             if key in self.lru:
-                self.hits += count
+                if key in self.prefetched:    # a miss whose copy the prefetch already started
+                    self.prefetched.discard(key)
+                    self.misses += count
+                else:
+                    self.hits += count
                 self.lru.move_to_end(key)
                 slot = self.lru[key]
             else:
