@@ -71,11 +71,43 @@ int tg_expert_forward_q4_0(const uint8_t *q4_data, const float *input, float *ou
                            int embed_dim, int inter_dim);
 
 /* csrc/libtinygiant.c:599-643 with separate gate/up/down pointers (the symbol the
- * reference engine calls, tinygiant/engine.py:249-257).  Supported down_format:
- * TG_FMT_Q4_0; the others return TG_EUNSUPPORTED. */
+ * reference engine calls, tinygiant/engine.py:249-257; bound at tinygiant/_lib.py:40-41).
+ * down_format TG_FMT_Q4_K / TG_FMT_F16 / TG_FMT_Q6_K: Q4_K gate and up, down in that
+ * format, the reference's formats and float order (see below); TG_FMT_Q4_0: all three
+ * matrices Q4_0, this library's decode format.  Other codes return TG_EINVAL. */
 int tg_expert_forward_mixed(const uint8_t *gate_q4, const uint8_t *up_q4, const void *down_data,
                             int down_format, const float *input, float *output, float weight,
                             int embed_dim, int inter_dim);
+
+/* ---- the reference library's own formats (csrc/libtinygiant.c) ----
+ * Q4_K: 144-byte super-blocks of 256 values (fp16 d, fp16 dmin, 12 bytes of 6-bit
+ * sub-block scales and mins, 128 bytes of nibbles); Q6_K: 210-byte super-blocks (ql,
+ * qh, int8 scales, fp16 d); activations of Q4_K / Q6_K products are quantised to
+ * 256-wide Q8 blocks (scale = amax/127, round-half-even codes).  Float operations
+ * follow the reference source in order, each rounded separately (no contraction);
+ * results are bit-identical to oracle/tg_ref.c.  Row lengths: multiples of 256 for
+ * Q4_K / Q6_K (<= 65536), of 8 for f16 / f32 (<= 32768). */
+
+/* output[r] = row_r . Q8(input), csrc/libtinygiant.c:173-190 (_lib.py:42). */
+int tg_matmul_q4k(const uint8_t *q4_matrix, const float *input, float *output, int nrows, int ncols);
+/* Q6_K rows, csrc/libtinygiant.c:194-273 (_lib.py:43). */
+int tg_matmul_q6k(const uint8_t *q6_matrix, const float *input, float *output, int nrows, int ncols);
+/* f16 rows on the unquantised input, csrc/libtinygiant.c:262-296 (_lib.py:46): eight
+ * running fused sums (columns v, v + 8, ...) folded (v, v + 4) then pairwise. */
+int tg_f16_matvec(const uint16_t *A, const float *x, float *out, int nrows, int ncols);
+/* f32 rows, csrc/libtinygiant.c:298-318 (_lib.py:45), same order as tg_f16_matvec. */
+int tg_f32_matvec(const float *A, const float *x, float *out, int nrows, int ncols);
+/* out = x * scale * weight, scale = 1/sqrtf(sum x^2 / dim + eps) with the sum as four
+ * fused chains folded pairwise, csrc/libtinygiant.c:322-340 (_lib.py:44); dim % 4 == 0. */
+int tg_rms_norm(const float *x, const float *weight, float *out, int dim, float eps);
+/* output += weight * expert(input) of one all-Q4_K blob gate | up | down,
+ * csrc/libtinygiant.c:555-595 (_lib.py:39). */
+int tg_expert_forward(const uint8_t *q4_data, const float *input, float *output, float weight,
+                      int embed_dim, int inter_dim);
+/* output = sum_e weights[e] * expert_e(input), from zero, experts in order (1..64 Q4_K
+ * blobs), csrc/libtinygiant.c:647-655 (exported, not bound by the reference's Python). */
+int tg_moe_forward(const uint8_t **expert_ptrs, const float *weights, int n_experts, const float *input,
+                   float *output, int embed_dim, int inter_dim);
 
 /* output = sum_e weights[e] * expert_e(input), accumulated in e order from zero.
  * Q4_0 twin of tg_moe_forward, csrc/libtinygiant.c:647-655. */
@@ -205,6 +237,28 @@ int tgx_fused_info(tgx_ctx *ctx, int *ctas, int *smem_bytes, int *arena_bytes);
  * (idx[k] in ascending-logit order, w[k], logits[E]); any pointer may be NULL.
  * Synchronises the context's device. */
 int tgx_last_routing(tgx_ctx *ctx, int layer, int32_t *idx, float *w, float *logits);
+
+/* ===================== the reference's formats on device pointers ===================== */
+
+/* Device bytes of a rows x cols matrix of format fmt (0 Q4_K, 1 f16, 2 Q6_K, 4 f32;
+ * the same as the reference's byte size), or 0 for a shape the kernels do not take. */
+size_t tgx_kq_matrix_bytes(int fmt, long long rows, int cols);
+/* Convert a matrix in the reference's byte layout (src_dev) into the kernels' device
+ * layout (dst_dev, same size, 16-byte aligned, not aliasing src): Q6_K blocks are
+ * split into 208-byte bodies followed by the fp16 d of every block; the other formats
+ * are copied unchanged. */
+int tgx_kq_prepare(int fmt, const void *src_dev, void *dst_dev, long long rows, int cols, void *stream);
+/* y_dev[rows] = W . x (tg_matmul_q4k / tg_matmul_q6k / tg_f16_matvec / tg_f32_matvec on
+ * device memory; W in device layout, all pointers 16-byte aligned). */
+int tgx_kq_matvec(int fmt, const void *W_dev, const float *x_dev, float *y_dev, int rows, int cols, void *stream);
+/* n experts at once (tg_moe_forward / tg_expert_forward_mixed on device memory):
+ * out = (accumulate ? out : 0) + sum_e w[e] * down_e(silu(gate_e . x) * (up_e . x)),
+ * experts in order.  gate_dev / up_dev / down_dev: DEVICE arrays of n device pointers
+ * (Q4_K gate and up; down in down_format 0 / 1 / 2, device layout); w_dev: n floats;
+ * h_dev: scratch of n * inter floats.  Allocates nothing; enqueued on stream. */
+int tgx_kq_experts_forward(const void *const *gate_dev, const void *const *up_dev, const void *const *down_dev,
+                           int down_format, int n, const float *w_dev, const float *x_dev, float *out_dev,
+                           int embed, int inter, int accumulate, float *h_dev, void *stream);
 
 #ifdef __cplusplus
 }

@@ -68,6 +68,10 @@ def lib():
         "ref_decode_step_mt": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, CI]),
         "ref_moe_layer_batched": (None, [VP, ctypes.c_size_t, VP, VP, CI, CI, CI, CI, CI, CI, CI]),
         "ref_moe_block_batched": (None, [VP, ctypes.c_size_t, VP, VP, CF, VP, CI, CI, CI, CI, CI, CI, CI]),
+        "ref_quantize_q8k": (None, [VP, VP, ctypes.c_int64]),
+        "ref_matvec_k": (None, [VP, CI, VP, VP, CI, CI]),
+        "ref_rms_norm_k": (None, [VP, VP, VP, CI, CF]),
+        "ref_expert_forward_k": (None, [VP, VP, VP, CI, VP, VP, CF, CI, CI, CI]),
         "ref_fill_normal": (None, [VP, I64, ctypes.c_uint64, CF]),
     }
     for name, (res, args) in sig.items():
@@ -265,6 +269,47 @@ def moe_block_batched(layer_blob, R, x, k, embed, inter, normw=None, eps: float 
                                 _p(np.ascontiguousarray(R, dtype=np.float32)), None if nw is None else _p(nw), eps,
                                 _p(x), T, R.shape[0], k, embed, inter, mode, n_threads)
     return x
+
+
+# ---------------------------------------------------------------- the reference's K-quant path
+
+Q4K_BYTES, Q6K_BYTES, Q8K_BYTES = 144, 210, 264
+FMT_Q4_K, FMT_F16, FMT_Q6_K, FMT_F32 = 0, 1, 2, 4
+
+
+def quantize_q8k(x) -> np.ndarray:
+    """The reference's 256-wide Q8 activation blocks (libtinygiant.c:55-89): per block
+    fp32 scale, int32 sum of codes, 256 int8 codes; 264 bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.size // 256 * Q8K_BYTES, np.uint8)
+    lib().ref_quantize_q8k(_p(x), _p(out), x.size)
+    return out
+
+
+def matvec_k(W, fmt, x, rows, cols) -> np.ndarray:
+    """y = W . x with W in Q4_K (fmt 0, on Q8(256) of x), f16 (1), Q6_K (2) or f32 (4)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(rows, np.float32)
+    lib().ref_matvec_k(_p(np.ascontiguousarray(W)), fmt, _p(x), _p(y), rows, cols)
+    return y
+
+
+def rms_norm_k(x, w, eps):
+    """tg_rms_norm in the reference's order (libtinygiant.c:322-340)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out = np.empty_like(x)
+    lib().ref_rms_norm_k(_p(x), _p(w), _p(out), x.size, float(eps))
+    return out
+
+
+def expert_forward_k(gate, up, down, down_format, x, out, w, embed, inter, mode=TG_MIRROR):
+    """tg_expert_forward_mixed (libtinygiant.c:599-643): out += w * expert(x), in place."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    lib().ref_expert_forward_k(_p(np.ascontiguousarray(gate)), _p(np.ascontiguousarray(up)),
+                               _p(np.ascontiguousarray(down)), down_format, _p(x), _p(out), float(w),
+                               embed, inter, mode)
+    return out
 
 
 def fill_normal(n: int, seed: int, sigma: float) -> np.ndarray:

@@ -541,6 +541,191 @@ void ref_moe_layer_batched(const uint8_t *layer_blob, size_t expert_bytes, const
                       embed, inter, mode, NULL, NULL, NULL);
 }
 
+/* ------------------------------------------------------------------ the reference's K-quant path
+ *
+ * The shipped library's own formats (csrc/libtinygiant.c): Q4_K super-blocks of 256
+ * values (144 B: fp16 d, fp16 dmin, 12 B of 6-bit sub-block scales/mins, 128 B of
+ * nibbles), Q6_K (210 B), f16 rows, and 256-wide Q8 activation blocks {fp32 scale,
+ * int32 sum, int8 qs[256]}.  Float work follows the reference's order statement by
+ * statement (one block after another, C left-to-right, no contraction); integer dots
+ * are exact. */
+
+enum { REF_QKK = 256, REF_Q4K_BYTES = 144, REF_Q6K_BYTES = 210, REF_Q8K_BYTES = 264 };
+
+/* libtinygiant.c:42-51 */
+static void get_scale_min_k4(int j, const uint8_t *q, uint8_t *sc, uint8_t *m) {
+    if (j < 4) {
+        *sc = q[j] & 63;
+        *m = q[j + 4] & 63;
+    } else {
+        *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+/* libtinygiant.c:61-89: per 256 values amax, scale = amax/127, codes = round-half-even of
+ * x * (127/amax) (vcvtnq_s32_f32), sum of codes.  Output: n/256 blocks of 264 bytes. */
+void ref_quantize_q8k(const float *x, uint8_t *out, int64_t n) {
+    for (int64_t b = 0; b < n / REF_QKK; b++) {
+        const float *xb = x + b * REF_QKK;
+        float amax = 0.0f;
+        for (int i = 0; i < REF_QKK; i++) {
+            float a = fabsf(xb[i]);
+            if (a > amax) amax = a;
+        }
+        float sc = amax / 127.f;
+        float inv = amax > 0 ? 127.f / amax : 0;
+        uint8_t *o = out + b * REF_Q8K_BYTES;
+        int32_t sum = 0;
+        int8_t *qs = (int8_t *)(o + 8);
+        for (int i = 0; i < REF_QKK; i++) {
+            int32_t q = (int32_t)lrintf(xb[i] * inv);   /* round half to even */
+            qs[i] = (int8_t)q;
+            sum += q;
+        }
+        memcpy(o, &sc, 4);
+        memcpy(o + 4, &sum, 4);
+    }
+}
+
+/* Q4_K row dot, libtinygiant.c:104-169 */
+float ref_dot_q4k(const uint8_t *q4, const uint8_t *xq, int bpr) {
+    float total = 0;
+    for (int b = 0; b < bpr; b++) {
+        const uint8_t *bl = q4 + (size_t)b * REF_Q4K_BYTES;
+        uint16_t dr, dmr;
+        memcpy(&dr, bl, 2);
+        memcpy(&dmr, bl + 2, 2);
+        float d = ref_f16_to_f32(dr), dmin = ref_f16_to_f32(dmr);
+        const uint8_t *scales = bl + 4, *qs = bl + 16;
+        const uint8_t *xb = xq + (size_t)b * REF_Q8K_BYTES;
+        float sx;
+        memcpy(&sx, xb, 4);
+        const int8_t *xqs = (const int8_t *)(xb + 8);
+        float block_sum = 0;
+        for (int g = 0; g < 4; g++) {
+            uint8_t sc_lo, m_lo, sc_hi, m_hi;
+            get_scale_min_k4(2 * g, scales, &sc_lo, &m_lo);
+            get_scale_min_k4(2 * g + 1, scales, &sc_hi, &m_hi);
+            int32_t dot_lo = 0, dot_hi = 0, sum_lo = 0, sum_hi = 0;
+            for (int j = 0; j < 32; j++) {
+                int lo = qs[g * 32 + j] & 0xF, hi = qs[g * 32 + j] >> 4;
+                dot_lo += lo * xqs[g * 64 + j];
+                dot_hi += hi * xqs[g * 64 + 32 + j];
+                sum_lo += xqs[g * 64 + j];
+                sum_hi += xqs[g * 64 + 32 + j];
+            }
+            block_sum += d * (float)sc_lo * (float)dot_lo - dmin * (float)m_lo * (float)sum_lo;
+            block_sum += d * (float)sc_hi * (float)dot_hi - dmin * (float)m_hi * (float)sum_hi;
+        }
+        total += sx * block_sum;
+    }
+    return total;
+}
+
+/* Q6_K row dot, libtinygiant.c:194-243 */
+float ref_dot_q6k(const uint8_t *q6, const uint8_t *xq, int bpr) {
+    float total = 0;
+    for (int b = 0; b < bpr; b++) {
+        const uint8_t *bl = q6 + (size_t)b * REF_Q6K_BYTES;
+        const uint8_t *ql = bl, *qh = bl + 128;
+        const int8_t *sc = (const int8_t *)(bl + 192);
+        uint16_t dr;
+        memcpy(&dr, bl + 208, 2);
+        float d = ref_f16_to_f32(dr);
+        const uint8_t *xb = xq + (size_t)b * REF_Q8K_BYTES;
+        float sx;
+        memcpy(&sx, xb, 4);
+        const int8_t *xqs = (const int8_t *)(xb + 8);
+        float block_sum = 0;
+        for (int half = 0; half < 2; half++) {
+            const uint8_t *ql_h = ql + half * 64, *qh_h = qh + half * 32;
+            const int8_t *sc_h = sc + half * 8, *xq_h = xqs + half * 128;
+            for (int l = 0; l < 32; l += 16) {
+                int is = l / 16;
+                int32_t d1 = 0, d2 = 0, d3 = 0, d4 = 0;
+                for (int kk = 0; kk < 16; kk++) {
+                    int j = l + kk;
+                    int v1 = (ql_h[j] & 0xF) | (((qh_h[j] >> 0) & 3) << 4);
+                    int v2 = (ql_h[j + 32] & 0xF) | (((qh_h[j] >> 2) & 3) << 4);
+                    int v3 = (ql_h[j] >> 4) | (((qh_h[j] >> 4) & 3) << 4);
+                    int v4 = (ql_h[j + 32] >> 4) | (((qh_h[j] >> 6) & 3) << 4);
+                    d1 += (v1 - 32) * xq_h[l + kk];
+                    d2 += (v2 - 32) * xq_h[l + kk + 32];
+                    d3 += (v3 - 32) * xq_h[l + kk + 64];
+                    d4 += (v4 - 32) * xq_h[l + kk + 96];
+                }
+                block_sum += (float)sc_h[is + 0] * (float)d1;
+                block_sum += (float)sc_h[is + 2] * (float)d2;
+                block_sum += (float)sc_h[is + 4] * (float)d3;
+                block_sum += (float)sc_h[is + 6] * (float)d4;
+            }
+        }
+        total += d * sx * block_sum;
+    }
+    return total;
+}
+
+/* f16 row dot in the shape of libtinygiant.c:268-287: eight running fused sums, lane v
+ * taking columns v, v + 8, ..., then (s0+s4 + s1+s5) + (s2+s6 + s3+s7) pairwise. */
+float ref_dot_f16(const uint16_t *row, const float *x, int ncols) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i + 7 < ncols; i += 8)
+        for (int v = 0; v < 8; v++) acc[v] = fmaf(ref_f16_to_f32(row[i + v]), x[i + v], acc[v]);
+    float t0 = acc[0] + acc[4], t1 = acc[1] + acc[5], t2 = acc[2] + acc[6], t3 = acc[3] + acc[7];
+    return (t0 + t1) + (t2 + t3);
+}
+
+/* f32 row dot, libtinygiant.c:300-318: the f16 order above on fp32 weights. */
+float ref_dot_f32(const float *row, const float *x, int ncols) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int i = 0; i + 7 < ncols; i += 8)
+        for (int v = 0; v < 8; v++) acc[v] = fmaf(row[i + v], x[i + v], acc[v]);
+    float t0 = acc[0] + acc[4], t1 = acc[1] + acc[5], t2 = acc[2] + acc[6], t3 = acc[3] + acc[7];
+    return (t0 + t1) + (t2 + t3);
+}
+
+/* tg_rms_norm, libtinygiant.c:322-340 (dim a multiple of 4): four running fused sums of
+ * x^2 (lane v takes elements v, v + 4, ...), added pairwise, scale = 1 / sqrtf(ss/dim + eps),
+ * out = (x * scale) * w. */
+void ref_rms_norm_k(const float *x, const float *w, float *out, int dim, float eps) {
+    float acc[4] = {0, 0, 0, 0};
+    for (int i = 0; i + 3 < dim; i += 4)
+        for (int v = 0; v < 4; v++) acc[v] = fmaf(x[i + v], x[i + v], acc[v]);
+    float ss = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    float scale = 1.f / sqrtf(ss / dim + eps);
+    for (int i = 0; i < dim; i++) out[i] = (x[i] * scale) * w[i];
+}
+
+/* fmt: 0 Q4_K, 1 f16, 2 Q6_K, 4 f32 (rows of the reference's own byte layout). */
+void ref_matvec_k(const void *W, int fmt, const float *x, float *y, int rows, int cols) {
+    int bpr = cols / REF_QKK;
+    uint8_t *xq = malloc((size_t)bpr * REF_Q8K_BYTES);
+    if (fmt == 0 || fmt == 2) ref_quantize_q8k(x, xq, cols);
+    for (int r = 0; r < rows; r++) {
+        if (fmt == 0) y[r] = ref_dot_q4k((const uint8_t *)W + (size_t)r * bpr * REF_Q4K_BYTES, xq, bpr);
+        else if (fmt == 2) y[r] = ref_dot_q6k((const uint8_t *)W + (size_t)r * bpr * REF_Q6K_BYTES, xq, bpr);
+        else if (fmt == 4) y[r] = ref_dot_f32((const float *)W + (size_t)r * cols, x, cols);
+        else y[r] = ref_dot_f16((const uint16_t *)W + (size_t)r * cols, x, cols);
+    }
+    free(xq);
+}
+
+/* tg_expert_forward_mixed, libtinygiant.c:599-643 (down_format 0 = Q4_K also gives
+ * tg_expert_forward, :555-595): Q4_K gate/up on Q8(256) of x, h = g / (1 + exp(-g)) * u,
+ * down in its format (Q4_K and Q6_K on Q8(256) of h, f16 on h itself), out += w * y. */
+void ref_expert_forward_k(const uint8_t *gate, const uint8_t *up, const void *down, int down_format,
+                          const float *x, float *out, float w, int embed, int inter, int mode) {
+    float *g = malloc(sizeof(float) * inter), *u = malloc(sizeof(float) * inter);
+    float *h = malloc(sizeof(float) * inter), *y = malloc(sizeof(float) * embed);
+    ref_matvec_k(gate, 0, x, g, inter, embed);
+    ref_matvec_k(up, 0, x, u, inter, embed);
+    for (int i = 0; i < inter; i++) h[i] = ref_silu_mul(g[i], u[i], mode);
+    ref_matvec_k(down, down_format, h, y, embed, inter);
+    for (int i = 0; i < embed; i++) out[i] += w * y[i];
+    free(g); free(u); free(h); free(y);
+}
+
 /* The MoE block with its FFN RMSNorm for T independent tokens x[T][embed], in place:
  * ref_moe_block per token (engine.py:229-258 for each row of a batch); tokens run in
  * parallel across n_threads (0 = OpenMP default). */

@@ -91,6 +91,15 @@ void ref_decode_step(const uint8_t *const *layer_blobs, const float *const *rout
                      int mode, int32_t *idx_out /* [n_layers*k] or NULL */);
 
 /* Batched tokens: T independent tokens through one MoE block (x is [T][embed]). */
+void ref_quantize_q8k(const float *x, uint8_t *out, int64_t n);
+float ref_dot_q4k(const uint8_t *q4, const uint8_t *xq, int bpr);
+float ref_dot_q6k(const uint8_t *q6, const uint8_t *xq, int bpr);
+float ref_dot_f16(const uint16_t *row, const float *x, int ncols);
+float ref_dot_f32(const float *row, const float *x, int ncols);
+void ref_rms_norm_k(const float *x, const float *w, float *out, int dim, float eps);
+void ref_matvec_k(const void *W, int fmt, const float *x, float *y, int rows, int cols);
+void ref_expert_forward_k(const uint8_t *gate, const uint8_t *up, const void *down, int down_format,
+                          const float *x, float *out, float w, int embed, int inter, int mode);
 void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
                            float eps, float *x, int T, int n_experts, int k, int embed, int inter, int mode,
                            int n_threads);

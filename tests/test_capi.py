@@ -44,8 +44,15 @@ def test_argument_errors_without_device():
     out = np.zeros(64, np.uint8)
     assert lib.tg_quantize_q8_0(x.ctypes.data, out.ctypes.data, 48) == L.TG_EINVAL  # not a multiple of 32
     assert lib.tg_expert_forward_q4_0(out.ctypes.data, x.ctypes.data, x.ctypes.data, 1.0, 2000, 768) == L.TG_EINVAL
-    assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, L.TG_FMT_Q6_K,
-                                       x.ctypes.data, x.ctypes.data, 1.0, 2048, 768) == L.TG_EUNSUPPORTED
+    assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, 7,
+                                       x.ctypes.data, x.ctypes.data, 1.0, 2048, 768) == L.TG_EINVAL
+    assert lib.tg_matmul_q4k(out.ctypes.data, x.ctypes.data, x.ctypes.data, 4, 300) == L.TG_EINVAL
+    assert lib.tg_matmul_q6k(out.ctypes.data, x.ctypes.data, x.ctypes.data, 0, 256) == L.TG_EINVAL
+    assert lib.tg_f16_matvec(out.ctypes.data, x.ctypes.data, x.ctypes.data, 4, 12) == L.TG_EINVAL
+    assert lib.tg_rms_norm(x.ctypes.data, x.ctypes.data, x.ctypes.data, 6, 1e-6) == L.TG_EINVAL
+    assert lib.tgx_kq_matrix_bytes(2, 4, 300) == 0 and lib.tgx_kq_matrix_bytes(2, 4, 512) == 4 * 2 * 210
+    assert lib.tgx_kq_experts_forward(None, None, None, 0, 1, None, None, None, 2048, 768, 0, None,
+                                      None) == L.TG_EINVAL
     shape = L.TgxShape(2048, 768, 128, 8, 48, 1e-6)
     h = ctypes.c_void_p()
     bad = L.TgxShape(2048, 768, 128, 200, 48, 1e-6)
@@ -54,6 +61,8 @@ def test_argument_errors_without_device():
         assert lib.tgx_ctx_create(0, ctypes.byref(shape), ctypes.byref(h)) == L.TG_ENODEV
         xs = np.zeros(64, np.float32)
         assert lib.tg_quantize_q8_0(xs.ctypes.data, out.ctypes.data, 64) == L.TG_ENODEV
+        assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, L.TG_FMT_Q6_K,
+                                           x.ctypes.data, x.ctypes.data, 1.0, 2048, 768) == L.TG_ENODEV
 
 
 def test_mlock_matches_reference_semantics():

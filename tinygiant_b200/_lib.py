@@ -64,6 +64,17 @@ PROTOTYPES = {
     "tg_expert_forward_q4_0": (CI, [VP, VP, VP, CF, CI, CI]),
     "tg_expert_forward_mixed": (CI, [VP, VP, VP, CI, VP, VP, CF, CI, CI]),
     "tg_moe_forward_q4_0": (CI, [VP, VP, CI, VP, VP, CI, CI]),
+    "tg_matmul_q4k": (CI, [VP, VP, VP, CI, CI]),
+    "tg_matmul_q6k": (CI, [VP, VP, VP, CI, CI]),
+    "tg_f16_matvec": (CI, [VP, VP, VP, CI, CI]),
+    "tg_f32_matvec": (CI, [VP, VP, VP, CI, CI]),
+    "tg_rms_norm": (CI, [VP, VP, VP, CI, CF]),
+    "tg_expert_forward": (CI, [VP, VP, VP, CF, CI, CI]),
+    "tg_moe_forward": (CI, [VP, VP, CI, VP, VP, CI, CI]),
+    "tgx_kq_matrix_bytes": (SZ, [CI, ctypes.c_longlong, CI]),
+    "tgx_kq_prepare": (CI, [CI, VP, VP, ctypes.c_longlong, CI, VP]),
+    "tgx_kq_matvec": (CI, [CI, VP, VP, VP, CI, CI, VP]),
+    "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, VP]),
     "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),
     "tg_mlock": (CI, [VP, SZ]),
     "tgx_ctx_create": (CI, [CI, ctypes.POINTER(TgxShape), ctypes.POINTER(VP)]),

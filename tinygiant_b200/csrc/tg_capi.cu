@@ -270,16 +270,172 @@ extern "C" int tg_expert_forward_q4_0(const uint8_t* q4_data, const float* input
                                 embed_dim, inter_dim);
 }
 
+// ------------------------------------------------------------ the reference's own formats
+// (csrc/libtinygiant.c: Q4_K, Q6_K, f16, f32, RMSNorm; kernels in tg_kquant.cu)
+
+static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// Copy a host matrix in the reference's byte layout to dst in device layout (Q6_K is
+// split through W.raw; the other formats are copied as they are).
+static int kq_put(HostWS& W, int fmt, const void* src, long long rows, int cols, uint8_t* dst) {
+    size_t nb = tg::kq_matrix_bytes(fmt, rows, cols);
+    if (fmt == tg::KQ_Q6K) {
+        TG_TRY(ensure(W.raw, nb));
+        TG_CUDA(cudaMemcpyAsync(W.raw.p, src, nb, cudaMemcpyHostToDevice, W.s));
+        TG_CUDA(tg::launch_kq_split_q6k((const uint8_t*)W.raw.p, dst, rows * (cols / 256), W.s));
+    } else {
+        TG_CUDA(cudaMemcpyAsync(dst, src, nb, cudaMemcpyHostToDevice, W.s));
+    }
+    return TG_OK;
+}
+
+static int kq_matvec_host(int fmt, const void* A, const float* x, float* out, int nrows, int ncols, const char* fn) {
+    TG_CHECK(A && x && out, TG_EINVAL, std::string(fn) + ": null pointer");
+    TG_CHECK(tg::kq_valid(fmt, nrows, ncols), TG_EINVAL,
+             std::string(fn) + ": bad shape (rows > 0; ncols a multiple of 256 for Q4_K/Q6_K, of 8 for f16/f32)");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    TG_TRY(ensure(W.w, tg::kq_matrix_bytes(fmt, nrows, ncols)));
+    TG_TRY(ensure(W.x, sizeof(float) * ncols));
+    TG_TRY(ensure(W.out, sizeof(float) * nrows));
+    TG_TRY(kq_put(W, fmt, A, nrows, ncols, (uint8_t*)W.w.p));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, x, sizeof(float) * ncols, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_kq_matvec(fmt, (const uint8_t*)W.w.p, (const float*)W.x.p, (float*)W.out.p, nrows, ncols,
+                                 W.s));
+    TG_CUDA(cudaMemcpyAsync(out, W.out.p, sizeof(float) * nrows, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_matmul_q4k(const uint8_t* q4_matrix, const float* input, float* output, int nrows, int ncols) {
+    return kq_matvec_host(tg::KQ_Q4K, q4_matrix, input, output, nrows, ncols, "tg_matmul_q4k");
+}
+extern "C" int tg_matmul_q6k(const uint8_t* q6_matrix, const float* input, float* output, int nrows, int ncols) {
+    return kq_matvec_host(tg::KQ_Q6K, q6_matrix, input, output, nrows, ncols, "tg_matmul_q6k");
+}
+extern "C" int tg_f16_matvec(const uint16_t* A, const float* x, float* out, int nrows, int ncols) {
+    return kq_matvec_host(tg::KQ_F16, A, x, out, nrows, ncols, "tg_f16_matvec");
+}
+extern "C" int tg_f32_matvec(const float* A, const float* x, float* out, int nrows, int ncols) {
+    return kq_matvec_host(tg::KQ_F32, A, x, out, nrows, ncols, "tg_f32_matvec");
+}
+
+extern "C" int tg_rms_norm(const float* x, const float* weight, float* out, int dim, float eps) {
+    TG_CHECK(x && weight && out, TG_EINVAL, "tg_rms_norm: null pointer");
+    TG_CHECK(dim > 0 && dim % 4 == 0, TG_EINVAL, "tg_rms_norm: dim must be a positive multiple of 4");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    TG_TRY(ensure(W.x, sizeof(float) * dim));
+    TG_TRY(ensure(W.wts, sizeof(float) * dim));
+    TG_TRY(ensure(W.out, sizeof(float) * dim));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, x, sizeof(float) * dim, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.wts.p, weight, sizeof(float) * dim, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(tg::launch_rms_norm_ref((const float*)W.x.p, (const float*)W.wts.p, (float*)W.out.p, dim, eps, W.s));
+    TG_CUDA(cudaMemcpyAsync(out, W.out.p, sizeof(float) * dim, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+// n experts with Q4_K gate/up and a down matrix of format fmt (host pointers):
+// out = (accumulate ? output : 0) + sum_e w_e * expert_e(input), experts in order.
+static int kq_experts_host(const uint8_t* const* gate, const uint8_t* const* up, const void* const* down, int fmt,
+                           int n, const float* weights, float w_scalar, const float* input, float* output, int embed,
+                           int inter, int accumulate, const char* fn) {
+    TG_CHECK(n >= 1 && n <= 64, TG_EINVAL, std::string(fn) + ": 1 <= n_experts <= 64");
+    for (int e = 0; e < n; e++)
+        TG_CHECK(gate[e] && up[e] && down[e], TG_EINVAL, std::string(fn) + ": null expert pointer");
+    TG_CHECK(Geom::valid_dims(embed, inter), TG_EINVAL,
+             std::string(fn) + ": embed/inter must be positive multiples of 256 (<= 16384)");
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    const size_t gb = r256(tg::kq_matrix_bytes(tg::KQ_Q4K, inter, embed));
+    const size_t db = r256(tg::kq_matrix_bytes(fmt, embed, inter));
+    const size_t stride = 2 * gb + db;
+    TG_TRY(ensure(W.w, stride * n));
+    TG_TRY(ensure(W.x, sizeof(float) * embed));
+    TG_TRY(ensure(W.out, sizeof(float) * embed));
+    TG_TRY(ensure(W.hq, sizeof(float) * (size_t)n * inter));
+    TG_TRY(ensure(W.ptrs, sizeof(void*) * 3 * n));
+    TG_TRY(ensure(W.wts, sizeof(float) * n));
+    std::vector<const uint8_t*> ptrs(3 * n);
+    for (int e = 0; e < n; e++) {
+        uint8_t* base = (uint8_t*)W.w.p + stride * e;
+        ptrs[e] = base;
+        ptrs[n + e] = base + gb;
+        ptrs[2 * n + e] = base + 2 * gb;
+        TG_TRY(kq_put(W, tg::KQ_Q4K, gate[e], inter, embed, base));
+        TG_TRY(kq_put(W, tg::KQ_Q4K, up[e], inter, embed, base + gb));
+        TG_TRY(kq_put(W, fmt, down[e], embed, inter, base + 2 * gb));
+    }
+    std::vector<float> wv(n, w_scalar);
+    if (weights)
+        for (int e = 0; e < n; e++) wv[e] = weights[e];
+    TG_CUDA(cudaMemcpyAsync(W.ptrs.p, ptrs.data(), sizeof(void*) * 3 * n, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.wts.p, wv.data(), sizeof(float) * n, cudaMemcpyHostToDevice, W.s));
+    TG_CUDA(cudaMemcpyAsync(W.x.p, input, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
+    if (accumulate) TG_CUDA(cudaMemcpyAsync(W.out.p, output, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
+    const uint8_t* const* dp = (const uint8_t* const*)W.ptrs.p;
+    TG_CUDA(tg::launch_kq_gateup(dp, dp + n, n, (const float*)W.x.p, embed, inter, (float*)W.hq.p, W.s));
+    TG_CUDA(tg::launch_kq_down(fmt, dp + 2 * n, n, (const float*)W.hq.p, (const float*)W.wts.p, embed, inter,
+                               (float*)W.out.p, accumulate, W.s));
+    TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * embed, cudaMemcpyDeviceToHost, W.s));
+    TG_CUDA(cudaStreamSynchronize(W.s));
+    return TG_OK;
+}
+
+extern "C" int tg_expert_forward(const uint8_t* q4_data, const float* input, float* output, float weight,
+                                 int embed_dim, int inter_dim) {
+    TG_CHECK(q4_data && input && output, TG_EINVAL, "tg_expert_forward: null pointer");
+    TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
+             "tg_expert_forward: embed/inter must be positive multiples of 256 (<= 16384)");
+    const size_t gb = tg::kq_matrix_bytes(tg::KQ_Q4K, inter_dim, embed_dim);
+    const uint8_t* g = q4_data;
+    const uint8_t* u = q4_data + gb;
+    const void* d = q4_data + 2 * gb;
+    return kq_experts_host(&g, &u, &d, tg::KQ_Q4K, 1, nullptr, weight, input, output, embed_dim, inter_dim, 1,
+                           "tg_expert_forward");
+}
+
 extern "C" int tg_expert_forward_mixed(const uint8_t* gate_q4, const uint8_t* up_q4, const void* down_data,
                                        int down_format, const float* input, float* output, float weight,
                                        int embed_dim, int inter_dim) {
     TG_CHECK(gate_q4 && up_q4 && down_data && input && output, TG_EINVAL, "tg_expert_forward_mixed: null pointer");
-    if (down_format != TG_FMT_Q4_0)
-        return fail(TG_EUNSUPPORTED, "tg_expert_forward_mixed: only TG_FMT_Q4_0 experts are implemented");
     TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
-             "tg_expert_forward_mixed: embed/inter must be positive multiples of 256");
-    return expert_forward_parts(gate_q4, up_q4, (const uint8_t*)down_data, input, output, weight, embed_dim,
-                                inter_dim);
+             "tg_expert_forward_mixed: embed/inter must be positive multiples of 256 (<= 16384)");
+    if (down_format == TG_FMT_Q4_0)
+        return expert_forward_parts(gate_q4, up_q4, (const uint8_t*)down_data, input, output, weight, embed_dim,
+                                    inter_dim);
+    int fmt;
+    switch (down_format) {
+        case TG_FMT_Q4_K: fmt = tg::KQ_Q4K; break;
+        case TG_FMT_F16: fmt = tg::KQ_F16; break;
+        case TG_FMT_Q6_K: fmt = tg::KQ_Q6K; break;
+        default: return fail(TG_EINVAL, "tg_expert_forward_mixed: down_format must be 0 (Q4_K), 1 (f16), 2 (Q6_K) or 3 (Q4_0)");
+    }
+    return kq_experts_host(&gate_q4, &up_q4, &down_data, fmt, 1, nullptr, weight, input, output, embed_dim,
+                           inter_dim, 1, "tg_expert_forward_mixed");
+}
+
+extern "C" int tg_moe_forward(const uint8_t** expert_ptrs, const float* weights, int n_experts, const float* input,
+                              float* output, int embed_dim, int inter_dim) {
+    TG_CHECK(expert_ptrs && weights && input && output, TG_EINVAL, "tg_moe_forward: null pointer");
+    TG_CHECK(n_experts >= 1 && n_experts <= 64, TG_EINVAL, "tg_moe_forward: 1 <= n_experts <= 64");
+    TG_CHECK(Geom::valid_dims(embed_dim, inter_dim), TG_EINVAL,
+             "tg_moe_forward: embed/inter must be positive multiples of 256 (<= 16384)");
+    const size_t gb = tg::kq_matrix_bytes(tg::KQ_Q4K, inter_dim, embed_dim);
+    std::vector<const uint8_t*> g(n_experts), u(n_experts);
+    std::vector<const void*> d(n_experts);
+    for (int e = 0; e < n_experts; e++) {
+        TG_CHECK(expert_ptrs[e], TG_EINVAL, "tg_moe_forward: null expert");
+        g[e] = expert_ptrs[e];
+        u[e] = expert_ptrs[e] + gb;
+        d[e] = expert_ptrs[e] + 2 * gb;
+    }
+    return kq_experts_host(g.data(), u.data(), d.data(), tg::KQ_Q4K, n_experts, weights, 0.0f, input, output,
+                           embed_dim, inter_dim, 0, "tg_moe_forward");
 }
 
 extern "C" int tg_moe_forward_q4_0(const uint8_t** expert_ptrs, const float* weights, int n_experts,
@@ -859,5 +1015,56 @@ extern "C" int tgx_last_routing(tgx_ctx* ctx, int layer, int32_t* idx, float* w,
     if (w) TG_CUDA(cudaMemcpy(w, ctx->wts + (size_t)layer * k, sizeof(float) * k, cudaMemcpyDeviceToHost));
     if (logits)
         TG_CUDA(cudaMemcpy(logits, ctx->logits + (size_t)layer * E, sizeof(float) * E, cudaMemcpyDeviceToHost));
+    return TG_OK;
+}
+
+// ============================================================ reference formats on device pointers
+
+extern "C" size_t tgx_kq_matrix_bytes(int fmt, long long rows, int cols) {
+    return tg::kq_valid(fmt, rows > 0 && rows < (1LL << 31) ? (int)rows : 0, cols) ? tg::kq_matrix_bytes(fmt, rows, cols)
+                                                                                   : 0;
+}
+
+extern "C" int tgx_kq_prepare(int fmt, const void* src_dev, void* dst_dev, long long rows, int cols, void* stream) {
+    TG_CHECK(src_dev && dst_dev && src_dev != dst_dev, TG_EINVAL, "tgx_kq_prepare: null or aliased pointers");
+    TG_CHECK(rows > 0 && rows < (1LL << 31) && tg::kq_valid(fmt, (int)rows, cols), TG_EINVAL,
+             "tgx_kq_prepare: bad format or shape");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (fmt == tg::KQ_Q6K)
+        TG_CUDA(tg::launch_kq_split_q6k((const uint8_t*)src_dev, (uint8_t*)dst_dev, rows * (cols / 256), s));
+    else
+        TG_CUDA(cudaMemcpyAsync(dst_dev, src_dev, tg::kq_matrix_bytes(fmt, rows, cols), cudaMemcpyDeviceToDevice, s));
+    return TG_OK;
+}
+
+extern "C" int tgx_kq_matvec(int fmt, const void* W_dev, const float* x_dev, float* y_dev, int rows, int cols,
+                             void* stream) {
+    TG_CHECK(W_dev && x_dev && y_dev, TG_EINVAL, "tgx_kq_matvec: null pointer");
+    TG_CHECK(tg::kq_valid(fmt, rows, cols), TG_EINVAL, "tgx_kq_matvec: bad format or shape");
+    TG_CUDA(tg::launch_kq_matvec(fmt, (const uint8_t*)W_dev, x_dev, y_dev, rows, cols, (cudaStream_t)stream));
+    return TG_OK;
+}
+
+extern "C" int tgx_kq_experts_forward(const void* const* gate_dev, const void* const* up_dev,
+                                      const void* const* down_dev, int down_format, int n, const float* w_dev,
+                                      const float* x_dev, float* out_dev, int embed, int inter, int accumulate,
+                                      float* h_dev, void* stream) {
+    TG_CHECK(gate_dev && up_dev && down_dev && w_dev && x_dev && out_dev && h_dev, TG_EINVAL,
+             "tgx_kq_experts_forward: null pointer");
+    TG_CHECK(n >= 1 && n <= 65535, TG_EINVAL, "tgx_kq_experts_forward: 1 <= n <= 65535");
+    TG_CHECK(Geom::valid_dims(embed, inter), TG_EINVAL,
+             "tgx_kq_experts_forward: embed/inter must be positive multiples of 256 (<= 16384)");
+    int fmt;
+    switch (down_format) {
+        case TG_FMT_Q4_K: fmt = tg::KQ_Q4K; break;
+        case TG_FMT_F16: fmt = tg::KQ_F16; break;
+        case TG_FMT_Q6_K: fmt = tg::KQ_Q6K; break;
+        default: return fail(TG_EINVAL, "tgx_kq_experts_forward: down_format must be 0 (Q4_K), 1 (f16) or 2 (Q6_K)");
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    TG_CUDA(tg::launch_kq_gateup((const uint8_t* const*)gate_dev, (const uint8_t* const*)up_dev, n, x_dev, embed,
+                                 inter, h_dev, s));
+    TG_CUDA(tg::launch_kq_down(fmt, (const uint8_t* const*)down_dev, n, h_dev, w_dev, embed, inter, out_dev,
+                               accumulate, s));
     return TG_OK;
 }

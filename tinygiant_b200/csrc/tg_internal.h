@@ -83,6 +83,27 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
                                int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
                                float* w_out, float* logits_out, cudaStream_t s);
 
+// The reference library's own formats (tg_kquant.cu).  fmt: KQ_Q4K (ggml Q4_K
+// blocks), KQ_F16, KQ_Q6K (split layout: 208-byte bodies of all blocks, then their
+// fp16 d), KQ_F32.  Rows of the quantised formats hold a multiple of 256 values,
+// float rows a multiple of 8; matrices and vectors 16-byte aligned.
+constexpr int KQ_Q4K = 0, KQ_F16 = 1, KQ_Q6K = 2, KQ_F32 = 4;
+bool kq_valid(int fmt, int rows, int cols);
+size_t kq_matrix_bytes(int fmt, long long rows, int cols);   // ggml bytes (= device bytes)
+size_t kq_smem_bytes(int fmt, int cols);
+// Q6_K ggml blocks -> split layout; raw and dst must not alias.
+cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk, cudaStream_t s);
+// y[rows] = W . x (Q4_K / Q6_K on the 256-wide Q8 blocks of x; f16 / f32 on x).
+cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s);
+// h[e][I] = silu(gate_e . x) * (up_e . x) for n Q4_K experts (device pointer arrays).
+cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* up, int n, const float* x, int H,
+                             int I, float* h, cudaStream_t s);
+// out[H] = (accumulate ? out : 0) + sum_e w[e] * (down_e . h_e), experts in order.
+cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const float* h, const float* w, int H, int I,
+                           float* out, int accumulate, cudaStream_t s);
+// tg_rms_norm in the reference's order (dim a multiple of 4).
+cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s);
+
 // Record msg as the calling thread's tg_last_error() text; returns code.
 int set_error(int code, const char* msg);
 

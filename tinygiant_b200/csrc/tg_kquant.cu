@@ -1,0 +1,492 @@
+// tg_kquant.cu — the reference library's own weight formats on the GPU
+// (csrc/libtinygiant.c): Q4_K and Q6_K super-blocks of 256 values against 256-wide
+// Q8 activation blocks, f16 and f32 rows, and the RMSNorm, in the reference's float
+// order.
+//
+// Float work follows the reference source statement by statement with every
+// operation rounded on its own (the C text without contraction): within a block the
+// sub-block terms in source order, then the row total over blocks in order.  Integer
+// dots are exact (dp4a), so how they are split across lanes does not matter.
+//
+// A lane computes one (row, block) unit; a warp owns whole rows (32 / blocks-per-row
+// of them, or one row when a row has more than 32 blocks), so the chain of a row's
+// block terms runs in one lane and no step crosses warps.  A warp stages its units'
+// bytes into shared memory with coalesced 16-byte loads before computing.
+//
+// Device layouts: Q4_K as ggml blocks (144 B, so every block is 16-byte aligned);
+// Q6_K "split": the 208-byte bodies (ql | qh | scales) of all blocks of the matrix,
+// then the fp16 d of all blocks (the 210-byte ggml block is only 2-byte aligned);
+// f16 / f32 as row-major values.
+#include <cuda_runtime.h>
+
+#include "tg_device.cuh"
+#include "tg_internal.h"
+
+namespace tg {
+
+namespace {
+
+constexpr int KW = 4;                 // warps per CTA
+constexpr int KT = KW * 32;
+constexpr int Q4K_B = 144, Q6K_BODY = 208, Q6K_B = 210;
+constexpr int XC = 272;               // stride of a block's 256 codes in shared memory (bank spread)
+constexpr int STAGE = 32 * Q6K_BODY;  // staging bytes per warp (32 units of the largest body)
+constexpr int FROWS = 4;              // rows per warp of the f16 / f32 matvec (8 lanes per row)
+constexpr int FCH = 256;              // columns staged per step
+// FMT values: KQ_Q4K 0, KQ_F16 1, KQ_Q6K 2, KQ_F32 4 (tg_internal.h)
+
+// Shared-memory activation of one vector of bpr blocks (quantised formats).
+struct KAct {
+    int8_t* codes;  // [bpr][XC]
+    float* sx;      // [bpr] block scales
+    int* s32;       // [bpr][8] code sums of the 32-value sub-blocks
+    int* s16;       // [bpr][16] code sums of the 16-value groups
+};
+
+__host__ __device__ inline size_t r16(size_t n) { return (n + 15) & ~(size_t)15; }
+
+__host__ __device__ inline size_t act_region(int fmt, int cols) {
+    int bpr = cols / 256;
+    if (fmt == KQ_F16 || fmt == KQ_F32) return (size_t)cols * 4;
+    return r16((size_t)bpr * XC) + r16((size_t)bpr * 4) + (size_t)bpr * 32 + (size_t)bpr * 64;
+}
+__host__ __device__ inline int terms_per_warp(int cols) {
+    int bpr = cols / 256;
+    return bpr > 32 ? bpr : 32;
+}
+__host__ __device__ inline size_t kq_smem(int fmt, int cols) {
+    return act_region(fmt, cols) + (size_t)KW * (STAGE + r16((size_t)terms_per_warp(cols) * 4));
+}
+
+__device__ inline KAct act_at(uint8_t* base, int bpr) {
+    KAct a;
+    a.codes = (int8_t*)base;
+    a.sx = (float*)(base + r16((size_t)bpr * XC));
+    a.s32 = (int*)((uint8_t*)a.sx + r16((size_t)bpr * 4));
+    a.s16 = a.s32 + bpr * 8;
+    return a;
+}
+
+// quantize_q8, csrc/libtinygiant.c:61-89, for one vector x[bpr * 256]: one warp per
+// block, 8 values per lane.  scale = amax / 127, codes = round-half-even(x * (127 /
+// amax)), or 0 when amax is 0.  Also the exact code sums of 32- and 16-value groups.
+__device__ void quantize_q8k(const float* __restrict__ x, int bpr, KAct a, int warp, int lane) {
+    for (int b = warp; b < bpr; b += KW) {
+        const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * 256 + lane * 8);
+        float4 v0 = src[0], v1 = src[1];
+        float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float am = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+        float sc = __fdiv_rn(am, 127.0f);
+        float inv = am > 0.0f ? __fdiv_rn(127.0f, am) : 0.0f;
+        int q[8], s = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            q[i] = __float2int_rn(__fmul_rn(v[i], inv));
+            s += q[i];
+        }
+        uint2 packed;
+        packed.x = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((unsigned)(q[3] & 0xFF) << 24);
+        packed.y = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((unsigned)(q[7] & 0xFF) << 24);
+        *reinterpret_cast<uint2*>(a.codes + (size_t)b * XC + lane * 8) = packed;
+        int s16 = s + __shfl_xor_sync(0xffffffffu, s, 1);
+        int s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 2);
+        if ((lane & 1) == 0) a.s16[b * 16 + (lane >> 1)] = s16;
+        if ((lane & 3) == 0) a.s32[b * 8 + (lane >> 2)] = s32;
+        if (lane == 0) a.sx[b] = sc;
+    }
+}
+
+__device__ __forceinline__ unsigned byte_of(uint4 v, int i) {
+    unsigned w = i < 4 ? v.x : i < 8 ? v.y : i < 12 ? v.z : v.w;
+    return (w >> (8 * (i & 3))) & 0xFFu;
+}
+
+// get_scale_min_k4, csrc/libtinygiant.c:42-51 (q = the block's 12 scale bytes,
+// held as bytes 4..15 of its first 16-byte word).
+__device__ __forceinline__ void scale_min_k4(int j, uint4 h, float& sc, float& m) {
+#define QB(i) byte_of(h, 4 + (i))
+    unsigned s, mm;
+    if (j < 4) {
+        s = QB(j) & 63;
+        mm = QB(j + 4) & 63;
+    } else {
+        s = (QB(j + 4) & 0xF) | ((QB(j - 4) >> 6) << 4);
+        mm = (QB(j + 4) >> 4) | ((QB(j) >> 6) << 4);
+    }
+#undef QB
+    sc = (float)s;
+    m = (float)mm;
+}
+
+__device__ __forceinline__ unsigned word_of(uint4 v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// One Q4_K block against activation block b: sx * block_sum, dot_q4k_q8
+// (csrc/libtinygiant.c:104-169): block_sum += d*sc*dot - dmin*m*sum per sub-block.
+__device__ __forceinline__ float q4k_term(const uint8_t* blk, const KAct& a, int b) {
+    const uint4* w4 = reinterpret_cast<const uint4*>(blk);
+    const uint4 hd = w4[0];
+    const float d = f16_bits_to_f32((uint16_t)(hd.x & 0xFFFF));
+    const float dmin = f16_bits_to_f32((uint16_t)(hd.x >> 16));
+    const uint4* xc = reinterpret_cast<const uint4*>(a.codes + (size_t)b * XC);
+    const int* s32 = a.s32 + b * 8;
+    float bs = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        int dl = 0, dh = 0;
+#pragma unroll
+        for (int hq = 0; hq < 2; hq++) {
+            const uint4 q = w4[1 + 2 * g + hq];
+            const uint4 xl = xc[4 * g + hq], xh = xc[4 * g + 2 + hq];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const unsigned w = word_of(q, t);
+                dl = dp4a_us(w & 0x0F0F0F0Fu, (int)word_of(xl, t), dl);
+                dh = dp4a_us((w >> 4) & 0x0F0F0F0Fu, (int)word_of(xh, t), dh);
+            }
+        }
+        float sc_lo, m_lo, sc_hi, m_hi;
+        scale_min_k4(2 * g, hd, sc_lo, m_lo);
+        scale_min_k4(2 * g + 1, hd, sc_hi, m_hi);
+        float tl = __fsub_rn(__fmul_rn(__fmul_rn(d, sc_lo), __int2float_rn(dl)),
+                             __fmul_rn(__fmul_rn(dmin, m_lo), __int2float_rn(s32[2 * g])));
+        bs = __fadd_rn(bs, tl);
+        float th = __fsub_rn(__fmul_rn(__fmul_rn(d, sc_hi), __int2float_rn(dh)),
+                             __fmul_rn(__fmul_rn(dmin, m_hi), __int2float_rn(s32[2 * g + 1])));
+        bs = __fadd_rn(bs, th);
+    }
+    return __fmul_rn(a.sx[b], bs);
+}
+
+// One Q6_K block (208-byte body + its d) against activation block b: d * sx *
+// block_sum, dot_q6k_q8 (csrc/libtinygiant.c:194-243).  Values are the 6-bit codes
+// minus 32; sum (v - 32) * x = dp4a(v, x) - 32 * sum(x), exactly.
+__device__ __forceinline__ float q6k_term(const uint8_t* body, float d, const KAct& a, int b) {
+    const uint4* ql4 = reinterpret_cast<const uint4*>(body);
+    const uint4* qh4 = reinterpret_cast<const uint4*>(body + 128);
+    const uint4 scw = *reinterpret_cast<const uint4*>(body + 192);
+    const uint4* xc = reinterpret_cast<const uint4*>(a.codes + (size_t)b * XC);
+    const int* s16 = a.s16 + b * 16;
+    float bs = 0.0f;
+#pragma unroll
+    for (int half = 0; half < 2; half++) {
+#pragma unroll
+        for (int is = 0; is < 2; is++) {
+            const uint4 A = ql4[4 * half + is], B = ql4[4 * half + 2 + is], Qh = qh4[2 * half + is];
+            const uint4 X0 = xc[8 * half + is], X1 = xc[8 * half + is + 2], X2 = xc[8 * half + is + 4],
+                        X3 = xc[8 * half + is + 6];
+            int d1 = 0, d2 = 0, d3 = 0, d4 = 0;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                const unsigned a0 = word_of(A, t), b0 = word_of(B, t), h = word_of(Qh, t);
+                const unsigned v1 = (a0 & 0x0F0F0F0Fu) | ((h & 0x03030303u) << 4);
+                const unsigned v2 = (b0 & 0x0F0F0F0Fu) | (((h >> 2) & 0x03030303u) << 4);
+                const unsigned v3 = ((a0 >> 4) & 0x0F0F0F0Fu) | (((h >> 4) & 0x03030303u) << 4);
+                const unsigned v4 = ((b0 >> 4) & 0x0F0F0F0Fu) | (((h >> 6) & 0x03030303u) << 4);
+                d1 = dp4a_us(v1, (int)word_of(X0, t), d1);
+                d2 = dp4a_us(v2, (int)word_of(X1, t), d2);
+                d3 = dp4a_us(v3, (int)word_of(X2, t), d3);
+                d4 = dp4a_us(v4, (int)word_of(X3, t), d4);
+            }
+            const int g = 8 * half + is;   // scale index sc_h[is + 2q] and the matching 16-code group
+            d1 -= 32 * s16[g];
+            d2 -= 32 * s16[g + 2];
+            d3 -= 32 * s16[g + 4];
+            d4 -= 32 * s16[g + 6];
+            bs = __fadd_rn(bs, __fmul_rn((float)(int8_t)byte_of(scw, g), __int2float_rn(d1)));
+            bs = __fadd_rn(bs, __fmul_rn((float)(int8_t)byte_of(scw, g + 2), __int2float_rn(d2)));
+            bs = __fadd_rn(bs, __fmul_rn((float)(int8_t)byte_of(scw, g + 4), __int2float_rn(d3)));
+            bs = __fadd_rn(bs, __fmul_rn((float)(int8_t)byte_of(scw, g + 6), __int2float_rn(d4)));
+        }
+    }
+    return __fmul_rn(__fmul_rn(d, a.sx[b]), bs);
+}
+
+// Coalesced copy of `bytes` (a multiple of 16, both ends 16-byte aligned) into the
+// warp's staging area.
+__device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* __restrict__ src, int bytes, int lane) {
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    const int n = bytes >> 4;
+    for (int i = lane; i < n; i += 32) d[i] = __ldg(s + i);
+}
+
+// Rows [r0, r0 + nr) of a quantised matrix against activation a: returns the row
+// total of row r0 + lane in lanes < nr (0 elsewhere).
+template <int FMT>
+__device__ float kq_rows_warp(const uint8_t* __restrict__ M, long long nblk, int bpr, int r0, int nr,
+                              const KAct& a, uint8_t* stage, float* terms, int lane) {
+    constexpr int BB = FMT == KQ_Q4K ? Q4K_B : Q6K_BODY;
+    const long long ubase = (long long)r0 * bpr;
+    const int units = nr * bpr;
+    const uint16_t* d6 = reinterpret_cast<const uint16_t*>(M + (size_t)nblk * Q6K_BODY);
+    for (int c = 0; c < units; c += 32) {
+        const int cnt = min(32, units - c);
+        __syncwarp();
+        stage_copy(stage, M + (size_t)(ubase + c) * BB, cnt * BB, lane);
+        __syncwarp();
+        if (lane < cnt) {
+            const int b = (c + lane) % bpr;
+            float t;
+            if constexpr (FMT == KQ_Q4K)
+                t = q4k_term(stage + lane * BB, a, b);
+            else
+                t = q6k_term(stage + lane * BB, f16_bits_to_f32(__ldg(d6 + ubase + c + lane)), a, b);
+            terms[c + lane] = t;
+        }
+    }
+    __syncwarp();
+    float tot = 0.0f;
+    if (lane < nr)
+        for (int j = 0; j < bpr; j++) tot = __fadd_rn(tot, terms[lane * bpr + j]);
+    __syncwarp();
+    return tot;
+}
+
+// Rows [r0, r0 + nr) (nr <= 4) of an f16 / f32 matrix against fp32 x in shared
+// memory, csrc/libtinygiant.c:262-318: lane (row i, chain v) runs the fused sum of
+// columns v, v + 8, ...; the eight chains fold as (v, v + 4) then pairwise.  Returns
+// the total in lane 8 * i.
+template <int FMT>
+__device__ float fx_rows_warp(const uint8_t* __restrict__ M, int cols, int r0, int nr, const float* xs,
+                              uint8_t* stage, int lane) {
+    constexpr int ES = FMT == KQ_F16 ? 2 : 4;
+    constexpr int RS = FCH * ES + 16;   // padded staged row stride
+    const int ri = lane >> 3, v = lane & 7;
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < cols; c0 += FCH) {
+        const int cw = min(FCH, cols - c0);
+        const int per_row = cw * ES / 16;
+        __syncwarp();
+        for (int i = lane; i < nr * per_row; i += 32) {
+            const int r = i / per_row, k = i - r * per_row;
+            const uint4* s = reinterpret_cast<const uint4*>(M + ((size_t)(r0 + r) * cols + c0) * ES) + k;
+            *reinterpret_cast<uint4*>(stage + r * RS + k * 16) = __ldg(s);
+        }
+        __syncwarp();
+        if (ri < nr) {
+            const uint8_t* row = stage + ri * RS;
+            for (int s = 0; s < cw / 8; s++) {
+                const int col = 8 * s + v;
+                float w = FMT == KQ_F16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[col])
+                                        : reinterpret_cast<const float*>(row)[col];
+                acc = __fmaf_rn(w, xs[c0 + col], acc);
+            }
+        }
+    }
+    __syncwarp();
+    const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));   // chains v and v + 4
+    const float p = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 1));      // (t0 + t1), (t2 + t3)
+    return __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2));                // in lane 8i
+}
+
+struct KQParams {
+    const uint8_t* mat;           // MODE 0: the matrix
+    const uint8_t* const* A;      // MODE 1: gate matrices [n]; MODE 2: down matrices [n]
+    const uint8_t* const* B;      // MODE 1: up matrices [n]
+    const float* x;               // MODE 0 / 1: input [cols]; MODE 2: h [n][cols]
+    const float* w;               // MODE 2: combine weights [n]
+    float* out;                   // MODE 0: y [rows]; MODE 1: h [n][rows]; MODE 2: out [rows]
+    int rows, cols, n, accumulate;
+};
+
+// MODE 0: y = M . x.  MODE 1 (grid.y = expert e): h_e = silu(gate_e . x) * (up_e . x),
+// gate / up Q4_K.  MODE 2: out = (accumulate ? out : 0) + sum_e w_e * (down_e . h_e),
+// experts added in order.
+template <int FMT, int MODE>
+__global__ void __launch_bounds__(KT) k_kq(KQParams p) {
+    extern __shared__ __align__(16) uint8_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr bool FLOAT_FMT = FMT == KQ_F16 || FMT == KQ_F32;
+    const int cols = p.cols, bpr = cols / 256;
+    uint8_t* act = sm;
+    uint8_t* stage = sm + act_region(FMT, cols) + (size_t)warp * (STAGE + r16((size_t)terms_per_warp(cols) * 4));
+    float* terms = reinterpret_cast<float*>(stage + STAGE);
+    const KAct a = act_at(act, bpr);
+    float* xs = reinterpret_cast<float*>(act);
+    const int rpw = FLOAT_FMT ? FROWS : (bpr >= 32 ? 1 : 32 / bpr);
+    const int r0 = (blockIdx.x * KW + warp) * rpw;
+    const int nr = r0 < p.rows ? min(rpw, p.rows - r0) : 0;
+    const long long nblk = (long long)p.rows * bpr;
+    const bool has = FLOAT_FMT ? ((lane & 7) == 0 && (lane >> 3) < nr) : lane < nr;
+    const int row = r0 + (FLOAT_FMT ? (lane >> 3) : lane);
+
+    auto load_act = [&](const float* x) {
+        __syncthreads();
+        if constexpr (FLOAT_FMT) {
+            for (int i = threadIdx.x; i < cols / 4; i += KT)
+                reinterpret_cast<float4*>(xs)[i] = __ldg(reinterpret_cast<const float4*>(x) + i);
+        } else {
+            quantize_q8k(x, bpr, a, warp, lane);
+        }
+        __syncthreads();
+    };
+    auto rows_dot = [&](const uint8_t* M) -> float {
+        if (nr == 0) return 0.0f;
+        if constexpr (FLOAT_FMT)
+            return fx_rows_warp<FMT>(M, cols, r0, nr, xs, stage, lane);
+        else
+            return kq_rows_warp<FMT>(M, nblk, bpr, r0, nr, a, stage, terms, lane);
+    };
+
+    if (MODE == 0) {
+        load_act(p.x);
+        float y = rows_dot(p.mat);
+        if (has) p.out[row] = y;
+    } else if (MODE == 1) {
+        const int e = blockIdx.y;
+        load_act(p.x);
+        float g = rows_dot(p.A[e]);
+        float u = rows_dot(p.B[e]);
+        if (has) p.out[(size_t)e * p.rows + row] = silu_mul(g, u);
+    } else {
+        float acc = has && p.accumulate ? p.out[row] : 0.0f;
+        for (int e = 0; e < p.n; e++) {
+            load_act(p.x + (size_t)e * cols);
+            float y = rows_dot(p.A[e]);
+            if (has) acc = __fadd_rn(acc, __fmul_rn(__ldg(p.w + e), y));
+        }
+        if (has) p.out[row] = acc;
+    }
+}
+
+// Q6_K ggml blocks -> split layout (bodies, then d), one 2-byte word per thread.
+__global__ void k_split_q6k(const uint16_t* __restrict__ src, uint8_t* __restrict__ dst, long long nblk) {
+    const long long n = nblk * (Q6K_B / 2);
+    uint16_t* body = reinterpret_cast<uint16_t*>(dst);
+    uint16_t* dd = reinterpret_cast<uint16_t*>(dst + (size_t)nblk * Q6K_BODY);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long u = i / (Q6K_B / 2);
+        const int k = (int)(i - u * (Q6K_B / 2));
+        const uint16_t v = src[i];
+        if (k < Q6K_BODY / 2)
+            body[u * (Q6K_BODY / 2) + k] = v;
+        else
+            dd[u] = v;
+    }
+}
+
+// tg_rms_norm, csrc/libtinygiant.c:322-340, one CTA: four fused sums of x^2 (chain v
+// over elements v, v + 4, ...), folded pairwise; scale = 1 / sqrtf(ss / dim + eps);
+// out = (x * scale) * w.
+__global__ void k_rms_norm_ref(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
+                               int dim, float eps) {
+    __shared__ float s_scale;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float acc = 0.0f;
+        if (lane < 4)
+            for (int i = lane; i < dim; i += 4) acc = __fmaf_rn(x[i], x[i], acc);
+        const float p = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));   // (s0 + s1), (s2 + s3)
+        const float ss = __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2));
+        if (lane == 0) s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
+    }
+    __syncthreads();
+    const float sc = s_scale;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
+}
+
+template <int FMT, int MODE>
+cudaError_t launch_kq_t(const KQParams& p, int grid_y, cudaStream_t s) {
+    const size_t smem = kq_smem(FMT, p.cols);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(k_kq<FMT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const bool flt = FMT == KQ_F16 || FMT == KQ_F32;
+    const int bpr = p.cols / 256;
+    const int rpw = flt ? FROWS : (bpr >= 32 ? 1 : 32 / bpr);
+    const int rows_per_cta = rpw * KW;
+    dim3 grid((p.rows + rows_per_cta - 1) / rows_per_cta, grid_y);
+    k_kq<FMT, MODE><<<grid, KT, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_kq_fmt(int fmt, const KQParams& p, int grid_y, cudaStream_t s) {
+    switch (fmt) {
+        case KQ_Q4K: return launch_kq_t<KQ_Q4K, MODE>(p, grid_y, s);
+        case KQ_Q6K: return launch_kq_t<KQ_Q6K, MODE>(p, grid_y, s);
+        case KQ_F16: return launch_kq_t<KQ_F16, MODE>(p, grid_y, s);
+        case KQ_F32: return launch_kq_t<KQ_F32, MODE>(p, grid_y, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+bool kq_valid(int fmt, int rows, int cols) {
+    if (rows <= 0 || cols <= 0) return false;
+    if (fmt == KQ_Q4K || fmt == KQ_Q6K) return cols % 256 == 0 && cols <= 65536;
+    if (fmt == KQ_F16 || fmt == KQ_F32) return cols % 8 == 0 && cols <= 32768;   // x staged as fp32
+    return false;
+}
+
+size_t kq_matrix_bytes(int fmt, long long rows, int cols) {
+    switch (fmt) {
+        case KQ_Q4K: return (size_t)rows * (cols / 256) * Q4K_B;
+        case KQ_Q6K: return (size_t)rows * (cols / 256) * Q6K_B;
+        case KQ_F16: return (size_t)rows * cols * 2;
+        case KQ_F32: return (size_t)rows * cols * 4;
+        default: return 0;
+    }
+}
+
+size_t kq_smem_bytes(int fmt, int cols) { return kq_smem(fmt, cols); }
+
+cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk, cudaStream_t s) {
+    if (nblk <= 0) return cudaSuccess;
+    long long words = nblk * (Q6K_B / 2);
+    int grid = (int)((words + 255) / 256);
+    if (grid > 148 * 16) grid = 148 * 16;
+    k_split_q6k<<<grid, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(raw), dst, nblk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s) {
+    KQParams p{};
+    p.mat = W;
+    p.x = x;
+    p.out = y;
+    p.rows = rows;
+    p.cols = cols;
+    p.n = 1;
+    return launch_kq_fmt<0>(fmt, p, 1, s);
+}
+
+cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* up, int n, const float* x, int H,
+                             int I, float* h, cudaStream_t s) {
+    KQParams p{};
+    p.A = gate;
+    p.B = up;
+    p.x = x;
+    p.out = h;
+    p.rows = I;
+    p.cols = H;
+    p.n = n;
+    return launch_kq_t<KQ_Q4K, 1>(p, n, s);
+}
+
+cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const float* h, const float* w, int H, int I,
+                           float* out, int accumulate, cudaStream_t s) {
+    KQParams p{};
+    p.A = down;
+    p.x = h;
+    p.w = w;
+    p.out = out;
+    p.rows = H;
+    p.cols = I;
+    p.n = n;
+    p.accumulate = accumulate;
+    return launch_kq_fmt<2>(fmt, p, 1, s);
+}
+
+cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s) {
+    k_rms_norm_ref<<<1, 256, 0, s>>>(x, w, out, dim, eps);
+    return cudaGetLastError();
+}
+
+}  // namespace tg
