@@ -251,14 +251,26 @@ int tgx_kq_prepare(int fmt, const void *src_dev, void *dst_dev, long long rows, 
 /* y_dev[rows] = W . x (tg_matmul_q4k / tg_matmul_q6k / tg_f16_matvec / tg_f32_matvec on
  * device memory; W in device layout, all pointers 16-byte aligned). */
 int tgx_kq_matvec(int fmt, const void *W_dev, const float *x_dev, float *y_dev, int rows, int cols, void *stream);
+/* Scratch bytes of tgx_kq_experts_forward for n experts (0 for a bad shape). */
+size_t tgx_kq_scratch_bytes(int n, int embed, int inter);
+
+/* flags of tgx_kq_experts_forward: the kernel before this call on `stream` is a
+ * tgx_kq_experts_forward that writes none of this call's weights or pointer arrays
+ * (only x / out): this call's weight fetch then starts before that kernel ends. */
+#define TGX_KQ_CHAINED 1
+
 /* n experts at once (tg_moe_forward / tg_expert_forward_mixed on device memory):
  * out = (accumulate ? out : 0) + sum_e w[e] * down_e(silu(gate_e . x) * (up_e . x)),
- * experts in order.  gate_dev / up_dev / down_dev: DEVICE arrays of n device pointers
- * (Q4_K gate and up; down in down_format 0 / 1 / 2, device layout); w_dev: n floats;
- * h_dev: scratch of n * inter floats.  Allocates nothing; enqueued on stream. */
+ * experts in order; out may equal x.  gate_dev / up_dev / down_dev: DEVICE arrays of n
+ * device pointers (Q4_K gate and up; down in down_format 0 / 1 / 2, device layout);
+ * w_dev: n floats.  scratch: tgx_kq_scratch_bytes(n, embed, inter) bytes, 256-byte
+ * aligned, zero-filled before its first use; every call leaves it ready for the next
+ * (of any shape that fits it), and calls sharing it must be ordered on one stream.  Allocates nothing; two kernel
+ * launches on `stream`, the second a programmatic dependent of the first. */
 int tgx_kq_experts_forward(const void *const *gate_dev, const void *const *up_dev, const void *const *down_dev,
                            int down_format, int n, const float *w_dev, const float *x_dev, float *out_dev,
-                           int embed, int inter, int accumulate, float *h_dev, void *stream);
+                           int embed, int inter, int accumulate, void *scratch, size_t scratch_bytes, int flags,
+                           void *stream);
 
 #ifdef __cplusplus
 }

@@ -51,8 +51,10 @@ def test_argument_errors_without_device():
     assert lib.tg_f16_matvec(out.ctypes.data, x.ctypes.data, x.ctypes.data, 4, 12) == L.TG_EINVAL
     assert lib.tg_rms_norm(x.ctypes.data, x.ctypes.data, x.ctypes.data, 6, 1e-6) == L.TG_EINVAL
     assert lib.tgx_kq_matrix_bytes(2, 4, 300) == 0 and lib.tgx_kq_matrix_bytes(2, 4, 512) == 4 * 2 * 210
-    assert lib.tgx_kq_experts_forward(None, None, None, 0, 1, None, None, None, 2048, 768, 0, None,
+    assert lib.tgx_kq_experts_forward(None, None, None, 0, 1, None, None, None, 2048, 768, 0, None, 0, 0,
                                       None) == L.TG_EINVAL
+    assert lib.tgx_kq_scratch_bytes(8, 2048, 768) >= 8 * (768 + 2048) * 4
+    assert lib.tgx_kq_scratch_bytes(0, 2048, 768) == 0
     shape = L.TgxShape(2048, 768, 128, 8, 48, 1e-6)
     h = ctypes.c_void_p()
     bad = L.TgxShape(2048, 768, 128, 200, 48, 1e-6)

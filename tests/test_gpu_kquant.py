@@ -17,8 +17,13 @@ pytestmark = pytest.mark.gpu
 FQ4K, FF16, FQ6K, FF32 = 0, 1, 2, 4
 
 
-def q4k_blocks(rng, n):
+def q4k_blocks(rng, n, bounded=False):
     b = rng.integers(0, 256, size=(n, 144), dtype=np.uint8)
+    if bounded:   # near zero-mean weights (dmin ~ 7.5 d): activations stay bounded over chained layers
+        d = rng.uniform(5e-5, 1.5e-4, n)
+        b[:, 0:2] = np.asarray(d, np.float16).view(np.uint8).reshape(n, 2)
+        b[:, 2:4] = np.asarray(7.5 * d, np.float16).view(np.uint8).reshape(n, 2)
+        return b.ravel()
     b[:, 0:2] = np.asarray(rng.uniform(5e-4, 3e-3, n), np.float16).view(np.uint8).reshape(n, 2)
     b[:, 2:4] = np.asarray(rng.uniform(2e-4, 2e-3, n), np.float16).view(np.uint8).reshape(n, 2)
     return b.ravel()
@@ -118,12 +123,12 @@ def test_expert_forward_mixed_bit_exact(lib, oracle, fmt, H, I):
 def test_expert_forward_blob_and_golden(lib, oracle):
     gk = np.load(ROOT / "tests" / "golden" / "golden_kquant.npz")
     H, I = int(gk["ex_H"]), int(gk["ex_I"])
-    blob = gk["ex_blob"]
+    blob, x = gk["ex_blob"], gk["ex_x"]           # held: an NpzFile lookup returns a fresh array
     out = np.zeros(H, np.float32)
-    assert lib.tg_expert_forward(blob.ctypes.data, gk["ex_x"].ctypes.data, out.ctypes.data, 1.0, H, I) == 0
+    assert lib.tg_expert_forward(blob.ctypes.data, x.ctypes.data, out.ctypes.data, 1.0, H, I) == 0
     gb = I * (H // 256) * 144
     ref = np.zeros(H, np.float32)
-    oracle.expert_forward_k(blob[:gb], blob[gb:2 * gb], blob[2 * gb:], FQ4K, gk["ex_x"], ref, 1.0, H, I)
+    oracle.expert_forward_k(blob[:gb], blob[gb:2 * gb], blob[2 * gb:], FQ4K, x, ref, 1.0, H, I)
     assert same_bits(out, ref)
     y64 = gk["ex_y64"]
     assert np.linalg.norm(out - y64) / np.linalg.norm(y64) < 2e-3
@@ -171,17 +176,112 @@ def test_device_experts_forward(lib, oracle, fmt):
     x = rng.standard_normal(H).astype(np.float32)
     base = (rng.standard_normal(H) * 0.1).astype(np.float32)
     wd, xd, od = (torch.from_numpy(a.copy()).to(dev) for a in (w, x, base))
-    h = torch.empty(n * I, dtype=torch.float32, device=dev)
-    rc = lib.tgx_kq_experts_forward(*(ctypes.c_void_p(parr[k].data_ptr()) for k in "gud"), fmt, n,
-                                    ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
-                                    ctypes.c_void_p(od.data_ptr()), H, I, 1, ctypes.c_void_p(h.data_ptr()),
-                                    ctypes.c_void_p(s))
-    assert rc == 0, lib.tg_last_error()
+    sb = lib.tgx_kq_scratch_bytes(n, H, I)
+    scratch = torch.zeros(sb, dtype=torch.uint8, device=dev)
+
+    def run(out, flags):
+        rc = lib.tgx_kq_experts_forward(*(ctypes.c_void_p(parr[k].data_ptr()) for k in "gud"), fmt, n,
+                                        ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
+                                        ctypes.c_void_p(out.data_ptr()), H, I, 1, ctypes.c_void_p(scratch.data_ptr()),
+                                        sb, flags, ctypes.c_void_p(s))
+        assert rc == 0, lib.tg_last_error()
+
+    run(od, 0)
+    od2 = torch.from_numpy(base.copy()).to(dev)
+    run(od2, 1)                               # chained behind the previous call: same result
     torch.cuda.synchronize()
     ref = base.copy()
     for e, (g, u, d) in enumerate(experts):
         oracle.expert_forward_k(g, u, d, fmt, x, ref, float(w[e]), H, I)
     assert same_bits(od.cpu().numpy(), ref)
+    assert same_bits(od2.cpu().numpy(), ref)
+    # the row-block counters (the first 16 KB) are left at zero for the next call
+    assert int(scratch[:16384].count_nonzero()) == 0
+
+
+def test_device_scratch_across_shapes(lib, oracle):
+    # one scratch, a large shape then a small one: the small call finds its counters zero
+    import torch
+    dev = torch.device("cuda", 0)
+    s = torch.cuda.current_stream().cuda_stream
+    sb = lib.tgx_kq_scratch_bytes(2, 7168, 2048)
+    scratch = torch.zeros(sb, dtype=torch.uint8, device=dev)
+    rng = np.random.default_rng(5)
+    for H, I in ((7168, 2048), (512, 256), (2048, 768)):
+        ex = [expert(rng, FQ4K, H, I) for _ in range(2)]
+        keep = [[torch.from_numpy(m.copy()).to(dev) for m in e3] for e3 in ex]
+        tab = [torch.tensor([k[j].data_ptr() for k in keep], dtype=torch.int64, device=dev) for j in range(3)]
+        w = np.array([0.25, 0.75], np.float32)
+        x = rng.standard_normal(H).astype(np.float32)
+        wd, xd = torch.from_numpy(w).to(dev), torch.from_numpy(x).to(dev)
+        od = torch.zeros(H, dtype=torch.float32, device=dev)
+        rc = lib.tgx_kq_experts_forward(*(ctypes.c_void_p(t.data_ptr()) for t in tab), 0, 2,
+                                        ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
+                                        ctypes.c_void_p(od.data_ptr()), H, I, 0, ctypes.c_void_p(scratch.data_ptr()),
+                                        sb, 0, ctypes.c_void_p(s))
+        assert rc == 0, lib.tg_last_error()
+        torch.cuda.synchronize()
+        ref = np.zeros(H, np.float32)
+        for e, (g, u, d) in enumerate(ex):
+            oracle.expert_forward_k(g, u, d, FQ4K, x, ref, float(w[e]), H, I)
+        assert same_bits(od.cpu().numpy(), ref), (H, I)
+
+
+def test_device_chain_in_place(lib, oracle):
+    # x_{l+1} = x_l + sum_e w_e expert_e(x_l) over 6 chained layers, out == x, in one
+    # CUDA graph of chained calls: bit-exact to the oracle's sequence
+    import torch
+    H, I, n, L = 2048, 768, 8, 6
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(123)
+    layers = [[tuple(q4k_blocks(rng, I * H // 256, bounded=True) for _ in range(2)) +
+               (q4k_blocks(rng, H * I // 256, bounded=True),) for _ in range(n)] for _ in range(L)]
+    keep, tabs = [], []
+    for lay in layers:
+        ptr = {"g": [], "u": [], "d": []}
+        for g, u, d in lay:
+            for key, m in (("g", g), ("u", u), ("d", d)):
+                t = torch.from_numpy(m.copy()).to(dev)
+                keep.append(t)
+                ptr[key].append(t.data_ptr())
+        tabs.append({k: torch.tensor(v, dtype=torch.int64, device=dev) for k, v in ptr.items()})
+    w = rng.dirichlet(np.ones(n)).astype(np.float32)
+    x0 = (rng.standard_normal(H) * 0.05).astype(np.float32)
+    wd = torch.from_numpy(w).to(dev)
+    xd = torch.from_numpy(x0.copy()).to(dev)
+    sb = lib.tgx_kq_scratch_bytes(n, H, I)
+    scratch = torch.zeros(sb, dtype=torch.uint8, device=dev)
+
+    def token(stream):
+        for l in range(L):
+            rc = lib.tgx_kq_experts_forward(*(ctypes.c_void_p(tabs[l][k].data_ptr()) for k in "gud"), 0, n,
+                                            ctypes.c_void_p(wd.data_ptr()), ctypes.c_void_p(xd.data_ptr()),
+                                            ctypes.c_void_p(xd.data_ptr()), H, I, 1,
+                                            ctypes.c_void_p(scratch.data_ptr()), sb, 1 if l else 0,
+                                            ctypes.c_void_p(stream))
+            assert rc == 0, lib.tg_last_error()
+
+    token(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    eager = xd.cpu().numpy().copy()
+    xd.copy_(torch.from_numpy(x0))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        token(torch.cuda.current_stream().cuda_stream)
+    xd.copy_(torch.from_numpy(x0))
+    graph.replay()
+    torch.cuda.synchronize()
+    replayed = xd.cpu().numpy().copy()
+    del graph
+    ref = x0.copy()
+    for lay in layers:
+        acc = ref.copy()
+        for e, (g, u, d) in enumerate(lay):
+            oracle.expert_forward_k(g, u, d, FQ4K, ref, acc, float(w[e]), H, I)
+        ref = acc
+    assert np.all(np.isfinite(ref))
+    assert same_bits(eager, ref)
+    assert same_bits(replayed, ref)
 
 
 def test_expert_forward_ref_order_within_tolerance(lib, oracle):

@@ -35,6 +35,8 @@ TG_FMT_Q4_0 = 3
 
 TG_NOALLOC_SCRATCH_BYTES = 4194304  # include/tinygiant.h
 
+TGX_KQ_CHAINED = 1
+
 TGX_EAGER = 1
 TGX_MULTI = 2
 
@@ -74,7 +76,8 @@ PROTOTYPES = {
     "tgx_kq_matrix_bytes": (SZ, [CI, ctypes.c_longlong, CI]),
     "tgx_kq_prepare": (CI, [CI, VP, VP, ctypes.c_longlong, CI, VP]),
     "tgx_kq_matvec": (CI, [CI, VP, VP, VP, CI, CI, VP]),
-    "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, VP]),
+    "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
+    "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),
     "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),
     "tg_mlock": (CI, [VP, SZ]),
     "tgx_ctx_create": (CI, [CI, ctypes.POINTER(TgxShape), ctypes.POINTER(VP)]),

@@ -75,7 +75,7 @@ struct HostWS {
     std::mutex mu;
     int device = -1;
     cudaStream_t s = nullptr;
-    DevBuf raw, w, x, out, act, hq, ptrs, wts, i32;
+    DevBuf raw, w, x, out, act, hq, ptrs, wts, i32, kqs;
 
     int bind() {
         int dev = 0;
@@ -90,7 +90,7 @@ struct HostWS {
         return TG_OK;
     }
     void release() {
-        for (DevBuf* b : {&raw, &w, &x, &out, &act, &hq, &ptrs, &wts, &i32}) {
+        for (DevBuf* b : {&raw, &w, &x, &out, &act, &hq, &ptrs, &wts, &i32, &kqs}) {
             if (b->p) cudaFree(b->p);
             b->p = nullptr;
             b->n = 0;
@@ -358,6 +358,11 @@ static int kq_experts_host(const uint8_t* const* gate, const uint8_t* const* up,
     TG_TRY(ensure(W.x, sizeof(float) * embed));
     TG_TRY(ensure(W.out, sizeof(float) * embed));
     TG_TRY(ensure(W.hq, sizeof(float) * (size_t)n * inter));
+    const size_t dsb = tg::kq_down_scratch_bytes(n, embed, inter);
+    if (W.kqs.n < dsb) {   // the row-block counters start at zero; every launch leaves them zero
+        TG_TRY(ensure(W.kqs, dsb));
+        TG_CUDA(cudaMemsetAsync(W.kqs.p, 0, W.kqs.n, W.s));
+    }
     TG_TRY(ensure(W.ptrs, sizeof(void*) * 3 * n));
     TG_TRY(ensure(W.wts, sizeof(float) * n));
     std::vector<const uint8_t*> ptrs(3 * n);
@@ -378,9 +383,9 @@ static int kq_experts_host(const uint8_t* const* gate, const uint8_t* const* up,
     TG_CUDA(cudaMemcpyAsync(W.x.p, input, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
     if (accumulate) TG_CUDA(cudaMemcpyAsync(W.out.p, output, sizeof(float) * embed, cudaMemcpyHostToDevice, W.s));
     const uint8_t* const* dp = (const uint8_t* const*)W.ptrs.p;
-    TG_CUDA(tg::launch_kq_gateup(dp, dp + n, n, (const float*)W.x.p, embed, inter, (float*)W.hq.p, W.s));
+    TG_CUDA(tg::launch_kq_gateup(dp, dp + n, n, (const float*)W.x.p, embed, inter, (float*)W.hq.p, false, W.s));
     TG_CUDA(tg::launch_kq_down(fmt, dp + 2 * n, n, (const float*)W.hq.p, (const float*)W.wts.p, embed, inter,
-                               (float*)W.out.p, accumulate, W.s));
+                               (float*)W.out.p, accumulate, W.kqs.p, W.s));
     TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * embed, cudaMemcpyDeviceToHost, W.s));
     TG_CUDA(cudaStreamSynchronize(W.s));
     return TG_OK;
@@ -1045,15 +1050,23 @@ extern "C" int tgx_kq_matvec(int fmt, const void* W_dev, const float* x_dev, flo
     return TG_OK;
 }
 
+extern "C" size_t tgx_kq_scratch_bytes(int n, int embed, int inter) {
+    if (n < 1 || n > 65535 || !Geom::valid_dims(embed, inter)) return 0;
+    return r256(tg::kq_down_scratch_bytes(n, embed, inter)) + sizeof(float) * (size_t)n * inter;
+}
+
 extern "C" int tgx_kq_experts_forward(const void* const* gate_dev, const void* const* up_dev,
                                       const void* const* down_dev, int down_format, int n, const float* w_dev,
                                       const float* x_dev, float* out_dev, int embed, int inter, int accumulate,
-                                      float* h_dev, void* stream) {
-    TG_CHECK(gate_dev && up_dev && down_dev && w_dev && x_dev && out_dev && h_dev, TG_EINVAL,
+                                      void* scratch, size_t scratch_bytes, int flags, void* stream) {
+    TG_CHECK(gate_dev && up_dev && down_dev && w_dev && x_dev && out_dev && scratch, TG_EINVAL,
              "tgx_kq_experts_forward: null pointer");
     TG_CHECK(n >= 1 && n <= 65535, TG_EINVAL, "tgx_kq_experts_forward: 1 <= n <= 65535");
     TG_CHECK(Geom::valid_dims(embed, inter), TG_EINVAL,
              "tgx_kq_experts_forward: embed/inter must be positive multiples of 256 (<= 16384)");
+    TG_CHECK(scratch_bytes >= tgx_kq_scratch_bytes(n, embed, inter), TG_EINVAL,
+             "tgx_kq_experts_forward: scratch smaller than tgx_kq_scratch_bytes(n, embed, inter)");
+    TG_CHECK(((uintptr_t)scratch & 255) == 0, TG_EINVAL, "tgx_kq_experts_forward: scratch must be 256-byte aligned");
     int fmt;
     switch (down_format) {
         case TG_FMT_Q4_K: fmt = tg::KQ_Q4K; break;
@@ -1062,9 +1075,11 @@ extern "C" int tgx_kq_experts_forward(const void* const* gate_dev, const void* c
         default: return fail(TG_EINVAL, "tgx_kq_experts_forward: down_format must be 0 (Q4_K), 1 (f16) or 2 (Q6_K)");
     }
     cudaStream_t s = (cudaStream_t)stream;
+    void* ds = scratch;
+    float* h = (float*)((uint8_t*)scratch + r256(tg::kq_down_scratch_bytes(n, embed, inter)));
     TG_CUDA(tg::launch_kq_gateup((const uint8_t* const*)gate_dev, (const uint8_t* const*)up_dev, n, x_dev, embed,
-                                 inter, h_dev, s));
-    TG_CUDA(tg::launch_kq_down(fmt, (const uint8_t* const*)down_dev, n, h_dev, w_dev, embed, inter, out_dev,
-                               accumulate, s));
+                                 inter, h, (flags & TGX_KQ_CHAINED) != 0, s));
+    TG_CUDA(tg::launch_kq_down(fmt, (const uint8_t* const*)down_dev, n, h, w_dev, embed, inter, out_dev,
+                               accumulate, ds, s));
     return TG_OK;
 }

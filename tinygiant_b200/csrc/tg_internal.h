@@ -96,11 +96,17 @@ cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk
 // y[rows] = W . x (Q4_K / Q6_K on the 256-wide Q8 blocks of x; f16 / f32 on x).
 cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s);
 // h[e][I] = silu(gate_e . x) * (up_e . x) for n Q4_K experts (device pointer arrays).
+// pdl: start as a programmatic dependent of the previous kernel on s, which must not
+// write the weights or the pointer arrays.
 cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* up, int n, const float* x, int H,
-                             int I, float* h, cudaStream_t s);
-// out[H] = (accumulate ? out : 0) + sum_e w[e] * (down_e . h_e), experts in order.
+                             int I, float* h, bool pdl, cudaStream_t s);
+// out[H] = (accumulate ? out : 0) + sum_e w[e] * (down_e . h_e), experts in order;
+// launched as a programmatic dependent (of the gate/up kernel that writes h).
+// scratch: kq_down_scratch_bytes(n, H, I) bytes (H <= 16384), zero before the first
+// launch; every launch leaves it ready for the next, whatever the shapes.
+size_t kq_down_scratch_bytes(int n, int H, int I);
 cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const float* h, const float* w, int H, int I,
-                           float* out, int accumulate, cudaStream_t s);
+                           float* out, int accumulate, void* scratch, cudaStream_t s);
 // tg_rms_norm in the reference's order (dim a multiple of 4).
 cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s);
 

@@ -11,7 +11,15 @@
 // A lane computes one (row, block) unit; a warp owns whole rows (32 / blocks-per-row
 // of them, or one row when a row has more than 32 blocks), so the chain of a row's
 // block terms runs in one lane and no step crosses warps.  A warp stages its units'
-// bytes into shared memory with coalesced 16-byte loads before computing.
+// bytes into shared memory with coalesced 16-byte cp.async copies, issued before the
+// kernel waits for its inputs: every launch is a programmatic dependent launch, so a
+// kernel's weight fetch overlaps the tail of the kernel before it, and only the reads
+// of x / h wait (griddepcontrol.wait) for that kernel to complete.
+//
+// The expert down kernel runs one CTA per (row block, expert); each writes its rows'
+// y_e to scratch, and the last CTA of a row block to arrive (a counter per row block,
+// reset by that CTA) adds the experts' terms in expert order, so the combine keeps
+// the reference's sequential order without any CTA waiting on another.
 //
 // Device layouts: Q4_K as ggml blocks (144 B, so every block is 16-byte aligned);
 // Q6_K "split": the 208-byte bodies (ql | qh | scales) of all blocks of the matrix,
@@ -30,7 +38,6 @@ constexpr int KW = 4;                 // warps per CTA
 constexpr int KT = KW * 32;
 constexpr int Q4K_B = 144, Q6K_BODY = 208, Q6K_B = 210;
 constexpr int XC = 272;               // stride of a block's 256 codes in shared memory (bank spread)
-constexpr int STAGE = 32 * Q6K_BODY;  // staging bytes per warp (32 units of the largest body)
 constexpr int FROWS = 4;              // rows per warp of the f16 / f32 matvec (8 lanes per row)
 constexpr int FCH = 256;              // columns staged per step
 // FMT values: KQ_Q4K 0, KQ_F16 1, KQ_Q6K 2, KQ_F32 4 (tg_internal.h)
@@ -54,8 +61,21 @@ __host__ __device__ inline int terms_per_warp(int cols) {
     int bpr = cols / 256;
     return bpr > 32 ? bpr : 32;
 }
-__host__ __device__ inline size_t kq_smem(int fmt, int cols) {
-    return act_region(fmt, cols) + (size_t)KW * (STAGE + r16((size_t)terms_per_warp(cols) * 4));
+// Staging bytes of one warp: 32 units of the format's block (Q4_K 144 B, Q6_K body
+// 208 B) or four padded rows of 256 values (f16 / f32).
+__host__ __device__ constexpr int stage_bytes(int fmt) {
+    return fmt == KQ_Q4K ? 32 * Q4K_B : fmt == KQ_Q6K ? 32 * Q6K_BODY : 4 * (FCH * (fmt == KQ_F16 ? 2 : 4) + 16);
+}
+// stages per warp: gate and up (MODE 1), else one
+__host__ __device__ inline size_t warp_bytes(int fmt, int mode, int cols) {
+    return (size_t)(mode == 1 ? 2 : 1) * stage_bytes(fmt) + r16((size_t)terms_per_warp(cols) * 4);
+}
+__host__ __device__ inline size_t kq_smem(int fmt, int mode, int cols) {
+    return act_region(fmt, cols) + (size_t)KW * warp_bytes(fmt, mode, cols);
+}
+__host__ __device__ inline int rows_per_warp(int fmt, int cols) {
+    int bpr = cols / 256;
+    return (fmt == KQ_F16 || fmt == KQ_F32) ? FROWS : (bpr >= 32 ? 1 : 32 / bpr);
 }
 
 __device__ inline KAct act_at(uint8_t* base, int bpr) {
@@ -205,28 +225,54 @@ __device__ __forceinline__ float q6k_term(const uint8_t* body, float d, const KA
     return __fmul_rn(__fmul_rn(d, a.sx[b]), bs);
 }
 
-// Coalesced copy of `bytes` (a multiple of 16, both ends 16-byte aligned) into the
-// warp's staging area.
-__device__ __forceinline__ void stage_copy(uint8_t* dst, const uint8_t* __restrict__ src, int bytes, int lane) {
-    const uint4* s = reinterpret_cast<const uint4*>(src);
-    uint4* d = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Programmatic dependent launch: let the next kernel in the stream start, and wait
+// for the previous one to complete (both return at once outside such launches).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Asynchronous coalesced copy of `bytes` (a multiple of 16, both ends 16-byte
+// aligned) into a warp's staging area; one commit group per call.
+__device__ __forceinline__ void stage_issue(uint8_t* dst, const uint8_t* __restrict__ src, int bytes, int lane) {
     const int n = bytes >> 4;
-    for (int i = lane; i < n; i += 32) d[i] = __ldg(s + i);
+    for (int i = lane; i < n; i += 32) cp_async16(dst + 16 * i, src + 16 * i);
+    cp_async_commit();
+}
+
+// Quantised rows [r0, r0 + nr) of matrix M: issue the copy of their units when they
+// fit one chunk (32 units); returns whether it did.
+template <int FMT>
+__device__ __forceinline__ bool kq_issue(const uint8_t* __restrict__ M, int bpr, int r0, int nr, uint8_t* stage,
+                                         int lane) {
+    constexpr int BB = FMT == KQ_Q4K ? Q4K_B : Q6K_BODY;
+    const int units = nr * bpr;
+    if (units == 0 || units > 32) return false;
+    stage_issue(stage, M + (size_t)r0 * bpr * BB, units * BB, lane);
+    return true;
 }
 
 // Rows [r0, r0 + nr) of a quantised matrix against activation a: returns the row
-// total of row r0 + lane in lanes < nr (0 elsewhere).
+// total of row r0 + lane in lanes < nr (0 elsewhere).  `issued`: the first chunk is
+// already in flight (kq_issue).
 template <int FMT>
 __device__ float kq_rows_warp(const uint8_t* __restrict__ M, long long nblk, int bpr, int r0, int nr,
-                              const KAct& a, uint8_t* stage, float* terms, int lane) {
+                              const KAct& a, uint8_t* stage, float* terms, int lane, bool issued) {
     constexpr int BB = FMT == KQ_Q4K ? Q4K_B : Q6K_BODY;
     const long long ubase = (long long)r0 * bpr;
     const int units = nr * bpr;
     const uint16_t* d6 = reinterpret_cast<const uint16_t*>(M + (size_t)nblk * Q6K_BODY);
     for (int c = 0; c < units; c += 32) {
         const int cnt = min(32, units - c);
-        __syncwarp();
-        stage_copy(stage, M + (size_t)(ubase + c) * BB, cnt * BB, lane);
+        if (!(issued && c == 0)) {
+            __syncwarp();
+            stage_issue(stage, M + (size_t)(ubase + c) * BB, cnt * BB, lane);
+        }
+        cp_async_wait_all();
         __syncwarp();
         if (lane < cnt) {
             const int b = (c + lane) % bpr;
@@ -237,8 +283,8 @@ __device__ float kq_rows_warp(const uint8_t* __restrict__ M, long long nblk, int
                 t = q6k_term(stage + lane * BB, f16_bits_to_f32(__ldg(d6 + ubase + c + lane)), a, b);
             terms[c + lane] = t;
         }
+        __syncwarp();
     }
-    __syncwarp();
     float tot = 0.0f;
     if (lane < nr)
         for (int j = 0; j < bpr; j++) tot = __fadd_rn(tot, terms[lane * bpr + j]);
@@ -263,9 +309,10 @@ __device__ float fx_rows_warp(const uint8_t* __restrict__ M, int cols, int r0, i
         __syncwarp();
         for (int i = lane; i < nr * per_row; i += 32) {
             const int r = i / per_row, k = i - r * per_row;
-            const uint4* s = reinterpret_cast<const uint4*>(M + ((size_t)(r0 + r) * cols + c0) * ES) + k;
-            *reinterpret_cast<uint4*>(stage + r * RS + k * 16) = __ldg(s);
+            cp_async16(stage + r * RS + k * 16, M + ((size_t)(r0 + r) * cols + c0) * ES + 16 * k);
         }
+        cp_async_commit();
+        cp_async_wait_all();
         __syncwarp();
         if (ri < nr) {
             const uint8_t* row = stage + ri * RS;
@@ -290,66 +337,88 @@ struct KQParams {
     const float* x;               // MODE 0 / 1: input [cols]; MODE 2: h [n][cols]
     const float* w;               // MODE 2: combine weights [n]
     float* out;                   // MODE 0: y [rows]; MODE 1: h [n][rows]; MODE 2: out [rows]
+    float* ys;                    // MODE 2: per-expert rows y [n][rows]
+    unsigned* cnt;                // MODE 2: arrivals per row block (zero between launches)
     int rows, cols, n, accumulate;
 };
 
 // MODE 0: y = M . x.  MODE 1 (grid.y = expert e): h_e = silu(gate_e . x) * (up_e . x),
-// gate / up Q4_K.  MODE 2: out = (accumulate ? out : 0) + sum_e w_e * (down_e . h_e),
+// gate / up Q4_K.  MODE 2 (grid.y = expert e): y_e = down_e . h_e into ys; the last
+// CTA of each row block then writes out = (accumulate ? out : 0) + sum_e w_e * y_e,
 // experts added in order.
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(KT) k_kq(KQParams p) {
     extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int s_last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool FLOAT_FMT = FMT == KQ_F16 || FMT == KQ_F32;
+    constexpr int SB = stage_bytes(FMT);
     const int cols = p.cols, bpr = cols / 256;
     uint8_t* act = sm;
-    uint8_t* stage = sm + act_region(FMT, cols) + (size_t)warp * (STAGE + r16((size_t)terms_per_warp(cols) * 4));
-    float* terms = reinterpret_cast<float*>(stage + STAGE);
+    uint8_t* stage = sm + act_region(FMT, cols) + (size_t)warp * warp_bytes(FMT, MODE, cols);
+    float* terms = reinterpret_cast<float*>(stage + (MODE == 1 ? 2 : 1) * SB);
     const KAct a = act_at(act, bpr);
     float* xs = reinterpret_cast<float*>(act);
-    const int rpw = FLOAT_FMT ? FROWS : (bpr >= 32 ? 1 : 32 / bpr);
+    const int rpw = rows_per_warp(FMT, cols);
     const int r0 = (blockIdx.x * KW + warp) * rpw;
     const int nr = r0 < p.rows ? min(rpw, p.rows - r0) : 0;
     const long long nblk = (long long)p.rows * bpr;
     const bool has = FLOAT_FMT ? ((lane & 7) == 0 && (lane >> 3) < nr) : lane < nr;
     const int row = r0 + (FLOAT_FMT ? (lane >> 3) : lane);
+    const int e = blockIdx.y;
+    const uint8_t* M0 = MODE == 0 ? p.mat : p.A[e];
 
-    auto load_act = [&](const float* x) {
-        __syncthreads();
-        if constexpr (FLOAT_FMT) {
-            for (int i = threadIdx.x; i < cols / 4; i += KT)
-                reinterpret_cast<float4*>(xs)[i] = __ldg(reinterpret_cast<const float4*>(x) + i);
-        } else {
-            quantize_q8k(x, bpr, a, warp, lane);
-        }
-        __syncthreads();
-    };
-    auto rows_dot = [&](const uint8_t* M) -> float {
+    pdl_trigger();
+    // weights do not depend on the previous kernel: start their copies first
+    bool issued0 = false, issued1 = false;
+    if constexpr (!FLOAT_FMT) {
+        issued0 = kq_issue<FMT>(M0, bpr, r0, nr, stage, lane);
+        if constexpr (MODE == 1) issued1 = kq_issue<FMT>(p.B[e], bpr, r0, nr, stage + SB, lane);
+    }
+    pdl_wait();
+    const float* xin = MODE == 2 ? p.x + (size_t)e * cols : p.x;
+    if constexpr (FLOAT_FMT) {
+        for (int i = threadIdx.x; i < cols / 4; i += KT)
+            reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(xin)[i];
+    } else {
+        quantize_q8k(xin, bpr, a, warp, lane);
+    }
+    __syncthreads();
+
+    auto rows_dot = [&](const uint8_t* M, uint8_t* st, bool issued) -> float {
         if (nr == 0) return 0.0f;
         if constexpr (FLOAT_FMT)
-            return fx_rows_warp<FMT>(M, cols, r0, nr, xs, stage, lane);
+            return fx_rows_warp<FMT>(M, cols, r0, nr, xs, st, lane);
         else
-            return kq_rows_warp<FMT>(M, nblk, bpr, r0, nr, a, stage, terms, lane);
+            return kq_rows_warp<FMT>(M, nblk, bpr, r0, nr, a, st, terms, lane, issued);
     };
 
-    if (MODE == 0) {
-        load_act(p.x);
-        float y = rows_dot(p.mat);
+    if constexpr (MODE == 0) {
+        float y = rows_dot(M0, stage, issued0);
         if (has) p.out[row] = y;
-    } else if (MODE == 1) {
-        const int e = blockIdx.y;
-        load_act(p.x);
-        float g = rows_dot(p.A[e]);
-        float u = rows_dot(p.B[e]);
+    } else if constexpr (MODE == 1) {
+        float g = rows_dot(M0, stage, issued0);
+        float u = rows_dot(p.B[e], stage + SB, issued1);
         if (has) p.out[(size_t)e * p.rows + row] = silu_mul(g, u);
     } else {
-        float acc = has && p.accumulate ? p.out[row] : 0.0f;
-        for (int e = 0; e < p.n; e++) {
-            load_act(p.x + (size_t)e * cols);
-            float y = rows_dot(p.A[e]);
-            if (has) acc = __fadd_rn(acc, __fmul_rn(__ldg(p.w + e), y));
+        float y = rows_dot(M0, stage, issued0);
+        if (has) p.ys[(size_t)e * p.rows + row] = y;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(p.cnt + blockIdx.x, 1u) == (unsigned)(p.n - 1);
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            const int rb = rpw * KW;
+            const int lo = blockIdx.x * rb, hi = min(p.rows, lo + rb);
+            for (int r = lo + threadIdx.x; r < hi; r += KT) {
+                float acc = p.accumulate ? p.out[r] : 0.0f;
+                for (int j = 0; j < p.n; j++)
+                    acc = __fadd_rn(acc, __fmul_rn(__ldg(p.w + j), __ldcg(p.ys + (size_t)j * p.rows + r)));
+                p.out[r] = acc;
+            }
+            if (threadIdx.x == 0) p.cnt[blockIdx.x] = 0u;
         }
-        if (has) p.out[row] = acc;
     }
 }
 
@@ -389,29 +458,41 @@ __global__ void k_rms_norm_ref(const float* __restrict__ x, const float* __restr
     for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
 }
 
+int row_blocks(int fmt, int rows, int cols) {
+    const int rb = rows_per_warp(fmt, cols) * KW;
+    return (rows + rb - 1) / rb;
+}
+
+// pdl: launch as a programmatic dependent of the previous kernel on the stream (its
+// weight copies start before that kernel completes).  Only for a previous kernel that
+// does not write this launch's weights or pointer arrays.
 template <int FMT, int MODE>
-cudaError_t launch_kq_t(const KQParams& p, int grid_y, cudaStream_t s) {
-    const size_t smem = kq_smem(FMT, p.cols);
+cudaError_t launch_kq_t(const KQParams& p, int grid_y, bool pdl, cudaStream_t s) {
+    const size_t smem = kq_smem(FMT, MODE, p.cols);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(k_kq<FMT, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    const bool flt = FMT == KQ_F16 || FMT == KQ_F32;
-    const int bpr = p.cols / 256;
-    const int rpw = flt ? FROWS : (bpr >= 32 ? 1 : 32 / bpr);
-    const int rows_per_cta = rpw * KW;
-    dim3 grid((p.rows + rows_per_cta - 1) / rows_per_cta, grid_y);
-    k_kq<FMT, MODE><<<grid, KT, smem, s>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(row_blocks(FMT, p.rows, p.cols), grid_y);
+    cfg.blockDim = dim3(KT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_kq<FMT, MODE>, p);
 }
 
 template <int MODE>
-cudaError_t launch_kq_fmt(int fmt, const KQParams& p, int grid_y, cudaStream_t s) {
+cudaError_t launch_kq_fmt(int fmt, const KQParams& p, int grid_y, bool pdl, cudaStream_t s) {
     switch (fmt) {
-        case KQ_Q4K: return launch_kq_t<KQ_Q4K, MODE>(p, grid_y, s);
-        case KQ_Q6K: return launch_kq_t<KQ_Q6K, MODE>(p, grid_y, s);
-        case KQ_F16: return launch_kq_t<KQ_F16, MODE>(p, grid_y, s);
-        case KQ_F32: return launch_kq_t<KQ_F32, MODE>(p, grid_y, s);
+        case KQ_Q4K: return launch_kq_t<KQ_Q4K, MODE>(p, grid_y, pdl, s);
+        case KQ_Q6K: return launch_kq_t<KQ_Q6K, MODE>(p, grid_y, pdl, s);
+        case KQ_F16: return launch_kq_t<KQ_F16, MODE>(p, grid_y, pdl, s);
+        case KQ_F32: return launch_kq_t<KQ_F32, MODE>(p, grid_y, pdl, s);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -435,7 +516,20 @@ size_t kq_matrix_bytes(int fmt, long long rows, int cols) {
     }
 }
 
-size_t kq_smem_bytes(int fmt, int cols) { return kq_smem(fmt, cols); }
+size_t kq_smem_bytes(int fmt, int cols) {
+    size_t a = kq_smem(fmt, 0, cols), b = kq_smem(fmt, 2, cols);
+    return a > b ? a : b;
+}
+
+// Down scratch: the row-block arrival counters first, in a fixed region large enough
+// for any shape (at least 4 rows per CTA, H <= 16384), so counters left at zero by
+// one shape are zero for every other; then y [n][H].
+constexpr size_t KQ_CNT_BYTES = 16384 / 4 * 4;
+
+size_t kq_down_scratch_bytes(int n, int H, int I) {
+    (void)I;
+    return KQ_CNT_BYTES + r16((size_t)n * H * 4);
+}
 
 cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk, cudaStream_t s) {
     if (nblk <= 0) return cudaSuccess;
@@ -454,11 +548,11 @@ cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y
     p.rows = rows;
     p.cols = cols;
     p.n = 1;
-    return launch_kq_fmt<0>(fmt, p, 1, s);
+    return launch_kq_fmt<0>(fmt, p, 1, false, s);
 }
 
 cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* up, int n, const float* x, int H,
-                             int I, float* h, cudaStream_t s) {
+                             int I, float* h, bool pdl, cudaStream_t s) {
     KQParams p{};
     p.A = gate;
     p.B = up;
@@ -467,21 +561,23 @@ cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* u
     p.rows = I;
     p.cols = H;
     p.n = n;
-    return launch_kq_t<KQ_Q4K, 1>(p, n, s);
+    return launch_kq_t<KQ_Q4K, 1>(p, n, pdl, s);
 }
 
 cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const float* h, const float* w, int H, int I,
-                           float* out, int accumulate, cudaStream_t s) {
+                           float* out, int accumulate, void* scratch, cudaStream_t s) {
     KQParams p{};
     p.A = down;
     p.x = h;
     p.w = w;
     p.out = out;
+    p.cnt = (unsigned*)scratch;
+    p.ys = (float*)((uint8_t*)scratch + KQ_CNT_BYTES);
     p.rows = H;
     p.cols = I;
     p.n = n;
     p.accumulate = accumulate;
-    return launch_kq_fmt<2>(fmt, p, 1, s);
+    return launch_kq_fmt<2>(fmt, p, n, true, s);
 }
 
 cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s) {
