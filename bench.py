@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--tier", type=int, default=-1,
                     help="P >= 0: host tier with P experts per layer pinned in HBM, Zipf(1.1) routing (configs[3])")
     ap.add_argument("--cache-slots", type=int, default=24, help="HBM cache slots of the host tier")
+    ap.add_argument("--ep", action="store_true",
+                    help="expert parallelism: under torchrun each rank holds E/N experts of every layer and "
+                         "the ranks decode the same --tokens T tokens together (NCCL all-reduce per layer)")
     ap.add_argument("--format", choices=["q4_0", "q4_k", "q4_k_m"], default="q4_0",
                     help="q4_k / q4_k_m: the reference library's own formats (all-Q4_K experts, or Q4_K "
                          "gate/up with Q6_K down), expert FFN of 48 layers x top-8 per token")
@@ -701,10 +704,112 @@ def run_kquant(args):
     return 0
 
 
+def run_ep(args):
+    """Expert parallelism (configs 3 / 5 at the Qwen3 shape): rank r holds experts
+    [r*E/N, (r+1)*E/N) of all 48 layers; every rank routes the same T tokens, runs its
+    local experts, the ranks all-reduce the per-(token, slot) outputs over NCCL and
+    combine in slot order.  The job processes T tokens per step (strong scaling)."""
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = init_dist(ws, "nccl") if ws > 1 else None
+    T, NL = args.tokens, args.layers
+    ep = EPMoEModel(H, I, E, K_TOP, NL, rank=rank, size=ws, device=local)
+    ep.fill_synthetic(args.seed)                          # one model, sharded: the same seed on every rank
+    K, W = args.steps, max(3, args.warmup)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed + 1)
+    pool = [torch.randn(T, H, generator=gen, device="cuda") for _ in range(4)]
+    X = torch.empty(T, H, device="cuda")
+    stream = torch.cuda.current_stream()
+    X.copy_(pool[0])
+    ep.decode(X)                                          # allocates scratch and the exchange buffer
+    torch.cuda.synchronize()
+    graph, graphed = torch.cuda.CUDAGraph(), False
+    try:
+        with torch.cuda.graph(graph):
+            ep.decode(X)
+        graphed = True
+    except Exception:                                     # eager launches otherwise (same kernels)
+        graph = None
+    torch.cuda.synchronize()
+
+    def step():
+        if graphed:
+            graph.replay()
+        else:
+            ep.decode(X)
+
+    for i in range(W):
+        X.copy_(pool[i % 4])
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(K):
+        X.copy_(pool[i % 4])
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    Xh = pool[1].cpu().pin_memory()
+    Yh = torch.empty_like(Xh).pin_memory()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ke = max(1, K // 4)
+    e0.record(stream)
+    for i in range(ke):
+        X.copy_(Xh, non_blocking=True)
+        step()
+        Yh.copy_(X, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([ms, ems], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ems = float(t[0]), float(t[1])
+    assert torch.isfinite(Yh).all()
+    del graph                                             # holds NCCL calls: released before the group
+    ep.close()
+    if rank == 0:
+        distinct = min(E, T * K_TOP)
+        print(json.dumps({
+            "metric": f"expert-parallel MoE decode tok/s (Qwen3-30B-A3B shape, {T} tokens per step, EP over {ws} GPUs)",
+            "value": T * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"configs[2]/[4]: {T} tokens per step, {NL} layers, experts sharded {E // ws} "
+                                   f"per GPU, NCCL all-reduce of y per layer",
+                       "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "layers": NL, "tokens": T,
+                       "parallelism": f"ep{ws}", "cuda_graph": graphed},
+            "exchange_bytes_per_layer": T * K_TOP * H * 4,
+            "weights_read_upper_bound_gbs_per_gpu": NL * min(E // ws, distinct) * EXPERT_BYTES / (ms / K / 1000.0) / 1e9,
+            "e2e": {"value": T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
+                    "d2h_bytes_per_step": T * H * 4},
+            "gpu_launches": 6 * NL * K,
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.ep:
+        return run_ep(args)
     if args.format != "q4_0":
         return run_kquant(args)
     if args.tier >= 0:

@@ -238,6 +238,34 @@ int tgx_fused_info(tgx_ctx *ctx, int *ctas, int *smem_bytes, int *arena_bytes);
  * Synchronises the context's device. */
 int tgx_last_routing(tgx_ctx *ctx, int layer, int32_t *idx, float *w, float *logits);
 
+/* ===================== experts sharded over devices ===================== */
+
+/* Expert parallelism: rank r of G holds experts [r*E/G, (r+1)*E/G) of every layer
+ * (n_experts % G == 0); routers and FFN norms are replicated.  One MoE layer for T
+ * tokens x_dev[T][embed] (tinygiant/engine.py:229-258 per token):
+ *   tgx_ep_moe_partial(ep, layer, x, T, y, s)  every rank: the same routing, then
+ *       y[(t, j)][embed] for the pairs (token t, slot j) whose expert it holds, 0 for
+ *       the others (y: tgx_ep_y_floats(ep, T) floats, caller-owned);
+ *   sum y over the ranks (an NCCL all-reduce, or any exact sum: each element has one
+ *       nonzero contribution);
+ *   tgx_ep_combine(ep, x, T, y, s)  x[t] += sum_j w[t][j] * y[(t, j)] in slot order.
+ * The result equals tgx_moe_batched on one device with all experts, bit for bit.
+ * The first partial call for a larger T allocates scratch (make it before any graph
+ * capture). */
+typedef struct tgx_ep tgx_ep;
+int tgx_ep_create(int device, const tgx_shape *shape, int ep_rank, int ep_size, tgx_ep **out);
+int tgx_ep_destroy(tgx_ep *ep);
+int tgx_ep_expert_range(const tgx_ep *ep, int *first, int *n);
+/* experts [first, first + n) of a layer (global ids inside this rank's range), ggml blobs */
+int tgx_ep_load_experts(tgx_ep *ep, int layer, int first, int n, const void *src, int src_on_device);
+int tgx_ep_set_router(tgx_ep *ep, int layer, const float *R, int src_on_device);
+int tgx_ep_set_ffn_norm(tgx_ep *ep, int layer, const float *w, int src_on_device);
+/* the values tgx_fill_synthetic gives the same experts of a full model */
+int tgx_ep_fill_synthetic(tgx_ep *ep, uint64_t seed, float w_sigma, float r_sigma);
+size_t tgx_ep_y_floats(const tgx_ep *ep, int T);
+int tgx_ep_moe_partial(tgx_ep *ep, int layer, const float *x_dev, int T, float *y_dev, void *stream);
+int tgx_ep_combine(tgx_ep *ep, float *x_dev, int T, const float *y_dev, void *stream);
+
 /* ===================== the reference's formats on device pointers ===================== */
 
 /* Device bytes of a rows x cols matrix of format fmt (0 Q4_K, 1 f16, 2 Q6_K, 4 f32;

@@ -76,6 +76,16 @@ PROTOTYPES = {
     "tgx_kq_matrix_bytes": (SZ, [CI, ctypes.c_longlong, CI]),
     "tgx_kq_prepare": (CI, [CI, VP, VP, ctypes.c_longlong, CI, VP]),
     "tgx_kq_matvec": (CI, [CI, VP, VP, VP, CI, CI, VP]),
+    "tgx_ep_create": (CI, [CI, ctypes.POINTER(TgxShape), CI, CI, ctypes.POINTER(VP)]),
+    "tgx_ep_destroy": (CI, [VP]),
+    "tgx_ep_expert_range": (CI, [VP, ctypes.POINTER(CI), ctypes.POINTER(CI)]),
+    "tgx_ep_load_experts": (CI, [VP, CI, CI, CI, VP, CI]),
+    "tgx_ep_set_router": (CI, [VP, CI, VP, CI]),
+    "tgx_ep_set_ffn_norm": (CI, [VP, CI, VP, CI]),
+    "tgx_ep_fill_synthetic": (CI, [VP, U64, CF, CF]),
+    "tgx_ep_y_floats": (SZ, [VP, CI]),
+    "tgx_ep_moe_partial": (CI, [VP, CI, VP, CI, VP, VP]),
+    "tgx_ep_combine": (CI, [VP, VP, CI, VP, VP]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),
     "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),

@@ -116,8 +116,9 @@ __global__ void __launch_bounds__(256) k_topk_quant_batched(const float* __restr
 
 // one CTA of 256 threads: pairs p = t * k + j grouped by expert idx[p]; off[E + 1],
 // list[T * k] (the order inside a group does not affect any result) and the active experts
-__global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int E,
-                                                     int* __restrict__ off, int* __restrict__ list,
+// among those this device holds, [e_lo, e_lo + e_n)
+__global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int E, int e_lo,
+                                                     int e_n, int* __restrict__ off, int* __restrict__ list,
                                                      int* __restrict__ active) {
     __shared__ int cnt[1024];
     __shared__ int pos[1024];
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx
             off[e] = acc;
             pos[e] = acc;
             acc += cnt[e];
-            if (cnt[e]) active[1 + na++] = e;
+            if (cnt[e] && e >= e_lo && e < e_lo + e_n) active[1 + na++] = e;
         }
         off[E] = acc;
         active[0] = na;   // active[1 .. na]: the experts with tokens, ascending
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx
 // stages rows 32c .. 32c+31 of its
 // gate and up in shared memory, then for every pair p routed to e: 4 rows per warp,
 // h = silu(g) * u, and h's Q8_0 block c into hq[p].
-__global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer, Geom g,
+__global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer, int e_lo, Geom g,
                                                         const int* __restrict__ off, const int* __restrict__ list,
                                                         const int* __restrict__ active, int k,
                                                         const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq) {
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
     const int p0 = off[e], n = off[e + 1] - p0;
     if (n == 0) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint8_t* eb = layer + (size_t)e * g.expert_bytes;
+    const uint8_t* eb = layer + (size_t)(e - e_lo) * g.expert_bytes;
     const size_t unit = (size_t)32 * g.row_gu;
     {
         const int4* sg = reinterpret_cast<const int4*>(eb + (size_t)c * unit);
@@ -213,7 +214,7 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
 // grid (H / 16, min(E, T * k)), 256 threads.  CTA (rb, a) takes the a-th active expert e,
 // stages its down rows 16rb .. 16rb+15, then for every pair p routed to e: 2 rows per
 // warp, y[p][r] = row . hq[p].
-__global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer, Geom g,
+__global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer, int e_lo, Geom g,
                                                       const int* __restrict__ off, const int* __restrict__ list,
                                                       const int* __restrict__ active, const uint8_t* __restrict__ hq,
                                                       float* __restrict__ y) {
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
     const int r0 = rb * DOWN_ROWS;
     const int nrows = min(DOWN_ROWS, g.H - r0);
     {
-        const int4* src = reinterpret_cast<const int4*>(layer + (size_t)e * g.expert_bytes + 2 * g.t_gu +
+        const int4* src = reinterpret_cast<const int4*>(layer + (size_t)(e - e_lo) * g.expert_bytes + 2 * g.t_gu +
                                                         (size_t)r0 * g.row_d);
         int4* d = reinterpret_cast<int4*>(smem);
         const int n16 = (int)((size_t)nrows * g.row_d / 16);
@@ -275,17 +276,26 @@ size_t batched_smem_bytes(const Geom& g) {
     return m + 256;
 }
 
-size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
+// scratch of the partial step (router sums, activations, routing, pair lists, h)
+size_t batched_partial_bytes(const Geom& g, int E, int k, int T) {
     const size_t n_pairs = (size_t)T * k;
-    return (size_t)T * E * 8 + (size_t)(E + 1) * 4 + (size_t)T * act_bytes(g.nbH) + n_pairs * 8 + (E + 1) * 4 + n_pairs * 4 +
-           n_pairs * act_bytes(g.nbI) + n_pairs * g.H * 4 + (size_t)T * E * 4 + 8 * 256;
+    auto r = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    return r((size_t)T * E * 8) + r((size_t)(E + 1) * 4) + r((size_t)T * act_bytes(g.nbH)) + r(n_pairs * 4) +
+           r(n_pairs * 4) + r((size_t)(E + 1) * 4) + r(n_pairs * 4) + r(n_pairs * act_bytes(g.nbI));
 }
 
-cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
-                               int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
-                               float* w_out, float* logits_out, cudaStream_t s) {
+size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
+    const size_t n_pairs = (size_t)T * k;
+    return batched_partial_bytes(g, E, k, T) + ((n_pairs * 4 + 255) & ~(size_t)255) + n_pairs * g.H * 4;
+}
+
+cudaError_t launch_moe_batched_partial(const uint8_t* layer, int e_lo, int e_n, Geom g, const float* R,
+                                       const float* normw, float eps, int E, int k, const float* X, int T,
+                                       void* scratch, size_t scratch_bytes, float* y, int* idx_out, float* w_out,
+                                       float* logits_out, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || batched_scratch_bytes(g, E, k, T) > scratch_bytes)
+    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || e_lo < 0 || e_n < 0 || e_lo + e_n > E ||
+        batched_partial_bytes(g, E, k, T) > scratch_bytes)
         return cudaErrorInvalidValue;
     const size_t n_pairs = (size_t)T * k;
     uint8_t* p = static_cast<uint8_t*>(scratch);
@@ -302,30 +312,56 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
     int* off = reinterpret_cast<int*>(take((E + 1) * 4));
     int* list = reinterpret_cast<int*>(take(n_pairs * 4));
     uint8_t* hq = take(n_pairs * act_bytes(g.nbI));
-    float* y = reinterpret_cast<float*>(take(n_pairs * g.H * 4));
 
     cudaError_t e;
     if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
+    // pairs routed to experts held elsewhere keep y = 0 (their owner adds theirs)
+    if (e_n < E && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
     k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
                                                                                                 g.H, S);
     k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, S, idx, wts, logits_out, xq);
-    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, E, off, list, active);
-    const int n_act = (int)(n_pairs < (size_t)E ? n_pairs : (size_t)E);
+    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, E, e_lo, e_n, off, list, active);
+    const int n_act = (int)(n_pairs < (size_t)e_n ? n_pairs : (size_t)e_n);
+    if (n_act == 0) return cudaGetLastError();
     const size_t sm_gu = (size_t)2 * 32 * g.row_gu;
     if (sm_gu > 48 * 1024 &&
         (e = cudaFuncSetAttribute(k_gateup_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
             cudaSuccess)
         return e;
-    k_gateup_batched<<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, g, off, list, active, k, xq, hq);
+    k_gateup_batched<<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, e_lo, g, off, list, active, k, xq, hq);
     const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
     if (sm_d > 48 * 1024 &&
         (e = cudaFuncSetAttribute(k_down_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_d)) !=
             cudaSuccess)
         return e;
-    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, g, off, list, active,
-                                                                                      hq, y);
-    k_combine_batched<<<T, 256, 0, s>>>(X, g.H, k, wts, y);
+    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, e_lo, g, off, list,
+                                                                                      active, hq, y);
     return cudaGetLastError();
+}
+
+cudaError_t launch_moe_batched_combine(float* X, int T, int H, int k, const float* wts, const float* y,
+                                       cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    k_combine_batched<<<T, 256, 0, s>>>(X, H, k, wts, y);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
+                               int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
+                               float* w_out, float* logits_out, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || batched_scratch_bytes(g, E, k, T) > scratch_bytes)
+        return cudaErrorInvalidValue;
+    // the partial step's buffers, then w (unless given) and y at the end of the scratch
+    const size_t n_pairs = (size_t)T * k;
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    const size_t part = batched_partial_bytes(g, E, k, T);
+    float* wts = w_out ? w_out : reinterpret_cast<float*>(base + part);
+    float* y = reinterpret_cast<float*>(base + part + ((n_pairs * 4 + 255) & ~(size_t)255));
+    cudaError_t e = launch_moe_batched_partial(layer, 0, E, g, R, normw, eps, E, k, X, T, scratch, part, y, idx_out,
+                                               wts, logits_out, s);
+    if (e != cudaSuccess) return e;
+    return launch_moe_batched_combine(X, T, g.H, k, wts, y, s);
 }
 
 }  // namespace tg

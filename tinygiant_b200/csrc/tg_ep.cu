@@ -1,0 +1,272 @@
+// tg_ep.cu — experts sharded over devices (expert parallelism), one context per rank.
+//
+// Rank r of G holds experts [r * E/G, (r + 1) * E/G) of every layer; routers and
+// norms are replicated.  A layer for T tokens is
+//   tgx_ep_moe_partial   routing (the same on every rank), then y[(t, j)] for the
+//                        pairs whose expert is local, 0 for the others
+//   (caller)             sum of y over the ranks: an all-reduce (NCCL) or any exact sum
+//   tgx_ep_combine       x[t] += sum_j w[t][j] * y[(t, j)] in slot order
+// Every element of y has exactly one nonzero contribution and sums start from +0, so
+// the all-reduce is exact and the result equals the single-device path bit for bit
+// (tinygiant/engine.py:229-258 per token, the reference's sequential combine).
+#include <cuda_runtime.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/tinygiant.h"
+#include "tg_internal.h"
+
+using tg::Geom;
+
+struct tgx_ep {
+    int device = 0, rank = 0, size = 1, e_lo = 0, e_n = 0;
+    tgx_shape shape{};
+    Geom g;
+    float eps = 1e-6f;
+    size_t layer_bytes = 0;       // e_n experts
+    uint8_t* weights = nullptr;   // [L][e_n] local experts, row-split
+    float* routers = nullptr;     // [L][E][H]
+    float* norms = nullptr;       // [L][H]
+    uint8_t* staging = nullptr;
+    size_t staging_bytes = 0;
+    void* scratch = nullptr;      // partial-step scratch, grown on demand
+    size_t scratch_bytes = 0;
+    float* wts = nullptr;         // [T][k] routing weights of the last partial step
+    size_t wts_bytes = 0;
+    int last_T = 0;
+    cudaStream_t s = nullptr;
+};
+
+namespace {
+
+int ep_fail(int code, const std::string& msg) { return tg::set_error(code, msg.c_str()); }
+
+#define EP_CUDA(call)                                                                          \
+    do {                                                                                       \
+        cudaError_t e_ = (call);                                                               \
+        if (e_ != cudaSuccess)                                                                 \
+            return ep_fail(e_ == cudaErrorMemoryAllocation ? TG_ENOMEM : TG_ECUDA,              \
+                           std::string(#call) + ": " + cudaGetErrorString(e_));                 \
+    } while (0)
+#define EP_CHECK(cond, code, msg) \
+    do {                          \
+        if (!(cond)) return ep_fail((code), (msg)); \
+    } while (0)
+#define EP_TRY(expr)                  \
+    do {                              \
+        int rc_ = (expr);             \
+        if (rc_ != TG_OK) return rc_; \
+    } while (0)
+
+struct Dev {
+    int prev = -1;
+    explicit Dev(int d) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        cudaSetDevice(d);
+    }
+    ~Dev() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+void ep_free(tgx_ep* c) {
+    if (!c) return;
+    Dev dg(c->device);
+    for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->staging, c->scratch,
+                    (void*)c->wts})
+        if (p) cudaFree(p);
+    if (c->s) cudaStreamDestroy(c->s);
+    delete c;
+}
+
+int ep_alloc(void** p, size_t n, const char* fn) {
+    if (cudaMalloc(p, n) != cudaSuccess) {
+        cudaGetLastError();
+        return ep_fail(TG_ENOMEM, std::string(fn) + ": cudaMalloc of " + std::to_string(n) + " bytes failed");
+    }
+    return TG_OK;
+}
+
+// grow the partial-step scratch and the routing-weight buffer for T tokens
+int ep_reserve(tgx_ep* c, int T, cudaStream_t s, const char* fn) {
+    const tgx_shape& sh = c->shape;
+    const size_t need = tg::batched_partial_bytes(c->g, sh.n_experts, sh.top_k, T);
+    const size_t wneed = sizeof(float) * (size_t)T * sh.top_k;
+    if (need <= c->scratch_bytes && wneed <= c->wts_bytes) return TG_OK;
+    EP_CUDA(cudaStreamSynchronize(s));
+    if (need > c->scratch_bytes) {
+        if (c->scratch) cudaFree(c->scratch);
+        c->scratch = nullptr;
+        c->scratch_bytes = 0;
+        EP_TRY(ep_alloc(&c->scratch, need, fn));
+        c->scratch_bytes = need;
+    }
+    if (wneed > c->wts_bytes) {
+        if (c->wts) cudaFree(c->wts);
+        c->wts = nullptr;
+        c->wts_bytes = 0;
+        EP_TRY(ep_alloc((void**)&c->wts, wneed, fn));
+        c->wts_bytes = wneed;
+    }
+    return TG_OK;
+}
+
+}  // namespace
+
+extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int ep_rank, int ep_size, tgx_ep** out) {
+    EP_CHECK(shape && out, TG_EINVAL, "tgx_ep_create: null argument");
+    *out = nullptr;
+    EP_CHECK(Geom::valid_dims(shape->embed, shape->inter), TG_EINVAL,
+             "tgx_ep_create: embed/inter must be positive multiples of 256 (<= 16384)");
+    EP_CHECK(shape->n_experts > 0 && shape->n_experts <= 1024 && shape->top_k > 0 && shape->top_k <= 16 &&
+                 shape->top_k <= shape->n_experts && shape->n_layers > 0,
+             TG_EINVAL, "tgx_ep_create: bad expert/top_k/layer counts");
+    EP_CHECK(ep_size >= 1 && ep_rank >= 0 && ep_rank < ep_size && shape->n_experts % ep_size == 0, TG_EINVAL,
+             "tgx_ep_create: need 0 <= ep_rank < ep_size and n_experts divisible by ep_size");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) {
+        cudaGetLastError();
+        return ep_fail(TG_ENODEV, "no CUDA device");
+    }
+    EP_CHECK(device >= 0 && device < ndev, TG_EINVAL, "tgx_ep_create: bad device index");
+    Dev dg(device);
+    tgx_ep* c = new tgx_ep();
+    c->device = device;
+    c->rank = ep_rank;
+    c->size = ep_size;
+    c->shape = *shape;
+    c->g = Geom::make(shape->embed, shape->inter);
+    c->e_n = shape->n_experts / ep_size;
+    c->e_lo = ep_rank * c->e_n;
+    c->layer_bytes = c->g.expert_bytes * c->e_n;
+    if (shape->rms_eps > 0.0f) c->eps = shape->rms_eps;
+    const int L = shape->n_layers, E = shape->n_experts, H = shape->embed;
+    c->staging_bytes = c->g.expert_bytes * 4;
+    int rc;
+    if ((rc = ep_alloc((void**)&c->weights, c->layer_bytes * L, "tgx_ep_create")) ||
+        (rc = ep_alloc((void**)&c->routers, sizeof(float) * (size_t)L * E * H, "tgx_ep_create")) ||
+        (rc = ep_alloc((void**)&c->norms, sizeof(float) * (size_t)L * H, "tgx_ep_create")) ||
+        (rc = ep_alloc((void**)&c->staging, c->staging_bytes, "tgx_ep_create"))) {
+        ep_free(c);
+        return rc;
+    }
+    std::vector<float> ones((size_t)L * H, 1.0f);
+    cudaError_t e = cudaMemcpy(c->norms, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemset(c->routers, 0, sizeof(float) * (size_t)L * E * H);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->s, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        ep_free(c);
+        return ep_fail(TG_ECUDA, std::string("tgx_ep_create: ") + cudaGetErrorString(e));
+    }
+    *out = c;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_destroy(tgx_ep* ep) {
+    ep_free(ep);
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_expert_range(const tgx_ep* ep, int* first, int* n) {
+    EP_CHECK(ep && first && n, TG_EINVAL, "tgx_ep_expert_range: null argument");
+    *first = ep->e_lo;
+    *n = ep->e_n;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_load_experts(tgx_ep* ep, int layer, int first, int n, const void* src, int src_on_device) {
+    EP_CHECK(ep && src, TG_EINVAL, "tgx_ep_load_experts: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers && n >= 0 && first >= ep->e_lo && first + n <= ep->e_lo + ep->e_n,
+             TG_EINVAL, "tgx_ep_load_experts: layer out of range or experts not held by this rank");
+    Dev dg(ep->device);
+    const Geom& g = ep->g;
+    const int chunk = (int)(ep->staging_bytes / g.expert_bytes);
+    for (int e0 = 0; e0 < n; e0 += chunk) {
+        const int m = n - e0 < chunk ? n - e0 : chunk;
+        EP_CUDA(cudaMemcpyAsync(ep->staging, (const uint8_t*)src + (size_t)e0 * g.expert_bytes, (size_t)m * g.expert_bytes,
+                                src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ep->s));
+        for (int e = 0; e < m; e++) {
+            const uint8_t* raw = ep->staging + (size_t)e * g.expert_bytes;
+            uint8_t* dst = ep->weights + (size_t)layer * ep->layer_bytes + (size_t)(first - ep->e_lo + e0 + e) * g.expert_bytes;
+            EP_CUDA(tg::launch_repack_rows(raw, dst, 2LL * g.I, g.nbH, ep->s));
+            EP_CUDA(tg::launch_repack_rows(raw + 2 * g.t_gu, dst + 2 * g.t_gu, g.H, g.nbI, ep->s));
+        }
+        EP_CUDA(cudaStreamSynchronize(ep->s));
+    }
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_set_router(tgx_ep* ep, int layer, const float* R, int src_on_device) {
+    EP_CHECK(ep && R, TG_EINVAL, "tgx_ep_set_router: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_set_router: layer out of range");
+    Dev dg(ep->device);
+    const size_t n = (size_t)ep->shape.n_experts * ep->shape.embed;
+    EP_CUDA(cudaMemcpyAsync(ep->routers + (size_t)layer * n, R, n * sizeof(float),
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ep->s));
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_set_ffn_norm(tgx_ep* ep, int layer, const float* w, int src_on_device) {
+    EP_CHECK(ep && w, TG_EINVAL, "tgx_ep_set_ffn_norm: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_set_ffn_norm: layer out of range");
+    Dev dg(ep->device);
+    EP_CUDA(cudaMemcpyAsync(ep->norms + (size_t)layer * ep->shape.embed, w, sizeof(float) * ep->shape.embed,
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ep->s));
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_fill_synthetic(tgx_ep* ep, uint64_t seed, float w_sigma, float r_sigma) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_fill_synthetic: null context");
+    Dev dg(ep->device);
+    const Geom& g = ep->g;
+    const tgx_shape& sh = ep->shape;
+    const unsigned long long per_expert = 3ULL * g.H * g.I;
+    for (int l = 0; l < sh.n_layers; l++) {
+        // the values tgx_fill_synthetic gives experts e_lo .. e_lo + e_n - 1 of a full model
+        const unsigned long long base = ((unsigned long long)l * sh.n_experts + ep->e_lo) * per_expert;
+        EP_CUDA(tg::launch_fill_experts_q4_0(ep->weights + (size_t)l * ep->layer_bytes, ep->e_n, g, seed, base,
+                                             w_sigma, ep->s));
+        const size_t nr = (size_t)sh.n_experts * sh.embed;
+        EP_CUDA(tg::launch_fill_normal(ep->routers + (size_t)l * nr, (long long)nr, seed ^ 0x5DEECE66Dull,
+                                       (unsigned long long)l * nr * 2, r_sigma, ep->s));
+    }
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    return TG_OK;
+}
+
+extern "C" size_t tgx_ep_y_floats(const tgx_ep* ep, int T) {
+    return ep && T > 0 ? (size_t)T * ep->shape.top_k * ep->shape.embed : 0;
+}
+
+extern "C" int tgx_ep_moe_partial(tgx_ep* ep, int layer, const float* x_dev, int T, float* y_dev, void* stream) {
+    EP_CHECK(ep && x_dev && y_dev, TG_EINVAL, "tgx_ep_moe_partial: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_moe_partial: layer out of range");
+    EP_CHECK(T >= 1 && T <= 65536 / ep->shape.top_k, TG_EINVAL, "tgx_ep_moe_partial: T must be in [1, 65536/top_k]");
+    Dev dg(ep->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    int optin = 0;
+    EP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ep->device));
+    EP_CHECK(tg::batched_smem_bytes(ep->g) <= (size_t)optin, TG_EUNSUPPORTED,
+             "tgx_ep_moe_partial: shape needs more shared memory per block than the device has");
+    EP_TRY(ep_reserve(ep, T, s, "tgx_ep_moe_partial"));
+    const tgx_shape& sh = ep->shape;
+    const size_t nr = (size_t)sh.n_experts * sh.embed;
+    EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, ep->e_lo, ep->e_n, ep->g,
+                                           ep->routers + (size_t)layer * nr, ep->norms + (size_t)layer * sh.embed,
+                                           ep->eps, sh.n_experts, sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes,
+                                           y_dev, nullptr, ep->wts, nullptr, s));
+    ep->last_T = T;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_combine(tgx_ep* ep, float* x_dev, int T, const float* y_dev, void* stream) {
+    EP_CHECK(ep && x_dev && y_dev, TG_EINVAL, "tgx_ep_combine: null argument");
+    EP_CHECK(T >= 1 && T == ep->last_T, TG_EINVAL, "tgx_ep_combine: T must match the last tgx_ep_moe_partial");
+    Dev dg(ep->device);
+    EP_CUDA(tg::launch_moe_batched_combine(x_dev, T, ep->shape.embed, ep->shape.top_k, ep->wts, y_dev,
+                                           (cudaStream_t)stream));
+    return TG_OK;
+}

@@ -82,6 +82,20 @@ size_t batched_smem_bytes(const Geom& g);
 cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
                                int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
                                float* w_out, float* logits_out, cudaStream_t s);
+// The two halves of launch_moe_batched, for experts sharded over devices.  Partial:
+// routing of all T tokens (every device computes the same), then y[(t, j)][H] for the
+// pairs whose expert lies in [e_lo, e_lo + e_n) (layer points at expert e_lo), y = 0
+// for the others; w_out receives the routing weights [T][k].  Scratch of
+// batched_partial_bytes.  Combine: X[t] += sum_j w[t][j] * y[(t, j)] in slot order.
+// With the y of every device summed in between (one nonzero term per element, so the
+// sum is exact), the result is the single-device one bit for bit.
+size_t batched_partial_bytes(const Geom& g, int E, int k, int T);
+cudaError_t launch_moe_batched_partial(const uint8_t* layer, int e_lo, int e_n, Geom g, const float* R,
+                                       const float* normw, float eps, int E, int k, const float* X, int T,
+                                       void* scratch, size_t scratch_bytes, float* y, int* idx_out, float* w_out,
+                                       float* logits_out, cudaStream_t s);
+cudaError_t launch_moe_batched_combine(float* X, int T, int H, int k, const float* wts, const float* y,
+                                       cudaStream_t s);
 
 // The reference library's own formats (tg_kquant.cu).  fmt: KQ_Q4K (ggml Q4_K
 // blocks), KQ_F16, KQ_Q6K (split layout: 208-byte bodies of all blocks, then their

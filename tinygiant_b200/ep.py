@@ -1,0 +1,118 @@
+"""Experts sharded over GPUs (expert parallelism), one process per GPU.
+
+Rank r of G holds experts [r*E/G, (r+1)*E/G) of every layer; the routers and FFN
+norms are replicated, so every rank routes every token the same way.  One MoE layer
+(tinygiant/engine.py:229-258 for each of T tokens) is
+
+    tgx_ep_moe_partial   y[(t, j)] for the (token, slot) pairs whose expert is local, else 0
+    all_reduce(y, SUM)   over the expert-parallel group (NCCL on GPUs)
+    tgx_ep_combine       x[t] += sum_j w[t][j] * y[(t, j)] in slot order
+
+Each element of y has one nonzero contribution, so the sum is exact and the result is
+bit-identical to the single-GPU batched path (and, through it, to the CPU oracle).
+The all-reduce moves T * top_k * embed floats per layer.
+
+    ep = EPMoEModel(rank=r, size=G, device=local_rank)
+    ep.fill_synthetic(seed)            # or load_experts(layer, first, blob) for the local range
+    ep.decode(X)                       # X: cuda f32[T][embed], all layers, in place
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import _constants as C
+from ._lib import TgxShape, check, get_lib
+from .engine import _dev_ptr, _stream_handle
+
+
+def expert_range(n_experts: int, rank: int, size: int):
+    """(first, count) of the experts rank `rank` of `size` holds."""
+    if size < 1 or not 0 <= rank < size or n_experts % size:
+        raise ValueError("need 0 <= rank < size and n_experts divisible by size")
+    n = n_experts // size
+    return rank * n, n
+
+
+class EPMoEModel:
+    def __init__(self, embed=C.EMBED_DIM, inter=C.EXPERT_INTERMEDIATE, n_experts=C.N_EXPERTS,
+                 top_k=C.N_EXPERTS_USED, n_layers=C.N_LAYERS, rank=0, size=1, device=0, group=None):
+        self.lib = get_lib()
+        self.shape = TgxShape(embed, inter, n_experts, top_k, n_layers, C.RMS_EPS)
+        self.embed, self.inter, self.n_experts, self.top_k, self.n_layers = embed, inter, n_experts, top_k, n_layers
+        self.rank, self.size, self.device, self.group = rank, size, device, group
+        h = ctypes.c_void_p()
+        check(self.lib.tgx_ep_create(device, ctypes.byref(self.shape), rank, size, ctypes.byref(h)), self.lib)
+        self._ep = h
+        first, n = ctypes.c_int(), ctypes.c_int()
+        check(self.lib.tgx_ep_expert_range(h, ctypes.byref(first), ctypes.byref(n)), self.lib)
+        self.first, self.n_local = first.value, n.value
+        assert (self.first, self.n_local) == expert_range(n_experts, rank, size)
+        self.expert_bytes = C.expert_bytes(embed, inter)
+        self._y = {}
+
+    def close(self):
+        if self._ep:
+            self.lib.tgx_ep_destroy(self._ep)
+            self._ep = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---------------------------------------------------------------- weights
+    def fill_synthetic(self, seed: int, w_sigma: float = 0.02, r_sigma: float = 0.02):
+        """The weights MoEModel.fill_synthetic(seed) gives the same experts."""
+        check(self.lib.tgx_ep_fill_synthetic(self._ep, seed, w_sigma, r_sigma), self.lib)
+
+    def load_experts(self, layer: int, first: int, blob: np.ndarray):
+        """ggml Q4_0 experts [first, first + n) of a layer (inside the local range)."""
+        blob = np.ascontiguousarray(blob, dtype=np.uint8)
+        n = blob.size // self.expert_bytes
+        assert n * self.expert_bytes == blob.size
+        check(self.lib.tgx_ep_load_experts(self._ep, layer, first, n, blob.ctypes.data, 0), self.lib)
+
+    def set_router(self, layer: int, R: np.ndarray):
+        R = np.ascontiguousarray(R, dtype=np.float32)
+        assert R.shape == (self.n_experts, self.embed)
+        check(self.lib.tgx_ep_set_router(self._ep, layer, R.ctypes.data, 0), self.lib)
+
+    def set_ffn_norm(self, layer: int, w: np.ndarray):
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        assert w.shape == (self.embed,)
+        check(self.lib.tgx_ep_set_ffn_norm(self._ep, layer, w.ctypes.data, 0), self.lib)
+
+    # ---------------------------------------------------------------- compute
+    def y_buffer(self, T: int):
+        """The per-step exchange buffer for T tokens (reused, one per T)."""
+        import torch
+        if T not in self._y:
+            n = int(self.lib.tgx_ep_y_floats(self._ep, T))
+            self._y[T] = torch.empty(n, dtype=torch.float32, device=torch.device("cuda", self.device))
+        return self._y[T]
+
+    def partial(self, layer: int, X, Y, stream=None):
+        check(self.lib.tgx_ep_moe_partial(self._ep, layer, _dev_ptr(X), X.shape[0], _dev_ptr(Y),
+                                          _stream_handle(stream)), self.lib)
+
+    def combine(self, X, Y, stream=None):
+        check(self.lib.tgx_ep_combine(self._ep, _dev_ptr(X), X.shape[0], _dev_ptr(Y), _stream_handle(stream)),
+              self.lib)
+
+    def moe_layer(self, layer: int, X, stream=None):
+        """MoE block `layer` for the T tokens of X (cuda f32[T][embed]) in place."""
+        import torch.distributed as dist
+        assert X.dim() == 2 and X.shape[1] == self.embed
+        Y = self.y_buffer(X.shape[0])
+        self.partial(layer, X, Y, stream)
+        if self.size > 1:
+            dist.all_reduce(Y, op=dist.ReduceOp.SUM, group=self.group)
+        self.combine(X, Y, stream)
+
+    def decode(self, X, stream=None):
+        """All layers chained on X in place."""
+        for layer in range(self.n_layers):
+            self.moe_layer(layer, X, stream)
