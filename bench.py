@@ -30,6 +30,9 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# NCCL's own messages (its version line under NCCL_DEBUG=VERSION, for one) go to
+# stderr: stdout carries only the JSON result line
+os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
 METRIC = "expert-FFN decode tok/s (Qwen3-30B-A3B shape) & Q4 weight-read HBM GB/s"
 H, I, E, K_TOP, L = 2048, 768, 128, 8, 48

@@ -244,20 +244,28 @@ int tgx_last_routing(tgx_ctx *ctx, int layer, int32_t *idx, float *w, float *log
  * (n_experts % G == 0); routers and FFN norms are replicated.  One MoE layer for T
  * tokens x_dev[T][embed] (tinygiant/engine.py:229-258 per token):
  *   tgx_ep_moe_partial(ep, layer, x, T, y, s)  every rank: the same routing, then
- *       y[(t, j)][embed] for the pairs (token t, slot j) whose expert it holds, 0 for
- *       the others (y: tgx_ep_y_floats(ep, T) floats, caller-owned);
+ *       y[(t, j)][embed] for the pairs (token t, slot j) it owns, 0 for the others
+ *       (y: tgx_ep_y_floats(ep, T) floats, caller-owned);
  *   sum y over the ranks (an NCCL all-reduce, or any exact sum: each element has one
  *       nonzero contribution);
  *   tgx_ep_combine(ep, x, T, y, s)  x[t] += sum_j w[t][j] * y[(t, j)] in slot order.
  * The result equals tgx_moe_batched on one device with all experts, bit for bit.
+ * n_shared = 1 adds a shared expert (DeepSeek-V3-like): slot k of every token with
+ * weight 1, replicated on every rank and computed, per token, by the rank holding the
+ * fewest of that token's routed experts (ties to rank (t + i) mod G, smallest i).
  * The first partial call for a larger T allocates scratch (make it before any graph
  * capture). */
 typedef struct tgx_ep tgx_ep;
-int tgx_ep_create(int device, const tgx_shape *shape, int ep_rank, int ep_size, tgx_ep **out);
+int tgx_ep_create(int device, const tgx_shape *shape, int n_shared, int ep_rank, int ep_size, tgx_ep **out);
 int tgx_ep_destroy(tgx_ep *ep);
 int tgx_ep_expert_range(const tgx_ep *ep, int *first, int *n);
 /* experts [first, first + n) of a layer (global ids inside this rank's range), ggml blobs */
 int tgx_ep_load_experts(tgx_ep *ep, int layer, int first, int n, const void *src, int src_on_device);
+/* the shared expert of a layer (n_shared = 1), one ggml blob gate | up | down */
+int tgx_ep_load_shared(tgx_ep *ep, int layer, const void *src, int src_on_device);
+/* read expert e of a layer (a local routed id, or n_experts for the shared expert) back
+ * as one ggml blob into host memory */
+int tgx_ep_read_expert(tgx_ep *ep, int layer, int e, void *dst_host);
 int tgx_ep_set_router(tgx_ep *ep, int layer, const float *R, int src_on_device);
 int tgx_ep_set_ffn_norm(tgx_ep *ep, int layer, const float *w, int src_on_device);
 /* the values tgx_fill_synthetic gives the same experts of a full model */

@@ -68,6 +68,8 @@ def lib():
         "ref_decode_step_mt": (None, [VP, VP, VP, CF, CI, VP, CI, CI, CI, CI, CI, CI]),
         "ref_moe_layer_batched": (None, [VP, ctypes.c_size_t, VP, VP, CI, CI, CI, CI, CI, CI, CI]),
         "ref_moe_block_batched": (None, [VP, ctypes.c_size_t, VP, VP, CF, VP, CI, CI, CI, CI, CI, CI, CI]),
+        "ref_moe_block_batched_shared": (None, [VP, ctypes.c_size_t, VP, VP, CF, VP, CI, CI, CI, CI, CI, CI, CI,
+                                                VP]),
         "ref_quantize_q8k": (None, [VP, VP, ctypes.c_int64]),
         "ref_matvec_k": (None, [VP, CI, VP, VP, CI, CI]),
         "ref_rms_norm_k": (None, [VP, VP, VP, CI, CF]),
@@ -260,14 +262,20 @@ def moe_layer_batched(layer_blob, R, x, k, embed, inter, mode=TG_MIRROR, n_threa
 
 
 def moe_block_batched(layer_blob, R, x, k, embed, inter, normw=None, eps: float = RMS_EPS, mode=TG_MIRROR,
-                      n_threads=0):
-    """moe_block for every row of x[T][embed] (independent tokens); returns the new x."""
+                      n_threads=0, shared=None):
+    """moe_block for every row of x[T][embed] (independent tokens); returns the new x.
+    shared: an optional shared-expert blob, added with weight 1 after the routed experts."""
     x = np.array(x, dtype=np.float32, copy=True)
     T = x.shape[0]
     nw = None if normw is None else np.ascontiguousarray(normw, dtype=np.float32)
-    lib().ref_moe_block_batched(_p(np.ascontiguousarray(layer_blob)), expert_bytes(embed, inter),
-                                _p(np.ascontiguousarray(R, dtype=np.float32)), None if nw is None else _p(nw), eps,
-                                _p(x), T, R.shape[0], k, embed, inter, mode, n_threads)
+    args = (_p(np.ascontiguousarray(layer_blob)), expert_bytes(embed, inter),
+            _p(np.ascontiguousarray(R, dtype=np.float32)), None if nw is None else _p(nw), eps,
+            _p(x), T, R.shape[0], k, embed, inter, mode, n_threads)
+    if shared is None:
+        lib().ref_moe_block_batched(*args)
+    else:
+        sh = np.ascontiguousarray(shared, dtype=np.uint8)
+        lib().ref_moe_block_batched_shared(*args, _p(sh))
     return x
 
 

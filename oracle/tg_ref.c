@@ -427,9 +427,22 @@ void ref_moe_layer(const uint8_t *layer_blob, size_t expert_bytes, const float *
 
 /* The engine's MoE block (engine.py:229-258 without attention): normed =
  * RMSNorm(x) * w, route on normed, run the top-k experts on normed, x += moe. */
+/* The MoE block with an optional shared expert (DeepSeek-V3-like configs): after the k
+ * routed experts, moe += 1 * shared(normed), then x += moe. */
+static void moe_block_impl(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                           float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
+                           int32_t *idx_out, float *w_out, float *logits_out, const uint8_t *shared_blob);
+
 void ref_moe_block(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
                    float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
                    int32_t *idx_out, float *w_out, float *logits_out) {
+    moe_block_impl(layer_blob, expert_bytes, R, normw, eps, x, n_experts, k, embed, inter, mode, idx_out, w_out,
+                   logits_out, NULL);
+}
+
+static void moe_block_impl(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
+                           float eps, float *x, int n_experts, int k, int embed, int inter, int mode,
+                           int32_t *idx_out, float *w_out, float *logits_out, const uint8_t *shared_blob) {
     float *logits = malloc(sizeof(float) * n_experts);
     float *normed = malloc(sizeof(float) * embed);
     int32_t idx[64];
@@ -443,6 +456,11 @@ void ref_moe_block(const uint8_t *layer_blob, size_t expert_bytes, const float *
         const uint8_t *g, *u, *d;
         expert_ptrs(layer_blob + (size_t)idx[j] * expert_bytes, embed, inter, &g, &u, &d);
         ref_expert_forward(g, u, d, normed, moe, w[j], embed, inter, mode);
+    }
+    if (shared_blob) {
+        const uint8_t *g, *u, *d;
+        expert_ptrs(shared_blob, embed, inter, &g, &u, &d);
+        ref_expert_forward(g, u, d, normed, moe, 1.0f, embed, inter, mode);
     }
     for (int i = 0; i < embed; i++) x[i] = x[i] + moe[i];
     if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * k);
@@ -729,6 +747,20 @@ void ref_expert_forward_k(const uint8_t *gate, const uint8_t *up, const void *do
 /* The MoE block with its FFN RMSNorm for T independent tokens x[T][embed], in place:
  * ref_moe_block per token (engine.py:229-258 for each row of a batch); tokens run in
  * parallel across n_threads (0 = OpenMP default). */
+void ref_moe_block_batched_shared(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
+                                  const float *normw, float eps, float *x, int T, int n_experts, int k, int embed,
+                                  int inter, int mode, int n_threads, const uint8_t *shared_blob) {
+#ifdef _OPENMP
+    if (n_threads > 0) omp_set_num_threads(n_threads);
+    #pragma omp parallel for schedule(dynamic, 1)
+#else
+    (void)n_threads;
+#endif
+    for (int t = 0; t < T; t++)
+        moe_block_impl(layer_blob, expert_bytes, R, normw, eps, x + (size_t)t * embed, n_experts, k, embed, inter,
+                       mode, NULL, NULL, NULL, shared_blob);
+}
+
 void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
                            float eps, float *x, int T, int n_experts, int k, int embed, int inter, int mode,
                            int n_threads) {

@@ -100,6 +100,9 @@ void ref_rms_norm_k(const float *x, const float *w, float *out, int dim, float e
 void ref_matvec_k(const void *W, int fmt, const float *x, float *y, int rows, int cols);
 void ref_expert_forward_k(const uint8_t *gate, const uint8_t *up, const void *down, int down_format,
                           const float *x, float *out, float w, int embed, int inter, int mode);
+void ref_moe_block_batched_shared(const uint8_t *layer_blob, size_t expert_bytes, const float *R,
+                                  const float *normw, float eps, float *x, int T, int n_experts, int k, int embed,
+                                  int inter, int mode, int n_threads, const uint8_t *shared_blob);
 void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const float *R, const float *normw,
                            float eps, float *x, int T, int n_experts, int k, int embed, int inter, int mode,
                            int n_threads);

@@ -53,6 +53,78 @@ def test_ep_emulated_matches_single_gpu(G, T):
     full.close()
 
 
+def _emulate(ranks, X, L):
+    """G ranks on one GPU: partial on each, an exact torch sum of y, combine."""
+    T = X.shape[0]
+    Ys = [ep.y_buffer(T) for ep in ranks]
+    for layer in range(L):
+        for ep, Y in zip(ranks, Ys):
+            ep.partial(layer, X, Y)
+        total = Ys[0].clone()
+        for Y in Ys[1:]:
+            total += Y
+        ranks[0].combine(X, total)
+
+
+@pytest.mark.parametrize("G", [1, 2, 4])
+def test_ep_shared_expert_matches_oracle(oracle, G):
+    # host-made weights (oracle quantiser), a shared expert, two chained layers
+    import numpy as np
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    h, i, e, k, L, T = 512, 256, 16, 4, 2, 6
+    rng = np.random.default_rng(11)
+    eb = oracle.expert_bytes(h, i)
+    blobs = [oracle.quantize_q4_0(oracle.fill_normal(e * 3 * h * i, 30 + l, 0.05)) for l in range(L)]
+    shared = [oracle.quantize_q4_0(oracle.fill_normal(3 * h * i, 60 + l, 0.05)) for l in range(L)]
+    routers = [oracle.fill_normal(e * h, 90 + l, 0.05).reshape(e, h) for l in range(L)]
+    norms = [rng.uniform(0.5, 1.5, h).astype(np.float32) for _ in range(L)]
+    ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G, n_shared=1) for r in range(G)]
+    for ep in ranks:
+        for l in range(L):
+            ep.load_experts(l, ep.first, blobs[l][ep.first * eb:(ep.first + ep.n_local) * eb])
+            ep.load_shared(l, shared[l])
+            ep.set_router(l, routers[l])
+            ep.set_ffn_norm(l, norms[l])
+    X0 = rng.standard_normal((T, h)).astype(np.float32)
+    X = torch.from_numpy(X0.copy()).cuda()
+    _emulate(ranks, X, L)
+    torch.cuda.synchronize()
+    ref = X0.copy()
+    for l in range(L):
+        ref = oracle.moe_block_batched(blobs[l], routers[l], ref, k, h, i, normw=norms[l], shared=shared[l])
+    assert np.array_equal(X.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    for ep in ranks:
+        ep.close()
+
+
+def test_ep_dsv3_width_matches_oracle(oracle):
+    # DeepSeek-V3 widths (hidden 7168, intermediate 2048): 16-row gate/up units and the
+    # separate Q8_0 pass over h; 16 routed experts + the shared one, 2 emulated ranks
+    import numpy as np
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    h, i, e, k, L, T, G = 7168, 2048, 16, 8, 1, 2, 2
+    rng = np.random.default_rng(5)
+    R = (rng.standard_normal((e, h)) * 0.02).astype(np.float32)
+    ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G, n_shared=1) for r in range(G)]
+    for ep in ranks:
+        ep.fill_synthetic(123)
+        ep.set_router(0, R)
+    blob = np.concatenate([ranks[r].read_expert(0, x) for r in range(G)
+                           for x in range(ranks[r].first, ranks[r].first + ranks[r].n_local)])
+    shared = ranks[0].read_expert(0, e)
+    assert np.array_equal(shared, ranks[1].read_expert(0, e))      # replicated
+    X0 = rng.standard_normal((T, h)).astype(np.float32)
+    X = torch.from_numpy(X0.copy()).cuda()
+    _emulate(ranks, X, L)
+    torch.cuda.synchronize()
+    ref = oracle.moe_block_batched(blob, R, X0, k, h, i, shared=shared, n_threads=0)
+    assert np.array_equal(X.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    for ep in ranks:
+        ep.close()
+
+
 def test_ep_rejects_foreign_experts():
     import numpy as np
     from tinygiant_b200._lib import TinyGiantError

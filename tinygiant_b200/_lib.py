@@ -76,7 +76,9 @@ PROTOTYPES = {
     "tgx_kq_matrix_bytes": (SZ, [CI, ctypes.c_longlong, CI]),
     "tgx_kq_prepare": (CI, [CI, VP, VP, ctypes.c_longlong, CI, VP]),
     "tgx_kq_matvec": (CI, [CI, VP, VP, VP, CI, CI, VP]),
-    "tgx_ep_create": (CI, [CI, ctypes.POINTER(TgxShape), CI, CI, ctypes.POINTER(VP)]),
+    "tgx_ep_create": (CI, [CI, ctypes.POINTER(TgxShape), CI, CI, CI, ctypes.POINTER(VP)]),
+    "tgx_ep_load_shared": (CI, [VP, CI, VP, CI]),
+    "tgx_ep_read_expert": (CI, [VP, CI, CI, VP]),
     "tgx_ep_destroy": (CI, [VP]),
     "tgx_ep_expert_range": (CI, [VP, ctypes.POINTER(CI), ctypes.POINTER(CI)]),
     "tgx_ep_load_experts": (CI, [VP, CI, CI, CI, VP, CI]),

@@ -15,6 +15,13 @@
 // Each token's values use the same reduction order as the single-token kernels (lane-strided
 // block partials, xor butterfly), so a batch gives bit-identical results to T single-token
 // calls and to the CPU oracle's mirror mode.
+//
+// An optional shared expert (DeepSeek-V3-like models) is slot k of every token, weight 1,
+// expert id E; with experts sharded over G devices, a pair (token t, slot j) is computed by
+// the device holding its routed expert, and a token's shared-expert pair by the device that
+// holds the fewest of that token's routed experts (ties to (t + i) mod G, smallest i), a
+// rule every device evaluates the same way.  Rows wider than the shared-memory budget
+// allows for 32 gate/up rows use 16-row units and a separate Q8_0 pass over h.
 #include <cuda_runtime.h>
 
 #include "tg_device.cuh"
@@ -66,7 +73,7 @@ __global__ void __launch_bounds__(256) k_router_sums_batched(const float* __rest
 // grid T, 256 threads: token t's RMSNorm scale, logits, top-k and softmax weights, and
 // the Q8_0 activation form of (x * scale) * w.
 __global__ void __launch_bounds__(256) k_topk_quant_batched(const float* __restrict__ X, const float* __restrict__ normw,
-                                                            float eps, int E, int H, int k,
+                                                            float eps, int E, int H, int k, int ks,
                                                             const unsigned long long* __restrict__ S, int* __restrict__ idx,
                                                             float* __restrict__ wts, float* __restrict__ logits,
                                                             uint8_t* __restrict__ xq) {
@@ -97,8 +104,11 @@ __global__ void __launch_bounds__(256) k_topk_quant_batched(const float* __restr
     __syncthreads();
     topk_softmax_block(sl, E, k, sidx, sw);
     if (threadIdx.x < k) {
-        idx[(size_t)t * k + threadIdx.x] = sidx[threadIdx.x];
-        wts[(size_t)t * k + threadIdx.x] = sw[threadIdx.x];
+        idx[(size_t)t * ks + threadIdx.x] = sidx[threadIdx.x];
+        wts[(size_t)t * ks + threadIdx.x] = sw[threadIdx.x];
+    } else if (threadIdx.x < ks) {   // the shared expert: id E, weight 1
+        idx[(size_t)t * ks + threadIdx.x] = E;
+        wts[(size_t)t * ks + threadIdx.x] = 1.0f;
     }
     // Q8_0 of the normed input, one warp per block (the single-token quantiser's order)
     const int nb = H / 32;
@@ -117,38 +127,73 @@ __global__ void __launch_bounds__(256) k_topk_quant_batched(const float* __restr
 // one CTA of 256 threads: pairs p = t * k + j grouped by expert idx[p]; off[E + 1],
 // list[T * k] (the order inside a group does not affect any result) and the active experts
 // among those this device holds, [e_lo, e_lo + e_n)
-__global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int E, int e_lo,
-                                                     int e_n, int* __restrict__ off, int* __restrict__ list,
-                                                     int* __restrict__ active) {
-    __shared__ int cnt[1024];
-    __shared__ int pos[1024];
-    for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+// Whether this device (rank of G, holding routed experts [rank*e_n, (rank+1)*e_n))
+// computes pair p = t * ks + j: a routed slot by its expert's holder, the shared slot
+// (j >= k) by the holder of the fewest of token t's routed experts.
+__device__ __forceinline__ bool pair_owned(const int* __restrict__ idx, int p, int ks, int k, int e_n, int rank,
+                                           int G) {
+    const int t = p / ks, j = p - t * ks;
+    if (j < k) return idx[p] / e_n == rank;
+    int best = 0, best_n = 1 << 30;
+    for (int i = 0; i < G; i++) {
+        const int r = (t + i) % G;
+        int n = 0;
+        for (int q = 0; q < k; q++) n += idx[(size_t)t * ks + q] / e_n == r;
+        if (n < best_n) {
+            best_n = n;
+            best = r;
+        }
+    }
+    return best == rank;
+}
+
+// one CTA of 256 threads: the pairs this device computes, grouped by expert id (routed
+// experts 0..E-1, the shared expert E): off[E_tot + 1], list (the order inside a group
+// does not affect any result) and active[0] = count, active[1..] = the experts, ascending
+__global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int ks, int k,
+                                                     int E_tot, int e_n, int rank, int G, int* __restrict__ off,
+                                                     int* __restrict__ list, int* __restrict__ active) {
+    __shared__ int cnt[1025];
+    __shared__ int pos[1025];
+    for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
-    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) atomicAdd(&cnt[idx[p]], 1);
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x)
+        if (pair_owned(idx, p, ks, k, e_n, rank, G)) atomicAdd(&cnt[idx[p]], 1);
     __syncthreads();
     if (threadIdx.x == 0) {
         int acc = 0, na = 0;
-        for (int e = 0; e < E; e++) {
+        for (int e = 0; e < E_tot; e++) {
             off[e] = acc;
             pos[e] = acc;
             acc += cnt[e];
-            if (cnt[e] && e >= e_lo && e < e_lo + e_n) active[1 + na++] = e;
+            if (cnt[e]) active[1 + na++] = e;
         }
-        off[E] = acc;
-        active[0] = na;   // active[1 .. na]: the experts with tokens, ascending
+        off[E_tot] = acc;
+        active[0] = na;
     }
     __syncthreads();
-    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) list[atomicAdd(&pos[idx[p]], 1)] = p;
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x)
+        if (pair_owned(idx, p, ks, k, e_n, rank, G)) list[atomicAdd(&pos[idx[p]], 1)] = p;
 }
 
-// grid (I / 32, min(E, T * k)), 256 threads.  CTA (c, a) takes the a-th active expert e and
-// stages rows 32c .. 32c+31 of its
-// gate and up in shared memory, then for every pair p routed to e: 4 rows per warp,
-// h = silu(g) * u, and h's Q8_0 block c into hq[p].
-__global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer, int e_lo, Geom g,
+// expert e's blob: a local routed expert, or the shared expert (e == E)
+__device__ __forceinline__ const uint8_t* expert_base(const uint8_t* layer, const uint8_t* shared, int e, int E,
+                                                      int e_lo, size_t expert_bytes) {
+    return e == E ? shared : layer + (size_t)(e - e_lo) * expert_bytes;
+}
+
+// grid (I / R, active experts), 256 threads.  CTA (c, a) takes the a-th active expert e and
+// stages rows R*c .. R*c+R-1 of its gate and up in shared memory, then for every pair p
+// routed to e: R/8 rows per warp and h = silu(g) * u; with R = 32 the unit is one Q8_0
+// block of h, quantised here into hq[p], with R = 16 h goes to hf[p] for k_quant_h.
+template <int R>
+__global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer,
+                                                        const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                         const int* __restrict__ off, const int* __restrict__ list,
-                                                        const int* __restrict__ active, int k,
-                                                        const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq) {
+                                                        const int* __restrict__ active, int ks,
+                                                        const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq,
+                                                        float* __restrict__ hf) {
+    constexpr int RW = R / 8;   // rows per warp
     extern __shared__ __align__(16) uint8_t smem[];   // gate rows | up rows
     __shared__ float sh[32];
     if ((int)blockIdx.y >= active[0]) return;
@@ -156,8 +201,8 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
     const int p0 = off[e], n = off[e + 1] - p0;
     if (n == 0) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint8_t* eb = layer + (size_t)(e - e_lo) * g.expert_bytes;
-    const size_t unit = (size_t)32 * g.row_gu;
+    const uint8_t* eb = expert_base(layer, shared, e, E, e_lo, g.expert_bytes);
+    const size_t unit = (size_t)R * g.row_gu;
     {
         const int4* sg = reinterpret_cast<const int4*>(eb + (size_t)c * unit);
         const int4* su = reinterpret_cast<const int4*>(eb + g.t_gu + (size_t)c * unit);
@@ -171,16 +216,18 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
     __syncthreads();
     const uint8_t* gate = smem;
     const uint8_t* up = smem + unit;
-    const int nb = g.nbH, i0 = warp * 4;
+    const int nb = g.nbH, i0 = warp * RW;
     const size_t abx = act_bytes(nb), abh = act_bytes(g.nbI);
     for (int q = 0; q < n; q++) {
-        const int p = list[p0 + q], t = p / k;
+        const int p = list[p0 + q], t = p / ks;
         const ActView xa = act_view(xq + (size_t)t * abx, nb);
-        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+        float ag[RW], au[RW];
+#pragma unroll
+        for (int r = 0; r < RW; r++) ag[r] = au[r] = 0.0f;
         for (int b = lane; b < nb; b += 32) {
             const XBlk xb = load_xblk(xa, b);
 #pragma unroll
-            for (int r = 0; r < 4; r++) {
+            for (int r = 0; r < RW; r++) {
                 const uint8_t* rg = gate + (size_t)(i0 + r) * g.row_gu;
                 const uint8_t* ru = up + (size_t)(i0 + r) * g.row_gu;
                 const uint4 wg = *reinterpret_cast<const uint4*>(rg + 16 * b);
@@ -192,29 +239,53 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
             }
         }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
+        for (int r = 0; r < RW; r++) {
             const float gv = warp_sum_butterfly(ag[r]);
             const float uv = warp_sum_butterfly(au[r]);
-            if (lane == r) sh[i0 + r] = silu_mul(gv, uv);
-        }
-        __syncthreads();
-        if (warp == 0) {
-            const Q8Lane qz = quantize_lane(sh[lane]);
-            ActView ha = act_view(hq + (size_t)p * abh, g.nbI);
-            ha.qs[(size_t)c * 32 + lane] = (int8_t)qz.q;
-            if (lane == 0) {
-                ha.d[c] = f16_bits_to_f32(qz.dh);
-                ha.s8[c] = qz.s8;
+            if (R == 32) {
+                if (lane == r) sh[i0 + r] = silu_mul(gv, uv);
+            } else if (lane == 0) {
+                hf[(size_t)p * g.I + (size_t)c * R + i0 + r] = silu_mul(gv, uv);
             }
         }
-        __syncthreads();
+        if (R == 32) {
+            __syncthreads();
+            if (warp == 0) {
+                const Q8Lane qz = quantize_lane(sh[lane]);
+                ActView ha = act_view(hq + (size_t)p * abh, g.nbI);
+                ha.qs[(size_t)c * 32 + lane] = (int8_t)qz.q;
+                if (lane == 0) {
+                    ha.d[c] = f16_bits_to_f32(qz.dh);
+                    ha.s8[c] = qz.s8;
+                }
+            }
+            __syncthreads();
+        }
     }
 }
 
-// grid (H / 16, min(E, T * k)), 256 threads.  CTA (rb, a) takes the a-th active expert e,
+// one warp per (pair, block) of h: the Q8_0 activation form of hf[p] into hq[p]
+// (the single-token quantiser, block by block, so the same bytes as the fused units).
+__global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, int n_pairs, Geom g,
+                                                 uint8_t* __restrict__ hq) {
+    const int lane = threadIdx.x & 31;
+    const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (wid >= (long long)n_pairs * g.nbI) return;
+    const int p = (int)(wid / g.nbI), b = (int)(wid - (long long)p * g.nbI);
+    const Q8Lane qz = quantize_lane(hf[(size_t)p * g.I + (size_t)b * 32 + lane]);
+    ActView ha = act_view(hq + (size_t)p * act_bytes(g.nbI), g.nbI);
+    ha.qs[(size_t)b * 32 + lane] = (int8_t)qz.q;
+    if (lane == 0) {
+        ha.d[b] = f16_bits_to_f32(qz.dh);
+        ha.s8[b] = qz.s8;
+    }
+}
+
+// grid (H / 16, active experts), 256 threads.  CTA (rb, a) takes the a-th active expert e,
 // stages its down rows 16rb .. 16rb+15, then for every pair p routed to e: 2 rows per
 // warp, y[p][r] = row . hq[p].
-__global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer, int e_lo, Geom g,
+__global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer,
+                                                      const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                       const int* __restrict__ off, const int* __restrict__ list,
                                                       const int* __restrict__ active, const uint8_t* __restrict__ hq,
                                                       float* __restrict__ y) {
@@ -227,7 +298,7 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
     const int r0 = rb * DOWN_ROWS;
     const int nrows = min(DOWN_ROWS, g.H - r0);
     {
-        const int4* src = reinterpret_cast<const int4*>(layer + (size_t)(e - e_lo) * g.expert_bytes + 2 * g.t_gu +
+        const int4* src = reinterpret_cast<const int4*>(expert_base(layer, shared, e, E, e_lo, g.expert_bytes) + 2 * g.t_gu +
                                                         (size_t)r0 * g.row_d);
         int4* d = reinterpret_cast<int4*>(smem);
         const int n16 = (int)((size_t)nrows * g.row_d / 16);
@@ -270,79 +341,106 @@ __global__ void __launch_bounds__(256) k_combine_batched(float* __restrict__ X, 
 
 }  // namespace
 
+// gate/up rows per unit: 32 when 32 gate + 32 up rows fit one CTA's shared memory, else 16
+static int gu_rows(const Geom& g, size_t smem_optin) { return (size_t)2 * 32 * g.row_gu <= smem_optin ? 32 : 16; }
+
 size_t batched_smem_bytes(const Geom& g) {
-    size_t m = (size_t)2 * 32 * g.row_gu;
+    size_t m = (size_t)2 * 16 * g.row_gu;
     m = m > (size_t)DOWN_ROWS * g.row_d ? m : (size_t)DOWN_ROWS * g.row_d;
     return m + 256;
 }
 
-// scratch of the partial step (router sums, activations, routing, pair lists, h)
-size_t batched_partial_bytes(const Geom& g, int E, int k, int T) {
-    const size_t n_pairs = (size_t)T * k;
-    auto r = [](size_t n) { return (n + 255) & ~(size_t)255; };
-    return r((size_t)T * E * 8) + r((size_t)(E + 1) * 4) + r((size_t)T * act_bytes(g.nbH)) + r(n_pairs * 4) +
-           r(n_pairs * 4) + r((size_t)(E + 1) * 4) + r(n_pairs * 4) + r(n_pairs * act_bytes(g.nbI));
+static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T) {
+    const size_t ks = (size_t)k + n_shared, n_pairs = (size_t)T * ks, E_tot = (size_t)E + n_shared;
+    return r256((size_t)T * E * 8) + r256((E_tot + 1) * 4) + r256((size_t)T * act_bytes(g.nbH)) + r256(n_pairs * 4) +
+           r256(n_pairs * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256(n_pairs * act_bytes(g.nbI)) +
+           r256(n_pairs * g.I * 4);
 }
 
 size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
     const size_t n_pairs = (size_t)T * k;
-    return batched_partial_bytes(g, E, k, T) + ((n_pairs * 4 + 255) & ~(size_t)255) + n_pairs * g.H * 4;
+    return batched_partial_bytes(g, E, 0, k, T) + r256(n_pairs * 4) + n_pairs * g.H * 4;
 }
 
-cudaError_t launch_moe_batched_partial(const uint8_t* layer, int e_lo, int e_n, Geom g, const float* R,
-                                       const float* normw, float eps, int E, int k, const float* X, int T,
-                                       void* scratch, size_t scratch_bytes, float* y, int* idx_out, float* w_out,
+cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shared, int e_lo, int e_n, int rank,
+                                       int G, Geom g, const float* R, const float* normw, float eps, int E,
+                                       int n_shared, int k, const float* X, int T, void* scratch,
+                                       size_t scratch_bytes, float* y, int* idx_out, float* w_out,
                                        float* logits_out, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || e_lo < 0 || e_n < 0 || e_lo + e_n > E ||
-        batched_partial_bytes(g, E, k, T) > scratch_bytes)
+    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || n_shared < 0 || n_shared > 1 ||
+        (n_shared && !shared) || k + n_shared > MAX_TOPK + 1 || G < 1 || rank < 0 || rank >= G || e_n * G != E ||
+        e_lo != rank * e_n || batched_partial_bytes(g, E, n_shared, k, T) > scratch_bytes)
         return cudaErrorInvalidValue;
-    const size_t n_pairs = (size_t)T * k;
+    const int ks = k + n_shared, E_tot = E + n_shared;
+    const size_t n_pairs = (size_t)T * ks;
     uint8_t* p = static_cast<uint8_t*>(scratch);
     auto take = [&](size_t n) {
         uint8_t* r = p;
-        p += (n + 255) & ~(size_t)255;
+        p += r256(n);
         return r;
     };
     unsigned long long* S = reinterpret_cast<unsigned long long*>(take((size_t)T * E * 8));
-    int* active = reinterpret_cast<int*>(take((E + 1) * 4));
+    int* active = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
     uint8_t* xq = take((size_t)T * act_bytes(g.nbH));
-    int* idx = idx_out ? idx_out : reinterpret_cast<int*>(take(n_pairs * 4));
-    float* wts = w_out ? w_out : reinterpret_cast<float*>(take(n_pairs * 4));
-    int* off = reinterpret_cast<int*>(take((E + 1) * 4));
+    int* idx_s = reinterpret_cast<int*>(take(n_pairs * 4));
+    float* wts_s = reinterpret_cast<float*>(take(n_pairs * 4));
+    int* idx = idx_out ? idx_out : idx_s;
+    float* wts = w_out ? w_out : wts_s;
+    int* off = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
     int* list = reinterpret_cast<int*>(take(n_pairs * 4));
     uint8_t* hq = take(n_pairs * act_bytes(g.nbI));
+    float* hf = reinterpret_cast<float*>(take(n_pairs * g.I * 4));
 
+    int dev = 0, optin = 0;
     cudaError_t e;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
+    if (batched_smem_bytes(g) > (size_t)optin) return cudaErrorInvalidValue;
     if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
-    // pairs routed to experts held elsewhere keep y = 0 (their owner adds theirs)
-    if (e_n < E && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
+    // pairs computed on other devices keep y = 0 (their owner adds theirs)
+    if (G > 1 && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
     k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
                                                                                                 g.H, S);
-    k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, S, idx, wts, logits_out, xq);
-    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, E, e_lo, e_n, off, list, active);
-    const int n_act = (int)(n_pairs < (size_t)e_n ? n_pairs : (size_t)e_n);
-    if (n_act == 0) return cudaGetLastError();
-    const size_t sm_gu = (size_t)2 * 32 * g.row_gu;
-    if (sm_gu > 48 * 1024 &&
-        (e = cudaFuncSetAttribute(k_gateup_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
-            cudaSuccess)
-        return e;
-    k_gateup_batched<<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, e_lo, g, off, list, active, k, xq, hq);
+    k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, ks, S, idx, wts, logits_out, xq);
+    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active);
+    const size_t max_act = (size_t)e_n + n_shared;
+    const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
+    const int R_gu = gu_rows(g, (size_t)optin);
+    const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
+    if (R_gu == 32) {
+        if (sm_gu > 48 * 1024 && (e = cudaFuncSetAttribute(k_gateup_batched<32>,
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
+                                     cudaSuccess)
+            return e;
+        k_gateup_batched<32><<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active,
+                                                                        ks, xq, hq, hf);
+    } else {
+        if (sm_gu > 48 * 1024 && (e = cudaFuncSetAttribute(k_gateup_batched<16>,
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
+                                     cudaSuccess)
+            return e;
+        k_gateup_batched<16><<<dim3(g.I / 16, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active,
+                                                                        ks, xq, hq, hf);
+        const long long warps = (long long)n_pairs * g.nbI;
+        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, (int)n_pairs, g, hq);
+    }
     const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
     if (sm_d > 48 * 1024 &&
         (e = cudaFuncSetAttribute(k_down_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_d)) !=
             cudaSuccess)
         return e;
-    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, e_lo, g, off, list,
-                                                                                      active, hq, y);
+    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, shared, E, e_lo, g, off,
+                                                                                      list, active, hq, y);
     return cudaGetLastError();
 }
 
-cudaError_t launch_moe_batched_combine(float* X, int T, int H, int k, const float* wts, const float* y,
+cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    k_combine_batched<<<T, 256, 0, s>>>(X, H, k, wts, y);
+    k_combine_batched<<<T, 256, 0, s>>>(X, H, ks, wts, y);
     return cudaGetLastError();
 }
 
@@ -355,11 +453,11 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
     // the partial step's buffers, then w (unless given) and y at the end of the scratch
     const size_t n_pairs = (size_t)T * k;
     uint8_t* base = static_cast<uint8_t*>(scratch);
-    const size_t part = batched_partial_bytes(g, E, k, T);
+    const size_t part = batched_partial_bytes(g, E, 0, k, T);
     float* wts = w_out ? w_out : reinterpret_cast<float*>(base + part);
-    float* y = reinterpret_cast<float*>(base + part + ((n_pairs * 4 + 255) & ~(size_t)255));
-    cudaError_t e = launch_moe_batched_partial(layer, 0, E, g, R, normw, eps, E, k, X, T, scratch, part, y, idx_out,
-                                               wts, logits_out, s);
+    float* y = reinterpret_cast<float*>(base + part + r256(n_pairs * 4));
+    cudaError_t e = launch_moe_batched_partial(layer, nullptr, 0, E, 0, 1, g, R, normw, eps, E, 0, k, X, T, scratch,
+                                               part, y, idx_out, wts, logits_out, s);
     if (e != cudaSuccess) return e;
     return launch_moe_batched_combine(X, T, g.H, k, wts, y, s);
 }

@@ -1,9 +1,12 @@
 // tg_ep.cu — experts sharded over devices (expert parallelism), one context per rank.
 //
-// Rank r of G holds experts [r * E/G, (r + 1) * E/G) of every layer; routers and
-// norms are replicated.  A layer for T tokens is
+// Rank r of G holds experts [r * E/G, (r + 1) * E/G) of every layer; routers, norms and
+// the optional shared expert (DeepSeek-V3-like: every token, weight 1, after the routed
+// slots) are replicated.  A layer for T tokens is
 //   tgx_ep_moe_partial   routing (the same on every rank), then y[(t, j)] for the
-//                        pairs whose expert is local, 0 for the others
+//                        pairs this rank owns (routed: their expert is local; shared:
+//                        this rank holds the fewest of the token's routed experts),
+//                        0 for the others
 //   (caller)             sum of y over the ranks: an all-reduce (NCCL) or any exact sum
 //   tgx_ep_combine       x[t] += sum_j w[t][j] * y[(t, j)] in slot order
 // Every element of y has exactly one nonzero contribution and sums start from +0, so
@@ -20,12 +23,13 @@
 using tg::Geom;
 
 struct tgx_ep {
-    int device = 0, rank = 0, size = 1, e_lo = 0, e_n = 0;
+    int device = 0, rank = 0, size = 1, e_lo = 0, e_n = 0, n_shared = 0;
     tgx_shape shape{};
     Geom g;
     float eps = 1e-6f;
     size_t layer_bytes = 0;       // e_n experts
     uint8_t* weights = nullptr;   // [L][e_n] local experts, row-split
+    uint8_t* shared = nullptr;    // [L] shared expert (n_shared = 1), row-split
     float* routers = nullptr;     // [L][E][H]
     float* norms = nullptr;       // [L][H]
     uint8_t* staging = nullptr;
@@ -73,8 +77,8 @@ struct Dev {
 void ep_free(tgx_ep* c) {
     if (!c) return;
     Dev dg(c->device);
-    for (void* p : {(void*)c->weights, (void*)c->routers, (void*)c->norms, (void*)c->staging, c->scratch,
-                    (void*)c->wts})
+    for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
+                    c->scratch, (void*)c->wts})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -91,8 +95,8 @@ int ep_alloc(void** p, size_t n, const char* fn) {
 // grow the partial-step scratch and the routing-weight buffer for T tokens
 int ep_reserve(tgx_ep* c, int T, cudaStream_t s, const char* fn) {
     const tgx_shape& sh = c->shape;
-    const size_t need = tg::batched_partial_bytes(c->g, sh.n_experts, sh.top_k, T);
-    const size_t wneed = sizeof(float) * (size_t)T * sh.top_k;
+    const size_t need = tg::batched_partial_bytes(c->g, sh.n_experts, c->n_shared, sh.top_k, T);
+    const size_t wneed = sizeof(float) * (size_t)T * (sh.top_k + c->n_shared);
     if (need <= c->scratch_bytes && wneed <= c->wts_bytes) return TG_OK;
     EP_CUDA(cudaStreamSynchronize(s));
     if (need > c->scratch_bytes) {
@@ -114,7 +118,8 @@ int ep_reserve(tgx_ep* c, int T, cudaStream_t s, const char* fn) {
 
 }  // namespace
 
-extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int ep_rank, int ep_size, tgx_ep** out) {
+extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int n_shared, int ep_rank, int ep_size,
+                             tgx_ep** out) {
     EP_CHECK(shape && out, TG_EINVAL, "tgx_ep_create: null argument");
     *out = nullptr;
     EP_CHECK(Geom::valid_dims(shape->embed, shape->inter), TG_EINVAL,
@@ -124,6 +129,7 @@ extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int ep_rank, in
              TG_EINVAL, "tgx_ep_create: bad expert/top_k/layer counts");
     EP_CHECK(ep_size >= 1 && ep_rank >= 0 && ep_rank < ep_size && shape->n_experts % ep_size == 0, TG_EINVAL,
              "tgx_ep_create: need 0 <= ep_rank < ep_size and n_experts divisible by ep_size");
+    EP_CHECK(n_shared == 0 || n_shared == 1, TG_EINVAL, "tgx_ep_create: n_shared must be 0 or 1");
     int ndev = 0;
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= 0) {
         cudaGetLastError();
@@ -140,6 +146,7 @@ extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int ep_rank, in
     c->e_n = shape->n_experts / ep_size;
     c->e_lo = ep_rank * c->e_n;
     c->layer_bytes = c->g.expert_bytes * c->e_n;
+    c->n_shared = n_shared;
     if (shape->rms_eps > 0.0f) c->eps = shape->rms_eps;
     const int L = shape->n_layers, E = shape->n_experts, H = shape->embed;
     c->staging_bytes = c->g.expert_bytes * 4;
@@ -147,7 +154,8 @@ extern "C" int tgx_ep_create(int device, const tgx_shape* shape, int ep_rank, in
     if ((rc = ep_alloc((void**)&c->weights, c->layer_bytes * L, "tgx_ep_create")) ||
         (rc = ep_alloc((void**)&c->routers, sizeof(float) * (size_t)L * E * H, "tgx_ep_create")) ||
         (rc = ep_alloc((void**)&c->norms, sizeof(float) * (size_t)L * H, "tgx_ep_create")) ||
-        (rc = ep_alloc((void**)&c->staging, c->staging_bytes, "tgx_ep_create"))) {
+        (rc = ep_alloc((void**)&c->staging, c->staging_bytes, "tgx_ep_create")) ||
+        (n_shared && (rc = ep_alloc((void**)&c->shared, c->g.expert_bytes * L, "tgx_ep_create")))) {
         ep_free(c);
         return rc;
     }
@@ -197,6 +205,38 @@ extern "C" int tgx_ep_load_experts(tgx_ep* ep, int layer, int first, int n, cons
     return TG_OK;
 }
 
+extern "C" int tgx_ep_load_shared(tgx_ep* ep, int layer, const void* src, int src_on_device) {
+    EP_CHECK(ep && src, TG_EINVAL, "tgx_ep_load_shared: null argument");
+    EP_CHECK(ep->n_shared == 1, TG_EINVAL, "tgx_ep_load_shared: context has no shared expert");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_load_shared: layer out of range");
+    Dev dg(ep->device);
+    const Geom& g = ep->g;
+    EP_CUDA(cudaMemcpyAsync(ep->staging, src, g.expert_bytes,
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ep->s));
+    uint8_t* dst = ep->shared + (size_t)layer * g.expert_bytes;
+    EP_CUDA(tg::launch_repack_rows(ep->staging, dst, 2LL * g.I, g.nbH, ep->s));
+    EP_CUDA(tg::launch_repack_rows(ep->staging + 2 * g.t_gu, dst + 2 * g.t_gu, g.H, g.nbI, ep->s));
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_read_expert(tgx_ep* ep, int layer, int e, void* dst_host) {
+    EP_CHECK(ep && dst_host, TG_EINVAL, "tgx_ep_read_expert: null argument");
+    const bool is_shared = e == ep->shape.n_experts;
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers &&
+                 ((e >= ep->e_lo && e < ep->e_lo + ep->e_n) || (is_shared && ep->n_shared)),
+             TG_EINVAL, "tgx_ep_read_expert: layer out of range or expert not held by this rank");
+    Dev dg(ep->device);
+    const Geom& g = ep->g;
+    const uint8_t* src = is_shared ? ep->shared + (size_t)layer * g.expert_bytes
+                                   : ep->weights + (size_t)layer * ep->layer_bytes + (size_t)(e - ep->e_lo) * g.expert_bytes;
+    EP_CUDA(tg::launch_unpack_rows(src, ep->staging, 2LL * g.I, g.nbH, ep->s));
+    EP_CUDA(tg::launch_unpack_rows(src + 2 * g.t_gu, ep->staging + 2 * g.t_gu, g.H, g.nbI, ep->s));
+    EP_CUDA(cudaMemcpyAsync(dst_host, ep->staging, g.expert_bytes, cudaMemcpyDeviceToHost, ep->s));
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    return TG_OK;
+}
+
 extern "C" int tgx_ep_set_router(tgx_ep* ep, int layer, const float* R, int src_on_device) {
     EP_CHECK(ep && R, TG_EINVAL, "tgx_ep_set_router: null argument");
     EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_set_router: layer out of range");
@@ -232,13 +272,16 @@ extern "C" int tgx_ep_fill_synthetic(tgx_ep* ep, uint64_t seed, float w_sigma, f
         const size_t nr = (size_t)sh.n_experts * sh.embed;
         EP_CUDA(tg::launch_fill_normal(ep->routers + (size_t)l * nr, (long long)nr, seed ^ 0x5DEECE66Dull,
                                        (unsigned long long)l * nr * 2, r_sigma, ep->s));
+        if (ep->n_shared)   // its own stream of values: layer l's shared expert at l * per_expert
+            EP_CUDA(tg::launch_fill_experts_q4_0(ep->shared + (size_t)l * g.expert_bytes, 1, g, seed ^ 0xC2B2AE3D27D4EB4Full,
+                                                 (unsigned long long)l * per_expert, w_sigma, ep->s));
     }
     EP_CUDA(cudaStreamSynchronize(ep->s));
     return TG_OK;
 }
 
 extern "C" size_t tgx_ep_y_floats(const tgx_ep* ep, int T) {
-    return ep && T > 0 ? (size_t)T * ep->shape.top_k * ep->shape.embed : 0;
+    return ep && T > 0 ? (size_t)T * (ep->shape.top_k + ep->n_shared) * ep->shape.embed : 0;
 }
 
 extern "C" int tgx_ep_moe_partial(tgx_ep* ep, int layer, const float* x_dev, int T, float* y_dev, void* stream) {
@@ -254,10 +297,12 @@ extern "C" int tgx_ep_moe_partial(tgx_ep* ep, int layer, const float* x_dev, int
     EP_TRY(ep_reserve(ep, T, s, "tgx_ep_moe_partial"));
     const tgx_shape& sh = ep->shape;
     const size_t nr = (size_t)sh.n_experts * sh.embed;
-    EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, ep->e_lo, ep->e_n, ep->g,
-                                           ep->routers + (size_t)layer * nr, ep->norms + (size_t)layer * sh.embed,
-                                           ep->eps, sh.n_experts, sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes,
-                                           y_dev, nullptr, ep->wts, nullptr, s));
+    const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
+    EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, shared, ep->e_lo, ep->e_n,
+                                           ep->rank, ep->size, ep->g, ep->routers + (size_t)layer * nr,
+                                           ep->norms + (size_t)layer * sh.embed, ep->eps, sh.n_experts, ep->n_shared,
+                                           sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, y_dev, nullptr, ep->wts,
+                                           nullptr, s));
     ep->last_T = T;
     return TG_OK;
 }
@@ -266,7 +311,7 @@ extern "C" int tgx_ep_combine(tgx_ep* ep, float* x_dev, int T, const float* y_de
     EP_CHECK(ep && x_dev && y_dev, TG_EINVAL, "tgx_ep_combine: null argument");
     EP_CHECK(T >= 1 && T == ep->last_T, TG_EINVAL, "tgx_ep_combine: T must match the last tgx_ep_moe_partial");
     Dev dg(ep->device);
-    EP_CUDA(tg::launch_moe_batched_combine(x_dev, T, ep->shape.embed, ep->shape.top_k, ep->wts, y_dev,
-                                           (cudaStream_t)stream));
+    EP_CUDA(tg::launch_moe_batched_combine(x_dev, T, ep->shape.embed, ep->shape.top_k + ep->n_shared, ep->wts,
+                                           y_dev, (cudaStream_t)stream));
     return TG_OK;
 }

@@ -82,19 +82,24 @@ size_t batched_smem_bytes(const Geom& g);
 cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
                                int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
                                float* w_out, float* logits_out, cudaStream_t s);
-// The two halves of launch_moe_batched, for experts sharded over devices.  Partial:
-// routing of all T tokens (every device computes the same), then y[(t, j)][H] for the
-// pairs whose expert lies in [e_lo, e_lo + e_n) (layer points at expert e_lo), y = 0
-// for the others; w_out receives the routing weights [T][k].  Scratch of
-// batched_partial_bytes.  Combine: X[t] += sum_j w[t][j] * y[(t, j)] in slot order.
-// With the y of every device summed in between (one nonzero term per element, so the
-// sum is exact), the result is the single-device one bit for bit.
-size_t batched_partial_bytes(const Geom& g, int E, int k, int T);
-cudaError_t launch_moe_batched_partial(const uint8_t* layer, int e_lo, int e_n, Geom g, const float* R,
-                                       const float* normw, float eps, int E, int k, const float* X, int T,
-                                       void* scratch, size_t scratch_bytes, float* y, int* idx_out, float* w_out,
+// The two halves of launch_moe_batched, generalised to experts sharded over G devices
+// and an optional shared expert.  Partial: routing of all T tokens (every device
+// computes the same), then y[(t, j)][H] for the pairs this device owns (routed slot j < k:
+// its expert lies in [e_lo, e_lo + e_n), e_lo = rank * e_n, e_n * G = E; the shared slot
+// j = k when n_shared = 1: this device holds the fewest of token t's routed experts, ties
+// to (t + i) mod G, smallest i), y = 0 for the others when G > 1.  layer points at
+// expert e_lo, shared at the shared expert (weight 1, id E).  w_out receives the
+// routing weights [T][k + n_shared].  Scratch of batched_partial_bytes.  Combine:
+// X[t] += sum_j w[t][j] * y[(t, j)] in slot order (ks = k + n_shared slots).  With the y
+// of every device summed in between (one nonzero term per element, so the sum is
+// exact), the result is the single-device one bit for bit.
+size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T);
+cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shared, int e_lo, int e_n, int rank,
+                                       int G, Geom g, const float* R, const float* normw, float eps, int E,
+                                       int n_shared, int k, const float* X, int T, void* scratch,
+                                       size_t scratch_bytes, float* y, int* idx_out, float* w_out,
                                        float* logits_out, cudaStream_t s);
-cudaError_t launch_moe_batched_combine(float* X, int T, int H, int k, const float* wts, const float* y,
+cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s);
 
 // The reference library's own formats (tg_kquant.cu).  fmt: KQ_Q4K (ggml Q4_K

@@ -1,7 +1,9 @@
 """Experts sharded over GPUs (expert parallelism), one process per GPU.
 
-Rank r of G holds experts [r*E/G, (r+1)*E/G) of every layer; the routers and FFN
-norms are replicated, so every rank routes every token the same way.  One MoE layer
+Rank r of G holds experts [r*E/G, (r+1)*E/G) of every layer; the routers, FFN norms
+and the optional shared expert (n_shared=1: slot k of every token, weight 1) are
+replicated, so every rank routes every token the same way.  A token's shared-expert
+output is computed by the rank holding the fewest of its routed experts.  One MoE layer
 (tinygiant/engine.py:229-258 for each of T tokens) is
 
     tgx_ep_moe_partial   y[(t, j)] for the (token, slot) pairs whose expert is local, else 0
@@ -35,15 +37,32 @@ def expert_range(n_experts: int, rank: int, size: int):
     return rank * n, n
 
 
+def shared_owner(routed_ids, t: int, n_experts: int, size: int) -> int:
+    """The rank that computes token t's shared-expert output: the one holding the fewest
+    of the token's routed experts, ties to rank (t + i) mod size with the smallest i
+    (the rule the partial step's kernels apply)."""
+    e_n = n_experts // size
+    counts = [0] * size
+    for e in routed_ids:
+        counts[int(e) // e_n] += 1
+    best, best_n = 0, 1 << 30
+    for i in range(size):
+        r = (t + i) % size
+        if counts[r] < best_n:
+            best, best_n = r, counts[r]
+    return best
+
+
 class EPMoEModel:
     def __init__(self, embed=C.EMBED_DIM, inter=C.EXPERT_INTERMEDIATE, n_experts=C.N_EXPERTS,
-                 top_k=C.N_EXPERTS_USED, n_layers=C.N_LAYERS, rank=0, size=1, device=0, group=None):
+                 top_k=C.N_EXPERTS_USED, n_layers=C.N_LAYERS, rank=0, size=1, device=0, group=None, n_shared=0):
         self.lib = get_lib()
         self.shape = TgxShape(embed, inter, n_experts, top_k, n_layers, C.RMS_EPS)
         self.embed, self.inter, self.n_experts, self.top_k, self.n_layers = embed, inter, n_experts, top_k, n_layers
-        self.rank, self.size, self.device, self.group = rank, size, device, group
+        self.rank, self.size, self.device, self.group, self.n_shared = rank, size, device, group, n_shared
         h = ctypes.c_void_p()
-        check(self.lib.tgx_ep_create(device, ctypes.byref(self.shape), rank, size, ctypes.byref(h)), self.lib)
+        check(self.lib.tgx_ep_create(device, ctypes.byref(self.shape), n_shared, rank, size, ctypes.byref(h)),
+              self.lib)
         self._ep = h
         first, n = ctypes.c_int(), ctypes.c_int()
         check(self.lib.tgx_ep_expert_range(h, ctypes.byref(first), ctypes.byref(n)), self.lib)
@@ -74,6 +93,18 @@ class EPMoEModel:
         n = blob.size // self.expert_bytes
         assert n * self.expert_bytes == blob.size
         check(self.lib.tgx_ep_load_experts(self._ep, layer, first, n, blob.ctypes.data, 0), self.lib)
+
+    def load_shared(self, layer: int, blob: np.ndarray):
+        """The layer's shared expert (n_shared = 1): one ggml Q4_0 blob gate | up | down."""
+        blob = np.ascontiguousarray(blob, dtype=np.uint8)
+        assert blob.size == self.expert_bytes
+        check(self.lib.tgx_ep_load_shared(self._ep, layer, blob.ctypes.data, 0), self.lib)
+
+    def read_expert(self, layer: int, e: int) -> np.ndarray:
+        """Expert e (local routed id, or n_experts for the shared expert) as a ggml blob."""
+        out = np.empty(self.expert_bytes, np.uint8)
+        check(self.lib.tgx_ep_read_expert(self._ep, layer, e, out.ctypes.data), self.lib)
+        return out
 
     def set_router(self, layer: int, R: np.ndarray):
         R = np.ascontiguousarray(R, dtype=np.float32)
