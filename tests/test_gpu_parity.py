@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from tinygiant_b200 import _constants as C
-from tinygiant_b200._lib import TG_EUNSUPPORTED, TG_FMT_Q6_K, check
+from tinygiant_b200._lib import TG_EINVAL, check
 
 pytestmark = pytest.mark.gpu
 
@@ -164,8 +164,8 @@ def test_expert_forward_mixed_and_formats(lib, oracle):
     g, u, d = blob[:t].copy(), blob[t:2 * t].copy(), blob[2 * t:].copy()
     check(lib.tg_expert_forward_mixed(p(g), p(u), p(d), 3, p(x), p(b), ctypes.c_float(0.3), H, I), lib)
     assert np.array_equal(a, b)
-    assert lib.tg_expert_forward_mixed(p(g), p(u), p(d), TG_FMT_Q6_K, p(x), p(b), ctypes.c_float(0.3),
-                                       H, I) == TG_EUNSUPPORTED
+    # down formats 0 / 1 / 2 are the reference's own (tests/test_gpu_kquant.py); others are rejected
+    assert lib.tg_expert_forward_mixed(p(g), p(u), p(d), 9, p(x), p(b), ctypes.c_float(0.3), H, I) == TG_EINVAL
 
 
 def test_expert_forward_zero_input(lib, oracle):
