@@ -53,13 +53,18 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--multi", action="store_true", help="three kernels per layer instead of the fused kernel")
     ap.add_argument("--layers", type=int, default=L, help="fewer layers, for small profiling cases only")
-    ap.add_argument("--tokens", type=int, default=1, help="T > 1: T tokens per step through the batched path")
+    ap.add_argument("--tokens", type=str, default="1",
+                    help="T > 1: T tokens per step through the batched path; with --ep a comma list runs each "
+                         "batch size on one filled model (one JSON line each)")
     ap.add_argument("--tier", type=int, default=-1,
                     help="P >= 0: host tier with P experts per layer pinned in HBM, Zipf(1.1) routing (configs[3])")
     ap.add_argument("--cache-slots", type=int, default=24, help="HBM cache slots of the host tier")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism: under torchrun each rank holds E/N experts of every layer and "
                          "the ranks decode the same --tokens T tokens together (NCCL all-reduce per layer)")
+    ap.add_argument("--shape", choices=["qwen3", "dsv3"], default="qwen3",
+                    help="with --ep: qwen3 (configs[2]) or the DeepSeek-V3-like configs[4] (hidden 7168, "
+                         "inter 2048, 256 routed + 1 shared expert, 58 layers, as many as fit per GPU)")
     ap.add_argument("--format", choices=["q4_0", "q4_k", "q4_k_m"], default="q4_0",
                     help="q4_k / q4_k_m: the reference library's own formats (all-Q4_K experts, or Q4_K "
                          "gate/up with Q6_K down), expert FFN of 48 layers x top-8 per token")
@@ -717,13 +722,40 @@ def run_ep(args):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     dist = init_dist(ws, "nccl") if ws > 1 else None
-    T, NL = args.tokens, args.layers
-    ep = EPMoEModel(H, I, E, K_TOP, NL, rank=rank, size=ws, device=local)
+    T = args.tokens
+    if args.shape == "dsv3":
+        h, inter, e_all, n_sh, full_layers = 7168, 2048, 256, 1, 58
+    else:
+        h, inter, e_all, n_sh, full_layers = H, I, E, 0, L
+    eb = 3 * inter * (h // 32) * 18
+    per_layer = (e_all // ws + n_sh) * eb + e_all * h * 4
+    if args.shape == "dsv3":   # per-layer subset: the layers that fit this GPU (all 58 from 8 GPUs up)
+        free, _ = torch.cuda.mem_get_info()
+        NL = max(1, min(full_layers, int(0.85 * (free - (8 << 30)) // per_layer)))
+        if dist:
+            t = torch.tensor([NL], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            NL = int(t.item())
+        if args.layers != L:
+            NL = min(NL, args.layers)
+    else:
+        NL = args.layers
+    ep = EPMoEModel(h, inter, e_all, K_TOP, NL, rank=rank, size=ws, device=local, n_shared=n_sh)
     ep.fill_synthetic(args.seed)                          # one model, sharded: the same seed on every rank
+    for T in args.token_list:
+        ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist)
+    ep.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
+def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist):
+    import torch
     K, W = args.steps, max(3, args.warmup)
     gen = torch.Generator(device="cuda").manual_seed(args.seed + 1)
-    pool = [torch.randn(T, H, generator=gen, device="cuda") for _ in range(4)]
-    X = torch.empty(T, H, device="cuda")
+    pool = [torch.randn(T, h, generator=gen, device="cuda") for _ in range(4)]
+    X = torch.empty(T, h, device="cuda")
     stream = torch.cuda.current_stream()
     X.copy_(pool[0])
     ep.decode(X)                                          # allocates scratch and the exchange buffer
@@ -783,32 +815,49 @@ def run_ep(args):
         ms, ems = float(t[0]), float(t[1])
     assert torch.isfinite(Yh).all()
     del graph                                             # holds NCCL calls: released before the group
-    ep.close()
     if rank == 0:
-        distinct = min(E, T * K_TOP)
+        distinct = min(e_all, T * K_TOP)
+        name = "DeepSeek-V3-like shape" if args.shape == "dsv3" else "Qwen3-30B-A3B shape"
+        value = T * K / (ms / 1000.0)
+        # expected distinct routed experts per layer under uniform routing, + the shared one
+        exp_distinct = e_all * (1.0 - (1.0 - K_TOP / e_all) ** T) + n_sh
+        alg = NL * exp_distinct * eb
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        peak = peaks.get("hbm_gbs", 6650.0)
+        achieved = alg / (ms / K / 1000.0) / 1e9
         print(json.dumps({
-            "metric": f"expert-parallel MoE decode tok/s (Qwen3-30B-A3B shape, {T} tokens per step, EP over {ws} GPUs)",
-            "value": T * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "metric": f"expert-parallel MoE decode tok/s ({name}, {T} tokens per step, EP over {ws} GPUs)",
+            "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"configs[2]/[4]: {T} tokens per step, {NL} layers, experts sharded {E // ws} "
-                                   f"per GPU, NCCL all-reduce of y per layer",
-                       "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "layers": NL, "tokens": T,
-                       "parallelism": f"ep{ws}", "cuda_graph": graphed},
-            "exchange_bytes_per_layer": T * K_TOP * H * 4,
-            "weights_read_upper_bound_gbs_per_gpu": NL * min(E // ws, distinct) * EXPERT_BYTES / (ms / K / 1000.0) / 1e9,
-            "e2e": {"value": T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
-                    "d2h_bytes_per_step": T * H * 4},
-            "gpu_launches": 6 * NL * K,
+            "config": {"workload": f"{'configs[4]' if args.shape == 'dsv3' else 'configs[2]'}: {T} tokens per step, "
+                                   f"{NL} of {full_layers} layers, experts sharded {e_all // ws} per GPU"
+                                   f"{' + the shared expert' if n_sh else ''}, NCCL all-reduce of y per layer",
+                       "hidden": h, "inter": inter, "experts": e_all, "shared_experts": n_sh, "top_k": K_TOP,
+                       "layers": NL, "full_layers": full_layers, "tokens": T, "parallelism": f"ep{ws}",
+                       "cuda_graph": graphed},
+            "tok_s_full_depth": value * NL / full_layers,
+            "exchange_bytes_per_layer": T * (K_TOP + n_sh) * h * 4,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ws, "unit": "GB/s",
+                         "frac": achieved / (peak * ws), "traffic": None,
+                         "algorithmic_bytes": alg,
+                         "algorithmic_bytes_def": "expected distinct experts per layer (uniform routing) + shared, "
+                                                  "x expert bytes x layers; peak = per-GPU peak x GPUs",
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback"},
+            "e2e": {"value": T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * h * 4,
+                    "d2h_bytes_per_step": T * h * 4},
+            "gpu_launches": (6 + (1 if args.shape == "dsv3" else 0)) * NL * K,
             "clocks": clocks.summary(),
         }), flush=True)
-    if dist:
-        dist.destroy_process_group()
-    return 0
 
 
 def main():
     args = parse()
+    token_list = [int(t) for t in str(args.tokens).split(",")]
+    if len(token_list) > 1 and not args.ep:
+        raise SystemExit("a list of --tokens needs --ep")
+    args.token_list = token_list
+    args.tokens = token_list[0]
     if args.impl == "reference":
         return run_reference(args)
     if args.ep:
