@@ -30,9 +30,16 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
-# NCCL's own messages (its version line under NCCL_DEBUG=VERSION, for one) go to
-# stderr: stdout carries only the JSON result line
-os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+# stdout carries only the JSON result lines: they go to a private copy of the original
+# stdout, and file descriptor 1 is pointed at stderr, so whatever libraries print there
+# (NCCL's version line when NCCL_DEBUG is set, for one) lands in the log instead
+_RESULT = os.fdopen(os.dup(1), "w")
+os.dup2(2, 1)
+
+
+def emit(obj) -> None:
+    _RESULT.write(json.dumps(obj) + "\n")
+    _RESULT.flush()
 
 METRIC = "expert-FFN decode tok/s (Qwen3-30B-A3B shape) & Q4 weight-read HBM GB/s"
 H, I, E, K_TOP, L = 2048, 768, 128, 8, 48
@@ -202,7 +209,7 @@ def run_reference(args):
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(out), flush=True)
+    emit(out)
     return 0
 
 
@@ -359,7 +366,7 @@ def run_ours(args):
             "gpu_launches": kernels_per_step * K,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(out), flush=True)
+        emit(out)
     if ws > 1:
         dist.destroy_process_group()
     return 0
@@ -434,7 +441,7 @@ def run_batched(args):
             "gpu_launches": 7 * NL * K,
             "clocks": clocks.summary(),
         }
-        print(json.dumps(out), flush=True)
+        emit(out)
     if dist:
         dist.destroy_process_group()
     return 0
@@ -506,7 +513,7 @@ def run_tier(args):
     ms = ev0.elapsed_time(ev1)
     hits, misses, nbytes = cache.hits - h0, cache.misses - m0, cache.bytes_h2d - b0
     model.close()
-    print(json.dumps({
+    emit(({
         "metric": f"host-tier expert decode tok/s (Qwen3-30B-A3B shape, {P} experts per layer pinned in HBM)",
         "value": K / (ms / 1000.0), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -516,7 +523,7 @@ def run_tier(args):
                    "layers": NL, "pinned_per_layer": P, "cache_slots": args.cache_slots},
         "hit_rate": hits / max(1, hits + misses), "misses_per_token": misses / K,
         "h2d_gbs": nbytes / (ms / 1000.0) / 1e9, "wall_tok_s": K / wall,
-    }), flush=True)
+    }))
     return 0
 
 
@@ -687,7 +694,7 @@ def run_kquant(args):
     alg = NL * K_TOP * expert_bytes
     achieved = alg / (graph_ms / 1000.0) / 1e9
     if rank == 0:
-        print(json.dumps({
+        emit(({
             "metric": f"expert-FFN decode tok/s, reference formats ({fmt.upper()}, Qwen3-30B-A3B shape)",
             "value": ws * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -706,7 +713,7 @@ def run_kquant(args):
                     "d2h_bytes_per_step": H * 4},
             "gpu_launches": 2 * NL * K,
             "clocks": clocks.summary(),
-        }), flush=True)
+        }))
     if dist:
         dist.destroy_process_group()
     return 0
@@ -825,7 +832,7 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
         peak = peaks.get("hbm_gbs", 6650.0)
         achieved = alg / (ms / K / 1000.0) / 1e9
-        print(json.dumps({
+        emit(({
             "metric": f"expert-parallel MoE decode tok/s ({name}, {T} tokens per step, EP over {ws} GPUs)",
             "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -848,7 +855,7 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
                     "d2h_bytes_per_step": T * h * 4},
             "gpu_launches": (6 + (1 if args.shape == "dsv3" else 0)) * NL * K,
             "clocks": clocks.summary(),
-        }), flush=True)
+        }))
 
 
 def main():
