@@ -196,6 +196,10 @@ int tgx_moe_batched(tgx_ctx *ctx, int layer, float *x_dev, int T, void *stream);
 
 /* All L MoE blocks for T tokens, layer after layer (tgx_moe_batched for l = 0 .. L-1). */
 int tgx_decode_batched(tgx_ctx *ctx, float *x_dev, int T, void *stream);
+/* expert matmul kernels of tgx_moe_batched / tgx_decode_batched: 0 auto (tensor cores,
+ * tcgen05, when experts average >= 16 pairs), 1 dp4a, 2 tensor cores; all give the same
+ * bits.  tgx_sync_status reports an expired bounded wait of the tensor-core kernels. */
+int tgx_set_batched_kernels(tgx_ctx *ctx, int kernels);
 
 /* The MoE block of layer `layer` over a given list of experts (routing decided by the
  * caller, e.g. a host-tier cache): x += sum_j weights[j] * expert_j((x * scale) * ffn_norm),
@@ -273,6 +277,12 @@ int tgx_ep_fill_synthetic(tgx_ep *ep, uint64_t seed, float w_sigma, float r_sigm
 size_t tgx_ep_y_floats(const tgx_ep *ep, int T);
 int tgx_ep_moe_partial(tgx_ep *ep, int layer, const float *x_dev, int T, float *y_dev, void *stream);
 int tgx_ep_combine(tgx_ep *ep, float *x_dev, int T, const float *y_dev, void *stream);
+/* expert matmul kernels of the partial step: 0 auto (tensor cores when experts average
+ * >= 16 pairs), 1 dp4a, 2 tensor cores (tcgen05); all give the same bits */
+int tgx_ep_set_kernels(tgx_ep *ep, int kernels);
+/* synchronise `stream`; TG_ETIMEOUT (and the flag cleared) if a tensor-core kernel's
+ * bounded wait expired since the last call */
+int tgx_ep_status(tgx_ep *ep, void *stream);
 
 /* ===================== the reference's formats on device pointers ===================== */
 

@@ -2,7 +2,8 @@
 expert's weights are read once per layer): bit-exact against the CPU oracle's
 per-token MoE block (tinygiant/engine.py:229-258 for every row) and against the
 single-token path, including a token count that leaves experts with no tokens and
-chained layers."""
+chained layers, with the expert matmuls on dp4a (kernels=1) and on the tensor
+cores (kernels=2, tcgen05)."""
 import numpy as np
 import pytest
 
@@ -29,11 +30,13 @@ def build_model(oracle, H, I, E, k, L, seed):
     return m, blobs, Rs, Ns, rng
 
 
+@pytest.mark.parametrize("kernels", [1, 2])
 @pytest.mark.parametrize("T", [1, 5, 64, 257])
-def test_batched_layer_matches_oracle_and_single_token(oracle, T):
+def test_batched_layer_matches_oracle_and_single_token(oracle, T, kernels):
     import torch
     H, I, E, k = 512, 256, 16, 4
     m, blobs, Rs, Ns, rng = build_model(oracle, H, I, E, k, 1, seed=T)
+    m.set_batched_kernels(kernels)
     X = (rng.standard_normal((T, H)) * 1.5).astype(np.float32)
     want = oracle.moe_block_batched(blobs[0], Rs[0], X, k, H, I, normw=Ns[0])
     Xd = torch.from_numpy(X.copy()).cuda()
@@ -48,18 +51,40 @@ def test_batched_layer_matches_oracle_and_single_token(oracle, T):
     m.close()
 
 
-def test_batched_decode_qwen_shape(oracle):
+@pytest.mark.parametrize("kernels,T", [(1, 24), (2, 24), (2, 600)])
+def test_batched_decode_qwen_shape(oracle, kernels, T):
     import torch
-    H, I, E, k, L, T = C.EMBED_DIM, C.EXPERT_INTERMEDIATE, C.N_EXPERTS, C.N_EXPERTS_USED, 2, 24
+    H, I, E, k, L = C.EMBED_DIM, C.EXPERT_INTERMEDIATE, C.N_EXPERTS, C.N_EXPERTS_USED, 2
     m, blobs, Rs, Ns, rng = build_model(oracle, H, I, E, k, L, seed=3)
+    m.set_batched_kernels(kernels)
     X = rng.standard_normal((T, H)).astype(np.float32)
     want = X
     for l in range(L):
         want = oracle.moe_block_batched(blobs[l], Rs[l], want, k, H, I, normw=Ns[l])
     Xd = torch.from_numpy(X.copy()).cuda()
     m.decode_batched(Xd)
-    torch.cuda.synchronize()
+    m.sync_status()
     assert np.array_equal(Xd.cpu().numpy(), want)
+    m.close()
+
+
+def test_tensor_core_and_dp4a_paths_agree_on_many_tokens():
+    # experts with more than one 32-token tile, every expert active
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    H, I, E, k, L, T = C.EMBED_DIM, C.EXPERT_INTERMEDIATE, C.N_EXPERTS, C.N_EXPERTS_USED, 1, 1024
+    m = MoEModel(H, I, E, k, L)
+    m.fill_synthetic(9)
+    X = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(4), device="cuda")
+    outs = []
+    for kernels in (1, 2, 0):
+        m.set_batched_kernels(kernels)
+        Xd = X.clone()
+        m.decode_batched(Xd)
+        m.sync_status()
+        outs.append(Xd)
+    assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32))
+    assert torch.equal(outs[0].view(torch.int32), outs[2].view(torch.int32))
     m.close()
 
 

@@ -20,7 +20,7 @@ H, I, E, K = 2048, 768, 128, 8
 
 
 @pytest.mark.parametrize("G", [2, 4, 8])
-@pytest.mark.parametrize("T", [1, 5, 64])
+@pytest.mark.parametrize("T", [1, 5, 64, 300])
 def test_ep_emulated_matches_single_gpu(G, T):
     import torch
     from tinygiant_b200.engine import MoEModel
@@ -66,8 +66,8 @@ def _emulate(ranks, X, L):
         ranks[0].combine(X, total)
 
 
-@pytest.mark.parametrize("G", [1, 2, 4])
-def test_ep_shared_expert_matches_oracle(oracle, G):
+@pytest.mark.parametrize("G,kernels", [(1, 1), (2, 1), (4, 1), (1, 2), (2, 2)])
+def test_ep_shared_expert_matches_oracle(oracle, G, kernels):
     # host-made weights (oracle quantiser), a shared expert, two chained layers
     import numpy as np
     import torch
@@ -81,6 +81,7 @@ def test_ep_shared_expert_matches_oracle(oracle, G):
     norms = [rng.uniform(0.5, 1.5, h).astype(np.float32) for _ in range(L)]
     ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G, n_shared=1) for r in range(G)]
     for ep in ranks:
+        ep.set_kernels(kernels)
         for l in range(L):
             ep.load_experts(l, ep.first, blobs[l][ep.first * eb:(ep.first + ep.n_local) * eb])
             ep.load_shared(l, shared[l])
@@ -108,9 +109,10 @@ def test_ep_dsv3_width_matches_oracle(oracle):
     rng = np.random.default_rng(5)
     R = (rng.standard_normal((e, h)) * 0.02).astype(np.float32)
     ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G, n_shared=1) for r in range(G)]
-    for ep in ranks:
+    for r, ep in enumerate(ranks):
         ep.fill_synthetic(123)
         ep.set_router(0, R)
+        ep.set_kernels(1 + r % 2)          # dp4a on one rank, tensor cores on the other
     blob = np.concatenate([ranks[r].read_expert(0, x) for r in range(G)
                            for x in range(ranks[r].first, ranks[r].first + ranks[r].n_local)])
     shared = ranks[0].read_expert(0, e)

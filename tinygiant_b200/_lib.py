@@ -88,6 +88,9 @@ PROTOTYPES = {
     "tgx_ep_y_floats": (SZ, [VP, CI]),
     "tgx_ep_moe_partial": (CI, [VP, CI, VP, CI, VP, VP]),
     "tgx_ep_combine": (CI, [VP, VP, CI, VP, VP]),
+    "tgx_ep_set_kernels": (CI, [VP, CI]),
+    "tgx_ep_status": (CI, [VP, VP]),
+    "tgx_set_batched_kernels": (CI, [VP, CI]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),
     "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),

@@ -32,7 +32,27 @@ namespace tg {
 namespace {
 
 constexpr int RT_TOK = 4;         // tokens per router CTA
-constexpr int DOWN_ROWS = 16;     // output rows per down CTA
+constexpr int DOWN_ROWS = 16;     // output rows per down CTA (2 per warp)
+constexpr int DOWN_TOK = 16;      // tokens per pass of the down CTA (2 rows x 16 tokens = 32 sums)
+
+// Sum each of 32 per-lane values over the warp with the same pairing tree as 32
+// separate xor butterflies (so the same bits), in 31 shuffles: at offsets 16, 8, 4, 2, 1
+// each lane hands half of its remaining values to its partner and keeps the other half
+// (the upper half when the lane has that offset's bit).  Value j ends in lane j.
+__device__ __forceinline__ float warp_sum32_transposed(float (&v)[32], int lane) {
+    __syncwarp();
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int i = 0; i < o; i++) {
+            const float send = up ? v[i] : v[i + o];
+            const float keep = up ? v[i + o] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+        }
+    }
+    return v[0];
+}
 
 // grid (ceil(T / RT_TOK), ceil(E / 8), H / 256), 256 threads: warp w adds expert
 // 8 * blockIdx.y + w's fixed-point partial sums over a 256-column chunk for RT_TOK tokens
@@ -183,9 +203,13 @@ __device__ __forceinline__ const uint8_t* expert_base(const uint8_t* layer, cons
 }
 
 // grid (I / R, active experts), 256 threads.  CTA (c, a) takes the a-th active expert e and
-// stages rows R*c .. R*c+R-1 of its gate and up in shared memory, then for every pair p
-// routed to e: R/8 rows per warp and h = silu(g) * u; with R = 32 the unit is one Q8_0
-// block of h, quantised here into hq[p], with R = 16 h goes to hf[p] for k_quant_h.
+// stages rows R*c .. R*c+R-1 of its gate and up in shared memory, then takes the pairs
+// routed to e in tiles of P = 32 / (R/8) tokens: each warp owns R/8 rows, each lane runs
+// the lane-strided block chains of those rows for every token of the tile (a staged
+// weight block is read once per tile), and two transposed reductions leave lane l with
+// the gate and up sums of (row l / P, token l % P).  With R = 32 the unit is one Q8_0
+// block of h: warp w quantises token w's 32 values into hq[p]; with R = 16 h goes to
+// hf[p] for k_quant_h.  Per (row, token) the arithmetic is exactly the single-token one.
 template <int R>
 __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer,
                                                         const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
@@ -193,9 +217,11 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
                                                         const int* __restrict__ active, int ks,
                                                         const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq,
                                                         float* __restrict__ hf) {
-    constexpr int RW = R / 8;   // rows per warp
+    constexpr int RW = R / 8;        // rows per warp
+    constexpr int P = 32 / RW;       // tokens per tile
     extern __shared__ __align__(16) uint8_t smem[];   // gate rows | up rows
-    __shared__ float sh[32];
+    __shared__ float sh[P][32];      // h of the tile (R = 32)
+    __shared__ int sp[P];            // the tile's pairs
     if ((int)blockIdx.y >= active[0]) return;
     const int e = active[1 + blockIdx.y], c = blockIdx.x;
     const int p0 = off[e], n = off[e + 1] - p0;
@@ -213,66 +239,79 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
             d[n16 + i] = __ldg(su + i);
         }
     }
-    __syncthreads();
     const uint8_t* gate = smem;
     const uint8_t* up = smem + unit;
     const int nb = g.nbH, i0 = warp * RW;
     const size_t abx = act_bytes(nb), abh = act_bytes(g.nbI);
-    for (int q = 0; q < n; q++) {
-        const int p = list[p0 + q], t = p / ks;
-        const ActView xa = act_view(xq + (size_t)t * abx, nb);
-        float ag[RW], au[RW];
+    for (int q0 = 0; q0 < n; q0 += P) {
+        const int nt = min(P, n - q0);
+        __syncthreads();   // the previous tile's sh / sp are consumed (and, first time, the weights staged)
+        if (threadIdx.x < P) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
+        __syncthreads();
+        float ag[32], au[32];   // [row r][token t] at r * P + t
 #pragma unroll
-        for (int r = 0; r < RW; r++) ag[r] = au[r] = 0.0f;
+        for (int i = 0; i < 32; i++) ag[i] = au[i] = 0.0f;
         for (int b = lane; b < nb; b += 32) {
-            const XBlk xb = load_xblk(xa, b);
+            uint4 wg[RW], wu[RW];
+            float dg[RW], du[RW];
 #pragma unroll
             for (int r = 0; r < RW; r++) {
                 const uint8_t* rg = gate + (size_t)(i0 + r) * g.row_gu;
                 const uint8_t* ru = up + (size_t)(i0 + r) * g.row_gu;
-                const uint4 wg = *reinterpret_cast<const uint4*>(rg + 16 * b);
-                const uint4 wu = *reinterpret_cast<const uint4*>(ru + 16 * b);
-                const float dg = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 16 * (size_t)nb + 2 * b));
-                const float du = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru + 16 * (size_t)nb + 2 * b));
-                ag[r] = __fadd_rn(ag[r], block_term(block_sumi(wg, xb), dg, xb.d));
-                au[r] = __fadd_rn(au[r], block_term(block_sumi(wu, xb), du, xb.d));
+                wg[r] = *reinterpret_cast<const uint4*>(rg + 16 * b);
+                wu[r] = *reinterpret_cast<const uint4*>(ru + 16 * b);
+                dg[r] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(rg + 16 * (size_t)nb + 2 * b));
+                du[r] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(ru + 16 * (size_t)nb + 2 * b));
+            }
+#pragma unroll
+            for (int t = 0; t < P; t++) {
+                if (t < nt) {
+                    const ActView xa = act_view(xq + (size_t)(sp[t] / ks) * abx, nb);
+                    const XBlk xb = load_xblk(xa, b);
+#pragma unroll
+                    for (int r = 0; r < RW; r++) {
+                        ag[r * P + t] = __fadd_rn(ag[r * P + t], block_term(block_sumi(wg[r], xb), dg[r], xb.d));
+                        au[r * P + t] = __fadd_rn(au[r * P + t], block_term(block_sumi(wu[r], xb), du[r], xb.d));
+                    }
+                }
             }
         }
-#pragma unroll
-        for (int r = 0; r < RW; r++) {
-            const float gv = warp_sum_butterfly(ag[r]);
-            const float uv = warp_sum_butterfly(au[r]);
-            if (R == 32) {
-                if (lane == r) sh[i0 + r] = silu_mul(gv, uv);
-            } else if (lane == 0) {
-                hf[(size_t)p * g.I + (size_t)c * R + i0 + r] = silu_mul(gv, uv);
-            }
+        const float gv = warp_sum32_transposed(ag, lane);
+        const float uv = warp_sum32_transposed(au, lane);
+        const int r = lane / P, t = lane % P;
+        if (t < nt) {
+            const float hv = silu_mul(gv, uv);
+            if (R == 32)
+                sh[t][i0 + r] = hv;
+            else
+                hf[(size_t)sp[t] * g.I + (size_t)c * R + i0 + r] = hv;
         }
         if (R == 32) {
             __syncthreads();
-            if (warp == 0) {
-                const Q8Lane qz = quantize_lane(sh[lane]);
-                ActView ha = act_view(hq + (size_t)p * abh, g.nbI);
+            if (warp < nt) {
+                const Q8Lane qz = quantize_lane(sh[warp][lane]);
+                ActView ha = act_view(hq + (size_t)sp[warp] * abh, g.nbI);
                 ha.qs[(size_t)c * 32 + lane] = (int8_t)qz.q;
                 if (lane == 0) {
                     ha.d[c] = f16_bits_to_f32(qz.dh);
                     ha.s8[c] = qz.s8;
                 }
             }
-            __syncthreads();
         }
     }
 }
 
 // one warp per (pair, block) of h: the Q8_0 activation form of hf[p] into hq[p]
-// (the single-token quantiser, block by block, so the same bytes as the fused units).
-__global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, int n_pairs, Geom g,
-                                                 uint8_t* __restrict__ hq) {
+// (the single-token quantiser, block by block, so the same bytes as the fused units);
+// with uf, h = silu(hf) * uf first (hf, uf: the gate and up sums).
+__global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, const float* __restrict__ uf,
+                                                 int n_pairs, Geom g, uint8_t* __restrict__ hq) {
     const int lane = threadIdx.x & 31;
     const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (wid >= (long long)n_pairs * g.nbI) return;
     const int p = (int)(wid / g.nbI), b = (int)(wid - (long long)p * g.nbI);
-    const Q8Lane qz = quantize_lane(hf[(size_t)p * g.I + (size_t)b * 32 + lane]);
+    const size_t i = (size_t)p * g.I + (size_t)b * 32 + lane;
+    const Q8Lane qz = quantize_lane(uf ? silu_mul(hf[i], uf[i]) : hf[i]);
     ActView ha = act_view(hq + (size_t)p * act_bytes(g.nbI), g.nbI);
     ha.qs[(size_t)b * 32 + lane] = (int8_t)qz.q;
     if (lane == 0) {
@@ -282,14 +321,17 @@ __global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, i
 }
 
 // grid (H / 16, active experts), 256 threads.  CTA (rb, a) takes the a-th active expert e,
-// stages its down rows 16rb .. 16rb+15, then for every pair p routed to e: 2 rows per
-// warp, y[p][r] = row . hq[p].
+// stages its down rows 16rb .. 16rb+15 (2 per warp), then takes the pairs routed to e in
+// tiles of 16 tokens: each lane runs the lane-strided block chains of its warp's 2 rows
+// for every token of the tile, and one transposed reduction leaves lane l with the sum of
+// (row l / 16, token l % 16): y[p][r] = row . hq[p], exactly the single-token arithmetic.
 __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer,
                                                       const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                       const int* __restrict__ off, const int* __restrict__ list,
                                                       const int* __restrict__ active, const uint8_t* __restrict__ hq,
                                                       float* __restrict__ y) {
     extern __shared__ __align__(16) uint8_t smem[];   // DOWN_ROWS rows
+    __shared__ int sp[DOWN_TOK];
     if ((int)blockIdx.y >= active[0]) return;
     const int e = active[1 + blockIdx.y], rb = blockIdx.x;
     const int p0 = off[e], n = off[e + 1] - p0;
@@ -304,27 +346,41 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
         const int n16 = (int)((size_t)nrows * g.row_d / 16);
         for (int i = threadIdx.x; i < n16; i += blockDim.x) d[i] = __ldg(src + i);
     }
-    __syncthreads();
     const int nb = g.nbI;
     const size_t abh = act_bytes(nb);
-    for (int q = 0; q < n; q++) {
-        const int p = list[p0 + q];
-        const ActView ha = act_view(hq + (size_t)p * abh, nb);
+    const int lr0 = warp * 2;
+    for (int q0 = 0; q0 < n; q0 += DOWN_TOK) {
+        const int nt = min(DOWN_TOK, n - q0);
+        __syncthreads();
+        if (threadIdx.x < DOWN_TOK) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
+        __syncthreads();
+        if (lr0 >= nrows) continue;
+        float acc[32];   // [row r][token t] at r * 16 + t
 #pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            const int lr = warp * 2 + rr;
-            if (lr >= nrows) break;
-            const uint8_t* row = smem + (size_t)lr * g.row_d;
-            float acc = 0.0f;
-            for (int b = lane; b < nb; b += 32) {
-                const XBlk xb = load_xblk(ha, b);
-                const uint4 wv = *reinterpret_cast<const uint4*>(row + 16 * b);
-                const float dw = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * (size_t)nb + 2 * b));
-                acc = __fadd_rn(acc, block_term(block_sumi(wv, xb), dw, xb.d));
+        for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+        for (int b = lane; b < nb; b += 32) {
+            uint4 wv[2];
+            float dw[2];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const uint8_t* row = smem + (size_t)min(lr0 + r, nrows - 1) * g.row_d;
+                wv[r] = *reinterpret_cast<const uint4*>(row + 16 * b);
+                dw[r] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * (size_t)nb + 2 * b));
             }
-            const float yv = warp_sum_butterfly(acc);
-            if (lane == 0) y[(size_t)p * g.H + r0 + lr] = yv;
+#pragma unroll
+            for (int t = 0; t < DOWN_TOK; t++) {
+                if (t < nt) {
+                    const XBlk xb = load_xblk(act_view(hq + (size_t)sp[t] * abh, nb), b);
+#pragma unroll
+                    for (int r = 0; r < 2; r++)
+                        acc[r * DOWN_TOK + t] = __fadd_rn(acc[r * DOWN_TOK + t],
+                                                          block_term(block_sumi(wv[r], xb), dw[r], xb.d));
+                }
+            }
         }
+        const float yv = warp_sum32_transposed(acc, lane);
+        const int r = lane / DOWN_TOK, t = lane % DOWN_TOK;
+        if (t < nt && lr0 + r < nrows) y[(size_t)sp[t] * g.H + r0 + lr0 + r] = yv;
     }
 }
 
@@ -356,8 +412,12 @@ size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T) {
     const size_t ks = (size_t)k + n_shared, n_pairs = (size_t)T * ks, E_tot = (size_t)E + n_shared;
     return r256((size_t)T * E * 8) + r256((E_tot + 1) * 4) + r256((size_t)T * act_bytes(g.nbH)) + r256(n_pairs * 4) +
            r256(n_pairs * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256(n_pairs * act_bytes(g.nbI)) +
-           r256(n_pairs * g.I * 4);
+           r256(n_pairs * g.I * 4) + r256(n_pairs * g.I * 4) + 256;
 }
+
+// the tensor-core expert matmuls pay off once experts average this many (token, slot)
+// pairs; below it the dp4a kernels run
+constexpr int MMA_MIN_PAIRS_PER_EXPERT = 16;
 
 size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
     const size_t n_pairs = (size_t)T * k;
@@ -368,7 +428,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                                        int G, Geom g, const float* R, const float* normw, float eps, int E,
                                        int n_shared, int k, const float* X, int T, void* scratch,
                                        size_t scratch_bytes, float* y, int* idx_out, float* w_out,
-                                       float* logits_out, cudaStream_t s) {
+                                       float* logits_out, int kernels, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || n_shared < 0 || n_shared > 1 ||
         (n_shared && !shared) || k + n_shared > MAX_TOPK + 1 || G < 1 || rank < 0 || rank >= G || e_n * G != E ||
@@ -382,6 +442,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
         p += r256(n);
         return r;
     };
+    unsigned* err = reinterpret_cast<unsigned*>(take(4));   // first: at the scratch's start for every T
     unsigned long long* S = reinterpret_cast<unsigned long long*>(take((size_t)T * E * 8));
     int* active = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
     uint8_t* xq = take((size_t)T * act_bytes(g.nbH));
@@ -393,6 +454,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     int* list = reinterpret_cast<int*>(take(n_pairs * 4));
     uint8_t* hq = take(n_pairs * act_bytes(g.nbI));
     float* hf = reinterpret_cast<float*>(take(n_pairs * g.I * 4));
+    float* uf = reinterpret_cast<float*>(take(n_pairs * g.I * 4));
 
     int dev = 0, optin = 0;
     cudaError_t e;
@@ -408,6 +470,17 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active);
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
+    const bool mma = q4_mma_supported(g) &&
+                     (kernels == BATCHED_MMA ||
+                      (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * (E + n_shared)));
+    if (mma) {
+        if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, n_act, ks, xq, hf, uf, err, s)) !=
+            cudaSuccess)
+            return e;
+        const long long warps = (long long)n_pairs * g.nbI;
+        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq);
+        return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, n_act, ks, hq, y, nullptr, err, s);
+    }
     const int R_gu = gu_rows(g, (size_t)optin);
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
     if (R_gu == 32) {
@@ -425,7 +498,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
         k_gateup_batched<16><<<dim3(g.I / 16, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active,
                                                                         ks, xq, hq, hf);
         const long long warps = (long long)n_pairs * g.nbI;
-        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, (int)n_pairs, g, hq);
+        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, nullptr, (int)n_pairs, g, hq);
     }
     const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
     if (sm_d > 48 * 1024 &&
@@ -446,7 +519,7 @@ cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const flo
 
 cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
                                int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
-                               float* w_out, float* logits_out, cudaStream_t s) {
+                               float* w_out, float* logits_out, int kernels, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || batched_scratch_bytes(g, E, k, T) > scratch_bytes)
         return cudaErrorInvalidValue;
@@ -457,7 +530,7 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
     float* wts = w_out ? w_out : reinterpret_cast<float*>(base + part);
     float* y = reinterpret_cast<float*>(base + part + r256(n_pairs * 4));
     cudaError_t e = launch_moe_batched_partial(layer, nullptr, 0, E, 0, 1, g, R, normw, eps, E, 0, k, X, T, scratch,
-                                               part, y, idx_out, wts, logits_out, s);
+                                               part, y, idx_out, wts, logits_out, kernels, s);
     if (e != cudaSuccess) return e;
     return launch_moe_batched_combine(X, T, g.H, k, wts, y, s);
 }

@@ -515,6 +515,7 @@ struct tgx_ctx {
     tg::FusedParams fp{};
     void* bscratch = nullptr;           // batched path scratch, grown on demand
     size_t bscratch_bytes = 0;
+    int batched_kernels = 0;            // tg::BATCHED_AUTO / _DP4A / _MMA
     // tgx_experts_forward: up to 16 expert pointers and weights, their h blocks, the norm scale
     const uint8_t** lptrs = nullptr;
     float* lwts = nullptr;
@@ -847,12 +848,14 @@ int batched_run(tgx_ctx* ctx, int l0, int l1, float* x_dev, int T, cudaStream_t 
             return fail(TG_ENOMEM, std::string(fn) + ": cudaMalloc of " + std::to_string(need) + " bytes failed");
         }
         ctx->bscratch_bytes = need;
+        TG_CUDA(cudaMemset(ctx->bscratch, 0, 256));   // the error flag
     }
     const size_t n = (size_t)sh.n_experts * sh.embed;
     for (int l = l0; l < l1; l++)
         TG_CUDA(tg::launch_moe_batched(ctx->weights + (size_t)l * ctx->layer_bytes, ctx->g, ctx->routers + (size_t)l * n,
                                        ctx->norms + (size_t)l * sh.embed, ctx->eps, sh.n_experts, sh.top_k, x_dev, T,
-                                       ctx->bscratch, ctx->bscratch_bytes, nullptr, nullptr, nullptr, s));
+                                       ctx->bscratch, ctx->bscratch_bytes, nullptr, nullptr, nullptr,
+                                       ctx->batched_kernels, s));
     return TG_OK;
 }
 }  // namespace
@@ -949,10 +952,25 @@ extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int fla
     return TG_OK;
 }
 
+extern "C" int tgx_set_batched_kernels(tgx_ctx* ctx, int kernels) {
+    TG_CHECK(ctx && kernels >= 0 && kernels <= 2, TG_EINVAL,
+             "tgx_set_batched_kernels: kernels must be 0 (auto), 1 (dp4a) or 2 (tensor cores)");
+    ctx->batched_kernels = kernels;
+    return TG_OK;
+}
+
 extern "C" int tgx_sync_status(tgx_ctx* ctx) {
     TG_CHECK(ctx, TG_EINVAL, "tgx_sync_status: null context");
     DeviceGuard dg(ctx->device);
     TG_CUDA(cudaDeviceSynchronize());
+    if (ctx->bscratch) {   // the batched path's tensor-core kernels
+        unsigned flag = 0;
+        TG_CUDA(cudaMemcpy(&flag, ctx->bscratch, sizeof(flag), cudaMemcpyDeviceToHost));
+        if (flag) {
+            TG_CUDA(cudaMemset(ctx->bscratch, 0, sizeof(flag)));
+            return fail(TG_ETIMEOUT, "batched path: a tensor-core expert kernel's bounded wait expired");
+        }
+    }
     if (!ctx->ctl) return TG_OK;
     unsigned ctl[4];
     TG_CUDA(cudaMemcpy(ctl, ctx->ctl, sizeof(ctl), cudaMemcpyDeviceToHost));

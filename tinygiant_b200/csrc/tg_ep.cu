@@ -39,6 +39,7 @@ struct tgx_ep {
     float* wts = nullptr;         // [T][k] routing weights of the last partial step
     size_t wts_bytes = 0;
     int last_T = 0;
+    int kernels = 0;              // tg::BATCHED_AUTO / _DP4A / _MMA
     cudaStream_t s = nullptr;
 };
 
@@ -105,6 +106,7 @@ int ep_reserve(tgx_ep* c, int T, cudaStream_t s, const char* fn) {
         c->scratch_bytes = 0;
         EP_TRY(ep_alloc(&c->scratch, need, fn));
         c->scratch_bytes = need;
+        EP_CUDA(cudaMemset(c->scratch, 0, 256));   // the error flag
     }
     if (wneed > c->wts_bytes) {
         if (c->wts) cudaFree(c->wts);
@@ -302,7 +304,7 @@ extern "C" int tgx_ep_moe_partial(tgx_ep* ep, int layer, const float* x_dev, int
                                            ep->rank, ep->size, ep->g, ep->routers + (size_t)layer * nr,
                                            ep->norms + (size_t)layer * sh.embed, ep->eps, sh.n_experts, ep->n_shared,
                                            sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, y_dev, nullptr, ep->wts,
-                                           nullptr, s));
+                                           nullptr, ep->kernels, s));
     ep->last_T = T;
     return TG_OK;
 }
@@ -313,5 +315,25 @@ extern "C" int tgx_ep_combine(tgx_ep* ep, float* x_dev, int T, const float* y_de
     Dev dg(ep->device);
     EP_CUDA(tg::launch_moe_batched_combine(x_dev, T, ep->shape.embed, ep->shape.top_k + ep->n_shared, ep->wts,
                                            y_dev, (cudaStream_t)stream));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_set_kernels(tgx_ep* ep, int kernels) {
+    EP_CHECK(ep && kernels >= 0 && kernels <= 2, TG_EINVAL, "tgx_ep_set_kernels: kernels must be 0 (auto), 1 (dp4a) or 2 (tensor cores)");
+    ep->kernels = kernels;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_status(tgx_ep* ep, void* stream) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_status: null context");
+    if (!ep->scratch) return TG_OK;
+    Dev dg(ep->device);
+    EP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    unsigned flag = 0;
+    EP_CUDA(cudaMemcpy(&flag, ep->scratch, sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag) {
+        EP_CUDA(cudaMemset(ep->scratch, 0, sizeof(flag)));
+        return ep_fail(TG_ETIMEOUT, "tgx_ep: a tensor-core expert kernel's bounded wait expired");
+    }
     return TG_OK;
 }

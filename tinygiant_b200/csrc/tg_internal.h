@@ -77,11 +77,23 @@ cudaError_t prepare_kernels(Geom g, int k);
 // least batched_scratch_bytes(g, E, k, T); idx_out / w_out / logits_out optional
 // ([T][k], [T][k], [T][E]).  batched_smem_bytes: the largest dynamic shared memory
 // a CTA of the path needs.
+// kernels: which expert matmuls run — BATCHED_AUTO picks the tensor-core path
+// (tg_tc.cu) when experts average >= 16 pairs, BATCHED_DP4A / BATCHED_MMA force one;
+// both give the same bits.
+constexpr int BATCHED_AUTO = 0, BATCHED_DP4A = 1, BATCHED_MMA = 2;
 size_t batched_scratch_bytes(const Geom& g, int E, int k, int T);
 size_t batched_smem_bytes(const Geom& g);
 cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
                                int k, float* X, int T, void* scratch, size_t scratch_bytes, int* idx_out,
-                               float* w_out, float* logits_out, cudaStream_t s);
+                               float* w_out, float* logits_out, int kernels, cudaStream_t s);
+// Tensor-core expert matmuls (tg_tc.cu) over the grouped pairs: down = 0 gives the gate
+// sums (out0) and up sums (out1) [pair][I] from the tokens' Q8_0 x (act = xq per token),
+// down = 1 the down sums y [pair][H] from the pairs' Q8_0 h (act = hq per pair).  Rows of
+// I and H must be multiples of 128.  err is set when a bounded wait expired.
+bool q4_mma_supported(const Geom& g);
+cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
+                          const int* off, const int* list, const int* active, int n_act, int ks, const uint8_t* act,
+                          float* out0, float* out1, unsigned* err, cudaStream_t s);
 // The two halves of launch_moe_batched, generalised to experts sharded over G devices
 // and an optional shared expert.  Partial: routing of all T tokens (every device
 // computes the same), then y[(t, j)][H] for the pairs this device owns (routed slot j < k:
@@ -89,7 +101,9 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
 // j = k when n_shared = 1: this device holds the fewest of token t's routed experts, ties
 // to (t + i) mod G, smallest i), y = 0 for the others when G > 1.  layer points at
 // expert e_lo, shared at the shared expert (weight 1, id E).  w_out receives the
-// routing weights [T][k + n_shared].  Scratch of batched_partial_bytes.  Combine:
+// routing weights [T][k + n_shared].  Scratch of batched_partial_bytes, whose first word
+// is an error flag (zero it when the scratch is allocated; a tensor-core launch whose
+// bounded wait expired sets it).  Combine:
 // X[t] += sum_j w[t][j] * y[(t, j)] in slot order (ks = k + n_shared slots).  With the y
 // of every device summed in between (one nonzero term per element, so the sum is
 // exact), the result is the single-device one bit for bit.
@@ -98,7 +112,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                                        int G, Geom g, const float* R, const float* normw, float eps, int E,
                                        int n_shared, int k, const float* X, int T, void* scratch,
                                        size_t scratch_bytes, float* y, int* idx_out, float* w_out,
-                                       float* logits_out, cudaStream_t s);
+                                       float* logits_out, int kernels, cudaStream_t s);
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s);
 

@@ -113,6 +113,10 @@ class MoEModel:
         assert X.dim() == 2 and X.shape[1] == self.embed
         check(self.lib.tgx_decode_batched(self._ctx, _dev_ptr(X), X.shape[0], _stream_handle(stream)), self.lib)
 
+    def set_batched_kernels(self, kernels: int):
+        """Expert matmuls of the batched path: 0 auto, 1 dp4a, 2 tensor cores; same bits."""
+        check(self.lib.tgx_set_batched_kernels(self._ctx, kernels), self.lib)
+
     def sync_status(self):
         """Synchronise; raise if a bounded wait inside the fused kernel expired."""
         check(self.lib.tgx_sync_status(self._ctx), self.lib)

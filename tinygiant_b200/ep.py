@@ -116,6 +116,13 @@ class EPMoEModel:
         assert w.shape == (self.embed,)
         check(self.lib.tgx_ep_set_ffn_norm(self._ep, layer, w.ctypes.data, 0), self.lib)
 
+    def set_kernels(self, kernels: int):
+        """0 auto, 1 dp4a, 2 tensor cores (tcgen05) for the expert matmuls; same bits."""
+        check(self.lib.tgx_ep_set_kernels(self._ep, kernels), self.lib)
+
+    def status(self, stream=None):
+        check(self.lib.tgx_ep_status(self._ep, _stream_handle(stream)), self.lib)
+
     # ---------------------------------------------------------------- compute
     def y_buffer(self, T: int):
         """The per-step exchange buffer for T tokens (reused, one per T)."""
