@@ -13,12 +13,11 @@
 //
 // CTA: 128 weight rows (one matrix of one expert) x a tile of 32 tokens; 16 warps.
 // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and owns tokens 8 (w / 4) .. + 7.
-// K runs in groups of 8 steps: double-buffered shared-memory stages and TMEM
-// accumulators (2 x 8 x 32 columns); every thread stages the next group's operands
-// (global loads into registers before the current group's epilogue, shared stores
-// after it), thread 0 issues the group's MMAs and commits them to an mbarrier.  Every
-// mbarrier wait is bounded; on expiry the CTA records the failure, stops issuing, and
-// frees its TMEM.
+// K runs in groups of 8 steps through three shared stages and two TMEM accumulator sets
+// (2 x 8 x 32 columns): while the epilogue reads group g, the tensor cores run group
+// g + 1 and every thread's global loads for group g + 2 are in flight; thread 0 issues
+// each group's MMAs and commits them to an mbarrier.  Every mbarrier wait is bounded; on
+// expiry the CTA records the failure, drains its MMAs (bounded), frees its TMEM and returns.
 #include <cuda_runtime.h>
 
 #include "tg_device.cuh"
@@ -37,7 +36,8 @@ constexpr int B_STEP = TN * 32;  // bytes of B per K step (1 KB)
 // shared stage: A [KG][4 KB] | B [KG][1 KB] | dw [KG][TM] f32 | dx [KG][TN] f32
 constexpr int ST_A = 0, ST_B = KG * A_STEP, ST_DW = ST_B + KG * B_STEP, ST_DX = ST_DW + KG * TM * 4;
 constexpr int STAGE_BYTES = ST_DX + KG * TN * 4;
-constexpr int TC_SMEM = 2 * STAGE_BYTES + 1024;   // + alignment slack
+constexpr int NSTAGE = 3;        // shared stages: group g+2 is written while g+1 is in the MMA, g in the epilogue
+constexpr int TC_SMEM = NSTAGE * STAGE_BYTES + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = 2 * KG * TN;       // 512
 constexpr long long TC_WAIT_CYCLES = 2000000000ll;
 
@@ -71,21 +71,46 @@ __device__ __forceinline__ void build_steps(int nb, uint16_t* steps) {
     }
 }
 
-// push class sum v (class ordinal c) into the butterfly stack; st[5] is the total
-__device__ __forceinline__ void stack_push(float (&st)[6], float v, int c) {
-    bool done = false;
+// Push the class sums v[t] (class ordinal c, the same for the whole warp) into the
+// butterfly stacks: the trailing ones of c are the merges the tree makes at this leaf
+// (siblings are earlier stack entries); st[t][5] ends as the total.
+__device__ __forceinline__ void push8(float (&st)[8][6], const float (&v)[8], int c) {
+    switch (__ffs(~c) - 1) {
+        case 0:
 #pragma unroll
-    for (int lv = 0; lv < 5; lv++) {
-        if (!done) {
-            if ((c >> lv) & 1) {
-                v = __fadd_rn(st[lv], v);
-            } else {
-                st[lv] = v;
-                done = true;
-            }
-        }
+            for (int t = 0; t < 8; t++) st[t][0] = v[t];
+            break;
+        case 1:
+#pragma unroll
+            for (int t = 0; t < 8; t++) st[t][1] = __fadd_rn(st[t][0], v[t]);
+            break;
+        case 2:
+#pragma unroll
+            for (int t = 0; t < 8; t++) st[t][2] = __fadd_rn(st[t][1], __fadd_rn(st[t][0], v[t]));
+            break;
+        case 3:
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                st[t][3] = __fadd_rn(st[t][2], __fadd_rn(st[t][1], __fadd_rn(st[t][0], v[t])));
+            break;
+        case 4:
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                st[t][4] = __fadd_rn(st[t][3], __fadd_rn(st[t][2], __fadd_rn(st[t][1], __fadd_rn(st[t][0], v[t]))));
+            break;
+        default:
+#pragma unroll
+            for (int t = 0; t < 8; t++)
+                st[t][5] = __fadd_rn(st[t][4],
+                                     __fadd_rn(st[t][3], __fadd_rn(st[t][2], __fadd_rn(st[t][1], __fadd_rn(st[t][0], v[t])))));
+            break;
     }
-    if (!done) st[5] = v;
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t (&v)[8], uint32_t ta) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(ta));
 }
 
 struct TcParams {
@@ -147,9 +172,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tbase = s_taddr;
-    uint32_t uses[2] = {0u, 0u};                     // completions consumed per mbarrier
+    uint32_t use0 = 0u, use1 = 0u;                   // completions consumed per mbarrier
     const int NG = (nb + KG - 1) / KG;
     bool failed = false;
+    int fail_group = -1;
 
     for (int t0 = 0; t0 < n && !failed; t0 += TN) {
         const int nt = min(TN, n - t0);
@@ -220,26 +246,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         };
+        // MMAs of group gi: operands in stage gi % NSTAGE, accumulators in TMEM set gi & 1
         auto issue_group = [&](int gi) {
-            const int stg = gi & 1;
-            const uint8_t* base = smem + (size_t)stg * STAGE_BYTES;
+            const uint8_t* base = smem + (size_t)(gi % NSTAGE) * STAGE_BYTES;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             for (int jj = 0; jj < KG && gi * KG + jj < nb; jj++) {
                 const uint64_t da = kmajor_desc(base + ST_A + jj * A_STEP);
                 const uint64_t db = kmajor_desc(base + ST_B + jj * B_STEP);
-                const uint32_t dt = tbase + (uint32_t)(stg * KG * TN + jj * TN);
+                const uint32_t dt = tbase + (uint32_t)((gi & 1) * KG * TN + jj * TN);
                 asm volatile(
                     "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
                     "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
                     "l"(da), "l"(db), "r"(IDESC), "r"(0));
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             saddr(&mbar[stg]))
+                             saddr(&mbar[gi & 1]))
                          : "memory");
         };
-        auto wait_group = [&](int gi) -> bool {
-            const int stg = gi & 1;
-            const uint32_t parity = uses[stg] & 1u;
+        auto try_group = [&](int gi) -> bool {   // bounded wait for group gi's commit
+            const uint32_t parity = ((gi & 1) ? use1 : use0) & 1u;
             const long long t_start = clock64();
             while (true) {
                 uint32_t done;
@@ -247,13 +272,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
                     "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                     "selp.u32 %0, 1, 0, p;\n\t}"
                     : "=r"(done)
-                    : "r"(saddr(&mbar[stg])), "r"(parity)
+                    : "r"(saddr(&mbar[gi & 1])), "r"(parity)
                     : "memory");
-                if (done) break;
+                if (done) return true;
                 if (clock64() - t_start > TC_WAIT_CYCLES) return false;
             }
-            uses[stg]++;
-            return true;
         };
 
         float leaf[8], st[8][6];
@@ -263,67 +286,73 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
 #pragma unroll
             for (int q = 0; q < 6; q++) st[t][q] = 0.0f;
         }
-        int next_cls = 0;   // class ordinal the stack expects next (empty classes are pushed as 0)
+        const float zero8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        int next_cls = 0;   // class ordinal the stacks expect next (classes without blocks push 0)
 
         load_group(0);
         store_group(0);
+        if (NG > 1) {
+            load_group(1);
+            store_group(1);
+        }
         __syncthreads();
         if (tid == 0) issue_group(0);
         for (int gi = 0; gi < NG; gi++) {
-            if (gi + 1 < NG) load_group(gi + 1);
-            const bool ok = wait_group(gi);
+            if (tid == 0 && gi + 1 < NG) issue_group(gi + 1);
+            if (gi + 2 < NG) load_group(gi + 2);
+            const bool ok = try_group(gi);
             if (!ok) {
                 atomicExch(&s_fail, 1);
-                uses[gi & 1]++;   // the completion, if it ever comes, belongs to this group
+                fail_group = gi;
+            } else if (gi & 1) {
+                use1++;
+            } else {
+                use0++;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (ok) {
-                const float* dwp = reinterpret_cast<const float*>(smem + (size_t)(gi & 1) * STAGE_BYTES + ST_DW);
-                const float* dxp = reinterpret_cast<const float*>(smem + (size_t)(gi & 1) * STAGE_BYTES + ST_DX);
+                const uint8_t* stage = smem + (size_t)(gi % NSTAGE) * STAGE_BYTES;
+                const float* dwp = reinterpret_cast<const float*>(stage + ST_DW);
+                const float* dxp = reinterpret_cast<const float*>(stage + ST_DX);
+                const uint32_t tcol = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((gi & 1) * KG * TN + cg * 8);
+                const int nsteps = min(KG, nb - gi * KG);
+                uint32_t va[8], vb[8];
+                tmem_ld8(va, tcol);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
                 for (int jj = 0; jj < KG; jj++) {
-                    const int s = gi * KG + jj;
-                    if (s >= nb) break;
-                    const int c = (s_steps[s] >> 10) & 31;
-                    const bool lst = (s_steps[s] >> 15) != 0;
-                    for (; next_cls < c; next_cls++)       // classes without blocks contribute +0
-#pragma unroll
-                        for (int t = 0; t < 8; t++) stack_push(st[t], 0.0f, next_cls);
-                    uint32_t v[8];
-                    const uint32_t ta = tbase + ((uint32_t)((warp & 3) * 32) << 16) +
-                                        (uint32_t)((gi & 1) * KG * TN + jj * TN + cg * 8);
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                          "=r"(v[7])
-                        : "r"(ta));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    const float dw = dwp[jj * TM + row];
-#pragma unroll
-                    for (int t = 0; t < 8; t++) {
-                        const float term = __fmul_rn(__fmul_rn(__int2float_rn((int)v[t]), dw), dxp[jj * TN + cg * 8 + t]);
-                        leaf[t] = __fadd_rn(leaf[t], term);
-                    }
-                    if (lst) {
+                    if (jj < nsteps) {
+                        uint32_t (&cur)[8] = (jj & 1) ? vb : va;
+                        uint32_t (&nxt)[8] = (jj & 1) ? va : vb;
+                        if (jj + 1 < nsteps) tmem_ld8(nxt, tcol + (uint32_t)((jj + 1) * TN));
+                        const int code = s_steps[gi * KG + jj];
+                        const int c = (code >> 10) & 31;
+                        for (; next_cls < c; next_cls++) push8(st, zero8, next_cls);
+                        const float dw = dwp[jj * TM + row];
 #pragma unroll
                         for (int t = 0; t < 8; t++) {
-                            stack_push(st[t], leaf[t], c);
-                            leaf[t] = 0.0f;
+                            const float term =
+                                __fmul_rn(__fmul_rn(__int2float_rn((int)cur[t]), dw), dxp[jj * TN + cg * 8 + t]);
+                            leaf[t] = __fadd_rn(leaf[t], term);
                         }
-                        next_cls = c + 1;
+                        if (code >> 15) {
+                            push8(st, leaf, c);
+#pragma unroll
+                            for (int t = 0; t < 8; t++) leaf[t] = 0.0f;
+                            next_cls = c + 1;
+                        }
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     }
                 }
             }
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            if (gi + 1 < NG) store_group((gi + 1) & 1);
+            if (gi + 2 < NG) store_group((gi + 2) % NSTAGE);
             __syncthreads();
             failed = s_fail != 0;
             if (failed) break;
-            if (tid == 0 && gi + 1 < NG) issue_group(gi + 1);
         }
         if (failed) break;
-        for (; next_cls < 32; next_cls++)
-#pragma unroll
-            for (int t = 0; t < 8; t++) stack_push(st[t], 0.0f, next_cls);
+        for (; next_cls < 32; next_cls++) push8(st, zero8, next_cls);
 #pragma unroll
         for (int t = 0; t < 8; t++) {
             const int tk = cg * 8 + t;
@@ -331,18 +360,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
         }
     }
     if (failed) {
-        // the failed group's MMAs may still be in flight: give them one more bounded wait
-        // before the TMEM is freed
+        // drain (bounded) the MMAs still in flight, the failed group's and the one issued
+        // after it, before the TMEM is freed
         const long long t_start = clock64();
-        for (int b = 0; b < 2; b++) {
-            const uint32_t parity = (uses[b] - 1u) & 1u;
+        for (int gi = fail_group; gi >= 0 && gi <= fail_group + 1 && gi < NG; gi++) {
+            const uint32_t parity = ((gi & 1) ? use1 : use0) & 1u;
             while (clock64() - t_start < TC_WAIT_CYCLES) {
                 uint32_t done;
                 asm volatile(
                     "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                     "selp.u32 %0, 1, 0, p;\n\t}"
                     : "=r"(done)
-                    : "r"(saddr(&mbar[b])), "r"(parity)
+                    : "r"(saddr(&mbar[gi & 1])), "r"(parity)
                     : "memory");
                 if (done) break;
             }
