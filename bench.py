@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism: under torchrun each rank holds E/N experts of every layer and "
                          "the ranks decode the same --tokens T tokens together (NCCL all-reduce per layer)")
+    ap.add_argument("--batched-kernels", choices=["auto", "dp4a", "mma"], default="auto",
+                    help="expert matmuls of the batched / EP path: auto (tensor cores from 16 pairs per expert), "
+                         "dp4a, or mma (tcgen05); all give the same bits")
     ap.add_argument("--shape", choices=["qwen3", "dsv3"], default="qwen3",
                     help="with --ep: qwen3 (configs[2]) or the DeepSeek-V3-like configs[4] (hidden 7168, "
                          "inter 2048, 256 routed + 1 shared expert, 58 layers, as many as fit per GPU)")
@@ -383,6 +386,7 @@ def run_batched(args):
     T, NL = args.tokens, args.layers
     model = MoEModel(H, I, E, K_TOP, NL, device=local)
     model.fill_synthetic(args.seed + 7919 * rank)
+    model.set_batched_kernels(KERNELS[args.batched_kernels])
     K, W = args.steps, max(3, args.warmup)
     gen = torch.Generator(device="cuda").manual_seed(args.seed + rank)
     pool = [torch.randn(T, H, generator=gen, device="cuda") for _ in range(4)]
@@ -434,6 +438,7 @@ def run_batched(args):
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"configs[2]: {T} tokens per step, {NL} layers, batched path",
                        "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "layers": NL, "tokens": T,
+                       "batched_kernels": args.batched_kernels,
                        "parallelism": "replicas" if ws > 1 else "single GPU"},
             "weights_read_upper_bound_gbs": NL * distinct * EXPERT_BYTES / (ms / K / 1000.0) / 1e9,
             "e2e": {"value": ws * T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * H * 4,
@@ -527,6 +532,7 @@ def run_tier(args):
     return 0
 
 
+KERNELS = {"auto": 0, "dp4a": 1, "mma": 2}
 Q4K_BLOCK, Q6K_BLOCK = 144, 210
 
 
@@ -749,6 +755,7 @@ def run_ep(args):
         NL = args.layers
     ep = EPMoEModel(h, inter, e_all, K_TOP, NL, rank=rank, size=ws, device=local, n_shared=n_sh)
     ep.fill_synthetic(args.seed)                          # one model, sharded: the same seed on every rank
+    ep.set_kernels(KERNELS[args.batched_kernels])
     for T in args.token_list:
         ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist)
     ep.close()
@@ -842,7 +849,7 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
                                    f"{' + the shared expert' if n_sh else ''}, NCCL all-reduce of y per layer",
                        "hidden": h, "inter": inter, "experts": e_all, "shared_experts": n_sh, "top_k": K_TOP,
                        "layers": NL, "full_layers": full_layers, "tokens": T, "parallelism": f"ep{ws}",
-                       "cuda_graph": graphed},
+                       "cuda_graph": graphed, "batched_kernels": args.batched_kernels},
             "tok_s_full_depth": value * NL / full_layers,
             "exchange_bytes_per_layer": T * (K_TOP + n_sh) * h * 4,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ws, "unit": "GB/s",

@@ -134,6 +134,12 @@ int tg_expert_forward_q4_0_noalloc(const uint8_t *q4_data, const float *input, f
  * csrc/libtinygiant.c:761-766 does. */
 int tg_mlock(const void *addr, size_t len);
 
+/* posix_madvise(WILLNEED) of the pages of [addr, addr+len), csrc/libtinygiant.c:745-750;
+ * returns posix_madvise's result (the reference's is void). */
+int tg_prefetch(const void *addr, size_t len);
+/* tg_prefetch over count ranges, csrc/libtinygiant.c:752-759; the first nonzero result. */
+int tg_prefetch_batch(const void **addrs, const size_t *lens, int count);
+
 /* ===================== device-resident API ===================== */
 
 typedef struct tgx_ctx tgx_ctx;

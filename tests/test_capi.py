@@ -72,3 +72,15 @@ def test_mlock_matches_reference_semantics():
     buf = np.zeros(1 << 16, np.uint8)
     rc = lib.tg_mlock(buf.ctypes.data, buf.nbytes)
     assert rc in (0, -1)  # mlock's own result, as csrc/libtinygiant.c:761-766 returns it
+
+
+def test_prefetch_hints_match_reference_semantics():
+    # csrc/libtinygiant.c:745-759: page-aligned WILLNEED advice, no effect on the data
+    lib = L.load_tinygiant_lib()
+    buf = np.arange(1 << 16, dtype=np.uint8)
+    assert lib.tg_prefetch(buf.ctypes.data + 123, 40000) == 0
+    addrs = (ctypes.c_void_p * 2)(buf.ctypes.data, buf.ctypes.data + 5000)
+    lens = (ctypes.c_size_t * 2)(100, 20000)
+    assert lib.tg_prefetch_batch(addrs, lens, 2) == 0
+    assert lib.tg_prefetch_batch(addrs, lens, 0) == 0
+    assert np.array_equal(buf, np.arange(1 << 16, dtype=np.uint8))

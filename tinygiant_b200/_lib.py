@@ -95,6 +95,8 @@ PROTOTYPES = {
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),
     "tg_expert_forward_q4_0_noalloc": (CI, [VP, VP, VP, CF, CI, CI, VP]),
     "tg_mlock": (CI, [VP, SZ]),
+    "tg_prefetch": (CI, [VP, SZ]),
+    "tg_prefetch_batch": (CI, [VP, VP, CI]),
     "tgx_ctx_create": (CI, [CI, ctypes.POINTER(TgxShape), ctypes.POINTER(VP)]),
     "tgx_ctx_destroy": (CI, [VP]),
     "tgx_expert_bytes": (SZ, [VP]),

@@ -67,6 +67,18 @@ class HostTierCache:
             self.pinned[key] = dst
         torch.cuda.synchronize()
 
+    def pin_from_profile(self, reader, n_per_layer: int) -> int:
+        """Pin each layer's n most active experts by the relayout's activation profile
+        (the reference's ExpertCache.pin_hot_experts, tinygiant/cache.py:84-100);
+        returns how many were pinned."""
+        count = 0
+        for layer in range(len(self.host)):
+            ids = reader.hot_experts(layer, n_per_layer)
+            if ids:
+                self.pin(layer, ids)
+                count += len(ids)
+        return count
+
     # ------------------------------------------------------------ the HBM slot tier
     def _load(self, key, protect):
         """Start loading expert key into a slot (evicting the least recently used slot not

@@ -7,6 +7,7 @@
 //         runs the routed MoE decode on caller streams.
 #include <cuda_runtime.h>
 #include <sys/mman.h>
+#include <cerrno>
 #include <unistd.h>
 
 #include <mutex>
@@ -476,6 +477,28 @@ extern "C" int tg_mlock(const void* addr, size_t len) {
     uintptr_t a = (uintptr_t)addr & ~(page - 1);
     size_t l = len + ((uintptr_t)addr - a);
     return mlock((const void*)a, l);
+}
+
+// posix_madvise(WILLNEED) over the pages of [addr, addr + len): the reference's page
+// hint ahead of reading a cold expert (csrc/libtinygiant.c:745-750); here the host
+// tier's pinned copies make it a hint for relayout files mapped from disk.  Returns
+// posix_madvise's result (0 or an errno value).
+extern "C" int tg_prefetch(const void* addr, size_t len) {
+    if (!addr || !len) return 0;
+    const uintptr_t page = (uintptr_t)sysconf(_SC_PAGESIZE);
+    const uintptr_t a = (uintptr_t)addr & ~(page - 1);
+    return posix_madvise((void*)a, len + ((uintptr_t)addr - a), POSIX_MADV_WILLNEED);
+}
+
+// tg_prefetch over count ranges (csrc/libtinygiant.c:752-759); the first nonzero result.
+extern "C" int tg_prefetch_batch(const void** addrs, const size_t* lens, int count) {
+    if (!addrs || !lens || count <= 0) return count < 0 ? EINVAL : 0;
+    int rc = 0;
+    for (int i = 0; i < count; i++) {
+        const int r = tg_prefetch(addrs[i], lens[i]);
+        if (r && !rc) rc = r;
+    }
+    return rc;
 }
 
 // ============================================================ device-resident
