@@ -69,6 +69,9 @@ def parse():
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism: under torchrun each rank holds E/N experts of every layer and "
                          "the ranks decode the same --tokens T tokens together (NCCL all-reduce per layer)")
+    ap.add_argument("--p2p", action="store_true",
+                    help="with --ep: exchange by direct NVLink stores and flags (tgx_ep_moe_layer_p2p) instead "
+                         "of the NCCL all-reduce")
     ap.add_argument("--batched-kernels", choices=["auto", "dp4a", "mma"], default="auto",
                     help="expert matmuls of the batched / EP path: auto (tensor cores from 16 pairs per expert), "
                          "dp4a, or mma (tcgen05); all give the same bits")
@@ -756,6 +759,8 @@ def run_ep(args):
     ep = EPMoEModel(h, inter, e_all, K_TOP, NL, rank=rank, size=ws, device=local, n_shared=n_sh)
     ep.fill_synthetic(args.seed)                          # one model, sharded: the same seed on every rank
     ep.set_kernels(KERNELS[args.batched_kernels])
+    if args.p2p:
+        ep.enable_p2p(max(args.token_list))
     for T in args.token_list:
         ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist)
     ep.close()
@@ -827,6 +832,8 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
         t = torch.tensor([ms, ems], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ems = float(t[0]), float(t[1])
+    if getattr(ep, "p2p", False):
+        ep.p2p_status()                                   # raises if a peer's flag wait expired
     assert torch.isfinite(Yh).all()
     del graph                                             # holds NCCL calls: released before the group
     if rank == 0:
@@ -846,10 +853,12 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"{'configs[4]' if args.shape == 'dsv3' else 'configs[2]'}: {T} tokens per step, "
                                    f"{NL} of {full_layers} layers, experts sharded {e_all // ws} per GPU"
-                                   f"{' + the shared expert' if n_sh else ''}, NCCL all-reduce of y per layer",
+                                   f"{' + the shared expert' if n_sh else ''}, "
+                                   f"{'NVLink stores + flags' if args.p2p else 'NCCL all-reduce'} of y per layer",
                        "hidden": h, "inter": inter, "experts": e_all, "shared_experts": n_sh, "top_k": K_TOP,
                        "layers": NL, "full_layers": full_layers, "tokens": T, "parallelism": f"ep{ws}",
-                       "cuda_graph": graphed, "batched_kernels": args.batched_kernels},
+                       "cuda_graph": graphed, "batched_kernels": args.batched_kernels,
+                       "exchange": "p2p" if args.p2p else "nccl_all_reduce"},
             "tok_s_full_depth": value * NL / full_layers,
             "exchange_bytes_per_layer": T * (K_TOP + n_sh) * h * 4,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ws, "unit": "GB/s",

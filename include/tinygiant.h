@@ -290,6 +290,27 @@ int tgx_ep_set_kernels(tgx_ep *ep, int kernels);
  * bounded wait expired since the last call */
 int tgx_ep_status(tgx_ep *ep, void *stream);
 
+/* The exchange over NVLink instead of a collective.  Every rank: tgx_ep_p2p_init(ep,
+ * T_max, handle) allocates its exchange region and returns its CUDA IPC handle
+ * (tgx_ep_p2p_handle_bytes() bytes); the caller gathers all ranks' handles in rank order
+ * (any host-side exchange) and passes them to tgx_ep_p2p_connect.  Then one call per
+ * layer, tgx_ep_moe_layer_p2p(ep, layer, x, T, stream): the partial step's down kernels
+ * store each (token, slot) sum straight into every rank's region (layer parity double
+ * buffer), a one-thread kernel publishes this rank's epoch to every rank's flags, and the
+ * combine waits (bounded, ~1 s) for all ranks' flags before adding in slot order.  All
+ * ranks must run the same layers in the same order; bit-identical to the all-reduce path.
+ * No collective library is involved; capturable in a CUDA graph (after the first call for
+ * the largest T).  tgx_ep_p2p_status reports an expired wait (TG_ETIMEOUT). */
+size_t tgx_ep_p2p_handle_bytes(void);
+int tgx_ep_p2p_init(tgx_ep *ep, int T_max, void *handle_out);
+int tgx_ep_p2p_connect(tgx_ep *ep, const void *handles);
+int tgx_ep_moe_layer_p2p(tgx_ep *ep, int layer, float *x_dev, int T, void *stream);
+int tgx_ep_p2p_status(tgx_ep *ep, void *stream);
+/* close this rank's mappings of the peers' regions (after its last layer).  A region may
+ * be freed (tgx_ep_destroy) only once every rank has disconnected: put a barrier
+ * between the two. */
+int tgx_ep_p2p_disconnect(tgx_ep *ep);
+
 /* ===================== the reference's formats on device pointers ===================== */
 
 /* Device bytes of a rows x cols matrix of format fmt (0 Q4_K, 1 f16, 2 Q6_K, 4 f32;

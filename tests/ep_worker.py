@@ -25,11 +25,16 @@ def main() -> int:
     try:
         ep = EPMoEModel(H, I, E, K, L, rank=rank, size=world, device=local)
         ep.fill_synthetic(2024)
+        p2p = os.environ.get("EP_P2P", "0") == "1"
+        if p2p:
+            ep.enable_p2p(64)
         g = torch.Generator(device="cuda").manual_seed(99)
         X = torch.randn(T, H, generator=g, device="cuda")           # the same tokens on every rank
         X0 = X.clone()
         ep.decode(X)
         torch.cuda.synchronize()
+        if p2p:
+            ep.p2p_status()
         same = torch.tensor([1.0], device="cuda")
         if rank == 0:
             full = MoEModel(H, I, E, K, L, device=local)
@@ -41,11 +46,12 @@ def main() -> int:
             same[0] = 1.0 if ok else 0.0
         dist.broadcast(same, 0)                                        # every rank takes the same steps
         ok = bool(same.item() == 1.0)
-        ep.close()
+        ep.close()                                                     # disconnect, barrier, free
     finally:
         dist.destroy_process_group()
     if rank == 0:
-        print("ep-nccl", "bit-identical" if ok else "MISMATCH", flush=True)
+        print("ep-p2p" if os.environ.get("EP_P2P") == "1" else "ep-nccl", "bit-identical" if ok else "MISMATCH",
+              flush=True)
     return 0 if ok else 1
 
 

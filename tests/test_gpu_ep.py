@@ -127,6 +127,42 @@ def test_ep_dsv3_width_matches_oracle(oracle):
         ep.close()
 
 
+@pytest.mark.parametrize("T,kernels", [(1, 0), (7, 1), (300, 2)])
+def test_ep_p2p_single_rank_matches_batched(T, kernels):
+    # the NVLink-exchange entry point with one rank (its own region, its own flags):
+    # chained layers (both buffer parities), eager and graph-replayed, against the
+    # single-GPU batched path
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    from tinygiant_b200.ep import EPMoEModel
+    L = 3
+    full = MoEModel(H, I, E, K, L)
+    full.fill_synthetic(31)
+    ep = EPMoEModel(H, I, E, K, L, rank=0, size=1)
+    ep.fill_synthetic(31)
+    ep.set_kernels(kernels)
+    ep.enable_p2p(512)
+    X = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda")
+    want = X.clone()
+    full.decode_batched(want)
+    got = X.clone()
+    ep.decode(got)
+    ep.p2p_status()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    graph = torch.cuda.CUDAGraph()
+    Xg = X.clone()
+    with torch.cuda.graph(graph):
+        ep.decode(Xg)
+    for _ in range(2):
+        Xg.copy_(X)
+        graph.replay()
+        ep.p2p_status()
+        assert torch.equal(Xg.view(torch.int32), want.view(torch.int32))
+    del graph
+    ep.close()
+    full.close()
+
+
 def test_ep_rejects_foreign_experts():
     import numpy as np
     from tinygiant_b200._lib import TinyGiantError
@@ -140,13 +176,16 @@ def test_ep_rejects_foreign_experts():
     ep.close()
 
 
-def test_ep_nccl_matches_single_gpu():
+@pytest.mark.parametrize("p2p", ["0", "1"])
+def test_ep_nccl_matches_single_gpu(p2p):
+    # p2p = 1: the exchange by direct NVLink stores and flags instead of the all-reduce
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_P2P=p2p)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531", str(ROOT / "tests" / "ep_worker.py")]
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(p2p)}",
+           str(ROOT / "tests" / "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
     assert "bit-identical" in r.stdout

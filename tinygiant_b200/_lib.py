@@ -90,6 +90,12 @@ PROTOTYPES = {
     "tgx_ep_combine": (CI, [VP, VP, CI, VP, VP]),
     "tgx_ep_set_kernels": (CI, [VP, CI]),
     "tgx_ep_status": (CI, [VP, VP]),
+    "tgx_ep_p2p_handle_bytes": (SZ, []),
+    "tgx_ep_p2p_init": (CI, [VP, CI, VP]),
+    "tgx_ep_p2p_connect": (CI, [VP, VP]),
+    "tgx_ep_moe_layer_p2p": (CI, [VP, CI, VP, CI, VP]),
+    "tgx_ep_p2p_status": (CI, [VP, VP]),
+    "tgx_ep_p2p_disconnect": (CI, [VP]),
     "tgx_set_batched_kernels": (CI, [VP, CI]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),

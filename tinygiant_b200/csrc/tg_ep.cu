@@ -14,6 +14,7 @@
 // (tinygiant/engine.py:229-258 per token, the reference's sequential combine).
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -41,6 +42,17 @@ struct tgx_ep {
     int last_T = 0;
     int kernels = 0;              // tg::BATCHED_AUTO / _DP4A / _MMA
     cudaStream_t s = nullptr;
+    // NVLink exchange (tgx_ep_p2p_*): one region per rank, y[0] | y[1] | flags[G], shared
+    // through CUDA IPC; y[b] holds layer parity b's per-(token, slot) down sums
+    int p2p_T = 0;                // tokens per step the region holds
+    uint8_t* region = nullptr;    // this rank's region
+    size_t y_bytes = 0, region_bytes = 0;
+    void* peers[64] = {};         // opened peer regions (null for this rank)
+    float** dst_dev = nullptr;    // [2][G]: rank q's y[b]
+    unsigned** flag_dev = nullptr;  // [G]: rank q's flags
+    unsigned* epoch = nullptr;    // layers exchanged so far (device)
+    unsigned* p2p_err = nullptr;  // a bounded wait expired
+    bool p2p_ready = false;
 };
 
 namespace {
@@ -78,6 +90,10 @@ struct Dev {
 void ep_free(tgx_ep* c) {
     if (!c) return;
     Dev dg(c->device);
+    for (int q = 0; q < 64; q++)
+        if (c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
+    for (void* p : {(void*)c->region, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err})
+        if (p) cudaFree(p);
     for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
                     c->scratch, (void*)c->wts})
         if (p) cudaFree(p);
@@ -334,6 +350,178 @@ extern "C" int tgx_ep_status(tgx_ep* ep, void* stream) {
     if (flag) {
         EP_CUDA(cudaMemset(ep->scratch, 0, sizeof(flag)));
         return ep_fail(TG_ETIMEOUT, "tgx_ep: a tensor-core expert kernel's bounded wait expired");
+    }
+    return TG_OK;
+}
+
+// ------------------------------------------------------------ the NVLink exchange
+
+namespace {
+
+constexpr long long EP_WAIT_CYCLES = 2000000000ll;   // ~1 s
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One thread, after this rank's down kernel on the same stream: the layer's exchange
+// stores are complete (kernel boundary; the down threads fenced them system-wide), so
+// publish the next epoch in this rank's slot of every rank's flags.
+__global__ void k_ep_signal(unsigned* epoch, unsigned* const* flags, int rank, int G) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    __threadfence_system();
+    const unsigned e = *epoch + 1u;
+    *epoch = e;
+    for (int q = 0; q < G; q++) st_release_sys(flags[q] + rank, e);
+}
+
+// grid T: wait (bounded) until every rank published this layer's epoch, then
+// x[t] += sum_j w[t][j] * y[(t, j)] in slot order from this rank's buffer.
+__global__ void __launch_bounds__(256) k_ep_combine_p2p(float* __restrict__ X, int H, int ks,
+                                                        const float* __restrict__ wts, const float* y,
+                                                        const unsigned* flags, const unsigned* epoch, int G,
+                                                        unsigned* err) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+        const unsigned e = *epoch;
+        int good = 1;
+        const long long t0 = clock64();
+        for (int q = 0; q < G && good; q++)
+            while ((int)(ld_acquire_sys(flags + q) - e) < 0)
+                if (clock64() - t0 > EP_WAIT_CYCLES) {
+                    good = 0;
+                    break;
+                }
+        if (!good) atomicExch(err, 1u);
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;
+    const int t = blockIdx.x;
+    for (int r = threadIdx.x; r < H; r += blockDim.x) {
+        float a = 0.0f;
+        for (int j = 0; j < ks; j++)
+            a = __fadd_rn(a, __fmul_rn(wts[(size_t)t * ks + j], __ldcg(y + ((size_t)t * ks + j) * H + r)));
+        X[(size_t)t * H + r] = __fadd_rn(X[(size_t)t * H + r], a);
+    }
+}
+
+}  // namespace
+
+extern "C" int tgx_ep_p2p_init(tgx_ep* ep, int T_max, void* handle_out) {
+    EP_CHECK(ep && handle_out, TG_EINVAL, "tgx_ep_p2p_init: null argument");
+    EP_CHECK(T_max >= 1 && T_max <= 65536 / ep->shape.top_k, TG_EINVAL, "tgx_ep_p2p_init: T_max out of range");
+    EP_CHECK(!ep->region, TG_EINVAL, "tgx_ep_p2p_init: already initialised");
+    EP_CHECK(ep->size <= 64, TG_EINVAL, "tgx_ep_p2p_init: at most 64 ranks");
+    Dev dg(ep->device);
+    const size_t ks = (size_t)ep->shape.top_k + ep->n_shared;
+    ep->p2p_T = T_max;
+    ep->y_bytes = ((size_t)T_max * ks * ep->shape.embed * 4 + 255) & ~(size_t)255;
+    ep->region_bytes = 2 * ep->y_bytes + 256;
+    EP_TRY(ep_alloc((void**)&ep->region, ep->region_bytes, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->dst_dev, sizeof(float*) * 2 * ep->size, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->flag_dev, sizeof(unsigned*) * ep->size, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->epoch, 256, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->p2p_err, 256, "tgx_ep_p2p_init"));
+    EP_CUDA(cudaMemset(ep->region + 2 * ep->y_bytes, 0, 256));   // flags
+    EP_CUDA(cudaMemset(ep->epoch, 0, 256));
+    EP_CUDA(cudaMemset(ep->p2p_err, 0, 256));
+    cudaIpcMemHandle_t h;
+    EP_CUDA(cudaIpcGetMemHandle(&h, ep->region));
+    memcpy(handle_out, &h, sizeof(h));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_p2p_connect(tgx_ep* ep, const void* handles) {
+    EP_CHECK(ep && handles, TG_EINVAL, "tgx_ep_p2p_connect: null argument");
+    EP_CHECK(ep->region && !ep->p2p_ready, TG_EINVAL, "tgx_ep_p2p_connect: call tgx_ep_p2p_init first, once");
+    Dev dg(ep->device);
+    const int G = ep->size;
+    std::vector<uint8_t*> base(G);
+    for (int q = 0; q < G; q++) {
+        if (q == ep->rank) {
+            base[q] = ep->region;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + (size_t)q * sizeof(h), sizeof(h));
+        EP_CUDA(cudaIpcOpenMemHandle(&ep->peers[q], h, cudaIpcMemLazyEnablePeerAccess));
+        base[q] = (uint8_t*)ep->peers[q];
+    }
+    std::vector<float*> dst(2 * G);
+    std::vector<unsigned*> fl(G);
+    for (int q = 0; q < G; q++) {
+        dst[q] = (float*)base[q];
+        dst[G + q] = (float*)(base[q] + ep->y_bytes);
+        fl[q] = (unsigned*)(base[q] + 2 * ep->y_bytes);
+    }
+    EP_CUDA(cudaMemcpy(ep->dst_dev, dst.data(), sizeof(float*) * 2 * G, cudaMemcpyHostToDevice));
+    EP_CUDA(cudaMemcpy(ep->flag_dev, fl.data(), sizeof(unsigned*) * G, cudaMemcpyHostToDevice));
+    ep->p2p_ready = true;
+    return TG_OK;
+}
+
+extern "C" size_t tgx_ep_p2p_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int tgx_ep_p2p_disconnect(tgx_ep* ep) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_p2p_disconnect: null context");
+    Dev dg(ep->device);
+    EP_CUDA(cudaDeviceSynchronize());
+    for (int q = 0; q < 64; q++)
+        if (ep->peers[q]) {
+            EP_CUDA(cudaIpcCloseMemHandle(ep->peers[q]));
+            ep->peers[q] = nullptr;
+        }
+    ep->p2p_ready = false;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_moe_layer_p2p(tgx_ep* ep, int layer, float* x_dev, int T, void* stream) {
+    EP_CHECK(ep && x_dev, TG_EINVAL, "tgx_ep_moe_layer_p2p: null argument");
+    EP_CHECK(ep->p2p_ready, TG_EINVAL, "tgx_ep_moe_layer_p2p: exchange not connected (tgx_ep_p2p_connect)");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_moe_layer_p2p: layer out of range");
+    EP_CHECK(T >= 1 && T <= ep->p2p_T, TG_EINVAL, "tgx_ep_moe_layer_p2p: T must be in [1, the T_max of p2p_init]");
+    Dev dg(ep->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    int optin = 0;
+    EP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ep->device));
+    EP_CHECK(tg::batched_smem_bytes(ep->g) <= (size_t)optin, TG_EUNSUPPORTED,
+             "tgx_ep_moe_layer_p2p: shape needs more shared memory per block than the device has");
+    EP_TRY(ep_reserve(ep, T, s, "tgx_ep_moe_layer_p2p"));
+    const tgx_shape& sh = ep->shape;
+    const size_t nr = (size_t)sh.n_experts * sh.embed;
+    const int b = layer & 1, G = ep->size, ks = sh.top_k + ep->n_shared;
+    const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
+    EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, shared, ep->e_lo, ep->e_n,
+                                           ep->rank, G, ep->g, ep->routers + (size_t)layer * nr,
+                                           ep->norms + (size_t)layer * sh.embed, ep->eps, sh.n_experts, ep->n_shared,
+                                           sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, nullptr, nullptr,
+                                           ep->wts, nullptr, ep->kernels, s, ep->dst_dev + (size_t)b * G, G));
+    k_ep_signal<<<1, 32, 0, s>>>(ep->epoch, ep->flag_dev, ep->rank, G);
+    EP_CUDA(cudaGetLastError());
+    k_ep_combine_p2p<<<T, 256, 0, s>>>(x_dev, sh.embed, ks, ep->wts,
+                                        (const float*)(ep->region + (size_t)b * ep->y_bytes),
+                                        (const unsigned*)(ep->region + 2 * ep->y_bytes), ep->epoch, G, ep->p2p_err);
+    EP_CUDA(cudaGetLastError());
+    ep->last_T = T;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_p2p_status(tgx_ep* ep, void* stream) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_p2p_status: null context");
+    if (!ep->p2p_err) return TG_OK;
+    Dev dg(ep->device);
+    EP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    unsigned flag = 0;
+    EP_CUDA(cudaMemcpy(&flag, ep->p2p_err, sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag) {
+        EP_CUDA(cudaMemset(ep->p2p_err, 0, sizeof(flag)));
+        return ep_fail(TG_ETIMEOUT, "tgx_ep_moe_layer_p2p: a peer's exchange flag did not arrive within the wait limit");
     }
     return TG_OK;
 }

@@ -12,7 +12,9 @@ output is computed by the rank holding the fewest of its routed experts.  One Mo
 
 Each element of y has one nonzero contribution, so the sum is exact and the result is
 bit-identical to the single-GPU batched path (and, through it, to the CPU oracle).
-The all-reduce moves T * top_k * embed floats per layer.
+The all-reduce moves T * top_k * embed floats per layer.  After enable_p2p() the
+exchange is direct instead: the down kernels store each (token, slot) sum into every
+rank's exchange buffer over NVLink and the combine waits on per-rank epoch flags.
 
     ep = EPMoEModel(rank=r, size=G, device=local_rank)
     ep.fill_synthetic(seed)            # or load_experts(layer, first, blob) for the local range
@@ -71,14 +73,23 @@ class EPMoEModel:
         self.expert_bytes = C.expert_bytes(embed, inter)
         self._y = {}
 
-    def close(self):
+    def close(self, barrier: bool = True):
+        """Free the context.  With the NVLink exchange every rank first drops its
+        mappings of the others' regions, then a barrier, then the regions are freed."""
         if self._ep:
+            if getattr(self, "p2p", False):
+                self.lib.tgx_ep_p2p_disconnect(self._ep)
+                if self.size > 1 and barrier:
+                    import torch.distributed as dist
+                    if dist.is_initialized():
+                        dist.barrier(group=self.group)
+                self.p2p = False
             self.lib.tgx_ep_destroy(self._ep)
             self._ep = None
 
     def __del__(self):
         try:
-            self.close()
+            self.close(barrier=False)   # never a collective from the garbage collector
         except Exception:
             pass
 
@@ -140,10 +151,39 @@ class EPMoEModel:
         check(self.lib.tgx_ep_combine(self._ep, _dev_ptr(X), X.shape[0], _dev_ptr(Y), _stream_handle(stream)),
               self.lib)
 
+    def enable_p2p(self, t_max: int, exchange=None):
+        """Switch the exchange from the all-reduce to direct NVLink stores between the
+        ranks' down kernels (tgx_ep_p2p_*).  exchange(bytes) -> list of every rank's bytes
+        in rank order; default: torch.distributed.all_gather_object on self.group."""
+        n = int(self.lib.tgx_ep_p2p_handle_bytes())
+        h = (ctypes.c_uint8 * n)()
+        check(self.lib.tgx_ep_p2p_init(self._ep, t_max, h), self.lib)
+        mine = bytes(h)
+        if exchange is None:
+            if self.size == 1:
+                handles = [mine]
+            else:
+                import torch.distributed as dist
+                handles = [None] * self.size
+                dist.all_gather_object(handles, mine, group=self.group)
+        else:
+            handles = exchange(mine)
+        assert len(handles) == self.size and handles[self.rank] == mine
+        buf = (ctypes.c_uint8 * (n * self.size)).from_buffer_copy(b"".join(handles))
+        check(self.lib.tgx_ep_p2p_connect(self._ep, buf), self.lib)
+        self.p2p = True
+
+    def p2p_status(self, stream=None):
+        check(self.lib.tgx_ep_p2p_status(self._ep, _stream_handle(stream)), self.lib)
+
     def moe_layer(self, layer: int, X, stream=None):
         """MoE block `layer` for the T tokens of X (cuda f32[T][embed]) in place."""
-        import torch.distributed as dist
         assert X.dim() == 2 and X.shape[1] == self.embed
+        if getattr(self, "p2p", False):
+            check(self.lib.tgx_ep_moe_layer_p2p(self._ep, layer, _dev_ptr(X), X.shape[0], _stream_handle(stream)),
+                  self.lib)
+            return
+        import torch.distributed as dist
         Y = self.y_buffer(X.shape[0])
         self.partial(layer, X, Y, stream)
         if self.size > 1:
