@@ -294,10 +294,11 @@ int tgx_ep_status(tgx_ep *ep, void *stream);
  * T_max, handle) allocates its exchange region and returns its CUDA IPC handle
  * (tgx_ep_p2p_handle_bytes() bytes); the caller gathers all ranks' handles in rank order
  * (any host-side exchange) and passes them to tgx_ep_p2p_connect.  Then one call per
- * layer, tgx_ep_moe_layer_p2p(ep, layer, x, T, stream): the partial step's down kernels
- * store each (token, slot) sum straight into every rank's region (layer parity double
- * buffer), a one-thread kernel publishes this rank's epoch to every rank's flags, and the
- * combine waits (bounded, ~1 s) for all ranks' flags before adding in slot order.  All
+ * layer, tgx_ep_moe_layer_p2p(ep, layer, x, T, stream): the partial step writes this
+ * rank's (token, slot) sums into its own region (layer parity double buffer), one kernel
+ * copies each of those rows (contiguous) into every peer's region over NVLink and, in its
+ * last CTA, publishes this rank's epoch to every rank's flags, and the combine waits
+ * (bounded, ~1 s) for all ranks' flags before adding in slot order.  All
  * ranks must run the same layers in the same order; bit-identical to the all-reduce path.
  * No collective library is involved; capturable in a CUDA graph (after the first call for
  * the largest T).  tgx_ep_p2p_status reports an expired wait (TG_ETIMEOUT). */

@@ -172,7 +172,8 @@ __device__ __forceinline__ bool pair_owned(const int* __restrict__ idx, int p, i
 // does not affect any result) and active[0] = count, active[1..] = the experts, ascending
 __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int ks, int k,
                                                      int E_tot, int e_n, int rank, int G, int* __restrict__ off,
-                                                     int* __restrict__ list, int* __restrict__ active) {
+                                                     int* __restrict__ list, int* __restrict__ active,
+                                                     int* __restrict__ owned) {
     __shared__ int cnt[1025];
     __shared__ int pos[1025];
     for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
@@ -190,10 +191,15 @@ __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx
         }
         off[E_tot] = acc;
         active[0] = na;
+        if (owned) owned[0] = acc;
     }
     __syncthreads();
     for (int p = threadIdx.x; p < n_pairs; p += blockDim.x)
-        if (pair_owned(idx, p, ks, k, e_n, rank, G)) list[atomicAdd(&pos[idx[p]], 1)] = p;
+        if (pair_owned(idx, p, ks, k, e_n, rank, G)) {
+            const int slot = atomicAdd(&pos[idx[p]], 1);
+            list[slot] = p;
+            if (owned) owned[1 + slot] = p;
+        }
 }
 
 // expert e's blob: a local routed expert, or the shared expert (e == E)
@@ -325,13 +331,11 @@ __global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, c
 // tiles of 16 tokens: each lane runs the lane-strided block chains of its warp's 2 rows
 // for every token of the tile, and one transposed reduction leaves lane l with the sum of
 // (row l / 16, token l % 16): y[p][r] = row . hq[p], exactly the single-token arithmetic.
-// With n_dst > 0 each value goes to the n_dst buffers of ydst instead of y.
 __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer,
                                                       const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                       const int* __restrict__ off, const int* __restrict__ list,
                                                       const int* __restrict__ active, const uint8_t* __restrict__ hq,
-                                                      float* __restrict__ y, float* const* __restrict__ ydst,
-                                                      int n_dst) {
+                                                      float* __restrict__ y) {
     extern __shared__ __align__(16) uint8_t smem[];   // DOWN_ROWS rows
     __shared__ int sp[DOWN_TOK];
     if ((int)blockIdx.y >= active[0]) return;
@@ -382,15 +386,8 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
         }
         const float yv = warp_sum32_transposed(acc, lane);
         const int r = lane / DOWN_TOK, t = lane % DOWN_TOK;
-        if (t < nt && lr0 + r < nrows) {
-            const size_t o = (size_t)sp[t] * g.H + r0 + lr0 + r;
-            if (n_dst == 0)
-                y[o] = yv;
-            else   // every rank's exchange buffer, peers' over NVLink
-                for (int q = 0; q < n_dst; q++) ydst[q][o] = yv;
-        }
+        if (t < nt && lr0 + r < nrows) y[(size_t)sp[t] * g.H + r0 + lr0 + r] = yv;
     }
-    if (n_dst) __threadfence_system();   // the exchange stores are visible system-wide before the signal
 }
 
 // grid T, 256 threads: x[t][r] = x[t][r] + (sum over slots j in order of w[t][j] * y[t*k+j][r])
@@ -437,8 +434,8 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                                        int G, Geom g, const float* R, const float* normw, float eps, int E,
                                        int n_shared, int k, const float* X, int T, void* scratch,
                                        size_t scratch_bytes, float* y, int* idx_out, float* w_out,
-                                       float* logits_out, int kernels, cudaStream_t s, float* const* ydst,
-                                       int n_dst) {
+                                       float* logits_out, int kernels, cudaStream_t s, bool zero_y,
+                                       int* owned) {
     if (T <= 0) return cudaSuccess;
     if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || n_shared < 0 || n_shared > 1 ||
         (n_shared && !shared) || k + n_shared > MAX_TOPK + 1 || G < 1 || rank < 0 || rank >= G || e_n * G != E ||
@@ -473,24 +470,23 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     if (batched_smem_bytes(g) > (size_t)optin) return cudaErrorInvalidValue;
     if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
     // pairs computed on other devices keep y = 0 (their owner adds theirs)
-    if (G > 1 && n_dst == 0 && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
+    if (G > 1 && zero_y && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
     k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
                                                                                                 g.H, S);
     k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, ks, S, idx, wts, logits_out, xq);
-    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active);
+    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active, owned);
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
     const bool mma = q4_mma_supported(g) &&
                      (kernels == BATCHED_MMA ||
                       (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * (E + n_shared)));
     if (mma) {
-        if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, n_act, ks, xq, hf, uf, err, s,
-                               nullptr, 0)) != cudaSuccess)
+        if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, n_act, ks, xq, hf, uf, err, s)) !=
+            cudaSuccess)
             return e;
         const long long warps = (long long)n_pairs * g.nbI;
         k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq);
-        return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, n_act, ks, hq, y, nullptr, err, s,
-                             ydst, n_dst);
+        return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, n_act, ks, hq, y, nullptr, err, s);
     }
     const int R_gu = gu_rows(g, (size_t)optin);
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
@@ -517,7 +513,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
             cudaSuccess)
         return e;
     k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, shared, E, e_lo, g, off,
-                                                                                      list, active, hq, y, ydst, n_dst);
+                                                                                      list, active, hq, y);
     return cudaGetLastError();
 }
 

@@ -52,6 +52,8 @@ struct tgx_ep {
     unsigned** flag_dev = nullptr;  // [G]: rank q's flags
     unsigned* epoch = nullptr;    // layers exchanged so far (device)
     unsigned* p2p_err = nullptr;  // a bounded wait expired
+    unsigned* p2p_count = nullptr;  // push CTAs finished this layer (zero between layers)
+    int* owned = nullptr;         // [1 + T * ks]: count and list of the pairs this rank computed
     bool p2p_ready = false;
 };
 
@@ -92,7 +94,8 @@ void ep_free(tgx_ep* c) {
     Dev dg(c->device);
     for (int q = 0; q < 64; q++)
         if (c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
-    for (void* p : {(void*)c->region, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err})
+    for (void* p : {(void*)c->region, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err,
+                    (void*)c->p2p_count, (void*)c->owned})
         if (p) cudaFree(p);
     for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
                     c->scratch, (void*)c->wts})
@@ -369,15 +372,35 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// One thread, after this rank's down kernel on the same stream: the layer's exchange
-// stores are complete (kernel boundary; the down threads fenced them system-wide), so
-// publish the next epoch in this rank's slot of every rank's flags.
-__global__ void k_ep_signal(unsigned* epoch, unsigned* const* flags, int rank, int G) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    __threadfence_system();
-    const unsigned e = *epoch + 1u;
-    *epoch = e;
-    for (int q = 0; q < G; q++) st_release_sys(flags[q] + rank, e);
+// grid = T * ks CTAs, after this rank's partial step on the same stream: CTA i < owned[0]
+// copies the i-th pair this rank computed (its y row, H floats, contiguous) into every
+// peer's buffer with 16-byte stores over NVLink, fenced system-wide; the last CTA to
+// finish publishes the next epoch in this rank's slot of every rank's flags.
+__global__ void __launch_bounds__(256) k_ep_push_signal(const int* __restrict__ owned, const float* __restrict__ y,
+                                                        float* const* __restrict__ dst, int G, int rank, int H,
+                                                        unsigned* count, unsigned* epoch, unsigned* const* flags) {
+    const int i = blockIdx.x;
+    if (i < owned[0]) {
+        const int p = owned[1 + i];
+        const float4* src = reinterpret_cast<const float4*>(y + (size_t)p * H);
+        for (int q = 0; q < G; q++) {
+            if (q == rank) continue;
+            float4* d = reinterpret_cast<float4*>(dst[q] + (size_t)p * H);
+            for (int c = threadIdx.x; c < H / 4; c += blockDim.x) d[c] = __ldcg(src + c);
+        }
+        __threadfence_system();
+    }
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) last = atomicAdd(count, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence_system();
+        *count = 0u;
+        const unsigned e = *epoch + 1u;
+        *epoch = e;
+        for (int q = 0; q < G; q++) st_release_sys(flags[q] + rank, e);
+    }
 }
 
 // grid T: wait (bounded) until every rank published this layer's epoch, then
@@ -428,9 +451,12 @@ extern "C" int tgx_ep_p2p_init(tgx_ep* ep, int T_max, void* handle_out) {
     EP_TRY(ep_alloc((void**)&ep->flag_dev, sizeof(unsigned*) * ep->size, "tgx_ep_p2p_init"));
     EP_TRY(ep_alloc((void**)&ep->epoch, 256, "tgx_ep_p2p_init"));
     EP_TRY(ep_alloc((void**)&ep->p2p_err, 256, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->p2p_count, 256, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->owned, sizeof(int) * (1 + (size_t)T_max * ks), "tgx_ep_p2p_init"));
     EP_CUDA(cudaMemset(ep->region + 2 * ep->y_bytes, 0, 256));   // flags
     EP_CUDA(cudaMemset(ep->epoch, 0, 256));
     EP_CUDA(cudaMemset(ep->p2p_err, 0, 256));
+    EP_CUDA(cudaMemset(ep->p2p_count, 0, 256));
     cudaIpcMemHandle_t h;
     EP_CUDA(cudaIpcGetMemHandle(&h, ep->region));
     memcpy(handle_out, &h, sizeof(h));
@@ -497,12 +523,14 @@ extern "C" int tgx_ep_moe_layer_p2p(tgx_ep* ep, int layer, float* x_dev, int T, 
     const size_t nr = (size_t)sh.n_experts * sh.embed;
     const int b = layer & 1, G = ep->size, ks = sh.top_k + ep->n_shared;
     const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
+    float* y = (float*)(ep->region + (size_t)b * ep->y_bytes);
     EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, shared, ep->e_lo, ep->e_n,
                                            ep->rank, G, ep->g, ep->routers + (size_t)layer * nr,
                                            ep->norms + (size_t)layer * sh.embed, ep->eps, sh.n_experts, ep->n_shared,
-                                           sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, nullptr, nullptr,
-                                           ep->wts, nullptr, ep->kernels, s, ep->dst_dev + (size_t)b * G, G));
-    k_ep_signal<<<1, 32, 0, s>>>(ep->epoch, ep->flag_dev, ep->rank, G);
+                                           sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, y, nullptr, ep->wts,
+                                           nullptr, ep->kernels, s, false, ep->owned));
+    k_ep_push_signal<<<T * ks, 256, 0, s>>>(ep->owned, y, ep->dst_dev + (size_t)b * G, G, ep->rank, sh.embed,
+                                            ep->p2p_count, ep->epoch, ep->flag_dev);
     EP_CUDA(cudaGetLastError());
     k_ep_combine_p2p<<<T, 256, 0, s>>>(x_dev, sh.embed, ks, ep->wts,
                                         (const float*)(ep->region + (size_t)b * ep->y_bytes),

@@ -93,8 +93,7 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
 bool q4_mma_supported(const Geom& g);
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
                           const int* off, const int* list, const int* active, int n_act, int ks, const uint8_t* act,
-                          float* out0, float* out1, unsigned* err, cudaStream_t s, float* const* dst = nullptr,
-                          int n_dst = 0);
+                          float* out0, float* out1, unsigned* err, cudaStream_t s);
 // The two halves of launch_moe_batched, generalised to experts sharded over G devices
 // and an optional shared expert.  Partial: routing of all T tokens (every device
 // computes the same), then y[(t, j)][H] for the pairs this device owns (routed slot j < k:
@@ -107,17 +106,16 @@ cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, in
 // bounded wait expired sets it).  Combine:
 // X[t] += sum_j w[t][j] * y[(t, j)] in slot order (ks = k + n_shared slots).  With the y
 // of every device summed in between (one nonzero term per element, so the sum is
-// exact), the result is the single-device one bit for bit.  With n_dst > 0 the down
-// sums go to the n_dst buffers of the device array ydst (every rank's exchange buffer,
-// peers' mapped over NVLink) instead of y, and y is neither used nor zeroed: every pair
-// has exactly one owner, so the buffers end complete.
+// exact), the result is the single-device one bit for bit.  zero_y = false leaves the
+// other devices' pairs of y untouched (an exchange that writes them itself); owned, when
+// given ([1 + T * ks] ints), receives the count and list of the pairs this device computed.
 size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T);
 cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shared, int e_lo, int e_n, int rank,
                                        int G, Geom g, const float* R, const float* normw, float eps, int E,
                                        int n_shared, int k, const float* X, int T, void* scratch,
                                        size_t scratch_bytes, float* y, int* idx_out, float* w_out,
-                                       float* logits_out, int kernels, cudaStream_t s, float* const* ydst = nullptr,
-                                       int n_dst = 0);
+                                       float* logits_out, int kernels, cudaStream_t s, bool zero_y = true,
+                                       int* owned = nullptr);
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s);
 

@@ -127,8 +127,6 @@ struct TcParams {
     float* out0;               // [pair][rows]
     float* out1;
     unsigned* err;             // set when a bounded wait expired
-    float* const* dst;         // down with n_dst > 0: the n_dst buffers each value goes to (instead of out0)
-    int n_dst;
 };
 
 __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
@@ -358,13 +356,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
 #pragma unroll
         for (int t = 0; t < 8; t++) {
             const int tk = cg * 8 + t;
-            if (tk < nt) {
-                const size_t o = (size_t)s_pair[tk] * rows + r_base + row;
-                if (P.n_dst == 0)
-                    out[o] = st[t][5];
-                else   // every rank's exchange buffer, peers' over NVLink
-                    for (int q = 0; q < P.n_dst; q++) P.dst[q][o] = st[t][5];
-            }
+            if (tk < nt) out[(size_t)s_pair[tk] * rows + r_base + row] = st[t][5];
         }
     }
     if (failed) {
@@ -386,7 +378,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
         }
         if (tid == 0) atomicExch(P.err, 1u);
     }
-    if (P.n_dst) __threadfence_system();   // the exchange stores are visible system-wide before the signal
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(TMEM_COLS));
@@ -398,7 +389,7 @@ bool q4_mma_supported(const Geom& g) { return g.I % TM == 0 && g.H % TM == 0; }
 
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
                           const int* off, const int* list, const int* active, int n_act, int ks, const uint8_t* act,
-                          float* out0, float* out1, unsigned* err, cudaStream_t s, float* const* dst, int n_dst) {
+                          float* out0, float* out1, unsigned* err, cudaStream_t s) {
     if (n_act <= 0) return cudaSuccess;
     if (!q4_mma_supported(g)) return cudaErrorInvalidValue;
     TcParams P;
@@ -416,8 +407,6 @@ cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, in
     P.out0 = out0;
     P.out1 = out1;
     P.err = err;
-    P.dst = dst;
-    P.n_dst = n_dst;
     cudaError_t e = cudaFuncSetAttribute(k_q4_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     if (e != cudaSuccess) return e;
     const int gx = down ? g.H / TM : 2 * (g.I / TM);
