@@ -173,7 +173,7 @@ __device__ __forceinline__ bool pair_owned(const int* __restrict__ idx, int p, i
 __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int ks, int k,
                                                      int E_tot, int e_n, int rank, int G, int* __restrict__ off,
                                                      int* __restrict__ list, int* __restrict__ active,
-                                                     int* __restrict__ owned) {
+                                                     int* __restrict__ owned, int* __restrict__ tile_pre, int tile) {
     __shared__ int cnt[1025];
     __shared__ int pos[1025];
     for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
@@ -182,13 +182,18 @@ __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx
         if (pair_owned(idx, p, ks, k, e_n, rank, G)) atomicAdd(&cnt[idx[p]], 1);
     __syncthreads();
     if (threadIdx.x == 0) {
-        int acc = 0, na = 0;
+        int acc = 0, na = 0, tiles = 0;
         for (int e = 0; e < E_tot; e++) {
             off[e] = acc;
             pos[e] = acc;
             acc += cnt[e];
-            if (cnt[e]) active[1 + na++] = e;
+            if (cnt[e]) {
+                tile_pre[na] = tiles;          // token tiles of the active experts before this one
+                tiles += (cnt[e] + tile - 1) / tile;
+                active[1 + na++] = e;
+            }
         }
+        tile_pre[na] = tiles;
         off[E_tot] = acc;
         active[0] = na;
         if (owned) owned[0] = acc;
@@ -417,7 +422,8 @@ static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
 size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T) {
     const size_t ks = (size_t)k + n_shared, n_pairs = (size_t)T * ks, E_tot = (size_t)E + n_shared;
     return r256((size_t)T * E * 8) + r256((E_tot + 1) * 4) + r256((size_t)T * act_bytes(g.nbH)) + r256(n_pairs * 4) +
-           r256(n_pairs * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256(n_pairs * act_bytes(g.nbI)) +
+           r256(n_pairs * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256((E_tot + 2) * 4) +
+           r256(n_pairs * act_bytes(g.nbI)) +
            r256(n_pairs * g.I * 4) + r256(n_pairs * g.I * 4) + 256;
 }
 
@@ -459,6 +465,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     float* wts = w_out ? w_out : wts_s;
     int* off = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
     int* list = reinterpret_cast<int*>(take(n_pairs * 4));
+    int* tile_pre = reinterpret_cast<int*>(take((size_t)(E_tot + 2) * 4));
     uint8_t* hq = take(n_pairs * act_bytes(g.nbI));
     float* hf = reinterpret_cast<float*>(take(n_pairs * g.I * 4));
     float* uf = reinterpret_cast<float*>(take(n_pairs * g.I * 4));
@@ -474,19 +481,21 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
                                                                                                 g.H, S);
     k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, ks, S, idx, wts, logits_out, xq);
-    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active, owned);
+    k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active, owned,
+                                    tile_pre, q4_mma_tile_tokens());
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
     const bool mma = q4_mma_supported(g) &&
                      (kernels == BATCHED_MMA ||
                       (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * (E + n_shared)));
     if (mma) {
-        if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, n_act, ks, xq, hf, uf, err, s)) !=
-            cudaSuccess)
+        if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, tile_pre, n_act, ks, xq, hf, uf, err,
+                               s)) != cudaSuccess)
             return e;
         const long long warps = (long long)n_pairs * g.nbI;
         k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq);
-        return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, n_act, ks, hq, y, nullptr, err, s);
+        return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, tile_pre, n_act, ks, hq, y, nullptr, err,
+                             s);
     }
     const int R_gu = gu_rows(g, (size_t)optin);
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;

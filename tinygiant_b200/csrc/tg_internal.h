@@ -90,10 +90,13 @@ cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, con
 // sums (out0) and up sums (out1) [pair][I] from the tokens' Q8_0 x (act = xq per token),
 // down = 1 the down sums y [pair][H] from the pairs' Q8_0 h (act = hq per pair).  Rows of
 // I and H must be multiples of 128.  err is set when a bounded wait expired.
+// tile_pre[a] (a = 0 .. active count): prefix sums of the active experts' 32-token
+// tiles (q4_mma_tile_tokens()).
 bool q4_mma_supported(const Geom& g);
+int q4_mma_tile_tokens();
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
-                          const int* off, const int* list, const int* active, int n_act, int ks, const uint8_t* act,
-                          float* out0, float* out1, unsigned* err, cudaStream_t s);
+                          const int* off, const int* list, const int* active, const int* tile_pre, int n_act, int ks,
+                          const uint8_t* act, float* out0, float* out1, unsigned* err, cudaStream_t s);
 // The two halves of launch_moe_batched, generalised to experts sharded over G devices
 // and an optional shared expert.  Partial: routing of all T tokens (every device
 // computes the same), then y[(t, j)][H] for the pairs this device owns (routed slot j < k:

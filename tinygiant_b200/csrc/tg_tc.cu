@@ -11,7 +11,8 @@
 // tree's siblings consecutive, so a 6-slot stack per (row, token) evaluates it as the
 // class sums arrive.
 //
-// CTA: 128 weight rows (one matrix of one expert) x a tile of 32 tokens; 16 warps.
+// Work item: 128 weight rows (one matrix of one expert) x a tile of 32 tokens; 16 warps,
+// one persistent CTA per SM walking its items' K groups as one pipeline.
 // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and owns tokens 8 (w / 4) .. + 7.
 // K runs in groups of 8 steps through three shared stages and two TMEM accumulator sets
 // (2 x 8 x 32 columns): while the epilogue reads group g, the tensor cores run group
@@ -107,6 +108,13 @@ __device__ __forceinline__ void push8(float (&st)[8][6], const float (&v)[8], in
     }
 }
 
+// Q4_0 codes of four bytes' low (or, after >> 4, high) nibbles as four signed bytes
+// q - 8: with bit 7 set first, the per-byte subtraction cannot borrow across bytes, and
+// the xor clears it again.
+__device__ __forceinline__ uint32_t nib_minus8(uint32_t x) {
+    return (((x & 0x0F0F0F0Fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+}
+
 __device__ __forceinline__ void tmem_ld8(uint32_t (&v)[8], uint32_t ta) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
@@ -121,6 +129,7 @@ struct TcParams {
     const int* off;            // pairs grouped by expert
     const int* list;
     const int* active;         // [0] count, [1..] experts
+    const int* tile_pre;       // [count + 1]: 32-token tiles of the active experts, prefix sums
     int ks;                    // slots per token
     int down;                  // 0: gate (out0) and up (out1) of the rows of I; 1: down rows of H (out0)
     const uint8_t* act;        // gate/up: xq per token (act_bytes(nbH)); down: hq per pair (act_bytes(nbI))
@@ -129,29 +138,38 @@ struct TcParams {
     unsigned* err;             // set when a bounded wait expired
 };
 
+constexpr int MAX_ACT = 1025;   // active experts (routed + shared)
+constexpr int RING = 4;         // work items whose token lists are held at once
+
+// Persistent: one CTA per SM takes work items w = blockIdx.x, + gridDim.x, ...; an item
+// is (token tile of an active expert, 128-row tile of one matrix), token-tile-major so
+// CTAs working at once share the tile's activations.  Its K groups are consecutive in
+// the CTA's flattened group sequence f, so the pipeline (three shared stages, two TMEM
+// sets) runs across item boundaries without restarting.
 __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t mbar[2];
     __shared__ uint32_t s_taddr;
-    __shared__ int s_pair[TN];
     __shared__ int s_fail;
     __shared__ uint16_t s_steps[MAX_STEPS];
+    __shared__ int s_tp[MAX_ACT + 1];             // tile prefix per active expert
+    __shared__ int s_e[MAX_ACT];                  // the active experts
+    __shared__ int s_p0[MAX_ACT], s_n[MAX_ACT];   // their first pair and pair count
+    __shared__ int s_pairs[RING][TN];             // token lists of the items in flight
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    if ((int)blockIdx.y >= P.active[0]) return;
-    const int e = P.active[1 + blockIdx.y];
-    const int p0 = P.off[e], n = P.off[e + 1] - p0;
-    if (n == 0) return;
     const Geom& g = P.g;
+    const int n_act = P.active[0];
     const int rows = P.down ? g.H : g.I;
     const int tiles = rows / TM;
-    const int mat = P.down ? 2 : (int)blockIdx.x / tiles;          // 0 gate, 1 up, 2 down
-    const int r_base = ((int)blockIdx.x % tiles) * TM;
+    const int MT = P.down ? tiles : 2 * tiles;       // matrix row tiles per token tile
+    const int n_items = P.tile_pre[n_act] * MT;
+    if ((int)blockIdx.x >= n_items) return;
+    const int n_mine = (n_items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
     const int nb = P.down ? g.nbI : g.nbH;
     const size_t row_bytes = P.down ? g.row_d : g.row_gu;
-    const uint8_t* eb = (e == P.E ? P.shared : P.layer + (size_t)(e - P.e_lo) * g.expert_bytes) +
-                        (size_t)mat * g.t_gu + (size_t)r_base * row_bytes;
     const size_t ab = act_bytes(nb);
-    float* out = mat == 1 ? P.out1 : P.out0;
+    const int NG = (nb + KG - 1) / KG;
+    const int F = n_mine * NG;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int row = (warp & 3) * 32 + lane;          // this thread's TMEM lane / weight row
     const int cg = warp >> 2;                        // token group: tokens 8cg .. 8cg+7
@@ -168,210 +186,260 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
         s_fail = 0;
         build_steps(nb, s_steps);
     }
+    for (int a = tid; a <= n_act; a += TC_THREADS) s_tp[a] = P.tile_pre[a];
+    for (int a = tid; a < n_act; a += TC_THREADS) {
+        const int e = P.active[1 + a];
+        s_e[a] = e;
+        s_p0[a] = P.off[e];
+        s_n[a] = P.off[e + 1] - P.off[e];
+    }
+    __syncthreads();
+
+    // item i of this CTA: its expert slot a, token tile j, matrix, row tile
+    struct Item {
+        int a, j, nt, mat, r_base;
+    };
+    auto item = [&](int i) -> Item {
+        Item it;
+        const int w = (int)blockIdx.x + i * (int)gridDim.x;
+        const int gt = w / MT, mt = w - gt * MT;
+        int lo = 0, hi = n_act;                      // s_tp[lo] <= gt < s_tp[hi]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (s_tp[mid] <= gt) lo = mid; else hi = mid;
+        }
+        it.a = lo;
+        it.j = gt - s_tp[lo];
+        it.nt = min(TN, s_n[lo] - TN * it.j);
+        it.mat = P.down ? 2 : mt / tiles;
+        it.r_base = (mt % tiles) * TM;
+        return it;
+    };
+    auto fill_ring = [&](int i) {   // token list of item i (threads < TN)
+        if (i < n_mine && tid < TN) {
+            const Item it = item(i);
+            s_pairs[i & (RING - 1)][tid] = tid < it.nt ? P.list[s_p0[it.a] + TN * it.j + tid] : -1;
+        }
+    };
+    for (int i = 0; i < 3; i++) fill_ring(i);
+
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tbase = s_taddr;
     uint32_t use0 = 0u, use1 = 0u;                   // completions consumed per mbarrier
-    const int NG = (nb + KG - 1) / KG;
+    int fail_f = -1;
     bool failed = false;
-    int fail_group = -1;
 
-    for (int t0 = 0; t0 < n && !failed; t0 += TN) {
-        const int nt = min(TN, n - t0);
-        __syncthreads();
-        if (tid < TN) s_pair[tid] = tid < nt ? P.list[p0 + t0 + tid] : -1;
-        __syncthreads();
-
-        // operand staging: 2 A items (row, step) and 1 B item (token, step) per thread
-        uint4 ra[2];
-        float rdw[2];
-        uint4 rb0, rb1;
-        float rdx = 0.0f;
-        auto load_group = [&](int gi) {
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int it = tid + TC_THREADS * u, r = it & (TM - 1), jj = it >> 7;
-                const int s = gi * KG + jj;
-                ra[u] = make_uint4(0, 0, 0, 0);
-                rdw[u] = 0.0f;
-                if (s < nb) {
-                    const int b = s_steps[s] & 1023;
-                    const uint8_t* rp = eb + (size_t)r * row_bytes;
-                    ra[u] = __ldg(reinterpret_cast<const uint4*>(rp + 16 * b));
-                    rdw[u] = f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(rp + 16 * (size_t)nb + 2 * b)));
-                }
-            }
-            rb0 = rb1 = make_uint4(0, 0, 0, 0);
-            rdx = 0.0f;
-            if (tid < TN * KG) {
-                const int tk = tid & (TN - 1), jj = tid >> 5, s = gi * KG + jj;
-                if (s < nb && tk < nt) {
-                    const int b = s_steps[s] & 1023;
-                    const int p = s_pair[tk];
-                    const uint8_t* ap = P.act + (size_t)(P.down ? p : p / P.ks) * ab;
-                    const ActView av = act_view(ap, nb);
-                    const uint4* q = reinterpret_cast<const uint4*>(av.qs + (size_t)b * 32);
-                    rb0 = __ldg(q);
-                    rb1 = __ldg(q + 1);
-                    rdx = __ldg(av.d + b);
-                }
-            }
-        };
-        auto store_group = [&](int stg) {
-            uint8_t* base = smem + (size_t)stg * STAGE_BYTES;
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const int it = tid + TC_THREADS * u, r = it & (TM - 1), jj = it >> 7;
-                uint8_t* a = base + ST_A + jj * A_STEP + (r >> 3) * 256 + (r & 7) * 16;
-                uint4 lo, hi;   // element j < 16: low nibble of byte j; 16 + j: high nibble; both minus 8
-                lo.x = __vsub4(ra[u].x & 0x0F0F0F0Fu, 0x08080808u);
-                lo.y = __vsub4(ra[u].y & 0x0F0F0F0Fu, 0x08080808u);
-                lo.z = __vsub4(ra[u].z & 0x0F0F0F0Fu, 0x08080808u);
-                lo.w = __vsub4(ra[u].w & 0x0F0F0F0Fu, 0x08080808u);
-                hi.x = __vsub4((ra[u].x >> 4) & 0x0F0F0F0Fu, 0x08080808u);
-                hi.y = __vsub4((ra[u].y >> 4) & 0x0F0F0F0Fu, 0x08080808u);
-                hi.z = __vsub4((ra[u].z >> 4) & 0x0F0F0F0Fu, 0x08080808u);
-                hi.w = __vsub4((ra[u].w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
-                *reinterpret_cast<uint4*>(a) = lo;
-                *reinterpret_cast<uint4*>(a + 128) = hi;
-                reinterpret_cast<float*>(base + ST_DW)[jj * TM + r] = rdw[u];
-            }
-            if (tid < TN * KG) {
-                const int tk = tid & (TN - 1), jj = tid >> 5;
-                uint8_t* bp = base + ST_B + jj * B_STEP + (tk >> 3) * 256 + (tk & 7) * 16;
-                *reinterpret_cast<uint4*>(bp) = rb0;
-                *reinterpret_cast<uint4*>(bp + 128) = rb1;
-                reinterpret_cast<float*>(base + ST_DX)[jj * TN + tk] = rdx;
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        };
-        // MMAs of group gi: operands in stage gi % NSTAGE, accumulators in TMEM set gi & 1
-        auto issue_group = [&](int gi) {
-            const uint8_t* base = smem + (size_t)(gi % NSTAGE) * STAGE_BYTES;
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            for (int jj = 0; jj < KG && gi * KG + jj < nb; jj++) {
-                const uint64_t da = kmajor_desc(base + ST_A + jj * A_STEP);
-                const uint64_t db = kmajor_desc(base + ST_B + jj * B_STEP);
-                const uint32_t dt = tbase + (uint32_t)((gi & 1) * KG * TN + jj * TN);
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
-                    "l"(da), "l"(db), "r"(IDESC), "r"(0));
-            }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             saddr(&mbar[gi & 1]))
-                         : "memory");
-        };
-        auto try_group = [&](int gi) -> bool {   // bounded wait for group gi's commit
-            const uint32_t parity = ((gi & 1) ? use1 : use0) & 1u;
-            const long long t_start = clock64();
-            while (true) {
-                uint32_t done;
-                asm volatile(
-                    "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-                    "selp.u32 %0, 1, 0, p;\n\t}"
-                    : "=r"(done)
-                    : "r"(saddr(&mbar[gi & 1])), "r"(parity)
-                    : "memory");
-                if (done) return true;
-                if (clock64() - t_start > TC_WAIT_CYCLES) return false;
-            }
-        };
-
-        float leaf[8], st[8][6];
-#pragma unroll
-        for (int t = 0; t < 8; t++) {
-            leaf[t] = 0.0f;
-#pragma unroll
-            for (int q = 0; q < 6; q++) st[t][q] = 0.0f;
+    // operand staging: 2 A items (row, step) and 1 B item (token, step) per thread
+    uint4 ra[2];
+    float rdw[2];
+    uint4 rb0, rb1;
+    float rdx = 0.0f;
+    int ld_i = -1;              // the loader's current item and where its rows start
+    Item ld_it{};
+    const uint8_t* ld_eb = nullptr;
+    auto load_group = [&](int f) {
+        const int i = f / NG, gi = f - i * NG;
+        if (i != ld_i) {
+            ld_i = i;
+            ld_it = item(i);
+            const int e = s_e[ld_it.a];
+            ld_eb = (e == P.E ? P.shared : P.layer + (size_t)(e - P.e_lo) * g.expert_bytes) +
+                    (size_t)ld_it.mat * g.t_gu + (size_t)ld_it.r_base * row_bytes;
         }
-        const float zero8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-        int next_cls = 0;   // class ordinal the stacks expect next (classes without blocks push 0)
-
-        load_group(0);
-        store_group(0);
-        if (NG > 1) {
-            load_group(1);
-            store_group(1);
-        }
-        __syncthreads();
-        if (tid == 0) issue_group(0);
-        for (int gi = 0; gi < NG; gi++) {
-            if (tid == 0 && gi + 1 < NG) issue_group(gi + 1);
-            if (gi + 2 < NG) load_group(gi + 2);
-            const bool ok = try_group(gi);
-            if (!ok) {
-                atomicExch(&s_fail, 1);
-                fail_group = gi;
-            } else if (gi & 1) {
-                use1++;
-            } else {
-                use0++;
+        const Item& it = ld_it;
+        const uint8_t* eb = ld_eb;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int x = tid + TC_THREADS * u, r = x & (TM - 1), jj = x >> 7;
+            const int s = gi * KG + jj;
+            ra[u] = make_uint4(0, 0, 0, 0);
+            rdw[u] = 0.0f;
+            if (s < nb) {
+                const int b = s_steps[s] & 1023;
+                const uint8_t* rp = eb + (size_t)r * row_bytes;
+                ra[u] = __ldg(reinterpret_cast<const uint4*>(rp + 16 * b));
+                rdw[u] = f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(rp + 16 * (size_t)nb + 2 * b)));
             }
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            if (ok) {
-                const uint8_t* stage = smem + (size_t)(gi % NSTAGE) * STAGE_BYTES;
-                const float* dwp = reinterpret_cast<const float*>(stage + ST_DW);
-                const float* dxp = reinterpret_cast<const float*>(stage + ST_DX);
-                const uint32_t tcol = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((gi & 1) * KG * TN + cg * 8);
-                const int nsteps = min(KG, nb - gi * KG);
-                uint32_t va[8], vb[8];
-                tmem_ld8(va, tcol);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        }
+        rb0 = rb1 = make_uint4(0, 0, 0, 0);
+        rdx = 0.0f;
+        if (tid < TN * KG) {
+            const int tk = tid & (TN - 1), jj = tid >> 5, s = gi * KG + jj;
+            if (s < nb && tk < it.nt) {
+                const int b = s_steps[s] & 1023;
+                const int p = s_pairs[i & (RING - 1)][tk];
+                const ActView av = act_view(P.act + (size_t)(P.down ? p : p / P.ks) * ab, nb);
+                const uint4* q = reinterpret_cast<const uint4*>(av.qs + (size_t)b * 32);
+                rb0 = __ldg(q);
+                rb1 = __ldg(q + 1);
+                rdx = __ldg(av.d + b);
+            }
+        }
+    };
+    auto store_group = [&](int stg) {
+        uint8_t* base = smem + (size_t)stg * STAGE_BYTES;
 #pragma unroll
-                for (int jj = 0; jj < KG; jj++) {
-                    if (jj < nsteps) {
-                        uint32_t (&cur)[8] = (jj & 1) ? vb : va;
-                        uint32_t (&nxt)[8] = (jj & 1) ? va : vb;
-                        if (jj + 1 < nsteps) tmem_ld8(nxt, tcol + (uint32_t)((jj + 1) * TN));
-                        const int code = s_steps[gi * KG + jj];
-                        const int c = (code >> 10) & 31;
-                        for (; next_cls < c; next_cls++) push8(st, zero8, next_cls);
-                        const float dw = dwp[jj * TM + row];
+        for (int u = 0; u < 2; u++) {
+            const int x = tid + TC_THREADS * u, r = x & (TM - 1), jj = x >> 7;
+            uint8_t* a = base + ST_A + jj * A_STEP + (r >> 3) * 256 + (r & 7) * 16;
+            uint4 lo, hi;   // element j < 16: low nibble of byte j; 16 + j: high nibble; both minus 8
+            lo.x = nib_minus8(ra[u].x);
+            lo.y = nib_minus8(ra[u].y);
+            lo.z = nib_minus8(ra[u].z);
+            lo.w = nib_minus8(ra[u].w);
+            hi.x = nib_minus8(ra[u].x >> 4);
+            hi.y = nib_minus8(ra[u].y >> 4);
+            hi.z = nib_minus8(ra[u].z >> 4);
+            hi.w = nib_minus8(ra[u].w >> 4);
+            *reinterpret_cast<uint4*>(a) = lo;
+            *reinterpret_cast<uint4*>(a + 128) = hi;
+            reinterpret_cast<float*>(base + ST_DW)[jj * TM + r] = rdw[u];
+        }
+        if (tid < TN * KG) {
+            const int tk = tid & (TN - 1), jj = tid >> 5;
+            uint8_t* bp = base + ST_B + jj * B_STEP + (tk >> 3) * 256 + (tk & 7) * 16;
+            *reinterpret_cast<uint4*>(bp) = rb0;
+            *reinterpret_cast<uint4*>(bp + 128) = rb1;
+            reinterpret_cast<float*>(base + ST_DX)[jj * TN + tk] = rdx;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    };
+    // MMAs of group f: operands in stage f % NSTAGE, accumulators in TMEM set f & 1
+    auto issue_group = [&](int f) {
+        const int gi = f % NG;
+        const uint8_t* base = smem + (size_t)(f % NSTAGE) * STAGE_BYTES;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int jj = 0; jj < KG && gi * KG + jj < nb; jj++) {
+            const uint64_t da = kmajor_desc(base + ST_A + jj * A_STEP);
+            const uint64_t db = kmajor_desc(base + ST_B + jj * B_STEP);
+            const uint32_t dt = tbase + (uint32_t)((f & 1) * KG * TN + jj * TN);
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(dt),
+                "l"(da), "l"(db), "r"(IDESC), "r"(0));
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         saddr(&mbar[f & 1]))
+                     : "memory");
+    };
+    auto try_group = [&](int f) -> bool {   // bounded wait for group f's commit
+        const uint32_t parity = ((f & 1) ? use1 : use0) & 1u;
+        const long long t_start = clock64();
+        while (true) {
+            uint32_t done;
+            asm volatile(
+                "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                "selp.u32 %0, 1, 0, p;\n\t}"
+                : "=r"(done)
+                : "r"(saddr(&mbar[f & 1])), "r"(parity)
+                : "memory");
+            if (done) return true;
+            if (clock64() - t_start > TC_WAIT_CYCLES) return false;
+        }
+    };
+
+    float leaf[8], st[8][6];
+    const float zero8[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    int next_cls = 0;   // class ordinal the stacks expect next (classes without blocks push 0)
+
+    load_group(0);
+    store_group(0);
+    if (F > 1) {
+        load_group(1);
+        store_group(1);
+    }
+    __syncthreads();
+    if (tid == 0) issue_group(0);
+    for (int f = 0; f < F; f++) {
+        const int i = f / NG, gi = f - i * NG;
+        if (tid == 0 && f + 1 < F) issue_group(f + 1);
+        if (f + 2 < F) load_group(f + 2);
+        if (gi == 0) {   // a new item: fresh chains and stacks
 #pragma unroll
-                        for (int t = 0; t < 8; t++) {
-                            const float term =
-                                __fmul_rn(__fmul_rn(__int2float_rn((int)cur[t]), dw), dxp[jj * TN + cg * 8 + t]);
-                            leaf[t] = __fadd_rn(leaf[t], term);
-                        }
-                        if (code >> 15) {
-                            push8(st, leaf, c);
+            for (int t = 0; t < 8; t++) {
+                leaf[t] = 0.0f;
 #pragma unroll
-                            for (int t = 0; t < 8; t++) leaf[t] = 0.0f;
-                            next_cls = c + 1;
-                        }
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                for (int q = 0; q < 6; q++) st[t][q] = 0.0f;
+            }
+            next_cls = 0;
+        }
+        const bool ok = try_group(f);
+        if (!ok) {
+            atomicExch(&s_fail, 1);
+            fail_f = f;
+        } else if (f & 1) {
+            use1++;
+        } else {
+            use0++;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok) {
+            const uint8_t* stage = smem + (size_t)(f % NSTAGE) * STAGE_BYTES;
+            const float* dwp = reinterpret_cast<const float*>(stage + ST_DW);
+            const float* dxp = reinterpret_cast<const float*>(stage + ST_DX);
+            const uint32_t tcol = tbase + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)((f & 1) * KG * TN + cg * 8);
+            const int nsteps = min(KG, nb - gi * KG);
+            uint32_t va[8], vb[8];
+            tmem_ld8(va, tcol);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int jj = 0; jj < KG; jj++) {
+                if (jj < nsteps) {
+                    uint32_t (&cur)[8] = (jj & 1) ? vb : va;
+                    uint32_t (&nxt)[8] = (jj & 1) ? va : vb;
+                    if (jj + 1 < nsteps) tmem_ld8(nxt, tcol + (uint32_t)((jj + 1) * TN));
+                    const int code = s_steps[gi * KG + jj];
+                    const int c = (code >> 10) & 31;
+                    for (; next_cls < c; next_cls++) push8(st, zero8, next_cls);
+                    const float dw = dwp[jj * TM + row];
+                    const float4 dxa = *reinterpret_cast<const float4*>(dxp + jj * TN + cg * 8);
+                    const float4 dxb = *reinterpret_cast<const float4*>(dxp + jj * TN + cg * 8 + 4);
+                    const float dx[8] = {dxa.x, dxa.y, dxa.z, dxa.w, dxb.x, dxb.y, dxb.z, dxb.w};
+#pragma unroll
+                    for (int t = 0; t < 8; t++)
+                        leaf[t] = __fadd_rn(leaf[t], __fmul_rn(__fmul_rn(__int2float_rn((int)cur[t]), dw), dx[t]));
+                    if (code >> 15) {
+                        push8(st, leaf, c);
+#pragma unroll
+                        for (int t = 0; t < 8; t++) leaf[t] = 0.0f;
+                        next_cls = c + 1;
                     }
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
             }
-            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-            if (gi + 2 < NG) store_group((gi + 2) % NSTAGE);
-            __syncthreads();
-            failed = s_fail != 0;
-            if (failed) break;
-        }
-        if (failed) break;
-        for (; next_cls < 32; next_cls++) push8(st, zero8, next_cls);
+            if (gi == NG - 1) {   // the item's last group: finish the trees, write the sums
+                for (; next_cls < 32; next_cls++) push8(st, zero8, next_cls);
+                const Item it = item(i);
+                float* out = it.mat == 1 ? P.out1 : P.out0;
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            const int tk = cg * 8 + t;
-            if (tk < nt) out[(size_t)s_pair[tk] * rows + r_base + row] = st[t][5];
+                for (int t = 0; t < 8; t++) {
+                    const int tk = cg * 8 + t;
+                    if (tk < it.nt) out[(size_t)s_pairs[i & (RING - 1)][tk] * rows + it.r_base + row] = st[t][5];
+                }
+            }
         }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        if (f + 2 < F) store_group((f + 2) % NSTAGE);
+        if (f + 3 < F && (f + 3) % NG == 0) fill_ring((f + 3) / NG);   // the token list of the item after
+        __syncthreads();
+        failed = s_fail != 0;
+        if (failed) break;
     }
     if (failed) {
         // drain (bounded) the MMAs still in flight, the failed group's and the one issued
         // after it, before the TMEM is freed
         const long long t_start = clock64();
-        for (int gi = fail_group; gi >= 0 && gi <= fail_group + 1 && gi < NG; gi++) {
-            const uint32_t parity = ((gi & 1) ? use1 : use0) & 1u;
+        for (int f = fail_f; f >= 0 && f <= fail_f + 1 && f < F; f++) {
+            const uint32_t parity = ((f & 1) ? use1 : use0) & 1u;
             while (clock64() - t_start < TC_WAIT_CYCLES) {
                 uint32_t done;
                 asm volatile(
                     "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
                     "selp.u32 %0, 1, 0, p;\n\t}"
                     : "=r"(done)
-                    : "r"(saddr(&mbar[gi & 1])), "r"(parity)
+                    : "r"(saddr(&mbar[f & 1])), "r"(parity)
                     : "memory");
                 if (done) break;
             }
@@ -386,11 +454,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
 }  // namespace
 
 bool q4_mma_supported(const Geom& g) { return g.I % TM == 0 && g.H % TM == 0; }
+int q4_mma_tile_tokens() { return TN; }
 
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
-                          const int* off, const int* list, const int* active, int n_act, int ks, const uint8_t* act,
-                          float* out0, float* out1, unsigned* err, cudaStream_t s) {
+                          const int* off, const int* list, const int* active, const int* tile_pre, int n_act, int ks,
+                          const uint8_t* act, float* out0, float* out1, unsigned* err, cudaStream_t s) {
     if (n_act <= 0) return cudaSuccess;
+    if (n_act > MAX_ACT) return cudaErrorInvalidValue;
     if (!q4_mma_supported(g)) return cudaErrorInvalidValue;
     TcParams P;
     P.layer = layer;
@@ -401,6 +471,7 @@ cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, in
     P.off = off;
     P.list = list;
     P.active = active;
+    P.tile_pre = tile_pre;
     P.ks = ks;
     P.down = down;
     P.act = act;
@@ -409,8 +480,10 @@ cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, in
     P.err = err;
     cudaError_t e = cudaFuncSetAttribute(k_q4_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     if (e != cudaSuccess) return e;
-    const int gx = down ? g.H / TM : 2 * (g.I / TM);
-    k_q4_mma<<<dim3(gx, n_act), TC_THREADS, TC_SMEM, s>>>(P);
+    int dev = 0, sms = 0;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    k_q4_mma<<<sms, TC_THREADS, TC_SMEM, s>>>(P);   // persistent: one CTA per SM
     return cudaGetLastError();
 }
 
