@@ -33,22 +33,32 @@ namespace {
 
 constexpr int RT_TOK = 4;         // tokens per router CTA
 constexpr int DOWN_ROWS = 16;     // output rows per down CTA (2 per warp)
-constexpr int DOWN_TOK = 16;      // tokens per pass of the down CTA (2 rows x 16 tokens = 32 sums)
+// tokens per pass of the batched dp4a kernels: wide tiles (gate/up 8 or 16, down 16) when
+// experts average >= 8 pairs, narrow ones (2 or 4, 4) below, which keep more CTAs per SM
+constexpr int WIDE_MIN_PAIRS = 8;
 
-// Sum each of 32 per-lane values over the warp with the same pairing tree as 32
-// separate xor butterflies (so the same bits), in 31 shuffles: at offsets 16, 8, 4, 2, 1
-// each lane hands half of its remaining values to its partner and keeps the other half
-// (the upper half when the lane has that offset's bit).  Value j ends in lane j.
-__device__ __forceinline__ float warp_sum32_transposed(float (&v)[32], int lane) {
+// Sum each of N (8, 16 or 32) per-lane values over the warp with the same pairing tree
+// as N separate xor butterflies (so the same bits): at offsets 16, 8, ... each lane hands
+// half of its remaining values to its partner and keeps the other half (the upper half
+// when the lane has that offset's bit) until one value is left, then plain butterflies.
+// Value j ends in lanes j * (32 / N) .. j * (32 / N) + 32 / N - 1.
+template <int N>
+__device__ __forceinline__ float warp_sum_transposed(float (&v)[N], int lane) {
     __syncwarp();
 #pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-        const bool up = lane & o;
+    for (int lvl = 0; lvl < 5; lvl++) {
+        const int o = 16 >> lvl;          // offset of this level
+        const int h = (N >> lvl) / 2;     // values handed over (0: one value left)
+        if (h > 0) {
+            const bool up = lane & o;
 #pragma unroll
-        for (int i = 0; i < o; i++) {
-            const float send = up ? v[i] : v[i + o];
-            const float keep = up ? v[i + o] : v[i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+            for (int i = 0; i < h; i++) {
+                const float send = up ? v[i] : v[i + h];
+                const float keep = up ? v[i + h] : v[i];
+                v[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+            }
+        } else {
+            v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], o));
         }
     }
     return v[0];
@@ -221,7 +231,7 @@ __device__ __forceinline__ const uint8_t* expert_base(const uint8_t* layer, cons
 // the gate and up sums of (row l / P, token l % P).  With R = 32 the unit is one Q8_0
 // block of h: warp w quantises token w's 32 values into hq[p]; with R = 16 h goes to
 // hf[p] for k_quant_h.  Per (row, token) the arithmetic is exactly the single-token one.
-template <int R>
+template <int R, int P>
 __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer,
                                                         const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                         const int* __restrict__ off, const int* __restrict__ list,
@@ -229,7 +239,8 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
                                                         const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq,
                                                         float* __restrict__ hf) {
     constexpr int RW = R / 8;        // rows per warp
-    constexpr int P = 32 / RW;       // tokens per tile
+    constexpr int NV = RW * P;       // sums per lane and matrix: 8 or 32
+    constexpr int LPV = 32 / NV;     // lanes holding each reduced sum
     extern __shared__ __align__(16) uint8_t smem[];   // gate rows | up rows
     __shared__ float sh[P][32];      // h of the tile (R = 32)
     __shared__ int sp[P];            // the tile's pairs
@@ -259,9 +270,9 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
         __syncthreads();   // the previous tile's sh / sp are consumed (and, first time, the weights staged)
         if (threadIdx.x < P) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
         __syncthreads();
-        float ag[32], au[32];   // [row r][token t] at r * P + t
+        float ag[NV], au[NV];   // [row r][token t] at r * P + t
 #pragma unroll
-        for (int i = 0; i < 32; i++) ag[i] = au[i] = 0.0f;
+        for (int i = 0; i < NV; i++) ag[i] = au[i] = 0.0f;
         for (int b = lane; b < nb; b += 32) {
             uint4 wg[RW], wu[RW];
             float dg[RW], du[RW];
@@ -287,10 +298,10 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
                 }
             }
         }
-        const float gv = warp_sum32_transposed(ag, lane);
-        const float uv = warp_sum32_transposed(au, lane);
-        const int r = lane / P, t = lane % P;
-        if (t < nt) {
+        const float gv = warp_sum_transposed<NV>(ag, lane);
+        const float uv = warp_sum_transposed<NV>(au, lane);
+        const int j = lane / LPV, r = j / P, t = j % P;
+        if (lane % LPV == 0 && t < nt) {
             const float hv = silu_mul(gv, uv);
             if (R == 32)
                 sh[t][i0 + r] = hv;
@@ -336,13 +347,16 @@ __global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, c
 // tiles of 16 tokens: each lane runs the lane-strided block chains of its warp's 2 rows
 // for every token of the tile, and one transposed reduction leaves lane l with the sum of
 // (row l / 16, token l % 16): y[p][r] = row . hq[p], exactly the single-token arithmetic.
+template <int DT>
 __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict__ layer,
                                                       const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                       const int* __restrict__ off, const int* __restrict__ list,
                                                       const int* __restrict__ active, const uint8_t* __restrict__ hq,
                                                       float* __restrict__ y) {
+    constexpr int NV = 2 * DT;       // sums per lane: 2 rows x DT tokens
+    constexpr int LPV = 32 / NV;
     extern __shared__ __align__(16) uint8_t smem[];   // DOWN_ROWS rows
-    __shared__ int sp[DOWN_TOK];
+    __shared__ int sp[DT];
     if ((int)blockIdx.y >= active[0]) return;
     const int e = active[1 + blockIdx.y], rb = blockIdx.x;
     const int p0 = off[e], n = off[e + 1] - p0;
@@ -360,15 +374,15 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
     const int nb = g.nbI;
     const size_t abh = act_bytes(nb);
     const int lr0 = warp * 2;
-    for (int q0 = 0; q0 < n; q0 += DOWN_TOK) {
-        const int nt = min(DOWN_TOK, n - q0);
+    for (int q0 = 0; q0 < n; q0 += DT) {
+        const int nt = min(DT, n - q0);
         __syncthreads();
-        if (threadIdx.x < DOWN_TOK) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
+        if (threadIdx.x < DT) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
         __syncthreads();
         if (lr0 >= nrows) continue;
-        float acc[32];   // [row r][token t] at r * 16 + t
+        float acc[NV];   // [row r][token t] at r * DT + t
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+        for (int i = 0; i < NV; i++) acc[i] = 0.0f;
         for (int b = lane; b < nb; b += 32) {
             uint4 wv[2];
             float dw[2];
@@ -379,19 +393,18 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
                 dw[r] = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * (size_t)nb + 2 * b));
             }
 #pragma unroll
-            for (int t = 0; t < DOWN_TOK; t++) {
+            for (int t = 0; t < DT; t++) {
                 if (t < nt) {
                     const XBlk xb = load_xblk(act_view(hq + (size_t)sp[t] * abh, nb), b);
 #pragma unroll
                     for (int r = 0; r < 2; r++)
-                        acc[r * DOWN_TOK + t] = __fadd_rn(acc[r * DOWN_TOK + t],
-                                                          block_term(block_sumi(wv[r], xb), dw[r], xb.d));
+                        acc[r * DT + t] = __fadd_rn(acc[r * DT + t], block_term(block_sumi(wv[r], xb), dw[r], xb.d));
                 }
             }
         }
-        const float yv = warp_sum32_transposed(acc, lane);
-        const int r = lane / DOWN_TOK, t = lane % DOWN_TOK;
-        if (t < nt && lr0 + r < nrows) y[(size_t)sp[t] * g.H + r0 + lr0 + r] = yv;
+        const float yv = warp_sum_transposed<NV>(acc, lane);
+        const int j = lane / LPV, r = j / DT, t = j % DT;
+        if (lane % LPV == 0 && t < nt && lr0 + r < nrows) y[(size_t)sp[t] * g.H + r0 + lr0 + r] = yv;
     }
 }
 
@@ -498,32 +511,37 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                              s);
     }
     const int R_gu = gu_rows(g, (size_t)optin);
+    const bool wide = n_pairs >= (size_t)WIDE_MIN_PAIRS * (E + n_shared);
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
-    if (R_gu == 32) {
-        if (sm_gu > 48 * 1024 && (e = cudaFuncSetAttribute(k_gateup_batched<32>,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
-                                     cudaSuccess)
-            return e;
-        k_gateup_batched<32><<<dim3(g.I / 32, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active,
-                                                                        ks, xq, hq, hf);
-    } else {
-        if (sm_gu > 48 * 1024 && (e = cudaFuncSetAttribute(k_gateup_batched<16>,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) !=
-                                     cudaSuccess)
-            return e;
-        k_gateup_batched<16><<<dim3(g.I / 16, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active,
-                                                                        ks, xq, hq, hf);
+    auto gateup = [&](auto kern, int rows_per_cta) -> cudaError_t {
+        cudaError_t r;
+        if (sm_gu > 48 * 1024 &&
+            (r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) != cudaSuccess)
+            return r;
+        kern<<<dim3(g.I / rows_per_cta, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active, ks, xq,
+                                                                 hq, hf);
+        return cudaGetLastError();
+    };
+    if (R_gu == 32)
+        e = wide ? gateup(k_gateup_batched<32, 8>, 32) : gateup(k_gateup_batched<32, 2>, 32);
+    else
+        e = wide ? gateup(k_gateup_batched<16, 16>, 16) : gateup(k_gateup_batched<16, 4>, 16);
+    if (e != cudaSuccess) return e;
+    if (R_gu == 16) {
         const long long warps = (long long)n_pairs * g.nbI;
         k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, nullptr, (int)n_pairs, g, hq);
     }
     const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
-    if (sm_d > 48 * 1024 &&
-        (e = cudaFuncSetAttribute(k_down_batched, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_d)) !=
-            cudaSuccess)
-        return e;
-    k_down_batched<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, shared, E, e_lo, g, off,
-                                                                                      list, active, hq, y);
-    return cudaGetLastError();
+    auto down = [&](auto kern) -> cudaError_t {
+        cudaError_t r;
+        if (sm_d > 48 * 1024 &&
+            (r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_d)) != cudaSuccess)
+            return r;
+        kern<<<dim3((g.H + DOWN_ROWS - 1) / DOWN_ROWS, n_act), 256, sm_d, s>>>(layer, shared, E, e_lo, g, off, list,
+                                                                              active, hq, y);
+        return cudaGetLastError();
+    };
+    return wide ? down(k_down_batched<16>) : down(k_down_batched<4>);
 }
 
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
