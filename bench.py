@@ -78,6 +78,10 @@ def parse():
     ap.add_argument("--shape", choices=["qwen3", "dsv3"], default="qwen3",
                     help="with --ep: qwen3 (configs[2]) or the DeepSeek-V3-like configs[4] (hidden 7168, "
                          "inter 2048, 256 routed + 1 shared expert, 58 layers, as many as fit per GPU)")
+    ap.add_argument("--attention", action="store_true",
+                    help="whole decode layers: the reference's attention step (Q4_K / f16 weights, fp32 KV cache) "
+                         "then the MoE block, 48 layers per token in one CUDA graph")
+    ap.add_argument("--pos", type=int, default=1024, help="--attention: rows already cached when timing starts")
     ap.add_argument("--format", choices=["q4_0", "q4_k", "q4_k_m"], default="q4_0",
                     help="q4_k / q4_k_m: the reference library's own formats (all-Q4_K experts, or Q4_K "
                          "gate/up with Q6_K down), expert FFN of 48 layers x top-8 per token")
@@ -728,6 +732,149 @@ def run_kquant(args):
     return 0
 
 
+def run_layers(args):
+    """Whole decode layers at the Qwen3-30B-A3B shape, as the reference engine runs them
+    (tinygiant/engine.py:199-258): x += attention(RMSNorm(x)) by the tg_attention_decode_q4
+    step (Q4_K wq / wk / wo, f16 wv, fp32 KV cache, 32 query / 4 kv heads of 128), then the
+    MoE block (router, top-8, Q4_0 experts), for 48 layers; one CUDA graph per token, the
+    cache position read on the device.  Every step is a new token at the next position."""
+    import torch
+    from tinygiant_b200.engine import AttentionModel, MoEModel
+    from tinygiant_b200 import _constants as C
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = init_dist(ws, "nccl") if ws > 1 else None
+    NL, K, W, P0 = args.layers, args.steps, max(3, args.warmup), args.pos
+    kv_max = P0 + K + W + 2
+    NH, NKV, HD = C.N_HEADS, C.N_KV_HEADS, C.HEAD_DIM
+    moe = MoEModel(H, I, E, K_TOP, NL, device=local)
+    moe.fill_synthetic(args.seed + 7919 * rank)
+    am = AttentionModel(H, NH, NKV, HD, NL, kv_max=kv_max, q4=True, device=local)
+    am.fill_synthetic(args.seed + 31 + 7919 * rank)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed + rank)
+    X = torch.randn(K + W, H, generator=gen, device="cuda", dtype=torch.float32)
+    x = torch.empty(H, device="cuda", dtype=torch.float32)
+    s = torch.cuda.current_stream()
+    am.reset(P0)
+    for i in range(W):
+        x.copy_(X[i])
+        am.decode_token(x, moe, s)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev0.record(s)
+    for i in range(K):
+        x.copy_(X[W + i])
+        ks[i].record(s)
+        am.decode_token(x, moe, s)
+        ke[i].record(s)
+    ev1.record(s)
+    torch.cuda.synchronize()
+    clocks.stop()
+    assert am.status() == P0 + W + K
+    moe.sync_status()
+    assert torch.isfinite(x).all()
+    ms = ev0.elapsed_time(ev1)
+    tok_ms = float(np.mean([a.elapsed_time(b) for a, b in zip(ks, ke)]))
+    # e2e: pinned host token in, hidden state out, every step, from the same position
+    Xh = X.cpu().pin_memory()
+    Yh = torch.empty_like(Xh).pin_memory()
+    am.reset(P0 + W)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(K):
+        x.copy_(Xh[W + i], non_blocking=True)
+        am.decode_token(x, moe, s)
+        Yh[W + i].copy_(x, non_blocking=True)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ems = e0.elapsed_time(e1)
+    am.status()
+    if dist:
+        t = torch.tensor([ms, ems, tok_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ems, tok_ms = float(t[0]), float(t[1]), float(t[2])
+
+    wq, wk, wv, wo = am.matrix_bytes()
+    attn_w = wq + wk + wv + wo
+    seq_mean = P0 + W + (K + 1) / 2.0                       # rows attended, averaged over the timed tokens
+    kv_read = 2 * NKV * HD * 4 * seq_mean
+    alg = NL * (attn_w + kv_read + K_TOP * EXPERT_BYTES)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        rng = np.random.default_rng(args.seed)
+        qd, kvd = NH * HD, NKV * HD
+
+        def q4k(nbytes):
+            b = rng.integers(0, 256, size=(nbytes // 144, 144), dtype=np.uint8)
+            b[:, 0:4] = np.asarray(rng.uniform(5e-5, 1.5e-4, (b.shape[0], 2)), np.float16).view(np.uint8)
+            return b.ravel()
+
+        Wh = (q4k(wq), q4k(wk), (rng.standard_normal(kvd * H) * 0.02).astype(np.float16).view(np.uint16), q4k(wo))
+        ones = np.ones(HD, np.float32)
+        seq = int(seq_mean)
+        kk = np.zeros((NKV, seq + 1, HD), np.float32)
+        vv = np.zeros((NKV, seq + 1, HD), np.float32)
+        cos, sin = np.ones((1, HD // 2), np.float32), np.zeros((1, HD // 2), np.float32)
+        blob = moe.read_experts(0, 0, E)
+        R = (rng.standard_normal((E, H)) * 0.02).astype(np.float32)
+        xs = X[0].cpu().numpy()
+        t0, n_layers = time.perf_counter(), 0
+        while True:
+            nrm = O.rms_norm_k(xs, np.ones(H, np.float32), 1e-6)
+            out = O.attention_decode(True, *Wh, ones, ones, kk, vv, seq, cos, sin, nrm, H, NH, NKV, HD, 0)
+            xs = O.moe_block(blob, R, (xs + out).astype(np.float32), K_TOP, H, I)[0]
+            n_layers += 1
+            el = time.perf_counter() - t0
+            if el >= min(args.cpu_seconds, 10.0) or n_layers >= 200:
+                break
+        cpu = {"value": n_layers / el / NL, "unit": "tok/s", "cores": 1, "kind": "port",
+               "sample": f"{n_layers} whole layers (attention at {seq} cached rows + MoE block), {el:.1f} s, "
+                         f"oracle C port single-threaded, scaled by {NL} layers per token"}
+    peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = alg / (tok_ms / 1000.0) / 1e9
+    if rank == 0:
+        emit({
+            "metric": "decode tok/s, whole layers (attention + MoE, Qwen3-30B-A3B shape)",
+            "value": ws * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{NL} decode layers per token: attention (Q4_K / f16, fp32 KV cache, "
+                                   f"positions {P0 + W}..{P0 + W + K - 1}) then the MoE block (top-{K_TOP} of {E} "
+                                   f"Q4_0 experts)", "hidden": H, "inter": I, "experts": E, "layers": NL,
+                       "heads": NH, "kv_heads": NKV, "head_dim": HD, "kv_max": kv_max,
+                       "l2": f"inputs larger than L2 ({alg / 1e9:.2f} GB read per token)",
+                       "parallelism": "replicas" if ws > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "kernel": f"token graph: {NL} x (RMSNorm, 7 attention kernels, fused MoE "
+                                                    f"layer) + position advance", "token_ms": tok_ms,
+                         "algorithmic_bytes": alg,
+                         "algorithmic_bytes_def": "per layer: Q4_K/f16 attention weights + K and V rows read "
+                                                  "(mean position) + Q4_0 bytes of the 8 experts",
+                         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": ws * K / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": H * 4,
+                    "d2h_bytes_per_step": H * 4},
+            "gpu_launches": (9 * NL + 1) * K,
+            "clocks": clocks.summary(),
+        })
+    am.close()
+    moe.close()
+    if dist:
+        dist.destroy_process_group()
+    return 0
+
+
 def run_ep(args):
     """Expert parallelism (configs 3 / 5 at the Qwen3 shape): rank r holds experts
     [r*E/N, (r+1)*E/N) of all 48 layers; every rank routes the same T tokens, runs its
@@ -885,6 +1032,8 @@ def main():
         return run_reference(args)
     if args.ep:
         return run_ep(args)
+    if args.attention:
+        return run_layers(args)
     if args.format != "q4_0":
         return run_kquant(args)
     if args.tier >= 0:

@@ -100,6 +100,25 @@ int tg_f32_matvec(const float *A, const float *x, float *out, int nrows, int nco
 /* out = x * scale * weight, scale = 1/sqrtf(sum x^2 / dim + eps) with the sum as four
  * fused chains folded pairwise, csrc/libtinygiant.c:322-340 (_lib.py:44); dim % 4 == 0. */
 int tg_rms_norm(const float *x, const float *weight, float *out, int dim, float eps);
+/* GQA attention decode of one token, csrc/libtinygiant.c:364-456 (tg_attention_decode,
+ * fp32 wq [n_heads*head_dim][embed], wk / wv [n_kv*head_dim][embed], wo
+ * [embed][n_heads*head_dim]) and :460-551 (tg_attention_decode_q4: the same matrices
+ * with Q4_K wq / wk / wo and f16 wv); called by engine.py:205-226.  q, k, v
+ * projections; per-head RMSNorm (eps 1e-6) of q and k; RoPE with the rows of `pos` of
+ * rope_cos / rope_sin [positions][head_dim/2]; k and v written to row kv_len of the
+ * caches kv_k / kv_v [n_kv][kv_max][head_dim]; query head h attends over kv head
+ * h / (n_heads/n_kv), rows 0 .. kv_len; output[embed] = wo . attention (written, not
+ * added).  head_dim % 8 == 0 and <= 256; n_heads / n_kv_heads <= 32; Q4_K needs embed
+ * and n_heads*head_dim to be multiples of 256. */
+int tg_attention_decode(const float *wq, const float *wk, const float *wv, const float *wo,
+                        const float *q_norm_w, const float *k_norm_w, float *kv_k, float *kv_v, int kv_len,
+                        int kv_max, const float *rope_cos, const float *rope_sin, const float *input, float *output,
+                        int embed_dim, int n_heads, int n_kv_heads, int head_dim, int pos);
+int tg_attention_decode_q4(const uint8_t *wq_q4, const uint8_t *wk_q4, const uint16_t *wv_f16,
+                           const uint8_t *wo_q4, const float *q_norm_w, const float *k_norm_w, float *kv_k,
+                           float *kv_v, int kv_len, int kv_max, const float *rope_cos, const float *rope_sin,
+                           const float *input, float *output, int embed_dim, int n_heads, int n_kv_heads,
+                           int head_dim, int pos);
 /* output += weight * expert(input) of one all-Q4_K blob gate | up | down,
  * csrc/libtinygiant.c:555-595 (_lib.py:39). */
 int tg_expert_forward(const uint8_t *q4_data, const float *input, float *output, float weight,
@@ -345,6 +364,61 @@ int tgx_kq_experts_forward(const void *const *gate_dev, const void *const *up_de
                            int down_format, int n, const float *w_dev, const float *x_dev, float *out_dev,
                            int embed, int inter, int accumulate, void *scratch, size_t scratch_bytes, int flags,
                            void *stream);
+
+/* tg_attention_decode (q4 = 0) / tg_attention_decode_q4 (q4 = 1) on device memory:
+ * every pointer is a device pointer (16-byte aligned), the caches [n_kv][kv_max][head_dim]
+ * stay resident, `output` is written.  scratch: tgx_attention_scratch_bytes(n_heads,
+ * n_kv_heads, head_dim, kv_max) bytes.  Seven kernel launches on `stream` (three
+ * projections, norm + RoPE + append, scores, softmax + V, output projection); allocates
+ * nothing.  kv_max <= 32768. */
+size_t tgx_attention_scratch_bytes(int n_heads, int n_kv_heads, int head_dim, int kv_max);
+int tgx_attention_decode(int q4, const void *wq, const void *wk, const void *wv, const void *wo,
+                         const float *q_norm_w, const float *k_norm_w, float *kv_k, float *kv_v, int kv_len,
+                         int kv_max, const float *rope_cos, const float *rope_sin, const float *input, float *output,
+                         int embed_dim, int n_heads, int n_kv_heads, int head_dim, int pos, void *scratch,
+                         size_t scratch_bytes, void *stream);
+
+/* ===================== device-resident attention and the whole decode layer ===================== */
+
+/* The attention half of a decode layer for an n_layers model (engine.py:199-226,
+ * tinygiant/engine.py's _forward_c): per layer wq, wk, wv, wo (q4: Q4_K / f16 as in
+ * tg_attention_decode_q4, else fp32), the q / k norm weights and the attention RMSNorm
+ * weight; rope tables [kv_max][head_dim/2] (default: base 1e6, evaluated in double);
+ * KV caches [n_layers][2][n_kv][kv_max][head_dim] fp32 (zero at creation); and a
+ * device position word = rows already cached, 0 at creation. */
+typedef struct tgx_attn tgx_attn;
+int tgx_attn_create(int device, int q4, int n_layers, int embed_dim, int n_heads, int n_kv_heads, int head_dim,
+                    int kv_max, float eps, tgx_attn **out);
+int tgx_attn_destroy(tgx_attn *a);
+/* Device bytes of one layer's four matrices (each in a 256-byte aligned slot). */
+size_t tgx_attn_layer_bytes(const tgx_attn *a);
+/* Copy one layer's weights in; any pointer may be NULL to keep that part. */
+int tgx_attn_set_layer(tgx_attn *a, int layer, const void *wq, const void *wk, const void *wv, const void *wo,
+                       const float *q_norm_w, const float *k_norm_w, const float *attn_norm_w, int src_on_device);
+/* Replace the rope tables with the first kv_max rows of cos / sin [n_pos][head_dim/2]
+ * (the reference's build_rope_cache). */
+int tgx_attn_set_rope(tgx_attn *a, const float *rope_cos, const float *rope_sin, int n_pos, int src_on_device);
+/* Set the position (rows cached; 0 starts a new sequence, engine.py:145-148).  Synchronises. */
+int tgx_attn_set_pos(tgx_attn *a, int pos);
+/* Synchronise, report the device position, and TG_EINVAL if a step ran at a position
+ * outside the cache since the last call (such a step writes nothing). */
+int tgx_attn_status(tgx_attn *a, int *pos);
+/* Device pointers of layer `layer`'s caches [n_kv][kv_max][head_dim]. */
+int tgx_attn_kv(tgx_attn *a, int layer, float **kv_k_dev, float **kv_v_dev);
+/* Synchronise and copy layer `layer`'s caches [n_kv][kv_max][head_dim] to host memory
+ * (either pointer may be NULL). */
+int tgx_attn_read_kv(tgx_attn *a, int layer, float *kv_k_host, float *kv_v_host);
+/* x_dev[embed] += attention(RMSNorm(x) * attn_norm) of layer `layer` at the device
+ * position (engine.py:203-226): tg_rms_norm then the tg_attention_decode step with
+ * kv_len = pos; the position does not move. */
+int tgx_attn_layer(tgx_attn *a, int layer, float *x_dev, void *stream);
+/* pos += 1 on the device (after the last layer of a token). */
+int tgx_attn_advance(tgx_attn *a, void *stream);
+/* One decode token through every layer: x += attention_l(x), then the MoE block of
+ * layer l (tgx_moe_layer on `moe`; NULL: attention only), for l = 0 .. n_layers - 1,
+ * then pos += 1.  Replayed from a CUDA graph captured on first use for this x_dev and
+ * moe (flags TGX_EAGER: launched directly).  TG_EINVAL once the cache is full. */
+int tgx_decode_token(tgx_attn *a, tgx_ctx *moe, float *x_dev, void *stream, int flags);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,9 @@ def lib():
         "ref_matvec_k": (None, [VP, CI, VP, VP, CI, CI]),
         "ref_rms_norm_k": (None, [VP, VP, VP, CI, CF]),
         "ref_expert_forward_k": (None, [VP, VP, VP, CI, VP, VP, CF, CI, CI, CI]),
+        "ref_rope": (None, [VP, CI, CI, VP, VP]),
+        "ref_attention_decode": (None, [CI, VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP,
+                                        CI, CI, CI, CI, CI, CI]),
         "ref_fill_normal": (None, [VP, I64, ctypes.c_uint64, CF]),
     }
     for name, (res, args) in sig.items():
@@ -317,6 +320,34 @@ def expert_forward_k(gate, up, down, down_format, x, out, w, embed, inter, mode=
     lib().ref_expert_forward_k(_p(np.ascontiguousarray(gate)), _p(np.ascontiguousarray(up)),
                                _p(np.ascontiguousarray(down)), down_format, _p(x), _p(out), float(w),
                                embed, inter, mode)
+    return out
+
+
+def rope(x, cos_row, sin_row, n_heads, head_dim):
+    """apply_rope_inplace (libtinygiant.c:344-360) on a copy of x[n_heads * head_dim]."""
+    x = np.array(x, dtype=np.float32, copy=True)
+    lib().ref_rope(_p(x), n_heads, head_dim, _p(np.ascontiguousarray(cos_row, np.float32)),
+                   _p(np.ascontiguousarray(sin_row, np.float32)))
+    return x
+
+
+def attention_decode(q4, wq, wk, wv, wo, q_norm_w, k_norm_w, kv_k, kv_v, kv_len, rope_cos, rope_sin, x,
+                     embed, n_heads, n_kv, head_dim, pos, mode=TG_MIRROR):
+    """tg_attention_decode (q4 False: fp32 weights) / tg_attention_decode_q4 (q4 True: Q4_K
+    wq / wk / wo bytes, f16 wv), libtinygiant.c:364-551.  kv_k / kv_v [n_kv][kv_max][head_dim]
+    are updated in place (row kv_len); returns the output [embed]."""
+    assert kv_k.dtype == np.float32 and kv_k.flags.c_contiguous and kv_v.flags.c_contiguous
+    kv_max = kv_k.shape[1]
+    out = np.empty(embed, np.float32)
+    arrs = [np.ascontiguousarray(a) for a in (wq, wk, wv, wo)]
+    qn = np.ascontiguousarray(q_norm_w, np.float32)
+    kn = np.ascontiguousarray(k_norm_w, np.float32)
+    rc = np.ascontiguousarray(rope_cos, np.float32)
+    rs = np.ascontiguousarray(rope_sin, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    lib().ref_attention_decode(int(bool(q4)), *[_p(a) for a in arrs], _p(qn), _p(kn), _p(kv_k), _p(kv_v),
+                               kv_len, kv_max, _p(rc), _p(rs), _p(x), _p(out), embed, n_heads, n_kv, head_dim,
+                               pos, mode)
     return out
 
 

@@ -775,6 +775,98 @@ void ref_moe_block_batched(const uint8_t *layer_blob, size_t expert_bytes, const
                       mode, NULL, NULL, NULL);
 }
 
+/* ------------------------------------------------------------------ attention decode
+ *
+ * The reference's GQA attention step for one token (csrc/libtinygiant.c:344-551),
+ * statement by statement, every float operation rounded on its own except the
+ * source's fused multiply-adds (vfmaq_f32). */
+
+/* apply_rope_inplace, libtinygiant.c:344-360: for each head and i < head_dim / 2, with
+ * x1 = x[i], x2 = x[i + half], c = cos[i], s = sin[i] (the rows of position pos):
+ *   x[i]        = x1*c - x2*s       (vmlsq_f32: multiply, multiply, subtract)
+ *   x[i + half] = fma(x1, s, x2*c)  (vfmaq_f32 on vmulq_f32) */
+void ref_rope(float *x, int n_heads, int head_dim, const float *c, const float *s) {
+    int half = head_dim / 2;
+    for (int h = 0; h < n_heads; h++) {
+        float *xh = x + (size_t)h * head_dim;
+        for (int i = 0; i < half; i++) {
+            float x1 = xh[i], x2 = xh[half + i];
+            float a = x1 * c[i], b = x2 * s[i];
+            xh[i] = a - b;
+            xh[half + i] = fmaf(x1, s[i], x2 * c[i]);
+        }
+    }
+}
+
+/* One head's attention over seq cached rows (libtinygiant.c:406-453 / 498-547):
+ * score_t = dot(q, k_t) * (1 / sqrtf(head_dim)), the dot as four fused chains (chain v
+ * over d = v, v + 4, ...) added pairwise; softmax with the running max from -1e30, the
+ * exps summed in t order; out[d] = fused sum over t of (e_t * inv_sum) * v_t[d]. */
+static void attend_head(const float *q, const float *kc, const float *vc, int seq, int hd, float *out, float *sc,
+                        int mode) {
+    float inv_sqrt = 1.f / sqrtf((float)hd);
+    float mx = -1e30f;
+    for (int t = 0; t < seq; t++) {
+        const float *kt = kc + (size_t)t * hd;
+        float acc[4] = {0, 0, 0, 0};
+        for (int d = 0; d + 3 < hd; d += 4)
+            for (int v = 0; v < 4; v++) acc[v] = fmaf(q[d + v], kt[d + v], acc[v]);
+        float dot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+        sc[t] = dot * inv_sqrt;
+        if (sc[t] > mx) mx = sc[t];
+    }
+    float sum = 0.f;
+    for (int t = 0; t < seq; t++) {
+        float a = sc[t] - mx;
+        sc[t] = mode == TG_REF_ORDER ? expf(a) : ref_expf(a);
+        sum += sc[t];
+    }
+    float inv = 1.f / sum;
+    for (int d = 0; d < hd; d++) out[d] = 0.f;
+    for (int t = 0; t < seq; t++) {
+        float w = sc[t] * inv;
+        const float *vt = vc + (size_t)t * hd;
+        for (int d = 0; d < hd; d++) out[d] = fmaf(w, vt[d], out[d]);
+    }
+}
+
+/* tg_attention_decode (libtinygiant.c:364-456, q4 = 0: wq, wk, wv, wo fp32) and
+ * tg_attention_decode_q4 (:460-551, q4 = 1: wq, wk, wo Q4_K on Q8(256) of their input,
+ * wv f16).  q = Wq.in, k = Wk.in, v = Wv.in; per-head RMSNorm (eps 1e-6) of q and k
+ * with q_norm_w / k_norm_w; RoPE at pos; k and v appended to the caches
+ * [n_kv][kv_max][head_dim] at row kv_len; GQA attention of query head h over kv head
+ * h / (n_heads / n_kv) for rows 0..kv_len; output = Wo.attn (written, not added). */
+void ref_attention_decode(int q4, const void *wq, const void *wk, const void *wv, const void *wo,
+                          const float *q_norm_w, const float *k_norm_w, float *kv_k, float *kv_v, int kv_len,
+                          int kv_max, const float *rope_cos, const float *rope_sin, const float *input,
+                          float *output, int embed, int n_heads, int n_kv, int head_dim, int pos, int mode) {
+    int qd = n_heads * head_dim, kvd = n_kv * head_dim, ratio = n_heads / n_kv, half = head_dim / 2;
+    int seq = kv_len + 1;
+    float *q = malloc(sizeof(float) * qd), *k = malloc(sizeof(float) * kvd), *v = malloc(sizeof(float) * kvd);
+    float *qn = malloc(sizeof(float) * qd), *kn = malloc(sizeof(float) * kvd), *att = malloc(sizeof(float) * qd);
+    float *sc = malloc(sizeof(float) * seq);
+    ref_matvec_k(wq, q4 ? 0 : 4, input, q, qd, embed);
+    ref_matvec_k(wk, q4 ? 0 : 4, input, k, kvd, embed);
+    ref_matvec_k(wv, q4 ? 1 : 4, input, v, kvd, embed);
+    for (int h = 0; h < n_heads; h++)
+        ref_rms_norm_k(q + (size_t)h * head_dim, q_norm_w, qn + (size_t)h * head_dim, head_dim, 1e-6f);
+    for (int h = 0; h < n_kv; h++)
+        ref_rms_norm_k(k + (size_t)h * head_dim, k_norm_w, kn + (size_t)h * head_dim, head_dim, 1e-6f);
+    ref_rope(qn, n_heads, head_dim, rope_cos + (size_t)pos * half, rope_sin + (size_t)pos * half);
+    ref_rope(kn, n_kv, head_dim, rope_cos + (size_t)pos * half, rope_sin + (size_t)pos * half);
+    for (int h = 0; h < n_kv; h++) {
+        memcpy(kv_k + ((size_t)h * kv_max + kv_len) * head_dim, kn + (size_t)h * head_dim, sizeof(float) * head_dim);
+        memcpy(kv_v + ((size_t)h * kv_max + kv_len) * head_dim, v + (size_t)h * head_dim, sizeof(float) * head_dim);
+    }
+    for (int h = 0; h < n_heads; h++) {
+        int kvh = h / ratio;
+        attend_head(qn + (size_t)h * head_dim, kv_k + (size_t)kvh * kv_max * head_dim,
+                    kv_v + (size_t)kvh * kv_max * head_dim, seq, head_dim, att + (size_t)h * head_dim, sc, mode);
+    }
+    ref_matvec_k(wo, q4 ? 0 : 4, att, output, embed, qd);
+    free(q); free(k); free(v); free(qn); free(kn); free(att); free(sc);
+}
+
 /* ------------------------------------------------------------------ data */
 
 static inline uint64_t splitmix64(uint64_t *s) {

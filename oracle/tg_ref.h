@@ -115,6 +115,15 @@ void ref_decode_step_mt(const uint8_t *const *layer_blobs, const float *const *r
                         const float *const *norms, float eps, int n_layers, float *x, int n_experts, int k,
                         int embed, int inter, int mode, int n_threads);
 
+/* Attention decode of one token (csrc/libtinygiant.c:344-551): q4 = 0 all-fp32 weights
+ * (tg_attention_decode), q4 = 1 Q4_K wq/wk/wo and f16 wv (tg_attention_decode_q4).
+ * Appends k, v at row kv_len of the caches [n_kv][kv_max][head_dim]; writes output. */
+void ref_rope(float *x, int n_heads, int head_dim, const float *cos_row, const float *sin_row);
+void ref_attention_decode(int q4, const void *wq, const void *wk, const void *wv, const void *wo,
+                          const float *q_norm_w, const float *k_norm_w, float *kv_k, float *kv_v, int kv_len,
+                          int kv_max, const float *rope_cos, const float *rope_sin, const float *input,
+                          float *output, int embed, int n_heads, int n_kv, int head_dim, int pos, int mode);
+
 /* Seeded synthetic data: splitmix64 stream -> N(0, sigma) floats (Box-Muller). */
 void ref_fill_normal(float *out, int64_t n, uint64_t seed, float sigma);
 

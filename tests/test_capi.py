@@ -55,6 +55,18 @@ def test_argument_errors_without_device():
                                       None) == L.TG_EINVAL
     assert lib.tgx_kq_scratch_bytes(8, 2048, 768) >= 8 * (768 + 2048) * 4
     assert lib.tgx_kq_scratch_bytes(0, 2048, 768) == 0
+    # attention decode: head_dim not a multiple of 8, kv_len outside the cache, null pointers
+    p = x.ctypes.data
+    assert lib.tg_attention_decode(p, p, p, p, p, p, p, p, 0, 4, p, p, p, p, 48, 4, 2, 12, 0) == L.TG_EINVAL
+    assert lib.tg_attention_decode_q4(p, p, p, p, p, p, p, p, 4, 4, p, p, p, p, 256, 2, 1, 128, 0) == L.TG_EINVAL
+    assert lib.tg_attention_decode_q4(None, p, p, p, p, p, p, p, 0, 4, p, p, p, p, 256, 2, 1, 128, 0) == L.TG_EINVAL
+    assert lib.tgx_attention_decode(1, p, p, p, p, p, p, p, p, 0, 8, p, p, p, p, 2048, 32, 5, 128, 0, p, 1 << 20,
+                                    None) == L.TG_EINVAL   # 32 query heads over 5 kv heads
+    assert lib.tgx_attention_scratch_bytes(32, 4, 128, 4096) == 4 * ((4096 + 1024) + 4096 + 32 * 4096 + 4096)
+    assert lib.tgx_attention_scratch_bytes(0, 4, 128, 4096) == 0
+    sb = lib.tgx_attention_scratch_bytes(32, 4, 128, 64)
+    assert lib.tgx_attention_decode(1, p, p, p, p, p, p, p, p, 0, 64, p, p, p, p, 2048, 32, 4, 128, 0, p, sb - 16,
+                                    None) == L.TG_EINVAL   # scratch too small
     shape = L.TgxShape(2048, 768, 128, 8, 48, 1e-6)
     h = ctypes.c_void_p()
     bad = L.TgxShape(2048, 768, 128, 200, 48, 1e-6)

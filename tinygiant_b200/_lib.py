@@ -71,6 +71,23 @@ PROTOTYPES = {
     "tg_f16_matvec": (CI, [VP, VP, VP, CI, CI]),
     "tg_f32_matvec": (CI, [VP, VP, VP, CI, CI]),
     "tg_rms_norm": (CI, [VP, VP, VP, CI, CF]),
+    "tg_attention_decode": (CI, [VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP, CI, CI, CI, CI, CI]),
+    "tg_attention_decode_q4": (CI, [VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP, CI, CI, CI, CI, CI]),
+    "tgx_attention_scratch_bytes": (SZ, [CI, CI, CI, CI]),
+    "tgx_attn_create": (CI, [CI, CI, CI, CI, CI, CI, CI, CI, CF, VP]),
+    "tgx_attn_destroy": (CI, [VP]),
+    "tgx_attn_layer_bytes": (SZ, [VP]),
+    "tgx_attn_set_layer": (CI, [VP, CI, VP, VP, VP, VP, VP, VP, VP, CI]),
+    "tgx_attn_set_rope": (CI, [VP, VP, VP, CI, CI]),
+    "tgx_attn_set_pos": (CI, [VP, CI]),
+    "tgx_attn_status": (CI, [VP, VP]),
+    "tgx_attn_kv": (CI, [VP, CI, VP, VP]),
+    "tgx_attn_read_kv": (CI, [VP, CI, VP, VP]),
+    "tgx_attn_layer": (CI, [VP, CI, VP, VP]),
+    "tgx_attn_advance": (CI, [VP, VP]),
+    "tgx_decode_token": (CI, [VP, VP, VP, VP, CI]),
+    "tgx_attention_decode": (CI, [CI, VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP, CI, CI, CI, CI, CI,
+                                  VP, SZ, VP]),
     "tg_expert_forward": (CI, [VP, VP, VP, CF, CI, CI]),
     "tg_moe_forward": (CI, [VP, VP, CI, VP, VP, CI, CI]),
     "tgx_kq_matrix_bytes": (SZ, [CI, ctypes.c_longlong, CI]),

@@ -15,7 +15,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OUT = PKG / "libtinygiant.so"
-SOURCES = ["tg_kernels.cu", "tg_decode.cu", "tg_batched.cu", "tg_tc.cu", "tg_kquant.cu", "tg_capi.cu", "tg_ep.cu", "tg_noalloc.cu"]
+SOURCES = ["tg_kernels.cu", "tg_decode.cu", "tg_batched.cu", "tg_tc.cu", "tg_kquant.cu", "tg_capi.cu", "tg_ep.cu", "tg_noalloc.cu", "tg_attn.cu"]
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
     "-gencode", "arch=compute_100a,code=sm_100a",

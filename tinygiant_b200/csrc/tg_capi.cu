@@ -76,7 +76,7 @@ struct HostWS {
     std::mutex mu;
     int device = -1;
     cudaStream_t s = nullptr;
-    DevBuf raw, w, x, out, act, hq, ptrs, wts, i32, kqs;
+    DevBuf raw, w, x, out, act, hq, ptrs, wts, i32, kqs, att;   // kqs: down counters must stay zero
 
     int bind() {
         int dev = 0;
@@ -91,7 +91,7 @@ struct HostWS {
         return TG_OK;
     }
     void release() {
-        for (DevBuf* b : {&raw, &w, &x, &out, &act, &hq, &ptrs, &wts, &i32, &kqs}) {
+        for (DevBuf* b : {&raw, &w, &x, &out, &act, &hq, &ptrs, &wts, &i32, &kqs, &att}) {
             if (b->p) cudaFree(b->p);
             b->p = nullptr;
             b->n = 0;
@@ -337,6 +337,93 @@ extern "C" int tg_rms_norm(const float* x, const float* weight, float* out, int 
     TG_CUDA(cudaMemcpyAsync(out, W.out.p, sizeof(float) * dim, cudaMemcpyDeviceToHost, W.s));
     TG_CUDA(cudaStreamSynchronize(W.s));
     return TG_OK;
+}
+
+// tg_attention_decode / tg_attention_decode_q4 on host buffers (csrc/libtinygiant.c:
+// 364-551): the weights, the cached rows 0 .. kv_len - 1 and the rope rows of pos go
+// to the device; the output and the appended cache row (kv_len) come back.
+static int attention_host(int q4, const void* wq, const void* wk, const void* wv, const void* wo,
+                          const float* q_norm_w, const float* k_norm_w, float* kv_k, float* kv_v, int kv_len,
+                          int kv_max, const float* rope_cos, const float* rope_sin, const float* input,
+                          float* output, int embed, int n_heads, int n_kv, int head_dim, int pos, const char* fn) {
+    TG_CHECK(wq && wk && wv && wo && q_norm_w && k_norm_w && kv_k && kv_v && rope_cos && rope_sin && input && output,
+             TG_EINVAL, std::string(fn) + ": null pointer");
+    TG_CHECK(kv_len >= 0 && kv_len < kv_max && pos >= 0, TG_EINVAL,
+             std::string(fn) + ": need 0 <= kv_len < kv_max and pos >= 0");
+    const int seq = kv_len + 1;
+    TG_CHECK(tg::attention_valid(q4, embed, n_heads, n_kv, head_dim, seq), TG_EINVAL,
+             std::string(fn) + ": bad shape (head_dim a multiple of 8 in [8, 256]; n_heads a multiple of "
+                               "n_kv_heads, at most 32 per kv head; kv_len < 32768)");
+    const int qd = n_heads * head_dim, kvd = n_kv * head_dim, half = head_dim / 2;
+    const int fq = q4 ? tg::KQ_Q4K : tg::KQ_F32, fv = q4 ? tg::KQ_F16 : tg::KQ_F32;
+    auto r16 = [](size_t n) { return (n + 15) & ~(size_t)15; };
+    const size_t bq = tg::kq_matrix_bytes(fq, qd, embed), bk = tg::kq_matrix_bytes(fq, kvd, embed),
+                 bv = tg::kq_matrix_bytes(fv, kvd, embed), bo = tg::kq_matrix_bytes(fq, embed, qd);
+    const size_t cache = (size_t)n_kv * seq * head_dim * sizeof(float);
+    const size_t small = r16(sizeof(float) * (2 * head_dim + 2 * half + embed));
+    const size_t scratch = tg::attention_scratch_bytes(n_heads, n_kv, head_dim, seq);
+    HostWS& W = ws();
+    std::lock_guard<std::mutex> lk(W.mu);
+    TG_TRY(W.bind());
+    TG_TRY(ensure(W.w, r16(bq) + r16(bk) + r16(bv) + r16(bo)));
+    TG_TRY(ensure(W.att, 2 * r16(cache) + small + scratch));
+    TG_TRY(ensure(W.out, sizeof(float) * embed));
+    uint8_t* wdev = (uint8_t*)W.w.p;
+    uint8_t *dq = wdev, *dk = dq + r16(bq), *dv = dk + r16(bk), *dw = dv + r16(bv);
+    uint8_t* sdev = (uint8_t*)W.att.p;
+    float* ck = (float*)sdev;
+    float* cv = (float*)(sdev + r16(cache));
+    float* fs = (float*)(sdev + 2 * r16(cache));   // q_norm | k_norm | cos row | sin row | input
+    void* scr = sdev + 2 * r16(cache) + small;
+    cudaStream_t s = W.s;
+    TG_CUDA(cudaMemcpyAsync(dq, wq, bq, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(dk, wk, bk, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(dv, wv, bv, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(dw, wo, bo, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(fs, q_norm_w, sizeof(float) * head_dim, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(fs + head_dim, k_norm_w, sizeof(float) * head_dim, cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(fs + 2 * head_dim, rope_cos + (size_t)pos * half, sizeof(float) * half,
+                            cudaMemcpyHostToDevice, s));
+    TG_CUDA(cudaMemcpyAsync(fs + 2 * head_dim + half, rope_sin + (size_t)pos * half, sizeof(float) * half,
+                            cudaMemcpyHostToDevice, s));
+    float* xd = fs + 2 * head_dim + 2 * half;
+    TG_CUDA(cudaMemcpyAsync(xd, input, sizeof(float) * embed, cudaMemcpyHostToDevice, s));
+    const size_t hpitch = (size_t)kv_max * head_dim * sizeof(float), dpitch = (size_t)seq * head_dim * sizeof(float);
+    if (kv_len > 0) {
+        const size_t width = (size_t)kv_len * head_dim * sizeof(float);
+        TG_CUDA(cudaMemcpy2DAsync(ck, dpitch, kv_k, hpitch, width, n_kv, cudaMemcpyHostToDevice, s));
+        TG_CUDA(cudaMemcpy2DAsync(cv, dpitch, kv_v, hpitch, width, n_kv, cudaMemcpyHostToDevice, s));
+    }
+    // the device caches hold seq rows per head; the rope rows of pos sit at row 0
+    TG_CUDA(tg::launch_attention(q4, dq, dk, dv, dw, fs, fs + head_dim, ck, cv, kv_len, seq, fs + 2 * head_dim,
+                                 fs + 2 * head_dim + half, xd, (float*)W.out.p, embed, n_heads, n_kv, head_dim, 0,
+                                 nullptr, scr, s));
+    TG_CUDA(cudaMemcpyAsync(output, W.out.p, sizeof(float) * embed, cudaMemcpyDeviceToHost, s));
+    const size_t row = (size_t)head_dim * sizeof(float);
+    TG_CUDA(cudaMemcpy2DAsync(kv_k + (size_t)kv_len * head_dim, hpitch, ck + (size_t)kv_len * head_dim, dpitch, row,
+                              n_kv, cudaMemcpyDeviceToHost, s));
+    TG_CUDA(cudaMemcpy2DAsync(kv_v + (size_t)kv_len * head_dim, hpitch, cv + (size_t)kv_len * head_dim, dpitch, row,
+                              n_kv, cudaMemcpyDeviceToHost, s));
+    TG_CUDA(cudaStreamSynchronize(s));
+    return TG_OK;
+}
+
+extern "C" int tg_attention_decode(const float* wq, const float* wk, const float* wv, const float* wo,
+                                   const float* q_norm_w, const float* k_norm_w, float* kv_k, float* kv_v, int kv_len,
+                                   int kv_max, const float* rope_cos, const float* rope_sin, const float* input,
+                                   float* output, int embed_dim, int n_heads, int n_kv_heads, int head_dim, int pos) {
+    return attention_host(0, wq, wk, wv, wo, q_norm_w, k_norm_w, kv_k, kv_v, kv_len, kv_max, rope_cos, rope_sin, input,
+                          output, embed_dim, n_heads, n_kv_heads, head_dim, pos, "tg_attention_decode");
+}
+
+extern "C" int tg_attention_decode_q4(const uint8_t* wq_q4, const uint8_t* wk_q4, const uint16_t* wv_f16,
+                                      const uint8_t* wo_q4, const float* q_norm_w, const float* k_norm_w, float* kv_k,
+                                      float* kv_v, int kv_len, int kv_max, const float* rope_cos,
+                                      const float* rope_sin, const float* input, float* output, int embed_dim,
+                                      int n_heads, int n_kv_heads, int head_dim, int pos) {
+    return attention_host(1, wq_q4, wk_q4, wv_f16, wo_q4, q_norm_w, k_norm_w, kv_k, kv_v, kv_len, kv_max, rope_cos,
+                          rope_sin, input, output, embed_dim, n_heads, n_kv_heads, head_dim, pos,
+                          "tg_attention_decode_q4");
 }
 
 // n experts with Q4_K gate/up and a down matrix of format fmt (host pointers):

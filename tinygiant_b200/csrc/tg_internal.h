@@ -132,8 +132,12 @@ size_t kq_matrix_bytes(int fmt, long long rows, int cols);   // ggml bytes (= de
 size_t kq_smem_bytes(int fmt, int cols);
 // Q6_K ggml blocks -> split layout; raw and dst must not alias.
 cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk, cudaStream_t s);
-// y[rows] = W . x (Q4_K / Q6_K on the 256-wide Q8 blocks of x; f16 / f32 on x).
-cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s);
+// y[rows] = W . x (Q4_K / Q6_K on the 256-wide Q8 blocks of x; f16 / f32 on x), or
+// y[r] = y[r] + (W . x)[r] with accumulate.  pdl: start as a programmatic dependent of
+// the previous kernel on s (the weight copies overlap it; x is read after it
+// completes); it must not write W.
+cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s,
+                             bool pdl = false, bool accumulate = false);
 // h[e][I] = silu(gate_e . x) * (up_e . x) for n Q4_K experts (device pointer arrays).
 // pdl: start as a programmatic dependent of the previous kernel on s, which must not
 // write the weights or the pointer arrays.
@@ -148,6 +152,23 @@ cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const flo
                            float* out, int accumulate, void* scratch, cudaStream_t s);
 // tg_rms_norm in the reference's order (dim a multiple of 4).
 cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s);
+
+// The reference's attention decode step (tg_attn.cu; csrc/libtinygiant.c:344-551).
+// q4: Q4_K wq / wk / wo and f16 wv (tg_attention_decode_q4), else fp32 weights
+// (tg_attention_decode).  Caches [n_kv][kv_max][head_dim] fp32; k and v of this token
+// go to row kv_len; rope tables [positions][head_dim / 2], row pos used.  pos_dev:
+// when set, kv_len = pos = *pos_dev, read on the device (for graph replay).
+// scratch: attention_scratch_bytes(...) bytes.
+constexpr int ATTN_MAX_ROWS = 32768;   // kv_max bound: a softmax weight per row + the V ring in shared memory
+bool attention_valid(int q4, int embed, int n_heads, int n_kv, int head_dim, int kv_max);
+size_t attention_scratch_bytes(int n_heads, int n_kv, int head_dim, int kv_max);
+// pos_dev[1] is the error word of the device-position form: a position outside
+// [0, kv_max) sets it to 1 and the step writes nothing.  accumulate: out += result.
+cudaError_t launch_attention(int q4, const uint8_t* wq, const uint8_t* wk, const uint8_t* wv, const uint8_t* wo,
+                             const float* q_norm, const float* k_norm, float* kv_k, float* kv_v, int kv_len,
+                             int kv_max, const float* rope_cos, const float* rope_sin, const float* x, float* out,
+                             int embed, int n_heads, int n_kv, int head_dim, int pos, int* pos_dev,
+                             void* scratch, cudaStream_t s, bool accumulate = false);
 
 // Record msg as the calling thread's tg_last_error() text; returns code.
 int set_error(int code, const char* msg);

@@ -40,6 +40,7 @@ constexpr int Q4K_B = 144, Q6K_BODY = 208, Q6K_B = 210;
 constexpr int XC = 272;               // stride of a block's 256 codes in shared memory (bank spread)
 constexpr int FROWS = 4;              // rows per warp of the f16 / f32 matvec (8 lanes per row)
 constexpr int FCH = 256;              // columns staged per step
+constexpr int FDEPTH = 4;             // f16 / f32: column chunks of a warp's rows in flight
 // FMT values: KQ_Q4K 0, KQ_F16 1, KQ_Q6K 2, KQ_F32 4 (tg_internal.h)
 
 // Shared-memory activation of one vector of bpr blocks (quantised formats).
@@ -62,9 +63,10 @@ __host__ __device__ inline int terms_per_warp(int cols) {
     return bpr > 32 ? bpr : 32;
 }
 // Staging bytes of one warp: 32 units of the format's block (Q4_K 144 B, Q6_K body
-// 208 B) or four padded rows of 256 values (f16 / f32).
+// 208 B), or a ring of FDEPTH slots of four padded rows of 256 values (f16 / f32).
+__host__ __device__ constexpr int fx_slot_bytes(int fmt) { return FROWS * (FCH * (fmt == KQ_F16 ? 2 : 4) + 16); }
 __host__ __device__ constexpr int stage_bytes(int fmt) {
-    return fmt == KQ_Q4K ? 32 * Q4K_B : fmt == KQ_Q6K ? 32 * Q6K_BODY : 4 * (FCH * (fmt == KQ_F16 ? 2 : 4) + 16);
+    return fmt == KQ_Q4K ? 32 * Q4K_B : fmt == KQ_Q6K ? 32 * Q6K_BODY : FDEPTH * fx_slot_bytes(fmt);
 }
 // stages per warp: gate and up (MODE 1), else one
 __host__ __device__ inline size_t warp_bytes(int fmt, int mode, int cols) {
@@ -231,6 +233,8 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_n() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 // Programmatic dependent launch: let the next kernel in the stream start, and wait
 // for the previous one to complete (both return at once outside such launches).
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -292,30 +296,47 @@ __device__ float kq_rows_warp(const uint8_t* __restrict__ M, long long nblk, int
     return tot;
 }
 
+// Column chunk c (FCH values) of rows [r0, r0 + nr) of an f16 / f32 matrix into ring
+// slot c % FDEPTH of a warp's staging area; one commit group per call (empty past the
+// last chunk).
+template <int FMT>
+__device__ __forceinline__ void fx_issue(const uint8_t* __restrict__ M, int cols, int r0, int nr, uint8_t* stage,
+                                         int c, int lane) {
+    constexpr int ES = FMT == KQ_F16 ? 2 : 4;
+    constexpr int RS = FCH * ES + 16;   // padded staged row stride
+    if (c * FCH < cols) {
+        const int c0 = c * FCH, cw = min(FCH, cols - c0), per_row = cw * ES / 16;
+        uint8_t* slot = stage + (c % FDEPTH) * fx_slot_bytes(FMT);
+        for (int i = lane; i < nr * per_row; i += 32) {
+            const int r = i / per_row, k = i - r * per_row;
+            cp_async16(slot + r * RS + k * 16, M + ((size_t)(r0 + r) * cols + c0) * ES + 16 * k);
+        }
+    }
+    cp_async_commit();
+}
+
 // Rows [r0, r0 + nr) (nr <= 4) of an f16 / f32 matrix against fp32 x in shared
 // memory, csrc/libtinygiant.c:262-318: lane (row i, chain v) runs the fused sum of
 // columns v, v + 8, ...; the eight chains fold as (v, v + 4) then pairwise.  Returns
-// the total in lane 8 * i.
+// the total in lane 8 * i.  FDEPTH column chunks stay in flight (`issued`: the
+// first FDEPTH are already, fx_issue).
 template <int FMT>
 __device__ float fx_rows_warp(const uint8_t* __restrict__ M, int cols, int r0, int nr, const float* xs,
-                              uint8_t* stage, int lane) {
+                              uint8_t* stage, int lane, bool issued) {
     constexpr int ES = FMT == KQ_F16 ? 2 : 4;
-    constexpr int RS = FCH * ES + 16;   // padded staged row stride
+    constexpr int RS = FCH * ES + 16;
     const int ri = lane >> 3, v = lane & 7;
+    if (!issued)
+        for (int c = 0; c < FDEPTH; c++) fx_issue<FMT>(M, cols, r0, nr, stage, c, lane);
+    const int nch = (cols + FCH - 1) / FCH;
     float acc = 0.0f;
-    for (int c0 = 0; c0 < cols; c0 += FCH) {
-        const int cw = min(FCH, cols - c0);
-        const int per_row = cw * ES / 16;
+    for (int c = 0; c < nch; c++) {
+        cp_async_wait_n<FDEPTH - 1>();   // groups complete in order: chunk c has landed
         __syncwarp();
-        for (int i = lane; i < nr * per_row; i += 32) {
-            const int r = i / per_row, k = i - r * per_row;
-            cp_async16(stage + r * RS + k * 16, M + ((size_t)(r0 + r) * cols + c0) * ES + 16 * k);
-        }
-        cp_async_commit();
-        cp_async_wait_all();
-        __syncwarp();
+        const int c0 = c * FCH, cw = min(FCH, cols - c0);
         if (ri < nr) {
-            const uint8_t* row = stage + ri * RS;
+            const uint8_t* row = stage + (c % FDEPTH) * fx_slot_bytes(FMT) + ri * RS;
+#pragma unroll 8
             for (int s = 0; s < cw / 8; s++) {
                 const int col = 8 * s + v;
                 float w = FMT == KQ_F16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t*>(row)[col])
@@ -323,7 +344,10 @@ __device__ float fx_rows_warp(const uint8_t* __restrict__ M, int cols, int r0, i
                 acc = __fmaf_rn(w, xs[c0 + col], acc);
             }
         }
+        __syncwarp();
+        fx_issue<FMT>(M, cols, r0, nr, stage, c + FDEPTH, lane);
     }
+    cp_async_wait_n<0>();
     __syncwarp();
     const float t = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));   // chains v and v + 4
     const float p = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 1));      // (t0 + t1), (t2 + t3)
@@ -374,6 +398,9 @@ __global__ void __launch_bounds__(KT) k_kq(KQParams p) {
     if constexpr (!FLOAT_FMT) {
         issued0 = kq_issue<FMT>(M0, bpr, r0, nr, stage, lane);
         if constexpr (MODE == 1) issued1 = kq_issue<FMT>(p.B[e], bpr, r0, nr, stage + SB, lane);
+    } else if (nr > 0) {
+        for (int c = 0; c < FDEPTH; c++) fx_issue<FMT>(M0, cols, r0, nr, stage, c, lane);
+        issued0 = true;
     }
     pdl_wait();
     const float* xin = MODE == 2 ? p.x + (size_t)e * cols : p.x;
@@ -388,14 +415,14 @@ __global__ void __launch_bounds__(KT) k_kq(KQParams p) {
     auto rows_dot = [&](const uint8_t* M, uint8_t* st, bool issued) -> float {
         if (nr == 0) return 0.0f;
         if constexpr (FLOAT_FMT)
-            return fx_rows_warp<FMT>(M, cols, r0, nr, xs, st, lane);
+            return fx_rows_warp<FMT>(M, cols, r0, nr, xs, st, lane, issued);
         else
             return kq_rows_warp<FMT>(M, nblk, bpr, r0, nr, a, st, terms, lane, issued);
     };
 
     if constexpr (MODE == 0) {
         float y = rows_dot(M0, stage, issued0);
-        if (has) p.out[row] = y;
+        if (has) p.out[row] = p.accumulate ? __fadd_rn(p.out[row], y) : y;
     } else if constexpr (MODE == 1) {
         float g = rows_dot(M0, stage, issued0);
         float u = rows_dot(p.B[e], stage + SB, issued1);
@@ -441,21 +468,35 @@ __global__ void k_split_q6k(const uint16_t* __restrict__ src, uint8_t* __restric
 // tg_rms_norm, csrc/libtinygiant.c:322-340, one CTA: four fused sums of x^2 (chain v
 // over elements v, v + 4, ...), folded pairwise; scale = 1 / sqrtf(ss / dim + eps);
 // out = (x * scale) * w.
+// x is staged in shared memory first (up to RMS_STAGE floats from a 16-byte aligned
+// x; otherwise read from global memory), so the four chains run at the fused
+// multiply-add latency.
+constexpr int RMS_STAGE = 8192;
 __global__ void k_rms_norm_ref(const float* __restrict__ x, const float* __restrict__ w, float* __restrict__ out,
                                int dim, float eps) {
     __shared__ float s_scale;
+    __shared__ __align__(16) float xs[RMS_STAGE];
+    const bool staged = dim <= RMS_STAGE && ((uintptr_t)x & 15) == 0;
+    if (staged) {
+        for (int i = threadIdx.x; i < dim / 4; i += blockDim.x)
+            reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(x)[i];
+        __syncthreads();
+    }
+    const float* xv = staged ? xs : x;
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float acc = 0.0f;
-        if (lane < 4)
-            for (int i = lane; i < dim; i += 4) acc = __fmaf_rn(x[i], x[i], acc);
+        if (lane < 4) {
+#pragma unroll 16
+            for (int i = lane; i < dim; i += 4) acc = __fmaf_rn(xv[i], xv[i], acc);
+        }
         const float p = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1));   // (s0 + s1), (s2 + s3)
         const float ss = __fadd_rn(p, __shfl_down_sync(0xffffffffu, p, 2));
         if (lane == 0) s_scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)dim), eps)));
     }
     __syncthreads();
     const float sc = s_scale;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(x[i], sc), w[i]);
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) out[i] = __fmul_rn(__fmul_rn(xv[i], sc), w[i]);
 }
 
 int row_blocks(int fmt, int rows, int cols) {
@@ -540,7 +581,8 @@ cudaError_t launch_kq_split_q6k(const uint8_t* raw, uint8_t* dst, long long nblk
     return cudaGetLastError();
 }
 
-cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s) {
+cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y, int rows, int cols, cudaStream_t s,
+                             bool pdl, bool accumulate) {
     KQParams p{};
     p.mat = W;
     p.x = x;
@@ -548,7 +590,8 @@ cudaError_t launch_kq_matvec(int fmt, const uint8_t* W, const float* x, float* y
     p.rows = rows;
     p.cols = cols;
     p.n = 1;
-    return launch_kq_fmt<0>(fmt, p, 1, false, s);
+    p.accumulate = accumulate ? 1 : 0;
+    return launch_kq_fmt<0>(fmt, p, 1, pdl, s);
 }
 
 cudaError_t launch_kq_gateup(const uint8_t* const* gate, const uint8_t* const* up, int n, const float* x, int H,

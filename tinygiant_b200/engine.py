@@ -146,3 +146,131 @@ def expert_forward(lib, q4: np.ndarray, x: np.ndarray, out: np.ndarray, weight: 
     check(lib.tg_expert_forward_mixed(q4.ctypes.data, q4.ctypes.data + t, q4.ctypes.data + 2 * t, 3,
                                       x.ctypes.data, out.ctypes.data, ctypes.c_float(weight), embed, inter), lib)
     return out
+
+
+def rope_cache(max_pos: int, head_dim: int = C.HEAD_DIM, base: float = C.ROPE_BASE):
+    """The reference's build_rope_cache (tinygiant/_math.py:11-17): fp32 inverse
+    frequencies 1 / base^(2i / head_dim), their outer product with the fp32 positions,
+    fp32 cos and sin, each [max_pos][head_dim / 2]."""
+    inv = (1.0 / (base ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))).astype(np.float32)
+    f = np.outer(np.arange(max_pos, dtype=np.float32), inv)
+    return np.cos(f).astype(np.float32), np.sin(f).astype(np.float32)
+
+
+def _host_or_dev(a):
+    """(pointer, on_device) of a numpy array (kept alive by the caller) or a cuda tensor."""
+    if a is None:
+        return None, 0
+    if isinstance(a, np.ndarray):
+        assert a.flags.c_contiguous
+        return a.ctypes.data, 0
+    assert a.is_cuda and a.is_contiguous()
+    return a.data_ptr(), 1
+
+
+class AttentionModel:
+    """The attention half of every decode layer, resident in HBM (engine.py:199-226):
+    x += attention(RMSNorm(x) * attn_norm) with the reference's tg_attention_decode(_q4)
+    step, KV caches [n_layers][2][n_kv][kv_max][head_dim] fp32 and a device position.
+
+    With a MoEModel, decode_token runs whole decode layers (attention, then the MoE
+    block) for one token, replayed from a CUDA graph."""
+
+    def __init__(self, embed=C.EMBED_DIM, n_heads=C.N_HEADS, n_kv_heads=C.N_KV_HEADS, head_dim=C.HEAD_DIM,
+                 n_layers=C.N_LAYERS, kv_max=4096, q4=True, device=0, eps=C.RMS_EPS):
+        self.lib = get_lib()
+        self.embed, self.n_heads, self.n_kv_heads, self.head_dim = embed, n_heads, n_kv_heads, head_dim
+        self.n_layers, self.kv_max, self.q4, self.device = n_layers, kv_max, bool(q4), device
+        h = ctypes.c_void_p()
+        check(self.lib.tgx_attn_create(device, int(self.q4), n_layers, embed, n_heads, n_kv_heads, head_dim, kv_max,
+                                       float(eps), ctypes.byref(h)), self.lib)
+        self._a = h
+        cos, sin = rope_cache(kv_max, head_dim)
+        self.set_rope(cos, sin)
+
+    def close(self):
+        if self._a:
+            self.lib.tgx_attn_destroy(self._a)
+            self._a = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._a
+
+    def matrix_bytes(self):
+        """Bytes of wq, wk, wv, wo in this model's formats (Q4_K / f16, or fp32)."""
+        qd, kvd, E = self.n_heads * self.head_dim, self.n_kv_heads * self.head_dim, self.embed
+        if self.q4:
+            return qd * E // 256 * 144, kvd * E // 256 * 144, kvd * E * 2, E * qd // 256 * 144
+        return qd * E * 4, kvd * E * 4, kvd * E * 4, E * qd * 4
+
+    def set_layer(self, layer: int, wq=None, wk=None, wv=None, wo=None, q_norm=None, k_norm=None, attn_norm=None):
+        """Weights of one layer (numpy host arrays or cuda tensors, all of one kind); None keeps a part."""
+        parts = [_host_or_dev(a) for a in (wq, wk, wv, wo, q_norm, k_norm, attn_norm)]
+        kinds = {d for p, d in parts if p is not None}
+        assert len(kinds) <= 1, "pass host arrays or device tensors, not both"
+        on_dev = kinds.pop() if kinds else 0
+        check(self.lib.tgx_attn_set_layer(self._a, layer, *(p for p, _ in parts), on_dev), self.lib)
+
+    def set_rope(self, cos: np.ndarray, sin: np.ndarray):
+        cos = np.ascontiguousarray(cos, np.float32)
+        sin = np.ascontiguousarray(sin, np.float32)
+        check(self.lib.tgx_attn_set_rope(self._a, cos.ctypes.data, sin.ctypes.data, cos.shape[0], 0), self.lib)
+
+    def fill_synthetic(self, seed: int):
+        """Random weights generated on the device: Q4_K blocks of random bytes with fp16
+        scales d in [5e-5, 1.5e-4] and dmin = 7.5 d (near zero-mean weights), f16 wv of
+        N(0, 0.02) (fp32 N(0, 0.02) matrices when q4 is off), norm weights 1."""
+        import torch
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        dev = torch.device("cuda", self.device)
+        sizes = self.matrix_bytes()
+        for l in range(self.n_layers):
+            mats = []
+            for i, n in enumerate(sizes):
+                if self.q4 and i != 2:
+                    b = torch.randint(0, 256, (n,), dtype=torch.uint8, device=dev, generator=gen).view(-1, 144)
+                    d = torch.empty(b.shape[0], device=dev).uniform_(5e-5, 1.5e-4, generator=gen)
+                    b[:, 0:2] = d.half().view(torch.uint8).view(-1, 2)
+                    b[:, 2:4] = (d * 7.5).half().view(torch.uint8).view(-1, 2)
+                    mats.append(b.view(-1))
+                else:
+                    v = torch.randn(n // (2 if self.q4 else 4), device=dev, generator=gen) * 0.02
+                    mats.append((v.half() if self.q4 else v).view(torch.uint8))
+            self.set_layer(l, *mats)
+        torch.cuda.synchronize()
+
+    def reset(self, pos: int = 0):
+        """Start a sequence at `pos` rows cached (engine.py:145-148's kv_len = 0)."""
+        check(self.lib.tgx_attn_set_pos(self._a, pos), self.lib)
+
+    def status(self) -> int:
+        """Synchronise; the device position; raises if a step ran past the cache."""
+        p = ctypes.c_int()
+        check(self.lib.tgx_attn_status(self._a, ctypes.byref(p)), self.lib)
+        return p.value
+
+    def read_kv(self, layer: int):
+        shape = (self.n_kv_heads, self.kv_max, self.head_dim)
+        k, v = np.empty(shape, np.float32), np.empty(shape, np.float32)
+        check(self.lib.tgx_attn_read_kv(self._a, layer, k.ctypes.data, v.ctypes.data), self.lib)
+        return k, v
+
+    def layer(self, layer: int, x, stream=None):
+        """x (cuda f32[embed]) += attention of `layer` at the current position."""
+        check(self.lib.tgx_attn_layer(self._a, layer, _dev_ptr(x), _stream_handle(stream)), self.lib)
+
+    def advance(self, stream=None):
+        check(self.lib.tgx_attn_advance(self._a, _stream_handle(stream)), self.lib)
+
+    def decode_token(self, x, moe: "MoEModel | None" = None, stream=None, eager: bool = False):
+        """One token through every layer (attention, then moe's MoE block when given),
+        then the position moves on; x (cuda f32[embed]) in place."""
+        check(self.lib.tgx_decode_token(self._a, moe.handle if moe is not None else None, _dev_ptr(x),
+                                        _stream_handle(stream), TGX_EAGER if eager else 0), self.lib)
