@@ -856,7 +856,7 @@ def run_layers(args):
                        "l2": f"inputs larger than L2 ({alg / 1e9:.2f} GB read per token)",
                        "parallelism": "replicas" if ws > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": None, "kernel": f"token graph: {NL} x (RMSNorm, 7 attention kernels, fused MoE "
+                         "traffic": None, "kernel": f"token graph: {NL} x (RMSNorm, 6 attention kernels, fused MoE "
                                                     f"layer) + position advance", "token_ms": tok_ms,
                          "algorithmic_bytes": alg,
                          "algorithmic_bytes_def": "per layer: Q4_K/f16 attention weights + K and V rows read "
@@ -865,7 +865,7 @@ def run_layers(args):
             "cpu_baseline": cpu,
             "e2e": {"value": ws * K / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": H * 4,
                     "d2h_bytes_per_step": H * 4},
-            "gpu_launches": (9 * NL + 1) * K,
+            "gpu_launches": (8 * NL + 1) * K,
             "clocks": clocks.summary(),
         })
     am.close()

@@ -63,6 +63,7 @@ def test_argument_errors_without_device():
     assert lib.tgx_attention_decode(1, p, p, p, p, p, p, p, p, 0, 8, p, p, p, p, 2048, 32, 5, 128, 0, p, 1 << 20,
                                     None) == L.TG_EINVAL   # 32 query heads over 5 kv heads
     assert lib.tgx_attention_scratch_bytes(32, 4, 128, 4096) == 4 * ((4096 + 1024) + 4096 + 32 * 4096 + 4096)
+    assert lib.tgx_attention_scratch_bytes(32, 4, 128, 4097) == 4 * ((4096 + 1024) + 4096 + 32 * 4100 + 4096)
     assert lib.tgx_attention_scratch_bytes(0, 4, 128, 4096) == 0
     sb = lib.tgx_attention_scratch_bytes(32, 4, 128, 64)
     assert lib.tgx_attention_decode(1, p, p, p, p, p, p, p, p, 0, 64, p, p, p, p, 2048, 32, 4, 128, 0, p, sb - 16,

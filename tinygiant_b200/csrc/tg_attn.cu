@@ -58,10 +58,11 @@ struct AttnArgs {
     float* qf;               // normalised, rotated q [NH*HD]
     float* kv_k;             // [NKV][kv_max][HD]
     float* kv_v;
-    float* S;                // scores [NH][kv_max]
+    float* S;                // scores [NH][s_stride]
     float* att;              // attention output [NH*HD]
     int* pos_dev;            // when set: kv_len = pos = pos_dev[0]; pos_dev[1] the error word
     int NH, NKV, HD, kv_max, kv_len, pos;
+    int s_stride;            // floats per score row: kv_max rounded up to 4 (16-byte rows)
 };
 
 __device__ __forceinline__ int kv_len_of(const AttnArgs& a) { return a.pos_dev ? *a.pos_dev : a.kv_len; }
@@ -166,7 +167,7 @@ __global__ void __launch_bounds__(1024) k_attn_scores(AttnArgs a) {
     }
     const float dot = __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
     const float inv_sqrt = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));
-    a.S[(size_t)(j * R + w) * a.kv_max + t0 + lane] = __fmul_rn(dot, inv_sqrt);
+    a.S[(size_t)(j * R + w) * a.s_stride + t0 + lane] = __fmul_rn(dot, inv_sqrt);
 }
 
 constexpr int VST = 3;           // V ring stages
@@ -218,7 +219,8 @@ __global__ void __launch_bounds__(256) k_attn_softmax_v(AttnArgs a, int hpc, int
         if (cols) *reinterpret_cast<float4*>(a.att + (size_t)h * HD + 4 * ht) = make_float4(0.f, 0.f, 0.f, 0.f);
         return;
     }
-    const int seq = kv_len + 1, vr = VSTAGE / (HD * 4), nch = (seq + vr - 1) / vr, gpr = HD / 4;
+    // rows per stage: a multiple of 8, so each 8-row block's weights are two 16-byte reads
+    const int seq = kv_len + 1, vr = (VSTAGE / (HD * 4)) & ~7, nch = (seq + vr - 1) / vr, gpr = HD / 4;
     float* ring = sm;                                           // [VST][VSTAGE / 4]
     float* e = sm + VST * (VSTAGE / 4) + (size_t)hs * e_stride(cap);   // this head's weights
     const float* vbase = a.kv_v + (size_t)j * a.kv_max * HD;
@@ -231,15 +233,24 @@ __global__ void __launch_bounds__(256) k_attn_softmax_v(AttnArgs a, int hpc, int
         }
         cp_async_commit();
     };
+    if (ht < 32) {   // the head's first warp: its score row into e, ahead of the V copies
+        const float* srow = a.S + (size_t)h * a.s_stride;
+        for (int i = lane; i < (seq + 3) / 4; i += 32) cp_async16(e + 4 * i, srow + 4 * i);
+    }
+    cp_async_commit();
 #pragma unroll
     for (int i = 0; i < VST; i++) issue(i);
     if (ht < 32) {   // the head's first warp: the softmax
-        const float* srow = a.S + (size_t)h * a.kv_max;
+        cp_async_wait<VST>();   // the score row has landed
+        __syncwarp();
         float m = -1e30f;   // a NaN score never becomes the max, as with `>`
-        for (int t = lane; t < seq; t += 32) m = fmaxf(m, srow[t]);
+#pragma unroll 4
+        for (int t = lane; t < seq; t += 32) m = fmaxf(m, e[t]);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        for (int t = lane; t < seq + EPAD; t += 32) e[t] = t < seq ? tg_expf(__fsub_rn(srow[t], m)) : 0.0f;
+#pragma unroll 4
+        for (int t = lane; t < seq; t += 32) e[t] = tg_expf(__fsub_rn(e[t], m));
+        for (int t = seq + lane; t < seq + EPAD; t += 32) e[t] = 0.0f;
         __syncwarp();
         float inv = 0.0f;
         if (lane == 0) {   // row order; 16-byte reads, the next two loaded before the adds
@@ -268,9 +279,25 @@ __global__ void __launch_bounds__(256) k_attn_softmax_v(AttnArgs a, int hpc, int
         const float* buf = ring + (ch % VST) * (VSTAGE / 4) + 4 * ht;
         const float* w = e + ch * vr;
         const int nr = min(vr, seq - ch * vr);
-        if (cols) {
-#pragma unroll 8
-            for (int r = 0; r < nr; r++) {
+        if (cols) {   // blocks of 8 rows: their weights and V values loaded, then 32 fused steps row by row
+            const int n8 = nr & ~7;
+#pragma unroll 2
+            for (int r = 0; r < n8; r += 8) {
+                const float4 w0 = *reinterpret_cast<const float4*>(w + r);
+                const float4 w1 = *reinterpret_cast<const float4*>(w + r + 4);
+                float4 v[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = *reinterpret_cast<const float4*>(buf + (r + u) * HD);
+                const float wr[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    acc.x = __fmaf_rn(wr[u], v[u].x, acc.x);
+                    acc.y = __fmaf_rn(wr[u], v[u].y, acc.y);
+                    acc.z = __fmaf_rn(wr[u], v[u].z, acc.z);
+                    acc.w = __fmaf_rn(wr[u], v[u].w, acc.w);
+                }
+            }
+            for (int r = n8; r < nr; r++) {
                 const float4 v = *reinterpret_cast<const float4*>(buf + r * HD);
                 const float wr = w[r];
                 acc.x = __fmaf_rn(wr, v.x, acc.x);
@@ -320,7 +347,7 @@ bool attention_valid(int q4, int embed, int n_heads, int n_kv, int head_dim, int
 
 size_t attention_scratch_bytes(int n_heads, int n_kv, int head_dim, int kv_max) {
     const size_t qd = (size_t)n_heads * head_dim, kvd = (size_t)n_kv * head_dim;
-    return 4 * (r16f(qd + 2 * kvd) + r16f(qd) + r16f((size_t)n_heads * kv_max) + r16f(qd));
+    return 4 * (r16f(qd + 2 * kvd) + r16f(qd) + (size_t)n_heads * r16f(kv_max) + r16f(qd));
 }
 
 cudaError_t launch_attention(int q4, const uint8_t* wq, const uint8_t* wk, const uint8_t* wv, const uint8_t* wo,
@@ -334,7 +361,8 @@ cudaError_t launch_attention(int q4, const uint8_t* wq, const uint8_t* wk, const
     a.qkv = base;
     a.qf = base + r16f((size_t)qd + 2 * kvd);
     a.S = a.qf + r16f(qd);
-    a.att = a.S + r16f((size_t)n_heads * kv_max);
+    a.s_stride = (int)r16f(kv_max);
+    a.att = a.S + (size_t)n_heads * a.s_stride;
     a.q_norm = q_norm;
     a.k_norm = k_norm;
     a.rope_cos = rope_cos;
@@ -351,8 +379,12 @@ cudaError_t launch_attention(int q4, const uint8_t* wq, const uint8_t* wk, const
     const int fq = q4 ? KQ_Q4K : KQ_F32, fv = q4 ? KQ_F16 : KQ_F32;
     float* qkv = base;
     cudaError_t e;
-    if ((e = launch_kq_matvec(fq, wq, x, qkv, qd, embed, s, true)) != cudaSuccess) return e;
-    if ((e = launch_kq_matvec(fq, wk, x, qkv + qd, kvd, embed, s, true)) != cudaSuccess) return e;
+    if (wk == wq + kq_matrix_bytes(fq, qd, embed)) {   // wq | wk contiguous (the context's layout): one launch
+        if ((e = launch_kq_matvec(fq, wq, x, qkv, qd + kvd, embed, s, true)) != cudaSuccess) return e;
+    } else {
+        if ((e = launch_kq_matvec(fq, wq, x, qkv, qd, embed, s, true)) != cudaSuccess) return e;
+        if ((e = launch_kq_matvec(fq, wk, x, qkv + qd, kvd, embed, s, true)) != cudaSuccess) return e;
+    }
     if ((e = launch_kq_matvec(fv, wv, x, qkv + qd + kvd, kvd, embed, s, true)) != cudaSuccess) return e;
     if ((e = launch_pdl(k_attn_qk, dim3(n_heads + n_kv), dim3(32), 4 * head_dim * sizeof(float), s, a)) != cudaSuccess)
         return e;

@@ -761,10 +761,13 @@ int fused_launch(tgx_ctx* c, int L0, int nL, float* x, cudaStream_t s) {
     P.L0 = L0;
     P.nL = nL;
     P.x_in = x;
-    // in place is safe when nL >= 2 (every read of x_in precedes the last layer's writes)
-    P.x_out = nL >= 2 ? x : c->xbuf;
+    // In place is safe when every read of x_in precedes the first write of x_out: with
+    // nL >= 2, or when every CTA owns a gate/up unit (x_out is written after all h
+    // records are gathered, and each CTA reads x_in before computing its units).
+    const bool inplace = nL >= 2 || c->fp.k * c->g.nbI >= c->G;
+    P.x_out = inplace ? x : c->xbuf;
     TG_CUDA(tg::launch_decode_fused(P, c->G, s));
-    if (nL < 2)
+    if (!inplace)
         TG_CUDA(cudaMemcpyAsync(x, P.x_out, sizeof(float) * c->g.H, cudaMemcpyDeviceToDevice, s));
     return TG_OK;
 }

@@ -37,7 +37,7 @@ struct FusedParams {
     int k_early;              // > 0: down in two stages, slots [0, k_early) (all their gate/up units
                               // first in their CTAs) before the rest; 0: one stage
     const float* x_in;        // hidden state in
-    float* x_out;             // hidden state out (may equal x_in when nL >= 2)
+    float* x_out;             // hidden state out (may equal x_in when nL >= 2 or every CTA has a gate/up unit)
     unsigned long long* xw;   // [Lmax + 1][H] hidden states between layers: (tag << 32) | f32 bits
     unsigned long long* acc;  // [nL][FUSED_ACC][E + 1] count-tagged fixed-point router sums, then
                               // sum of x^2 (zero between launches)

@@ -624,7 +624,7 @@ cudaError_t launch_kq_down(int fmt, const uint8_t* const* down, int n, const flo
 }
 
 cudaError_t launch_rms_norm_ref(const float* x, const float* w, float* out, int dim, float eps, cudaStream_t s) {
-    k_rms_norm_ref<<<1, 256, 0, s>>>(x, w, out, dim, eps);
+    k_rms_norm_ref<<<1, 1024, 0, s>>>(x, w, out, dim, eps);
     return cudaGetLastError();
 }
 
