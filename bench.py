@@ -66,6 +66,9 @@ def parse():
     ap.add_argument("--tier", type=int, default=-1,
                     help="P >= 0: host tier with P experts per layer pinned in HBM, Zipf(1.1) routing (configs[3])")
     ap.add_argument("--cache-slots", type=int, default=24, help="HBM cache slots of the host tier")
+    ap.add_argument("--layout", choices=["ggml", "rows"], default="ggml",
+                    help="--tier: host bytes as ggml blobs (repacked after each copy) or a version-4 row-split "
+                         "relayout (copied as they are)")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallelism: under torchrun each rank holds E/N experts of every layer and "
                          "the ranks decode the same --tokens T tokens together (NCCL all-reduce per layer)")
@@ -486,15 +489,21 @@ def run_tier(args):
     NL, P = args.layers, args.tier
     model = MoEModel(H, I, E, K_TOP, NL)
     model.fill_synthetic(args.seed)
+    from tinygiant_b200 import relayout as RL
     host = []
     for l in range(NL):   # the relayout bytes of each layer in pinned host memory
         t = torch.empty(E * EXPERT_BYTES, dtype=torch.uint8, pin_memory=True)
         r = model.lib.tgx_read_experts(model.handle, l, 0, E, ctypes.c_void_p(t.data_ptr()))
         assert r == 0
+        if args.layout == "rows":   # as a version-4 relayout stores them
+            v = t.numpy()
+            for e in range(E):
+                v[e * EXPERT_BYTES:(e + 1) * EXPERT_BYTES] = RL.expert_convert(
+                    v[e * EXPERT_BYTES:(e + 1) * EXPERT_BYTES], H, I, True)
         host.append(t)
     K, W = args.steps, max(3, args.warmup)
     ids, perms = zipf_routes(K + W, NL, E, K_TOP, 1.1, args.seed + 1)
-    cache = HostTierCache(model, host, cache_slots=args.cache_slots)
+    cache = HostTierCache(model, host, cache_slots=args.cache_slots, layout=args.layout)
     for l in range(NL):
         cache.pin(l, perms[l][:P])
     w = np.full(K_TOP, 1.0 / K_TOP, np.float32)
@@ -531,8 +540,9 @@ def run_tier(args):
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
         "config": {"workload": f"configs[3]: {NL} layers, top-{K_TOP} by Zipf(1.1) routing, {P} pinned per layer, "
-                               f"{args.cache_slots} HBM cache slots, relayout bytes in pinned host memory",
-                   "layers": NL, "pinned_per_layer": P, "cache_slots": args.cache_slots},
+                               f"{args.cache_slots} HBM cache slots, relayout bytes in pinned host memory "
+                               f"({args.layout} layout)",
+                   "layers": NL, "pinned_per_layer": P, "cache_slots": args.cache_slots, "layout": args.layout},
         "hit_rate": hits / max(1, hits + misses), "misses_per_token": misses / K,
         "h2d_gbs": nbytes / (ms / 1000.0) / 1e9, "wall_tok_s": K / wall,
     }))

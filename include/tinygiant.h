@@ -185,6 +185,11 @@ size_t tgx_expert_bytes(const tgx_ctx *ctx);
  * src is host memory (pinned or pageable) unless src_on_device. */
 int tgx_load_experts(tgx_ctx *ctx, int layer, int first, int n, const void *src, int src_on_device);
 
+/* tgx_load_experts for blobs already in the row-split layout the kernels read (each
+ * matrix row: its Q4_0 blocks' 16-byte nibble groups, then their fp16 scales; a
+ * version-4 "rows" relayout stores experts so): a plain copy, no repack. */
+int tgx_load_experts_rows(tgx_ctx *ctx, int layer, int first, int n, const void *src, int src_on_device);
+
 /* Read n experts of a layer back as ggml blobs into host memory. */
 int tgx_read_experts(tgx_ctx *ctx, int layer, int first, int n, void *dst_host);
 

@@ -18,13 +18,18 @@ def oracle_block(oracle, blob, x, ids, w, H, I, normw):
     return x + moe
 
 
-def test_host_tier_matches_oracle(oracle):
+@pytest.mark.parametrize("layout", ["ggml", "rows"])
+def test_host_tier_matches_oracle(oracle, layout):
+    """Host bytes as ggml blobs (repacked on the device after each copy) or as a
+    version-4 row-split relayout holds them (copied as they are)."""
     import torch
+    from tinygiant_b200 import relayout as R
     from tinygiant_b200.cache import HostTierCache
     from tinygiant_b200.engine import MoEModel
     H, I, E, k, L = 512, 256, 16, 4, 2
     rng = np.random.default_rng(21)
     m = MoEModel(H, I, E, k, L)
+    eb = m.expert_bytes
     blobs, norms, host = [], [], []
     for l in range(L):
         b = oracle.quantize_q4_0((rng.standard_normal(E * 3 * H * I) * 0.02).astype(np.float32))
@@ -32,8 +37,10 @@ def test_host_tier_matches_oracle(oracle):
         m.set_ffn_norm(l, nw)
         blobs.append(b)
         norms.append(nw)
-        host.append(torch.from_numpy(b).pin_memory())
-    cache = HostTierCache(m, host, cache_slots=6)
+        hb = b if layout == "ggml" else np.concatenate(
+            [R.expert_convert(b[e * eb:(e + 1) * eb], H, I, True) for e in range(E)])
+        host.append(torch.from_numpy(hb).pin_memory())
+    cache = HostTierCache(m, host, cache_slots=6, layout=layout)
     cache.pin(0, [3])
     x = rng.standard_normal(H).astype(np.float32)
     xd = torch.from_numpy(x.copy()).cuda()

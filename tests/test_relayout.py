@@ -41,6 +41,43 @@ def test_write_and_read_q4_0_relayout(tmp_path):
     rd.close()
 
 
+def test_row_split_conversion():
+    # rows of blocks: nibble groups first, then the fp16 scales; and back
+    rng = np.random.default_rng(5)
+    g = _blob(rng, 2 * 3 * 18)                       # 2 rows x 3 blocks
+    r = R.rows_from_ggml(g, 2, 3)
+    assert r.size == g.size
+    b = g.reshape(2, 3, 18)
+    assert np.array_equal(r.reshape(2, 54)[:, :48], b[:, :, 2:].reshape(2, 48))
+    assert np.array_equal(r.reshape(2, 54)[:, 48:], b[:, :, :2].reshape(2, 6))
+    assert np.array_equal(R.ggml_from_rows(r, 2, 3), g)
+    H, I = 512, 256
+    eb = 3 * I * (H // 32) * 18
+    x = _blob(rng, eb)
+    y = R.expert_convert(x, H, I, True)
+    gb = I * (H // 32) * 18
+    assert np.array_equal(y[:gb], R.rows_from_ggml(x[:gb], I, H // 32))               # gate
+    assert np.array_equal(y[2 * gb:], R.rows_from_ggml(x[2 * gb:], H, I // 32))       # down
+    assert np.array_equal(R.expert_convert(y, H, I, False), x)
+
+
+def test_write_and_read_rows_relayout(tmp_path):
+    rng = np.random.default_rng(6)
+    H, I, E, L = 256, 256, 3, 2
+    eb = 3 * I * (H // 32) * 18
+    blobs = [_blob(rng, E * eb) for _ in range(L)]
+    idx = R.write_model(tmp_path, blobs, E, 2, H, I, layout="rows")
+    assert idx["version"] == 4 and idx["layout"] == "rows" and idx["dtype"] == "q4_0"
+    rd = R.RelayoutReader(tmp_path)
+    assert rd.layout == "rows" and rd.formats(0) == {k: "q4_0_rows" for k in ("gate", "up", "down")}
+    for l in range(L):
+        for e in range(E):
+            g = blobs[l][e * eb:(e + 1) * eb]
+            assert np.array_equal(rd.expert_blob(l, e), R.expert_convert(g, H, I, True))
+            assert np.array_equal(rd.expert_ggml(l, e), g)
+    rd.close()
+
+
 def test_reads_the_reference_q4_k_index(tmp_path):
     # the reference relayout's own version-2 layout: Q4_K gate/up, Q6_K down (relayout.py:111-157)
     rng = np.random.default_rng(1)
@@ -104,3 +141,35 @@ def test_relayout_round_trip_through_hbm(tmp_path):
     rd.close()
     m.close()
     m2.close()
+
+
+@pytest.mark.gpu
+def test_rows_relayout_loads_without_repack(tmp_path):
+    # the host conversion gives the device repack's bytes: a "rows" relayout copied in
+    # as it is reads back as the original ggml experts and decodes bit for bit alike
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    H, I, E, k, L = 512, 256, 8, 2, 2
+    m, m3 = MoEModel(H, I, E, k, L), MoEModel(H, I, E, k, L)
+    m.fill_synthetic(7)
+    m3.fill_synthetic(8)
+    rng = np.random.default_rng(9)
+    for l in range(L):
+        Rl = (rng.standard_normal((E, H)) * 0.05).astype(np.float32)
+        m.set_router(l, Rl)
+        m3.set_router(l, Rl)
+    blobs = [m.read_experts(l, 0, E) for l in range(L)]
+    R.write_model(tmp_path, blobs, E, k, H, I, layout="rows")
+    rd = R.RelayoutReader(tmp_path)
+    rd.load_into(m3)
+    for l in range(L):
+        assert np.array_equal(m3.read_experts(l, 0, E), blobs[l])
+    X = torch.randn(H, device="cuda")
+    a, b = X.clone(), X.clone()
+    m.decode_step(a, eager=True)
+    m3.decode_step(b, eager=True)
+    torch.cuda.synchronize()
+    assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+    rd.close()
+    m.close()
+    m3.close()

@@ -24,10 +24,14 @@ from ._lib import check
 
 
 class HostTierCache:
-    def __init__(self, model, host_layers, cache_slots: int = 24, staging: int = 2):
+    def __init__(self, model, host_layers, cache_slots: int = 24, staging: int = 2, layout: str = "ggml"):
         """model: an engine.MoEModel (its shape, norms and kernels); host_layers[l]: a
-        pinned uint8 torch tensor holding layer l's E expert blobs (ggml Q4_0,
-        expert-contiguous relayout order)."""
+        pinned uint8 torch tensor holding layer l's E expert blobs (Q4_0,
+        expert-contiguous relayout order) in `layout`: "ggml" blobs are repacked on the
+        device after each copy, "rows" blobs (a version-4 relayout) are copied into their
+        slot as they are."""
+        assert layout in ("ggml", "rows")
+        self.rows = layout == "rows"
         import torch
         self.torch = torch
         self.model = model
@@ -60,10 +64,13 @@ class HostTierCache:
                 continue
             dst = torch.empty(self.eb, dtype=torch.uint8, device=self.slots.device)
             raw = self.host[layer][int(e) * self.eb:(int(e) + 1) * self.eb]
-            self.stage[0].copy_(raw)
-            check(self.lib.tgx_repack_experts(self.model.handle, ctypes.c_void_p(self.stage[0].data_ptr()),
-                                              ctypes.c_void_p(dst.data_ptr()), 1,
-                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), self.lib)
+            if self.rows:
+                dst.copy_(raw)
+            else:
+                self.stage[0].copy_(raw)
+                check(self.lib.tgx_repack_experts(self.model.handle, ctypes.c_void_p(self.stage[0].data_ptr()),
+                                                  ctypes.c_void_p(dst.data_ptr()), 1,
+                                                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), self.lib)
             self.pinned[key] = dst
         torch.cuda.synchronize()
 
@@ -97,10 +104,14 @@ class HostTierCache:
         st = self.stage[self.next_stage]
         self.next_stage = (self.next_stage + 1) % self.n_stage
         with self.torch.cuda.stream(cs):
-            st.copy_(self.host[layer][e * self.eb:(e + 1) * self.eb], non_blocking=True)
-            check(self.lib.tgx_repack_experts(self.model.handle, ctypes.c_void_p(st.data_ptr()),
-                                              ctypes.c_void_p(self.slots[slot].data_ptr()), 1,
-                                              ctypes.c_void_p(cs.cuda_stream)), self.lib)
+            src = self.host[layer][e * self.eb:(e + 1) * self.eb]
+            if self.rows:   # already in the kernels' layout: straight into the slot
+                self.slots[slot].copy_(src, non_blocking=True)
+            else:
+                st.copy_(src, non_blocking=True)
+                check(self.lib.tgx_repack_experts(self.model.handle, ctypes.c_void_p(st.data_ptr()),
+                                                  ctypes.c_void_p(self.slots[slot].data_ptr()), 1,
+                                                  ctypes.c_void_p(cs.cuda_stream)), self.lib)
             self.ready[slot].record(cs)
         self.bytes_h2d += self.eb
         self.lru[key] = slot

@@ -871,6 +871,20 @@ extern "C" int tgx_load_experts(tgx_ctx* ctx, int layer, int first, int n, const
     return TG_OK;
 }
 
+extern "C" int tgx_load_experts_rows(tgx_ctx* ctx, int layer, int first, int n, const void* src,
+                                     int src_on_device) {
+    TG_CHECK(ctx && src, TG_EINVAL, "tgx_load_experts_rows: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers && first >= 0 && n >= 0 && first + n <= ctx->shape.n_experts,
+             TG_EINVAL, "tgx_load_experts_rows: layer/expert range out of bounds");
+    DeviceGuard dg(ctx->device);
+    const Geom& g = ctx->g;
+    uint8_t* dst = ctx->weights + (size_t)layer * ctx->layer_bytes + (size_t)first * g.expert_bytes;
+    TG_CUDA(cudaMemcpyAsync(dst, src, (size_t)n * g.expert_bytes,
+                            src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->s));
+    TG_CUDA(cudaStreamSynchronize(ctx->s));
+    return TG_OK;
+}
+
 extern "C" int tgx_read_experts(tgx_ctx* ctx, int layer, int first, int n, void* dst_host) {
     TG_CHECK(ctx && dst_host, TG_EINVAL, "tgx_read_experts: null argument");
     TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers && first >= 0 && n >= 0 && first + n <= ctx->shape.n_experts,

@@ -68,6 +68,14 @@ class MoEModel:
         assert n * self.expert_bytes == blob.size
         check(self.lib.tgx_load_experts(self._ctx, layer, first, n, blob.ctypes.data, 0), self.lib)
 
+    def load_experts_rows(self, layer: int, blob: np.ndarray, first: int = 0):
+        """blob: experts already in the row-split layout (a version-4 "rows" relayout):
+        copied as they are."""
+        blob = np.ascontiguousarray(blob, dtype=np.uint8)
+        n = blob.size // self.expert_bytes
+        assert n * self.expert_bytes == blob.size
+        check(self.lib.tgx_load_experts_rows(self._ctx, layer, first, n, blob.ctypes.data, 0), self.lib)
+
     def load_experts_device(self, layer: int, ptr: int, n: int, first: int = 0):
         check(self.lib.tgx_load_experts(self._ctx, layer, first, n, ptr, 1), self.lib)
 

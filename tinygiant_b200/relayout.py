@@ -5,16 +5,20 @@ A relayout directory holds one file per MoE layer, `layer_{L:03d}.q4.bin`: the l
 experts in id order, each the raw bytes of its gate | up | down matrices (row-major by
 output row, blocks contiguous per row).  `index.json` describes it:
 
-    magic "NWSMOE01"; version (2 = the reference's Q4_K / Q6_K relayout, 3 = Q4_0);
-    dtype ("q4_k" or "q4_0"); n_layers, n_experts, n_experts_used, embed_dim;
+    magic "NWSMOE01"; version (2 = the reference's Q4_K / Q6_K relayout, 3 = Q4_0 ggml
+    blocks, 4 = Q4_0 in the row-split layout); dtype ("q4_k" or "q4_0"); layout ("ggml"
+    or "rows", versions 3 / 4); n_layers, n_experts, n_experts_used, embed_dim;
     layers[L] = {file, total_bytes, expert_offsets[e] = {offset, sizes{gate, up, down}},
                  tensor_formats{gate, up, down}};
     q4_sizes{gate, up, down} = {out_dim, in_dim}; expert_shapes; activation_profile[L] =
     {expert_ranking, activation_counts} (optional)
 
-The writer here emits version 3 / "q4_0" (the format the HBM decode path runs); the
-reader takes both versions.  Layers are read with pread straight into pinned host memory
-for the host tier (HostTierCache) or copied into a device context.
+The writer emits version 3 (ggml Q4_0 blocks) or, with layout="rows", version 4: every
+matrix row as its blocks' 16-byte nibble groups followed by their fp16 scales, the
+layout the device kernels read, so loads (tgx_load_experts_rows) and host-tier misses
+copy the bytes as they are, with no repack.  The reader takes versions 2 to 4.  Layers
+are read with pread straight into pinned host memory for the host tier (HostTierCache)
+or copied into a device context.
 """
 from __future__ import annotations
 
@@ -29,6 +33,8 @@ from . import _constants as C
 
 MAGIC = "NWSMOE01"
 VERSION_Q4_0 = 3
+VERSION_Q4_0_ROWS = 4
+LAYOUT_GGML, LAYOUT_ROWS = "ggml", "rows"
 EXPERT_KEYS = C.EXPERT_KEYS_ORDER          # gate, up, down
 
 
@@ -38,6 +44,43 @@ def layer_file_name(layer: int) -> str:
 
 def q4_0_matrix_bytes(out_dim: int, in_dim: int) -> int:
     return out_dim * (in_dim // C.QK) * C.Q4_0_BYTES
+
+
+def rows_from_ggml(blocks: np.ndarray, nrows: int, nb: int) -> np.ndarray:
+    """Q4_0 rows of nb ggml blocks (fp16 d | 16 nibble bytes, 18 B each) -> row-split rows:
+    the nb 16-byte nibble groups, then the nb fp16 scales (same bytes per row)."""
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(nrows, nb, C.Q4_0_BYTES)
+    out = np.empty((nrows, nb * C.Q4_0_BYTES), np.uint8)
+    out[:, :nb * 16] = b[:, :, 2:].reshape(nrows, nb * 16)
+    out[:, nb * 16:] = b[:, :, :2].reshape(nrows, nb * 2)
+    return out.reshape(-1)
+
+
+def ggml_from_rows(rows: np.ndarray, nrows: int, nb: int) -> np.ndarray:
+    """The inverse of rows_from_ggml."""
+    r = np.ascontiguousarray(rows, dtype=np.uint8).reshape(nrows, nb * C.Q4_0_BYTES)
+    out = np.empty((nrows, nb, C.Q4_0_BYTES), np.uint8)
+    out[:, :, 2:] = r[:, :nb * 16].reshape(nrows, nb, 16)
+    out[:, :, :2] = r[:, nb * 16:].reshape(nrows, nb, 2)
+    return out.reshape(-1)
+
+
+def _expert_matrices(embed: int, inter: int):
+    """(rows, blocks per row) of gate, up, down."""
+    return ((inter, embed // C.QK), (inter, embed // C.QK), (embed, inter // C.QK))
+
+
+def expert_convert(blob: np.ndarray, embed: int, inter: int, to_rows: bool) -> np.ndarray:
+    """One expert blob gate | up | down between the ggml and row-split layouts."""
+    blob = np.ascontiguousarray(blob, dtype=np.uint8)
+    parts, pos = [], 0
+    for rows, nb in _expert_matrices(embed, inter):
+        n = rows * nb * C.Q4_0_BYTES
+        fn = rows_from_ggml if to_rows else ggml_from_rows
+        parts.append(fn(blob[pos:pos + n], rows, nb))
+        pos += n
+    assert pos == blob.size
+    return np.concatenate(parts)
 
 
 def write_layer(out_dir, layer: int, experts, formats=None) -> dict:
@@ -61,11 +104,14 @@ def write_layer(out_dir, layer: int, experts, formats=None) -> dict:
 
 
 def write_index(out_dir, layers: dict, n_experts: int, n_experts_used: int, embed_dim: int, inter_dim: int,
-                n_layers: int | None = None, activation_profile=None, model: str = "synthetic") -> dict:
+                n_layers: int | None = None, activation_profile=None, model: str = "synthetic",
+                layout: str = LAYOUT_GGML) -> dict:
     """index.json for a Q4_0 relayout (the reference's fields, relayout.py:276-330, with
-    dtype "q4_0" and version 3)."""
+    dtype "q4_0" and version 3, or version 4 with layout "rows")."""
+    assert layout in (LAYOUT_GGML, LAYOUT_ROWS)
     index = {
-        "magic": MAGIC, "version": VERSION_Q4_0, "model": model,
+        "magic": MAGIC, "version": VERSION_Q4_0_ROWS if layout == LAYOUT_ROWS else VERSION_Q4_0,
+        "layout": layout, "model": model,
         "n_layers": n_layers if n_layers is not None else len(layers), "n_experts": n_experts,
         "n_experts_used": n_experts_used, "embed_dim": embed_dim, "dtype": "q4_0",
         "expert_shapes": {"gate": [inter_dim, embed_dim], "up": [inter_dim, embed_dim], "down": [embed_dim, inter_dim]},
@@ -82,9 +128,10 @@ def write_index(out_dir, layers: dict, n_experts: int, n_experts_used: int, embe
 
 
 def write_model(out_dir, layer_blobs, n_experts: int, n_experts_used: int, embed_dim: int, inter_dim: int,
-                activation_profile=None) -> dict:
+                activation_profile=None, layout: str = LAYOUT_GGML) -> dict:
     """A whole Q4_0 relayout from per-layer blobs (E experts, each gate | up | down,
-    ggml Q4_0, expert-contiguous, as tgx_read_experts returns them)."""
+    ggml Q4_0, expert-contiguous, as tgx_read_experts returns them); layout "rows"
+    stores every expert in the row-split layout (version 4)."""
     out_dir = Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
     gb = q4_0_matrix_bytes(inter_dim, embed_dim)
@@ -94,11 +141,16 @@ def write_model(out_dir, layer_blobs, n_experts: int, n_experts_used: int, embed
     for l, blob in enumerate(layer_blobs):
         blob = np.ascontiguousarray(blob, dtype=np.uint8)
         assert blob.size == n_experts * eb
-        experts = [(blob[e * eb:e * eb + gb], blob[e * eb + gb:e * eb + 2 * gb], blob[e * eb + 2 * gb:(e + 1) * eb])
-                   for e in range(n_experts)]
-        layers[l] = write_layer(out_dir, l, experts)
+        experts = []
+        for e in range(n_experts):
+            x = blob[e * eb:(e + 1) * eb]
+            if layout == LAYOUT_ROWS:
+                x = expert_convert(x, embed_dim, inter_dim, True)
+            experts.append((x[:gb], x[gb:2 * gb], x[2 * gb:]))
+        fmt = "q4_0_rows" if layout == LAYOUT_ROWS else "q4_0"
+        layers[l] = write_layer(out_dir, l, experts, {k: fmt for k in EXPERT_KEYS})
     return write_index(out_dir, layers, n_experts, n_experts_used, embed_dim, inter_dim, len(layer_blobs),
-                       activation_profile)
+                       activation_profile, layout=layout)
 
 
 class RelayoutReader:
@@ -112,6 +164,7 @@ class RelayoutReader:
             raise ValueError(f"{self.dir}: not a relayout index (magic {self.index.get('magic')!r})")
         self.version = int(self.index.get("version", 0))
         self.dtype = self.index.get("dtype")
+        self.layout = self.index.get("layout", LAYOUT_ROWS if self.version == VERSION_Q4_0_ROWS else LAYOUT_GGML)
         self.layers = {int(k): v for k, v in self.index["layers"].items()}
         self.n_experts = int(self.index["n_experts"])
         self._maps = {}
@@ -139,6 +192,14 @@ class RelayoutReader:
             out[k] = np.frombuffer(mm, dtype=np.uint8, count=n, offset=pos)
             pos += n
         return out
+
+    def expert_ggml(self, layer: int, e: int) -> np.ndarray:
+        """One Q4_0 expert as a ggml blob, whatever the file's layout."""
+        blob = self.expert_blob(layer, e)
+        if self.layout != LAYOUT_ROWS:
+            return blob
+        return expert_convert(blob, int(self.index["embed_dim"]), int(self.index["q4_sizes"]["gate"]["out_dim"]),
+                              False)
 
     def expert_blob(self, layer: int, e: int) -> np.ndarray:
         info = self.layers[layer]["expert_offsets"][str(e)]
@@ -179,11 +240,15 @@ class RelayoutReader:
         return list(prof["expert_ranking"][:n]) if prof else []
 
     def load_into(self, model) -> None:
-        """Copy every layer into an engine.MoEModel (Q4_0 relayouts only)."""
+        """Copy every layer into an engine.MoEModel (Q4_0 relayouts only); a "rows" file
+        goes in as it is, a ggml one through the device repack."""
         if self.dtype != "q4_0":
             raise ValueError(f"load_into needs a q4_0 relayout, not {self.dtype!r}")
         for layer in sorted(self.layers):
-            model.load_experts(layer, self.layer_bytes(layer))
+            if self.layout == LAYOUT_ROWS:
+                model.load_experts_rows(layer, self.layer_bytes(layer))
+            else:
+                model.load_experts(layer, self.layer_bytes(layer))
 
     def close(self):
         """Drop the mappings; one still viewed by an array handed out stays mapped until
