@@ -68,12 +68,20 @@ def test_argument_errors_without_device():
     sb = lib.tgx_attention_scratch_bytes(32, 4, 128, 64)
     assert lib.tgx_attention_decode(1, p, p, p, p, p, p, p, p, 0, 64, p, p, p, p, 2048, 32, 4, 128, 0, p, sb - 16,
                                     None) == L.TG_EINVAL   # scratch too small
+    ah = ctypes.c_void_p()
+    assert lib.tgx_attn_create(0, 1, 48, 2048, 32, 4, 12, 4096, 1e-6, ctypes.byref(ah)) == L.TG_EINVAL  # head_dim
+    assert lib.tgx_attn_create(0, 1, 0, 2048, 32, 4, 128, 4096, 1e-6, ctypes.byref(ah)) == L.TG_EINVAL   # layers
+    assert lib.tgx_attn_create(0, 1, 48, 2048, 32, 4, 128, 40000, 1e-6, ctypes.byref(ah)) == L.TG_EINVAL  # kv_max
+    assert lib.tgx_decode_token(None, None, None, None, 0) == L.TG_EINVAL
+    assert lib.tgx_attn_set_pos(None, 0) == L.TG_EINVAL
+    assert lib.tgx_load_experts_rows(None, 0, 0, 1, p, 0) == L.TG_EINVAL
     shape = L.TgxShape(2048, 768, 128, 8, 48, 1e-6)
     h = ctypes.c_void_p()
     bad = L.TgxShape(2048, 768, 128, 200, 48, 1e-6)
     assert lib.tgx_ctx_create(0, ctypes.byref(bad), ctypes.byref(h)) == L.TG_EINVAL
     if lib.tg_device_count() == 0:
         assert lib.tgx_ctx_create(0, ctypes.byref(shape), ctypes.byref(h)) == L.TG_ENODEV
+        assert lib.tgx_attn_create(0, 1, 48, 2048, 32, 4, 128, 4096, 1e-6, ctypes.byref(ah)) == L.TG_ENODEV
         xs = np.zeros(64, np.float32)
         assert lib.tg_quantize_q8_0(xs.ctypes.data, out.ctypes.data, 64) == L.TG_ENODEV
         assert lib.tg_expert_forward_mixed(out.ctypes.data, out.ctypes.data, out.ctypes.data, L.TG_FMT_Q6_K,
