@@ -349,6 +349,9 @@ int tgx_kq_prepare(int fmt, const void *src_dev, void *dst_dev, long long rows, 
 /* y_dev[rows] = W . x (tg_matmul_q4k / tg_matmul_q6k / tg_f16_matvec / tg_f32_matvec on
  * device memory; W in device layout, all pointers 16-byte aligned). */
 int tgx_kq_matvec(int fmt, const void *W_dev, const float *x_dev, float *y_dev, int rows, int cols, void *stream);
+/* tg_rms_norm on device memory (x, w, out 16-byte aligned; dim % 4 == 0), e.g. the
+ * final norm before the output projection (engine.py:261-265). */
+int tgx_rms_norm(const float *x_dev, const float *w_dev, float *out_dev, int dim, float eps, void *stream);
 /* Scratch bytes of tgx_kq_experts_forward for n experts (0 for a bad shape). */
 size_t tgx_kq_scratch_bytes(int n, int embed, int inter);
 

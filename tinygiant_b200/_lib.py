@@ -83,6 +83,7 @@ PROTOTYPES = {
     "tgx_attn_status": (CI, [VP, VP]),
     "tgx_attn_kv": (CI, [VP, CI, VP, VP]),
     "tgx_load_experts_rows": (CI, [VP, CI, CI, CI, VP, CI]),
+    "tgx_rms_norm": (CI, [VP, VP, VP, CI, CF, VP]),
     "tgx_attn_read_kv": (CI, [VP, CI, VP, VP]),
     "tgx_attn_layer": (CI, [VP, CI, VP, VP]),
     "tgx_attn_advance": (CI, [VP, VP]),

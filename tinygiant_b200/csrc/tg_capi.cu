@@ -1195,6 +1195,13 @@ extern "C" int tgx_kq_matvec(int fmt, const void* W_dev, const float* x_dev, flo
     return TG_OK;
 }
 
+extern "C" int tgx_rms_norm(const float* x_dev, const float* w_dev, float* out_dev, int dim, float eps, void* stream) {
+    TG_CHECK(x_dev && w_dev && out_dev, TG_EINVAL, "tgx_rms_norm: null pointer");
+    TG_CHECK(dim > 0 && dim % 4 == 0, TG_EINVAL, "tgx_rms_norm: dim must be a positive multiple of 4");
+    TG_CUDA(tg::launch_rms_norm_ref(x_dev, w_dev, out_dev, dim, eps, (cudaStream_t)stream));
+    return TG_OK;
+}
+
 extern "C" size_t tgx_kq_scratch_bytes(int n, int embed, int inter) {
     if (n < 1 || n > 65535 || !Geom::valid_dims(embed, inter)) return 0;
     return r256(tg::kq_down_scratch_bytes(n, embed, inter)) + sizeof(float) * (size_t)n * inter;

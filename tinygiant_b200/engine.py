@@ -282,3 +282,94 @@ class AttentionModel:
         then the position moves on; x (cuda f32[embed]) in place."""
         check(self.lib.tgx_decode_token(self._a, moe.handle if moe is not None else None, _dev_ptr(x),
                                         _stream_handle(stream), TGX_EAGER if eager else 0), self.lib)
+
+
+def sample_token(logits: np.ndarray, temperature: float, top_p: float, rng=np.random) -> int:
+    """The reference's choice of the next token (engine.py:344-360, 395-407): the argmax
+    when temperature is 0, else top-p sampling of softmax(logits / temperature): the
+    most probable tokens whose cumulative probability first reaches top_p (plus the one
+    that crosses it), renormalised, drawn with rng.choice (np.random, the reference's
+    generator, by default)."""
+    if temperature <= 0:
+        return int(np.argmax(logits))
+    p = np.exp((logits - np.max(logits)) / temperature)
+    p /= np.sum(p)
+    order = np.argsort(p)[::-1]
+    keep = order[:np.searchsorted(np.cumsum(p[order]), top_p) + 1]
+    q = p[keep]
+    q /= np.sum(q)
+    return int(rng.choice(keep, p=q))
+
+
+class DecodeEngine:
+    """The reference engine's token loop on the device (tinygiant/engine.py:188-266,
+    378-409): the token's embedding row, then for every layer x += attention(x) and the
+    MoE block (one CUDA graph per token, AttentionModel.decode_token), then the final
+    RMSNorm (tg_rms_norm's order) and the output projection (tg_f32_matvec /
+    tg_f16_matvec's order; the reference evaluates it with numpy, equal within fp32
+    rounding).  Positions follow the reference: forward_one_token(token, pos) caches
+    row pos; generate_stream prefills the prompt at 0 .. P-1."""
+
+    def __init__(self, moe: MoEModel, attn: AttentionModel, token_embd, output_norm, output_weight,
+                 eps: float = C.RMS_EPS):
+        import torch
+        assert moe.embed == attn.embed and moe.n_layers == attn.n_layers
+        assert token_embd.is_cuda and token_embd.dtype == torch.float32 and token_embd.dim() == 2
+        assert output_weight.is_cuda and output_weight.dtype in (torch.float32, torch.float16)
+        self.torch, self.lib, self.moe, self.attn = torch, moe.lib, moe, attn
+        self.embd, self.norm, self.head = token_embd.contiguous(), output_norm.contiguous(), output_weight.contiguous()
+        self.vocab, self.embed, self.eps = token_embd.shape[0], moe.embed, float(eps)
+        assert self.head.shape == (self.vocab, self.embed) and self.norm.shape == (self.embed,)
+        self.fmt = 1 if self.head.dtype == torch.float16 else 4   # tg_f16_matvec / tg_f32_matvec
+        dev = token_embd.device
+        self.x = torch.empty(self.embed, dtype=torch.float32, device=dev)
+        self.normed = torch.empty(self.embed, dtype=torch.float32, device=dev)
+        self.logits = torch.empty(self.vocab, dtype=torch.float32, device=dev)
+        self.next_pos = None
+
+    @classmethod
+    def synthetic(cls, moe: MoEModel, attn: AttentionModel, vocab: int, seed: int, head_f16: bool = True):
+        """Random embeddings and output weights N(0, 0.02), output norm weights 1."""
+        import torch
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        dev = torch.device("cuda", moe.device)
+        embd = torch.randn(vocab, moe.embed, generator=gen, device=dev) * 0.02
+        head = torch.randn(vocab, moe.embed, generator=gen, device=dev) * 0.02
+        return cls(moe, attn, embd, torch.ones(moe.embed, device=dev), head.half() if head_f16 else head)
+
+    def reset(self):
+        """A new sequence (engine.py:143-151): the caches are empty again."""
+        self.attn.reset(0)
+        self.next_pos = 0
+
+    def forward_one_token(self, token_id: int, pos: int, stream=None):
+        """Logits [vocab] (a cuda tensor, overwritten by the next call) of token_id at pos."""
+        if pos != self.next_pos:
+            self.attn.reset(pos)
+        s = _stream_handle(stream)
+        self.x.copy_(self.embd[int(token_id)])
+        self.attn.decode_token(self.x, self.moe, stream)
+        check(self.lib.tgx_rms_norm(_dev_ptr(self.x), _dev_ptr(self.norm), _dev_ptr(self.normed), self.embed,
+                                    self.eps, s), self.lib)
+        check(self.lib.tgx_kq_matvec(self.fmt, self.head.data_ptr(), _dev_ptr(self.normed), _dev_ptr(self.logits),
+                                     self.vocab, self.embed, s), self.lib)
+        self.next_pos = pos + 1
+        return self.logits
+
+    def generate_stream(self, prompt_tokens, n_tokens: int = 128, temperature: float = 0.7, top_p: float = 0.9,
+                        rng=np.random):
+        """Yield n_tokens generated after the prompt (engine.py:378-409): greedy on the
+        device when temperature is 0, else sample_token on the host."""
+        logits = None
+        for i, tok in enumerate(prompt_tokens):
+            logits = self.forward_one_token(tok, i)
+        nxt = None
+        for step in range(n_tokens):
+            pos = len(prompt_tokens) + step
+            if step > 0:
+                logits = self.forward_one_token(nxt, pos - 1)
+            if temperature <= 0:
+                nxt = int(self.torch.argmax(logits).item())
+            else:
+                nxt = sample_token(logits.cpu().numpy(), temperature, top_p, rng)
+            yield nxt
