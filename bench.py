@@ -85,6 +85,9 @@ def parse():
                     help="whole decode layers: the reference's attention step (Q4_K / f16 weights, fp32 KV cache) "
                          "then the MoE block, 48 layers per token in one CUDA graph")
     ap.add_argument("--pos", type=int, default=1024, help="--attention: rows already cached when timing starts")
+    ap.add_argument("--head", action="store_true",
+                    help="--attention: whole tokens (engine.DecodeEngine): embedding row, the layers, final RMSNorm "
+                         "and the f16 output projection over the Qwen3 vocabulary")
     ap.add_argument("--format", choices=["q4_0", "q4_k", "q4_k_m"], default="q4_0",
                     help="q4_k / q4_k_m: the reference library's own formats (all-Q4_K experts, or Q4_K "
                          "gate/up with Q6_K down), expert FFN of 48 layers x top-8 per token")
@@ -765,10 +768,22 @@ def run_layers(args):
     X = torch.randn(K + W, H, generator=gen, device="cuda", dtype=torch.float32)
     x = torch.empty(H, device="cuda", dtype=torch.float32)
     s = torch.cuda.current_stream()
+    eng = None
+    if args.head:   # whole tokens: embedding row, the layers, final norm, output projection
+        from tinygiant_b200.engine import DecodeEngine
+        eng = DecodeEngine.synthetic(moe, am, C.VOCAB_SIZE, args.seed + 97 + rank)
+        toks = np.random.default_rng(args.seed + rank).integers(0, C.VOCAB_SIZE, K + W)
+
+    def step(i):   # token i of the run, at position P0 + i
+        if eng is not None:
+            eng.forward_one_token(int(toks[i]), P0 + i, s)
+        else:
+            am.decode_token(x, moe, s)
+
     am.reset(P0)
     for i in range(W):
         x.copy_(X[i])
-        am.decode_token(x, moe, s)
+        step(i)
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -783,7 +798,7 @@ def run_layers(args):
     for i in range(K):
         x.copy_(X[W + i])
         ks[i].record(s)
-        am.decode_token(x, moe, s)
+        step(W + i)
         ke[i].record(s)
     ev1.record(s)
     torch.cuda.synchronize()
@@ -797,13 +812,19 @@ def run_layers(args):
     Xh = X.cpu().pin_memory()
     Yh = torch.empty_like(Xh).pin_memory()
     am.reset(P0 + W)
+    if eng is not None:
+        eng.next_pos = P0 + W
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
     for i in range(K):
-        x.copy_(Xh[W + i], non_blocking=True)
-        am.decode_token(x, moe, s)
-        Yh[W + i].copy_(x, non_blocking=True)
+        if eng is not None:   # the greedy token loop: the chosen token read back every step
+            eng.forward_one_token(int(toks[W + i]), P0 + W + i, s)
+            int(torch.argmax(eng.logits).item())
+        else:
+            x.copy_(Xh[W + i], non_blocking=True)
+            am.decode_token(x, moe, s)
+            Yh[W + i].copy_(x, non_blocking=True)
     e1.record(s)
     torch.cuda.synchronize()
     ems = e0.elapsed_time(e1)
@@ -818,6 +839,8 @@ def run_layers(args):
     seq_mean = P0 + W + (K + 1) / 2.0                       # rows attended, averaged over the timed tokens
     kv_read = 2 * NKV * HD * 4 * seq_mean
     alg = NL * (attn_w + kv_read + K_TOP * EXPERT_BYTES)
+    if eng is not None:
+        alg += C.VOCAB_SIZE * H * 2 + H * 4                 # the f16 output projection, the embedding row
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
@@ -855,13 +878,17 @@ def run_layers(args):
     achieved = alg / (tok_ms / 1000.0) / 1e9
     if rank == 0:
         emit({
-            "metric": "decode tok/s, whole layers (attention + MoE, Qwen3-30B-A3B shape)",
+            "metric": ("decode tok/s, whole tokens (embedding, attention + MoE layers, output projection, "
+                       "Qwen3-30B-A3B shape)") if eng is not None else
+                      "decode tok/s, whole layers (attention + MoE, Qwen3-30B-A3B shape)",
             "value": ws * K / (ms / 1000.0), "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"{NL} decode layers per token: attention (Q4_K / f16, fp32 KV cache, "
                                    f"positions {P0 + W}..{P0 + W + K - 1}) then the MoE block (top-{K_TOP} of {E} "
-                                   f"Q4_0 experts)", "hidden": H, "inter": I, "experts": E, "layers": NL,
+                                   f"Q4_0 experts)" + (f"; final RMSNorm and the f16 output projection over "
+                                                       f"{C.VOCAB_SIZE} tokens" if eng is not None else ""),
+                       "hidden": H, "inter": I, "experts": E, "layers": NL,
                        "heads": NH, "kv_heads": NKV, "head_dim": HD, "kv_max": kv_max,
                        "l2": f"inputs larger than L2 ({alg / 1e9:.2f} GB read per token)",
                        "parallelism": "replicas" if ws > 1 else "single GPU"},
@@ -870,12 +897,15 @@ def run_layers(args):
                                                     f"layer) + position advance", "token_ms": tok_ms,
                          "algorithmic_bytes": alg,
                          "algorithmic_bytes_def": "per layer: Q4_K/f16 attention weights + K and V rows read "
-                                                  "(mean position) + Q4_0 bytes of the 8 experts",
+                                                  "(mean position) + Q4_0 bytes of the 8 experts"
+                                                  + ("; + the f16 output matrix and one embedding row per token"
+                                                     if eng is not None else ""),
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback"},
             "cpu_baseline": cpu,
-            "e2e": {"value": ws * K / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": H * 4,
-                    "d2h_bytes_per_step": H * 4},
-            "gpu_launches": (8 * NL + 1) * K,
+            "e2e": {"value": ws * K / (ems / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 0 if eng is not None else H * 4,   # a token id is a host scalar
+                    "d2h_bytes_per_step": 8 if eng is not None else H * 4},  # the greedy token, or x
+            "gpu_launches": (8 * NL + 1 + (3 if eng is not None else 0)) * K,
             "clocks": clocks.summary(),
         })
     am.close()
