@@ -905,7 +905,7 @@ def run_layers(args):
             "e2e": {"value": ws * K / (ems / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 0 if eng is not None else H * 4,   # a token id is a host scalar
                     "d2h_bytes_per_step": 8 if eng is not None else H * 4},  # the greedy token, or x
-            "gpu_launches": (8 * NL + 1 + (3 if eng is not None else 0)) * K,
+            "gpu_launches": (8 * NL + 1 + (2 if eng is not None else 0)) * K,
             "clocks": clocks.summary(),
         })
     am.close()
