@@ -347,7 +347,10 @@ class DecodeEngine:
         if pos != self.next_pos:
             self.attn.reset(pos)
         s = _stream_handle(stream)
-        self.x.copy_(self.embd[int(token_id)])
+        torch = self.torch
+        st = stream if stream is None or isinstance(stream, torch.cuda.Stream) else torch.cuda.ExternalStream(s)
+        with torch.cuda.stream(st):   # the row copy goes on the same stream as the kernels
+            self.x.copy_(self.embd[int(token_id)])
         self.attn.decode_token(self.x, self.moe, stream)
         check(self.lib.tgx_rms_norm(_dev_ptr(self.x), _dev_ptr(self.norm), _dev_ptr(self.normed), self.embed,
                                     self.eps, s), self.lib)
