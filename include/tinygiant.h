@@ -224,7 +224,9 @@ int tgx_decode_step(tgx_ctx *ctx, float *x_dev, void *stream, int flags);
  * buffer in the context on first use of a larger T (cudaMalloc; not during capture). */
 int tgx_moe_batched(tgx_ctx *ctx, int layer, float *x_dev, int T, void *stream);
 
-/* All L MoE blocks for T tokens, layer after layer (tgx_moe_batched for l = 0 .. L-1). */
+/* All L MoE blocks for T tokens, layer after layer (tgx_moe_batched for l = 0 .. L-1).
+ * With the automatic kernel choice and T <= 8, each token runs the fused single-token
+ * step instead (the same bits, faster for few tokens). */
 int tgx_decode_batched(tgx_ctx *ctx, float *x_dev, int T, void *stream);
 /* expert matmul kernels of tgx_moe_batched / tgx_decode_batched: 0 auto (tensor cores,
  * tcgen05, when experts average >= 16 pairs), 1 dp4a, 2 tensor cores; all give the same

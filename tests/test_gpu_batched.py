@@ -88,6 +88,28 @@ def test_tensor_core_and_dp4a_paths_agree_on_many_tokens():
     m.close()
 
 
+def test_few_tokens_take_the_fused_step_with_the_same_bits():
+    # automatic choice at T <= 8 runs the fused single-token step per token; forced dp4a
+    # runs the batched kernels: the same bits (T = 9 takes the batched kernels both ways)
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    H, I, E, k, L = C.EMBED_DIM, C.EXPERT_INTERMEDIATE, C.N_EXPERTS, C.N_EXPERTS_USED, 2
+    m = MoEModel(H, I, E, k, L)
+    m.fill_synthetic(12)
+    assert m.fused_info()[0] > 0
+    for T in (1, 8, 9):
+        X = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda")
+        outs = []
+        for kernels in (0, 1):
+            m.set_batched_kernels(kernels)
+            Xd = X.clone()
+            m.decode_batched(Xd)
+            m.sync_status()
+            outs.append(Xd)
+        assert torch.equal(outs[0].view(torch.int32), outs[1].view(torch.int32)), T
+    m.close()
+
+
 def test_batched_rejects_bad_token_count(oracle):
     import ctypes
     import torch
