@@ -31,8 +31,9 @@ I64 = ctypes.c_int64
 
 
 def build() -> Path:
-    """Compile the oracle with its Makefile (gcc), returning the .so path."""
-    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    """Compile the oracle from its sources with its Makefile (gcc; -B: always, never a
+    stale library), returning the .so path."""
+    subprocess.run(["make", "-s", "-B", "-C", str(HERE)], check=True)
     return LIB_PATH
 
 

@@ -43,9 +43,11 @@ struct tgx_ep {
     int kernels = 0;              // tg::BATCHED_AUTO / _DP4A / _MMA
     cudaStream_t s = nullptr;
     // NVLink exchange (tgx_ep_p2p_*): one region per rank, y[0] | y[1] | flags[G], shared
-    // through CUDA IPC; y[b] holds layer parity b's per-(token, slot) down sums
+    // through CUDA IPC; y[b] receives the per-(token, slot) down sums of the exchange
+    // calls whose epoch (calls exchanged before them) has parity b
     int p2p_T = 0;                // tokens per step the region holds
     uint8_t* region = nullptr;    // this rank's region
+    float* ystage = nullptr;      // this rank's partial sums before the push (local, y_bytes)
     size_t y_bytes = 0, region_bytes = 0;
     void* peers[64] = {};         // opened peer regions (null for this rank)
     float** dst_dev = nullptr;    // [2][G]: rank q's y[b]
@@ -94,7 +96,7 @@ void ep_free(tgx_ep* c) {
     Dev dg(c->device);
     for (int q = 0; q < 64; q++)
         if (c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
-    for (void* p : {(void*)c->region, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err,
+    for (void* p : {(void*)c->region, (void*)c->ystage, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err,
                     (void*)c->p2p_count, (void*)c->owned})
         if (p) cudaFree(p);
     for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
@@ -373,26 +375,35 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 }
 
 // grid = T * ks CTAs, after this rank's partial step on the same stream: CTA i < owned[0]
-// copies the i-th pair this rank computed (its y row, H floats, contiguous) into every
-// peer's buffer with 16-byte stores over NVLink, fenced system-wide; the last CTA to
-// finish publishes the next epoch in this rank's slot of every rank's flags.
+// copies the i-th pair this rank computed (its y row, H floats, contiguous) into buffer
+// b = epoch & 1 of every rank, this one included, with 16-byte stores (over NVLink for
+// the peers), fenced system-wide; the last CTA to finish publishes the next epoch in
+// this rank's slot of every rank's flags.  The buffer follows the call count, not the
+// layer, so consecutive calls alternate buffers for any layer count and under graph
+// replay: a rank stores into buffer b again only after seeing every rank's flag of
+// the call in between, which each rank publishes after its combine of this call.
 __global__ void __launch_bounds__(256) k_ep_push_signal(const int* __restrict__ owned, const float* __restrict__ y,
                                                         float* const* __restrict__ dst, int G, int rank, int H,
                                                         unsigned* count, unsigned* epoch, unsigned* const* flags) {
     const int i = blockIdx.x;
+    // every CTA reads the epoch before its atomicAdd below; the last CTA advances it
+    // only after all of them have added
+    const unsigned b = *(volatile unsigned*)epoch & 1u;
     if (i < owned[0]) {
         const int p = owned[1 + i];
         const float4* src = reinterpret_cast<const float4*>(y + (size_t)p * H);
         for (int q = 0; q < G; q++) {
-            if (q == rank) continue;
-            float4* d = reinterpret_cast<float4*>(dst[q] + (size_t)p * H);
+            float4* d = reinterpret_cast<float4*>(dst[(size_t)b * G + q] + (size_t)p * H);
             for (int c = threadIdx.x; c < H / 4; c += blockDim.x) d[c] = __ldcg(src + c);
         }
         __threadfence_system();
     }
     __syncthreads();
     __shared__ int last;
-    if (threadIdx.x == 0) last = atomicAdd(count, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(count, 1u) == gridDim.x - 1;
+    }
     __syncthreads();
     if (last && threadIdx.x == 0) {
         __threadfence_system();
@@ -403,15 +414,17 @@ __global__ void __launch_bounds__(256) k_ep_push_signal(const int* __restrict__ 
     }
 }
 
-// grid T: wait (bounded) until every rank published this layer's epoch, then
-// x[t] += sum_j w[t][j] * y[(t, j)] in slot order from this rank's buffer.
+// grid T: wait (bounded) until every rank published this call's epoch e, then
+// x[t] += sum_j w[t][j] * y[(t, j)] in slot order from this rank's buffer (e - 1) & 1,
+// the one the push of this call filled.
 __global__ void __launch_bounds__(256) k_ep_combine_p2p(float* __restrict__ X, int H, int ks,
-                                                        const float* __restrict__ wts, const float* y,
-                                                        const unsigned* flags, const unsigned* epoch, int G,
-                                                        unsigned* err) {
+                                                        const float* __restrict__ wts, const uint8_t* region,
+                                                        size_t y_bytes, const unsigned* flags, const unsigned* epoch,
+                                                        int G, unsigned* err) {
     __shared__ int ok;
+    const unsigned e = *(const volatile unsigned*)epoch;
+    const float* y = reinterpret_cast<const float*>(region + (size_t)((e - 1u) & 1u) * y_bytes);
     if (threadIdx.x == 0) {
-        const unsigned e = *epoch;
         int good = 1;
         const long long t0 = clock64();
         for (int q = 0; q < G && good; q++)
@@ -447,6 +460,7 @@ extern "C" int tgx_ep_p2p_init(tgx_ep* ep, int T_max, void* handle_out) {
     ep->y_bytes = ((size_t)T_max * ks * ep->shape.embed * 4 + 255) & ~(size_t)255;
     ep->region_bytes = 2 * ep->y_bytes + 256;
     EP_TRY(ep_alloc((void**)&ep->region, ep->region_bytes, "tgx_ep_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->ystage, ep->y_bytes, "tgx_ep_p2p_init"));
     EP_TRY(ep_alloc((void**)&ep->dst_dev, sizeof(float*) * 2 * ep->size, "tgx_ep_p2p_init"));
     EP_TRY(ep_alloc((void**)&ep->flag_dev, sizeof(unsigned*) * ep->size, "tgx_ep_p2p_init"));
     EP_TRY(ep_alloc((void**)&ep->epoch, 256, "tgx_ep_p2p_init"));
@@ -521,19 +535,18 @@ extern "C" int tgx_ep_moe_layer_p2p(tgx_ep* ep, int layer, float* x_dev, int T, 
     EP_TRY(ep_reserve(ep, T, s, "tgx_ep_moe_layer_p2p"));
     const tgx_shape& sh = ep->shape;
     const size_t nr = (size_t)sh.n_experts * sh.embed;
-    const int b = layer & 1, G = ep->size, ks = sh.top_k + ep->n_shared;
+    const int G = ep->size, ks = sh.top_k + ep->n_shared;
     const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
-    float* y = (float*)(ep->region + (size_t)b * ep->y_bytes);
+    float* y = ep->ystage;
     EP_CUDA(tg::launch_moe_batched_partial(ep->weights + (size_t)layer * ep->layer_bytes, shared, ep->e_lo, ep->e_n,
                                            ep->rank, G, ep->g, ep->routers + (size_t)layer * nr,
                                            ep->norms + (size_t)layer * sh.embed, ep->eps, sh.n_experts, ep->n_shared,
                                            sh.top_k, x_dev, T, ep->scratch, ep->scratch_bytes, y, nullptr, ep->wts,
                                            nullptr, ep->kernels, s, false, ep->owned));
-    k_ep_push_signal<<<T * ks, 256, 0, s>>>(ep->owned, y, ep->dst_dev + (size_t)b * G, G, ep->rank, sh.embed,
-                                            ep->p2p_count, ep->epoch, ep->flag_dev);
+    k_ep_push_signal<<<T * ks, 256, 0, s>>>(ep->owned, y, ep->dst_dev, G, ep->rank, sh.embed, ep->p2p_count,
+                                            ep->epoch, ep->flag_dev);
     EP_CUDA(cudaGetLastError());
-    k_ep_combine_p2p<<<T, 256, 0, s>>>(x_dev, sh.embed, ks, ep->wts,
-                                        (const float*)(ep->region + (size_t)b * ep->y_bytes),
+    k_ep_combine_p2p<<<T, 256, 0, s>>>(x_dev, sh.embed, ks, ep->wts, ep->region, ep->y_bytes,
                                         (const unsigned*)(ep->region + 2 * ep->y_bytes), ep->epoch, G, ep->p2p_err);
     EP_CUDA(cudaGetLastError());
     ep->last_T = T;
