@@ -119,6 +119,21 @@ int tg_attention_decode_q4(const uint8_t *wq_q4, const uint8_t *wk_q4, const uin
                            float *kv_v, int kv_len, int kv_max, const float *rope_cos, const float *rope_sin,
                            const float *input, float *output, int embed_dim, int n_heads, int n_kv_heads,
                            int head_dim, int pos);
+/* One whole decoder layer, csrc/libtinygiant.c:662-702 (registered by _lib.py:65-74):
+ * RMSNorm of x (eps 1e-6) with attn_norm_w, tg_attention_decode (fp32 weights; row
+ * kv_len of kv_k / kv_v is written), x += attention output; RMSNorm with ffn_norm_w,
+ * then the n_active (<= 64) experts accumulated from zero in order with
+ * tg_expert_forward_mixed (gate_ptrs[e], up_ptrs[e], down_ptrs[e], down format
+ * down_is_f16[e]: 0 Q4_K, 1 f16, 2 Q6_K, 3 Q4_0, weight expert_weights[e]), x += that
+ * sum.  x is updated in place.  The reference's routing stays with the caller, as in
+ * the reference. */
+int tg_transformer_layer(const float *wq, const float *wk, const float *wv, const float *wo,
+                         const float *attn_norm_w, const float *q_norm_w, const float *k_norm_w,
+                         const float *ffn_norm_w, float *kv_k, float *kv_v, int kv_len, int kv_max,
+                         const float *rope_cos, const float *rope_sin, const uint8_t **gate_ptrs,
+                         const uint8_t **up_ptrs, const void **down_ptrs, const int *down_is_f16,
+                         const float *expert_weights, int n_active, float *x, int embed_dim, int inter_dim,
+                         int n_heads, int n_kv_heads, int head_dim, int pos);
 /* output += weight * expert(input) of one all-Q4_K blob gate | up | down,
  * csrc/libtinygiant.c:555-595 (_lib.py:39). */
 int tg_expert_forward(const uint8_t *q4_data, const float *input, float *output, float weight,
@@ -145,6 +160,9 @@ int tg_moe_forward_q4_0(const uint8_t **expert_ptrs, const float *weights, int n
  * per device, so an expert needing more (expert bytes rounded up to 256, + 40 * inter/32
  * + 256) is rejected with TG_EINVAL.  The first call on each device sets that scratch
  * up (symbol address, one synchronous copy): make it before any stream capture.
+ * That set-up is kept for the life of the process: after a cudaDeviceReset of a device
+ * the stored address and table are stale, so do not call this entry point on that
+ * device again in the same process.
  * Calls overlapping in time on one device share the scratch and race; order them. */
 int tg_expert_forward_q4_0_noalloc(const uint8_t *q4_data, const float *input, float *output, float weight,
                                    int embed_dim, int inter_dim, void *stream);
@@ -249,6 +267,20 @@ int tgx_repack_experts(tgx_ctx *ctx, const void *raw_dev, void *dst_dev, int n, 
  * fused decode kernel expired since the last call (TG_ETIMEOUT; the kernel's
  * cross-block state is then reset).  TG_OK otherwise. */
 int tgx_sync_status(tgx_ctx *ctx);
+
+/* Limit of every bounded wait inside the fused decode kernel, in SM cycles (0: the
+ * default, 2e9, about one second at the B200's clock; else >= 1000).  A wait that runs
+ * out makes the kernel record the failure and return; tgx_sync_status then reports
+ * TG_ETIMEOUT and resets the kernel's state, and the context stays usable.  Applies to
+ * launches made after the call (the context's captured decode graph is dropped and
+ * recaptured); graphs captured elsewhere keep the limit they were captured with. */
+int tgx_set_wait_limit(tgx_ctx *ctx, long long cycles);
+
+/* Failure injection for tests, on the host: the fused kernel's launches after this
+ * call wait for n (0..16) router-sum contributions that no block sends, as if n blocks
+ * never arrived, so its first routing wait runs out at the wait limit.  n = 0 restores
+ * normal operation.  Nothing faults: see tgx_set_wait_limit. */
+int tgx_fused_inject_missing(tgx_ctx *ctx, int n);
 
 /* Diagnostics of the fused path: its control words (epoch, finished blocks, error
  * stage, error detail = (layer << 20) | (entry << 8) | observed count) and the first

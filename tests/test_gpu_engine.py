@@ -22,6 +22,7 @@ class OracleEngine:
         E, NH, NKV, HD, I, k, KVM = shape
         self.caches = [(np.zeros((NKV, KVM, HD), np.float32), np.zeros((NKV, KVM, HD), np.float32))
                        for _ in layers]
+        self.routes = []   # (layer, top-k ids) of every MoE block evaluated
 
     def forward(self, token, pos):
         o, (E, NH, NKV, HD, I, k, KVM) = self.o, self.shape
@@ -32,7 +33,8 @@ class OracleEngine:
             att = o.attention_decode(True, *W, qn, kn, self.caches[l][0], self.caches[l][1], pos, self.cos, self.sin,
                                      normed, E, NH, NKV, HD, pos, TG_MIRROR)
             x = (x + att).astype(np.float32)
-            x = o.moe_block(blobs[l], Rs[l], x, k, E, I, normw=norms[l])[0]
+            x, idx = o.moe_block(blobs[l], Rs[l], x, k, E, I, normw=norms[l])[:2]
+            self.routes.append((l, idx))
         final = o.rms_norm_k(x, self.onorm, 1e-6)
         return o.matvec_k(self.head, self.head_fmt, final, self.head.shape[0], E)
 
@@ -110,5 +112,40 @@ def test_generate_stream_greedy_and_sampled(oracle):
     sampled = list(eng.generate_stream(prompt, n_tokens=4, temperature=0.8, top_p=0.9,
                                        rng=np.random.RandomState(7)))
     assert sampled == ref_s.generate(prompt, 4, 0.8, 0.9, np.random.RandomState(7))
+    am.close()
+    m.close()
+
+
+def test_calibrate_and_pin_experts(oracle):
+    """engine.py:154-186 on the device: calibrate() counts every layer's routing of the
+    prompt and the greedy tokens (the oracle's routing of the same tokens), then
+    pin_experts() pins each layer's most requested experts in a host-tier cache."""
+    import torch
+    from tinygiant_b200.cache import HostTierCache
+    eng, ref, m, am = _build(oracle, False)
+    prompt = [3, 141, 59]
+    eng.reset()
+    counts = eng.calibrate(prompt, n_tokens=2)
+    # the oracle's routing of the same tokens: the prompt, then two greedy steps
+    logits = None
+    for i, t in enumerate(prompt):
+        logits = ref.forward(t, i)
+    nxt = int(np.argmax(logits))
+    for step in range(2):
+        logits = ref.forward(nxt, len(prompt) + step)
+        nxt = int(np.argmax(logits))
+    want = {}
+    for l, idx in ref.routes:
+        for e in idx:
+            want[(l, int(e))] = want.get((l, int(e)), 0) + 1
+    assert counts == want
+    host = [torch.from_numpy(m.read_experts(l, 0, m.n_experts)).pin_memory() for l in range(m.n_layers)]
+    cache = HostTierCache(m, host, cache_slots=4)
+    eng.reset()
+    n = eng.pin_experts(cache, 2, calibrate_tokens=2, prompt_tokens=prompt)
+    assert n == 2 * m.n_layers and cache.access_counts == {}
+    for l in range(m.n_layers):
+        top = sorted((-c, e) for (ll, e), c in want.items() if ll == l)[:2]
+        assert all((l, e) in cache.pinned for _, e in top)
     am.close()
     m.close()

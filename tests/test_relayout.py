@@ -106,6 +106,14 @@ def test_rejects_foreign_directories(tmp_path):
         R.RelayoutReader(tmp_path)
 
 
+@pytest.mark.parametrize("version", [0, 1, 5, 99])
+def test_rejects_unknown_versions(tmp_path, version):
+    (tmp_path / "index.json").write_text(json.dumps({"magic": R.MAGIC, "version": version, "layers": {},
+                                                    "n_experts": 8}))
+    with pytest.raises(ValueError, match="version"):
+        R.RelayoutReader(tmp_path)
+
+
 @pytest.mark.gpu
 def test_relayout_round_trip_through_hbm(tmp_path):
     # a model's experts written as a relayout, read back (mmap and pinned pread) into a

@@ -1,7 +1,8 @@
 """tg_expert_forward_q4_0_noalloc: the expert forward on device pointers with a
 fixed static scratch, checked against tg_expert_forward_q4_0 (the host-pointer
-entry point) on two calls in a row.  Collected last, so it also runs after every
-other test in the same process; it must pass alone in a fresh process too."""
+entry point) and against the CPU oracle on two calls in a row.  Collected last, so
+it also runs after every other test in the same process; it must pass alone in a
+fresh process too."""
 import ctypes
 
 import numpy as np
@@ -52,6 +53,9 @@ def test_noalloc_matches_host_entry_point_twice(lib, oracle):
         stream.synchronize()
         got = d_out.cpu().numpy()
         assert np.array_equal(got, want), (H, I, float(np.max(np.abs(got - want))))
+        # and, independently of the other CUDA path, the oracle's mirror order
+        ref = oracle.expert_forward(blob, x, out0.copy(), wt, H, I, 1)
+        assert np.array_equal(got, ref), (H, I, float(np.max(np.abs(got - ref))))
 
 
 @pytest.mark.gpu

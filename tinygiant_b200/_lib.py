@@ -73,6 +73,7 @@ PROTOTYPES = {
     "tg_rms_norm": (CI, [VP, VP, VP, CI, CF]),
     "tg_attention_decode": (CI, [VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP, CI, CI, CI, CI, CI]),
     "tg_attention_decode_q4": (CI, [VP, VP, VP, VP, VP, VP, VP, VP, CI, CI, VP, VP, VP, VP, CI, CI, CI, CI, CI]),
+    "tg_transformer_layer": (CI, [VP] * 10 + [CI, CI] + [VP] * 7 + [CI, VP] + [CI] * 6),
     "tgx_attention_scratch_bytes": (SZ, [CI, CI, CI, CI]),
     "tgx_attn_create": (CI, [CI, CI, CI, CI, CI, CI, CI, CI, CF, VP]),
     "tgx_attn_destroy": (CI, [VP]),
@@ -137,6 +138,8 @@ PROTOTYPES = {
     "tgx_experts_forward": (CI, [VP, CI, VP, VP, CI, VP, VP]),
     "tgx_repack_experts": (CI, [VP, VP, VP, CI, VP]),
     "tgx_sync_status": (CI, [VP]),
+    "tgx_set_wait_limit": (CI, [VP, ctypes.c_longlong]),
+    "tgx_fused_inject_missing": (CI, [VP, CI]),
     "tgx_fused_info": (CI, [VP, VP, VP, VP]),
     "tgx_fused_debug": (CI, [VP, VP, VP, SZ]),
     "tgx_fused_trace": (CI, [VP, VP, VP, VP]),

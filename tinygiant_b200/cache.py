@@ -6,10 +6,16 @@ expert is copied into an HBM slot on demand on a side stream, least recently use
 slot first, so the next layer's misses can be fetched while the current layer
 computes.
 
-    cache = HostTierCache(model, host_layers, cache_slots=24)
+    cache = HostTierCache(model, host_layers, cache_slots=24, index=reader.index)
     cache.pin(layer, ids)                    # resident for the cache's lifetime
     cache.prefetch(layer + 1, next_ids)      # start the copies of the misses
     cache.forward(layer, ids, weights, x)    # x += sum_j w_j expert_j(RMSNorm(x) * norm)
+
+The reference's ExpertCache surface is kept: get(layer, eid) counts the access and
+returns the resident expert; pin_hot_experts (the relayout's static activation
+profile), pin_from_usage (calibration counts, then the profile) and pin_nonuniform
+(a per-layer pin count) choose experts exactly as tinygiant/cache.py:72-152 does and
+pin them in HBM.
 
 Device memory of the slots comes from torch; the copies and repacks are ordered
 with CUDA events (a slot is overwritten only after the last kernel reading it)."""
@@ -23,13 +29,51 @@ import numpy as np
 from ._lib import check
 
 
+def select_pins(access_counts: dict, profile: dict, pins_per_layer: dict, n_layers: int):
+    """The experts the reference's pin_from_usage / pin_nonuniform pin
+    (tinygiant/cache.py:84-152), as (layer, expert) pairs in pinning order: per layer,
+    the pins_per_layer[layer] most accessed experts of the calibration counts (ties: the
+    smaller id first), then, while fewer are chosen, the relayout profile's
+    expert_ranking[layer] in its order, skipping experts already chosen."""
+    per_layer = {}
+    for (layer, expert), cnt in access_counts.items():
+        per_layer.setdefault(layer, []).append((-cnt, expert))
+    out = []
+    for layer in range(n_layers):
+        n_pin = pins_per_layer.get(layer, 0)
+        if n_pin <= 0:
+            continue
+        chosen = []
+        for _, e in sorted(per_layer.get(layer, []))[:n_pin]:
+            chosen.append(int(e))
+        if len(chosen) < n_pin and str(layer) in profile:
+            for e in profile[str(layer)]["expert_ranking"]:
+                if len(chosen) >= n_pin:
+                    break
+                if int(e) not in chosen:
+                    chosen.append(int(e))
+        out.extend((layer, e) for e in chosen)
+    return out
+
+
+def select_hot(profile: dict, n_per_layer: int):
+    """The experts the reference's pin_hot_experts pins (tinygiant/cache.py:72-82): the
+    first n of every profiled layer's expert_ranking, layers in numeric order."""
+    out = []
+    for key in sorted(profile.keys(), key=int):
+        out.extend((int(key), int(e)) for e in profile[key]["expert_ranking"][:n_per_layer])
+    return out
+
+
 class HostTierCache:
-    def __init__(self, model, host_layers, cache_slots: int = 24, staging: int = 2, layout: str = "ggml"):
+    def __init__(self, model, host_layers, cache_slots: int = 24, staging: int = 2, layout: str = "ggml",
+                 index: dict | None = None):
         """model: an engine.MoEModel (its shape, norms and kernels); host_layers[l]: a
         pinned uint8 torch tensor holding layer l's E expert blobs (Q4_0,
         expert-contiguous relayout order) in `layout`: "ggml" blobs are repacked on the
         device after each copy, "rows" blobs (a version-4 relayout) are copied into their
-        slot as they are."""
+        slot as they are.  index: the relayout's index.json (its activation_profile feeds
+        pin_hot_experts and the backfill of pin_from_usage / pin_nonuniform)."""
         assert layout in ("ggml", "rows")
         self.rows = layout == "rows"
         import torch
@@ -51,6 +95,8 @@ class HostTierCache:
         self.lru: OrderedDict = OrderedDict()   # (layer, expert) -> slot, oldest first
         self.pinned = {}                        # (layer, expert) -> device tensor (row-split)
         self.hits = self.misses = self.pinned_hits = 0
+        self.access_counts = {}                 # (layer, expert) -> requests, as the reference counts them
+        self.index = index or {}
         self.bytes_h2d = 0
         self.prefetched = set()   # loaded by prefetch, not yet requested: a miss when requested
 
@@ -67,12 +113,69 @@ class HostTierCache:
             if self.rows:
                 dst.copy_(raw)
             else:
+                # the staging ring belongs to the copy stream (_load): wait until it is done
+                # with every slot before this stream reuses one
+                torch.cuda.current_stream().wait_stream(self.copy_stream)
                 self.stage[0].copy_(raw)
                 check(self.lib.tgx_repack_experts(self.model.handle, ctypes.c_void_p(self.stage[0].data_ptr()),
                                                   ctypes.c_void_p(dst.data_ptr()), 1,
                                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), self.lib)
             self.pinned[key] = dst
         torch.cuda.synchronize()
+
+    def _pin_pairs(self, pairs) -> int:
+        by_layer = {}
+        for layer, e in pairs:
+            if layer < len(self.host):
+                by_layer.setdefault(layer, []).append(e)
+        for layer, ids in by_layer.items():
+            self.pin(layer, ids)
+        return sum(len(v) for v in by_layer.values())
+
+    def pin_hot_experts(self, n_per_layer: int) -> int:
+        """tinygiant/cache.py:72-82: pin the top n_per_layer experts of every layer by the
+        relayout's static activation profile; resets the hit counters; returns the count."""
+        profile = self.index.get("activation_profile")
+        if not profile:
+            return 0
+        count = self._pin_pairs(select_hot(profile, n_per_layer))
+        self.hits = self.misses = self.pinned_hits = 0
+        return count
+
+    def pin_from_usage(self, n_per_layer: int, n_layers: int) -> int:
+        """tinygiant/cache.py:84-113: pin each layer's n_per_layer most requested experts
+        since the last reset (calibration), backfilled from the static profile; resets
+        the hit counters and the request counts; returns the count."""
+        return self.pin_nonuniform({layer: n_per_layer for layer in range(n_layers)}, n_layers)
+
+    def pin_nonuniform(self, pins_per_layer: dict, n_layers: int) -> int:
+        """tinygiant/cache.py:115-152: pin pins_per_layer[layer] experts per layer, from
+        the request counts first and the static profile after; resets the counters."""
+        pairs = select_pins(self.access_counts, self.index.get("activation_profile", {}), pins_per_layer, n_layers)
+        count = self._pin_pairs(pairs)
+        self.hits = self.misses = self.pinned_hits = 0
+        self.access_counts = {}
+        return count
+
+    def record(self, layer: int, ids):
+        """Count requests of experts `ids` of `layer` without loading them (calibration
+        from routing decided elsewhere)."""
+        for e in ids:
+            key = (layer, int(e))
+            self.access_counts[key] = self.access_counts.get(key, 0) + 1
+
+    def get(self, layer: int, expert_id: int):
+        """The reference's ExpertCache.get (tinygiant/cache.py:154-160): count the request
+        and return the expert, resident in HBM (a uint8 cuda tensor in the kernels'
+        row-split layout).  The current stream is made to wait for its copy.  A slot's
+        expert stays valid until a later request evicts it; a pinned one for the cache's
+        lifetime."""
+        ptrs, slots = self.resident(layer, [expert_id])
+        key = (layer, int(expert_id))
+        if key in self.pinned:
+            return self.pinned[key]
+        self.torch.cuda.current_stream().wait_event(self.ready[slots[0]])
+        return self.slots[slots[0]]
 
     def pin_from_profile(self, reader, n_per_layer: int) -> int:
         """Pin each layer's n most active experts by the relayout's activation profile
@@ -132,6 +235,8 @@ class HostTierCache:
         protect = set(keys)
         ptrs, slots = [], []
         for key in keys:
+            if count:
+                self.access_counts[key] = self.access_counts.get(key, 0) + 1
             if key in self.pinned:
                 self.pinned_hits += count
                 self.hits += count

@@ -6,6 +6,7 @@
 // tgx_* : a context that owns an L x E expert model and L routers in HBM and
 //         runs the routed MoE decode on caller streams.
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <sys/mman.h>
 #include <cerrno>
 #include <unistd.h>
@@ -512,6 +513,42 @@ extern "C" int tg_expert_forward_mixed(const uint8_t* gate_q4, const uint8_t* up
                            inter_dim, 1, "tg_expert_forward_mixed");
 }
 
+// One whole decoder layer on host buffers, csrc/libtinygiant.c:662-702: RMSNorm (eps
+// 1e-6), the fp32-weight attention step (appending row kv_len of the caches), x += attn;
+// RMSNorm with the FFN weight, then the n_active experts accumulated into a zeroed
+// moe_out in order with tg_expert_forward_mixed (down format down_is_f16[e]: 0 Q4_K,
+// 1 f16, 2 Q6_K, 3 Q4_0), x += moe_out.  The same calls in the same order as the
+// reference, each on the GPU; the two residual adds are single fp32 additions per
+// element on the host buffers.
+extern "C" int tg_transformer_layer(const float* wq, const float* wk, const float* wv, const float* wo,
+                                    const float* attn_norm_w, const float* q_norm_w, const float* k_norm_w,
+                                    const float* ffn_norm_w, float* kv_k, float* kv_v, int kv_len, int kv_max,
+                                    const float* rope_cos, const float* rope_sin, const uint8_t** gate_ptrs,
+                                    const uint8_t** up_ptrs, const void** down_ptrs, const int* down_is_f16,
+                                    const float* expert_weights, int n_active, float* x, int embed_dim,
+                                    int inter_dim, int n_heads, int n_kv_heads, int head_dim, int pos) {
+    TG_CHECK(wq && wk && wv && wo && attn_norm_w && q_norm_w && k_norm_w && ffn_norm_w && kv_k && kv_v && rope_cos &&
+                 rope_sin && x,
+             TG_EINVAL, "tg_transformer_layer: null pointer");
+    TG_CHECK(n_active >= 0 && n_active <= 64, TG_EINVAL, "tg_transformer_layer: 0 <= n_active <= 64");
+    TG_CHECK(n_active == 0 || (gate_ptrs && up_ptrs && down_ptrs && down_is_f16 && expert_weights), TG_EINVAL,
+             "tg_transformer_layer: null expert table");
+    TG_CHECK(embed_dim > 0 && embed_dim % 4 == 0, TG_EINVAL, "tg_transformer_layer: embed_dim must be a positive "
+                                                             "multiple of 4");
+    std::vector<float> normed(embed_dim), part(embed_dim);
+    TG_TRY(tg_rms_norm(x, attn_norm_w, normed.data(), embed_dim, 1e-6f));
+    TG_TRY(tg_attention_decode(wq, wk, wv, wo, q_norm_w, k_norm_w, kv_k, kv_v, kv_len, kv_max, rope_cos, rope_sin,
+                               normed.data(), part.data(), embed_dim, n_heads, n_kv_heads, head_dim, pos));
+    for (int i = 0; i < embed_dim; i++) x[i] = x[i] + part[i];
+    TG_TRY(tg_rms_norm(x, ffn_norm_w, normed.data(), embed_dim, 1e-6f));
+    std::fill(part.begin(), part.end(), 0.0f);
+    for (int e = 0; e < n_active; e++)
+        TG_TRY(tg_expert_forward_mixed(gate_ptrs[e], up_ptrs[e], down_ptrs[e], down_is_f16[e], normed.data(),
+                                       part.data(), expert_weights[e], embed_dim, inter_dim));
+    for (int i = 0; i < embed_dim; i++) x[i] = x[i] + part[i];
+    return TG_OK;
+}
+
 extern "C" int tg_moe_forward(const uint8_t** expert_ptrs, const float* weights, int n_experts, const float* input,
                               float* output, int embed_dim, int inter_dim) {
     TG_CHECK(expert_ptrs && weights && input && output, TG_EINVAL, "tg_moe_forward: null pointer");
@@ -741,6 +778,8 @@ int fused_setup(tgx_ctx* c) {
     P.w_out = c->wts;
     P.logits_out = c->logits;
     P.trace = nullptr;
+    P.wait_cycles = tg::FUSED_WAIT_CYCLES;
+    P.missing = 0;
     P.arena_bytes = arena;
     if (tg::fused_smem_layout(P).total > (uint32_t)smem_optin) return TG_OK;
     if ((rc = A((void**)&c->plan, plan.size() * sizeof(uint16_t)))) return rc;
@@ -1088,6 +1127,34 @@ extern "C" int tgx_decode_step(tgx_ctx* ctx, float* x_dev, void* stream, int fla
         gx = x_dev;
     }
     TG_CUDA(cudaGraphLaunch(exec, s));
+    return TG_OK;
+}
+
+// The fused kernel's parameters are baked into the step graph at capture: drop it so
+// the next replay captures the new ones.
+static void drop_fused_graph(tgx_ctx* ctx) {
+    if (ctx->fexec) cudaGraphExecDestroy(ctx->fexec);
+    ctx->fexec = nullptr;
+    ctx->fx = nullptr;
+}
+
+extern "C" int tgx_set_wait_limit(tgx_ctx* ctx, long long cycles) {
+    TG_CHECK(ctx, TG_EINVAL, "tgx_set_wait_limit: null context");
+    TG_CHECK(cycles == 0 || cycles >= 1000, TG_EINVAL, "tgx_set_wait_limit: cycles must be 0 (default) or >= 1000");
+    DeviceGuard dg(ctx->device);
+    TG_CUDA(cudaDeviceSynchronize());
+    ctx->fp.wait_cycles = cycles ? cycles : tg::FUSED_WAIT_CYCLES;
+    drop_fused_graph(ctx);
+    return TG_OK;
+}
+
+extern "C" int tgx_fused_inject_missing(tgx_ctx* ctx, int n) {
+    TG_CHECK(ctx && n >= 0 && n <= 16, TG_EINVAL, "tgx_fused_inject_missing: 0 <= n <= 16");
+    TG_CHECK(ctx->fused_ok, TG_EUNSUPPORTED, "tgx_fused_inject_missing: fused path not available for this shape");
+    DeviceGuard dg(ctx->device);
+    TG_CUDA(cudaDeviceSynchronize());
+    ctx->fp.missing = n;
+    drop_fused_graph(ctx);
     return TG_OK;
 }
 

@@ -23,8 +23,9 @@
 // order, so results are bit-identical.  No grid-wide barrier and no memory fence
 // sits in the layer loop: every cross-CTA word validates itself.
 //
-// Every wait (mbarrier, tag poll) has a cycle limit; on expiry the kernel records
-// an error in ctl[2..3], drains its own outstanding copies and returns.
+// Every wait (mbarrier, tag poll) has a cycle limit (FusedParams::wait_cycles); on
+// expiry the kernel records an error in ctl[2..3], drains its own outstanding copies
+// and returns.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -42,9 +43,8 @@ constexpr int CW = FUSED_COMPUTE_WARPS;       // compute warps
 constexpr int CT = CW * 32;                   // compute threads
 constexpr int PT = CT;                        // the producer thread (lane 0 of the last warp)
 constexpr unsigned long long CNT_UNIT = 1ull << 56;   // count tag unit in acc words (<= 255 CTAs)
-// Wait limit in SM cycles (~1 s at the B200's 1.9-2 GHz; longer if clocks drop).
-// clock64 is a per-SM counter and cheap to read, unlike %globaltimer.
-constexpr long long WAIT_CYCLES = 2000000000ll;
+// Wait limits are in SM cycles (FusedParams::wait_cycles; clock64 is a per-SM counter
+// and cheap to read, unlike %globaltimer).
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -202,7 +202,7 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 // only (the stage loop), so the layer loop holds one copy of it.
 __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, int nwords, int jlo, int nbI,
                                               uint8_t* hq_base, int ab_i, unsigned tag, unsigned* ctl, int* flags,
-                                              int l) {
+                                              int l, long long limit) {
     const int tid = threadIdx.x;
     unsigned mine = 0, done = 0;
     for (int i = 0; i * NT + tid < nwords; i++) mine |= 1u << i;
@@ -241,7 +241,7 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
         }
         if (done == mine) break;
         if ((++spins & 63) == 0) {
-            if (clock64() - t0 > WAIT_CYCLES) {
+            if (clock64() - t0 > limit) {
                 const int i = __ffs(mine & ~done) - 1, w = i * NT + tid;
                 flags[1] = (l << 20) | (((jlo * nbI + w / 6) & 0xfff) << 8);
                 record_failure(ctl, flags, 4);
@@ -381,7 +381,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         const long long t0 = clock64();
         int spins = 0;
         while (!mbar_try_wait(bar, parity)) {
-            if ((++spins & 255) == 0 && clock64() - t0 > WAIT_CYCLES) {
+            if ((++spins & 255) == 0 && clock64() - t0 > P.wait_cycles) {
                 fail(code);
                 return false;
             }
@@ -534,7 +534,8 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                         } else {
                             // copy a holds the CTAs c with c % FUSED_ACC == a
                             const int a = (w - g.H) / (E + 1);
-                            const unsigned long long want = (unsigned long long)((G - a + FUSED_ACC - 1) / FUSED_ACC);
+                            const unsigned long long want =
+                                (unsigned long long)((G - a + FUSED_ACC - 1) / FUSED_ACC + (a == 0 ? P.missing : 0));
                             const unsigned long long cnt = (v[t] + (1ull << 55)) >> 56;
                             if (cnt == want) {
                                 slog_fx[w - g.H] = (long long)(v[t] - want * CNT_UNIT);
@@ -545,7 +546,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                 }
                 if (done == mine) break;
                 if ((++spins & 63) == 0) {
-                    if (clock64() - t0 > WAIT_CYCLES) {
+                    if (clock64() - t0 > P.wait_cycles) {
                         const int i = __ffs(mine & ~done) - 1, w = i * NT + tid;
                         flags[1] = (l << 20) | (((w < g.H ? w : w - g.H) & 0xfff) << 8) | (w < g.H ? 0xff : 0xfe);
                         fail(2);
@@ -789,7 +790,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         const unsigned long long* hwl = P.hqt + (size_t)l * k * nbI * 6;
         auto gather_h = [&](int jlo, int jhi) -> bool {
             return gather_h_records(hwl + (size_t)jlo * nbI * 6, (jhi - jlo) * nbI * 6, jlo, nbI, hq_base, (int)ab_i,
-                                    tag, P.ctl, flags, l);
+                                    tag, P.ctl, flags, l, P.wait_cycles);
         };
         auto down_partial = [&](int jlo, int jhi) {
             // one row per warp up to 16 rows, else two rows per warp sharing each h block load
@@ -873,13 +874,13 @@ drain:
         const long long t0 = clock64();
         for (int u = 0; u < FUSED_MAX_GU; u++)
             if (pending >> u & 1u)
-                while (!mbar_try_wait(mbar_gu + u, (unsigned)cur_l & 1u) && clock64() - t0 < WAIT_CYCLES) {
+                while (!mbar_try_wait(mbar_gu + u, (unsigned)cur_l & 1u) && clock64() - t0 < P.wait_cycles) {
                 }
         if (pending >> 4 & 1u)
-            while (!mbar_try_wait(mbar_d, (unsigned)cur_l & 1u) && clock64() - t0 < WAIT_CYCLES) {
+            while (!mbar_try_wait(mbar_d, (unsigned)cur_l & 1u) && clock64() - t0 < P.wait_cycles) {
             }
         if (pending >> 5 & 1u)
-            while (!mbar_try_wait(mbar_rt0, 0) && clock64() - t0 < WAIT_CYCLES) {
+            while (!mbar_try_wait(mbar_rt0, 0) && clock64() - t0 < P.wait_cycles) {
             }
     }
     cta_sync();

@@ -24,6 +24,8 @@ constexpr int FUSED_TRACE = 32;
 // router sums are spread over this many accumulator copies (CTA c adds into copy
 // c % FUSED_ACC), so each word takes ~G / FUSED_ACC atomic adds instead of G
 constexpr int FUSED_ACC = 8;
+// default bounded-wait limit in SM cycles (~1 s at the B200's 1.9-2 GHz)
+constexpr long long FUSED_WAIT_CYCLES = 2000000000ll;
 
 struct FusedParams {
     const uint8_t* weights;   // [L][E] row-split experts
@@ -36,6 +38,9 @@ struct FusedParams {
     int max_rows;             // largest down-row range of any CTA
     int k_early;              // > 0: down in two stages, slots [0, k_early) (all their gate/up units
                               // first in their CTAs) before the rest; 0: one stage
+    long long wait_cycles;    // limit of every bounded wait in the kernel, in SM cycles
+    int missing;              // router-sum contributions to wait for that no CTA sends (0; > 0 makes
+                              // the first routing wait run out: the failure path under test)
     const float* x_in;        // hidden state in
     float* x_out;             // hidden state out (may equal x_in when nL >= 2 or every CTA has a gate/up unit)
     unsigned long long* xw;   // [Lmax + 1][H] hidden states between layers: (tag << 32) | f32 bits

@@ -13,6 +13,8 @@
 // partial sums are reduced with an xor butterfly (the oracle's mirror order).
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "tg_device.cuh"
 #include "tg_internal.h"
 
@@ -692,15 +694,27 @@ cudaError_t launch_transpose(const float* in, float* out, int rows, int cols, cu
     return cudaGetLastError();
 }
 
+// The dynamic shared-memory limit of a kernel is one process-wide attribute per
+// device, and contexts and host-pointer calls of different shapes share it: it is only
+// ever raised (per device, behind a mutex), so a smaller shape never lowers it under a
+// larger one that another thread is about to launch.
 cudaError_t prepare_kernels(Geom g, int k) {
-    cudaError_t e;
-    int sm_gu = (int)act_bytes(g.nbH);
-    int sm_d = (int)(act_bytes(g.nbI) * k);
-    int mx = sm_gu > sm_d ? sm_gu : sm_d;
-    if (mx > 48 * 1024) {
-        if ((e = cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_gu)) != cudaSuccess) return e;
-        if ((e = cudaFuncSetAttribute(k_down_combine, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_d)) != cudaSuccess) return e;
-        if ((e = cudaFuncSetAttribute(k_matvec, cudaFuncAttributeMaxDynamicSharedMemorySize, sm_gu)) != cudaSuccess) return e;
+    static std::mutex mu;
+    static int raised[3][64] = {};   // [kernel][device]: the largest limit set so far
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    const int sm_gu = (int)act_bytes(g.nbH);
+    const int sm_d = (int)(act_bytes(g.nbI) * k);
+    const void* fns[3] = {(const void*)k_gateup, (const void*)k_down_combine, (const void*)k_matvec};
+    const int want[3] = {sm_gu, sm_d, sm_gu};
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < 3; i++) {
+        if (want[i] <= 48 * 1024 || want[i] <= raised[i][dev]) continue;
+        if ((e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, want[i])) != cudaSuccess)
+            return e;
+        raised[i][dev] = want[i];
     }
     return cudaSuccess;
 }

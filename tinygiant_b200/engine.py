@@ -129,6 +129,15 @@ class MoEModel:
         """Synchronise; raise if a bounded wait inside the fused kernel expired."""
         check(self.lib.tgx_sync_status(self._ctx), self.lib)
 
+    def set_wait_limit(self, cycles: int = 0):
+        """Limit of every bounded wait in the fused kernel, in SM cycles (0: the default)."""
+        check(self.lib.tgx_set_wait_limit(self._ctx, cycles), self.lib)
+
+    def inject_missing(self, n: int):
+        """Test hook: make the fused kernel wait for n router-sum contributions that never
+        come (n = 0: normal), so its first routing wait runs out."""
+        check(self.lib.tgx_fused_inject_missing(self._ctx, n), self.lib)
+
     def fused_info(self):
         ctas, smem, arena = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
         check(self.lib.tgx_fused_info(self._ctx, ctypes.byref(ctas), ctypes.byref(smem), ctypes.byref(arena)),
@@ -341,6 +350,40 @@ class DecodeEngine:
         """A new sequence (engine.py:143-151): the caches are empty again."""
         self.attn.reset(0)
         self.next_pos = 0
+
+    def calibrate(self, prompt_tokens, n_tokens: int = 10, counts: dict | None = None) -> dict:
+        """engine.py:154-161: run the prompt and n_tokens greedy tokens, then start a new
+        sequence.  Every layer's routing of every token is added to counts[(layer,
+        expert)] (a cache's access_counts, so that pin_from_usage follows it); returns the
+        counts."""
+        counts = {} if counts is None else counts
+
+        def record():
+            for layer in range(self.moe.n_layers):
+                for e in self.moe.last_routing(layer)[0]:
+                    key = (layer, int(e))
+                    counts[key] = counts.get(key, 0) + 1
+
+        logits = None
+        for i, tok in enumerate(prompt_tokens):
+            logits = self.forward_one_token(tok, i)
+            record()
+        nxt = int(self.torch.argmax(logits).item())
+        for step in range(n_tokens):
+            logits = self.forward_one_token(nxt, len(prompt_tokens) + step)
+            record()
+            nxt = int(self.torch.argmax(logits).item())
+        self.reset()
+        return counts
+
+    def pin_experts(self, cache, n_per_layer: int, calibrate_tokens: int | None = None, prompt_tokens=None) -> int:
+        """engine.py:163-186 on a HostTierCache: with calibrate_tokens and prompt_tokens,
+        calibrate into the cache's request counts and pin from usage (backfilled from the
+        relayout profile); else pin the static profile's hot experts.  Returns the count."""
+        if calibrate_tokens and prompt_tokens:
+            self.calibrate(prompt_tokens, n_tokens=calibrate_tokens, counts=cache.access_counts)
+            return cache.pin_from_usage(n_per_layer, self.moe.n_layers)
+        return cache.pin_hot_experts(n_per_layer)
 
     def forward_one_token(self, token_id: int, pos: int, stream=None):
         """Logits [vocab] (a cuda tensor, overwritten by the next call) of token_id at pos."""

@@ -153,8 +153,13 @@ def write_model(out_dir, layer_blobs, n_experts: int, n_experts_used: int, embed
                        activation_profile, layout=layout)
 
 
+SUPPORTED_VERSIONS = (2, VERSION_Q4_0, VERSION_Q4_0_ROWS)
+
+
 class RelayoutReader:
-    """Reads a relayout directory (versions 2 and 3)."""
+    """Reads a relayout directory: version 2 (the reference's writer, Q4_K / Q6_K / f16
+    experts), 3 (Q4_0 ggml blocks) or 4 (Q4_0 in the kernels' row-split rows).  Any other
+    version is rejected, since its byte layout is unknown."""
 
     def __init__(self, path):
         self.dir = Path(path)
@@ -163,6 +168,8 @@ class RelayoutReader:
         if self.index.get("magic") != MAGIC:
             raise ValueError(f"{self.dir}: not a relayout index (magic {self.index.get('magic')!r})")
         self.version = int(self.index.get("version", 0))
+        if self.version not in SUPPORTED_VERSIONS:
+            raise ValueError(f"{self.dir}: relayout version {self.version} is not one of {SUPPORTED_VERSIONS}")
         self.dtype = self.index.get("dtype")
         self.layout = self.index.get("layout", LAYOUT_ROWS if self.version == VERSION_Q4_0_ROWS else LAYOUT_GGML)
         self.layers = {int(k): v for k, v in self.index["layers"].items()}
