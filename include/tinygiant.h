@@ -211,6 +211,14 @@ int tgx_load_experts_rows(tgx_ctx *ctx, int layer, int first, int n, const void 
 /* Read n experts of a layer back as ggml blobs into host memory. */
 int tgx_read_experts(tgx_ctx *ctx, int layer, int first, int n, void *dst_host);
 
+/* out_dev += weight * expert(x_dev) for expert `expert` of layer `layer` held in the
+ * context: tg_expert_forward_q4_0 (csrc/libtinygiant.c:555-595, the reference's
+ * tg_expert_forward) on device memory: Q8_0 of x, gate and up rows, SwiGLU, Q8_0 of h,
+ * down rows, enqueued on `stream`.  The first call allocates a pointer table and an h
+ * buffer in the context. */
+int tgx_expert_forward(tgx_ctx *ctx, int layer, int expert, const float *x_dev, float *out_dev, float weight,
+                       void *stream);
+
 /* Set layer `layer`'s router, R[E][embed] fp32 row-major (engine.py:231 `self.routers[i]`). */
 int tgx_set_router(tgx_ctx *ctx, int layer, const float *R, int src_on_device);
 

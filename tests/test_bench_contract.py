@@ -19,4 +19,8 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference" and d["steps"] == 5 and d["warmup"] == 3
     assert d["value"] > 0 and d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert "workload" in d["config"]
+    # the same config dict as the GPU arm's headline line (bench.headline_config), so the
+    # two arms describe one workload; the pool sample is reported beside it
+    assert set(d["config"]) == {"workload", "hidden", "inter", "experts", "top_k", "layers", "weights",
+                                "hidden_states", "l2", "parallelism"}
+    assert d["config"]["layers"] == 48 and "layers_per_step" in d

@@ -24,12 +24,13 @@ def reflib():
     from tinygiant_b200._lib import find_library
     table = json.loads((ROOT / "tests" / "golden" / "ref_bindings.json").read_text())["functions"]
     lib = ctypes.CDLL(str(find_library()))
-    types = {"c_void_p": ctypes.c_void_p, "c_int": ctypes.c_int, "c_float": ctypes.c_float,
-             "c_size_t": ctypes.c_size_t, "None": None}
+    def ctype(name):   # the recorded ctypes class names (c_size_t is recorded as its alias's name)
+        return None if name == "None" else getattr(ctypes, name)
+
     for name, proto in table.items():
         fn = getattr(lib, name)
-        fn.restype = types[proto["restype"]]
-        fn.argtypes = [types[a] for a in proto["argtypes"]]
+        fn.restype = ctype(proto["restype"])
+        fn.argtypes = [ctype(a) for a in proto["argtypes"]]
     lib.called = set()
     return lib, table
 

@@ -125,8 +125,9 @@ def test_calibrated_pinned_tier_decode(oracle, tmp_path):
     assert cache.pinned_hits > 0 and cache.hits + cache.misses == 6 * L * k
     # get(): the resident expert, counted like a request
     e0 = int(rd.index["activation_profile"]["0"]["expert_ranking"][0])
+    before = cache.access_counts.get((0, e0), 0)
     dev = cache.get(0, e0)
-    assert dev.numel() == m.expert_bytes and cache.access_counts[(0, e0)] == 1
+    assert dev.numel() == m.expert_bytes and cache.access_counts[(0, e0)] == before + 1
     torch.cuda.synchronize()
     file_expert = rd.layer_bytes(0)[e0 * m.expert_bytes:(e0 + 1) * m.expert_bytes]
     assert np.array_equal(dev.cpu().numpy(), R.expert_convert(file_expert, H, I, True))   # the kernels' layout

@@ -138,6 +138,7 @@ PROTOTYPES = {
     "tgx_experts_forward": (CI, [VP, CI, VP, VP, CI, VP, VP]),
     "tgx_repack_experts": (CI, [VP, VP, VP, CI, VP]),
     "tgx_sync_status": (CI, [VP]),
+    "tgx_expert_forward": (CI, [VP, CI, CI, VP, VP, CF, VP]),
     "tgx_set_wait_limit": (CI, [VP, ctypes.c_longlong]),
     "tgx_fused_inject_missing": (CI, [VP, CI]),
     "tgx_fused_info": (CI, [VP, VP, VP, VP]),

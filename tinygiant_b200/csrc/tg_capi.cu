@@ -663,6 +663,8 @@ struct tgx_ctx {
     void* bscratch = nullptr;           // batched path scratch, grown on demand
     size_t bscratch_bytes = 0;
     int batched_kernels = 0;            // tg::BATCHED_AUTO / _DP4A / _MMA
+    const uint8_t** eall = nullptr;     // [L][E] pointers to every expert (tgx_expert_forward)
+    uint8_t* ehq = nullptr;             // its requantised h (one expert)
     // tgx_experts_forward: up to 16 expert pointers and weights, their h blocks, the norm scale
     const uint8_t** lptrs = nullptr;
     float* lwts = nullptr;
@@ -694,7 +696,8 @@ void ctx_free(tgx_ctx* c) {
                     (void*)c->counter, (void*)c->logits,
                     (void*)c->idx, (void*)c->wts, (void*)c->eptrs, (void*)c->hq, (void*)c->staging, (void*)c->RT,
                     (void*)c->xw, (void*)c->xbuf, (void*)c->bscratch, (void*)c->lptrs, (void*)c->lwts,
-                    (void*)c->lhq, (void*)c->lscale, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan})
+                    (void*)c->lhq, (void*)c->lscale, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan,
+                    (void*)c->eall, (void*)c->ehq})
         if (p) cudaFree(p);
     if (c->s) cudaStreamDestroy(c->s);
     delete c;
@@ -888,6 +891,41 @@ extern "C" int tgx_ctx_destroy(tgx_ctx* ctx) {
 }
 
 extern "C" size_t tgx_expert_bytes(const tgx_ctx* ctx) { return ctx ? ctx->g.expert_bytes : 0; }
+
+// out += weight * expert(x) for expert `expert` of layer `layer`, resident in the
+// context: tg_expert_forward_q4_0 (csrc/libtinygiant.c:555-595) on device memory, the
+// gate/up and down kernels of the multi-kernel path with one expert.  The first call
+// allocates the context's table of expert pointers and an h buffer; later calls only
+// enqueue the two kernels on `stream`.
+extern "C" int tgx_expert_forward(tgx_ctx* ctx, int layer, int expert, const float* x_dev, float* out_dev,
+                                  float weight, void* stream) {
+    TG_CHECK(ctx && x_dev && out_dev, TG_EINVAL, "tgx_expert_forward: null argument");
+    TG_CHECK(layer >= 0 && layer < ctx->shape.n_layers && expert >= 0 && expert < ctx->shape.n_experts, TG_EINVAL,
+             "tgx_expert_forward: layer/expert out of range");
+    DeviceGuard dg(ctx->device);
+    const int L = ctx->shape.n_layers, E = ctx->shape.n_experts;
+    if (!ctx->eall) {
+        std::vector<const uint8_t*> ptrs((size_t)L * E);
+        for (size_t i = 0; i < ptrs.size(); i++) ptrs[i] = ctx->weights + i * ctx->g.expert_bytes;
+        const uint8_t** t = nullptr;
+        uint8_t* h = nullptr;
+        if (cudaMalloc((void**)&t, sizeof(void*) * ptrs.size()) != cudaSuccess ||
+            cudaMalloc((void**)&h, tg::act_bytes(ctx->g.nbI)) != cudaSuccess) {
+            cudaGetLastError();
+            if (t) cudaFree((void*)t);
+            return fail(TG_ENOMEM, "tgx_expert_forward: cudaMalloc failed");
+        }
+        TG_CUDA(cudaMemcpy(t, ptrs.data(), sizeof(void*) * ptrs.size(), cudaMemcpyHostToDevice));
+        TG_CUDA(tg::prepare_kernels(ctx->g, 1));
+        ctx->eall = t;
+        ctx->ehq = h;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    const uint8_t* const* ep = ctx->eall + (size_t)layer * E + expert;
+    TG_CUDA(tg::launch_gateup(ep, 1, x_dev, nullptr, nullptr, ctx->g, ctx->ehq, nullptr, nullptr, s));
+    TG_CUDA(tg::launch_down_combine(ep, 1, ctx->ehq, nullptr, weight, ctx->g, nullptr, out_dev, 1, nullptr, s));
+    return TG_OK;
+}
 
 extern "C" int tgx_load_experts(tgx_ctx* ctx, int layer, int first, int n, const void* src, int src_on_device) {
     TG_CHECK(ctx && src, TG_EINVAL, "tgx_load_experts: null argument");

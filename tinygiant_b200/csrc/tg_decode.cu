@@ -72,6 +72,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// The same, but the thread may be suspended (issuing nothing) until the phase
+// completes or about hint_ns pass, so waiting warps leave the issue slots to the warps
+// that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
     asm volatile(
@@ -379,9 +393,8 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     // recorded) when the limit passes
     auto wait_bar = [&](uint64_t* bar, unsigned parity, unsigned code) -> bool {
         const long long t0 = clock64();
-        int spins = 0;
-        while (!mbar_try_wait(bar, parity)) {
-            if ((++spins & 255) == 0 && clock64() - t0 > P.wait_cycles) {
+        while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
+            if (clock64() - t0 > P.wait_cycles) {
                 fail(code);
                 return false;
             }
@@ -908,12 +921,17 @@ int fused_plan(const Geom& g, int E, int k, int G, std::vector<uint16_t>& plan, 
     for (int i = 0; i < g.H % G; i++) rows[order[i]]++;
     plan.assign((size_t)G * FUSED_PLAN, 0);
     arena_bytes = 0;
+    // the arena the units alone need; down rows that fit beside a CTA's units within it
+    // go there (placement 0: copied as soon as the CTA's last unit has landed), the
+    // others into the first unit's space once it is computed (placement 1)
+    size_t cap = 0;
+    for (int c = 0; c < G; c++) cap = std::max(cap, gu[c].size() * gu_b);
     max_rows = 0;
     int lo = 0;
     for (int c = 0; c < G; c++) {
         if ((int)gu[c].size() > FUSED_MAX_GU || rows[c] > FUSED_MAX_ROWS) return -2;
         const size_t down_b = (size_t)rows[c] * k * g.row_d;
-        const int place = (!gu[c].empty() && down_b <= gu_b) ? 1 : 0;
+        const int place = (!gu[c].empty() && down_b <= gu_b && gu[c].size() * gu_b + down_b > cap) ? 1 : 0;
         uint16_t* p = plan.data() + (size_t)c * FUSED_PLAN;
         p[0] = (uint16_t)gu[c].size();
         p[1] = (uint16_t)lo;

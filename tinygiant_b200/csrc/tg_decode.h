@@ -96,9 +96,10 @@ TG_HD FusedSmem fused_smem_layout(const FusedParams& P) {
 
 // Static work split of one layer over G CTAs: gate/up units by longest-processing-
 // time greedy, then contiguous down-row ranges of H/G or H/G + 1 rows (the extra
-// rows to CTAs with fewer units).  A CTA's down rows go into the space of its first
-// gate/up unit once that unit is computed when they fit there (placement 1), else
-// after its units (placement 0, fetched once its last unit has landed).  k_early
+// rows to CTAs with fewer units).  A CTA's down rows go after its units (placement 0,
+// fetched once its last unit has landed) when units and rows together fit the arena
+// the largest unit set needs anyway, else into the space of its first gate/up unit
+// once that unit is computed (placement 1).  k_early
 // counts the leading slots whose units are all first units of their CTAs (their h
 // is complete early).  Returns 0, or < 0 when the shape does not fit the limits.
 int fused_plan(const Geom& g, int E, int k, int G, std::vector<uint16_t>& plan, size_t& arena_bytes,

@@ -99,6 +99,12 @@ class MoEModel:
         check(self.lib.tgx_fill_synthetic(self._ctx, seed, w_sigma, r_sigma), self.lib)
 
     # ---------------------------------------------------------------- compute
+    def expert_forward(self, layer: int, expert: int, x, out, weight: float, stream=None):
+        """out (cuda f32[embed]) += weight * expert(x): one resident expert, the reference's
+        tg_expert_forward on device memory."""
+        check(self.lib.tgx_expert_forward(self._ctx, layer, expert, _dev_ptr(x), _dev_ptr(out), weight,
+                                          _stream_handle(stream)), self.lib)
+
     def moe_layer(self, layer: int, x, stream=None):
         """MoE block `layer` on x (cuda f32[embed]) in place:
         x += sum_j w_j * expert_j(RMSNorm(x) * ffn_norm)."""
