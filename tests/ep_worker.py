@@ -20,7 +20,10 @@ def main() -> int:
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120))
-    H, I, E, K, L, T = 2048, 768, 128, 8, 3, int(os.environ.get("EP_TOKENS", "5"))
+    H, I, E, K, T = 2048, 768, 128, 8, int(os.environ.get("EP_TOKENS", "5"))
+    # an odd layer count and several decodes back to back: consecutive exchange calls must
+    # alternate receive buffers across decode boundaries too
+    L, R = int(os.environ.get("EP_LAYERS", "3")), int(os.environ.get("EP_REPEAT", "1"))
     ok = True
     try:
         ep = EPMoEModel(H, I, E, K, L, rank=rank, size=world, device=local)
@@ -28,22 +31,41 @@ def main() -> int:
         p2p = os.environ.get("EP_P2P", "0") == "1"
         if p2p:
             ep.enable_p2p(64)
-        g = torch.Generator(device="cuda").manual_seed(99)
-        X = torch.randn(T, H, generator=g, device="cuda")           # the same tokens on every rank
-        X0 = X.clone()
-        ep.decode(X)
-        torch.cuda.synchronize()
-        if p2p:
-            ep.p2p_status()
-        same = torch.tensor([1.0], device="cuda")
+        full = None
         if rank == 0:
             full = MoEModel(H, I, E, K, L, device=local)
             full.fill_synthetic(2024)
-            full.decode_batched(X0)
+        same = torch.tensor([1.0], device="cuda")
+        for rep in range(R):
+            g = torch.Generator(device="cuda").manual_seed(99 + rep)
+            X = torch.randn(T, H, generator=g, device="cuda")       # the same tokens on every rank
+            X0 = X.clone()
+            ep.decode(X)
             torch.cuda.synchronize()
-            ok = torch.equal(X.view(torch.int32), X0.view(torch.int32))
+            if p2p:
+                ep.p2p_status()
+            if rank == 0:
+                full.decode_batched(X0)
+                torch.cuda.synchronize()
+                if not torch.equal(X.view(torch.int32), X0.view(torch.int32)):
+                    same[0] = 0.0
+        if full is not None:
             full.close()
-            same[0] = 1.0 if ok else 0.0
+        if p2p and os.environ.get("EP_SKIP") == "1":
+            # rank 1 skips one exchange: rank 0's combine waits for a flag that never comes,
+            # gives up at the wait limit (~1 s) and reports it; nothing faults.  Rank 1 has
+            # no kernel in flight meanwhile, and both meet again in close().
+            from tinygiant_b200._lib import TG_ETIMEOUT, TinyGiantError
+            if rank == 0:
+                Xs = torch.randn(T, H, device="cuda")
+                ep.moe_layer(0, Xs)
+                torch.cuda.synchronize()
+                try:
+                    ep.p2p_status()
+                    same[0] = 0.0                                      # the wait should have run out
+                except TinyGiantError as err:
+                    if err.code != TG_ETIMEOUT:
+                        same[0] = 0.0
         dist.broadcast(same, 0)                                        # every rank takes the same steps
         ok = bool(same.item() == 1.0)
         ep.close()                                                     # disconnect, barrier, free

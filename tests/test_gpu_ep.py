@@ -176,15 +176,20 @@ def test_ep_rejects_foreign_experts():
     ep.close()
 
 
-@pytest.mark.parametrize("p2p", ["0", "1"])
-def test_ep_nccl_matches_single_gpu(p2p):
-    # p2p = 1: the exchange by direct NVLink stores and flags instead of the all-reduce
+@pytest.mark.parametrize("p2p,layers,repeat,skip", [("0", 3, 1, "0"), ("1", 3, 1, "0"), ("1", 3, 4, "0"),
+                                                    ("1", 1, 5, "0"), ("1", 3, 2, "1")])
+def test_ep_nccl_matches_single_gpu(p2p, layers, repeat, skip):
+    # p2p = 1: the exchange by direct NVLink stores and flags instead of the all-reduce;
+    # odd layer counts with several decodes back to back reuse the receive buffers across
+    # decode boundaries
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_P2P=p2p)
+    # skip = 1: afterwards rank 1 skips one exchange and rank 0 must report TG_ETIMEOUT
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_P2P=p2p, EP_LAYERS=str(layers), EP_REPEAT=str(repeat),
+               EP_SKIP=skip)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(p2p)}",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(p2p) + 2 * layers + 16 * repeat + 100 * int(skip)}",
            str(ROOT / "tests" / "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
