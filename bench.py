@@ -12,8 +12,12 @@ HBM (16.3 GB); routers N(0, 0.02); a fresh N(0, 1) hidden state per step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints one JSON line (rank 0).  Under torchrun with N > 1 each rank runs its
-own full model replica (weak scaling); timings are max over ranks.
+Prints one JSON line (rank 0).  Under torchrun with N > 1 the ranks decode the
+same token stream with the experts sharded over them (expert parallelism: rank r
+holds experts [r*128/N, (r+1)*128/N) of every layer, one persistent kernel per rank
+and token, the per-slot down values exchanged over NVLink inside it; strong
+scaling); --replicas instead gives each rank its own full model (weak scaling).
+Timings are max over ranks.
 """
 from __future__ import annotations
 
@@ -59,6 +63,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--multi", action="store_true", help="three kernels per layer instead of the fused kernel")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: every rank decodes its own tokens on its own full model (weak scaling) instead "
+                         "of the expert-parallel decode of one token stream")
     ap.add_argument("--single-expert", action="store_true",
                     help="configs[0]: single-expert Q4_0 FFN forwards (64 distinct resident experts per step)")
     ap.add_argument("--layers", type=int, default=L, help="fewer layers, for small profiling cases only")
@@ -170,14 +177,21 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def headline_config(n_layers: int, ws: int) -> dict:
+def headline_parallelism(ws: int, replicas: bool) -> tuple[str, str]:
+    """(parallelism, scaling) of the headline line at ws ranks."""
+    if ws <= 1:
+        return "single GPU", "weak"
+    return ("replicas", "weak") if replicas else (f"ep{ws}", "strong")
+
+
+def headline_config(n_layers: int, ws: int, replicas: bool = False) -> dict:
     """The workload of the headline line, printed identically by both arms."""
     return {"workload": f"qwen3-30b-a3b moe decode, batch 1, {n_layers} layers (configs[1])",
             "hidden": H, "inter": I, "experts": E, "top_k": K_TOP, "layers": n_layers,
             "weights": f"Q4_0 of N(0,0.02), {n_layers} layers x {E} experts",
             "hidden_states": "fresh N(0,1) per step",
             "l2": "inputs larger than L2 (1.02 GB of Q4 weights read per step)",
-            "parallelism": "replicas" if ws > 1 else "single GPU"}
+            "parallelism": headline_parallelism(ws, replicas)[0]}
 
 
 # ---------------------------------------------------------------- CPU arm
@@ -253,8 +267,9 @@ def run_reference(args):
     out = {
         "metric": METRIC, "value": rate, "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": K, "warmup": W, "ms_per_step": 1000.0 * el / K, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": rate / PUBLISHED_TOKS, "dtype": "int8", "data": "synthetic",
-        "config": headline_config(L, ws),
+        "scaling": headline_parallelism(ws, args.replicas)[1], "vs_baseline": rate / PUBLISHED_TOKS,
+        "dtype": "int8", "data": "synthetic",
+        "config": headline_config(L, ws, args.replicas),
         "layers_per_step": m,
         "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -402,7 +417,7 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
             "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / PUBLISHED_TOKS, "dtype": "int8", "data": "synthetic",
-            "config": headline_config(NL, ws),
+            "config": headline_config(NL, ws, True),
             "path": "fused" if fused else "multi-kernel",
             "residency": f"{NL} x {E} experts resident in HBM ({NL * E * EXPERT_BYTES / 1e9:.1f} GB)",
             "q4_weight_gbs": achieved,
@@ -415,6 +430,170 @@ def run_ours(args):
         emit(out)
     if ws > 1:
         dist.destroy_process_group()
+    return 0
+
+
+def ep_split(stamps: np.ndarray) -> dict:
+    """Per-layer phases of one traced expert-parallel step on one rank, from the kernel's
+    globaltimer stamps ([layers][CTAs][32]), µs after the layer's first routing stamp,
+    median over layers: partial = every CTA has stored its local slots' down values to
+    every rank (routing, gate/up, h exchange, down), exchange = every CTA has received
+    all k slots' values (the NVLink stores and the wait for the slowest rank), combine =
+    every CTA has combined and sent the next layer's router sums."""
+    ns = stamps[:, :, :16].astype(np.int64)
+    t0 = ns[:, :, 0].min(axis=1)
+    part = ns[:, :, 12].max(axis=1) - t0
+    recv = ns[:, :, 13].max(axis=1) - t0
+    done = ns[:, :, 7].max(axis=1) - t0
+    nl = ns.shape[0]
+    layer = np.diff(t0) if nl > 1 else done
+    med = lambda a: float(np.median(a[: max(1, nl - 1)])) / 1000.0
+    return {"layer_us": med(layer), "partial_us": med(part), "exchange_us": med(recv - part),
+            "combine_us": med(done - recv)}
+
+
+def run_ep_fused(args):
+    """N > 1 ranks decode ONE token stream of the configs[1] model together: rank r holds
+    experts [r*E/N, (r+1)*E/N) of every layer (tgx_ep_*), every rank routes every layer,
+    and one persistent kernel per rank and token (tgx_ep_decode_step) computes the local
+    slots and exchanges the per-slot down values over NVLink.  value = tokens of the one
+    stream per second (strong scaling); e2e and the per-layer split as in the one-GPU
+    line."""
+    import torch
+    ws, rank, local = dist_env()
+    args.gpus = ws
+    torch.cuda.set_device(local)
+    dist = init_dist(ws, "nccl")
+    from tinygiant_b200.ep import EPMoEModel
+
+    NL = args.layers
+    model = EPMoEModel(H, I, E, K_TOP, NL, rank=rank, size=ws, device=local)
+    model.fill_synthetic(args.seed)          # one model, sharded: the same seed on every rank
+    model.enable_fused()
+    q4_bytes = NL * K_TOP * EXPERT_BYTES
+    K, W = args.steps, max(3, args.warmup)
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)   # the same tokens on every rank
+    X = torch.randn(K + W, H, generator=gen, device="cuda", dtype=torch.float32)
+    x = torch.empty(H, device="cuda", dtype=torch.float32)
+    stream = torch.cuda.current_stream()
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident timing
+    dist.barrier()
+    for i in range(W):
+        x.copy_(X[i])
+        model.decode_step(x, stream)
+    torch.cuda.synchronize()
+    model.fused_status()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ke = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ev0.record(stream)
+    for i in range(K):
+        x.copy_(X[W + i])
+        ks[i].record(stream)
+        model.decode_step(x, stream)
+        ke[i].record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.stop()
+    model.fused_status()
+    dist.barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    step_ms = ms / K
+    value = K / (ms / 1000.0)
+    kernel_ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in zip(ks, ke)])))
+
+    # ---- end to end: pinned host input -> decode step -> host result, every step, every rank
+    Xh = X.cpu().pin_memory()
+    Yh = torch.empty_like(Xh).pin_memory()
+    dist.barrier()
+    for i in range(W):
+        x.copy_(Xh[i], non_blocking=True)
+        model.decode_step(x, stream)
+        Yh[i].copy_(x, non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        x.copy_(Xh[W + i], non_blocking=True)
+        model.decode_step(x, stream)
+        Yh[W + i].copy_(x, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    model.fused_status()
+    ems = max_over_ranks(e0.elapsed_time(e1))
+    assert torch.isfinite(Yh[W:W + K]).all()
+    e2e = K / (ems / 1000.0)
+    # every rank ends every step with the same hidden state
+    last = Yh[W + K - 1].cuda()
+    got = [torch.empty_like(last) for _ in range(ws)]
+    dist.all_gather(got, last)
+    same_state = all(torch.equal(g.view(torch.int32), last.view(torch.int32)) for g in got)
+
+    # ---- per-layer split from one traced step (not timed)
+    dist.barrier()
+    x.copy_(X[0])
+    stamps = model.fused_trace(x, stream)
+    model.fused_status()
+    split = ep_split(stamps)
+    splits = [None] * ws
+    dist.all_gather_object(splits, split)
+    worst = {kk: max(sp[kk] for sp in splits) for kk in split}
+    limiter = max(("partial_us", "exchange_us", "combine_us"), key=lambda kk: worst[kk])
+
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    peak_gbs = peaks.get("hbm_gbs", 6650.0)
+    achieved = q4_bytes / (kernel_ms / 1000.0) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak_gbs * ws, "unit": "GB/s",
+                "frac": achieved / (peak_gbs * ws), "traffic": None,
+                "kernel": f"k_decode_fused (experts sharded): one launch per rank and token, all layers, {ws} ranks",
+                "kernel_ms": kernel_ms, "algorithmic_bytes": q4_bytes,
+                "algorithmic_bytes_def": "Q4_0 bytes of the k=8 distinct experts read per layer, x layers, "
+                                         "summed over the ranks (each reads its local slots' experts)",
+                "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs) x ranks" if "hbm_gbs" in peaks
+                                else "fallback x ranks")}
+    clk = clocks.summary()
+    model.close()
+    if rank == 0:
+        par, scaling = headline_parallelism(ws, False)
+        out = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": K, "warmup": W,
+            "ms_per_step": step_ms, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": value / PUBLISHED_TOKS, "dtype": "int8", "data": "synthetic",
+            "config": headline_config(NL, ws),
+            "path": "fused, experts sharded over the ranks (tgx_ep_decode_step)",
+            "residency": f"{NL} x {E // ws} experts per rank resident in HBM "
+                         f"({NL * E // ws * EXPERT_BYTES / 1e9:.1f} GB)",
+            "q4_weight_gbs": achieved,
+            "roofline": roofline,
+            "cpu_baseline": None,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": ws * H * 4, "d2h_bytes_per_step": ws * H * 4},
+            "gpu_launches": ws * K, "gpu_launches_per_rank": K,
+            "ep_split": {"rank0": split, "max_over_ranks": worst, "limiter": limiter,
+                         "nvlink_bytes_per_layer_per_rank": f"~{K_TOP // ws if ws <= K_TOP else 1} local slots x "
+                                                            f"{H} rows x 8 B to each of {ws - 1} peers"},
+            "ranks_agree": same_state,
+            "clocks": clk,
+        }
+        emit(out)
+    dist.destroy_process_group()
     return 0
 
 
@@ -1242,6 +1421,8 @@ def main():
         return run_tier(args)
     if args.tokens > 1:
         return run_batched(args)
+    if dist_env()[0] > 1 and not args.replicas and not args.multi:
+        return run_ep_fused(args)
     return run_ours(args)
 
 

@@ -373,10 +373,38 @@ int tgx_ep_p2p_init(tgx_ep *ep, int T_max, void *handle_out);
 int tgx_ep_p2p_connect(tgx_ep *ep, const void *handles);
 int tgx_ep_moe_layer_p2p(tgx_ep *ep, int layer, float *x_dev, int T, void *stream);
 int tgx_ep_p2p_status(tgx_ep *ep, void *stream);
-/* close this rank's mappings of the peers' regions (after its last layer).  A region may
- * be freed (tgx_ep_destroy) only once every rank has disconnected: put a barrier
- * between the two. */
+/* close this rank's mappings of the peers' regions (after its last layer), those of the
+ * fused decode too.  A region may be freed (tgx_ep_destroy) only once every rank has
+ * disconnected: put a barrier between the two. */
 int tgx_ep_p2p_disconnect(tgx_ep *ep);
+
+/* The whole decode step of one token in ONE persistent kernel per rank (the one-device
+ * tgx_decode_step's kernel restricted to the local experts): every rank routes every
+ * layer, computes the gate/up and down rows of the slots whose expert it holds, and
+ * stores each output row's per-slot value into every rank's y buffer over NVLink as a
+ * tagged 64-bit word; each rank then combines all k slots in slot order, so every rank
+ * ends every layer with the same hidden state, bit-identical to tgx_decode_step
+ * (tinygiant/engine.py:229-258 per layer, attention excluded).  No shared expert.
+ *   tgx_ep_fused_init(ep, handle)     every rank: state, plan, y buffer; its CUDA IPC
+ *                                     handle (tgx_ep_p2p_handle_bytes() bytes) out
+ *   tgx_ep_fused_connect(ep, handles) all ranks' handles in rank order
+ *   tgx_ep_decode_step(ep, x, stream) every rank, the same x (device f32[embed]), in place;
+ *                                     all ranks take the same steps
+ *   tgx_ep_fused_trace                the same with per-CTA phase stamps ([L][CTAs][32]
+ *                                     u64: globaltimer ns at slots 0..15, clock64 at 16..31)
+ * Every wait is bounded (tgx_ep_set_wait_limit, SM cycles; 0 = ~1 s); tgx_ep_fused_status
+ * reports an expired one (TG_ETIMEOUT).  To recover, every rank calls
+ * tgx_ep_fused_reset(ep, e) with the same e above every rank's tgx_ep_fused_epoch. */
+int tgx_ep_fused_init(tgx_ep *ep, void *handle_out);
+int tgx_ep_fused_connect(tgx_ep *ep, const void *handles);
+int tgx_ep_decode_step(tgx_ep *ep, float *x_dev, void *stream);
+int tgx_ep_fused_trace(tgx_ep *ep, float *x_dev, uint64_t *stamps_host, void *stream);
+int tgx_ep_fused_info(tgx_ep *ep, int *ctas, int *smem_bytes);
+int tgx_ep_set_wait_limit(tgx_ep *ep, long long cycles);
+int tgx_ep_fused_last_routing(tgx_ep *ep, int layer, int32_t *idx, float *w);
+int tgx_ep_fused_status(tgx_ep *ep, void *stream);
+int tgx_ep_fused_epoch(tgx_ep *ep, unsigned *epoch);
+int tgx_ep_fused_reset(tgx_ep *ep, unsigned epoch);
 
 /* ===================== the reference's formats on device pointers ===================== */
 

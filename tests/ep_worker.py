@@ -1,6 +1,15 @@
-"""Worker of tests/test_gpu_ep.py::test_ep_nccl_matches_single_gpu, one process per GPU
-under torchrun: expert-parallel decode over NCCL, compared on rank 0 with the
-single-GPU batched path holding all experts.  Exit status 0 = bit-identical."""
+"""Worker of tests/test_gpu_ep.py::test_ep_multi_gpu_matches_single_gpu, one process per
+GPU under torchrun: expert-parallel decode compared on rank 0 with one GPU holding all
+experts.  EP_MODE:
+  nccl   per layer: partial step, NCCL all-reduce, combine (T tokens at once), against
+         the single-GPU batched path
+  p2p    the same with the NVLink push exchange instead of the all-reduce
+  fused  one persistent kernel per rank and token over all layers (tgx_ep_decode_step),
+         against the single-GPU fused step (tgx_decode_step); every rank's hidden
+         state must equal rank 0's
+EP_SKIP=1 afterwards makes rank 1 skip one step: rank 0's bounded wait must run out and
+report TG_ETIMEOUT, nothing faults, and (fused) both ranks recover and decode bit-exact
+again.  Exit status 0 = bit-identical."""
 from __future__ import annotations
 
 import os
@@ -14,66 +23,105 @@ sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 def main() -> int:
     import torch
     import torch.distributed as dist
+    from tinygiant_b200._lib import TG_ETIMEOUT, TinyGiantError
     from tinygiant_b200.engine import MoEModel
     from tinygiant_b200.ep import EPMoEModel
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    mode = os.environ.get("EP_MODE", "nccl")
     H, I, E, K, T = 2048, 768, 128, 8, int(os.environ.get("EP_TOKENS", "5"))
-    # an odd layer count and several decodes back to back: consecutive exchange calls must
-    # alternate receive buffers across decode boundaries too
+    # odd layer counts and several decodes back to back: consecutive exchange calls (and
+    # fused steps) must alternate receive buffers across decode boundaries too
     L, R = int(os.environ.get("EP_LAYERS", "3")), int(os.environ.get("EP_REPEAT", "1"))
     ok = True
     try:
         ep = EPMoEModel(H, I, E, K, L, rank=rank, size=world, device=local)
         ep.fill_synthetic(2024)
-        p2p = os.environ.get("EP_P2P", "0") == "1"
-        if p2p:
+        if mode == "p2p":
             ep.enable_p2p(64)
+        elif mode == "fused":
+            ep.enable_fused()
         full = None
         if rank == 0:
             full = MoEModel(H, I, E, K, L, device=local)
             full.fill_synthetic(2024)
         same = torch.tensor([1.0], device="cuda")
+
+        def fused_tokens(X):
+            for t in range(X.shape[0]):
+                ep.decode_step(X[t])
+            ep.fused_status()
+
+        def check_against_full(X, X0):
+            # every rank holds the same state; rank 0's equals one GPU's
+            xs = [torch.empty_like(X) for _ in range(world)]
+            dist.all_gather(xs, X)
+            if rank == 0:
+                if mode == "fused":
+                    for t in range(X0.shape[0]):
+                        full.decode_step(X0[t], eager=True)
+                else:
+                    full.decode_batched(X0)
+                torch.cuda.synchronize()
+                for x in xs + [X]:
+                    if not torch.equal(x.view(torch.int32), X0.view(torch.int32)):
+                        same[0] = 0.0
+
         for rep in range(R):
             g = torch.Generator(device="cuda").manual_seed(99 + rep)
             X = torch.randn(T, H, generator=g, device="cuda")       # the same tokens on every rank
             X0 = X.clone()
-            ep.decode(X)
-            torch.cuda.synchronize()
-            if p2p:
-                ep.p2p_status()
-            if rank == 0:
-                full.decode_batched(X0)
+            dist.barrier()      # the ranks' steps start together (a lagging rank would be waited on)
+            if mode == "fused":
+                fused_tokens(X)
+            else:
+                ep.decode(X)
                 torch.cuda.synchronize()
-                if not torch.equal(X.view(torch.int32), X0.view(torch.int32)):
-                    same[0] = 0.0
-        if full is not None:
-            full.close()
-        if p2p and os.environ.get("EP_SKIP") == "1":
-            # rank 1 skips one exchange: rank 0's combine waits for a flag that never comes,
-            # gives up at the wait limit (~1 s) and reports it; nothing faults.  Rank 1 has
-            # no kernel in flight meanwhile, and both meet again in close().
-            from tinygiant_b200._lib import TG_ETIMEOUT, TinyGiantError
+                if mode == "p2p":
+                    ep.p2p_status()
+            check_against_full(X, X0)
+        if mode in ("p2p", "fused") and os.environ.get("EP_SKIP") == "1":
+            # rank 1 skips a step: rank 0 waits for down values (p2p: an epoch flag) that
+            # never come, gives up at the wait limit and reports it; nothing faults.  Rank 1
+            # has no kernel in flight meanwhile.
+            dist.barrier()
+            if mode == "fused":
+                ep.set_wait_limit(4_000_000)                           # ~2 ms
             if rank == 0:
                 Xs = torch.randn(T, H, device="cuda")
-                ep.moe_layer(0, Xs)
-                torch.cuda.synchronize()
                 try:
-                    ep.p2p_status()
+                    if mode == "fused":
+                        ep.decode_step(Xs[0])
+                        ep.fused_status()
+                    else:
+                        ep.moe_layer(0, Xs)
+                        torch.cuda.synchronize()
+                        ep.p2p_status()
                     same[0] = 0.0                                      # the wait should have run out
                 except TinyGiantError as err:
                     if err.code != TG_ETIMEOUT:
                         same[0] = 0.0
+            if mode == "fused":
+                # every rank restarts its launch count above every rank's, then decodes again
+                ep.fused_recover()
+                ep.set_wait_limit(0)
+                g = torch.Generator(device="cuda").manual_seed(7)
+                X = torch.randn(2, H, generator=g, device="cuda")
+                X0 = X.clone()
+                dist.barrier()
+                fused_tokens(X)
+                check_against_full(X, X0)
+        if full is not None:
+            full.close()
         dist.broadcast(same, 0)                                        # every rank takes the same steps
         ok = bool(same.item() == 1.0)
         ep.close()                                                     # disconnect, barrier, free
     finally:
         dist.destroy_process_group()
     if rank == 0:
-        print("ep-p2p" if os.environ.get("EP_P2P") == "1" else "ep-nccl", "bit-identical" if ok else "MISMATCH",
-              flush=True)
+        print("ep-" + mode, "bit-identical" if ok else "MISMATCH", flush=True)
     return 0 if ok else 1
 
 

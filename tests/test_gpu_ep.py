@@ -176,21 +176,73 @@ def test_ep_rejects_foreign_experts():
     ep.close()
 
 
-@pytest.mark.parametrize("p2p,layers,repeat,skip", [("0", 3, 1, "0"), ("1", 3, 1, "0"), ("1", 3, 4, "0"),
-                                                    ("1", 1, 5, "0"), ("1", 3, 2, "1")])
-def test_ep_nccl_matches_single_gpu(p2p, layers, repeat, skip):
-    # p2p = 1: the exchange by direct NVLink stores and flags instead of the all-reduce;
-    # odd layer counts with several decodes back to back reuse the receive buffers across
-    # decode boundaries
+def test_ep_fused_single_rank_matches_decode_step():
+    # the one-kernel EP step with one rank (every expert local, its own y buffer): odd and
+    # even step counts (both buffer halves), a router changed after set-up, a graph replay,
+    # against the one-GPU fused step
+    import numpy as np
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    from tinygiant_b200.ep import EPMoEModel
+    L = 3
+    full = MoEModel(H, I, E, K, L)
+    full.fill_synthetic(41)
+    ep = EPMoEModel(H, I, E, K, L, rank=0, size=1)
+    ep.fill_synthetic(41)
+    ep.enable_fused()
+    R = (np.random.default_rng(3).standard_normal((E, H)) * 0.02).astype(np.float32)
+    full.set_router(1, R)
+    ep.set_router(1, R)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for _ in range(3):
+        x = torch.randn(H, generator=g, device="cuda")
+        want = x.clone()
+        full.decode_step(want, eager=True)
+        got = x.clone()
+        ep.decode_step(got)
+        ep.fused_status()
+        assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+        for layer in range(L):
+            idx, w = ep.fused_routing(layer)
+            ridx, rw, _ = full.last_routing(layer)
+            assert np.array_equal(idx, ridx) and np.array_equal(w.view(np.uint32), rw.view(np.uint32))
+    graph = torch.cuda.CUDAGraph()
+    xg = torch.empty(H, device="cuda")
+    with torch.cuda.graph(graph):
+        ep.decode_step(xg)
+    for _ in range(2):
+        x = torch.randn(H, generator=g, device="cuda")
+        want = x.clone()
+        full.decode_step(want, eager=True)
+        xg.copy_(x)
+        graph.replay()
+        ep.fused_status()
+        assert torch.equal(xg.view(torch.int32), want.view(torch.int32))
+    del graph
+    ep.close()
+    full.close()
+
+
+@pytest.mark.parametrize("mode,layers,repeat,skip", [("nccl", 3, 1, "0"), ("p2p", 3, 1, "0"), ("p2p", 3, 4, "0"),
+                                                     ("p2p", 1, 5, "0"), ("p2p", 3, 2, "1"),
+                                                     ("fused", 3, 3, "0"), ("fused", 2, 2, "1"),
+                                                     ("fused", 48, 1, "0")])
+def test_ep_multi_gpu_matches_single_gpu(mode, layers, repeat, skip):
+    # p2p: the exchange by direct NVLink stores and flags instead of the all-reduce; fused:
+    # one kernel per rank and token; odd layer counts with several decodes back to back
+    # reuse the receive buffers across decode boundaries; 48 layers is the benchmarked
+    # model
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    # skip = 1: afterwards rank 1 skips one exchange and rank 0 must report TG_ETIMEOUT
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_P2P=p2p, EP_LAYERS=str(layers), EP_REPEAT=str(repeat),
+    # skip = 1: afterwards rank 1 skips one step and rank 0 must report TG_ETIMEOUT
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_MODE=mode, EP_LAYERS=str(layers), EP_REPEAT=str(repeat),
                EP_SKIP=skip)
+    port = 29531 + ("nccl", "p2p", "fused").index(mode) + 3 * layers + 200 * repeat + 1000 * int(skip)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={29531 + int(p2p) + 2 * layers + 16 * repeat + 100 * int(skip)}",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
            str(ROOT / "tests" / "ep_worker.py")]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    first = r.stderr.find("Traceback")                 # a worker's own error, ahead of torchrun's summary
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[max(0, first):][:3000]
     assert "bit-identical" in r.stdout

@@ -116,6 +116,16 @@ PROTOTYPES = {
     "tgx_ep_moe_layer_p2p": (CI, [VP, CI, VP, CI, VP]),
     "tgx_ep_p2p_status": (CI, [VP, VP]),
     "tgx_ep_p2p_disconnect": (CI, [VP]),
+    "tgx_ep_fused_init": (CI, [VP, VP]),
+    "tgx_ep_fused_connect": (CI, [VP, VP]),
+    "tgx_ep_decode_step": (CI, [VP, VP, VP]),
+    "tgx_ep_fused_trace": (CI, [VP, VP, VP, VP]),
+    "tgx_ep_fused_info": (CI, [VP, ctypes.POINTER(CI), ctypes.POINTER(CI)]),
+    "tgx_ep_set_wait_limit": (CI, [VP, ctypes.c_longlong]),
+    "tgx_ep_fused_last_routing": (CI, [VP, CI, VP, VP]),
+    "tgx_ep_fused_status": (CI, [VP, VP]),
+    "tgx_ep_fused_epoch": (CI, [VP, ctypes.POINTER(ctypes.c_uint)]),
+    "tgx_ep_fused_reset": (CI, [VP, ctypes.c_uint]),
     "tgx_set_batched_kernels": (CI, [VP, CI]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),

@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include "tg_decode.h"
@@ -116,6 +117,15 @@ __device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+// system scope: words that other devices store over NVLink
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void red_add_relaxed_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -211,12 +221,14 @@ __device__ __forceinline__ float warp_sum4_transposed(float v0, float v1, float 
 
 // Gather the h records of slots [jlo, jlo + nwords / (6 * nbI)) of one layer (six
 // tagged words each) straight into the activation form: codes, fp32 scale, 8 * sum
-// of codes.  Each thread re-polls only its missing words.  False when the wait limit
-// passed (error recorded) or another CTA reported an error.  Called from one place
-// only (the stage loop), so the layer loop holds one copy of it.
+// of codes.  With lmap (experts sharded over devices) hw is the layer's first record
+// and the records gathered are those of slots lmap[0 .. nwords / (6 * nbI)), stored
+// in that order.  Each thread re-polls only its missing words.  False when the wait
+// limit passed (error recorded) or another CTA reported an error.  Called from one
+// place only, so the layer loop holds one copy of it.
 __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, int nwords, int jlo, int nbI,
                                               uint8_t* hq_base, int ab_i, unsigned tag, unsigned* ctl, int* flags,
-                                              int l, long long limit) {
+                                              int l, long long limit, const int* lmap = nullptr) {
     const int tid = threadIdx.x;
     unsigned mine = 0, done = 0;
     for (int i = 0; i * NT + tid < nwords; i++) mine |= 1u << i;
@@ -229,7 +241,12 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
 #pragma unroll
             for (int t = 0; t < 8; t++) {
                 const int i = i0 + t, w = i * NT + tid;
-                v[t] = (w < nwords && !(done >> i & 1u)) ? ld_relaxed_u64(hw + w) : 0ull;
+                int src = w;
+                if (lmap && w < nwords) {
+                    const int rec = w / 6, jl = rec / nbI;
+                    src = (lmap[jl] - jl) * nbI * 6 + w;
+                }
+                v[t] = (w < nwords && !(done >> i & 1u)) ? ld_relaxed_u64(hw + src) : 0ull;
             }
 #pragma unroll
             for (int t = 0; t < 8; t++) {
@@ -267,58 +284,53 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
     return true;
 }
 
-// Down values y_j of this CTA's rows for slots [jlo, jhi) into ys[j][q]: a warp per
-// row (two rows per warp above 16 rows, sharing each h block load), lane partials
-// in block order b = lane, lane + 32, ... for up to 8 slots, then one transposed
-// reduction per row (the mirror order).  Called from one place only.
-template <bool TWO>
+// Down values y_j of this CTA's rows for slots [jlo, jhi) into ys[j][q].  One task
+// per warp: one slot and a group of at most 8 consecutive rows, enough groups per slot
+// to occupy the warps.  The lanes hold the slot's h blocks b = lane, lane + 32, ... in
+// registers across the group's rows (each h block is read from shared memory once per
+// task, not once per row), lane partials in block order b = lane, lane + 32, ..., then
+// one transposed reduction over the group's rows.  Each row's reduction is the same
+// pairing tree as a butterfly over the lanes whatever the other values in the
+// reduction, so the bits are the mirror order's.  Called from one place only.
 __device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* hq_base, float* ys, uint32_t d_chunk,
-                                       int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi) {
+                                          int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (warp >= CW) return;
-    const int rpw = TWO ? 2 : 1;
-    for (int pr = warp; pr * rpw < d_n; pr += CW) {
-        const int q0 = pr * rpw;
-        const bool two = TWO && q0 + 1 < d_n;
-        for (int j0 = jlo; j0 < jhi; j0 += 8) {
-            float acc0[8], acc1[8];
+    const int ns = jhi - jlo;
+    if (warp >= CW || ns <= 0 || d_n <= 0) return;
+    int gps = CW / ns > 1 ? CW / ns : 1;         // row groups per slot
+    int R = (d_n + gps - 1) / gps;               // rows per group
+    if (R > 8) R = 8;
+    gps = (d_n + R - 1) / R;
+    for (int t = warp; t < ns * gps; t += CW) {
+        const int js = t / gps, grp = t - js * gps, j = jlo + js;
+        const int q0 = grp * R, nr = d_n - q0 < R ? d_n - q0 : R;
+        const uint8_t* rows = dbase + (size_t)j * d_chunk + (size_t)q0 * row_d;
+        const ActView hv = act_view(hq_base + (size_t)j * ab_i, nbI);
+        float acc[8];
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++) acc0[jj] = acc1[jj] = 0.0f;
+        for (int r = 0; r < 8; r++) acc[r] = 0.0f;
 #pragma unroll 1
-            for (int b = lane; b < nbI; b += 32) {
+        for (int b = lane; b < nbI; b += 32) {
+            const XBlk xb = load_xblk(hv, b);
 #pragma unroll
-                for (int jj = 0; jj < 8; jj++) {
-                    const int j = j0 + jj;
-                    if (j < jhi) {
-                        const uint8_t* row = dbase + (size_t)j * d_chunk + (size_t)q0 * row_d;
-                        const XBlk xb = load_xblk(act_view(hq_base + (size_t)j * ab_i, nbI), b);
-                        const uint4 w0 = *reinterpret_cast<const uint4*>(row + 16 * b);
-                        const float dw0 = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * nbI + 2 * b));
-                        acc0[jj] = __fadd_rn(acc0[jj], block_term(block_sumi(w0, xb), dw0, xb.d));
-                        if (two) {
-                            const uint8_t* row1 = row + row_d;
-                            const uint4 w1 = *reinterpret_cast<const uint4*>(row1 + 16 * b);
-                            const float dw1 =
-                                f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row1 + 16 * nbI + 2 * b));
-                            acc1[jj] = __fadd_rn(acc1[jj], block_term(block_sumi(w1, xb), dw1, xb.d));
-                        }
-                    }
+            for (int r = 0; r < 8; r++) {
+                if (r < nr) {
+                    const uint8_t* row = rows + (size_t)r * row_d;
+                    const uint4 w = *reinterpret_cast<const uint4*>(row + 16 * b);
+                    const float dw = f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(row + 16 * nbI + 2 * b));
+                    acc[r] = __fadd_rn(acc[r], block_term(block_sumi(w, xb), dw, xb.d));
                 }
             }
-            const float y0 = warp_sum8_transposed(acc0, lane);   // slot j0+jj in lanes 4jj..4jj+3
-            const float y1 = two ? warp_sum8_transposed(acc1, lane) : 0.0f;
-            const int jj = lane >> 2;
-            if ((lane & 3) == 0 && j0 + jj < jhi) {
-                ys[(size_t)(j0 + jj) * max_rows + q0] = y0;
-                if (two) ys[(size_t)(j0 + jj) * max_rows + q0 + 1] = y1;
-            }
         }
+        const float y = warp_sum8_transposed(acc, lane);   // row q0 + r in lanes 4r .. 4r+3
+        const int r = lane >> 2;
+        if ((lane & 3) == 0 && r < nr) ys[(size_t)j * max_rows + q0 + r] = y;
     }
 }
 
 }  // namespace
 
-template <bool TRACE>
+template <bool TRACE, bool EP>
 __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     extern __shared__ __align__(128) uint8_t smem[];
     const FusedSmem S = fused_smem_layout(P);
@@ -330,6 +342,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     float* slog = reinterpret_cast<float*>(smem + S.slog);
     unsigned long long* skey = reinterpret_cast<unsigned long long*>(smem + S.skey);   // [E] rank keys
     int* sidx = reinterpret_cast<int*>(smem + S.sidx);
+    int* lmap = reinterpret_cast<int*>(smem + S.lmap);     // EP: local slot -> slot
     int* flags = reinterpret_cast<int*>(smem + S.flags);   // [0] error seen, [1] error detail, [2] last CTA
     float* sscale = reinterpret_cast<float*>(flags + 4);   // RMSNorm scale of the current layer
     float* xs = reinterpret_cast<float*>(smem + S.xs);
@@ -342,6 +355,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     float* rt = reinterpret_cast<float*>(smem + S.rt);        // router columns of this CTA's rows [rows][E]
     float* snorm = reinterpret_cast<float*>(smem + S.snorm);  // [2][H]
     float* ys = reinterpret_cast<float*>(smem + S.ys);        // [k][max_rows] per-slot down values
+    float* yr = reinterpret_cast<float*>(smem + S.yr);        // EP: [k][max_rows] as received
     uint8_t* arena = smem + S.arena;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -360,7 +374,10 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     }
     if (tid < 4) flags[tid] = 0;
     cta_sync();
-    const int n_gu = plan[0], d_lo = plan[1], d_n = plan[2], d_place = plan[3];
+    // one device: the static plan; experts sharded over devices: n_gu, d_place and
+    // dbase are set per layer from the slots whose expert is held here
+    int n_gu = plan[0], d_place = plan[3];
+    const int d_lo = plan[1], d_n = plan[2];
     const uint16_t* gu_units = plan + 4;
     const uint32_t d_chunk = (uint32_t)d_n * (uint32_t)g.row_d;   // this CTA's rows of one expert's down
     const uint32_t rt_bytes = (uint32_t)d_n * (uint32_t)E * 4u;  // their router columns
@@ -368,6 +385,20 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     uint8_t* dbase = arena + (d_place ? (size_t)0 : (size_t)n_gu * 2 * gu_unit_bytes);
     const unsigned epoch = ld_relaxed_u32(P.ctl);
     const unsigned tag = epoch % 65535u + 1u;   // 1..65535; the tagged buffers are cleared before it repeats
+    // EP: the y words carry the full launch count (never cleared; every rank launches
+    // the same sequence) and alternate buffer halves by launch parity, so a rank one
+    // launch ahead never overwrites a word another rank has still to read
+    const unsigned ytag = epoch + 1u;
+    int nloc = k;   // EP: slots whose expert is held here this layer
+    // gate/up unit u of this CTA (slot * nbI + 32-row chunk): the static plan's, or with
+    // experts sharded, unit cta + u * G of the local slots in slot order (the same
+    // assignment the plan's greedy makes, u mod G, over nloc * nbI units)
+    auto unit_of = [&](int u) -> int {
+        if (!EP) return gu_units[u];
+        const int U = cta + u * G, jl = U / nbI;
+        return lmap[jl] * nbI + (U - jl * nbI);
+    };
+    auto expert_of = [&](int j) -> int { return EP ? sidx[j] - P.e_lo : sidx[j]; };
     const uint64_t pol_stream = policy_evict_first();
     const uint64_t pol_keep = policy_evict_last();
 
@@ -376,6 +407,10 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     // wait for in layer l is l & 1 (0 for the one-off first router copy).
     unsigned pending = 0;  // bits 0..3: gate/up units, bit 4: down group, bit 5: first router copy
     int cur_l = 0;
+    // phase parity of each gate/up unit's mbarrier (bit u), flipped every layer the unit
+    // is used: with experts sharded over devices a CTA's unit count changes per layer,
+    // so a unit's mbarrier does not complete once in every layer
+    unsigned gu_par = 0;
 
     auto fail = [&](unsigned code) { record_failure(P.ctl, flags, code); };
     auto error_seen = [&]() -> bool { return ld_relaxed_u32(P.ctl + 2) != 0; };
@@ -415,18 +450,20 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     auto issue_gateup = [&](const uint8_t* lbase) {
         for (int pi = lane; pi < 2 * n_gu; pi += 32) {
             const int u = pi >> 1, half = pi & 1;
-            const int unit = gu_units[u];
+            const int unit = unit_of(u);
             const int j = unit / nbI, c = unit - j * nbI;
-            const uint8_t* src = lbase + (size_t)sidx[j] * g.expert_bytes + (half ? g.t_gu : 0) +
+            const uint8_t* src = lbase + (size_t)expert_of(j) * g.expert_bytes + (half ? g.t_gu : 0) +
                                  (size_t)c * gu_unit_bytes;
             bulk_g2s(arena + ((size_t)u * 2 + half) * gu_unit_bytes, src, gu_unit_bytes, mbar_gu + u, pol_stream);
         }
     };
-    // producer warp: this layer's down rows of all k experts, plus the next layer's
-    // router columns and norm weights, all on mbar_d
+    // producer warp: this layer's down rows of all k experts (EP: of the nloc local
+    // slots, in local order), plus the next layer's router columns and norm weights,
+    // all on mbar_d
     auto issue_down = [&](int l, int layer, const uint8_t* lbase, bool next) {
         if (!(d_n > 0 || next)) return;
-        const uint32_t total = (uint32_t)k * d_chunk + (next ? rt_bytes + norm_bytes : 0u);
+        const int ns = EP ? nloc : k;
+        const uint32_t total = (uint32_t)ns * d_chunk + (next ? rt_bytes + norm_bytes : 0u);
         if (lane == 0) {
             mbar_arrive_expect_tx(mbar_d, total);
             pending |= 1u << 4;
@@ -435,16 +472,17 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         const int npd = d_n > 0 ? pieces_of(d_chunk) : 0;
         const int npr = (next && d_n > 0) ? pieces_of(rt_bytes) : 0;
         const int npn = next ? pieces_of(norm_bytes) : 0;
-        const int nd = k * npd;
+        const int nd = ns * npd;
         for (int pi = lane; pi < nd + npr + npn; pi += 32) {
             uint32_t off, n;
             const uint8_t* src;
             uint8_t* dst;
             uint64_t pol;
             if (pi < nd) {
-                const int j = pi / npd, p = pi - j * npd;
+                const int j = pi / npd, p = pi - j * npd;   // EP: j is the local slot
                 piece_span(d_chunk, npd, p, off, n);
-                src = lbase + (size_t)sidx[j] * g.expert_bytes + 2 * g.t_gu + (size_t)d_lo * g.row_d + off;
+                src = lbase + (size_t)expert_of(EP ? lmap[j] : j) * g.expert_bytes + 2 * g.t_gu +
+                      (size_t)d_lo * g.row_d + off;
                 dst = dbase + (size_t)j * d_chunk + off;
                 pol = pol_stream;
             } else if (pi < nd + npr) {
@@ -624,6 +662,24 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         }
         cta_sync();
         if (tid == 0) stamp(l, 9);
+        if (EP) {
+            // the slots whose expert is held here, this CTA's share of their gate/up units
+            // (units cta, cta + G, ... of nloc * nbI) and where its down rows go
+            unsigned lmask = 0;
+            for (int j = 0; j < k; j++)
+                if ((unsigned)(sidx[j] - P.e_lo) < (unsigned)P.e_n) lmask |= 1u << j;
+            nloc = __popc(lmask);
+            const int nu = nloc * nbI;
+            n_gu = cta < nu ? (nu - 1 - cta) / G + 1 : 0;
+            d_place = (n_gu > 0 && (size_t)n_gu * 2 * gu_unit_bytes + (size_t)nloc * d_chunk > P.arena_bytes) ? 1 : 0;
+            dbase = arena + (d_place ? (size_t)0 : (size_t)n_gu * 2 * gu_unit_bytes);
+            // the producer warp writes the slot map; the compute warps read it after the
+            // next barrier
+            if (warp == CW) {
+                if (lane < k && (lmask >> lane & 1u)) lmap[__popc(lmask & ((1u << lane) - 1u))] = lane;
+                __syncwarp();
+            }
+        }
 
         // ------------------------------------------------------------ B: copies, softmax, x quantise
         if (warp == CW) {
@@ -715,9 +771,9 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             if (lane + 32 < nbH) xr1 = load_xblk(xq, lane + 32);
         }
         for (int u = 0; u < n_gu; u++) {
-            const bool ok = wait_bar(mbar_gu + u, (unsigned)l & 1u, 3);
+            const bool ok = wait_bar(mbar_gu + u, gu_par >> u & 1u, 3);
             if (u == 0 && tid == 0) stamp(l, 8);
-            const int unit = gu_units[u];
+            const int unit = unit_of(u);
             const int j = unit / nbI, c = unit - j * nbI;
             float* shu = sh + (u & 1) * 32;
             if (warp == CW) {
@@ -791,6 +847,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             // the next unit writes the other sh / hrec buffer; the one after it is
             // ordered behind this publish by the next unit's barrier
         }
+        gu_par ^= (1u << n_gu) - 1u;   // every unit used this layer has completed one phase
         if (tid == 0) stamp(l, 3);
 
         // ------------------------------------------------------------ D: down rows + combine + next routing
@@ -806,14 +863,70 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
                                     tag, P.ctl, flags, l, P.wait_cycles);
         };
         auto down_partial = [&](int jlo, int jhi) {
-            // one row per warp up to 16 rows, else two rows per warp sharing each h block load
-            if (d_n <= CW)
-                down_rows<false>(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
-            else
-                down_rows<true>(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
+            down_rows(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, jlo, jhi);
         };
+        if (EP) {
+            // the local slots' h records, down rows and per-slot down values, stored into
+            // every rank's y buffer; then this CTA's rows of all k slots from its own
+            const size_t ylay = ((size_t)(epoch & 1u) * P.Lmax + l) * k * g.H;
+            if (d_n > 0 && nloc > 0) {
+                if (!cta_sync_and(gather_h_records(hwl, nloc * nbI * 6, 0, nbI, hq_base, (int)ab_i, tag, P.ctl, flags,
+                                                   l, P.wait_cycles, lmap)))
+                    goto drain;
+            }
+            if (tid == 0) stamp(l, 4);
+            if (!cta_sync_and(!(d_n > 0 || next) || wait_bar(mbar_d, (unsigned)l & 1u, 5))) goto drain;
+            if (tid == PT) pending &= ~(1u << 4);
+            if (tid == 0) stamp(l, 5);
+            if (d_n > 0 && nloc > 0) down_partial(0, nloc);
+            cta_sync();
+            const int nyw = nloc * d_n;
+            for (int w = tid; w < nyw * P.ep_size; w += NT) {
+                const int r = w / nyw, rem = w - r * nyw, jl = rem / d_n, q = rem - jl * d_n;
+                st_relaxed_sys_u64(P.ypeer[r] + ylay + (size_t)lmap[jl] * g.H + d_lo + q,
+                                   ((unsigned long long)ytag << 32) |
+                                       __float_as_uint(ys[(size_t)jl * P.max_rows + q]));
+            }
+            if (tid == 0) stamp(l, 12);
+            if (d_n > 0) {
+                const unsigned long long* yown = P.ypeer[P.ep_rank] + ylay;
+                const int npw = k * d_n;   // <= 16 * 64 words: at most 2 per thread
+                unsigned mine = 0, done = 0;
+                for (int i = 0; i * NT + tid < npw; i++) mine |= 1u << i;
+                const long long t0 = clock64();
+                int spins = 0;
+                bool ok = true;
+                while (done != mine) {
+                    for (int i = 0; i * NT + tid < npw; i++) {
+                        if (done >> i & 1u) continue;
+                        const int w = i * NT + tid, j = w / d_n, q = w - j * d_n;
+                        const unsigned long long v = ld_relaxed_sys_u64(yown + (size_t)j * g.H + d_lo + q);
+                        if ((unsigned)(v >> 32) == ytag) {
+                            yr[(size_t)j * P.max_rows + q] = __uint_as_float((unsigned)v);
+                            done |= 1u << i;
+                        }
+                    }
+                    if (done == mine) break;
+                    if ((++spins & 63) == 0) {
+                        if (clock64() - t0 > P.wait_cycles) {
+                            const int w = (__ffs(mine & ~done) - 1) * NT + tid;
+                            flags[1] = (l << 20) | (((w / d_n) & 0xfff) << 8) | 0xfd;
+                            fail(6);
+                            ok = false;
+                            break;
+                        }
+                        if (error_seen()) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+                if (!cta_sync_and(ok)) goto drain;
+            }
+            if (tid == 0) stamp(l, 13);
+        }
         // stage 0: slots [0, ke); stage 1: slots [ke, k) (empty when ke == k)
-        for (int stage = 0; stage < 2; stage++) {
+        for (int stage = 0; stage < (EP ? 0 : 2); stage++) {
             const int jlo = stage ? ke : 0, jhi = stage ? k : ke;
             if (jlo >= jhi) continue;
             if (d_n > 0) {
@@ -831,10 +944,11 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             cta_sync();
             // combine in slot order and the residual: x_{l+1} = x_l + sum_j w_j * y_j
             const float* nw1 = snorm + (size_t)((l + 1) & 1) * g.H;
+            const float* yv = EP ? yr : ys;
             for (int q = tid; q < d_n; q += NT) {
                 float a = 0.0f;
 #pragma unroll 1
-                for (int j = 0; j < k; j++) a = __fadd_rn(a, __fmul_rn(sh[64 + j], ys[(size_t)j * P.max_rows + q]));
+                for (int j = 0; j < k; j++) a = __fadd_rn(a, __fmul_rn(sh[64 + j], yv[(size_t)j * P.max_rows + q]));
                 const int r = d_lo + q;
                 const float xn = __fadd_rn(xs[r], a);
                 if (next) {
@@ -887,7 +1001,7 @@ drain:
         const long long t0 = clock64();
         for (int u = 0; u < FUSED_MAX_GU; u++)
             if (pending >> u & 1u)
-                while (!mbar_try_wait(mbar_gu + u, (unsigned)cur_l & 1u) && clock64() - t0 < P.wait_cycles) {
+                while (!mbar_try_wait(mbar_gu + u, gu_par >> u & 1u) && clock64() - t0 < P.wait_cycles) {
                 }
         if (pending >> 4 & 1u)
             while (!mbar_try_wait(mbar_d, (unsigned)cur_l & 1u) && clock64() - t0 < P.wait_cycles) {
@@ -957,17 +1071,29 @@ int fused_plan(const Geom& g, int E, int k, int G, std::vector<uint16_t>& plan, 
     return 0;
 }
 
+// The attribute is per kernel and device, shared by every context on the device: only
+// ever raise it, so a context with a smaller layout never lowers it below what another
+// context's launches need.
 cudaError_t fused_prepare(const FusedParams& P) {
-    cudaError_t e = cudaFuncSetAttribute(k_decode_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)fused_smem_layout(P).total);
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_decode_fused<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)fused_smem_layout(P).total);
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    const int bytes = (int)fused_smem_layout(P).total;
+    for (auto fn : {k_decode_fused<false, false>, k_decode_fused<true, false>, k_decode_fused<false, true>,
+                    k_decode_fused<true, true>}) {
+        cudaFuncAttributes fa;
+        cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+        if (e != cudaSuccess) return e;
+        if (fa.maxDynamicSharedSizeBytes >= bytes) continue;
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t fused_occupancy(const FusedParams& P, int* blocks_per_sm) {
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, k_decode_fused<false>, NT,
-                                                         fused_smem_layout(P).total);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        blocks_per_sm, P.ypeer ? k_decode_fused<false, true> : k_decode_fused<false, false>, NT,
+        fused_smem_layout(P).total);
 }
 
 cudaError_t launch_decode_fused(const FusedParams& P, int G, cudaStream_t s) {
@@ -981,8 +1107,12 @@ cudaError_t launch_decode_fused(const FusedParams& P, int G, cudaStream_t s) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (P.trace) return cudaLaunchKernelEx(&cfg, k_decode_fused<true>, P);
-    return cudaLaunchKernelEx(&cfg, k_decode_fused<false>, P);
+    if (P.ypeer) {
+        if (P.trace) return cudaLaunchKernelEx(&cfg, k_decode_fused<true, true>, P);
+        return cudaLaunchKernelEx(&cfg, k_decode_fused<false, true>, P);
+    }
+    if (P.trace) return cudaLaunchKernelEx(&cfg, k_decode_fused<true, false>, P);
+    return cudaLaunchKernelEx(&cfg, k_decode_fused<false, false>, P);
 }
 
 }  // namespace tg

@@ -18,8 +18,9 @@ constexpr int FUSED_PLAN = 4 + FUSED_MAX_GU;  // per CTA: n_gu, first down row, 
 // phase stamps: 0 routing and x seen, 1 gate/up copies issued, 2 x quantised,
 // 3 gate/up published, 4 early h gathered, 5 down data landed, 6 down rows done,
 // 7 next-layer sums sent, 8 first gate/up unit landed, 9 top-k done,
-// 10 down copies issued, 11 late h gathered; slots 16..31 hold the SM's clock64 at
-// the same events
+// 10 down copies issued, 11 late h gathered, 12 down values stored to every rank,
+// 13 every rank's down values received (12 and 13 with experts sharded over
+// devices); slots 16..31 hold the SM's clock64 at the same events
 constexpr int FUSED_TRACE = 32;
 // router sums are spread over this many accumulator copies (CTA c adds into copy
 // c % FUSED_ACC), so each word takes ~G / FUSED_ACC atomic adds instead of G
@@ -55,12 +56,21 @@ struct FusedParams {
     float* logits_out;        // [L][E]
     unsigned long long* trace;  // optional [nL][G][FUSED_TRACE] stamps per CTA and layer
     size_t arena_bytes;       // weight staging bytes per CTA
+    // Experts sharded over devices (ypeer != nullptr): this device holds experts
+    // [e_lo, e_lo + e_n) of every layer (weights / layer_bytes cover only them), routes
+    // every token like the others, computes the gate/up and down rows of the slots whose
+    // expert it holds, and stores each row's per-slot down value into every rank's y
+    // buffer ([2][Lmax][k][H] words (tag << 32) | f32 bits, half = launch parity) over
+    // NVLink; every rank then combines all k slots in slot order.  One device: 0, E, null.
+    int e_lo, e_n;
+    int ep_rank, ep_size;
+    unsigned long long* const* ypeer;   // [ep_size] every rank's y buffer (device pointers)
 };
 
 // Shared-memory carve-up, identical on host and device.
 struct FusedSmem {
-    uint32_t mbar, plan, slogfx, slog, skey, sidx, flags, xs, xq, hq, sh, hrec, xnext, xw, rt, snorm, ys, arena,
-        total;
+    uint32_t mbar, plan, slogfx, slog, skey, sidx, lmap, flags, xs, xq, hq, sh, hrec, xnext, xw, rt, snorm, ys, yr,
+        arena, total;
 };
 
 TG_HD uint32_t fused_take(uint32_t& o, size_t bytes) {
@@ -78,6 +88,7 @@ TG_HD FusedSmem fused_smem_layout(const FusedParams& P) {
     s.slog = fused_take(o, 4 * (size_t)P.E);
     s.skey = fused_take(o, 8 * (size_t)P.E);
     s.sidx = fused_take(o, 4 * 16);
+    s.lmap = fused_take(o, 4 * 16);           // local slot -> slot (experts sharded over devices)
     s.flags = fused_take(o, 4 * 8);
     s.xs = fused_take(o, 4 * (size_t)P.g.H);
     s.xq = fused_take(o, act_bytes(P.g.nbH));
@@ -89,6 +100,8 @@ TG_HD FusedSmem fused_smem_layout(const FusedParams& P) {
     s.rt = fused_take(o, 4 * (size_t)P.max_rows * P.E);
     s.snorm = fused_take(o, 2 * 4 * (size_t)P.g.H);   // FFN norm weights, double buffered by layer parity
     s.ys = fused_take(o, 4 * 16 * (size_t)P.max_rows);  // per-slot down values of this CTA's rows
+    // the same for all k slots as received from every rank (experts sharded over devices)
+    s.yr = fused_take(o, P.ypeer ? 4 * 16 * (size_t)P.max_rows : 0);
     s.arena = fused_take(o, P.arena_bytes);
     s.total = o;
     return s;

@@ -19,6 +19,7 @@
 #include <vector>
 
 #include "../../include/tinygiant.h"
+#include "tg_decode.h"
 #include "tg_internal.h"
 
 using tg::Geom;
@@ -57,6 +58,24 @@ struct tgx_ep {
     unsigned* p2p_count = nullptr;  // push CTAs finished this layer (zero between layers)
     int* owned = nullptr;         // [1 + T * ks]: count and list of the pairs this rank computed
     bool p2p_ready = false;
+    // fused decode (tgx_ep_fused_*): the one-kernel-per-step path restricted to the local
+    // experts; ybuf ([2][L][k][H] tagged words) receives every rank's per-slot down values
+    bool fused_ready = false;
+    int fG = 0;                         // CTAs = SMs
+    float* RT = nullptr;                // [L][H][E] transposed routers
+    unsigned long long* xw = nullptr;   // [L + 1][H]
+    unsigned long long* facc = nullptr; // [L][FUSED_ACC][E + 1]
+    unsigned long long* hqt = nullptr;  // [L][k * nbI * 6]
+    unsigned* ctl = nullptr;            // epoch, finish count, error
+    uint16_t* plan = nullptr;
+    int* fidx = nullptr;                // [L][k] routing record of the last step
+    float* fw = nullptr;                // [L][k]
+    float* flogits = nullptr;           // [L][E]
+    unsigned long long* ybuf = nullptr;
+    size_t ybuf_bytes = 0;
+    void* fpeers[64] = {};              // opened peer y buffers (null for this rank)
+    unsigned long long** ypeer = nullptr;   // [G] device pointers to every rank's y buffer
+    tg::FusedParams fp{};
 };
 
 namespace {
@@ -94,10 +113,15 @@ struct Dev {
 void ep_free(tgx_ep* c) {
     if (!c) return;
     Dev dg(c->device);
-    for (int q = 0; q < 64; q++)
+    for (int q = 0; q < 64; q++) {
         if (c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
+        if (c->fpeers[q]) cudaIpcCloseMemHandle(c->fpeers[q]);
+    }
     for (void* p : {(void*)c->region, (void*)c->ystage, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err,
                     (void*)c->p2p_count, (void*)c->owned})
+        if (p) cudaFree(p);
+    for (void* p : {(void*)c->RT, (void*)c->xw, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan,
+                    (void*)c->fidx, (void*)c->fw, (void*)c->flogits, (void*)c->ybuf, (void*)c->ypeer})
         if (p) cudaFree(p);
     for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
                     c->scratch, (void*)c->wts})
@@ -267,6 +291,9 @@ extern "C" int tgx_ep_set_router(tgx_ep* ep, int layer, const float* R, int src_
     const size_t n = (size_t)ep->shape.n_experts * ep->shape.embed;
     EP_CUDA(cudaMemcpyAsync(ep->routers + (size_t)layer * n, R, n * sizeof(float),
                             src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ep->s));
+    if (ep->RT)   // the fused path's transposed copy
+        EP_CUDA(tg::launch_transpose(ep->routers + (size_t)layer * n, ep->RT + (size_t)layer * n,
+                                     ep->shape.n_experts, ep->shape.embed, ep->s));
     EP_CUDA(cudaStreamSynchronize(ep->s));
     return TG_OK;
 }
@@ -298,6 +325,9 @@ extern "C" int tgx_ep_fill_synthetic(tgx_ep* ep, uint64_t seed, float w_sigma, f
         if (ep->n_shared)   // its own stream of values: layer l's shared expert at l * per_expert
             EP_CUDA(tg::launch_fill_experts_q4_0(ep->shared + (size_t)l * g.expert_bytes, 1, g, seed ^ 0xC2B2AE3D27D4EB4Full,
                                                  (unsigned long long)l * per_expert, w_sigma, ep->s));
+        if (ep->RT)
+            EP_CUDA(tg::launch_transpose(ep->routers + (size_t)l * nr, ep->RT + (size_t)l * nr, sh.n_experts,
+                                         sh.embed, ep->s));
     }
     EP_CUDA(cudaStreamSynchronize(ep->s));
     return TG_OK;
@@ -512,12 +542,18 @@ extern "C" int tgx_ep_p2p_disconnect(tgx_ep* ep) {
     EP_CHECK(ep, TG_EINVAL, "tgx_ep_p2p_disconnect: null context");
     Dev dg(ep->device);
     EP_CUDA(cudaDeviceSynchronize());
-    for (int q = 0; q < 64; q++)
+    for (int q = 0; q < 64; q++) {
         if (ep->peers[q]) {
             EP_CUDA(cudaIpcCloseMemHandle(ep->peers[q]));
             ep->peers[q] = nullptr;
         }
+        if (ep->fpeers[q]) {
+            EP_CUDA(cudaIpcCloseMemHandle(ep->fpeers[q]));
+            ep->fpeers[q] = nullptr;
+        }
+    }
     ep->p2p_ready = false;
+    ep->fused_ready = false;
     return TG_OK;
 }
 
@@ -564,5 +600,247 @@ extern "C" int tgx_ep_p2p_status(tgx_ep* ep, void* stream) {
         EP_CUDA(cudaMemset(ep->p2p_err, 0, sizeof(flag)));
         return ep_fail(TG_ETIMEOUT, "tgx_ep_moe_layer_p2p: a peer's exchange flag did not arrive within the wait limit");
     }
+    return TG_OK;
+}
+
+// ------------------------------------------------------------ fused decode, experts sharded
+
+// The one-kernel decode step (k_decode_fused) with this rank's experts: every rank
+// routes every layer, streams the gate/up and down rows of the slots whose expert it
+// holds, and stores each output row's per-slot down value into every rank's y buffer
+// over NVLink (tagged 64-bit words, no flag, no fence); each rank then combines all
+// k slots of its rows in slot order, so every rank ends each layer with the same
+// hidden state, bit-identical to one device (tinygiant/engine.py:229-258 per layer).
+extern "C" int tgx_ep_fused_init(tgx_ep* ep, void* handle_out) {
+    EP_CHECK(ep && handle_out, TG_EINVAL, "tgx_ep_fused_init: null argument");
+    EP_CHECK(!ep->ybuf, TG_EINVAL, "tgx_ep_fused_init: already initialised");
+    EP_CHECK(ep->n_shared == 0, TG_EUNSUPPORTED, "tgx_ep_fused_init: the fused path has no shared expert");
+    EP_CHECK(ep->size <= 64, TG_EINVAL, "tgx_ep_fused_init: at most 64 ranks");
+    Dev dg(ep->device);
+    const tgx_shape& sh = ep->shape;
+    const int L = sh.n_layers, E = sh.n_experts, k = sh.top_k, H = sh.embed;
+    int sms = 0, smem_optin = 0;
+    EP_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, ep->device));
+    EP_CUDA(cudaDeviceGetAttribute(&smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ep->device));
+    // the limits of the one-device fused path (count tags, fixed-point sums, 16-byte
+    // router columns, at most 32 polled words per thread)
+    EP_CHECK(sms <= 255 && H <= 16384 && E % 4 == 0 &&
+                 (size_t)H + (size_t)tg::FUSED_ACC * (E + 1) <= 32u * tg::FUSED_THREADS &&
+                 (size_t)k * ep->g.nbI * 6 <= 32u * tg::FUSED_THREADS,
+             TG_EUNSUPPORTED, "tgx_ep_fused_init: shape outside the fused path's limits");
+    std::vector<uint16_t> plan;
+    size_t arena = 0;
+    int max_rows = 0, k_early = 0;
+    EP_CHECK(tg::fused_plan(ep->g, E, k, sms, plan, arena, max_rows, k_early) == 0, TG_EUNSUPPORTED,
+             "tgx_ep_fused_init: shape does not fit one CTA per SM");
+    // The kernel assigns a layer's units per CTA from the number of local slots (units
+    // c, c + G, ... of nloc * nbI) and puts the local down rows after them, or into the
+    // first unit's space when they do not fit the arena: check every CTA and count.
+    {
+        const size_t gu_b = 2 * 32 * ep->g.row_gu;
+        for (int c = 0; c < sms; c++) {
+            const size_t rows = plan[(size_t)c * tg::FUSED_PLAN + 2];
+            for (int nloc = 0; nloc <= k; nloc++) {
+                const int nu = nloc * ep->g.nbI, n = c < nu ? (nu - 1 - c) / sms + 1 : 0;
+                const size_t down = (size_t)nloc * rows * ep->g.row_d;
+                const bool fits = n * gu_b + down <= arena || (n > 0 && down <= gu_b);
+                EP_CHECK(n <= tg::FUSED_MAX_GU && fits, TG_EUNSUPPORTED,
+                         "tgx_ep_fused_init: a CTA's units and down rows do not fit its arena");
+            }
+        }
+    }
+    const size_t nr = (size_t)L * E * H;
+    ep->ybuf_bytes = sizeof(unsigned long long) * 2 * (size_t)L * k * H;
+    EP_TRY(ep_alloc((void**)&ep->RT, sizeof(float) * nr, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->xw, sizeof(unsigned long long) * (size_t)(L + 1) * H, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->facc, sizeof(unsigned long long) * (size_t)L * tg::FUSED_ACC * (E + 1),
+                    "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->hqt, sizeof(unsigned long long) * (size_t)L * k * ep->g.nbI * 6, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->ctl, 256, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->plan, plan.size() * sizeof(uint16_t), "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->fidx, sizeof(int) * (size_t)L * k, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->fw, sizeof(float) * (size_t)L * k, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->flogits, sizeof(float) * (size_t)L * E, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->ybuf, ep->ybuf_bytes, "tgx_ep_fused_init"));
+    EP_TRY(ep_alloc((void**)&ep->ypeer, sizeof(void*) * ep->size, "tgx_ep_fused_init"));
+    EP_CUDA(cudaMemset(ep->xw, 0, sizeof(unsigned long long) * (size_t)(L + 1) * H));
+    EP_CUDA(cudaMemset(ep->facc, 0, sizeof(unsigned long long) * (size_t)L * tg::FUSED_ACC * (E + 1)));
+    EP_CUDA(cudaMemset(ep->hqt, 0, sizeof(unsigned long long) * (size_t)L * k * ep->g.nbI * 6));
+    EP_CUDA(cudaMemset(ep->ctl, 0, 256));
+    EP_CUDA(cudaMemset(ep->ybuf, 0, ep->ybuf_bytes));
+    EP_CUDA(cudaMemcpy(ep->plan, plan.data(), plan.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+    for (int l = 0; l < L; l++)
+        EP_CUDA(tg::launch_transpose(ep->routers + (size_t)l * E * H, ep->RT + (size_t)l * E * H, E, H, ep->s));
+    EP_CUDA(cudaStreamSynchronize(ep->s));
+    tg::FusedParams& P = ep->fp;
+    P = tg::FusedParams{};
+    P.weights = ep->weights;
+    P.layer_bytes = ep->layer_bytes;
+    P.g = ep->g;
+    P.RT = ep->RT;
+    P.normw = ep->norms;
+    P.eps = ep->eps;
+    P.E = E;
+    P.k = k;
+    P.L0 = 0;
+    P.nL = L;
+    P.max_rows = max_rows;
+    P.k_early = 0;
+    P.wait_cycles = tg::FUSED_WAIT_CYCLES;
+    P.missing = 0;
+    P.xw = ep->xw;
+    P.acc = ep->facc;
+    P.hqt = ep->hqt;
+    P.Lmax = L;
+    P.ctl = ep->ctl;
+    P.plan = ep->plan;
+    P.idx_out = ep->fidx;
+    P.w_out = ep->fw;
+    P.logits_out = ep->flogits;
+    P.trace = nullptr;
+    P.arena_bytes = arena;
+    P.e_lo = ep->e_lo;
+    P.e_n = ep->e_n;
+    P.ep_rank = ep->rank;
+    P.ep_size = ep->size;
+    P.ypeer = ep->ypeer;
+    EP_CHECK(tg::fused_smem_layout(P).total <= (uint32_t)smem_optin, TG_EUNSUPPORTED,
+             "tgx_ep_fused_init: shape needs more shared memory per block than the device has");
+    EP_CUDA(tg::fused_prepare(P));
+    int per_sm = 0;
+    EP_CUDA(tg::fused_occupancy(P, &per_sm));
+    EP_CHECK(per_sm >= 1, TG_EUNSUPPORTED, "tgx_ep_fused_init: the kernel does not fit one CTA per SM");
+    ep->fG = sms;
+    cudaIpcMemHandle_t h;
+    EP_CUDA(cudaIpcGetMemHandle(&h, ep->ybuf));
+    memcpy(handle_out, &h, sizeof(h));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_fused_connect(tgx_ep* ep, const void* handles) {
+    EP_CHECK(ep && handles, TG_EINVAL, "tgx_ep_fused_connect: null argument");
+    EP_CHECK(ep->ybuf && !ep->fused_ready, TG_EINVAL, "tgx_ep_fused_connect: call tgx_ep_fused_init first, once");
+    Dev dg(ep->device);
+    const int G = ep->size;
+    std::vector<unsigned long long*> base(G);
+    for (int q = 0; q < G; q++) {
+        if (q == ep->rank) {
+            base[q] = ep->ybuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + (size_t)q * sizeof(h), sizeof(h));
+        EP_CUDA(cudaIpcOpenMemHandle(&ep->fpeers[q], h, cudaIpcMemLazyEnablePeerAccess));
+        base[q] = (unsigned long long*)ep->fpeers[q];
+    }
+    EP_CUDA(cudaMemcpy(ep->ypeer, base.data(), sizeof(void*) * G, cudaMemcpyHostToDevice));
+    ep->fused_ready = true;
+    return TG_OK;
+}
+
+namespace {
+int ep_fused_launch(tgx_ep* ep, const tg::FusedParams& base, float* x_dev, cudaStream_t s) {
+    tg::FusedParams P = base;
+    P.x_in = x_dev;
+    P.x_out = x_dev;   // in place: nL >= 2, or a one-layer model whose CTAs all read x first
+    EP_CHECK(ep->shape.n_layers >= 2 || ep->shape.top_k * ep->g.nbI >= ep->fG, TG_EUNSUPPORTED,
+             "tgx_ep_decode_step: a one-layer model needs a gate/up unit in every CTA");
+    EP_CUDA(tg::launch_decode_fused(P, ep->fG, s));
+    return TG_OK;
+}
+}  // namespace
+
+extern "C" int tgx_ep_decode_step(tgx_ep* ep, float* x_dev, void* stream) {
+    EP_CHECK(ep && x_dev, TG_EINVAL, "tgx_ep_decode_step: null argument");
+    EP_CHECK(ep->fused_ready, TG_EINVAL, "tgx_ep_decode_step: call tgx_ep_fused_init and tgx_ep_fused_connect first");
+    Dev dg(ep->device);
+    return ep_fused_launch(ep, ep->fp, x_dev, (cudaStream_t)stream);
+}
+
+extern "C" int tgx_ep_fused_trace(tgx_ep* ep, float* x_dev, uint64_t* stamps_host, void* stream) {
+    EP_CHECK(ep && x_dev && stamps_host, TG_EINVAL, "tgx_ep_fused_trace: null argument");
+    EP_CHECK(ep->fused_ready, TG_EINVAL, "tgx_ep_fused_trace: call tgx_ep_fused_init and tgx_ep_fused_connect first");
+    Dev dg(ep->device);
+    const size_t n = (size_t)ep->shape.n_layers * ep->fG * tg::FUSED_TRACE;
+    unsigned long long* buf = nullptr;
+    EP_TRY(ep_alloc((void**)&buf, n * 8, "tgx_ep_fused_trace"));
+    tg::FusedParams P = ep->fp;
+    P.trace = buf;
+    cudaError_t e = cudaMemset(buf, 0, n * 8);
+    int rc = e == cudaSuccess ? ep_fused_launch(ep, P, x_dev, (cudaStream_t)stream)
+                              : ep_fail(TG_ECUDA, std::string("tgx_ep_fused_trace: ") + cudaGetErrorString(e));
+    if (rc == TG_OK) {
+        e = cudaStreamSynchronize((cudaStream_t)stream);
+        if (e == cudaSuccess) e = cudaMemcpy(stamps_host, buf, n * 8, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = ep_fail(TG_ECUDA, std::string("tgx_ep_fused_trace: ") + cudaGetErrorString(e));
+    }
+    cudaFree(buf);
+    return rc;
+}
+
+extern "C" int tgx_ep_fused_info(tgx_ep* ep, int* ctas, int* smem_bytes) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_fused_info: null context");
+    if (ctas) *ctas = ep->ybuf ? ep->fG : 0;
+    if (smem_bytes) *smem_bytes = ep->ybuf ? (int)tg::fused_smem_layout(ep->fp).total : 0;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_set_wait_limit(tgx_ep* ep, long long cycles) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_set_wait_limit: null context");
+    EP_CHECK(cycles == 0 || cycles >= 1000, TG_EINVAL, "tgx_ep_set_wait_limit: cycles must be 0 (default) or >= 1000");
+    ep->fp.wait_cycles = cycles ? cycles : tg::FUSED_WAIT_CYCLES;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_fused_last_routing(tgx_ep* ep, int layer, int32_t* idx, float* w) {
+    EP_CHECK(ep && ep->fidx, TG_EINVAL, "tgx_ep_fused_last_routing: null context or fused path not initialised");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_fused_last_routing: layer out of range");
+    Dev dg(ep->device);
+    EP_CUDA(cudaDeviceSynchronize());
+    const int k = ep->shape.top_k;
+    if (idx) EP_CUDA(cudaMemcpy(idx, ep->fidx + (size_t)layer * k, sizeof(int) * k, cudaMemcpyDeviceToHost));
+    if (w) EP_CUDA(cudaMemcpy(w, ep->fw + (size_t)layer * k, sizeof(float) * k, cudaMemcpyDeviceToHost));
+    return TG_OK;
+}
+
+// An expired wait inside the fused step: TG_ETIMEOUT with where it happened.  The
+// state stays as it was; recover with tgx_ep_fused_reset on every rank.
+extern "C" int tgx_ep_fused_status(tgx_ep* ep, void* stream) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_fused_status: null context");
+    if (!ep->ctl) return TG_OK;
+    Dev dg(ep->device);
+    EP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    unsigned ctl[4];
+    EP_CUDA(cudaMemcpy(ctl, ep->ctl, sizeof(ctl), cudaMemcpyDeviceToHost));
+    if (ctl[2] == 0) return TG_OK;
+    return ep_fail(TG_ETIMEOUT, "tgx_ep_decode_step: a bounded device wait expired (stage " + std::to_string(ctl[2]) +
+                                    ", layer " + std::to_string(ctl[3] >> 20) + ", entry " +
+                                    std::to_string((ctl[3] >> 8) & 0xfff) + ")");
+}
+
+// Steps this rank has completed (the launch count that tags the y words).
+extern "C" int tgx_ep_fused_epoch(tgx_ep* ep, unsigned* epoch) {
+    EP_CHECK(ep && epoch && ep->ctl, TG_EINVAL, "tgx_ep_fused_epoch: null argument or fused path not initialised");
+    Dev dg(ep->device);
+    EP_CUDA(cudaDeviceSynchronize());
+    EP_CUDA(cudaMemcpy(epoch, ep->ctl, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    return TG_OK;
+}
+
+// Recovery after a failed step (an expired wait, or a rank that did not take part):
+// clear this rank's cross-CTA state and restart the launch count at `epoch`.  Every
+// rank calls it with the same value, above every rank's tgx_ep_fused_epoch (so the
+// y words stored by the failed step, tagged at most with the old count + 1, are
+// never taken), once no rank has a step in flight.
+extern "C" int tgx_ep_fused_reset(tgx_ep* ep, unsigned epoch) {
+    EP_CHECK(ep && ep->ctl, TG_EINVAL, "tgx_ep_fused_reset: null context or fused path not initialised");
+    Dev dg(ep->device);
+    EP_CUDA(cudaDeviceSynchronize());
+    const tgx_shape& sh = ep->shape;
+    EP_CUDA(cudaMemset(ep->facc, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * tg::FUSED_ACC * (sh.n_experts + 1)));
+    EP_CUDA(cudaMemset(ep->xw, 0, sizeof(unsigned long long) * (size_t)(sh.n_layers + 1) * sh.embed));
+    EP_CUDA(cudaMemset(ep->hqt, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * sh.top_k * ep->g.nbI * 6));
+    const unsigned fresh[4] = {epoch, 0, 0, 0};
+    EP_CUDA(cudaMemcpy(ep->ctl, fresh, sizeof(fresh), cudaMemcpyHostToDevice));
     return TG_OK;
 }

@@ -15,6 +15,9 @@ bit-identical to the single-GPU batched path (and, through it, to the CPU oracle
 The all-reduce moves T * top_k * embed floats per layer.  After enable_p2p() the
 exchange is direct instead: the down kernels store each (token, slot) sum into every
 rank's exchange buffer over NVLink and the combine waits on per-rank epoch flags.
+After enable_fused(), decode_step(x) runs all layers of one token in one persistent
+kernel per rank (the one-GPU fused step over the local experts), the per-slot down
+values crossing NVLink as tagged words inside the kernel.
 
     ep = EPMoEModel(rank=r, size=G, device=local_rank)
     ep.fill_synthetic(seed)            # or load_experts(layer, first, blob) for the local range
@@ -172,6 +175,82 @@ class EPMoEModel:
         buf = (ctypes.c_uint8 * (n * self.size)).from_buffer_copy(b"".join(handles))
         check(self.lib.tgx_ep_p2p_connect(self._ep, buf), self.lib)
         self.p2p = True
+
+    def _gather_handles(self, mine: bytes, exchange):
+        if exchange is not None:
+            return exchange(mine)
+        if self.size == 1:
+            return [mine]
+        import torch.distributed as dist
+        handles = [None] * self.size
+        dist.all_gather_object(handles, mine, group=self.group)
+        return handles
+
+    def enable_fused(self, exchange=None):
+        """Set up the one-kernel decode step over the local experts (tgx_ep_fused_*):
+        every rank must call it, after its weights, routers and norms are set (later
+        router changes are picked up too).  exchange as for enable_p2p."""
+        n = int(self.lib.tgx_ep_p2p_handle_bytes())
+        h = (ctypes.c_uint8 * n)()
+        check(self.lib.tgx_ep_fused_init(self._ep, h), self.lib)
+        mine = bytes(h)
+        handles = self._gather_handles(mine, exchange)
+        assert len(handles) == self.size and handles[self.rank] == mine
+        buf = (ctypes.c_uint8 * (n * self.size)).from_buffer_copy(b"".join(handles))
+        check(self.lib.tgx_ep_fused_connect(self._ep, buf), self.lib)
+        self.p2p = True   # close() disconnects the mappings before the barrier
+        self.fused = True
+
+    def decode_step(self, x, stream=None):
+        """All layers of one token (cuda f32[embed], the same on every rank) in place,
+        in one kernel per rank; every rank ends with the same x."""
+        assert x.dim() == 1 and x.shape[0] == self.embed and x.is_contiguous()
+        check(self.lib.tgx_ep_decode_step(self._ep, _dev_ptr(x), _stream_handle(stream)), self.lib)
+
+    def fused_trace(self, x, stream=None) -> np.ndarray:
+        """decode_step with phase stamps: u64 [layers][CTAs][32] (globaltimer ns at
+        0..15, clock64 at 16..31)."""
+        ctas = ctypes.c_int()
+        check(self.lib.tgx_ep_fused_info(self._ep, ctypes.byref(ctas), None), self.lib)
+        out = np.zeros((self.n_layers, ctas.value, 32), np.uint64)
+        check(self.lib.tgx_ep_fused_trace(self._ep, _dev_ptr(x), out.ctypes.data, _stream_handle(stream)), self.lib)
+        return out
+
+    def fused_routing(self, layer: int):
+        """(expert ids, weights) of the last fused step at `layer`."""
+        idx = np.zeros(self.top_k, np.int32)
+        w = np.zeros(self.top_k, np.float32)
+        check(self.lib.tgx_ep_fused_last_routing(self._ep, layer, idx.ctypes.data, w.ctypes.data), self.lib)
+        return idx, w
+
+    def set_wait_limit(self, cycles: int):
+        check(self.lib.tgx_ep_set_wait_limit(self._ep, int(cycles)), self.lib)
+
+    def fused_status(self, stream=None):
+        check(self.lib.tgx_ep_fused_status(self._ep, _stream_handle(stream)), self.lib)
+
+    def fused_epoch(self) -> int:
+        e = ctypes.c_uint()
+        check(self.lib.tgx_ep_fused_epoch(self._ep, ctypes.byref(e)), self.lib)
+        return e.value
+
+    def fused_recover(self, max_over_ranks=None):
+        """After a failed step on any rank: every rank calls this; it restarts all ranks'
+        launch count at one above the largest (max_over_ranks(int) -> int; default: a
+        MAX all-reduce over self.group)."""
+        e = self.fused_epoch()
+        if max_over_ranks is not None:
+            top = int(max_over_ranks(e))
+        elif self.size == 1:
+            top = e
+        else:
+            import torch
+            import torch.distributed as dist
+            dev = "cpu" if dist.get_backend(self.group) == "gloo" else torch.device("cuda", self.device)
+            t = torch.tensor([e], dtype=torch.int64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+            top = int(t.item())
+        check(self.lib.tgx_ep_fused_reset(self._ep, top + 1), self.lib)
 
     def p2p_status(self, stream=None):
         check(self.lib.tgx_ep_p2p_status(self._ep, _stream_handle(stream)), self.lib)
