@@ -84,6 +84,10 @@ def parse():
     ap.add_argument("--p2p", action="store_true",
                     help="with --ep: exchange by direct NVLink stores and flags (tgx_ep_moe_layer_p2p) instead "
                          "of the NCCL all-reduce")
+    ap.add_argument("--dispatch", action="store_true",
+                    help="with --ep: token dispatch instead of replicated tokens: each rank holds T/N of the "
+                         "tokens and sends each (token, slot) pair's Q8_0 row to its expert's holder and gets y "
+                         "back (NCCL all-to-alls, tgx_ep_dispatch*)")
     ap.add_argument("--batched-kernels", choices=["auto", "dp4a", "mma"], default="auto",
                     help="expert matmuls of the batched / EP path: auto (tensor cores from 16 pairs per expert), "
                          "dp4a, or mma (tcgen05); all give the same bits")
@@ -1155,7 +1159,7 @@ def run_ep(args):
     ep = EPMoEModel(h, inter, e_all, K_TOP, NL, rank=rank, size=ws, device=local, n_shared=n_sh)
     ep.fill_synthetic(args.seed)                          # one model, sharded: the same seed on every rank
     ep.set_kernels(KERNELS[args.batched_kernels])
-    if args.p2p:
+    if args.p2p and not args.dispatch:
         ep.enable_p2p(max(args.token_list))
     for T in args.token_list:
         ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist)
@@ -1169,24 +1173,37 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
     import torch
     K, W = args.steps, max(3, args.warmup)
     gen = torch.Generator(device="cuda").manual_seed(args.seed + 1)
-    pool = [torch.randn(T, h, generator=gen, device="cuda") for _ in range(4)]
-    X = torch.empty(T, h, device="cuda")
+    disp = args.dispatch
+    # token dispatch: this rank's share [lo, lo + Tl) of the step's T tokens
+    sizes = [len(c) for c in torch.tensor_split(torch.arange(T), ws)] if disp else [T] * ws
+    lo, Tl = sum(sizes[:rank]) if disp else 0, sizes[rank]
+    pool = [torch.randn(T, h, generator=gen, device="cuda")[lo:lo + Tl].contiguous() for _ in range(4)]
+    X = torch.empty(Tl, h, device="cuda")
     stream = torch.cuda.current_stream()
     X.copy_(pool[0])
-    ep.decode(X)                                          # allocates scratch and the exchange buffer
+    stats = {}
+    if disp:
+        ep.decode_dispatch(X, stats=stats)                # grows the buffers; counts the bytes received
+    else:
+        ep.decode(X)                                      # allocates scratch and the exchange buffer
     torch.cuda.synchronize()
     graph, graphed = torch.cuda.CUDAGraph(), False
-    try:
-        with torch.cuda.graph(graph):
-            ep.decode(X)
-        graphed = True
-    except Exception:                                     # eager launches otherwise (same kernels)
-        graph = None
+    if disp:
+        graph = None                                      # the all-to-all sizes come from the host each layer
+    else:
+        try:
+            with torch.cuda.graph(graph):
+                ep.decode(X)
+            graphed = True
+        except Exception:                                 # eager launches otherwise (same kernels)
+            graph = None
     torch.cuda.synchronize()
 
     def step():
         if graphed:
             graph.replay()
+        elif disp:
+            ep.decode_dispatch(X)
         else:
             ep.decode(X)
 
@@ -1209,6 +1226,11 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
     torch.cuda.synchronize()
     clocks.stop()
     ms = ev0.elapsed_time(ev1)
+    recv_layer = stats.get("recv_bytes", 0) / max(1, stats.get("layers", 1))
+    if dist and disp:
+        t = torch.tensor([recv_layer], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        recv_layer = float(t.item())
     Xh = pool[1].cpu().pin_memory()
     Yh = torch.empty_like(Xh).pin_memory()
     if dist:
@@ -1228,8 +1250,9 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
         t = torch.tensor([ms, ems], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms, ems = float(t[0]), float(t[1])
-    if getattr(ep, "p2p", False):
+    if getattr(ep, "p2p", False) and not disp:
         ep.p2p_status()                                   # raises if a peer's flag wait expired
+    ep.status()
     assert torch.isfinite(Yh).all()
     del graph                                             # holds NCCL calls: released before the group
     if rank == 0:
@@ -1250,13 +1273,19 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
             "config": {"workload": f"{'configs[4]' if args.shape == 'dsv3' else 'configs[2]'}: {T} tokens per step, "
                                    f"{NL} of {full_layers} layers, experts sharded {e_all // ws} per GPU"
                                    f"{' + the shared expert' if n_sh else ''}, "
-                                   f"{'NVLink stores + flags' if args.p2p else 'NCCL all-reduce'} of y per layer",
+                                   + ("tokens sharded, pairs dispatched to their experts' holders and back "
+                                      "(NCCL all-to-alls)" if disp else
+                                      f"{'NVLink stores + flags' if args.p2p else 'NCCL all-reduce'} of y per layer"),
                        "hidden": h, "inter": inter, "experts": e_all, "shared_experts": n_sh, "top_k": K_TOP,
                        "layers": NL, "full_layers": full_layers, "tokens": T, "parallelism": f"ep{ws}",
                        "cuda_graph": graphed, "batched_kernels": args.batched_kernels,
-                       "exchange": "p2p" if args.p2p else "nccl_all_reduce"},
+                       "exchange": "dispatch" if disp else ("p2p" if args.p2p else "nccl_all_reduce")},
             "tok_s_full_depth": value * NL / full_layers,
             "exchange_bytes_per_layer": T * (K_TOP + n_sh) * h * 4,
+            "recv_bytes_per_layer_per_rank": (recv_layer if disp else T * (K_TOP + n_sh) * h * 4),
+            "recv_bytes_def": ("max over ranks of the records (16 B + Q8_0 row) and y rows (4 B x hidden) "
+                               "a rank receives per layer" if disp else
+                               "y of every (token, slot) pair, which every rank receives"),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak * ws, "unit": "GB/s",
                          "frac": achieved / (peak * ws), "traffic": None,
                          "algorithmic_bytes": alg,
@@ -1265,7 +1294,7 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback"},
             "e2e": {"value": T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * h * 4,
                     "d2h_bytes_per_step": T * h * 4},
-            "gpu_launches": (6 + (1 if args.shape == "dsv3" else 0)) * NL * K,
+            "gpu_launches": ((7 if disp else 6) + (1 if args.shape == "dsv3" else 0)) * NL * K,
             "clocks": clocks.summary(),
         }))
 

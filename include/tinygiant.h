@@ -406,6 +406,29 @@ int tgx_ep_fused_status(tgx_ep *ep, void *stream);
 int tgx_ep_fused_epoch(tgx_ep *ep, unsigned *epoch);
 int tgx_ep_fused_reset(tgx_ep *ep, unsigned epoch);
 
+/* Token dispatch: every rank holds its OWN tokens (not a copy of all of them).  Per layer:
+ *   tgx_ep_dispatch(ep, layer, x, T, send, counts, s)  route this rank's T tokens
+ *       (x: device f32[T][embed]); one record of tgx_ep_record_bytes(ep) bytes per (token,
+ *       slot) pair into send (device, T * (top_k + n_shared) records), grouped by
+ *       destination rank in rank order: a routed slot goes to its expert's holder, the
+ *       shared slot stays on this rank; counts (device int[ep_size]) = records per rank.
+ *       A record is a 16-byte header (int32 expert id, int32 pair index t * slots + j at
+ *       the sender, 0, 0) and the token's Q8_0 row in ggml form.
+ *   (caller) exchange the counts, then the records (an all-to-all: rank q's group of
+ *       this rank's send goes to rank q, received groups in source-rank order)
+ *   tgx_ep_dispatch_experts(ep, layer, recv, n, y, s)  the n received records' expert
+ *       FFNs, y: device f32[n][embed] in record order
+ *   (caller) the reverse all-to-all of y, so each rank gets back one row per record it
+ *       sent, in its send order
+ *   tgx_ep_dispatch_combine(ep, x, T, y_back, s)  x[t] += sum_j w[t][j] * y[(t, j)] in
+ *       slot order.
+ * Bit-identical to the single-device batched path (tinygiant/engine.py:229-258 per
+ * token).  tgx_ep_status reports an expired wait of the tensor-core expert kernels. */
+size_t tgx_ep_record_bytes(const tgx_ep *ep);
+int tgx_ep_dispatch(tgx_ep *ep, int layer, const float *x_dev, int T, void *send_dev, int *counts_dev, void *stream);
+int tgx_ep_dispatch_experts(tgx_ep *ep, int layer, const void *recv_dev, int n_recv, float *y_dev, void *stream);
+int tgx_ep_dispatch_combine(tgx_ep *ep, float *x_dev, int T, const float *y_back_dev, void *stream);
+
 /* ===================== the reference's formats on device pointers ===================== */
 
 /* Device bytes of a rows x cols matrix of format fmt (0 Q4_K, 1 f16, 2 Q6_K, 4 f32;

@@ -7,6 +7,9 @@ experts.  EP_MODE:
   fused  one persistent kernel per rank and token over all layers (tgx_ep_decode_step),
          against the single-GPU fused step (tgx_decode_step); every rank's hidden
          state must equal rank 0's
+  dispatch  every rank holds its own share of the T tokens; each (token, slot) pair
+         travels to its expert's holder and back (NCCL all-to-alls, tgx_ep_dispatch*),
+         against the single-GPU batched path
 EP_SKIP=1 afterwards makes rank 1 skip one step: rank 0's bounded wait must run out and
 report TG_ETIMEOUT, nothing faults, and (fused) both ranks recover and decode bit-exact
 again.  Exit status 0 = bit-identical."""
@@ -58,6 +61,8 @@ def main() -> int:
             # every rank holds the same state; rank 0's equals one GPU's
             xs = [torch.empty_like(X) for _ in range(world)]
             dist.all_gather(xs, X)
+            if mode == "dispatch":   # X: every rank's share, gathered back into the T tokens
+                xs = [X]
             if rank == 0:
                 if mode == "fused":
                     for t in range(X0.shape[0]):
@@ -76,6 +81,16 @@ def main() -> int:
             dist.barrier()      # the ranks' steps start together (a lagging rank would be waited on)
             if mode == "fused":
                 fused_tokens(X)
+            elif mode == "dispatch":
+                sizes = [len(c) for c in torch.tensor_split(torch.arange(T), world)]
+                mine = torch.tensor_split(X, world)[rank].contiguous()
+                ep.decode_dispatch(mine)
+                ep.status()
+                pad = torch.zeros(max(sizes), H, device="cuda")
+                pad[: sizes[rank]] = mine
+                parts = [torch.empty_like(pad) for _ in range(world)]
+                dist.all_gather(parts, pad)
+                X = torch.cat([p[:n] for p, n in zip(parts, sizes)])
             else:
                 ep.decode(X)
                 torch.cuda.synchronize()

@@ -176,6 +176,93 @@ def test_ep_rejects_foreign_experts():
     ep.close()
 
 
+def _dispatch_emulated(ranks, shards, L):
+    """Token dispatch of G ranks on one GPU: each rank's dispatch, the all-to-alls as
+    tensor copies (records to their destinations in source-rank order, y rows back in
+    each source's send order), the experts and the combine; no kernel waits on another."""
+    import torch
+    G = len(ranks)
+    rb = ranks[0].record_bytes()
+    for layer in range(L):
+        sends = [ep.dispatch(layer, xs) for ep, xs in zip(ranks, shards)]
+        counts = [c.cpu().tolist() for _, c in sends]          # counts[src][dst]
+        ys = []
+        for q, ep in enumerate(ranks):
+            parts = [sends[src][0][sum(counts[src][:q]) * rb:(sum(counts[src][:q]) + counts[src][q]) * rb]
+                     for src in range(G)]
+            n = sum(counts[src][q] for src in range(G))
+            ys.append(ep.dispatch_experts(layer, torch.cat(parts), n).clone())
+        for src, ep in enumerate(ranks):
+            parts = []
+            for q in range(G):
+                off = sum(counts[s2][q] for s2 in range(src))
+                parts.append(ys[q][off:off + counts[src][q]])
+            ep.dispatch_combine(shards[src], torch.cat(parts).reshape(-1))
+
+
+@pytest.mark.parametrize("G,T,kernels", [(1, 5, 0), (2, 7, 1), (4, 64, 0), (8, 300, 2), (8, 41, 1)])
+def test_ep_dispatch_emulated_matches_single_gpu(G, T, kernels):
+    # every rank holds its own tokens; the (token, slot) pairs travel to their experts'
+    # holders and back: the result must be the single-GPU batched path's, bit for bit
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    from tinygiant_b200.ep import EPMoEModel
+    L = 2
+    full = MoEModel(H, I, E, K, L)
+    full.fill_synthetic(77)
+    ranks = [EPMoEModel(H, I, E, K, L, rank=r, size=G) for r in range(G)]
+    for ep in ranks:
+        ep.fill_synthetic(77)
+        ep.set_kernels(kernels)
+    X = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(T), device="cuda")
+    want = X.clone()
+    full.decode_batched(want)
+    shards = [s.contiguous() for s in torch.tensor_split(X.clone(), G)]
+    _dispatch_emulated(ranks, shards, L)
+    for ep in ranks:
+        ep.status()
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(shards).view(torch.int32), want.view(torch.int32))
+    # a record is the 16-byte header and the Q8_0 row: 2,176 bytes at embed 2048
+    assert ranks[0].record_bytes() == 16 + H // 32 * 34
+    for ep in ranks:
+        ep.close()
+    full.close()
+
+
+@pytest.mark.parametrize("G", [1, 2, 4])
+def test_ep_dispatch_shared_expert_matches_oracle(oracle, G):
+    # host-made weights, a shared expert (dispatched to the token's own rank), two layers
+    import numpy as np
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    h, i, e, k, L, T = 512, 256, 16, 4, 2, 9
+    rng = np.random.default_rng(12)
+    eb = oracle.expert_bytes(h, i)
+    blobs = [oracle.quantize_q4_0(oracle.fill_normal(e * 3 * h * i, 31 + l, 0.05)) for l in range(L)]
+    shared = [oracle.quantize_q4_0(oracle.fill_normal(3 * h * i, 61 + l, 0.05)) for l in range(L)]
+    routers = [oracle.fill_normal(e * h, 91 + l, 0.05).reshape(e, h) for l in range(L)]
+    norms = [rng.uniform(0.5, 1.5, h).astype(np.float32) for _ in range(L)]
+    ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G, n_shared=1) for r in range(G)]
+    for ep in ranks:
+        for l in range(L):
+            ep.load_experts(l, ep.first, blobs[l][ep.first * eb:(ep.first + ep.n_local) * eb])
+            ep.load_shared(l, shared[l])
+            ep.set_router(l, routers[l])
+            ep.set_ffn_norm(l, norms[l])
+    X0 = rng.standard_normal((T, h)).astype(np.float32)
+    shards = [torch.from_numpy(s.copy()).cuda() for s in np.array_split(X0, G)]
+    _dispatch_emulated(ranks, shards, L)
+    torch.cuda.synchronize()
+    ref = X0.copy()
+    for l in range(L):
+        ref = oracle.moe_block_batched(blobs[l], routers[l], ref, k, h, i, normw=norms[l], shared=shared[l])
+    got = torch.cat(shards).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    for ep in ranks:
+        ep.close()
+
+
 def test_ep_fused_single_rank_matches_decode_step():
     # the one-kernel EP step with one rank (every expert local, its own y buffer): odd and
     # even step counts (both buffer halves), a router changed after set-up, a graph replay,
@@ -226,7 +313,7 @@ def test_ep_fused_single_rank_matches_decode_step():
 @pytest.mark.parametrize("mode,layers,repeat,skip", [("nccl", 3, 1, "0"), ("p2p", 3, 1, "0"), ("p2p", 3, 4, "0"),
                                                      ("p2p", 1, 5, "0"), ("p2p", 3, 2, "1"),
                                                      ("fused", 3, 3, "0"), ("fused", 2, 2, "1"),
-                                                     ("fused", 48, 1, "0")])
+                                                     ("fused", 48, 1, "0"), ("dispatch", 3, 2, "0")])
 def test_ep_multi_gpu_matches_single_gpu(mode, layers, repeat, skip):
     # p2p: the exchange by direct NVLink stores and flags instead of the all-reduce; fused:
     # one kernel per rank and token; odd layer counts with several decodes back to back
@@ -238,7 +325,7 @@ def test_ep_multi_gpu_matches_single_gpu(mode, layers, repeat, skip):
     # skip = 1: afterwards rank 1 skips one step and rank 0 must report TG_ETIMEOUT
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_MODE=mode, EP_LAYERS=str(layers), EP_REPEAT=str(repeat),
                EP_SKIP=skip)
-    port = 29531 + ("nccl", "p2p", "fused").index(mode) + 3 * layers + 200 * repeat + 1000 * int(skip)
+    port = 29531 + ("nccl", "p2p", "fused", "dispatch").index(mode) + 4 * layers + 200 * repeat + 1000 * int(skip)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
            str(ROOT / "tests" / "ep_worker.py")]

@@ -126,6 +126,10 @@ PROTOTYPES = {
     "tgx_ep_fused_status": (CI, [VP, VP]),
     "tgx_ep_fused_epoch": (CI, [VP, ctypes.POINTER(ctypes.c_uint)]),
     "tgx_ep_fused_reset": (CI, [VP, ctypes.c_uint]),
+    "tgx_ep_record_bytes": (SZ, [VP]),
+    "tgx_ep_dispatch": (CI, [VP, CI, VP, CI, VP, VP, VP]),
+    "tgx_ep_dispatch_experts": (CI, [VP, CI, VP, CI, VP, VP]),
+    "tgx_ep_dispatch_combine": (CI, [VP, VP, CI, VP, VP]),
     "tgx_set_batched_kernels": (CI, [VP, CI]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),

@@ -432,12 +432,16 @@ size_t batched_smem_bytes(const Geom& g) {
 
 static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
 
+size_t experts_scratch_bytes(const Geom& g, int E, int n_shared, size_t n_pairs) {
+    const size_t E_tot = (size_t)E + n_shared;
+    return r256(4) + r256((E_tot + 1) * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256((E_tot + 2) * 4) +
+           r256(n_pairs * act_bytes(g.nbI)) + r256(n_pairs * g.I * 4) + r256(n_pairs * g.I * 4);
+}
+
 size_t batched_partial_bytes(const Geom& g, int E, int n_shared, int k, int T) {
-    const size_t ks = (size_t)k + n_shared, n_pairs = (size_t)T * ks, E_tot = (size_t)E + n_shared;
-    return r256((size_t)T * E * 8) + r256((E_tot + 1) * 4) + r256((size_t)T * act_bytes(g.nbH)) + r256(n_pairs * 4) +
-           r256(n_pairs * 4) + r256((E_tot + 1) * 4) + r256(n_pairs * 4) + r256((E_tot + 2) * 4) +
-           r256(n_pairs * act_bytes(g.nbI)) +
-           r256(n_pairs * g.I * 4) + r256(n_pairs * g.I * 4) + 256;
+    const size_t ks = (size_t)k + n_shared, n_pairs = (size_t)T * ks;
+    return experts_scratch_bytes(g, E, n_shared, n_pairs) + r256((size_t)T * E * 8) +
+           r256((size_t)T * act_bytes(g.nbH)) + r256(n_pairs * 4) + r256(n_pairs * 4);
 }
 
 // the tensor-core expert matmuls pay off once experts average this many (token, slot)
@@ -449,33 +453,23 @@ size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
     return batched_partial_bytes(g, E, 0, k, T) + r256(n_pairs * 4) + n_pairs * g.H * 4;
 }
 
-cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shared, int e_lo, int e_n, int rank,
-                                       int G, Geom g, const float* R, const float* normw, float eps, int E,
-                                       int n_shared, int k, const float* X, int T, void* scratch,
-                                       size_t scratch_bytes, float* y, int* idx_out, float* w_out,
-                                       float* logits_out, int kernels, cudaStream_t s, bool zero_y,
-                                       int* owned) {
-    if (T <= 0) return cudaSuccess;
-    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || n_shared < 0 || n_shared > 1 ||
-        (n_shared && !shared) || k + n_shared > MAX_TOPK + 1 || G < 1 || rank < 0 || rank >= G || e_n * G != E ||
-        e_lo != rank * e_n || batched_partial_bytes(g, E, n_shared, k, T) > scratch_bytes)
-        return cudaErrorInvalidValue;
-    const int ks = k + n_shared, E_tot = E + n_shared;
-    const size_t n_pairs = (size_t)T * ks;
+cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, int e_n, int rank,
+                                   int G, Geom g, int n_shared, int k, int ks, const int* idx, int n_tok,
+                                   const uint8_t* xq, void* scratch, size_t scratch_bytes, float* y, int* owned,
+                                   int kernels, int pairs_per_expert_div, cudaStream_t s, unsigned* err_flag) {
+    const size_t n_pairs = (size_t)n_tok * ks;
+    const int E_tot = E + n_shared;
+    if (n_tok <= 0) return cudaSuccess;
+    if (experts_scratch_bytes(g, E, n_shared, n_pairs) > scratch_bytes) return cudaErrorInvalidValue;
     uint8_t* p = static_cast<uint8_t*>(scratch);
     auto take = [&](size_t n) {
         uint8_t* r = p;
         p += r256(n);
         return r;
     };
-    unsigned* err = reinterpret_cast<unsigned*>(take(4));   // first: at the scratch's start for every T
-    unsigned long long* S = reinterpret_cast<unsigned long long*>(take((size_t)T * E * 8));
+    unsigned* err = reinterpret_cast<unsigned*>(take(4));   // first: at the scratch's start
+    if (err_flag) err = err_flag;
     int* active = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
-    uint8_t* xq = take((size_t)T * act_bytes(g.nbH));
-    int* idx_s = reinterpret_cast<int*>(take(n_pairs * 4));
-    float* wts_s = reinterpret_cast<float*>(take(n_pairs * 4));
-    int* idx = idx_out ? idx_out : idx_s;
-    float* wts = w_out ? w_out : wts_s;
     int* off = reinterpret_cast<int*>(take((size_t)(E_tot + 1) * 4));
     int* list = reinterpret_cast<int*>(take(n_pairs * 4));
     int* tile_pre = reinterpret_cast<int*>(take((size_t)(E_tot + 2) * 4));
@@ -488,19 +482,13 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
     if (batched_smem_bytes(g) > (size_t)optin) return cudaErrorInvalidValue;
-    if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
-    // pairs computed on other devices keep y = 0 (their owner adds theirs)
-    if (G > 1 && zero_y && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
-    k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
-                                                                                                g.H, S);
-    k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, ks, S, idx, wts, logits_out, xq);
     k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active, owned,
                                     tile_pre, q4_mma_tile_tokens());
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
     const bool mma = q4_mma_supported(g) &&
                      (kernels == BATCHED_MMA ||
-                      (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * (E + n_shared)));
+                      (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * pairs_per_expert_div));
     if (mma) {
         if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, tile_pre, n_act, ks, xq, hf, uf, err,
                                s)) != cudaSuccess)
@@ -511,7 +499,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                              s);
     }
     const int R_gu = gu_rows(g, (size_t)optin);
-    const bool wide = n_pairs >= (size_t)WIDE_MIN_PAIRS * (E + n_shared);
+    const bool wide = n_pairs >= (size_t)WIDE_MIN_PAIRS * pairs_per_expert_div;
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
     auto gateup = [&](auto kern, int rows_per_cta) -> cudaError_t {
         cudaError_t r;
@@ -542,6 +530,57 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
         return cudaGetLastError();
     };
     return wide ? down(k_down_batched<16>) : down(k_down_batched<4>);
+}
+
+cudaError_t launch_batched_route(Geom g, const float* R, const float* normw, float eps, int E, int n_shared, int k,
+                                 const float* X, int T, unsigned long long* S, int* idx, float* wts, float* logits_out,
+                                 uint8_t* xq, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    const int ks = k + n_shared;
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(S, 0, (size_t)T * E * 8, s)) != cudaSuccess) return e;
+    k_router_sums_batched<<<dim3((T + RT_TOK - 1) / RT_TOK, (E + 7) / 8, g.H / 256), 256, 0, s>>>(X, T, R, normw, E,
+                                                                                                g.H, S);
+    k_topk_quant_batched<<<T, 256, 0, s>>>(X, normw, eps, E, g.H, k, ks, S, idx, wts, logits_out, xq);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shared, int e_lo, int e_n, int rank,
+                                       int G, Geom g, const float* R, const float* normw, float eps, int E,
+                                       int n_shared, int k, const float* X, int T, void* scratch,
+                                       size_t scratch_bytes, float* y, int* idx_out, float* w_out,
+                                       float* logits_out, int kernels, cudaStream_t s, bool zero_y,
+                                       int* owned) {
+    if (T <= 0) return cudaSuccess;
+    if (E <= 0 || E > 1024 || k <= 0 || k > MAX_TOPK || k > E || n_shared < 0 || n_shared > 1 ||
+        (n_shared && !shared) || k + n_shared > MAX_TOPK + 1 || G < 1 || rank < 0 || rank >= G || e_n * G != E ||
+        e_lo != rank * e_n || batched_partial_bytes(g, E, n_shared, k, T) > scratch_bytes)
+        return cudaErrorInvalidValue;
+    const int ks = k + n_shared;
+    const size_t n_pairs = (size_t)T * ks;
+    // the expert step's scratch (error flag first, so at the scratch's start), then the
+    // routing buffers
+    const size_t xs = experts_scratch_bytes(g, E, n_shared, n_pairs);
+    uint8_t* p = static_cast<uint8_t*>(scratch) + xs;
+    auto take = [&](size_t n) {
+        uint8_t* r = p;
+        p += r256(n);
+        return r;
+    };
+    unsigned long long* S = reinterpret_cast<unsigned long long*>(take((size_t)T * E * 8));
+    uint8_t* xq = take((size_t)T * act_bytes(g.nbH));
+    int* idx_s = reinterpret_cast<int*>(take(n_pairs * 4));
+    float* wts_s = reinterpret_cast<float*>(take(n_pairs * 4));
+    int* idx = idx_out ? idx_out : idx_s;
+    float* wts = w_out ? w_out : wts_s;
+    cudaError_t e;
+    // pairs computed on other devices keep y = 0 (their owner adds theirs)
+    if (G > 1 && zero_y && (e = cudaMemsetAsync(y, 0, n_pairs * g.H * 4, s)) != cudaSuccess) return e;
+    if ((e = launch_batched_route(g, R, normw, eps, E, n_shared, k, X, T, S, idx, wts, logits_out, xq, s)) !=
+        cudaSuccess)
+        return e;
+    return launch_batched_experts(layer, shared, E, e_lo, e_n, rank, G, g, n_shared, k, ks, idx, T, xq, scratch, xs, y,
+                                  owned, kernels, E + n_shared, s);
 }
 
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,

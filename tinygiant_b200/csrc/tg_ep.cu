@@ -20,6 +20,7 @@
 
 #include "../../include/tinygiant.h"
 #include "tg_decode.h"
+#include "tg_device.cuh"
 #include "tg_internal.h"
 
 using tg::Geom;
@@ -76,6 +77,13 @@ struct tgx_ep {
     void* fpeers[64] = {};              // opened peer y buffers (null for this rank)
     unsigned long long** ypeer = nullptr;   // [G] device pointers to every rank's y buffer
     tg::FusedParams fp{};
+    // token dispatch (tgx_ep_dispatch*): routing state of this rank's tokens between the
+    // dispatch and the combine, and the receive side's activation rows and expert scratch
+    void* dscratch = nullptr;
+    size_t dscratch_bytes = 0;
+    int d_T = 0;                        // tokens of the last tgx_ep_dispatch
+    float* d_wts = nullptr;             // [T][ks] their routing weights
+    int* d_slot = nullptr;              // [T][ks] each pair's record index in the send order
 };
 
 namespace {
@@ -121,7 +129,7 @@ void ep_free(tgx_ep* c) {
                     (void*)c->p2p_count, (void*)c->owned})
         if (p) cudaFree(p);
     for (void* p : {(void*)c->RT, (void*)c->xw, (void*)c->facc, (void*)c->hqt, (void*)c->ctl, (void*)c->plan,
-                    (void*)c->fidx, (void*)c->fw, (void*)c->flogits, (void*)c->ybuf, (void*)c->ypeer})
+                    (void*)c->fidx, (void*)c->fw, (void*)c->flogits, (void*)c->ybuf, (void*)c->ypeer, c->dscratch})
         if (p) cudaFree(p);
     for (void* p : {(void*)c->weights, (void*)c->shared, (void*)c->routers, (void*)c->norms, (void*)c->staging,
                     c->scratch, (void*)c->wts})
@@ -377,14 +385,17 @@ extern "C" int tgx_ep_set_kernels(tgx_ep* ep, int kernels) {
 
 extern "C" int tgx_ep_status(tgx_ep* ep, void* stream) {
     EP_CHECK(ep, TG_EINVAL, "tgx_ep_status: null context");
-    if (!ep->scratch) return TG_OK;
     Dev dg(ep->device);
     EP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
-    unsigned flag = 0;
-    EP_CUDA(cudaMemcpy(&flag, ep->scratch, sizeof(flag), cudaMemcpyDeviceToHost));
-    if (flag) {
-        EP_CUDA(cudaMemset(ep->scratch, 0, sizeof(flag)));
-        return ep_fail(TG_ETIMEOUT, "tgx_ep: a tensor-core expert kernel's bounded wait expired");
+    // the partial step's flag and the token dispatch's
+    for (void* f : {ep->scratch, ep->dscratch}) {
+        if (!f) continue;
+        unsigned flag = 0;
+        EP_CUDA(cudaMemcpy(&flag, f, sizeof(flag), cudaMemcpyDeviceToHost));
+        if (flag) {
+            EP_CUDA(cudaMemset(f, 0, sizeof(flag)));
+            return ep_fail(TG_ETIMEOUT, "tgx_ep: a tensor-core expert kernel's bounded wait expired");
+        }
     }
     return TG_OK;
 }
@@ -842,5 +853,255 @@ extern "C" int tgx_ep_fused_reset(tgx_ep* ep, unsigned epoch) {
     EP_CUDA(cudaMemset(ep->hqt, 0, sizeof(unsigned long long) * (size_t)sh.n_layers * sh.top_k * ep->g.nbI * 6));
     const unsigned fresh[4] = {epoch, 0, 0, 0};
     EP_CUDA(cudaMemcpy(ep->ctl, fresh, sizeof(fresh), cudaMemcpyHostToDevice));
+    return TG_OK;
+}
+
+// ------------------------------------------------------------ token dispatch
+
+// Every rank holds its own tokens.  Per layer:
+//   tgx_ep_dispatch          route this rank's T tokens (the batched path's routing and
+//                            Q8_0 activation rows), then one record per (token, slot) pair
+//                            in destination-rank order: a routed slot goes to its
+//                            expert's holder, the shared slot stays here; per-rank counts
+//   (caller)                 exchange the counts, then the records (any all-to-all)
+//   tgx_ep_dispatch_experts  the received records' expert FFNs: y [n][H], record order
+//   (caller)                 send each y row back to the record's sender (the reverse
+//                            all-to-all, so rows return in send order)
+//   tgx_ep_dispatch_combine  x[t] += sum_j w[t][j] * y[(t, j)] in slot order
+// A record carries the pair's Q8_0 activation row in ggml form (nbH blocks of fp16 scale +
+// 32 codes) behind 16 bytes of header (expert id).  The expert kernels are the batched
+// path's and each pair's arithmetic is independent of the others, so the result is the
+// single-device batched path's bit for bit (tinygiant/engine.py:229-258 per token).
+
+namespace {
+
+using tg::ActView;
+using tg::act_bytes;
+using tg::act_view;
+using tg::f16_bits_to_f32;
+using tg::f32_to_f16_bits;
+
+constexpr int REC_HDR = 16;
+
+size_t rec_bytes(const Geom& g) { return REC_HDR + (size_t)g.nbH * 34; }
+size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// one CTA of 1024 threads: destination of every pair, counts per rank, and a record
+// index per pair (destination-major; the order inside a destination does not affect
+// any result); send_map[record] = pair
+__global__ void __launch_bounds__(1024) k_dispatch_plan(const int* __restrict__ idx, int n_pairs, int ks, int k,
+                                                        int e_n, int rank, int G, int* __restrict__ counts,
+                                                        int* __restrict__ pair_slot, int* __restrict__ send_map) {
+    __shared__ int cnt[64], base[65];
+    for (int q = threadIdx.x; q < G; q += blockDim.x) cnt[q] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) {
+        const int j = p % ks;
+        atomicAdd(&cnt[j < k ? idx[p] / e_n : rank], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int a = 0;
+        for (int q = 0; q < G; q++) {
+            base[q] = a;
+            counts[q] = cnt[q];
+            a += cnt[q];
+            cnt[q] = 0;
+        }
+        base[G] = a;
+    }
+    __syncthreads();
+    for (int p = threadIdx.x; p < n_pairs; p += blockDim.x) {
+        const int j = p % ks, q = j < k ? idx[p] / e_n : rank;
+        const int slot = base[q] + atomicAdd(&cnt[q], 1);
+        pair_slot[p] = slot;
+        send_map[slot] = p;
+    }
+}
+
+// grid n_records, 128 threads: record i = pair p = send_map[i] of token t: header (expert
+// id, p) and the token's Q8_0 row in ggml form (the fp16 scale is the activation's own, exact)
+__global__ void __launch_bounds__(128) k_dispatch_pack(const int* __restrict__ send_map, const int* __restrict__ idx,
+                                                       int ks, int nb, const uint8_t* __restrict__ xq,
+                                                       uint8_t* __restrict__ out, size_t rec) {
+    const int i = blockIdx.x, p = send_map[i], t = p / ks;
+    uint8_t* r = out + (size_t)i * rec;
+    if (threadIdx.x < 4) reinterpret_cast<int*>(r)[threadIdx.x] = threadIdx.x == 0 ? idx[p] : threadIdx.x == 1 ? p : 0;
+    const ActView a = act_view(const_cast<uint8_t*>(xq) + (size_t)t * act_bytes(nb), nb);
+    // a 34-byte block starts on a 2-byte boundary (records are 16-byte aligned): the scale
+    // and the codes go as 17 little-endian 16-bit words
+    uint16_t* blk = reinterpret_cast<uint16_t*>(r + REC_HDR);
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        uint16_t* o = blk + (size_t)b * 17;
+        o[0] = f32_to_f16_bits(a.d[b]);
+        const uint8_t* q = reinterpret_cast<const uint8_t*>(a.qs) + (size_t)b * 32;
+        for (int c = 0; c < 16; c++) o[1 + c] = (uint16_t)(q[2 * c] | (q[2 * c + 1] << 8));
+    }
+}
+
+// grid n_records, 128 threads: a received record into the activation form (codes, fp32 of
+// the fp16 scale, 8 * sum of codes) and its expert id
+__global__ void __launch_bounds__(128) k_dispatch_unpack(const uint8_t* __restrict__ in, size_t rec, int nb,
+                                                         uint8_t* __restrict__ xq, int* __restrict__ idx) {
+    const int i = blockIdx.x;
+    const uint8_t* r = in + (size_t)i * rec;
+    if (threadIdx.x == 0) idx[i] = reinterpret_cast<const int*>(r)[0];
+    ActView a = act_view(xq + (size_t)i * act_bytes(nb), nb);
+    const uint16_t* blk = reinterpret_cast<const uint16_t*>(r + REC_HDR);
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        const uint16_t* o = blk + (size_t)b * 17;
+        a.d[b] = f16_bits_to_f32(o[0]);
+        int sum = 0;
+        for (int c = 0; c < 16; c++) {
+            const uint16_t w = o[1 + c];
+            const int8_t q0 = (int8_t)(w & 0xff), q1 = (int8_t)(w >> 8);
+            a.qs[(size_t)b * 32 + 2 * c] = q0;
+            a.qs[(size_t)b * 32 + 2 * c + 1] = q1;
+            sum += q0 + q1;
+        }
+        a.s8[b] = 8 * sum;
+    }
+}
+
+// grid T, 256 threads: x[t][r] += sum over slots j in order of w[t][j] * y_back[pair_slot[t*ks+j]][r]
+__global__ void __launch_bounds__(256) k_dispatch_combine(float* __restrict__ X, int H, int ks,
+                                                          const float* __restrict__ wts,
+                                                          const int* __restrict__ pair_slot,
+                                                          const float* __restrict__ y) {
+    const int t = blockIdx.x;
+    for (int r = threadIdx.x; r < H; r += blockDim.x) {
+        float a = 0.0f;
+        for (int j = 0; j < ks; j++)
+            a = __fadd_rn(a, __fmul_rn(wts[(size_t)t * ks + j], __ldg(y + (size_t)pair_slot[(size_t)t * ks + j] * H + r)));
+        X[(size_t)t * H + r] = __fadd_rn(X[(size_t)t * H + r], a);
+    }
+}
+
+// The dispatch scratch: an error flag for the expert step's tensor-core kernels, the
+// routing buffers of T own tokens (S, xq, idx, wts, pair_slot, send_map: offsets that
+// depend on T only), then the receive side for n_recv records (activation rows,
+// expert ids, the expert step's scratch).
+struct DispatchLayout {
+    size_t S, xq, idx, wts, slot, map, route_end, rxq, ridx, xs, total;
+};
+DispatchLayout dispatch_layout(const tgx_ep* ep, int T, int n_recv) {
+    const Geom& g = ep->g;
+    const int E = ep->shape.n_experts, ks = ep->shape.top_k + ep->n_shared;
+    DispatchLayout L;
+    size_t o = 256;
+    auto take = [&](size_t n) {
+        const size_t r = o;
+        o += r256(n);
+        return r;
+    };
+    L.S = take((size_t)T * E * 8);
+    L.xq = take((size_t)T * tg::act_bytes(g.nbH));
+    L.idx = take((size_t)T * ks * 4);
+    L.wts = take((size_t)T * ks * 4);
+    L.slot = take((size_t)T * ks * 4);
+    L.map = take((size_t)T * ks * 4);
+    L.route_end = o;
+    L.rxq = take((size_t)n_recv * tg::act_bytes(g.nbH));
+    L.ridx = take((size_t)n_recv * 4);
+    L.xs = take(tg::experts_scratch_bytes(g, E, ep->n_shared, (size_t)(n_recv > 0 ? n_recv : 1)));
+    L.total = o;
+    return L;
+}
+
+// grow the dispatch scratch to L, keeping the first `keep` bytes (the flag and a
+// pending dispatch's routing buffers)
+int dispatch_reserve(tgx_ep* ep, const DispatchLayout& L, size_t keep, cudaStream_t s, const char* fn) {
+    if (L.total <= ep->dscratch_bytes) return TG_OK;
+    EP_CUDA(cudaStreamSynchronize(s));
+    void* fresh = nullptr;
+    EP_TRY(ep_alloc(&fresh, L.total, fn));
+    if (ep->dscratch && keep)
+        EP_CUDA(cudaMemcpy(fresh, ep->dscratch, keep < ep->dscratch_bytes ? keep : ep->dscratch_bytes,
+                           cudaMemcpyDeviceToDevice));
+    else
+        EP_CUDA(cudaMemset(fresh, 0, 256));   // the error flag
+    if (ep->dscratch) cudaFree(ep->dscratch);
+    ep->dscratch = fresh;
+    ep->dscratch_bytes = L.total;
+    return TG_OK;
+}
+
+}  // namespace
+
+extern "C" size_t tgx_ep_record_bytes(const tgx_ep* ep) { return ep ? rec_bytes(ep->g) : 0; }
+
+extern "C" int tgx_ep_dispatch(tgx_ep* ep, int layer, const float* x_dev, int T, void* send_dev, int* counts_dev,
+                               void* stream) {
+    EP_CHECK(ep && x_dev && send_dev && counts_dev, TG_EINVAL, "tgx_ep_dispatch: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_dispatch: layer out of range");
+    EP_CHECK(T >= 1 && T <= 65536 / ep->shape.top_k, TG_EINVAL, "tgx_ep_dispatch: T must be in [1, 65536/top_k]");
+    EP_CHECK(ep->size <= 64, TG_EINVAL, "tgx_ep_dispatch: at most 64 ranks");
+    Dev dg(ep->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    const tgx_shape& sh = ep->shape;
+    const int ks = sh.top_k + ep->n_shared;
+    const DispatchLayout L = dispatch_layout(ep, T, 0);
+    EP_TRY(dispatch_reserve(ep, L, 256, s, "tgx_ep_dispatch"));
+    uint8_t* base = (uint8_t*)ep->dscratch;
+    auto* S = (unsigned long long*)(base + L.S);
+    uint8_t* xq = base + L.xq;
+    int* idx = (int*)(base + L.idx);
+    float* wts = (float*)(base + L.wts);
+    int* slot = (int*)(base + L.slot);
+    int* map = (int*)(base + L.map);
+    const size_t nr = (size_t)sh.n_experts * sh.embed;
+    EP_CUDA(tg::launch_batched_route(ep->g, ep->routers + (size_t)layer * nr, ep->norms + (size_t)layer * sh.embed,
+                                     ep->eps, sh.n_experts, ep->n_shared, sh.top_k, x_dev, T, S, idx, wts, nullptr, xq,
+                                     s));
+    k_dispatch_plan<<<1, 1024, 0, s>>>(idx, T * ks, ks, sh.top_k, ep->e_n, ep->rank, ep->size, counts_dev, slot, map);
+    EP_CUDA(cudaGetLastError());
+    k_dispatch_pack<<<T * ks, 128, 0, s>>>(map, idx, ks, ep->g.nbH, xq, (uint8_t*)send_dev, rec_bytes(ep->g));
+    EP_CUDA(cudaGetLastError());
+    ep->d_T = T;
+    ep->d_wts = wts;
+    ep->d_slot = slot;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_dispatch_experts(tgx_ep* ep, int layer, const void* recv_dev, int n_recv, float* y_dev,
+                                       void* stream) {
+    EP_CHECK(ep && (n_recv == 0 || (recv_dev && y_dev)), TG_EINVAL, "tgx_ep_dispatch_experts: null argument");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_dispatch_experts: layer out of range");
+    EP_CHECK(ep->d_T > 0, TG_EINVAL, "tgx_ep_dispatch_experts: call tgx_ep_dispatch first");
+    EP_CHECK(n_recv >= 0 && n_recv <= 65536 * 64, TG_EINVAL, "tgx_ep_dispatch_experts: bad record count");
+    if (n_recv == 0) return TG_OK;
+    Dev dg(ep->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    int optin = 0;
+    EP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ep->device));
+    EP_CHECK(tg::batched_smem_bytes(ep->g) <= (size_t)optin, TG_EUNSUPPORTED,
+             "tgx_ep_dispatch_experts: shape needs more shared memory per block than the device has");
+    const DispatchLayout L = dispatch_layout(ep, ep->d_T, n_recv);
+    EP_TRY(dispatch_reserve(ep, L, L.route_end, s, "tgx_ep_dispatch_experts"));
+    uint8_t* base = (uint8_t*)ep->dscratch;
+    ep->d_wts = (float*)(base + L.wts);
+    ep->d_slot = (int*)(base + L.slot);
+    uint8_t* rxq = base + L.rxq;
+    int* ridx = (int*)(base + L.ridx);
+    k_dispatch_unpack<<<n_recv, 128, 0, s>>>((const uint8_t*)recv_dev, rec_bytes(ep->g), ep->g.nbH, rxq, ridx);
+    EP_CUDA(cudaGetLastError());
+    const tgx_shape& sh = ep->shape;
+    const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
+    const int E_tot = sh.n_experts + ep->n_shared;
+    // every received record is computed here: rank 0 of one with all experts "owned"
+    EP_CUDA(tg::launch_batched_experts(ep->weights + (size_t)layer * ep->layer_bytes, shared, sh.n_experts, ep->e_lo,
+                                       E_tot, 0, 1, ep->g, ep->n_shared, 1, 1, ridx, n_recv, rxq, base + L.xs,
+                                       L.total - L.xs, y_dev, nullptr, ep->kernels, ep->e_n + ep->n_shared, s,
+                                       (unsigned*)base));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_dispatch_combine(tgx_ep* ep, float* x_dev, int T, const float* y_back_dev, void* stream) {
+    EP_CHECK(ep && x_dev && y_back_dev, TG_EINVAL, "tgx_ep_dispatch_combine: null argument");
+    EP_CHECK(T >= 1 && T == ep->d_T, TG_EINVAL, "tgx_ep_dispatch_combine: T must match the last tgx_ep_dispatch");
+    Dev dg(ep->device);
+    k_dispatch_combine<<<T, 256, 0, (cudaStream_t)stream>>>(x_dev, ep->shape.embed, ep->shape.top_k + ep->n_shared,
+                                                            ep->d_wts, ep->d_slot, y_back_dev);
+    EP_CUDA(cudaGetLastError());
     return TG_OK;
 }

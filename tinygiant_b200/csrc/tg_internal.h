@@ -121,6 +121,23 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
                                        int* owned = nullptr);
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s);
+// The partial step's halves.  Route: T tokens' fixed-point router sums (S, [T][E]),
+// top-k + softmax (idx / wts [T][k + n_shared], the shared slot last: id E, weight 1)
+// and the Q8_0 activation rows xq [T].  Experts: y[(t, j)][H] for the pairs (token t,
+// slot j of ks) this device computes (ownership as in the partial step: rank of G, e_n
+// experts each; rank 0 of G = 1 with e_n = E + n_shared takes every pair), from the
+// tokens' activation rows xq; scratch of experts_scratch_bytes (error flag first);
+// pairs_per_expert_div: the experts the pairs spread over, for the kernel choice;
+// err_flag, when given, replaces the scratch's own error flag.
+size_t experts_scratch_bytes(const Geom& g, int E, int n_shared, size_t n_pairs);
+cudaError_t launch_batched_route(Geom g, const float* R, const float* normw, float eps, int E, int n_shared, int k,
+                                 const float* X, int T, unsigned long long* S, int* idx, float* wts, float* logits_out,
+                                 uint8_t* xq, cudaStream_t s);
+cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, int e_n, int rank,
+                                   int G, Geom g, int n_shared, int k, int ks, const int* idx, int n_tok,
+                                   const uint8_t* xq, void* scratch, size_t scratch_bytes, float* y, int* owned,
+                                   int kernels, int pairs_per_expert_div, cudaStream_t s,
+                                   unsigned* err_flag = nullptr);
 
 // The reference library's own formats (tg_kquant.cu).  fmt: KQ_Q4K (ggml Q4_K
 // blocks), KQ_F16, KQ_Q6K (split layout: 208-byte bodies of all blocks, then their

@@ -15,6 +15,9 @@ bit-identical to the single-GPU batched path (and, through it, to the CPU oracle
 The all-reduce moves T * top_k * embed floats per layer.  After enable_p2p() the
 exchange is direct instead: the down kernels store each (token, slot) sum into every
 rank's exchange buffer over NVLink and the combine waits on per-rank epoch flags.
+moe_layer_dispatch / decode_dispatch instead shard the tokens: each rank routes its own,
+sends each (token, slot) pair's Q8_0 row to its expert's holder and gets the pair's y
+back (NCCL all-to-alls), so bytes per rank fall as 1/G (tgx_ep_dispatch*).
 After enable_fused(), decode_step(x) runs all layers of one token in one persistent
 kernel per rank (the one-GPU fused step over the local experts), the per-slot down
 values crossing NVLink as tagged words inside the kernel.
@@ -251,6 +254,90 @@ class EPMoEModel:
             dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
             top = int(t.item())
         check(self.lib.tgx_ep_fused_reset(self._ep, top + 1), self.lib)
+
+    # ---------------------------------------------------------------- token dispatch
+    def record_bytes(self) -> int:
+        return int(self.lib.tgx_ep_record_bytes(self._ep))
+
+    def _cuda(self, name: str, n: int, dtype):
+        """A reused device buffer of at least n elements (grown by doubling)."""
+        import torch
+        b = self._y.get(name)
+        if b is None or b.numel() < n:
+            b = torch.empty(max(n, 2 * (b.numel() if b is not None else 0)), dtype=dtype,
+                            device=torch.device("cuda", self.device))
+            self._y[name] = b
+        return b[:n]
+
+    def dispatch(self, layer: int, X, stream=None):
+        """Route this rank's tokens X (cuda f32[T][embed]); returns (send, counts): the
+        records grouped by destination rank (uint8 [T * slots * record_bytes]) and the
+        records per rank (cuda int32 [size])."""
+        import torch
+        T = X.shape[0]
+        ks = self.top_k + self.n_shared
+        send = self._cuda("d_send", T * ks * self.record_bytes(), torch.uint8)
+        counts = self._cuda("d_counts", self.size, torch.int32)
+        check(self.lib.tgx_ep_dispatch(self._ep, layer, _dev_ptr(X), T, send.data_ptr(), counts.data_ptr(),
+                                       _stream_handle(stream)), self.lib)
+        return send, counts
+
+    def dispatch_experts(self, layer: int, recv, n_recv: int, stream=None):
+        """The expert FFNs of n_recv received records: cuda f32 [n_recv][embed]."""
+        import torch
+        y = self._cuda("d_yr", max(1, n_recv) * self.embed, torch.float32)[: n_recv * self.embed]
+        check(self.lib.tgx_ep_dispatch_experts(self._ep, layer, recv.data_ptr() if n_recv else None, n_recv,
+                                               y.data_ptr() if n_recv else None, _stream_handle(stream)), self.lib)
+        return y.view(n_recv, self.embed)
+
+    def dispatch_combine(self, X, y_back, stream=None):
+        check(self.lib.tgx_ep_dispatch_combine(self._ep, _dev_ptr(X), X.shape[0], y_back.data_ptr(),
+                                               _stream_handle(stream)), self.lib)
+
+    def moe_layer_dispatch(self, layer: int, X, stream=None, stats=None):
+        """MoE block `layer` for this rank's tokens X (cuda f32[T][embed]) in place, the
+        pairs dispatched to their experts' holders and back with NCCL all-to-alls over
+        self.group.  stats (dict), when given, accumulates the bytes this rank received."""
+        import torch
+        import torch.distributed as dist
+        rb = self.record_bytes()
+        if X.shape[0] > 0:
+            send, counts = self.dispatch(layer, X, stream)
+        else:   # no tokens here: still take part in every exchange
+            send = self._cuda("d_send", 1, torch.uint8)
+            counts = self._cuda("d_counts", self.size, torch.int32)
+            counts.zero_()
+        rcounts = self._cuda("d_rcounts", self.size, torch.int32)
+        if self.size > 1:
+            dist.all_to_all_single(rcounts, counts, group=self.group)
+        else:
+            rcounts.copy_(counts)
+        both = torch.cat([counts, rcounts]).cpu().tolist()
+        sc, rc = both[: self.size], both[self.size:]
+        n_send, n_recv = sum(sc), sum(rc)
+        recv = self._cuda("d_recv", max(1, n_recv) * rb, torch.uint8)[: n_recv * rb]
+        if self.size > 1:
+            dist.all_to_all_single(recv, send[: n_send * rb], [c * rb for c in rc], [c * rb for c in sc],
+                                   group=self.group)
+        else:
+            recv.copy_(send[: n_send * rb])
+        y = self.dispatch_experts(layer, recv, n_recv, stream)
+        y_back = self._cuda("d_yback", max(1, n_send) * self.embed, torch.float32)[: n_send * self.embed]
+        if self.size > 1:
+            dist.all_to_all_single(y_back, y.reshape(-1), [c * self.embed for c in sc],
+                                   [c * self.embed for c in rc], group=self.group)
+        else:
+            y_back.copy_(y.reshape(-1))
+        if X.shape[0] > 0:
+            self.dispatch_combine(X, y_back, stream)
+        if stats is not None:
+            stats["recv_bytes"] = stats.get("recv_bytes", 0) + n_recv * rb + n_send * self.embed * 4
+            stats["layers"] = stats.get("layers", 0) + 1
+
+    def decode_dispatch(self, X, stream=None, stats=None):
+        """All layers chained on this rank's tokens X in place (token dispatch)."""
+        for layer in range(self.n_layers):
+            self.moe_layer_dispatch(layer, X, stream, stats)
 
     def p2p_status(self, stream=None):
         check(self.lib.tgx_ep_p2p_status(self._ep, _stream_handle(stream)), self.lib)
