@@ -1161,6 +1161,8 @@ def run_ep(args):
     ep.set_kernels(KERNELS[args.batched_kernels])
     if args.p2p and not args.dispatch:
         ep.enable_p2p(max(args.token_list))
+    if args.p2p and args.dispatch:   # device-side dispatch: regions sized for a rank's largest share
+        ep.enable_dispatch_p2p(-(-max(args.token_list) // ws))
     for T in args.token_list:
         ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank, local, dist)
     ep.close()
@@ -1182,18 +1184,36 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
     stream = torch.cuda.current_stream()
     X.copy_(pool[0])
     stats = {}
-    if disp:
+    dev_disp = disp and args.p2p                          # token dispatch through the IPC regions
+    rb = ep.record_bytes()
+
+    def one(Xs):
+        if dev_disp:
+            ep.decode_dispatch_p2p(Xs)
+        elif disp:
+            ep.decode_dispatch(Xs)
+        else:
+            ep.decode(Xs)
+
+    if dev_disp:   # bytes received, layer by layer (untimed, synchronising)
+        for layer in range(NL):
+            ep.moe_layer_dispatch_p2p(layer, X)
+            n_recv, n_sent = ep.dispatch_p2p_counts()
+            stats["recv_bytes"] = stats.get("recv_bytes", 0) + n_recv * rb + n_sent * h * 4
+            stats["layers"] = stats.get("layers", 0) + 1
+        ep.dispatch_p2p_status()
+    elif disp:
         ep.decode_dispatch(X, stats=stats)                # grows the buffers; counts the bytes received
     else:
         ep.decode(X)                                      # allocates scratch and the exchange buffer
     torch.cuda.synchronize()
     graph, graphed = torch.cuda.CUDAGraph(), False
-    if disp:
+    if disp and not dev_disp:
         graph = None                                      # the all-to-all sizes come from the host each layer
     else:
         try:
             with torch.cuda.graph(graph):
-                ep.decode(X)
+                one(X)
             graphed = True
         except Exception:                                 # eager launches otherwise (same kernels)
             graph = None
@@ -1202,10 +1222,8 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
     def step():
         if graphed:
             graph.replay()
-        elif disp:
-            ep.decode_dispatch(X)
         else:
-            ep.decode(X)
+            one(X)
 
     for i in range(W):
         X.copy_(pool[i % 4])
@@ -1252,6 +1270,8 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
         ms, ems = float(t[0]), float(t[1])
     if getattr(ep, "p2p", False) and not disp:
         ep.p2p_status()                                   # raises if a peer's flag wait expired
+    if dev_disp:
+        ep.dispatch_p2p_status()
     ep.status()
     assert torch.isfinite(Yh).all()
     del graph                                             # holds NCCL calls: released before the group
@@ -1274,12 +1294,14 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
                                    f"{NL} of {full_layers} layers, experts sharded {e_all // ws} per GPU"
                                    f"{' + the shared expert' if n_sh else ''}, "
                                    + ("tokens sharded, pairs dispatched to their experts' holders and back "
-                                      "(NCCL all-to-alls)" if disp else
+                                      + ("(NVLink stores into the ranks' regions, device-side)" if dev_disp
+                                         else "(NCCL all-to-alls)") if disp else
                                       f"{'NVLink stores + flags' if args.p2p else 'NCCL all-reduce'} of y per layer"),
                        "hidden": h, "inter": inter, "experts": e_all, "shared_experts": n_sh, "top_k": K_TOP,
                        "layers": NL, "full_layers": full_layers, "tokens": T, "parallelism": f"ep{ws}",
                        "cuda_graph": graphed, "batched_kernels": args.batched_kernels,
-                       "exchange": "dispatch" if disp else ("p2p" if args.p2p else "nccl_all_reduce")},
+                       "exchange": ("dispatch_p2p" if dev_disp else "dispatch") if disp else
+                                   ("p2p" if args.p2p else "nccl_all_reduce")},
             "tok_s_full_depth": value * NL / full_layers,
             "exchange_bytes_per_layer": T * (K_TOP + n_sh) * h * 4,
             "recv_bytes_per_layer_per_rank": (recv_layer if disp else T * (K_TOP + n_sh) * h * 4),
@@ -1294,7 +1316,7 @@ def ep_measure(args, ep, T, NL, h, inter, e_all, n_sh, full_layers, eb, ws, rank
                          "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback"},
             "e2e": {"value": T * ke / (ems / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": T * h * 4,
                     "d2h_bytes_per_step": T * h * 4},
-            "gpu_launches": ((7 if disp else 6) + (1 if args.shape == "dsv3" else 0)) * NL * K,
+            "gpu_launches": ((12 if dev_disp else 9 if disp else 6) + (1 if args.shape == "dsv3" else 0)) * NL * K,
             "clocks": clocks.summary(),
         }))
 

@@ -425,6 +425,21 @@ int tgx_ep_fused_reset(tgx_ep *ep, unsigned epoch);
  * Bit-identical to the single-device batched path (tinygiant/engine.py:229-258 per
  * token).  tgx_ep_status reports an expired wait of the tensor-core expert kernels. */
 size_t tgx_ep_record_bytes(const tgx_ep *ep);
+/* The same dispatch device-side, with no host sync and capturable in a CUDA graph: every
+ * rank tgx_ep_dispatch_p2p_init(ep, T_max, handle) (its region: records in, y rows back,
+ * flags; CUDA IPC handle of tgx_ep_p2p_handle_bytes() bytes), the caller gathers all
+ * handles in rank order, tgx_ep_dispatch_p2p_connect; then per layer
+ * tgx_ep_moe_layer_dispatch_p2p(ep, layer, x, T, s) on every rank (1 <= T <= T_max, its
+ * own tokens): records are stored into their destinations' regions over NVLink, counts
+ * travel in the flags, y rows come back the same way, and the combine adds in slot order.
+ * Bounded waits (~1 s; tgx_ep_dispatch_p2p_status reports TG_ETIMEOUT); after one the
+ * ranks must set up again.  tgx_ep_dispatch_p2p_counts: records received and sent by the
+ * last call.  tgx_ep_p2p_disconnect closes these mappings too. */
+int tgx_ep_dispatch_p2p_init(tgx_ep *ep, int T_max, void *handle_out);
+int tgx_ep_dispatch_p2p_connect(tgx_ep *ep, const void *handles);
+int tgx_ep_moe_layer_dispatch_p2p(tgx_ep *ep, int layer, float *x_dev, int T, void *stream);
+int tgx_ep_dispatch_p2p_counts(tgx_ep *ep, int *received, int *sent);
+int tgx_ep_dispatch_p2p_status(tgx_ep *ep, void *stream);
 int tgx_ep_dispatch(tgx_ep *ep, int layer, const float *x_dev, int T, void *send_dev, int *counts_dev, void *stream);
 int tgx_ep_dispatch_experts(tgx_ep *ep, int layer, const void *recv_dev, int n_recv, float *y_dev, void *stream);
 int tgx_ep_dispatch_combine(tgx_ep *ep, float *x_dev, int T, const float *y_back_dev, void *stream);

@@ -10,6 +10,8 @@ experts.  EP_MODE:
   dispatch  every rank holds its own share of the T tokens; each (token, slot) pair
          travels to its expert's holder and back (NCCL all-to-alls, tgx_ep_dispatch*),
          against the single-GPU batched path
+  dispatch_p2p  the same through the ranks' IPC regions over NVLink, no host sync
+         (tgx_ep_dispatch_p2p_*)
 EP_SKIP=1 afterwards makes rank 1 skip one step: rank 0's bounded wait must run out and
 report TG_ETIMEOUT, nothing faults, and (fused) both ranks recover and decode bit-exact
 again.  Exit status 0 = bit-identical."""
@@ -46,6 +48,8 @@ def main() -> int:
             ep.enable_p2p(64)
         elif mode == "fused":
             ep.enable_fused()
+        elif mode == "dispatch_p2p":
+            ep.enable_dispatch_p2p(-(-T // world))
         full = None
         if rank == 0:
             full = MoEModel(H, I, E, K, L, device=local)
@@ -61,7 +65,7 @@ def main() -> int:
             # every rank holds the same state; rank 0's equals one GPU's
             xs = [torch.empty_like(X) for _ in range(world)]
             dist.all_gather(xs, X)
-            if mode == "dispatch":   # X: every rank's share, gathered back into the T tokens
+            if mode.startswith("dispatch"):   # X: every rank's share, gathered back into the T tokens
                 xs = [X]
             if rank == 0:
                 if mode == "fused":
@@ -81,10 +85,14 @@ def main() -> int:
             dist.barrier()      # the ranks' steps start together (a lagging rank would be waited on)
             if mode == "fused":
                 fused_tokens(X)
-            elif mode == "dispatch":
+            elif mode.startswith("dispatch"):
                 sizes = [len(c) for c in torch.tensor_split(torch.arange(T), world)]
                 mine = torch.tensor_split(X, world)[rank].contiguous()
-                ep.decode_dispatch(mine)
+                if mode == "dispatch":
+                    ep.decode_dispatch(mine)
+                else:
+                    ep.decode_dispatch_p2p(mine)
+                    ep.dispatch_p2p_status()
                 ep.status()
                 pad = torch.zeros(max(sizes), H, device="cuda")
                 pad[: sizes[rank]] = mine
@@ -97,7 +105,7 @@ def main() -> int:
                 if mode == "p2p":
                     ep.p2p_status()
             check_against_full(X, X0)
-        if mode in ("p2p", "fused") and os.environ.get("EP_SKIP") == "1":
+        if mode in ("p2p", "fused", "dispatch_p2p") and os.environ.get("EP_SKIP") == "1":
             # rank 1 skips a step: rank 0 waits for down values (p2p: an epoch flag) that
             # never come, gives up at the wait limit and reports it; nothing faults.  Rank 1
             # has no kernel in flight meanwhile.
@@ -110,6 +118,9 @@ def main() -> int:
                     if mode == "fused":
                         ep.decode_step(Xs[0])
                         ep.fused_status()
+                    elif mode == "dispatch_p2p":
+                        ep.moe_layer_dispatch_p2p(0, Xs[:1].contiguous())
+                        ep.dispatch_p2p_status()
                     else:
                         ep.moe_layer(0, Xs)
                         torch.cuda.synchronize()

@@ -263,6 +263,43 @@ def test_ep_dispatch_shared_expert_matches_oracle(oracle, G):
         ep.close()
 
 
+@pytest.mark.parametrize("T,kernels", [(1, 1), (9, 0), (300, 2)])
+def test_ep_dispatch_p2p_single_rank_matches_batched(T, kernels):
+    # the device-side dispatch with one rank (its own region and flags): chained layers
+    # (both buffer halves), eager and graph-replayed, against the single-GPU batched path
+    import torch
+    from tinygiant_b200.engine import MoEModel
+    from tinygiant_b200.ep import EPMoEModel
+    L = 3
+    full = MoEModel(H, I, E, K, L)
+    full.fill_synthetic(33)
+    ep = EPMoEModel(H, I, E, K, L, rank=0, size=1)
+    ep.fill_synthetic(33)
+    ep.set_kernels(kernels)
+    ep.enable_dispatch_p2p(T)
+    X = torch.randn(T, H, generator=torch.Generator(device="cuda").manual_seed(T + 1), device="cuda")
+    want = X.clone()
+    full.decode_batched(want)
+    got = X.clone()
+    ep.decode_dispatch_p2p(got)
+    ep.dispatch_p2p_status()
+    ep.status()
+    assert torch.equal(got.view(torch.int32), want.view(torch.int32))
+    assert ep.dispatch_p2p_counts() == (T * K, T * K)
+    graph = torch.cuda.CUDAGraph()
+    Xg = X.clone()
+    with torch.cuda.graph(graph):
+        ep.decode_dispatch_p2p(Xg)
+    for _ in range(2):
+        Xg.copy_(X)
+        graph.replay()
+        ep.dispatch_p2p_status()
+        assert torch.equal(Xg.view(torch.int32), want.view(torch.int32))
+    del graph
+    ep.close()
+    full.close()
+
+
 def test_ep_fused_single_rank_matches_decode_step():
     # the one-kernel EP step with one rank (every expert local, its own y buffer): odd and
     # even step counts (both buffer halves), a router changed after set-up, a graph replay,
@@ -313,7 +350,8 @@ def test_ep_fused_single_rank_matches_decode_step():
 @pytest.mark.parametrize("mode,layers,repeat,skip", [("nccl", 3, 1, "0"), ("p2p", 3, 1, "0"), ("p2p", 3, 4, "0"),
                                                      ("p2p", 1, 5, "0"), ("p2p", 3, 2, "1"),
                                                      ("fused", 3, 3, "0"), ("fused", 2, 2, "1"),
-                                                     ("fused", 48, 1, "0"), ("dispatch", 3, 2, "0")])
+                                                     ("fused", 48, 1, "0"), ("dispatch", 3, 2, "0"),
+                                                     ("dispatch_p2p", 3, 3, "0"), ("dispatch_p2p", 2, 1, "1")])
 def test_ep_multi_gpu_matches_single_gpu(mode, layers, repeat, skip):
     # p2p: the exchange by direct NVLink stores and flags instead of the all-reduce; fused:
     # one kernel per rank and token; odd layer counts with several decodes back to back
@@ -325,7 +363,8 @@ def test_ep_multi_gpu_matches_single_gpu(mode, layers, repeat, skip):
     # skip = 1: afterwards rank 1 skips one step and rank 0 must report TG_ETIMEOUT
     env = dict(os.environ, NCCL_NVLS_ENABLE="0", EP_MODE=mode, EP_LAYERS=str(layers), EP_REPEAT=str(repeat),
                EP_SKIP=skip)
-    port = 29531 + ("nccl", "p2p", "fused", "dispatch").index(mode) + 4 * layers + 200 * repeat + 1000 * int(skip)
+    port = 29531 + ("nccl", "p2p", "fused", "dispatch", "dispatch_p2p").index(mode) + 5 * layers + 200 * repeat + \
+        1000 * int(skip)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={port}",
            str(ROOT / "tests" / "ep_worker.py")]

@@ -130,6 +130,11 @@ PROTOTYPES = {
     "tgx_ep_dispatch": (CI, [VP, CI, VP, CI, VP, VP, VP]),
     "tgx_ep_dispatch_experts": (CI, [VP, CI, VP, CI, VP, VP]),
     "tgx_ep_dispatch_combine": (CI, [VP, VP, CI, VP, VP]),
+    "tgx_ep_dispatch_p2p_init": (CI, [VP, CI, VP]),
+    "tgx_ep_dispatch_p2p_connect": (CI, [VP, VP]),
+    "tgx_ep_moe_layer_dispatch_p2p": (CI, [VP, CI, VP, CI, VP]),
+    "tgx_ep_dispatch_p2p_counts": (CI, [VP, ctypes.POINTER(CI), ctypes.POINTER(CI)]),
+    "tgx_ep_dispatch_p2p_status": (CI, [VP, VP]),
     "tgx_set_batched_kernels": (CI, [VP, CI]),
     "tgx_kq_scratch_bytes": (SZ, [CI, CI, CI]),
     "tgx_kq_experts_forward": (CI, [VP, VP, VP, CI, CI, VP, VP, VP, CI, CI, CI, VP, SZ, CI, VP]),

@@ -183,8 +183,10 @@ __device__ __forceinline__ bool pair_owned(const int* __restrict__ idx, int p, i
 __global__ void __launch_bounds__(256) k_group_pairs(const int* __restrict__ idx, int n_pairs, int ks, int k,
                                                      int E_tot, int e_n, int rank, int G, int* __restrict__ off,
                                                      int* __restrict__ list, int* __restrict__ active,
-                                                     int* __restrict__ owned, int* __restrict__ tile_pre, int tile) {
+                                                     int* __restrict__ owned, int* __restrict__ tile_pre, int tile,
+                                                     const int* __restrict__ n_dev = nullptr) {
     __shared__ int cnt[1025];
+    if (n_dev) n_pairs = *n_dev;   // the pair count on the device (n_pairs was an upper bound)
     __shared__ int pos[1025];
     for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
     __syncthreads();
@@ -325,11 +327,14 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
 
 // one warp per (pair, block) of h: the Q8_0 activation form of hf[p] into hq[p]
 // (the single-token quantiser, block by block, so the same bytes as the fused units);
-// with uf, h = silu(hf) * uf first (hf, uf: the gate and up sums).
+// with uf, h = silu(hf) * uf first (hf, uf: the gate and up sums).  n_dev, when given,
+// holds the pair count (the grid covers n_pairs, an upper bound).
 __global__ void __launch_bounds__(256) k_quant_h(const float* __restrict__ hf, const float* __restrict__ uf,
-                                                 int n_pairs, Geom g, uint8_t* __restrict__ hq) {
+                                                 int n_pairs, Geom g, uint8_t* __restrict__ hq,
+                                                 const int* __restrict__ n_dev = nullptr) {
     const int lane = threadIdx.x & 31;
     const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (n_dev) n_pairs = *n_dev;
     if (wid >= (long long)n_pairs * g.nbI) return;
     const int p = (int)(wid / g.nbI), b = (int)(wid - (long long)p * g.nbI);
     const size_t i = (size_t)p * g.I + (size_t)b * 32 + lane;
@@ -456,7 +461,8 @@ size_t batched_scratch_bytes(const Geom& g, int E, int k, int T) {
 cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, int e_n, int rank,
                                    int G, Geom g, int n_shared, int k, int ks, const int* idx, int n_tok,
                                    const uint8_t* xq, void* scratch, size_t scratch_bytes, float* y, int* owned,
-                                   int kernels, int pairs_per_expert_div, cudaStream_t s, unsigned* err_flag) {
+                                   int kernels, int pairs_per_expert_div, cudaStream_t s, unsigned* err_flag,
+                                   const int* n_pairs_dev) {
     const size_t n_pairs = (size_t)n_tok * ks;
     const int E_tot = E + n_shared;
     if (n_tok <= 0) return cudaSuccess;
@@ -483,7 +489,7 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return e;
     if (batched_smem_bytes(g) > (size_t)optin) return cudaErrorInvalidValue;
     k_group_pairs<<<1, 256, 0, s>>>(idx, (int)n_pairs, ks, k, E_tot, e_n, rank, G, off, list, active, owned,
-                                    tile_pre, q4_mma_tile_tokens());
+                                    tile_pre, q4_mma_tile_tokens(), n_pairs_dev);
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
     const bool mma = q4_mma_supported(g) &&
@@ -494,7 +500,7 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
                                s)) != cudaSuccess)
             return e;
         const long long warps = (long long)n_pairs * g.nbI;
-        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq);
+        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq, n_pairs_dev);
         return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, tile_pre, n_act, ks, hq, y, nullptr, err,
                              s);
     }
@@ -517,7 +523,7 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
     if (e != cudaSuccess) return e;
     if (R_gu == 16) {
         const long long warps = (long long)n_pairs * g.nbI;
-        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, nullptr, (int)n_pairs, g, hq);
+        k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, nullptr, (int)n_pairs, g, hq, n_pairs_dev);
     }
     const size_t sm_d = (size_t)DOWN_ROWS * g.row_d;
     auto down = [&](auto kern) -> cudaError_t {

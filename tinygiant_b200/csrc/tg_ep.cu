@@ -84,6 +84,19 @@ struct tgx_ep {
     int d_T = 0;                        // tokens of the last tgx_ep_dispatch
     float* d_wts = nullptr;             // [T][ks] their routing weights
     int* d_slot = nullptr;              // [T][ks] each pair's record index in the send order
+    // device-side token dispatch (tgx_ep_dispatch_p2p_*): one IPC region per rank (records
+    // in, y rows back, flags), every buffer sized at set-up for dp_T tokens per call
+    int dp_T = 0;
+    size_t dp_cap = 0;                  // records per (buffer half, peer)
+    uint8_t* dp_region = nullptr;
+    size_t dp_region_bytes = 0;
+    void* dp_peers[64] = {};
+    uint8_t** dp_bases = nullptr;       // [G] every rank's region (device pointers)
+    unsigned* dp_ctl = nullptr;         // [0] calls, [1..3] CTA counters, [4] error
+    int* dp_meta = nullptr;             // [0..64] send prefix, [65..130] receive prefix, [131] received
+    void* dp_work = nullptr;            // routing, receive side and expert scratch
+    size_t dp_work_bytes = 0;
+    bool dp_ready = false;
 };
 
 namespace {
@@ -124,7 +137,10 @@ void ep_free(tgx_ep* c) {
     for (int q = 0; q < 64; q++) {
         if (c->peers[q]) cudaIpcCloseMemHandle(c->peers[q]);
         if (c->fpeers[q]) cudaIpcCloseMemHandle(c->fpeers[q]);
+        if (c->dp_peers[q]) cudaIpcCloseMemHandle(c->dp_peers[q]);
     }
+    for (void* p : {(void*)c->dp_region, (void*)c->dp_bases, (void*)c->dp_ctl, (void*)c->dp_meta, c->dp_work})
+        if (p) cudaFree(p);
     for (void* p : {(void*)c->region, (void*)c->ystage, (void*)c->dst_dev, (void*)c->flag_dev, (void*)c->epoch, (void*)c->p2p_err,
                     (void*)c->p2p_count, (void*)c->owned})
         if (p) cudaFree(p);
@@ -562,9 +578,14 @@ extern "C" int tgx_ep_p2p_disconnect(tgx_ep* ep) {
             EP_CUDA(cudaIpcCloseMemHandle(ep->fpeers[q]));
             ep->fpeers[q] = nullptr;
         }
+        if (ep->dp_peers[q]) {
+            EP_CUDA(cudaIpcCloseMemHandle(ep->dp_peers[q]));
+            ep->dp_peers[q] = nullptr;
+        }
     }
     ep->p2p_ready = false;
     ep->fused_ready = false;
+    ep->dp_ready = false;
     return TG_OK;
 }
 
@@ -1103,5 +1124,429 @@ extern "C" int tgx_ep_dispatch_combine(tgx_ep* ep, float* x_dev, int T, const fl
     k_dispatch_combine<<<T, 256, 0, (cudaStream_t)stream>>>(x_dev, ep->shape.embed, ep->shape.top_k + ep->n_shared,
                                                             ep->d_wts, ep->d_slot, y_back_dev);
     EP_CUDA(cudaGetLastError());
+    return TG_OK;
+}
+
+// ------------------------------------------------------------ token dispatch over NVLink
+
+// The same exchange as tgx_ep_dispatch*, device-side: no host sync, capturable in a
+// CUDA graph.  Rank r's region: records in [2][G][cap][rec] (half, source, position),
+// y rows back [2][G][cap][H] (half, destination, position), record flags [2][G] and
+// y flags [2][G] (64-bit: (call + 1) << 32 | count).  Per call (one layer), with
+// e = calls so far and half e & 1:
+//   route, plan             this rank's tokens, records grouped by destination
+//   k_dp_pack_push          record i of destination q's group at position pos into q's
+//                           region [half][r][pos] (NVLink for peers); fence, and the last
+//                           CTA stores every destination's flag with its count
+//   k_dp_wait               wait (bounded) for all G record flags; counts -> receive prefix
+//   k_dp_unpack             records -> activation rows, expert ids, (source, position)
+//   experts                 the batched expert kernels, the pair count read on the device
+//   k_dp_return             y row of received record (q, pos) into q's region [half][r][pos];
+//                           fence, the last CTA stores every source's y flag
+//   k_dp_combine            wait (bounded) for all G y flags, x[t] += sum_j w_j * y_j in slot
+//                           order; the last CTA advances the call count
+// A rank reaches call e + 2 (the same half) only after every rank's y flags of call e + 1,
+// which each rank stores after finishing call e: a half is never rewritten while read.
+
+namespace {
+
+struct DpGeom {
+    size_t rec, cap, off_yb, off_rflag, off_yflag;
+    int G, H;
+};
+DpGeom dp_geom(const tgx_ep* ep) {
+    DpGeom d;
+    d.G = ep->size;
+    d.H = ep->shape.embed;
+    d.rec = rec_bytes(ep->g);
+    d.cap = ep->dp_cap;
+    size_t o = r256(2 * (size_t)d.G * d.cap * d.rec);
+    d.off_yb = o;
+    o += r256(2 * (size_t)d.G * d.cap * d.H * 4);
+    d.off_rflag = o;
+    o += r256(2 * (size_t)d.G * 8);
+    d.off_yflag = o;
+    return d;
+}
+size_t dp_region_bytes(const DpGeom& d) { return d.off_yflag + r256(2 * (size_t)d.G * 8); }
+
+__device__ __forceinline__ uint8_t* dp_rec(uint8_t* base, const DpGeom& d, unsigned half, int src, size_t pos) {
+    return base + (((size_t)half * d.G + src) * d.cap + pos) * d.rec;
+}
+__device__ __forceinline__ float* dp_yb(uint8_t* base, const DpGeom& d, unsigned half, int dst, size_t pos) {
+    return reinterpret_cast<float*>(base + d.off_yb) + (((size_t)half * d.G + dst) * d.cap + pos) * d.H;
+}
+__device__ __forceinline__ unsigned long long* dp_flag(uint8_t* base, size_t off, const DpGeom& d, unsigned half,
+                                                       int q) {
+    return reinterpret_cast<unsigned long long*>(base + off) + (size_t)half * d.G + q;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// the group a sorted index i falls in: pre[q] <= i < pre[q + 1]
+__device__ __forceinline__ int dp_group(const int* pre, int G, int i) {
+    int q = 0;
+    while (q + 1 < G && pre[q + 1] <= i) q++;
+    return q;
+}
+
+// one thread: the send order's group starts, pre[q] = records for ranks < q (pre[G] = all)
+__global__ void k_dp_prefix(const int* __restrict__ counts, int G, int* __restrict__ pre) {
+    if (threadIdx.x == 0) {
+        int a = 0;
+        for (int q = 0; q < G; q++) {
+            pre[q] = a;
+            a += counts[q];
+        }
+        pre[G] = a;
+    }
+}
+
+// grid n_records, 128 threads (the plan's send order): pack record i into its
+// destination's region, then the last CTA publishes every destination's flag
+__global__ void __launch_bounds__(128) k_dp_pack_push(const int* __restrict__ send_map, const int* __restrict__ idx,
+                                                      int ks, int nb, const uint8_t* __restrict__ xq,
+                                                      const int* __restrict__ counts, const int* __restrict__ pre,
+                                                      uint8_t* const* __restrict__ bases, int rank, DpGeom d,
+                                                      unsigned* ctl) {
+    __shared__ int last;
+    const unsigned e = *(volatile unsigned*)ctl, half = e & 1u;
+    const int i = blockIdx.x, p = send_map[i], t = p / ks;
+    const int q = dp_group(pre, d.G, i);
+    uint8_t* r = dp_rec(bases[q], d, half, rank, (size_t)(i - pre[q]));
+    if (threadIdx.x < 4) reinterpret_cast<int*>(r)[threadIdx.x] = threadIdx.x == 0 ? idx[p] : threadIdx.x == 1 ? p : 0;
+    const ActView a = act_view(const_cast<uint8_t*>(xq) + (size_t)t * act_bytes(nb), nb);
+    uint16_t* blk = reinterpret_cast<uint16_t*>(r + REC_HDR);
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        uint16_t* o = blk + (size_t)b * 17;
+        o[0] = f32_to_f16_bits(a.d[b]);
+        const uint8_t* c = reinterpret_cast<const uint8_t*>(a.qs) + (size_t)b * 32;
+        for (int u = 0; u < 16; u++) o[1 + u] = (uint16_t)(c[2 * u] | (c[2 * u + 1] << 8));
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ctl + 1, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+        __threadfence_system();
+        if ((int)threadIdx.x < d.G)
+            st_release_sys_u64(dp_flag(bases[threadIdx.x], d.off_rflag, d, half, rank),
+                               ((unsigned long long)(e + 1u) << 32) | (unsigned)counts[threadIdx.x]);
+        if (threadIdx.x == 0) ctl[1] = 0u;
+    }
+}
+
+// one CTA of 64 threads: wait (bounded) for every source's record flag of this call;
+// receive prefix and count into meta[65 ..]
+__global__ void __launch_bounds__(64) k_dp_wait(uint8_t* own, DpGeom d, unsigned* ctl, int* meta, long long limit) {
+    __shared__ int cnt[64];
+    __shared__ int bad;
+    const unsigned e = *(volatile unsigned*)ctl, half = e & 1u;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    const int q = threadIdx.x;
+    if (q < d.G) {
+        const unsigned long long* f = dp_flag(own, d.off_rflag, d, half, q);
+        const long long t0 = clock64();
+        unsigned long long v = ld_acquire_sys_u64(f);
+        while ((unsigned)(v >> 32) != e + 1u) {
+            if (clock64() - t0 > limit) {
+                atomicExch(&bad, 1);
+                break;
+            }
+            v = ld_acquire_sys_u64(f);
+        }
+        cnt[q] = (unsigned)(v >> 32) == e + 1u ? (int)(unsigned)v : 0;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int a = 0;
+        for (int s = 0; s < d.G; s++) {
+            meta[65 + s] = a;
+            a += cnt[s];
+        }
+        meta[65 + d.G] = a;
+        meta[131] = bad ? 0 : a;
+        if (bad) atomicExch(ctl + 4, 1u);
+    }
+}
+
+// grid-stride over the received records: activation rows, expert ids, (source, position)
+__global__ void __launch_bounds__(128) k_dp_unpack(uint8_t* own, DpGeom d, const unsigned* ctl,
+                                                   const int* __restrict__ meta, int nb, uint8_t* __restrict__ xq,
+                                                   int* __restrict__ idx, int* __restrict__ rsrc,
+                                                   int* __restrict__ rpos) {
+    const unsigned half = *(volatile const unsigned*)ctl & 1u;
+    const int n = meta[131];
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        const int q = dp_group(meta + 65, d.G, i), pos = i - meta[65 + q];
+        const uint8_t* r = dp_rec(own, d, half, q, (size_t)pos);
+        if (threadIdx.x == 0) {
+            idx[i] = __ldcg(reinterpret_cast<const int*>(r));
+            rsrc[i] = q;
+            rpos[i] = pos;
+        }
+        ActView a = act_view(xq + (size_t)i * act_bytes(nb), nb);
+        const unsigned short* blk = reinterpret_cast<const unsigned short*>(r + REC_HDR);
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+            const unsigned short* o = blk + (size_t)b * 17;
+            a.d[b] = f16_bits_to_f32(__ldcg(o));
+            int sum = 0;
+            for (int c = 0; c < 16; c++) {
+                const unsigned short w = __ldcg(o + 1 + c);
+                const int8_t q0 = (int8_t)(w & 0xff), q1 = (int8_t)(w >> 8);
+                a.qs[(size_t)b * 32 + 2 * c] = q0;
+                a.qs[(size_t)b * 32 + 2 * c + 1] = q1;
+                sum += q0 + q1;
+            }
+            a.s8[b] = 8 * sum;
+        }
+    }
+}
+
+// grid-stride over the received records: y row i back into its source's region at the
+// record's position; then the last CTA publishes every source's y flag
+__global__ void __launch_bounds__(256) k_dp_return(const float* __restrict__ y, const int* __restrict__ meta,
+                                                   const int* __restrict__ rsrc, const int* __restrict__ rpos,
+                                                   uint8_t* const* __restrict__ bases, int rank, DpGeom d,
+                                                   unsigned* ctl) {
+    __shared__ int last;
+    const unsigned e = *(volatile unsigned*)ctl, half = e & 1u;
+    const int n = meta[131];
+    for (int i = blockIdx.x; i < n; i += gridDim.x) {
+        float4* dst = reinterpret_cast<float4*>(dp_yb(bases[rsrc[i]], d, half, rank, (size_t)rpos[i]));
+        const float4* src = reinterpret_cast<const float4*>(y + (size_t)i * d.H);
+        for (int c = threadIdx.x; c < d.H / 4; c += blockDim.x) dst[c] = __ldcg(src + c);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(ctl + 2, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) {
+        __threadfence_system();
+        if ((int)threadIdx.x < d.G)
+            st_release_sys_u64(dp_flag(bases[threadIdx.x], d.off_yflag, d, half, rank),
+                               (unsigned long long)(e + 1u) << 32);
+        if (threadIdx.x == 0) ctl[2] = 0u;
+    }
+}
+
+// grid T, 256 threads: wait (bounded) for every destination's y flag of this call, then
+// x[t] += sum over slots j in order of w[t][j] * y[(t, j)] (y from this rank's region at
+// the pair's destination and position); the last CTA advances the call count
+__global__ void __launch_bounds__(256) k_dp_combine(float* __restrict__ X, int ks, const float* __restrict__ wts,
+                                                    const int* __restrict__ pair_slot, const int* __restrict__ pre,
+                                                    uint8_t* own, DpGeom d, unsigned* ctl, long long limit) {
+    __shared__ int ok, last;
+    __shared__ const float* yp[32];
+    const unsigned e = *(volatile unsigned*)ctl, half = e & 1u;
+    const int t = blockIdx.x;
+    if (threadIdx.x == 0) {
+        int good = 1;
+        const long long t0 = clock64();
+        for (int q = 0; q < d.G && good; q++) {
+            const unsigned long long* f = dp_flag(own, d.off_yflag, d, half, q);
+            while ((unsigned)(ld_acquire_sys_u64(f) >> 32) != e + 1u)
+                if (clock64() - t0 > limit) {
+                    good = 0;
+                    break;
+                }
+        }
+        if (!good) atomicExch(ctl + 4, 1u);
+        ok = good;
+    }
+    if ((int)threadIdx.x < ks) {
+        const int s = pair_slot[(size_t)t * ks + threadIdx.x];
+        const int q = dp_group(pre, d.G, s);
+        yp[threadIdx.x] = dp_yb(own, d, half, q, (size_t)(s - pre[q]));
+    }
+    __syncthreads();
+    if (ok) {
+        for (int r = threadIdx.x; r < d.H; r += blockDim.x) {
+            float a = 0.0f;
+            for (int j = 0; j < ks; j++) a = __fadd_rn(a, __fmul_rn(wts[(size_t)t * ks + j], __ldcg(yp[j] + r)));
+            X[(size_t)t * d.H + r] = __fadd_rn(X[(size_t)t * d.H + r], a);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        last = atomicAdd(ctl + 3, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        ctl[3] = 0u;
+        __threadfence();
+        *(volatile unsigned*)ctl = e + 1u;
+    }
+}
+
+// the work area for T tokens per call and N = G * cap received records at most
+struct DpWork {
+    size_t S, xq, idx, wts, slot, map, counts, rxq, ridx, rsrc, rpos, y, xs, total;
+};
+DpWork dp_work(const tgx_ep* ep) {
+    const Geom& g = ep->g;
+    const int E = ep->shape.n_experts, ks = ep->shape.top_k + ep->n_shared, T = ep->dp_T;
+    const size_t N = (size_t)ep->size * ep->dp_cap;
+    DpWork w;
+    size_t o = 256;   // the expert step's error flag
+    auto take = [&](size_t n) {
+        const size_t r = o;
+        o += r256(n);
+        return r;
+    };
+    w.S = take((size_t)T * E * 8);
+    w.xq = take((size_t)T * act_bytes(g.nbH));
+    w.idx = take((size_t)T * ks * 4);
+    w.wts = take((size_t)T * ks * 4);
+    w.slot = take((size_t)T * ks * 4);
+    w.map = take((size_t)T * ks * 4);
+    w.counts = take(64 * 4);
+    w.rxq = take(N * act_bytes(g.nbH));
+    w.ridx = take(N * 4);
+    w.rsrc = take(N * 4);
+    w.rpos = take(N * 4);
+    w.y = take(N * (size_t)g.H * 4);
+    w.xs = take(tg::experts_scratch_bytes(g, E, ep->n_shared, N));
+    w.total = o;
+    return w;
+}
+
+}  // namespace
+
+extern "C" int tgx_ep_dispatch_p2p_init(tgx_ep* ep, int T_max, void* handle_out) {
+    EP_CHECK(ep && handle_out, TG_EINVAL, "tgx_ep_dispatch_p2p_init: null argument");
+    EP_CHECK(!ep->dp_region, TG_EINVAL, "tgx_ep_dispatch_p2p_init: already initialised");
+    EP_CHECK(T_max >= 1 && T_max <= 65536 / ep->shape.top_k, TG_EINVAL, "tgx_ep_dispatch_p2p_init: T_max out of range");
+    EP_CHECK(ep->size <= 32, TG_EINVAL, "tgx_ep_dispatch_p2p_init: at most 32 ranks");
+    EP_CHECK(ep->shape.top_k + ep->n_shared <= 32, TG_EINVAL, "tgx_ep_dispatch_p2p_init: at most 32 slots");
+    Dev dg(ep->device);
+    ep->dp_T = T_max;
+    ep->dp_cap = (size_t)T_max * (ep->shape.top_k + ep->n_shared);
+    const DpGeom d = dp_geom(ep);
+    ep->dp_region_bytes = dp_region_bytes(d);
+    const DpWork w = dp_work(ep);
+    ep->dp_work_bytes = w.total;
+    EP_TRY(ep_alloc((void**)&ep->dp_region, ep->dp_region_bytes, "tgx_ep_dispatch_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->dp_bases, sizeof(void*) * ep->size, "tgx_ep_dispatch_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->dp_ctl, 256, "tgx_ep_dispatch_p2p_init"));
+    EP_TRY(ep_alloc((void**)&ep->dp_meta, 256 * 4, "tgx_ep_dispatch_p2p_init"));
+    EP_TRY(ep_alloc(&ep->dp_work, ep->dp_work_bytes, "tgx_ep_dispatch_p2p_init"));
+    // flags start at call 0 (no flag matches call 0 + 1); the records and y rows need no clearing
+    EP_CUDA(cudaMemset(ep->dp_region + d.off_rflag, 0, ep->dp_region_bytes - d.off_rflag));
+    EP_CUDA(cudaMemset(ep->dp_ctl, 0, 256));
+    EP_CUDA(cudaMemset(ep->dp_meta, 0, 256 * 4));
+    EP_CUDA(cudaMemset(ep->dp_work, 0, 256));
+    cudaIpcMemHandle_t h;
+    EP_CUDA(cudaIpcGetMemHandle(&h, ep->dp_region));
+    memcpy(handle_out, &h, sizeof(h));
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_dispatch_p2p_connect(tgx_ep* ep, const void* handles) {
+    EP_CHECK(ep && handles, TG_EINVAL, "tgx_ep_dispatch_p2p_connect: null argument");
+    EP_CHECK(ep->dp_region && !ep->dp_ready, TG_EINVAL,
+             "tgx_ep_dispatch_p2p_connect: call tgx_ep_dispatch_p2p_init first, once");
+    Dev dg(ep->device);
+    std::vector<uint8_t*> base(ep->size);
+    for (int q = 0; q < ep->size; q++) {
+        if (q == ep->rank) {
+            base[q] = ep->dp_region;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t*)handles + (size_t)q * sizeof(h), sizeof(h));
+        EP_CUDA(cudaIpcOpenMemHandle(&ep->dp_peers[q], h, cudaIpcMemLazyEnablePeerAccess));
+        base[q] = (uint8_t*)ep->dp_peers[q];
+    }
+    EP_CUDA(cudaMemcpy(ep->dp_bases, base.data(), sizeof(void*) * ep->size, cudaMemcpyHostToDevice));
+    ep->dp_ready = true;
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_moe_layer_dispatch_p2p(tgx_ep* ep, int layer, float* x_dev, int T, void* stream) {
+    EP_CHECK(ep && x_dev, TG_EINVAL, "tgx_ep_moe_layer_dispatch_p2p: null argument");
+    EP_CHECK(ep->dp_ready, TG_EINVAL, "tgx_ep_moe_layer_dispatch_p2p: call tgx_ep_dispatch_p2p_init / _connect first");
+    EP_CHECK(layer >= 0 && layer < ep->shape.n_layers, TG_EINVAL, "tgx_ep_moe_layer_dispatch_p2p: layer out of range");
+    EP_CHECK(T >= 1 && T <= ep->dp_T, TG_EINVAL, "tgx_ep_moe_layer_dispatch_p2p: T must be in [1, the T_max of init]");
+    Dev dg(ep->device);
+    cudaStream_t s = (cudaStream_t)stream;
+    int optin = 0;
+    EP_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ep->device));
+    EP_CHECK(tg::batched_smem_bytes(ep->g) <= (size_t)optin, TG_EUNSUPPORTED,
+             "tgx_ep_moe_layer_dispatch_p2p: shape needs more shared memory per block than the device has");
+    const tgx_shape& sh = ep->shape;
+    const int ks = sh.top_k + ep->n_shared, G = ep->size;
+    const DpGeom d = dp_geom(ep);
+    const DpWork w = dp_work(ep);
+    uint8_t* b = (uint8_t*)ep->dp_work;
+    const size_t N = (size_t)G * ep->dp_cap;
+    int* counts = (int*)(b + w.counts);
+    int* pre = ep->dp_meta;   // send prefix [0 .. G]
+    const size_t nr = (size_t)sh.n_experts * sh.embed;
+    EP_CUDA(tg::launch_batched_route(ep->g, ep->routers + (size_t)layer * nr, ep->norms + (size_t)layer * sh.embed,
+                                     ep->eps, sh.n_experts, ep->n_shared, sh.top_k, x_dev, T,
+                                     (unsigned long long*)(b + w.S), (int*)(b + w.idx), (float*)(b + w.wts), nullptr,
+                                     b + w.xq, s));
+    k_dispatch_plan<<<1, 1024, 0, s>>>((int*)(b + w.idx), T * ks, ks, sh.top_k, ep->e_n, ep->rank, G, counts,
+                                       (int*)(b + w.slot), (int*)(b + w.map));
+    EP_CUDA(cudaGetLastError());
+    k_dp_prefix<<<1, 32, 0, s>>>(counts, G, pre);
+    EP_CUDA(cudaGetLastError());
+    k_dp_pack_push<<<T * ks, 128, 0, s>>>((int*)(b + w.map), (int*)(b + w.idx), ks, ep->g.nbH, b + w.xq, counts, pre,
+                                          ep->dp_bases, ep->rank, d, ep->dp_ctl);
+    EP_CUDA(cudaGetLastError());
+    k_dp_wait<<<1, 64, 0, s>>>(ep->dp_region, d, ep->dp_ctl, ep->dp_meta, EP_WAIT_CYCLES);
+    EP_CUDA(cudaGetLastError());
+    const unsigned grid_n = (unsigned)(N < 1184 ? N : 1184);
+    k_dp_unpack<<<grid_n, 128, 0, s>>>(ep->dp_region, d, ep->dp_ctl, ep->dp_meta, ep->g.nbH, b + w.rxq,
+                                       (int*)(b + w.ridx), (int*)(b + w.rsrc), (int*)(b + w.rpos));
+    EP_CUDA(cudaGetLastError());
+    const uint8_t* shared = ep->n_shared ? ep->shared + (size_t)layer * ep->g.expert_bytes : nullptr;
+    // the expected received pairs per local expert picks the kernels (both give the same bits)
+    EP_CUDA(tg::launch_batched_experts(ep->weights + (size_t)layer * ep->layer_bytes, shared, sh.n_experts, ep->e_lo,
+                                       sh.n_experts + ep->n_shared, 0, 1, ep->g, ep->n_shared, 1, 1,
+                                       (int*)(b + w.ridx), (int)N, b + w.rxq, b + w.xs, w.total - w.xs,
+                                       (float*)(b + w.y), nullptr, ep->kernels,
+                                       (int)((size_t)ep->e_n * N / ((size_t)T * ks) + ep->n_shared), s,
+                                       (unsigned*)b, ep->dp_meta + 131));
+    k_dp_return<<<grid_n, 256, 0, s>>>((float*)(b + w.y), ep->dp_meta, (int*)(b + w.rsrc), (int*)(b + w.rpos),
+                                       ep->dp_bases, ep->rank, d, ep->dp_ctl);
+    EP_CUDA(cudaGetLastError());
+    k_dp_combine<<<T, 256, 0, s>>>(x_dev, ks, (float*)(b + w.wts), (int*)(b + w.slot), pre, ep->dp_region, d,
+                                   ep->dp_ctl, EP_WAIT_CYCLES);
+    EP_CUDA(cudaGetLastError());
+    return TG_OK;
+}
+
+// Records and y rows this rank received and sent in its last call (synchronises).
+extern "C" int tgx_ep_dispatch_p2p_counts(tgx_ep* ep, int* received, int* sent) {
+    EP_CHECK(ep && ep->dp_meta, TG_EINVAL, "tgx_ep_dispatch_p2p_counts: null context or not initialised");
+    Dev dg(ep->device);
+    EP_CUDA(cudaDeviceSynchronize());
+    int meta[132];
+    EP_CUDA(cudaMemcpy(meta, ep->dp_meta, sizeof(meta), cudaMemcpyDeviceToHost));
+    if (received) *received = meta[131];
+    if (sent) *sent = meta[ep->size];
+    return TG_OK;
+}
+
+extern "C" int tgx_ep_dispatch_p2p_status(tgx_ep* ep, void* stream) {
+    EP_CHECK(ep, TG_EINVAL, "tgx_ep_dispatch_p2p_status: null context");
+    if (!ep->dp_ctl) return TG_OK;
+    Dev dg(ep->device);
+    EP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    unsigned flag = 0;
+    EP_CUDA(cudaMemcpy(&flag, ep->dp_ctl + 4, sizeof(flag), cudaMemcpyDeviceToHost));
+    if (flag) {
+        EP_CUDA(cudaMemset(ep->dp_ctl + 4, 0, sizeof(flag)));
+        return ep_fail(TG_ETIMEOUT, "tgx_ep_moe_layer_dispatch_p2p: a peer's flag did not arrive within the wait limit");
+    }
     return TG_OK;
 }

@@ -128,7 +128,9 @@ cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const flo
 // experts each; rank 0 of G = 1 with e_n = E + n_shared takes every pair), from the
 // tokens' activation rows xq; scratch of experts_scratch_bytes (error flag first);
 // pairs_per_expert_div: the experts the pairs spread over, for the kernel choice;
-// err_flag, when given, replaces the scratch's own error flag.
+// err_flag, when given, replaces the scratch's own error flag; n_pairs_dev, when given,
+// holds the pair count on the device and n_tok * ks is only its upper bound (grids and
+// scratch are sized for the bound).
 size_t experts_scratch_bytes(const Geom& g, int E, int n_shared, size_t n_pairs);
 cudaError_t launch_batched_route(Geom g, const float* R, const float* normw, float eps, int E, int n_shared, int k,
                                  const float* X, int T, unsigned long long* S, int* idx, float* wts, float* logits_out,
@@ -137,7 +139,7 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
                                    int G, Geom g, int n_shared, int k, int ks, const int* idx, int n_tok,
                                    const uint8_t* xq, void* scratch, size_t scratch_bytes, float* y, int* owned,
                                    int kernels, int pairs_per_expert_div, cudaStream_t s,
-                                   unsigned* err_flag = nullptr);
+                                   unsigned* err_flag = nullptr, const int* n_pairs_dev = nullptr);
 
 // The reference library's own formats (tg_kquant.cu).  fmt: KQ_Q4K (ggml Q4_K
 // blocks), KQ_F16, KQ_Q6K (split layout: 208-byte bodies of all blocks, then their

@@ -339,6 +339,40 @@ class EPMoEModel:
         for layer in range(self.n_layers):
             self.moe_layer_dispatch(layer, X, stream, stats)
 
+    def enable_dispatch_p2p(self, t_max: int, exchange=None):
+        """Token dispatch without host syncs (tgx_ep_dispatch_p2p_*): records and y rows
+        travel through the ranks' IPC regions over NVLink.  t_max: the most tokens a rank
+        passes to one call.  exchange as for enable_p2p."""
+        n = int(self.lib.tgx_ep_p2p_handle_bytes())
+        h = (ctypes.c_uint8 * n)()
+        check(self.lib.tgx_ep_dispatch_p2p_init(self._ep, t_max, h), self.lib)
+        mine = bytes(h)
+        handles = self._gather_handles(mine, exchange)
+        assert len(handles) == self.size and handles[self.rank] == mine
+        buf = (ctypes.c_uint8 * (n * self.size)).from_buffer_copy(b"".join(handles))
+        check(self.lib.tgx_ep_dispatch_p2p_connect(self._ep, buf), self.lib)
+        self.p2p = True   # close() disconnects the mappings before the barrier
+
+    def moe_layer_dispatch_p2p(self, layer: int, X, stream=None):
+        """MoE block `layer` for this rank's tokens X (cuda f32[T][embed], 1 <= T <= t_max) in
+        place; every rank calls it for the same layers in the same order."""
+        assert X.dim() == 2 and X.shape[1] == self.embed and X.shape[0] >= 1
+        check(self.lib.tgx_ep_moe_layer_dispatch_p2p(self._ep, layer, _dev_ptr(X), X.shape[0],
+                                                     _stream_handle(stream)), self.lib)
+
+    def decode_dispatch_p2p(self, X, stream=None):
+        for layer in range(self.n_layers):
+            self.moe_layer_dispatch_p2p(layer, X, stream)
+
+    def dispatch_p2p_counts(self):
+        """(records received, records sent) by the last call."""
+        r, s = ctypes.c_int(), ctypes.c_int()
+        check(self.lib.tgx_ep_dispatch_p2p_counts(self._ep, ctypes.byref(r), ctypes.byref(s)), self.lib)
+        return r.value, s.value
+
+    def dispatch_p2p_status(self, stream=None):
+        check(self.lib.tgx_ep_dispatch_p2p_status(self._ep, _stream_handle(stream)), self.lib)
+
     def p2p_status(self, stream=None):
         check(self.lib.tgx_ep_p2p_status(self._ep, _stream_handle(stream)), self.lib)
 
