@@ -300,6 +300,37 @@ def test_ep_dispatch_p2p_single_rank_matches_batched(T, kernels):
     full.close()
 
 
+def test_ep_dispatch_p2p_shared_expert_matches_oracle(oracle):
+    # the device-side dispatch with a shared expert (its slot goes to the token's own rank),
+    # one rank, host-made weights, two layers, against the oracle
+    import numpy as np
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    h, i, e, k, L, T = 512, 256, 16, 4, 2, 7
+    rng = np.random.default_rng(21)
+    blobs = [oracle.quantize_q4_0(oracle.fill_normal(e * 3 * h * i, 41 + l, 0.05)) for l in range(L)]
+    shared = [oracle.quantize_q4_0(oracle.fill_normal(3 * h * i, 71 + l, 0.05)) for l in range(L)]
+    routers = [oracle.fill_normal(e * h, 81 + l, 0.05).reshape(e, h) for l in range(L)]
+    norms = [rng.uniform(0.5, 1.5, h).astype(np.float32) for _ in range(L)]
+    ep = EPMoEModel(h, i, e, k, L, rank=0, size=1, n_shared=1)
+    for l in range(L):
+        ep.load_experts(l, 0, blobs[l])
+        ep.load_shared(l, shared[l])
+        ep.set_router(l, routers[l])
+        ep.set_ffn_norm(l, norms[l])
+    ep.enable_dispatch_p2p(T)
+    X0 = rng.standard_normal((T, h)).astype(np.float32)
+    X = torch.from_numpy(X0.copy()).cuda()
+    ep.decode_dispatch_p2p(X)
+    ep.dispatch_p2p_status()
+    ref = X0.copy()
+    for l in range(L):
+        ref = oracle.moe_block_batched(blobs[l], routers[l], ref, k, h, i, normw=norms[l], shared=shared[l])
+    assert np.array_equal(X.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    assert ep.dispatch_p2p_counts() == (T * (k + 1), T * (k + 1))
+    ep.close()
+
+
 def test_ep_fused_single_rank_matches_decode_step():
     # the one-kernel EP step with one rank (every expert local, its own y buffer): odd and
     # even step counts (both buffer halves), a router changed after set-up, a graph replay,
