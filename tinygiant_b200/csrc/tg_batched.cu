@@ -6,9 +6,10 @@
 //   k_topk_quant_batched    per token: sum x^2 -> RMSNorm scale, logits, top-k + softmax
 //                           (engine.py:229-236), Q8_0 of (x * scale) * w (libtinygiant.c:61-89)
 //   k_group_pairs           (token, slot) pairs grouped by expert (counting sort)
-//   k_gateup_batched        per (expert, 32-row unit): the unit's gate and up rows are staged in
-//                           shared memory once, then h = silu(g) * u and its Q8_0 block for every
-//                           token routed to the expert (libtinygiant.c:566-586)
+//   k_gateup_batched        per (expert, 16-row unit): the unit's gate and up rows are staged in
+//                           shared memory once, then h = silu(g) * u for every token routed to
+//                           the expert (libtinygiant.c:566-586)
+//   k_quant_h               the Q8_0 blocks of h, one warp per (pair, block)
 //   k_down_batched          per (expert, 16 output rows): the rows are staged once, then
 //                           y[pair][r] for every token routed to the expert (:588-594)
 //   k_combine_batched       x[t] += sum_j w[t][j] * y[(t, j)] in slot order (engine.py:240-258)
@@ -20,8 +21,7 @@
 // expert id E; with experts sharded over G devices, a pair (token t, slot j) is computed by
 // the device holding its routed expert, and a token's shared-expert pair by the device that
 // holds the fewest of that token's routed experts (ties to (t + i) mod G, smallest i), a
-// rule every device evaluates the same way.  Rows wider than the shared-memory budget
-// allows for 32 gate/up rows use 16-row units and a separate Q8_0 pass over h.
+// rule every device evaluates the same way.
 #include <cuda_runtime.h>
 
 #include "tg_device.cuh"
@@ -413,11 +413,12 @@ __global__ void __launch_bounds__(256) k_down_batched(const uint8_t* __restrict_
     }
 }
 
-// grid T, 256 threads: x[t][r] = x[t][r] + (sum over slots j in order of w[t][j] * y[t*k+j][r])
+// grid (T, H / 256), 256 threads: x[t][r] = x[t][r] + (sum over slots j in order of
+// w[t][j] * y[t*k+j][r]), one row per thread
 __global__ void __launch_bounds__(256) k_combine_batched(float* __restrict__ X, int H, int k,
                                                          const float* __restrict__ wts, const float* __restrict__ y) {
     const int t = blockIdx.x;
-    for (int r = threadIdx.x; r < H; r += blockDim.x) {
+    for (int r = blockIdx.y * blockDim.x + threadIdx.x; r < H; r += gridDim.y * blockDim.x) {
         float a = 0.0f;
         for (int j = 0; j < k; j++) a = __fadd_rn(a, __fmul_rn(wts[(size_t)t * k + j], y[((size_t)t * k + j) * H + r]));
         X[(size_t)t * H + r] = __fadd_rn(X[(size_t)t * H + r], a);
@@ -426,8 +427,10 @@ __global__ void __launch_bounds__(256) k_combine_batched(float* __restrict__ X, 
 
 }  // namespace
 
-// gate/up rows per unit: 32 when 32 gate + 32 up rows fit one CTA's shared memory, else 16
-static int gu_rows(const Geom& g, size_t smem_optin) { return (size_t)2 * 32 * g.row_gu <= smem_optin ? 32 : 16; }
+// gate/up rows per CTA unit: 16, with the Q8_0 of h in a separate pass (k_quant_h).  Against
+// 32-row units quantising h in place, the smaller units fit twice the CTAs per SM, so more
+// weight loads are in flight: at the Qwen3 shape T = 64 -4%, T = 256 -12% per layer.
+constexpr int GU_ROWS = 16;
 
 size_t batched_smem_bytes(const Geom& g) {
     size_t m = (size_t)2 * 16 * g.row_gu;
@@ -504,7 +507,7 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
         return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, tile_pre, n_act, ks, hq, y, nullptr, err,
                              s);
     }
-    const int R_gu = gu_rows(g, (size_t)optin);
+    const int R_gu = GU_ROWS;
     const bool wide = n_pairs >= (size_t)WIDE_MIN_PAIRS * pairs_per_expert_div;
     const size_t sm_gu = (size_t)2 * R_gu * g.row_gu;
     auto gateup = [&](auto kern, int rows_per_cta) -> cudaError_t {
@@ -516,12 +519,9 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
                                                                  hq, hf);
         return cudaGetLastError();
     };
-    if (R_gu == 32)
-        e = wide ? gateup(k_gateup_batched<32, 8>, 32) : gateup(k_gateup_batched<32, 2>, 32);
-    else
-        e = wide ? gateup(k_gateup_batched<16, 16>, 16) : gateup(k_gateup_batched<16, 4>, 16);
+    e = wide ? gateup(k_gateup_batched<GU_ROWS, 16>, GU_ROWS) : gateup(k_gateup_batched<GU_ROWS, 4>, GU_ROWS);
     if (e != cudaSuccess) return e;
-    if (R_gu == 16) {
+    {
         const long long warps = (long long)n_pairs * g.nbI;
         k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, nullptr, (int)n_pairs, g, hq, n_pairs_dev);
     }
@@ -592,7 +592,7 @@ cudaError_t launch_moe_batched_partial(const uint8_t* layer, const uint8_t* shar
 cudaError_t launch_moe_batched_combine(float* X, int T, int H, int ks, const float* wts, const float* y,
                                        cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    k_combine_batched<<<T, 256, 0, s>>>(X, H, ks, wts, y);
+    k_combine_batched<<<dim3(T, (H + 255) / 256), 256, 0, s>>>(X, H, ks, wts, y);
     return cudaGetLastError();
 }
 
