@@ -225,26 +225,29 @@ __device__ __forceinline__ const uint8_t* expert_base(const uint8_t* layer, cons
     return e == E ? shared : layer + (size_t)(e - e_lo) * expert_bytes;
 }
 
-// grid (I / R, active experts), 256 threads.  CTA (c, a) takes the a-th active expert e and
-// stages rows R*c .. R*c+R-1 of its gate and up in shared memory, then takes the pairs
-// routed to e in tiles of P = 32 / (R/8) tokens: each warp owns R/8 rows, each lane runs
-// the lane-strided block chains of those rows for every token of the tile (a staged
-// weight block is read once per tile), and two transposed reductions leave lane l with
-// the gate and up sums of (row l / P, token l % P).  With R = 32 the unit is one Q8_0
-// block of h: warp w quantises token w's 32 values into hq[p]; with R = 16 h goes to
-// hf[p] for k_quant_h.  Per (row, token) the arithmetic is exactly the single-token one.
-template <int R, int P>
+// gate/up rows per CTA unit: 16, with the Q8_0 of h in a separate pass (k_quant_h).  Against
+// 32-row units quantising h in place, the smaller units fit twice the CTAs per SM, so more
+// weight loads are in flight: at the Qwen3 shape T = 64 -4%, T = 256 -12% per layer.
+constexpr int GU_ROWS = 16;
+
+// grid (I / 16, active experts), 256 threads.  CTA (c, a) takes the a-th active expert e and
+// stages rows 16c .. 16c+15 of its gate and up in shared memory, then takes the pairs
+// routed to e in tiles of P tokens: each warp owns 2 rows, each lane runs the lane-strided
+// block chains of those rows for every token of the tile (a staged weight block is read
+// once per tile), and two transposed reductions leave lane l with the gate and up sums of
+// (row l / P, token l % P); h = silu(g) * u goes to hf[p] for k_quant_h.  Per (row, token)
+// the arithmetic is exactly the single-token one.
+template <int P>
 __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restrict__ layer,
                                                         const uint8_t* __restrict__ shared, int E, int e_lo, Geom g,
                                                         const int* __restrict__ off, const int* __restrict__ list,
                                                         const int* __restrict__ active, int ks,
-                                                        const uint8_t* __restrict__ xq, uint8_t* __restrict__ hq,
-                                                        float* __restrict__ hf) {
+                                                        const uint8_t* __restrict__ xq, float* __restrict__ hf) {
+    constexpr int R = GU_ROWS;
     constexpr int RW = R / 8;        // rows per warp
     constexpr int NV = RW * P;       // sums per lane and matrix: 8 or 32
     constexpr int LPV = 32 / NV;     // lanes holding each reduced sum
     extern __shared__ __align__(16) uint8_t smem[];   // gate rows | up rows
-    __shared__ float sh[P][32];      // h of the tile (R = 32)
     __shared__ int sp[P];            // the tile's pairs
     if ((int)blockIdx.y >= active[0]) return;
     const int e = active[1 + blockIdx.y], c = blockIdx.x;
@@ -266,10 +269,10 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
     const uint8_t* gate = smem;
     const uint8_t* up = smem + unit;
     const int nb = g.nbH, i0 = warp * RW;
-    const size_t abx = act_bytes(nb), abh = act_bytes(g.nbI);
+    const size_t abx = act_bytes(nb);
     for (int q0 = 0; q0 < n; q0 += P) {
         const int nt = min(P, n - q0);
-        __syncthreads();   // the previous tile's sh / sp are consumed (and, first time, the weights staged)
+        __syncthreads();   // the previous tile's sp is consumed (and, first time, the weights staged)
         if (threadIdx.x < P) sp[threadIdx.x] = threadIdx.x < nt ? list[p0 + q0 + threadIdx.x] : -1;
         __syncthreads();
         float ag[NV], au[NV];   // [row r][token t] at r * P + t
@@ -303,25 +306,7 @@ __global__ void __launch_bounds__(256) k_gateup_batched(const uint8_t* __restric
         const float gv = warp_sum_transposed<NV>(ag, lane);
         const float uv = warp_sum_transposed<NV>(au, lane);
         const int j = lane / LPV, r = j / P, t = j % P;
-        if (lane % LPV == 0 && t < nt) {
-            const float hv = silu_mul(gv, uv);
-            if (R == 32)
-                sh[t][i0 + r] = hv;
-            else
-                hf[(size_t)sp[t] * g.I + (size_t)c * R + i0 + r] = hv;
-        }
-        if (R == 32) {
-            __syncthreads();
-            if (warp < nt) {
-                const Q8Lane qz = quantize_lane(sh[warp][lane]);
-                ActView ha = act_view(hq + (size_t)sp[warp] * abh, g.nbI);
-                ha.qs[(size_t)c * 32 + lane] = (int8_t)qz.q;
-                if (lane == 0) {
-                    ha.d[c] = f16_bits_to_f32(qz.dh);
-                    ha.s8[c] = qz.s8;
-                }
-            }
-        }
+        if (lane % LPV == 0 && t < nt) hf[(size_t)sp[t] * g.I + (size_t)c * R + i0 + r] = silu_mul(gv, uv);
     }
 }
 
@@ -427,11 +412,6 @@ __global__ void __launch_bounds__(256) k_combine_batched(float* __restrict__ X, 
 
 }  // namespace
 
-// gate/up rows per CTA unit: 16, with the Q8_0 of h in a separate pass (k_quant_h).  Against
-// 32-row units quantising h in place, the smaller units fit twice the CTAs per SM, so more
-// weight loads are in flight: at the Qwen3 shape T = 64 -4%, T = 256 -12% per layer.
-constexpr int GU_ROWS = 16;
-
 size_t batched_smem_bytes(const Geom& g) {
     size_t m = (size_t)2 * 16 * g.row_gu;
     m = m > (size_t)DOWN_ROWS * g.row_d ? m : (size_t)DOWN_ROWS * g.row_d;
@@ -516,10 +496,10 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
             (r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu)) != cudaSuccess)
             return r;
         kern<<<dim3(g.I / rows_per_cta, n_act), 256, sm_gu, s>>>(layer, shared, E, e_lo, g, off, list, active, ks, xq,
-                                                                 hq, hf);
+                                                                 hf);
         return cudaGetLastError();
     };
-    e = wide ? gateup(k_gateup_batched<GU_ROWS, 16>, GU_ROWS) : gateup(k_gateup_batched<GU_ROWS, 4>, GU_ROWS);
+    e = wide ? gateup(k_gateup_batched<16>, GU_ROWS) : gateup(k_gateup_batched<4>, GU_ROWS);
     if (e != cudaSuccess) return e;
     {
         const long long warps = (long long)n_pairs * g.nbI;
