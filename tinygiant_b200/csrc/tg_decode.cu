@@ -542,6 +542,12 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
         cur_l = l;
         unsigned long long* accl = P.acc + (size_t)l * acc_words;
         const bool next = l + 1 < P.nL;
+        // one device: the unit count is static, so the arena fence and the units' mbarrier
+        // arming come before the routing, off the path from top-k to the copies
+        if (!EP && tid == PT) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            for (int u = 0; u < n_gu; u++) mbar_arrive_expect_tx(mbar_gu + u, 2 * gu_unit_bytes);
+        }
         const uint8_t* lbase = P.weights + (size_t)layer * P.layer_bytes;
         // ------------------------------------------------------------ A: routing sums and x_l
         // Every word is validated on its own: x_l values carry the launch tag (x_in
@@ -688,8 +694,10 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             // bytes go first
             if (lane == 0) {
                 // the regions below were read by this CTA's threads in the previous layer
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                for (int u = 0; u < n_gu; u++) mbar_arrive_expect_tx(mbar_gu + u, 2 * gu_unit_bytes);
+                if (EP) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    for (int u = 0; u < n_gu; u++) mbar_arrive_expect_tx(mbar_gu + u, 2 * gu_unit_bytes);
+                }
                 pending |= (1u << n_gu) - 1u;
             }
             __syncwarp();
