@@ -387,9 +387,10 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
     const unsigned tag = epoch % 65535u + 1u;   // 1..65535; the tagged buffers are cleared before it repeats
     // EP: the y words carry the full launch count (never cleared; every rank launches
     // the same sequence) and alternate buffer halves by launch parity, so a rank one
-    // launch ahead never overwrites a word another rank has still to read.  The tag is
-    // 0, the buffers' initial value, only at launch 2^32 - 1: reset the context
-    // (tgx_ep_fused_reset) before that many steps.
+    // launch ahead never overwrites a word another rank has still to read.  Every launch
+    // rewrites every word of its half (each slot has one owner, which stores all rows), so
+    // a half holds the tag of two launches before, never the initial 0: the 32-bit tag may
+    // wrap.
     const unsigned ytag = epoch + 1u;
     int nloc = k;   // EP: slots whose expert is held here this layer
     // gate/up unit u of this CTA (slot * nbI + 32-row chunk): the static plan's, or with
