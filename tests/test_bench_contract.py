@@ -24,3 +24,43 @@ def test_reference_arm_json_line():
     assert set(d["config"]) == {"workload", "hidden", "inter", "experts", "top_k", "layers", "weights",
                                 "hidden_states", "l2", "parallelism"}
     assert d["config"]["layers"] == 48 and "layers_per_step" in d
+
+
+def test_headline_parallelism_labels():
+    # N > 1 runs the expert-parallel decode of one token stream (strong scaling) unless
+    # --replicas; both arms print the same labels from the same function
+    r = subprocess.run([sys.executable, "-c",
+                        "import sys; sys.path.insert(0, '.'); import bench; "
+                        "print(bench.headline_parallelism(1, False), bench.headline_parallelism(8, False), "
+                        "bench.headline_parallelism(8, True), bench.headline_config(48, 8)['parallelism'])"],
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    out = r.stderr + r.stdout   # bench.py points fd 1 at stderr on import
+    assert "('single GPU', 'weak') ('ep8', 'strong') ('replicas', 'weak') ep8" in out
+
+
+def test_ep_split_from_stamps():
+    # the per-layer split of the expert-parallel decode, from synthetic phase stamps:
+    # layer l starts at 20,000 l ns; stamps 12 / 13 / 7 (values pushed, received, sums sent)
+    # at +8,750 / +11,750 / +13,750 ns on the slowest CTA (bench.py imports in a child:
+    # it points file descriptor 1 at stderr)
+    r = subprocess.run([sys.executable, "-c", """
+import sys, json
+sys.path.insert(0, '.')
+import numpy as np
+import bench
+L, G = 5, 4
+st = np.zeros((L, G, 32), np.uint64)
+for l in range(L):
+    base = 20000 * l
+    for c in range(G):
+        st[l, c, 0] = base + 100 * c
+        st[l, c, 12] = base + 8000 + 250 * c
+        st[l, c, 13] = base + 11000 + 250 * c
+        st[l, c, 7] = base + 13000 + 250 * c
+print(json.dumps(bench.ep_split(st)))
+"""], capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    import json as _json
+    d = _json.loads([ln for ln in (r.stderr + r.stdout).splitlines() if ln.startswith("{")][-1])
+    assert d == {"layer_us": 20.0, "partial_us": 8.75, "exchange_us": 3.0, "combine_us": 2.0}
