@@ -232,6 +232,17 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
     const int tid = threadIdx.x;
     unsigned mine = 0, done = 0;
     for (int i = 0; i * NT + tid < nwords; i++) mine |= 1u << i;
+    // with a slot map, word w of record rec = w / 6 of local slot jl = rec / nbI lies at
+    // (lmap[jl] - jl) * nbI * 6 + w; the first batch's offsets are worked out once, not
+    // on every polling round
+    auto source = [&](int w) -> int {
+        if (!lmap || w >= nwords) return w;
+        const int jl = w / (6 * nbI);
+        return (lmap[jl] - jl) * nbI * 6 + w;
+    };
+    int src0[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) src0[t] = source(t * NT + tid);
     const long long t0 = clock64();
     int spins = 0;
     while (done != mine) {
@@ -241,11 +252,7 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
 #pragma unroll
             for (int t = 0; t < 8; t++) {
                 const int i = i0 + t, w = i * NT + tid;
-                int src = w;
-                if (lmap && w < nwords) {
-                    const int rec = w / 6, jl = rec / nbI;
-                    src = (lmap[jl] - jl) * nbI * 6 + w;
-                }
+                const int src = i0 == 0 ? src0[t] : source(w);
                 v[t] = (w < nwords && !(done >> i & 1u)) ? ld_relaxed_u64(hw + src) : 0ull;
             }
 #pragma unroll
@@ -292,8 +299,19 @@ __device__ __forceinline__ bool gather_h_records(const unsigned long long* hw, i
 // one transposed reduction over the group's rows.  Each row's reduction is the same
 // pairing tree as a butterfly over the lanes whatever the other values in the
 // reduction, so the bits are the mirror order's.  Called from one place only.
+// Experts sharded over devices: where the down values go besides ys (every rank's y
+// buffer, this launch's half and layer), as soon as each warp has them.
+struct DownPush {
+    unsigned long long* const* ypeer;
+    size_t ylay;        // this layer's words in every rank's buffer
+    const int* lmap;    // local slot -> slot
+    int d_lo, H, ep_size;
+    unsigned ytag;
+};
+
 __device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* hq_base, float* ys, uint32_t d_chunk,
-                                          int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi) {
+                                          int row_d, int nbI, int ab_i, int d_n, int max_rows, int jlo, int jhi,
+                                          const DownPush* push = nullptr) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ns = jhi - jlo;
     if (warp >= CW || ns <= 0 || d_n <= 0) return;
@@ -324,7 +342,14 @@ __device__ __forceinline__ void down_rows(const uint8_t* dbase, const uint8_t* h
         }
         const float y = warp_sum8_transposed(acc, lane);   // row q0 + r in lanes 4r .. 4r+3
         const int r = lane >> 2;
-        if ((lane & 3) == 0 && r < nr) ys[(size_t)j * max_rows + q0 + r] = y;
+        if ((lane & 3) == 0 && r < nr) {
+            ys[(size_t)j * max_rows + q0 + r] = y;
+            if (push) {
+                const unsigned long long word = ((unsigned long long)push->ytag << 32) | __float_as_uint(y);
+                const size_t at = push->ylay + (size_t)push->lmap[j] * push->H + push->d_lo + q0 + r;
+                for (int rr = 0; rr < push->ep_size; rr++) st_relaxed_sys_u64(push->ypeer[rr] + at, word);
+            }
+        }
     }
 }
 
@@ -889,14 +914,10 @@ __global__ void __launch_bounds__(NT, 1) k_decode_fused(FusedParams P) {
             if (!cta_sync_and(!(d_n > 0 || next) || wait_bar(mbar_d, (unsigned)l & 1u, 5))) goto drain;
             if (tid == PT) pending &= ~(1u << 4);
             if (tid == 0) stamp(l, 5);
-            if (d_n > 0 && nloc > 0) down_partial(0, nloc);
-            cta_sync();
-            const int nyw = nloc * d_n;
-            for (int w = tid; w < nyw * P.ep_size; w += NT) {
-                const int r = w / nyw, rem = w - r * nyw, jl = rem / d_n, q = rem - jl * d_n;
-                st_relaxed_sys_u64(P.ypeer[r] + ylay + (size_t)lmap[jl] * g.H + d_lo + q,
-                                   ((unsigned long long)ytag << 32) |
-                                       __float_as_uint(ys[(size_t)jl * P.max_rows + q]));
+            // each warp stores its rows' values into every rank's y buffer as it ends
+            if (d_n > 0 && nloc > 0) {
+                const DownPush push{P.ypeer, ylay, lmap, d_lo, g.H, P.ep_size, ytag};
+                down_rows(dbase, hq_base, ys, d_chunk, g.row_d, nbI, (int)ab_i, d_n, P.max_rows, 0, nloc, &push);
             }
             if (tid == 0) stamp(l, 12);
             if (d_n > 0) {
