@@ -88,9 +88,10 @@ def parse():
                     help="with --ep: token dispatch instead of replicated tokens: each rank holds T/N of the "
                          "tokens and sends each (token, slot) pair's Q8_0 row to its expert's holder and gets y "
                          "back (NCCL all-to-alls, tgx_ep_dispatch*)")
-    ap.add_argument("--batched-kernels", choices=["auto", "dp4a", "mma"], default="auto",
+    ap.add_argument("--batched-kernels", choices=["auto", "dp4a", "mma", "mma-fast"], default="auto",
                     help="expert matmuls of the batched / EP path: auto (tensor cores from 16 pairs per expert), "
-                         "dp4a, or mma (tcgen05); all give the same bits")
+                         "dp4a, or mma (tcgen05), which give the same bits; mma-fast: tcgen05 with the one-fma "
+                         "epilogue, within the accumulation-order tolerance instead of bit-identical")
     ap.add_argument("--shape", choices=["qwen3", "dsv3"], default="qwen3",
                     help="with --ep: qwen3 (configs[2]) or the DeepSeek-V3-like configs[4] (hidden 7168, "
                          "inter 2048, 256 routed + 1 shared expert, 58 layers, as many as fit per GPU)")
@@ -765,7 +766,7 @@ def run_tier(args):
     return 0
 
 
-KERNELS = {"auto": 0, "dp4a": 1, "mma": 2}
+KERNELS = {"auto": 0, "dp4a": 1, "mma": 2, "mma-fast": 3}
 Q4K_BLOCK, Q6K_BLOCK = 144, 210
 
 

@@ -255,8 +255,11 @@ int tgx_moe_batched(tgx_ctx *ctx, int layer, float *x_dev, int T, void *stream);
  * step instead (the same bits, faster for few tokens). */
 int tgx_decode_batched(tgx_ctx *ctx, float *x_dev, int T, void *stream);
 /* expert matmul kernels of tgx_moe_batched / tgx_decode_batched: 0 auto (tensor cores,
- * tcgen05, when experts average >= 16 pairs), 1 dp4a, 2 tensor cores; all give the same
- * bits.  tgx_sync_status reports an expired bounded wait of the tensor-core kernels. */
+ * tcgen05, when experts average >= 16 pairs), 1 dp4a, 2 tensor cores; these give the same
+ * bits.  3: tensor cores with the fast epilogue (one fma per Q4_0 block: the same exact
+ * int32 block dots, another fp32 summation order), within the reference's
+ * accumulation-order tolerance rather than bit-identical.  tgx_sync_status reports an
+ * expired bounded wait of the tensor-core kernels. */
 int tgx_set_batched_kernels(tgx_ctx *ctx, int kernels);
 
 /* The MoE block of layer `layer` over a given list of experts (routing decided by the
@@ -350,7 +353,8 @@ size_t tgx_ep_y_floats(const tgx_ep *ep, int T);
 int tgx_ep_moe_partial(tgx_ep *ep, int layer, const float *x_dev, int T, float *y_dev, void *stream);
 int tgx_ep_combine(tgx_ep *ep, float *x_dev, int T, const float *y_dev, void *stream);
 /* expert matmul kernels of the partial step: 0 auto (tensor cores when experts average
- * >= 16 pairs), 1 dp4a, 2 tensor cores (tcgen05); all give the same bits */
+ * >= 16 pairs), 1 dp4a, 2 tensor cores (tcgen05); these give the same bits.  3: tensor
+ * cores with the fast epilogue, as in tgx_set_batched_kernels. */
 int tgx_ep_set_kernels(tgx_ep *ep, int kernels);
 /* synchronise `stream`; TG_ETIMEOUT (and the flag cleared) if a tensor-core kernel's
  * bounded wait expired since the last call */

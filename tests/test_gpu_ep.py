@@ -127,6 +127,32 @@ def test_ep_dsv3_width_matches_oracle(oracle):
         ep.close()
 
 
+def test_ep_fast_epilogue_same_bits_on_every_sharding():
+    # kernels=3 (fast epilogue): each (row, token) sum is one fma chain over the blocks,
+    # whatever the tile or rank, so 1, 2 and 4 emulated ranks give the same bits
+    import numpy as np
+    import torch
+    from tinygiant_b200.ep import EPMoEModel
+    h, i, e, k, L, T = 2048, 768, 16, 4, 2, 96
+    rng = np.random.default_rng(3)
+    X0 = rng.standard_normal((T, h)).astype(np.float32)
+    outs = []
+    for G in (1, 2, 4):
+        ranks = [EPMoEModel(h, i, e, k, L, rank=r, size=G) for r in range(G)]
+        for ep in ranks:
+            ep.fill_synthetic(77)
+            ep.set_kernels(3)
+        X = torch.from_numpy(X0.copy()).cuda()
+        _emulate(ranks, X, L)
+        torch.cuda.synchronize()
+        outs.append(X.cpu().numpy())
+        for ep in ranks:
+            ep.close()
+    assert np.isfinite(outs[0]).all() and not np.array_equal(outs[0], X0)
+    for o in outs[1:]:
+        assert np.array_equal(o.view(np.uint32), outs[0].view(np.uint32))
+
+
 @pytest.mark.parametrize("T,kernels", [(1, 0), (7, 1), (300, 2)])
 def test_ep_p2p_single_rank_matches_batched(T, kernels):
     # the NVLink-exchange entry point with one rank (its own region, its own flags):

@@ -476,16 +476,17 @@ cudaError_t launch_batched_experts(const uint8_t* layer, const uint8_t* shared, 
     const size_t max_act = (size_t)e_n + n_shared;
     const int n_act = (int)(n_pairs < max_act ? n_pairs : max_act);
     const bool mma = q4_mma_supported(g) &&
-                     (kernels == BATCHED_MMA ||
+                     (kernels == BATCHED_MMA || kernels == BATCHED_MMA_FAST ||
                       (kernels == BATCHED_AUTO && n_pairs >= (size_t)MMA_MIN_PAIRS_PER_EXPERT * pairs_per_expert_div));
+    const bool exact = kernels != BATCHED_MMA_FAST;
     if (mma) {
         if ((e = launch_q4_mma(layer, shared, E, e_lo, g, 0, off, list, active, tile_pre, n_act, ks, xq, hf, uf, err,
-                               s)) != cudaSuccess)
+                               exact, s)) != cudaSuccess)
             return e;
         const long long warps = (long long)n_pairs * g.nbI;
         k_quant_h<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, s>>>(hf, uf, (int)n_pairs, g, hq, n_pairs_dev);
         return launch_q4_mma(layer, shared, E, e_lo, g, 1, off, list, active, tile_pre, n_act, ks, hq, y, nullptr, err,
-                             s);
+                             exact, s);
     }
     const int R_gu = GU_ROWS;
     const bool wide = n_pairs >= (size_t)WIDE_MIN_PAIRS * pairs_per_expert_div;

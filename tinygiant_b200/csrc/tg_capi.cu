@@ -1197,8 +1197,9 @@ extern "C" int tgx_fused_inject_missing(tgx_ctx* ctx, int n) {
 }
 
 extern "C" int tgx_set_batched_kernels(tgx_ctx* ctx, int kernels) {
-    TG_CHECK(ctx && kernels >= 0 && kernels <= 2, TG_EINVAL,
-             "tgx_set_batched_kernels: kernels must be 0 (auto), 1 (dp4a) or 2 (tensor cores)");
+    TG_CHECK(ctx && kernels >= 0 && kernels <= 3, TG_EINVAL,
+             "tgx_set_batched_kernels: kernels must be 0 (auto), 1 (dp4a), 2 (tensor cores) or 3 (tensor cores, "
+             "fast epilogue)");
     ctx->batched_kernels = kernels;
     return TG_OK;
 }

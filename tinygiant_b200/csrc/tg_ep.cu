@@ -394,7 +394,9 @@ extern "C" int tgx_ep_combine(tgx_ep* ep, float* x_dev, int T, const float* y_de
 }
 
 extern "C" int tgx_ep_set_kernels(tgx_ep* ep, int kernels) {
-    EP_CHECK(ep && kernels >= 0 && kernels <= 2, TG_EINVAL, "tgx_ep_set_kernels: kernels must be 0 (auto), 1 (dp4a) or 2 (tensor cores)");
+    EP_CHECK(ep && kernels >= 0 && kernels <= 3, TG_EINVAL,
+             "tgx_ep_set_kernels: kernels must be 0 (auto), 1 (dp4a), 2 (tensor cores) or 3 (tensor cores, fast "
+             "epilogue)");
     ep->kernels = kernels;
     return TG_OK;
 }

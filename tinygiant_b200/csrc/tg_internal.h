@@ -79,8 +79,9 @@ cudaError_t prepare_kernels(Geom g, int k);
 // a CTA of the path needs.
 // kernels: which expert matmuls run — BATCHED_AUTO picks the tensor-core path
 // (tg_tc.cu) when experts average >= 16 pairs, BATCHED_DP4A / BATCHED_MMA force one;
-// both give the same bits.
-constexpr int BATCHED_AUTO = 0, BATCHED_DP4A = 1, BATCHED_MMA = 2;
+// those give the same bits.  BATCHED_MMA_FAST: the tensor cores with the one-fma
+// epilogue, within the accumulation-order tolerance instead of bit-identical.
+constexpr int BATCHED_AUTO = 0, BATCHED_DP4A = 1, BATCHED_MMA = 2, BATCHED_MMA_FAST = 3;
 size_t batched_scratch_bytes(const Geom& g, int E, int k, int T);
 size_t batched_smem_bytes(const Geom& g);
 cudaError_t launch_moe_batched(const uint8_t* layer, Geom g, const float* R, const float* normw, float eps, int E,
@@ -96,7 +97,7 @@ bool q4_mma_supported(const Geom& g);
 int q4_mma_tile_tokens();
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
                           const int* off, const int* list, const int* active, const int* tile_pre, int n_act, int ks,
-                          const uint8_t* act, float* out0, float* out1, unsigned* err, cudaStream_t s);
+                          const uint8_t* act, float* out0, float* out1, unsigned* err, bool exact, cudaStream_t s);
 // The two halves of launch_moe_batched, generalised to experts sharded over G devices
 // and an optional shared expert.  Partial: routing of all T tokens (every device
 // computes the same), then y[(t, j)][H] for the pairs this device owns (routed slot j < k:

@@ -11,6 +11,12 @@
 // tree's siblings consecutive, so a 6-slot stack per (row, token) evaluates it as the
 // class sums arrive.
 //
+// EXACT = false: the fast epilogue.  Per (row, token) one fp32 accumulator takes
+// acc = fma(float(sumi), d_w * d_x, acc) block after block in the K order above; no class
+// chains, no tree.  The int32 block dots are the same exact values; only the fp32
+// summation order differs, so the result stays within the reference's accumulation-order
+// tolerance (1e-5 max-abs-rel before any Q8_0 requantisation), not bit-identical.
+//
 // Work item: 128 weight rows (one matrix of one expert) x a tile of 32 tokens; 16 warps,
 // one persistent CTA per SM walking its items' K groups as one pipeline.
 // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and owns tokens 8 (w / 4) .. + 7.
@@ -146,6 +152,7 @@ constexpr int RING = 4;         // work items whose token lists are held at once
 // CTAs working at once share the tile's activations.  Its K groups are consecutive in
 // the CTA's flattened group sequence f, so the pipeline (three shared stages, two TMEM
 // sets) runs across item boundaries without restarting.
+template <bool EXACT>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t mbar[2];
@@ -390,33 +397,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
                     uint32_t (&cur)[8] = (jj & 1) ? vb : va;
                     uint32_t (&nxt)[8] = (jj & 1) ? va : vb;
                     if (jj + 1 < nsteps) tmem_ld8(nxt, tcol + (uint32_t)((jj + 1) * TN));
-                    const int code = s_steps[gi * KG + jj];
-                    const int c = (code >> 10) & 31;
-                    for (; next_cls < c; next_cls++) push8(st, zero8, next_cls);
                     const float dw = dwp[jj * TM + row];
                     const float4 dxa = *reinterpret_cast<const float4*>(dxp + jj * TN + cg * 8);
                     const float4 dxb = *reinterpret_cast<const float4*>(dxp + jj * TN + cg * 8 + 4);
                     const float dx[8] = {dxa.x, dxa.y, dxa.z, dxa.w, dxb.x, dxb.y, dxb.z, dxb.w};
+                    if constexpr (EXACT) {
+                        const int code = s_steps[gi * KG + jj];
+                        const int c = (code >> 10) & 31;
+                        for (; next_cls < c; next_cls++) push8(st, zero8, next_cls);
 #pragma unroll
-                    for (int t = 0; t < 8; t++)
-                        leaf[t] = __fadd_rn(leaf[t], __fmul_rn(__fmul_rn(__int2float_rn((int)cur[t]), dw), dx[t]));
-                    if (code >> 15) {
-                        push8(st, leaf, c);
+                        for (int t = 0; t < 8; t++)
+                            leaf[t] = __fadd_rn(leaf[t], __fmul_rn(__fmul_rn(__int2float_rn((int)cur[t]), dw), dx[t]));
+                        if (code >> 15) {
+                            push8(st, leaf, c);
 #pragma unroll
-                        for (int t = 0; t < 8; t++) leaf[t] = 0.0f;
-                        next_cls = c + 1;
+                            for (int t = 0; t < 8; t++) leaf[t] = 0.0f;
+                            next_cls = c + 1;
+                        }
+                    } else {   // leaf[t] is the token's single accumulator
+#pragma unroll
+                        for (int t = 0; t < 8; t++)
+                            leaf[t] = __fmaf_rn(__int2float_rn((int)cur[t]), __fmul_rn(dw, dx[t]), leaf[t]);
                     }
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
             }
             if (gi == NG - 1) {   // the item's last group: finish the trees, write the sums
-                for (; next_cls < 32; next_cls++) push8(st, zero8, next_cls);
+                if constexpr (EXACT)
+                    for (; next_cls < 32; next_cls++) push8(st, zero8, next_cls);
                 const Item it = item(i);
                 float* out = it.mat == 1 ? P.out1 : P.out0;
 #pragma unroll
                 for (int t = 0; t < 8; t++) {
                     const int tk = cg * 8 + t;
-                    if (tk < it.nt) out[(size_t)s_pairs[i & (RING - 1)][tk] * rows + it.r_base + row] = st[t][5];
+                    if (tk < it.nt)
+                        out[(size_t)s_pairs[i & (RING - 1)][tk] * rows + it.r_base + row] = EXACT ? st[t][5] : leaf[t];
                 }
             }
         }
@@ -458,7 +473,7 @@ int q4_mma_tile_tokens() { return TN; }
 
 cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, int e_lo, Geom g, int down,
                           const int* off, const int* list, const int* active, const int* tile_pre, int n_act, int ks,
-                          const uint8_t* act, float* out0, float* out1, unsigned* err, cudaStream_t s) {
+                          const uint8_t* act, float* out0, float* out1, unsigned* err, bool exact, cudaStream_t s) {
     if (n_act <= 0) return cudaSuccess;
     if (n_act > MAX_ACT) return cudaErrorInvalidValue;
     if (!q4_mma_supported(g)) return cudaErrorInvalidValue;
@@ -478,12 +493,13 @@ cudaError_t launch_q4_mma(const uint8_t* layer, const uint8_t* shared, int E, in
     P.out0 = out0;
     P.out1 = out1;
     P.err = err;
-    cudaError_t e = cudaFuncSetAttribute(k_q4_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    auto kern = exact ? k_q4_mma<true> : k_q4_mma<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 0;
     if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    k_q4_mma<<<sms, TC_THREADS, TC_SMEM, s>>>(P);   // persistent: one CTA per SM
+    kern<<<sms, TC_THREADS, TC_SMEM, s>>>(P);   // persistent: one CTA per SM
     return cudaGetLastError();
 }
 

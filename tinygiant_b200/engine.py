@@ -128,7 +128,8 @@ class MoEModel:
         check(self.lib.tgx_decode_batched(self._ctx, _dev_ptr(X), X.shape[0], _stream_handle(stream)), self.lib)
 
     def set_batched_kernels(self, kernels: int):
-        """Expert matmuls of the batched path: 0 auto, 1 dp4a, 2 tensor cores; same bits."""
+        """Expert matmuls of the batched path: 0 auto, 1 dp4a, 2 tensor cores (same bits);
+        3 tensor cores with the fast epilogue (within the accumulation-order tolerance)."""
         check(self.lib.tgx_set_batched_kernels(self._ctx, kernels), self.lib)
 
     def sync_status(self):

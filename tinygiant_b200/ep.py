@@ -134,7 +134,8 @@ class EPMoEModel:
         check(self.lib.tgx_ep_set_ffn_norm(self._ep, layer, w.ctypes.data, 0), self.lib)
 
     def set_kernels(self, kernels: int):
-        """0 auto, 1 dp4a, 2 tensor cores (tcgen05) for the expert matmuls; same bits."""
+        """0 auto, 1 dp4a, 2 tensor cores (tcgen05) for the expert matmuls (same bits);
+        3 tensor cores with the fast epilogue (within the accumulation-order tolerance)."""
         check(self.lib.tgx_ep_set_kernels(self._ep, kernels), self.lib)
 
     def status(self, stream=None):
