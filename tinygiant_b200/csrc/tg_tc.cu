@@ -22,7 +22,8 @@
 // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (its rows) and owns tokens 8 (w / 4) .. + 7.
 // K runs in groups of 8 steps through three shared stages and two TMEM accumulator sets
 // (2 x 8 x 32 columns): while the epilogue reads group g, the tensor cores run group
-// g + 1 and every thread's global loads for group g + 2 are in flight; thread 0 issues
+// g + 1 and every thread's async copies (cp.async, into its own raw slots) for group
+// g + 2 are in flight, converted into the MMA layout after the epilogue; thread 0 issues
 // each group's MMAs and commits them to an mbarrier.  Every mbarrier wait is bounded; on
 // expiry the CTA records the failure, drains its MMAs (bounded), frees its TMEM and returns.
 #include <cuda_runtime.h>
@@ -44,7 +45,11 @@ constexpr int B_STEP = TN * 32;  // bytes of B per K step (1 KB)
 constexpr int ST_A = 0, ST_B = KG * A_STEP, ST_DW = ST_B + KG * B_STEP, ST_DX = ST_DW + KG * TM * 4;
 constexpr int STAGE_BYTES = ST_DX + KG * TN * 4;
 constexpr int NSTAGE = 3;        // shared stages: group g+2 is written while g+1 is in the MMA, g in the epilogue
-constexpr int TC_SMEM = NSTAGE * STAGE_BYTES + 1024;   // + alignment slack
+// raw staging: each thread's own slots for its async copies of the next group's operands
+// (A: 2 x 16 B codes + 2 x 4 B holding the f16 scale; B, threads < 256: 2 x 16 B + 4 B)
+constexpr int RAW_A = NSTAGE * STAGE_BYTES, RAW_AS = RAW_A + TC_THREADS * 32, RAW_B = RAW_AS + TC_THREADS * 8,
+              RAW_BD = RAW_B + TN * KG * 32, RAW_END = RAW_BD + TN * KG * 4;
+constexpr int TC_SMEM = RAW_END + 1024;   // + alignment slack
 constexpr uint32_t TMEM_COLS = 2 * KG * TN;       // 512
 constexpr long long TC_WAIT_CYCLES = 2000000000ll;
 
@@ -119,6 +124,14 @@ __device__ __forceinline__ void push8(float (&st)[8][6], const float (&v)[8], in
 // the xor clears it again.
 __device__ __forceinline__ uint32_t nib_minus8(uint32_t x) {
     return (((x & 0x0F0F0F0Fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+}
+
+// cp.async of 16 (cg: through L2 only) or 4 bytes; n = 0 copies nothing and zero-fills
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, int n) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(saddr(dst)), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, int n) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(saddr(dst)), "l"(src), "r"(n) : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld8(uint32_t (&v)[8], uint32_t ta) {
@@ -238,11 +251,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
     int fail_f = -1;
     bool failed = false;
 
-    // operand staging: 2 A items (row, step) and 1 B item (token, step) per thread
-    uint4 ra[2];
-    float rdw[2];
-    uint4 rb0, rb1;
-    float rdx = 0.0f;
+    // operand staging: 2 A items (row, step) and 1 B item (token, step) per thread.
+    // load_group issues the group's async copies into the thread's raw slots (they run
+    // behind the epilogue: no register waits on them); store_group waits for them, then
+    // converts the codes into the MMA layout.  A thread reads back only its own copies.
+    uint8_t* const raw_a = smem + RAW_A + tid * 32;
+    uint32_t* const raw_as = reinterpret_cast<uint32_t*>(smem + RAW_AS + tid * 8);
+    uint8_t* const raw_b = smem + RAW_B + (tid & (TN * KG - 1)) * 32;
+    float* const raw_bd = reinterpret_cast<float*>(smem + RAW_BD + (tid & (TN * KG - 1)) * 4);
+    uint32_t a_odd = 0;         // bit u: item u's scale is the upper half of its 4 copied bytes
     int ld_i = -1;              // the loader's current item and where its rows start
     Item ld_it{};
     const uint8_t* ld_eb = nullptr;
@@ -257,59 +274,67 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_q4_mma(TcParams P) {
         }
         const Item& it = ld_it;
         const uint8_t* eb = ld_eb;
+        a_odd = 0;
 #pragma unroll
         for (int u = 0; u < 2; u++) {
             const int x = tid + TC_THREADS * u, r = x & (TM - 1), jj = x >> 7;
             const int s = gi * KG + jj;
-            ra[u] = make_uint4(0, 0, 0, 0);
-            rdw[u] = 0.0f;
-            if (s < nb) {
-                const int b = s_steps[s] & 1023;
-                const uint8_t* rp = eb + (size_t)r * row_bytes;
-                ra[u] = __ldg(reinterpret_cast<const uint4*>(rp + 16 * b));
-                rdw[u] = f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(rp + 16 * (size_t)nb + 2 * b)));
-            }
+            const bool ok = s < nb;
+            const int b = ok ? s_steps[s] & 1023 : 0;
+            const uint8_t* rp = eb + (size_t)r * row_bytes;
+            cp_async16(raw_a + 16 * u, rp + 16 * b, ok ? 16 : 0);
+            // the f16 scale in an aligned 4-byte pair (the row's scales start 16-aligned,
+            // and nb is even, so the pair stays inside them)
+            cp_async4(raw_as + u, rp + 16 * (size_t)nb + 4 * (b >> 1), ok ? 4 : 0);
+            a_odd |= (uint32_t)(b & 1) << u;
         }
-        rb0 = rb1 = make_uint4(0, 0, 0, 0);
-        rdx = 0.0f;
         if (tid < TN * KG) {
             const int tk = tid & (TN - 1), jj = tid >> 5, s = gi * KG + jj;
-            if (s < nb && tk < it.nt) {
+            const bool ok = s < nb && tk < it.nt;
+            const uint8_t* q = P.act;
+            const float* d = reinterpret_cast<const float*>(P.act);
+            if (ok) {
                 const int b = s_steps[s] & 1023;
                 const int p = s_pairs[i & (RING - 1)][tk];
                 const ActView av = act_view(P.act + (size_t)(P.down ? p : p / P.ks) * ab, nb);
-                const uint4* q = reinterpret_cast<const uint4*>(av.qs + (size_t)b * 32);
-                rb0 = __ldg(q);
-                rb1 = __ldg(q + 1);
-                rdx = __ldg(av.d + b);
+                q = reinterpret_cast<const uint8_t*>(av.qs) + (size_t)b * 32;
+                d = av.d + b;
             }
+            cp_async16(raw_b, q, ok ? 16 : 0);
+            cp_async16(raw_b + 16, q + 16, ok ? 16 : 0);
+            cp_async4(raw_bd, d, ok ? 4 : 0);
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     };
     auto store_group = [&](int stg) {
         uint8_t* base = smem + (size_t)stg * STAGE_BYTES;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
         for (int u = 0; u < 2; u++) {
             const int x = tid + TC_THREADS * u, r = x & (TM - 1), jj = x >> 7;
             uint8_t* a = base + ST_A + jj * A_STEP + (r >> 3) * 256 + (r & 7) * 16;
+            const uint4 ra = *reinterpret_cast<const uint4*>(raw_a + 16 * u);
+            const uint32_t sp = raw_as[u];
             uint4 lo, hi;   // element j < 16: low nibble of byte j; 16 + j: high nibble; both minus 8
-            lo.x = nib_minus8(ra[u].x);
-            lo.y = nib_minus8(ra[u].y);
-            lo.z = nib_minus8(ra[u].z);
-            lo.w = nib_minus8(ra[u].w);
-            hi.x = nib_minus8(ra[u].x >> 4);
-            hi.y = nib_minus8(ra[u].y >> 4);
-            hi.z = nib_minus8(ra[u].z >> 4);
-            hi.w = nib_minus8(ra[u].w >> 4);
+            lo.x = nib_minus8(ra.x);
+            lo.y = nib_minus8(ra.y);
+            lo.z = nib_minus8(ra.z);
+            lo.w = nib_minus8(ra.w);
+            hi.x = nib_minus8(ra.x >> 4);
+            hi.y = nib_minus8(ra.y >> 4);
+            hi.z = nib_minus8(ra.z >> 4);
+            hi.w = nib_minus8(ra.w >> 4);
             *reinterpret_cast<uint4*>(a) = lo;
             *reinterpret_cast<uint4*>(a + 128) = hi;
-            reinterpret_cast<float*>(base + ST_DW)[jj * TM + r] = rdw[u];
+            reinterpret_cast<float*>(base + ST_DW)[jj * TM + r] =
+                f16_bits_to_f32((uint16_t)(((a_odd >> u) & 1) ? sp >> 16 : sp & 0xFFFFu));
         }
         if (tid < TN * KG) {
             const int tk = tid & (TN - 1), jj = tid >> 5;
             uint8_t* bp = base + ST_B + jj * B_STEP + (tk >> 3) * 256 + (tk & 7) * 16;
-            *reinterpret_cast<uint4*>(bp) = rb0;
-            *reinterpret_cast<uint4*>(bp + 128) = rb1;
-            reinterpret_cast<float*>(base + ST_DX)[jj * TN + tk] = rdx;
+            *reinterpret_cast<uint4*>(bp) = *reinterpret_cast<const uint4*>(raw_b);
+            *reinterpret_cast<uint4*>(bp + 128) = *reinterpret_cast<const uint4*>(raw_b + 16);
+            reinterpret_cast<float*>(base + ST_DX)[jj * TN + tk] = *raw_bd;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     };
