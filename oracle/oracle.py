@@ -18,6 +18,7 @@ LIB_PATH = HERE / "libtgref.so"
 
 TG_REF_ORDER = 0
 TG_MIRROR = 1
+TG_FAST_MMA = 2   # the tensor-core kernels' fast epilogue order (kernel mode 3)
 QK = 32
 Q4_0_BYTES = 18
 Q8_0_BYTES = 34

@@ -242,7 +242,25 @@ static inline float butterfly32(float *p) {
     return p[0];
 }
 
+/* 5-bit reversal: the lane class visited at ordinal c */
+static inline int rev5(int c) {
+    return ((c & 1) << 4) | ((c & 2) << 2) | (c & 4) | ((c & 8) >> 2) | ((c & 16) >> 4);
+}
+
 float ref_row_dot(const uint8_t *wrow, const uint8_t *xq, int nb, int mode) {
+    if (mode == TG_FAST_MMA) {
+        float acc = 0.0f;
+        for (int c = 0; c < 32; c++)
+            for (int b = rev5(c); b < nb; b += 32) {
+                const uint8_t *wblk = wrow + (size_t)b * REF_Q4_0_BYTES, *xblk = xq + (size_t)b * REF_Q8_0_BYTES;
+                uint16_t dw, dx;
+                memcpy(&dw, wblk, 2);
+                memcpy(&dx, xblk, 2);
+                const float d = ref_f16_to_f32(dw) * ref_f16_to_f32(dx);
+                acc = fmaf((float)ref_block_dot_q4_0_q8_0(wblk, xblk), d, acc);
+            }
+        return acc;
+    }
     if (mode == TG_REF_ORDER) {
         float total = 0.0f;
         for (int b = 0; b < nb; b++)

@@ -17,7 +17,12 @@
  *   TG_MIRROR   (1)   the device kernels' fixed order: each row dot is split over
  *                     32 lanes (lane L sums blocks L, L+32, ...) and reduced with
  *                     an xor butterfly; SiLU/softmax use tg_expf (Cody-Waite + Taylor).
- * Routing arithmetic is the same in both modes except for exp: logits are exact
+ *   TG_FAST_MMA (2)   as TG_MIRROR, except each row dot: the tensor-core kernels'
+ *                     fast epilogue, one accumulator taking
+ *                     acc = fmaf((float)sumi, d_w * d_x, acc) block after block, the
+ *                     blocks in lane-class order (classes in 5-bit-reversed order
+ *                     0, 16, 8, 24, ..., each class's blocks l, l + 32, ... ascending).
+ * Routing arithmetic is the same in all modes except for exp: logits are exact
  * fixed-point sums of fp32 products (see ref_router_logits).
  */
 #ifndef TG_REF_H
@@ -29,7 +34,7 @@
 extern "C" {
 #endif
 
-enum { TG_REF_ORDER = 0, TG_MIRROR = 1 };
+enum { TG_REF_ORDER = 0, TG_MIRROR = 1, TG_FAST_MMA = 2 };
 enum { REF_QK = 32, REF_Q4_0_BYTES = 18, REF_Q8_0_BYTES = 34 };
 
 float    ref_f16_to_f32(uint16_t h);

@@ -114,7 +114,8 @@ def test_few_tokens_take_the_fused_step_with_the_same_bits():
 @pytest.mark.parametrize("T", [64, 600])
 def test_fast_epilogue_within_reference_order_tolerance(oracle, T):
     # kernels=3: the tensor cores with one fma per Q4_0 block (exact int32 block dots,
-    # another fp32 summation order).  Held, per token, to the bound an order difference
+    # another fp32 summation order).  Bit-identical to the oracle's restatement of that
+    # order (TG_FAST_MMA), and held, per token, to the bound an order difference
     # gets against the reference's own order (tests/order_check.py): <= 1e-5 max-abs-rel,
     # except tokens whose Q8_0 requantisation of h takes a neighbouring code or scale,
     # <= FLIP_BOUND.  Flips are not visible through the API, so their count is bounded
@@ -128,6 +129,7 @@ def test_fast_epilogue_within_reference_order_tolerance(oracle, T):
     X = rng.standard_normal((T, H)).astype(np.float32)
     ref = oracle.moe_block_batched(blobs[0], Rs[0], X, k, H, I, normw=Ns[0], mode=oracle.TG_REF_ORDER)
     mir = oracle.moe_block_batched(blobs[0], Rs[0], X, k, H, I, normw=Ns[0])
+    fast = oracle.moe_block_batched(blobs[0], Rs[0], X, k, H, I, normw=Ns[0], mode=oracle.TG_FAST_MMA)
     m.set_batched_kernels(3)
     Xd = torch.from_numpy(X.copy()).cuda()
     m.moe_batched(0, Xd)
@@ -139,6 +141,8 @@ def test_fast_epilogue_within_reference_order_tolerance(oracle, T):
     def per_token(a):
         return np.abs((a.astype(np.float64) - X) - d_ref).max(1) / np.abs(d_ref).max(1)
 
+    # the oracle restates the fast epilogue's order too: bit for bit
+    assert np.array_equal(got.view(np.uint32), fast.view(np.uint32))
     e_fast, e_mir = per_token(got), per_token(mir)
     assert e_fast.max() <= FLIP_BOUND, e_fast.max()
     assert np.median(e_fast) <= REL_TOL

@@ -43,7 +43,7 @@ def test_block_dots_exact(oracle, golden):
     assert np.array_equal(s, golden["mv_sumi"])
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])   # reference order, mirror order, fast tensor-core epilogue
 def test_matvec_close_to_float64(oracle, golden, mode):
     y = oracle.matvec(golden["mv_W"], golden["mv_xq"], 96, 512, mode)
     y64 = golden["mv_y64"]
@@ -52,7 +52,7 @@ def test_matvec_close_to_float64(oracle, golden, mode):
     assert np.max(np.abs(y - y64)) <= bound
 
 
-@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("mode", [0, 1, 2])
 def test_expert_forward_matches_float64_pipeline(oracle, golden, mode):
     H, I = int(golden["ex_H"]), int(golden["ex_I"])
     st = oracle.expert_stages(golden["ex_blob"], golden["ex_x"], H, I, mode)
