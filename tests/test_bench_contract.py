@@ -64,3 +64,20 @@ print(json.dumps(bench.ep_split(st)))
     import json as _json
     d = _json.loads([ln for ln in (r.stderr + r.stdout).splitlines() if ln.startswith("{")][-1])
     assert d == {"layer_us": 20.0, "partial_us": 8.75, "exchange_us": 3.0, "combine_us": 2.0}
+
+
+def test_batched_kernel_choices_match_the_library_modes():
+    # --batched-kernels maps onto the expert-matmul modes the library defines
+    # (tg_internal.h BATCHED_*; tgx_set_batched_kernels / tgx_ep_set_kernels accept 0..3)
+    import re
+    r = subprocess.run([sys.executable, "-c",
+                        "import sys, json; sys.path.insert(0, '.'); import bench; print(json.dumps(bench.KERNELS))"],
+                       capture_output=True, text=True, timeout=120, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    kernels = json.loads([ln for ln in (r.stderr + r.stdout).splitlines() if ln.startswith("{")][-1])
+    src = (ROOT / "tinygiant_b200" / "csrc" / "tg_internal.h").read_text()
+    modes = dict(re.findall(r"BATCHED_(\w+) = (\d)", src))
+    assert {k: int(v) for k, v in modes.items()} == {"AUTO": 0, "DP4A": 1, "MMA": 2, "MMA_FAST": 3}
+    assert kernels == {"auto": 0, "dp4a": 1, "mma": 2, "mma-fast": 3}
+    for f in ("tg_capi.cu", "tg_ep.cu"):
+        assert "kernels >= 0 && kernels <= 3" in (ROOT / "tinygiant_b200" / "csrc" / f).read_text(), f
